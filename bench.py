@@ -1,0 +1,366 @@
+#!/usr/bin/env python
+"""Benchmark of the DSALT sparse-attention op on B200.
+
+Headline (BASELINE.json metric, config 2): attended-pair TFLOP/s of one
+forward+backward of the training op, B=4 packed sequences of N=4096, H=16,
+D=128, bf16, k_lmk=64, w̃ = 32 + σ(g)·480.  A "step" is one call of the public
+op ``dsalt_triton_train_attention`` plus its backward over the whole batch.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--workload config2|config3]
+    python bench.py --impl reference        # the CPU restatement on the host cores
+
+Multi-GPU (torchrun, one rank per GPU): every rank runs its own full batch
+(weak scaling over batch×heads, no collective in the timed region); ``value``
+sums the attended FLOPs of all ranks over the slowest rank's time.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT / "dsalt-library_b200"))
+sys.path.insert(0, str(ROOT))
+
+METRIC = "attended-pair TFLOP/s fwd+bwd (N=4096, D=128)"
+UNIT = "TFLOP/s"
+
+WORKLOADS = {
+    "config2": dict(lens=[4096] * 4, H=16, D=128, k=64, n_min=32, n_max=512,
+                    desc="config2: B=4 packed x N=4096, H=16, D=128, bf16, k_lmk=64, w=32+sigmoid(g)*480"),
+    "config3": dict(lens=None, H=16, D=128, k=64, n_min=64, n_max=1024,
+                    desc="config3: 16 varlen seqs (randint(256,4097) seed 0), H=16, D=128, bf16, k_lmk=64, "
+                         "w=64+sigmoid(g)*960"),
+}
+
+# per attended pair, algorithmic FLOPs of each kernel (fwd 4D; bwd 10D = dK/dV kernel: S, dP, dV, dK
+# = 8D; dQ kernel: dQ = 2D, its S/dP recompute is not algorithmic work)
+FLOPS_PER_PAIR = {"dsalt_attn_fwd": 4, "dsalt_attn_bwd_dkdv": 8, "dsalt_attn_bwd_dq": 2}
+# kernels launched by each C-ABI entry point
+KERNELS_PER_CALL = {"dsalt_build_schedule": 2, "dsalt_gather_landmarks": 1, "dsalt_attn_fwd": 1,
+                    "dsalt_attn_bwd_preprocess": 1, "dsalt_attn_bwd_dkdv": 1, "dsalt_attn_bwd_dq": 2}
+CLOCK_REASONS = {0x1: "gpu_idle", 0x2: "applications_clocks_setting", 0x4: "sw_power_cap",
+                 0x8: "hw_slowdown", 0x10: "sync_boost", 0x20: "sw_thermal_slowdown",
+                 0x40: "hw_thermal_slowdown", 0x80: "hw_power_brake_slowdown", 0x100: "display_clock_setting"}
+
+
+def seq_lens(wl) -> list[int]:
+    if wl["lens"] is not None:
+        return list(wl["lens"])
+    import torch
+    g = torch.Generator().manual_seed(0)
+    return [int(x) for x in torch.randint(256, 4097, (16,), generator=g)]
+
+
+def peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return float(d["bf16_tflops"]), float(d["bf16_tflops_sustained"]), float(d["hbm_gbs"]), "measured"
+    return 1590.0, 1400.0, 6650.0, "fallback"
+
+
+# ----------------------------------------------------------------- workload
+def make_workload(wl, seed, device):
+    import torch
+    from dsalt.kernels.selectors import select_topk
+    lens = seq_lens(wl)
+    T, H, D, k = sum(lens), wl["H"], wl["D"], wl["k"]
+    g = torch.Generator(device=device).manual_seed(seed)
+    q, kk, v, do = (torch.randn(T, H, D, generator=g, device=device).to(torch.bfloat16) for _ in range(4))
+    gate = torch.randn(T, generator=g, device=device)
+    w = wl["n_min"] + torch.sigmoid(gate) * (wl["n_max"] - wl["n_min"])
+    scores = torch.randn(T, H, generator=g, device=device)
+    cu = torch.tensor([0] + list(__import__("itertools").accumulate(lens)), dtype=torch.int32, device=device)
+    w_disc = w.floor().clamp(min=1)
+    lmk_pos = select_topk(scores, w_disc, cu, k, max(lens))
+    starts = cu[:-1].long()
+    s_sel = scores[starts[None, :, None] + lmk_pos.clamp(min=0), torch.arange(H, device=device)[:, None, None]]
+    lmk_logw = torch.log(torch.sigmoid(s_sel / 2.0).clamp(min=1e-20))
+    lmk_logw = torch.where(lmk_pos >= 0, lmk_logw, torch.full_like(lmk_logw, float("-inf")))
+    cu_list = [0] + list(__import__("itertools").accumulate(lens))
+    return dict(q=q, k=kk, v=v, do=do, w=w, lmk_pos=lmk_pos, lmk_logw=lmk_logw, cu=cu, cu_list=cu_list,
+                lens=lens, T=T, H=H, D=D, n_max=wl["n_max"])
+
+
+def step_fn(d):
+    import torch
+    from dsalt.kernels.dsalt_triton_train import dsalt_triton_train_attention
+    q = d["q"].requires_grad_(True)
+    k = d["k"].requires_grad_(True)
+    v = d["v"].requires_grad_(True)
+    w = d["w"].requires_grad_(True)
+    lw = d["lmk_logw"].requires_grad_(True)
+
+    def step():
+        o = dsalt_triton_train_attention(q, k, v, d["lmk_pos"], lw, w, d["cu"], 1.0, 4.0, d["n_max"],
+                                         d["cu_list"])
+        return torch.autograd.grad(o, (q, k, v, w, lw), d["do"])
+    return step
+
+
+# ------------------------------------------------------------------- clocks
+class ClockSampler:
+    def __init__(self, index: int):
+        self.index = index
+        self.proc = None
+        self.path = None
+
+    def __enter__(self):
+        fd, self.path = tempfile.mkstemp(suffix=".csv")
+        os.close(fd)
+        try:
+            self.f = open(self.path, "w")
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.index),
+                 "--query-gpu=clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active",
+                 "--format=csv,noheader,nounits", "-lms", "100"], stdout=self.f, stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+        time.sleep(0.3)
+        return self
+
+    def __exit__(self, *a):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+            self.f.close()
+
+    def summary(self):
+        if self.proc is None:
+            return None
+        sm, mx, reasons = [], [], 0
+        for line in Path(self.path).read_text().splitlines():
+            parts = [x.strip() for x in line.split(",")]
+            if len(parts) < 4:
+                continue
+            try:
+                sm.append(float(parts[0]))
+                mx.append(float(parts[1]))
+                reasons |= int(parts[3], 16) if parts[3].startswith("0x") else int(parts[3])
+            except ValueError:
+                continue
+        os.unlink(self.path)
+        if not sm:
+            return None
+        names = [n for b, n in CLOCK_REASONS.items() if reasons & b and n != "gpu_idle"]
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(mx), "reasons": names,
+                "samples": len(sm)}
+
+
+# ------------------------------------------------------------- cpu baseline
+def cpu_unit(wl, seed=0):
+    """One (sequence, head) unit of the workload, built on the host (numpy)."""
+    import numpy as np
+    import torch
+    from oracle import dsalt_oracle as O
+    L, D, k = seq_lens(wl)[0], wl["D"], wl["k"]
+    g = torch.Generator().manual_seed(1000 + seed)
+    q, kk, v, do = (torch.randn(L, 1, D, generator=g).to(torch.bfloat16).float().numpy() for _ in range(4))
+    gate = torch.randn(L, generator=g)
+    w = (wl["n_min"] + torch.sigmoid(gate) * (wl["n_max"] - wl["n_min"])).numpy().astype(np.float32)
+    scores = torch.randn(L, 1, generator=g).numpy()
+    cu = np.array([0, L])
+    pos = O.landmark_indices(scores, O.window_discrete(w), cu, k)
+    lw = O.landmark_logw(scores, pos, cu)
+    pairs = O.attended_pairs(w, pos, cu)
+    return dict(q=q, k=kk, v=v, do=do, w=w, pos=pos, lw=lw, cu=cu, pairs=pairs, D=D, L=L)
+
+
+def cpu_time_unit(u):
+    import numpy as np
+    from oracle import dsalt_oracle as O
+    t0 = time.perf_counter()
+    O.attention_bwd(u["q"], u["k"], u["v"], u["do"], u["pos"], u["lw"], u["w"], u["cu"], 1.0, 4.0, "train",
+                    dtype=np.float32)
+    return time.perf_counter() - t0
+
+
+def cpu_baseline(wl, units=2):
+    us = [cpu_unit(wl, s) for s in range(units)]
+    cpu_time_unit(us[0])  # warm-up (BLAS threads, page faults)
+    secs = sum(cpu_time_unit(u) for u in us)
+    flops = sum(14 * u["D"] * u["pairs"] for u in us)
+    return {"value": flops / secs / 1e12, "unit": UNIT, "cores": os.cpu_count(), "kind": "port",
+            "sample": f"{units} (sequence, head) units of N={us[0]['L']}, D={us[0]['D']}, fwd+bwd, numpy float32 "
+                      f"dense masked oracle, {secs:.1f} s"}
+
+
+def run_reference(args, wl):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    u = [cpu_unit(wl, s) for s in range(max(args.steps, 1))]
+    for s in range(args.warmup):
+        cpu_time_unit(u[s % len(u)])
+    secs = [cpu_time_unit(x) for x in u[:args.steps]]
+    flops = sum(14 * x["D"] * x["pairs"] for x in u[:args.steps])
+    val = flops / sum(secs) / 1e12
+    line = {"metric": METRIC, "value": val, "unit": UNIT, "n_gpus": args.gpus, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": 1e3 * sum(secs) / len(secs), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "impl": "reference",
+            "config": {"workload": wl["desc"] + " (one (sequence, head) unit per step)", "seq_len": u[0]["L"]},
+            "cpu_baseline": {"value": val, "unit": UNIT, "cores": os.cpu_count(), "kind": "port",
+                             "sample": "one (sequence, head) unit per step, numpy float32 dense masked oracle "
+                                       "(the reference is pure Python: its CPU path is restated in oracle/)"},
+            "e2e": {"value": val, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+# --------------------------------------------------------------------- main
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--workload", default="config2", choices=list(WORKLOADS))
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-e2e", action="store_true")
+    args = ap.parse_args()
+    wl = WORKLOADS[args.workload]
+    if args.impl == "reference":
+        run_reference(args, wl)
+        return
+
+    import torch
+    import torch.distributed as dist
+    from dsalt.kernels import _ext
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        import datetime
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    from dsalt.kernels.flops import attended_pairs
+    d = make_workload(wl, seed=rank, device=dev)
+    pairs = attended_pairs(d["w"], d["lmk_pos"], d["cu"])
+    step = step_fn(d)
+    for _ in range(max(args.warmup, 3)):
+        step()
+    torch.cuda.synchronize()
+    barrier()
+
+    with ClockSampler(local) as clk:
+        _ext.RECORD = []
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        barrier()
+        torch.cuda.synchronize()
+        e0.record()
+        for _ in range(args.steps):
+            step()
+        e1.record()
+        torch.cuda.synchronize()
+        rec, _ext.RECORD = _ext.RECORD, None
+        barrier()
+    ms = e0.elapsed_time(e1)
+    per_kernel = {}
+    for name, a, b in rec:
+        per_kernel.setdefault(name, []).append(a.elapsed_time(b))
+    launches = sum(KERNELS_PER_CALL.get(n, 1) for n, _, _ in rec)
+
+    t = torch.tensor([ms, 14.0 * d["D"] * pairs], dtype=torch.float64, device=dev)
+    if world > 1:
+        tm = t[:1].clone()
+        dist.all_reduce(tm, op=dist.ReduceOp.MAX)
+        tf = t[1:].clone()
+        dist.all_reduce(tf, op=dist.ReduceOp.SUM)
+        ms_max, flops_all = float(tm.item()), float(tf.item())
+    else:
+        ms_max, flops_all = ms, float(t[1].item())
+    value = flops_all * args.steps / (ms_max / 1e3) / 1e12
+
+    # end-to-end through the public op with host buffers
+    e2e = None
+    if not args.no_e2e:
+        host = {kk: d[kk].detach().cpu().pin_memory() for kk in ("q", "k", "v", "do", "w", "lmk_logw", "lmk_pos")}
+        outs = [torch.empty(d["q"].shape, dtype=torch.bfloat16).pin_memory() for _ in range(3)]
+        dwh = torch.empty(d["T"], dtype=torch.float32).pin_memory()
+        dlh = torch.empty(d["lmk_logw"].shape, dtype=torch.float32).pin_memory()
+        h2d = sum(x.numel() * x.element_size() for x in host.values())
+        d2h = sum(x.numel() * x.element_size() for x in outs) + dwh.numel() * 4 + dlh.numel() * 4
+        from dsalt.kernels.dsalt_triton_train import dsalt_triton_train_attention
+
+        def e2e_step():
+            q = host["q"].to(dev, non_blocking=True).requires_grad_(True)
+            k = host["k"].to(dev, non_blocking=True).requires_grad_(True)
+            v = host["v"].to(dev, non_blocking=True).requires_grad_(True)
+            w = host["w"].to(dev, non_blocking=True).requires_grad_(True)
+            lw = host["lmk_logw"].to(dev, non_blocking=True).requires_grad_(True)
+            pos = host["lmk_pos"].to(dev, non_blocking=True)
+            do = host["do"].to(dev, non_blocking=True)
+            o = dsalt_triton_train_attention(q, k, v, pos, lw, w, d["cu"], 1.0, 4.0, d["n_max"], d["cu_list"])
+            gq, gk, gv, gw, glw = torch.autograd.grad(o, (q, k, v, w, lw), do)
+            outs[0].copy_(gq, non_blocking=True)
+            outs[1].copy_(gk, non_blocking=True)
+            outs[2].copy_(gv, non_blocking=True)
+            dwh.copy_(gw, non_blocking=True)
+            dlh.copy_(glw, non_blocking=True)
+        for _ in range(3):
+            e2e_step()
+        torch.cuda.synchronize()
+        barrier()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        for _ in range(args.steps):
+            e2e_step()
+        b.record()
+        torch.cuda.synchronize()
+        ems = torch.tensor([a.elapsed_time(b)], dtype=torch.float64, device=dev)
+        if world > 1:
+            dist.all_reduce(ems, op=dist.ReduceOp.MAX)
+        e2e = {"value": flops_all * args.steps / (float(ems.item()) / 1e3) / 1e12, "unit": UNIT,
+               "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h)}
+
+    if rank == 0:
+        burst, sustained, hbm, src = peaks()
+        kern = {n: (sum(v) / len(v), sum(v)) for n, v in per_kernel.items()}
+        dom = max((n for n in kern if n in FLOPS_PER_PAIR), key=lambda n: kern[n][1])
+        ach = FLOPS_PER_PAIR[dom] * d["D"] * pairs / (kern[dom][0] / 1e3) / 1e12
+        roof = {"bound": "tensor", "kernel": dom, "achieved": ach, "peak": sustained, "unit": UNIT,
+                "frac": ach / sustained, "traffic": None,
+                "peak_source": f"{src} bf16_tflops_sustained (kernel timed inside a long step loop)"}
+        line = {"metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+                "warmup": max(args.warmup, 3), "ms_per_step": ms_max / args.steps, "higher_is_better": True,
+                "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+                "config": {"workload": wl["desc"], "global_batch": len(d["lens"]) * world,
+                           "seq_len": max(d["lens"]), "tokens_per_gpu": d["T"],
+                           "parallelism": f"dp{world} (batch x heads shards, no collective)",
+                           "l2": "inputs larger than L2 (q,k,v,dO = 256 MiB per step), no flush"},
+                "roofline": roof,
+                "kernels_ms": {n: round(v[0], 4) for n, v in kern.items()},
+                "attended_pairs_per_gpu": pairs,
+                "gpu_launches": launches,
+                "clocks": clk.summary()}
+        if e2e is not None:
+            line["e2e"] = e2e
+        if not args.no_cpu_baseline:
+            line["cpu_baseline"] = cpu_baseline(wl)
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        barrier()
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,317 @@
+// Exact-arithmetic SIMT kernels for the DSALT attention (fp32 math for every
+// input dtype).  These are the fp32 path (fp32 inputs keep fp32 precision,
+// unlike the reference, which casts them to fp16 at
+// dsalt/kernels/dsalt_triton_train.py:601-604) and the cross-check for the
+// tcgen05 kernels.  One warp owns one (token, head) row and walks the row's
+// attended set explicitly, so no masked work is done.
+//
+// Attended set of query i (training semantics; inference is mapped onto it by
+// row_window()):
+//   band      j in [i - min(W, i), i],  W = floor(w̃)      (dsalt_triton_train.py:147-150)
+//   landmarks the sorted landmark prefix with p <= i and float(p) < float(i) - w̃
+//                                                            (dsalt_triton_train.py:182-185)
+#include "common.cuh"
+
+namespace dsalt {
+
+constexpr int kSimtWarps = 8;  // warps per CTA
+
+template <typename T, int D>
+struct RowVec {
+  static constexpr int R = D / 32;
+  float x[R];
+  __device__ __forceinline__ void load(const T* __restrict__ p, int lane) {
+#pragma unroll
+    for (int r = 0; r < R; ++r) x[r] = to_f32<T>(p[lane + 32 * r]);
+  }
+  __device__ __forceinline__ float dot(const T* __restrict__ p, int lane) const {
+    float s = 0.f;
+#pragma unroll
+    for (int r = 0; r < R; ++r) s = fmaf(x[r], to_f32<T>(p[lane + 32 * r]), s);
+    return warp_sum(s);
+  }
+};
+
+// ------------------------------------------------------------------ forward
+template <typename T, int D>
+__global__ void __launch_bounds__(kSimtWarps * 32)
+simt_fwd_kernel(const DsaltAttnParams p) {
+  const int lane = threadIdx.x & 31;
+  const int64_t row = (int64_t)blockIdx.x * kSimtWarps + (threadIdx.x >> 5);
+  if (row >= p.T * p.H) return;
+  const int64_t t = row / p.H;
+  const int h = (int)(row % p.H);
+  const int s = find_seq(p.cu_seqlens, p.S, t);
+  const int64_t s0 = p.cu_seqlens[s];
+  const int i = (int)(t - s0);
+  const RowWindow rw = row_window(p.w[t], i, p.semantics, p.win_edge);
+  const float inv_tau = 1.0f / p.tau_win;
+  const int64_t HD = (int64_t)p.H * D;
+
+  const T* q = reinterpret_cast<const T*>(p.q) + t * HD + (int64_t)h * D;
+  const T* kb = reinterpret_cast<const T*>(p.k) + (int64_t)h * D;
+  const T* vb = reinterpret_cast<const T*>(p.v) + (int64_t)h * D;
+  RowVec<T, D> qv;
+  qv.load(q, lane);
+
+  constexpr int R = D / 32;
+  float acc[R];
+#pragma unroll
+  for (int r = 0; r < R; ++r) acc[r] = 0.f;
+  float m = -INFINITY, l = 0.f;
+
+  auto visit = [&](const T* kp, const T* vp, float bias) {
+    const float sc = fmaf(qv.dot(kp, lane), p.scale, bias);
+    if (sc > m) {
+      const float corr = (m == -INFINITY) ? 0.f : expf(m - sc);
+      l *= corr;
+#pragma unroll
+      for (int r = 0; r < R; ++r) acc[r] *= corr;
+      m = sc;
+    }
+    const float pr = expf(sc - m);
+    l += pr;
+#pragma unroll
+    for (int r = 0; r < R; ++r) acc[r] = fmaf(pr, to_f32<T>(vp[lane + 32 * r]), acc[r]);
+  };
+
+  if (rw.W >= 0) {
+    const int jlo = i - min(rw.W, i);
+    for (int j = jlo; j <= i; ++j) {
+      const float d = (float)(i - j);
+      const int64_t kt = s0 + j;
+      visit(kb + kt * HD, vb + kt * HD, edge_bias(rw, d, inv_tau));
+    }
+  }
+  const int64_t lbase = ((int64_t)h * p.S + s) * p.kp;
+  for (int c = 0; c < p.kp; ++c) {
+    const int ps = p.pos_sorted[lbase + c];
+    if (ps < 0 || ps > i || !((float)ps < rw.win_lo)) break;  // valid set is a sorted prefix
+    const T* lk = reinterpret_cast<const T*>(p.lmk_k) + (lbase + c) * D;
+    const T* lv = reinterpret_cast<const T*>(p.lmk_v) + (lbase + c) * D;
+    visit(lk, lv, p.w_sorted[lbase + c]);
+  }
+
+  const bool nonempty = l > 1e-9f;
+  const float inv_l = nonempty ? 1.0f / l : 0.f;
+  T* o = reinterpret_cast<T*>(p.o) + t * HD + (int64_t)h * D;
+  float* of = p.o_f32 ? p.o_f32 + t * HD + (int64_t)h * D : nullptr;
+#pragma unroll
+  for (int r = 0; r < R; ++r) {
+    const T ov = from_f32<T>(acc[r] * inv_l);
+    o[lane + 32 * r] = ov;
+    if (of) of[lane + 32 * r] = to_f32<T>(ov);
+  }
+  if (lane == 0) p.lse[t * p.H + h] = nonempty ? m + logf(l) : -INFINITY;
+}
+
+// ------------------------------------------------------------- preprocess
+// Delta[t,h] = Σ_d O·dO with O the stored (input-dtype) output
+// (dsalt_triton_train.py:220-237, 674).
+template <typename T, int D>
+__global__ void __launch_bounds__(kSimtWarps * 32)
+bwd_preprocess_kernel(const DsaltAttnParams p) {
+  const int lane = threadIdx.x & 31;
+  const int64_t row = (int64_t)blockIdx.x * kSimtWarps + (threadIdx.x >> 5);
+  if (row >= p.T * p.H) return;
+  const T* o = reinterpret_cast<const T*>(p.o) + row * D;
+  const T* g = reinterpret_cast<const T*>(p.dout) + row * D;
+  float s = 0.f;
+#pragma unroll
+  for (int r = 0; r < D / 32; ++r) s = fmaf(to_f32<T>(o[lane + 32 * r]), to_f32<T>(g[lane + 32 * r]), s);
+  s = warp_sum(s);
+  if (lane == 0) p.delta[row] = s;
+}
+
+// ---------------------------------------------------------------- dQ, d_w̃
+template <typename T, int D>
+__global__ void __launch_bounds__(kSimtWarps * 32)
+simt_bwd_dq_kernel(const DsaltAttnParams p) {
+  const int lane = threadIdx.x & 31;
+  const int64_t row = (int64_t)blockIdx.x * kSimtWarps + (threadIdx.x >> 5);
+  if (row >= p.T * p.H) return;
+  const int64_t t = row / p.H;
+  const int h = (int)(row % p.H);
+  const int s = find_seq(p.cu_seqlens, p.S, t);
+  const int64_t s0 = p.cu_seqlens[s];
+  const int i = (int)(t - s0);
+  const RowWindow rw = row_window(p.w[t], i, p.semantics, p.win_edge);
+  const float inv_tau = 1.0f / p.tau_win;
+  const int64_t HD = (int64_t)p.H * D;
+  constexpr int R = D / 32;
+
+  const float lse = p.lse[row];
+  const float delta = p.delta[row];
+  float dq[R];
+#pragma unroll
+  for (int r = 0; r < R; ++r) dq[r] = 0.f;
+  float dw = 0.f;
+
+  if (lse != -INFINITY) {
+    RowVec<T, D> qv, gv;
+    qv.load(reinterpret_cast<const T*>(p.q) + t * HD + (int64_t)h * D, lane);
+    gv.load(reinterpret_cast<const T*>(p.dout) + t * HD + (int64_t)h * D, lane);
+    const T* kb = reinterpret_cast<const T*>(p.k) + (int64_t)h * D;
+    const T* vb = reinterpret_cast<const T*>(p.v) + (int64_t)h * D;
+    auto visit = [&](const T* kp, const T* vp, float bias, float dbias) {
+      const float sc = fmaf(qv.dot(kp, lane), p.scale, bias);
+      const float pr = expf(sc - lse);
+      const float dp = gv.dot(vp, lane);
+      const float ds = pr * (dp - delta);
+      dw = fmaf(ds, dbias, dw);
+      const float dss = ds * p.scale;
+#pragma unroll
+      for (int r = 0; r < R; ++r) dq[r] = fmaf(dss, to_f32<T>(kp[lane + 32 * r]), dq[r]);
+    };
+    if (rw.W >= 0) {
+      const int jlo = i - min(rw.W, i);
+      for (int j = jlo; j <= i; ++j) {
+        const float d = (float)(i - j);
+        const int64_t kt = s0 + j;
+        visit(kb + kt * HD, vb + kt * HD, edge_bias(rw, d, inv_tau), edge_dbias(rw, d, inv_tau));
+      }
+    }
+    const int64_t lbase = ((int64_t)h * p.S + s) * p.kp;
+    for (int c = 0; c < p.kp; ++c) {
+      const int ps = p.pos_sorted[lbase + c];
+      if (ps < 0 || ps > i || !((float)ps < rw.win_lo)) break;
+      visit(reinterpret_cast<const T*>(p.lmk_k) + (lbase + c) * D,
+            reinterpret_cast<const T*>(p.lmk_v) + (lbase + c) * D, p.w_sorted[lbase + c], 0.f);
+    }
+  }
+  T* out = reinterpret_cast<T*>(p.dq) + t * HD + (int64_t)h * D;
+#pragma unroll
+  for (int r = 0; r < R; ++r) out[lane + 32 * r] = from_f32<T>(dq[r]);
+  if (lane == 0 && p.dw_head) p.dw_head[row] = dw;
+}
+
+// ---------------------------------------------------------- dK, dV, d_lw
+// Key-parallel and atomic-free: one warp owns key j of head h and visits every
+// query that attends it, through the band (i in [j, j + wmax]) and, when j is
+// a landmark of (h, seq), through the landmark rule (all later queries whose
+// window no longer covers j).  d_lw of that landmark is a plain warp sum.
+template <typename T, int D>
+__global__ void __launch_bounds__(kSimtWarps * 32)
+simt_bwd_dkdv_kernel(const DsaltAttnParams p) {
+  const int lane = threadIdx.x & 31;
+  const int64_t row = (int64_t)blockIdx.x * kSimtWarps + (threadIdx.x >> 5);
+  if (row >= p.T * p.H) return;
+  const int64_t t = row / p.H;
+  const int h = (int)(row % p.H);
+  const int s = find_seq(p.cu_seqlens, p.S, t);
+  const int64_t s0 = p.cu_seqlens[s];
+  const int L = (int)(p.cu_seqlens[s + 1] - s0);
+  const int j = (int)(t - s0);
+  const float inv_tau = 1.0f / p.tau_win;
+  const int64_t HD = (int64_t)p.H * D;
+  constexpr int R = D / 32;
+
+  RowVec<T, D> kv, vv;
+  kv.load(reinterpret_cast<const T*>(p.k) + t * HD + (int64_t)h * D, lane);
+  vv.load(reinterpret_cast<const T*>(p.v) + t * HD + (int64_t)h * D, lane);
+  const T* qb = reinterpret_cast<const T*>(p.q) + (int64_t)h * D;
+  const T* gb = reinterpret_cast<const T*>(p.dout) + (int64_t)h * D;
+  float dk[R], dv[R];
+#pragma unroll
+  for (int r = 0; r < R; ++r) { dk[r] = 0.f; dv[r] = 0.f; }
+
+  auto visit = [&](int64_t qt, float bias) -> float {
+    const float lse = p.lse[qt * p.H + h];
+    if (lse == -INFINITY) return 0.f;
+    const T* qp = qb + qt * HD;
+    const T* gp = gb + qt * HD;
+    const float sc = fmaf(kv.dot(qp, lane), p.scale, bias);
+    const float pr = expf(sc - lse);
+    const float dp = vv.dot(gp, lane);
+    const float ds = pr * (dp - p.delta[qt * p.H + h]);
+    const float dss = ds * p.scale;
+#pragma unroll
+    for (int r = 0; r < R; ++r) {
+      dv[r] = fmaf(pr, to_f32<T>(gp[lane + 32 * r]), dv[r]);
+      dk[r] = fmaf(dss, to_f32<T>(qp[lane + 32 * r]), dk[r]);
+    }
+    return ds;
+  };
+
+  // band: query i attends j iff 0 <= i - j <= W_i
+  const int ihi = min(L - 1, j + max(p.seq_wmax[s], 0));
+  for (int i = j; i <= ihi; ++i) {
+    const RowWindow rw = row_window(p.w[s0 + i], i, p.semantics, p.win_edge);
+    const int d = i - j;
+    if (d > rw.W) continue;
+    visit(s0 + i, edge_bias(rw, (float)d, inv_tau));
+  }
+  // landmark slots at this token (sorted, duplicates adjacent)
+  const int64_t lbase = ((int64_t)h * p.S + s) * p.kp;
+  int c = p.lmk_slot ? p.lmk_slot[t * p.H + h] : -1;
+  for (; c >= 0 && c < p.kp && p.pos_sorted[lbase + c] == j; ++c) {
+    const float bias = p.w_sorted[lbase + c];
+    float dlw = 0.f;
+    for (int i = j; i < L; ++i) {
+      const RowWindow rw = row_window(p.w[s0 + i], i, p.semantics, p.win_edge);
+      if (!((float)j < rw.win_lo)) continue;  // (p <= i holds: i >= j)
+      dlw += visit(s0 + i, bias);
+    }
+    const int slot = p.perm[lbase + c];
+    if (lane == 0 && slot >= 0 && p.d_lw) p.d_lw[((int64_t)h * p.S + s) * p.k_lmk + slot] = dlw;
+  }
+  T* dko = reinterpret_cast<T*>(p.dk) + t * HD + (int64_t)h * D;
+  T* dvo = reinterpret_cast<T*>(p.dv) + t * HD + (int64_t)h * D;
+#pragma unroll
+  for (int r = 0; r < R; ++r) {
+    dko[lane + 32 * r] = from_f32<T>(dk[r]);
+    dvo[lane + 32 * r] = from_f32<T>(dv[r]);
+  }
+}
+
+// d_w̃[t] = Σ_h dw_head[t,h], cast to the input dtype (dsalt_triton_train.py:748,756)
+template <typename T>
+__global__ void dw_reduce_kernel(const float* __restrict__ dw_head, T* __restrict__ dw, int64_t T_, int H) {
+  const int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (t >= T_) return;
+  float s = 0.f;
+  for (int h = 0; h < H; ++h) s += dw_head[t * H + h];
+  dw[t] = from_f32<T>(s);
+}
+
+// ------------------------------------------------------------------ launchers
+template <typename T, int D>
+static cudaError_t launch_simt(int stage, const DsaltAttnParams& p, cudaStream_t st) {
+  const int64_t rows = p.T * p.H;
+  if (rows == 0) return cudaSuccess;
+  const dim3 grid((unsigned)((rows + kSimtWarps - 1) / kSimtWarps));
+  const dim3 block(kSimtWarps * 32);
+  switch (stage) {
+    case 0: simt_fwd_kernel<T, D><<<grid, block, 0, st>>>(p); break;
+    case 1: bwd_preprocess_kernel<T, D><<<grid, block, 0, st>>>(p); break;
+    case 2: simt_bwd_dkdv_kernel<T, D><<<grid, block, 0, st>>>(p); break;
+    case 3:
+      simt_bwd_dq_kernel<T, D><<<grid, block, 0, st>>>(p);
+      if (p.dw && p.dw_head)
+        dw_reduce_kernel<T><<<(unsigned)((p.T + 255) / 256), 256, 0, st>>>(p.dw_head, reinterpret_cast<T*>(p.dw), p.T, p.H);
+      break;
+  }
+  return cudaGetLastError();
+}
+
+template <typename T>
+static cudaError_t launch_simt_d(int stage, const DsaltAttnParams& p, cudaStream_t st) {
+  switch (p.D) {
+    case 32: return launch_simt<T, 32>(stage, p, st);
+    case 64: return launch_simt<T, 64>(stage, p, st);
+    case 128: return launch_simt<T, 128>(stage, p, st);
+    case 256: return launch_simt<T, 256>(stage, p, st);
+  }
+  return cudaErrorInvalidValue;
+}
+
+cudaError_t simt_attention_stage(int stage, const DsaltAttnParams& p, cudaStream_t st) {
+  switch (p.dtype) {
+    case DSALT_F16: return launch_simt_d<__half>(stage, p, st);
+    case DSALT_BF16: return launch_simt_d<__nv_bfloat16>(stage, p, st);
+    case DSALT_F32: return launch_simt_d<float>(stage, p, st);
+  }
+  return cudaErrorInvalidValue;
+}
+
+}  // namespace dsalt

@@ -1,0 +1,151 @@
+// extern "C" entry points of libdsalt_b200.so: argument checks, then launches.
+// No entry point allocates device memory; every buffer belongs to the caller.
+#include "common.cuh"
+
+namespace dsalt {
+cudaError_t launch_schedule(const DsaltScheduleParams& p, cudaStream_t st);
+cudaError_t launch_gather(const DsaltGatherParams& p, cudaStream_t st);
+cudaError_t simt_attention_stage(int stage, const DsaltAttnParams& p, cudaStream_t st);
+cudaError_t launch_win_gate(const DsaltWinGateParams& p, cudaStream_t st);
+cudaError_t launch_hybrid_scores(const DsaltScoreParams& p, cudaStream_t st);
+cudaError_t launch_topk(const DsaltTopkParams& p, cudaStream_t st);
+// tcgen05 path (attn_tc.cu); returns cudaErrorNotSupported when the shape is
+// outside what the tensor-core kernels cover, so the caller can report it.
+cudaError_t tc_attention_stage(int stage, const DsaltAttnParams& p, cudaStream_t st);
+bool tc_supported(const DsaltAttnParams& p);
+}  // namespace dsalt
+
+using namespace dsalt;
+
+static int status_of(cudaError_t e) {
+  if (e == cudaSuccess) return DSALT_OK;
+  if (e == cudaErrorInvalidValue) return DSALT_ERR_ARG;
+  if (e == cudaErrorNoDevice || e == cudaErrorInsufficientDriver || e == cudaErrorNoKernelImageForDevice)
+    return DSALT_ERR_NO_DEVICE;
+  return DSALT_ERR_LAUNCH;
+}
+
+static bool aligned16(const void* p) { return ((uintptr_t)p & 15u) == 0; }
+
+static int check_attn(const DsaltAttnParams* p, int stage) {
+  if (!p) return DSALT_ERR_ARG;
+  if (p->dtype != DSALT_F16 && p->dtype != DSALT_BF16 && p->dtype != DSALT_F32) return DSALT_ERR_DTYPE;
+  if (p->D != 32 && p->D != 64 && p->D != 128 && p->D != 256) return DSALT_ERR_HEAD_DIM;
+  if (p->T < 0 || p->H <= 0 || p->S < 0 || p->k_lmk < 0 || p->kp < p->k_lmk) return DSALT_ERR_ARG;
+  if (p->semantics != DSALT_TRAIN && p->semantics != DSALT_INFER) return DSALT_ERR_ARG;
+  if (!(p->tau_win > 0.f)) return DSALT_ERR_ARG;
+  if (p->impl < DSALT_IMPL_AUTO || p->impl > DSALT_IMPL_TCGEN05) return DSALT_ERR_ARG;
+  if (p->T == 0) return DSALT_OK;
+  if (!p->q || !p->k || !p->v || !p->w || !p->cu_seqlens) return DSALT_ERR_ARG;
+  if (p->kp > 0 && (!p->lmk_k || !p->lmk_v || !p->pos_sorted || !p->w_sorted)) return DSALT_ERR_ARG;
+  if (!aligned16(p->q) || !aligned16(p->k) || !aligned16(p->v)) return DSALT_ERR_ALIGN;
+  switch (stage) {
+    case 0: if (!p->o || !p->lse) return DSALT_ERR_ARG; break;
+    case 1: if (!p->o || !p->dout || !p->delta) return DSALT_ERR_ARG; break;
+    case 2: if (!p->dout || !p->lse || !p->delta || !p->dk || !p->dv || !p->seq_wmax) return DSALT_ERR_ARG;
+            if (p->kp > 0 && (!p->lmk_slot || !p->perm)) return DSALT_ERR_ARG;
+            break;
+    case 3: if (!p->dout || !p->lse || !p->delta || !p->dq) return DSALT_ERR_ARG; break;
+  }
+  return DSALT_OK;
+}
+
+static int run_attn(const DsaltAttnParams* p, int stage, void* stream) {
+  int st = check_attn(p, stage);
+  if (st != DSALT_OK || p->T == 0) return st;
+  cudaStream_t s = (cudaStream_t)stream;
+  bool use_tc = false;
+  if (p->impl == DSALT_IMPL_TCGEN05) {
+    if (p->dtype == DSALT_F32 || !tc_supported(*p)) return DSALT_ERR_DTYPE;
+    use_tc = true;
+  } else if (p->impl == DSALT_IMPL_AUTO) {
+    use_tc = p->dtype != DSALT_F32 && tc_supported(*p);
+  }
+  cudaError_t e = use_tc ? tc_attention_stage(stage, *p, s) : simt_attention_stage(stage, *p, s);
+  return status_of(e);
+}
+
+extern "C" {
+
+int dsalt_b200_abi_version(void) { return DSALT_B200_ABI_VERSION; }
+
+const char* dsalt_b200_status_string(int status) {
+  switch (status) {
+    case DSALT_OK: return "ok";
+    case DSALT_ERR_ARG: return "invalid argument";
+    case DSALT_ERR_DTYPE: return "unsupported dtype for this kernel family";
+    case DSALT_ERR_HEAD_DIM: return "unsupported head_dim (32, 64, 128, 256)";
+    case DSALT_ERR_LAUNCH: return "CUDA launch or API error";
+    case DSALT_ERR_NO_DEVICE: return "no usable sm_100 device";
+    case DSALT_ERR_ALIGN: return "pointer not 16-byte aligned";
+    case DSALT_ERR_TOO_LARGE: return "size beyond a documented limit";
+  }
+  return "unknown status";
+}
+
+int dsalt_b200_params_sizeof(int which) {
+  switch (which) {
+    case 0: return (int)sizeof(DsaltScheduleParams);
+    case 1: return (int)sizeof(DsaltGatherParams);
+    case 2: return (int)sizeof(DsaltAttnParams);
+    case 3: return (int)sizeof(DsaltScoreParams);
+    case 4: return (int)sizeof(DsaltTopkParams);
+    case 5: return (int)sizeof(DsaltWinGateParams);
+  }
+  return -1;
+}
+
+int dsalt_build_schedule(const DsaltScheduleParams* p, void* stream) {
+  if (!p || p->S < 0 || p->T < 0 || p->block <= 0 || p->max_blocks < 0) return DSALT_ERR_ARG;
+  if (!p->cu_seqlens || !p->block_map || !p->num_blocks) return DSALT_ERR_ARG;
+  if ((p->seq_wmax || p->seq_id) && p->T > 0 && !p->w) return DSALT_ERR_ARG;
+  if (p->S == 0) return status_of(cudaMemsetAsync(p->num_blocks, 0, sizeof(int32_t), (cudaStream_t)stream));
+  return status_of(launch_schedule(*p, (cudaStream_t)stream));
+}
+
+int dsalt_gather_landmarks(const DsaltGatherParams* p, void* stream) {
+  if (!p || p->H <= 0 || p->S < 0 || p->k_lmk < 0 || p->kp < p->k_lmk || p->k_lmk > 1024) return DSALT_ERR_ARG;
+  if (p->dtype != DSALT_F16 && p->dtype != DSALT_BF16 && p->dtype != DSALT_F32) return DSALT_ERR_DTYPE;
+  if ((p->D * (p->dtype == DSALT_F32 ? 4 : 2)) % 16 != 0) return DSALT_ERR_HEAD_DIM;
+  if (p->kp == 0 || p->S == 0) return DSALT_OK;
+  if (!p->k || !p->v || !p->lmk_k || !p->lmk_v || !p->pos_sorted || !p->w_sorted || !p->perm ||
+      !p->lmk_slot || !p->cu_seqlens || (p->k_lmk > 0 && (!p->lmk_pos || !p->lmk_w)))
+    return DSALT_ERR_ARG;
+  if (!aligned16(p->k) || !aligned16(p->v) || !aligned16(p->lmk_k) || !aligned16(p->lmk_v)) return DSALT_ERR_ALIGN;
+  cudaStream_t s = (cudaStream_t)stream;
+  cudaError_t e = cudaMemsetAsync(p->lmk_slot, 0xFF, sizeof(int32_t) * (size_t)p->T * p->H, s);
+  if (e != cudaSuccess) return status_of(e);
+  return status_of(launch_gather(*p, s));
+}
+
+int dsalt_attn_fwd(const DsaltAttnParams* p, void* stream) { return run_attn(p, 0, stream); }
+int dsalt_attn_bwd_preprocess(const DsaltAttnParams* p, void* stream) { return run_attn(p, 1, stream); }
+int dsalt_attn_bwd_dkdv(const DsaltAttnParams* p, void* stream) { return run_attn(p, 2, stream); }
+int dsalt_attn_bwd_dq(const DsaltAttnParams* p, void* stream) { return run_attn(p, 3, stream); }
+
+int dsalt_hybrid_scores(const DsaltScoreParams* p, void* stream) {
+  if (!p || p->T < 0 || p->H <= 0 || p->n_kv <= 0 || p->H % p->n_kv != 0 || p->dh <= 0 || p->d_model <= 0)
+    return DSALT_ERR_ARG;
+  if (p->dtype != DSALT_F16 && p->dtype != DSALT_BF16 && p->dtype != DSALT_F32) return DSALT_ERR_DTYPE;
+  if (p->T == 0) return DSALT_OK;
+  if (!p->x || !p->xwv || !p->alpha || !p->scores || !p->stats || !p->norms) return DSALT_ERR_ARG;
+  return status_of(launch_hybrid_scores(*p, (cudaStream_t)stream));
+}
+
+int dsalt_select_topk(const DsaltTopkParams* p, void* stream) {
+  if (!p || p->T < 0 || p->H <= 0 || p->S < 0 || p->k < 0 || p->max_len < 0) return DSALT_ERR_ARG;
+  if (p->k > 1024 || p->max_len > 49152) return DSALT_ERR_TOO_LARGE;
+  if (p->S == 0 || p->k == 0) return DSALT_OK;
+  if (!p->scores || !p->w_sizes || !p->cu_seqlens || !p->idx) return DSALT_ERR_ARG;
+  return status_of(launch_topk(*p, (cudaStream_t)stream));
+}
+
+int dsalt_win_gate(const DsaltWinGateParams* p, void* stream) {
+  if (!p || p->T < 0 || p->d_model <= 0) return DSALT_ERR_ARG;
+  if (p->dtype != DSALT_F16 && p->dtype != DSALT_BF16 && p->dtype != DSALT_F32) return DSALT_ERR_DTYPE;
+  if (p->T == 0) return DSALT_OK;
+  if (!p->x || !p->weight || !p->bias || !p->w_cont) return DSALT_ERR_ARG;
+  return status_of(launch_win_gate(*p, (cudaStream_t)stream));
+}
+
+}  // extern "C"

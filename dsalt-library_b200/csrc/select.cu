@@ -1,0 +1,268 @@
+// Selection and gating kernels: window gate, hybrid landmark score, top-k.
+//
+// These replace the torch code of the reference's selectors:
+//   win_gate        DSALTAttention._window_continuous   (dsalt/modules/dsalt_attention.py:270-284)
+//   hybrid scores   hybrid_scores_per_head              (dsalt/kernels/landmark_tokens_ker.py:19-61)
+//   top-k           _compute_landmark_indices           (dsalt/kernels/selectors.py:75-134)
+// All three are HBM/latency-bound byte work: coalesced 16-byte loads, one warp
+// per token for the row reductions, shared-memory radix select for top-k.
+#include "common.cuh"
+
+namespace dsalt {
+
+// ------------------------------------------------------------------ win_gate
+// logit = x·W + b accumulated in fp32; under autocast (dtype f16/bf16) torch
+// rounds the Linear output, the sigmoid, the product with (n_max - n_min) and
+// the sum with n_min to the dtype, each once; fp32 rounds each op to fp32.
+template <typename T>
+__global__ void __launch_bounds__(256) win_gate_kernel(DsaltWinGateParams p) {
+  const int lane = threadIdx.x & 31;
+  const int64_t t = (int64_t)blockIdx.x * 8 + (threadIdx.x >> 5);
+  if (t >= p.T) return;
+  const T* x = reinterpret_cast<const T*>(p.x) + t * p.d_model;
+  const T* w = reinterpret_cast<const T*>(p.weight);
+  float acc = 0.f;
+  for (int d = lane; d < p.d_model; d += 32) acc = fmaf(to_f32<T>(x[d]), to_f32<T>(w[d]), acc);
+  acc = warp_sum(acc);
+  if (lane != 0) return;
+  const float b = to_f32<T>(reinterpret_cast<const T*>(p.bias)[0]);
+  const float logit = __fadd_rn(acc, b);
+  const float span = p.n_max - p.n_min;
+  float wv;
+  if (sizeof(T) == 4) {
+    const float sg = __fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-logit)));
+    wv = __fadd_rn(p.n_min, __fmul_rn(sg, span));
+  } else {
+    const float lg = round_to<T>(logit);
+    const float sg = round_to<T>(__fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-lg))));
+    const float pr = round_to<T>(__fmul_rn(sg, span));
+    wv = round_to<T>(__fadd_rn(p.n_min, pr));
+  }
+  reinterpret_cast<T*>(p.w_cont)[t] = from_f32<T>(wv);
+  if (p.w_f32) p.w_f32[t] = wv;
+  if (p.w_disc) p.w_disc[t] = fmaxf(floorf(wv), 1.0f);
+  if (p.logits) p.logits[t] = logit;
+}
+
+cudaError_t launch_win_gate(const DsaltWinGateParams& p, cudaStream_t st) {
+  if (p.T == 0) return cudaSuccess;
+  const unsigned grid = (unsigned)((p.T + 7) / 8);
+  switch (p.dtype) {
+    case DSALT_F16: win_gate_kernel<__half><<<grid, 256, 0, st>>>(p); break;
+    case DSALT_BF16: win_gate_kernel<__nv_bfloat16><<<grid, 256, 0, st>>>(p); break;
+    case DSALT_F32: win_gate_kernel<float><<<grid, 256, 0, st>>>(p); break;
+    default: return cudaErrorInvalidValue;
+  }
+  return cudaGetLastError();
+}
+
+// ------------------------------------------------------------- hybrid score
+// Pass 1: per token ‖x‖ and per kv-head ‖x W_Vᵀ‖, rounded to the dtype as
+// torch's norm on a dtype tensor is, then widened (landmark_tokens_ker.py:47,52).
+template <typename T>
+__global__ void __launch_bounds__(256) score_norms_kernel(DsaltScoreParams p) {
+  const int lane = threadIdx.x & 31;
+  const int64_t t = (int64_t)blockIdx.x * 8 + (threadIdx.x >> 5);
+  if (t >= p.T) return;
+  const T* x = reinterpret_cast<const T*>(p.x) + t * p.d_model;
+  float a = 0.f;
+  for (int d = lane; d < p.d_model; d += 32) { const float v = to_f32<T>(x[d]); a = fmaf(v, v, a); }
+  a = warp_sum(a);
+  const int ncols = 1 + p.n_kv;
+  if (lane == 0) p.norms[t * ncols] = round_to<T>(sqrtf(a));
+  const T* xv = reinterpret_cast<const T*>(p.xwv) + t * (int64_t)p.n_kv * p.dh;
+  for (int g = 0; g < p.n_kv; ++g) {
+    float b = 0.f;
+    for (int d = lane; d < p.dh; d += 32) { const float v = to_f32<T>(xv[g * p.dh + d]); b = fmaf(v, v, b); }
+    b = warp_sum(b);
+    if (lane == 0) p.norms[t * ncols + 1 + g] = round_to<T>(sqrtf(b));
+  }
+}
+
+// Pass 2 (one CTA): mean and unbiased std of every norm column over all T
+// packed tokens, accumulated in fp64 (landmark_tokens_ker.py:48, 53-54).
+__global__ void __launch_bounds__(1024) score_stats_kernel(DsaltScoreParams p) {
+  __shared__ double red[32];
+  const int ncols = 1 + p.n_kv;
+  for (int c = 0; c < ncols; ++c) {
+    double acc = 0.0;
+    for (int64_t t = threadIdx.x; t < p.T; t += blockDim.x) acc += p.norms[t * ncols + c];
+    acc = warp_sum_d(acc);
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = acc;
+    __syncthreads();
+    double tot = 0.0;
+    for (int w = 0; w < 32; ++w) tot += red[w];
+    __syncthreads();
+    const double mean = tot / (double)p.T;
+    double sq = 0.0;
+    for (int64_t t = threadIdx.x; t < p.T; t += blockDim.x) {
+      const double d = p.norms[t * ncols + c] - mean;
+      sq += d * d;
+    }
+    sq = warp_sum_d(sq);
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = sq;
+    __syncthreads();
+    double sqt = 0.0;
+    for (int w = 0; w < 32; ++w) sqt += red[w];
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      const float mu = (float)mean;
+      const float sd = p.T > 1 ? (float)sqrt(sqt / (double)(p.T - 1)) : NAN;
+      p.stats[2 * c] = mu;
+      p.stats[2 * c + 1] = fmaxf(sd, 1e-6f);
+    }
+  }
+}
+
+// Pass 3: z-scores and the per-head mix s = α·z_v + (1−α)·z_x (:49,55,60),
+// each op rounded to fp32 like the eager torch expression.
+__global__ void score_mix_kernel(DsaltScoreParams p) {
+  const int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (e >= p.T * p.H) return;
+  const int64_t t = e / p.H;
+  const int h = (int)(e % p.H);
+  const int ncols = 1 + p.n_kv;
+  const int g = h / (p.H / p.n_kv);
+  const float zx = __fdiv_rn(__fsub_rn(p.norms[t * ncols], p.stats[0]), p.stats[1]);
+  const float zv = __fdiv_rn(__fsub_rn(p.norms[t * ncols + 1 + g], p.stats[2 + 2 * g]), p.stats[3 + 2 * g]);
+  const float a = p.alpha[h];
+  p.scores[e] = __fadd_rn(__fmul_rn(a, zv), __fmul_rn(__fsub_rn(1.0f, a), zx));
+  if (p.z_v) p.z_v[e] = zv;
+  if (h == 0 && p.z_x) p.z_x[t] = zx;
+}
+
+cudaError_t launch_hybrid_scores(const DsaltScoreParams& p, cudaStream_t st) {
+  if (p.T == 0) return cudaSuccess;
+  const unsigned g1 = (unsigned)((p.T + 7) / 8);
+  switch (p.dtype) {
+    case DSALT_F16: score_norms_kernel<__half><<<g1, 256, 0, st>>>(p); break;
+    case DSALT_BF16: score_norms_kernel<__nv_bfloat16><<<g1, 256, 0, st>>>(p); break;
+    case DSALT_F32: score_norms_kernel<float><<<g1, 256, 0, st>>>(p); break;
+    default: return cudaErrorInvalidValue;
+  }
+  score_stats_kernel<<<1, 1024, 0, st>>>(p);
+  score_mix_kernel<<<(unsigned)((p.T * p.H + 255) / 256), 256, 0, st>>>(p);
+  return cudaGetLastError();
+}
+
+// -------------------------------------------------------------------- top-k
+// Orderable key: larger float -> larger unsigned; excluded / -inf -> 0.
+__device__ __forceinline__ uint32_t order_key(float f) {
+  if (!(f > -INFINITY)) return 0u;  // -inf and NaN are never selected
+  const uint32_t b = __float_as_uint(f);
+  return (b & 0x80000000u) ? ~b : (b | 0x80000000u);
+}
+
+constexpr int kTopkThreads = 1024;
+constexpr int kTopkMaxLen = 49152;  // keys held in shared memory
+constexpr int kTopkMaxK = 1024;
+
+// One CTA per (head, sequence): 4 rounds of 8-bit radix select find the k-th
+// largest key; the keys above it and the lowest-position ties fill the k slots.
+__global__ void __launch_bounds__(kTopkThreads) topk_kernel(DsaltTopkParams p) {
+  extern __shared__ uint32_t sm[];
+  uint32_t* keys = sm;                       // [max_len]
+  __shared__ uint32_t hist[256];
+  __shared__ uint32_t sel_prefix, sel_mask;
+  __shared__ int need, n_above, n_tie_taken;
+  __shared__ uint32_t out_key[kTopkMaxK];
+  __shared__ int out_pos[kTopkMaxK];
+
+  const int h = blockIdx.x / p.S;
+  const int s = blockIdx.x % p.S;
+  const int64_t s0 = p.cu_seqlens[s];
+  const int L = min((int)(p.cu_seqlens[s + 1] - s0), p.max_len);
+  const int tid = threadIdx.x;
+
+  for (int i = tid; i < L; i += kTopkThreads) {
+    const float ws = p.w_sizes[s0 + i];
+    // covered = seq_off < w_sizes.long()  (selectors.py:105) -> excluded
+    const bool covered = (float)i < truncf(ws);
+    keys[i] = covered ? 0u : order_key(p.scores[(s0 + i) * p.H + h]);
+  }
+  if (tid == 0) { sel_prefix = 0; sel_mask = 0; need = p.k; }
+  __syncthreads();
+
+  const int k_eff = min(p.k, L);
+  if (k_eff > 0) {
+    for (int shift = 24; shift >= 0; shift -= 8) {
+      for (int b = tid; b < 256; b += kTopkThreads) hist[b] = 0;
+      __syncthreads();
+      const uint32_t pre = sel_prefix, msk = sel_mask;
+      for (int i = tid; i < L; i += kTopkThreads) {
+        const uint32_t kk = keys[i];
+        if ((kk & msk) == pre) atomicAdd(&hist[(kk >> shift) & 255u], 1u);
+      }
+      __syncthreads();
+      if (tid == 0) {
+        int rem = (shift == 24) ? k_eff : need;
+        int b = 255;
+        for (; b > 0; --b) {
+          if ((int)hist[b] >= rem) break;
+          rem -= (int)hist[b];
+        }
+        sel_prefix = pre | ((uint32_t)b << shift);
+        sel_mask = msk | (255u << shift);
+        need = rem;  // how many keys equal to the final threshold are still needed
+      }
+      __syncthreads();
+    }
+  }
+  // threshold = sel_prefix (the k-th largest key); take all above, then `need` ties by position
+  const uint32_t thr = sel_prefix;
+  if (tid == 0) { n_above = 0; n_tie_taken = 0; }
+  __syncthreads();
+  if (k_eff > 0) {
+    for (int i = tid; i < L; i += kTopkThreads) {
+      if (keys[i] > thr) {
+        const int slot = atomicAdd(&n_above, 1);
+        if (slot < kTopkMaxK) { out_key[slot] = keys[i]; out_pos[slot] = i; }
+      }
+    }
+    __syncthreads();
+    // ties in position order: a single warp scans with ballots
+    if (tid < 32) {
+      int taken = 0;
+      const int base = n_above;
+      for (int i0 = 0; i0 < L && taken < need; i0 += 32) {
+        const int i = i0 + tid;
+        const bool tie = i < L && keys[i] == thr;
+        const uint32_t bal = __ballot_sync(0xffffffffu, tie);
+        const int before = __popc(bal & ((1u << tid) - 1u));
+        if (tie && taken + before < need) {
+          const int slot = base + taken + before;
+          if (slot < kTopkMaxK) { out_key[slot] = thr; out_pos[slot] = i; }
+        }
+        taken += __popc(bal);
+      }
+      if (tid == 0) n_tie_taken = min(taken, need);
+    }
+  }
+  __syncthreads();
+  const int n_sel = k_eff > 0 ? min(n_above + n_tie_taken, k_eff) : 0;
+  // order the selection: key descending, position ascending
+  int64_t* out = p.idx + ((int64_t)h * p.S + s) * p.k;
+  for (int r = tid; r < p.k; r += kTopkThreads) out[r] = -1;
+  __syncthreads();
+  for (int a = tid; a < n_sel; a += kTopkThreads) {
+    const uint32_t ka = out_key[a];
+    const int pa = out_pos[a];
+    int rank = 0;
+    for (int b = 0; b < n_sel; ++b) {
+      const uint32_t kb = out_key[b];
+      rank += (kb > ka) || (kb == ka && out_pos[b] < pa);
+    }
+    out[rank] = ka == 0u ? -1 : (int64_t)pa;  // non-finite scores give -1 (selectors.py:131-132)
+  }
+}
+
+cudaError_t launch_topk(const DsaltTopkParams& p, cudaStream_t st) {
+  if (p.H * p.S == 0) return cudaSuccess;
+  const size_t smem = sizeof(uint32_t) * (size_t)max(p.max_len, 1);
+  cudaError_t e = cudaFuncSetAttribute(topk_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  if (e != cudaSuccess) return e;
+  topk_kernel<<<p.H * p.S, kTopkThreads, smem, st>>>(p);
+  return cudaGetLastError();
+}
+
+}  // namespace dsalt

@@ -1,0 +1,183 @@
+"""ctypes binding of ``libdsalt_b200.so`` (the C ABI in ``include/dsalt_b200.h``).
+
+The library is built in-tree by ``dsalt-library_b200/build.py`` into
+``dsalt/_lib/libdsalt_b200.so``.  There is no fallback: if the library is
+missing or no CUDA device is present, every op raises.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import os
+from pathlib import Path
+
+import torch
+
+_LIB_PATH = Path(__file__).resolve().parents[1] / "_lib" / "libdsalt_b200.so"
+
+# status / enum values of include/dsalt_b200.h
+OK = 0
+F16, BF16, F32 = 0, 1, 2
+TRAIN, INFER = 0, 1
+IMPL_AUTO, IMPL_SIMT, IMPL_TCGEN05 = 0, 1, 2
+DEV_WAIT_TIMEOUT, DEV_BAD_INDEX = 1, 2
+
+_c_void_p = ctypes.c_void_p
+_i32 = ctypes.c_int32
+_i64 = ctypes.c_int64
+_f32 = ctypes.c_float
+
+
+class ScheduleParams(ctypes.Structure):
+    _fields_ = [("cu_seqlens", _c_void_p), ("w", _c_void_p), ("block_map", _c_void_p),
+                ("num_blocks", _c_void_p), ("seq_wmax", _c_void_p), ("seq_id", _c_void_p),
+                ("T", _i64), ("S", _i32), ("block", _i32), ("max_blocks", _i32),
+                ("semantics", _i32)]
+
+
+class GatherParams(ctypes.Structure):
+    _fields_ = [("k", _c_void_p), ("v", _c_void_p), ("lmk_pos", _c_void_p), ("lmk_w", _c_void_p),
+                ("cu_seqlens", _c_void_p), ("lmk_k", _c_void_p), ("lmk_v", _c_void_p),
+                ("pos_sorted", _c_void_p), ("w_sorted", _c_void_p), ("perm", _c_void_p),
+                ("lmk_slot", _c_void_p), ("status", _c_void_p),
+                ("T", _i64), ("H", _i32), ("D", _i32), ("S", _i32), ("k_lmk", _i32), ("kp", _i32),
+                ("dtype", _i32)]
+
+
+class AttnParams(ctypes.Structure):
+    _fields_ = [("q", _c_void_p), ("k", _c_void_p), ("v", _c_void_p), ("w", _c_void_p),
+                ("cu_seqlens", _c_void_p), ("block_map", _c_void_p), ("num_blocks", _c_void_p),
+                ("seq_wmax", _c_void_p), ("lmk_k", _c_void_p), ("lmk_v", _c_void_p),
+                ("pos_sorted", _c_void_p), ("w_sorted", _c_void_p), ("perm", _c_void_p),
+                ("lmk_slot", _c_void_p),
+                ("o", _c_void_p), ("o_f32", _c_void_p), ("lse", _c_void_p),
+                ("dout", _c_void_p), ("delta", _c_void_p), ("dq", _c_void_p), ("dk", _c_void_p),
+                ("dv", _c_void_p), ("dw_head", _c_void_p), ("dw", _c_void_p), ("d_lw", _c_void_p),
+                ("status", _c_void_p),
+                ("T", _i64), ("H", _i32), ("D", _i32), ("S", _i32), ("k_lmk", _i32), ("kp", _i32),
+                ("max_blocks", _i32), ("scale", _f32), ("tau_win", _f32), ("win_edge", _f32),
+                ("semantics", _i32), ("dtype", _i32), ("impl", _i32)]
+
+
+class ScoreParams(ctypes.Structure):
+    _fields_ = [("x", _c_void_p), ("xwv", _c_void_p), ("alpha", _c_void_p), ("scores", _c_void_p),
+                ("z_x", _c_void_p), ("z_v", _c_void_p), ("stats", _c_void_p), ("norms", _c_void_p),
+                ("T", _i64), ("d_model", _i32), ("H", _i32), ("n_kv", _i32), ("dh", _i32),
+                ("dtype", _i32)]
+
+
+class TopkParams(ctypes.Structure):
+    _fields_ = [("scores", _c_void_p), ("w_sizes", _c_void_p), ("cu_seqlens", _c_void_p),
+                ("idx", _c_void_p), ("T", _i64), ("H", _i32), ("S", _i32), ("k", _i32),
+                ("max_len", _i32)]
+
+
+class WinGateParams(ctypes.Structure):
+    _fields_ = [("x", _c_void_p), ("weight", _c_void_p), ("bias", _c_void_p), ("w_cont", _c_void_p),
+                ("w_f32", _c_void_p), ("w_disc", _c_void_p), ("logits", _c_void_p),
+                ("T", _i64), ("d_model", _i32), ("n_min", _f32), ("n_max", _f32), ("dtype", _i32)]
+
+
+_STRUCTS = [ScheduleParams, GatherParams, AttnParams, ScoreParams, TopkParams, WinGateParams]
+_ENTRY = {
+    "dsalt_build_schedule": ScheduleParams,
+    "dsalt_gather_landmarks": GatherParams,
+    "dsalt_attn_fwd": AttnParams,
+    "dsalt_attn_bwd_preprocess": AttnParams,
+    "dsalt_attn_bwd_dkdv": AttnParams,
+    "dsalt_attn_bwd_dq": AttnParams,
+    "dsalt_hybrid_scores": ScoreParams,
+    "dsalt_select_topk": TopkParams,
+    "dsalt_win_gate": WinGateParams,
+}
+
+_lib = None
+
+
+def lib_path() -> Path:
+    return Path(os.environ.get("DSALT_B200_LIB", str(_LIB_PATH)))
+
+
+def load() -> ctypes.CDLL:
+    """Load (once) and check the shared library; raise if it is missing or stale."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    path = lib_path()
+    if not path.exists():
+        raise RuntimeError(
+            f"DSALT CUDA library not found at {path}; build it with "
+            "`python dsalt-library_b200/build.py` (there is no CPU fallback)")
+    lib = ctypes.CDLL(str(path))
+    lib.dsalt_b200_abi_version.restype = ctypes.c_int
+    lib.dsalt_b200_status_string.restype = ctypes.c_char_p
+    lib.dsalt_b200_status_string.argtypes = [ctypes.c_int]
+    lib.dsalt_b200_params_sizeof.restype = ctypes.c_int
+    lib.dsalt_b200_params_sizeof.argtypes = [ctypes.c_int]
+    if lib.dsalt_b200_abi_version() != 1:
+        raise RuntimeError("libdsalt_b200.so ABI version mismatch; rebuild the library")
+    for i, st in enumerate(_STRUCTS):
+        n = lib.dsalt_b200_params_sizeof(i)
+        if n != ctypes.sizeof(st):
+            raise RuntimeError(f"{st.__name__}: ctypes size {ctypes.sizeof(st)} != C size {n}")
+    for name, st in _ENTRY.items():
+        fn = getattr(lib, name)
+        fn.restype = ctypes.c_int
+        fn.argtypes = [ctypes.POINTER(st), ctypes.c_void_p]
+    _lib = lib
+    return lib
+
+
+def status_string(code: int) -> str:
+    return load().dsalt_b200_status_string(int(code)).decode()
+
+
+# Optional launch recorder: when a list, every call appends (name, start, end)
+# CUDA events recorded on the launching stream (used by the benchmark to time
+# individual kernels live).
+RECORD: list | None = None
+
+
+def call(name: str, params) -> None:
+    """Launch ``name`` on the current CUDA stream; raise RuntimeError on a bad status."""
+    lib = load()
+    cs = torch.cuda.current_stream()
+    rec = RECORD
+    if rec is not None:
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record(cs)
+    rc = getattr(lib, name)(ctypes.byref(params), ctypes.c_void_p(cs.cuda_stream))
+    if rc != OK:
+        raise RuntimeError(f"{name} failed: {status_string(rc)} (status {rc})")
+    if rec is not None:
+        e1.record(cs)
+        rec.append((name, e0, e1))
+
+
+def ptr(t) -> int:
+    """Device address of a tensor (0 for None)."""
+    return 0 if t is None else int(t.data_ptr())
+
+
+def dtype_code(dt: torch.dtype) -> int:
+    if dt == torch.float16:
+        return F16
+    if dt == torch.bfloat16:
+        return BF16
+    if dt == torch.float32:
+        return F32
+    raise TypeError(f"unsupported dtype {dt}")
+
+
+def require_cuda(t: torch.Tensor, what: str = "input") -> None:
+    if not t.is_cuda:
+        raise RuntimeError(
+            f"dsalt (B200 build) runs on CUDA devices only; {what} is on {t.device} "
+            "(there is no CPU fallback)")
+
+
+def default_impl() -> int:
+    """Kernel family: DSALT_IMPL env var ('auto' | 'simt' | 'tcgen05')."""
+    v = os.environ.get("DSALT_IMPL", "auto").lower()
+    return {"auto": IMPL_AUTO, "simt": IMPL_SIMT, "tcgen05": IMPL_TCGEN05}.get(v, IMPL_AUTO)

@@ -1,0 +1,196 @@
+"""Host side of the DSALT attention op on B200: buffer allocation and launches.
+
+Every launch goes through the C ABI of ``libdsalt_b200.so`` (``_ext``).  This
+module owns the order of the stages and the scratch buffers; the autograd
+Functions with the reference's signatures live in ``dsalt_triton_train`` and
+``dsalt_triton_attn`` (module names kept so the package drops in for the
+reference's Triton path).
+
+Stages (reference counterparts in dsalt/kernels/dsalt_triton_train.py):
+  schedule  (seq, block) table + per-sequence max window   (_build_seq_block_map, :618)
+  gather    landmarks sorted by position, K/V rows gathered (_build_landmark_kv, :617)
+  fwd       O (input dtype), O as fp32, LSE                 (_train_fwd_kernel, :629-645)
+  bwd       Delta, key-parallel dK/dV/d_logw, query-parallel dQ/d_w̃
+                                                            (:693-745)
+"""
+
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass
+
+import torch
+
+from . import _ext
+
+BLOCK_M = 128  # query rows per tensor-core tile (tcgen05 M=128)
+
+_STATUS: dict = {}
+
+
+def device_status(device: torch.device) -> torch.Tensor:
+    """Per-device int32 status word the kernels OR their fault bits into."""
+    key = (device.type, device.index if device.index is not None else torch.cuda.current_device())
+    st = _STATUS.get(key)
+    if st is None:
+        st = torch.zeros(1, dtype=torch.int32, device=device)
+        _STATUS[key] = st
+    return st
+
+
+def check_device_status(device: torch.device, reset: bool = True) -> int:
+    """Read (and optionally clear) the device status word; raise on a fault bit."""
+    st = device_status(device)
+    v = int(st.item())
+    if reset:
+        st.zero_()
+    if v & _ext.DEV_WAIT_TIMEOUT:
+        raise RuntimeError("dsalt kernel: an mbarrier wait timed out (device status %d)" % v)
+    if v & _ext.DEV_BAD_INDEX:
+        raise RuntimeError("dsalt kernel: an index was out of range (device status %d)" % v)
+    return v
+
+
+def padded_landmarks(k_lmk: int) -> int:
+    """Landmark slots after padding: a multiple of 16, at least 16 (0 stays 0)."""
+    return 0 if k_lmk <= 0 else max(16, (k_lmk + 15) // 16 * 16)
+
+
+@dataclass
+class Prepared:
+    """Per-call metadata shared by the forward and the backward."""
+    T: int
+    H: int
+    D: int
+    S: int
+    k_lmk: int
+    kp: int
+    semantics: int
+    cu: torch.Tensor
+    w: torch.Tensor
+    block_map: torch.Tensor
+    num_blocks: torch.Tensor
+    seq_wmax: torch.Tensor
+    lmk_k: torch.Tensor
+    lmk_v: torch.Tensor
+    pos_sorted: torch.Tensor
+    w_sorted: torch.Tensor
+    perm: torch.Tensor
+    lmk_slot: torch.Tensor
+    max_blocks: int
+
+
+def prepare(k_c: torch.Tensor, v_c: torch.Tensor, lmk_pos: torch.Tensor, lmk_w: torch.Tensor,
+            w: torch.Tensor, cu_seqlens: torch.Tensor, semantics: int) -> Prepared:
+    """Build the schedule and the sorted landmark buffers on the device."""
+    T, H, D = k_c.shape
+    dev = k_c.device
+    cu = cu_seqlens.to(device=dev, dtype=torch.int32).contiguous()
+    S = cu.shape[0] - 1
+    if lmk_pos.dim() != 3 or lmk_pos.shape[0] != H or lmk_pos.shape[1] != S:
+        raise ValueError(f"lmk_pos must be [H={H}, S={S}, k], got {tuple(lmk_pos.shape)}")
+    k_lmk = int(lmk_pos.shape[2])
+    kp = padded_landmarks(k_lmk)
+    w32 = w.detach().to(device=dev, dtype=torch.float32).contiguous()
+    if w32.shape != (T,):
+        raise ValueError(f"window must be [T={T}], got {tuple(w32.shape)}")
+    max_blocks = (T + BLOCK_M - 1) // BLOCK_M + S
+    block_map = torch.empty(max(max_blocks, 1), 2, dtype=torch.int32, device=dev)
+    num_blocks = torch.empty(1, dtype=torch.int32, device=dev)
+    seq_wmax = torch.empty(max(S, 1), dtype=torch.int32, device=dev)
+    sp = _ext.ScheduleParams(
+        cu_seqlens=_ext.ptr(cu), w=_ext.ptr(w32), block_map=_ext.ptr(block_map),
+        num_blocks=_ext.ptr(num_blocks), seq_wmax=_ext.ptr(seq_wmax), seq_id=0,
+        T=T, S=S, block=BLOCK_M, max_blocks=max_blocks, semantics=semantics)
+    _ext.call("dsalt_build_schedule", sp)
+
+    dt = k_c.dtype
+    lmk_k = torch.empty(H, S, kp, D, dtype=dt, device=dev)
+    lmk_v = torch.empty(H, S, kp, D, dtype=dt, device=dev)
+    pos_sorted = torch.empty(H, S, kp, dtype=torch.int32, device=dev)
+    w_sorted = torch.empty(H, S, kp, dtype=torch.float32, device=dev)
+    perm = torch.empty(H, S, kp, dtype=torch.int32, device=dev)
+    lmk_slot = torch.empty(T, H, dtype=torch.int32, device=dev)
+    if kp > 0 and S > 0:
+        lp = lmk_pos.detach().to(device=dev, dtype=torch.int64).contiguous()
+        lw = lmk_w.detach().to(device=dev, dtype=torch.float32).contiguous()
+        gp = _ext.GatherParams(
+            k=_ext.ptr(k_c), v=_ext.ptr(v_c), lmk_pos=_ext.ptr(lp), lmk_w=_ext.ptr(lw),
+            cu_seqlens=_ext.ptr(cu), lmk_k=_ext.ptr(lmk_k), lmk_v=_ext.ptr(lmk_v),
+            pos_sorted=_ext.ptr(pos_sorted), w_sorted=_ext.ptr(w_sorted), perm=_ext.ptr(perm),
+            lmk_slot=_ext.ptr(lmk_slot), status=_ext.ptr(device_status(dev)),
+            T=T, H=H, D=D, S=S, k_lmk=k_lmk, kp=kp, dtype=_ext.dtype_code(dt))
+        _ext.call("dsalt_gather_landmarks", gp)
+    else:
+        lmk_slot.fill_(-1)
+    return Prepared(T, H, D, S, k_lmk, kp, semantics, cu, w32, block_map, num_blocks, seq_wmax,
+                    lmk_k, lmk_v, pos_sorted, w_sorted, perm, lmk_slot, max_blocks)
+
+
+def _params(prep: Prepared, q_c, k_c, v_c, tau_win: float, win_edge: float, impl: int,
+            **bufs) -> _ext.AttnParams:
+    p = _ext.AttnParams(
+        q=_ext.ptr(q_c), k=_ext.ptr(k_c), v=_ext.ptr(v_c), w=_ext.ptr(prep.w),
+        cu_seqlens=_ext.ptr(prep.cu), block_map=_ext.ptr(prep.block_map),
+        num_blocks=_ext.ptr(prep.num_blocks), seq_wmax=_ext.ptr(prep.seq_wmax),
+        lmk_k=_ext.ptr(prep.lmk_k), lmk_v=_ext.ptr(prep.lmk_v), pos_sorted=_ext.ptr(prep.pos_sorted),
+        w_sorted=_ext.ptr(prep.w_sorted), perm=_ext.ptr(prep.perm), lmk_slot=_ext.ptr(prep.lmk_slot),
+        status=_ext.ptr(device_status(q_c.device)),
+        T=prep.T, H=prep.H, D=prep.D, S=prep.S, k_lmk=prep.k_lmk, kp=prep.kp,
+        max_blocks=prep.max_blocks, scale=1.0 / math.sqrt(prep.D), tau_win=float(tau_win),
+        win_edge=float(win_edge) if prep.semantics == _ext.TRAIN else 0.0,
+        semantics=prep.semantics, dtype=_ext.dtype_code(q_c.dtype), impl=impl)
+    for name, t in bufs.items():
+        setattr(p, name, _ext.ptr(t))
+    return p
+
+
+def forward(q_c, k_c, v_c, prep: Prepared, tau_win: float, win_edge: float, impl: int):
+    """Run the forward; returns ``(o [T,H,D] input dtype, o_f32 [T,H,D] fp32, lse [T,H] fp32)``."""
+    o = torch.empty_like(q_c)
+    o_f32 = torch.empty(q_c.shape, dtype=torch.float32, device=q_c.device) \
+        if q_c.dtype != torch.float32 else None
+    lse = torch.empty(prep.T, prep.H, dtype=torch.float32, device=q_c.device)
+    p = _params(prep, q_c, k_c, v_c, tau_win, win_edge, impl, o=o, o_f32=o_f32, lse=lse)
+    _ext.call("dsalt_attn_fwd", p)
+    return o, (o_f32 if o_f32 is not None else o), lse
+
+
+def backward(do_c, q_c, k_c, v_c, o, lse, prep: Prepared, tau_win: float, win_edge: float,
+             impl: int, want_dw: bool):
+    """Run the backward stages; returns ``(dq, dk, dv, d_lw [H,S,k] fp32, dw [T] or None)``."""
+    dev = q_c.device
+    T, H = prep.T, prep.H
+    delta = torch.empty(T, H, dtype=torch.float32, device=dev)
+    dq = torch.empty_like(q_c)
+    dk = torch.empty_like(k_c)
+    dv = torch.empty_like(v_c)
+    d_lw = torch.zeros(H, prep.S, prep.k_lmk, dtype=torch.float32, device=dev)
+    dw_head = torch.empty(T, H, dtype=torch.float32, device=dev) if want_dw else None
+    dw = torch.empty(T, dtype=q_c.dtype, device=dev) if want_dw else None
+    p = _params(prep, q_c, k_c, v_c, tau_win, win_edge, impl, o=o, lse=lse, dout=do_c,
+                delta=delta, dq=dq, dk=dk, dv=dv, dw_head=dw_head, dw=dw, d_lw=d_lw)
+    _ext.call("dsalt_attn_bwd_preprocess", p)
+    _ext.call("dsalt_attn_bwd_dkdv", p)
+    _ext.call("dsalt_attn_bwd_dq", p)
+    return dq, dk, dv, d_lw, dw
+
+
+def compute_dtype(q: torch.Tensor) -> torch.dtype:
+    """Arithmetic dtype of the op: the input dtype (fp16, bf16 or exact fp32)."""
+    if q.dtype in (torch.float16, torch.bfloat16, torch.float32):
+        return q.dtype
+    raise TypeError(f"unsupported dtype {q.dtype}")
+
+
+def check_inputs(q, k, v, cu_seqlens):
+    for name, t in (("q", q), ("k", k), ("v", v)):
+        _ext.require_cuda(t, name)
+        if t.dim() != 3:
+            raise ValueError(f"{name} must be [T, H, D], got {tuple(t.shape)}")
+    if k.shape != q.shape or v.shape != q.shape:
+        raise ValueError(f"q/k/v shapes differ: {tuple(q.shape)} {tuple(k.shape)} {tuple(v.shape)}")
+    if q.shape[2] not in (32, 64, 128, 256):
+        raise ValueError(f"head_dim {q.shape[2]} not supported (32, 64, 128, 256)")
+    if cu_seqlens.dim() != 1 or cu_seqlens.shape[0] < 1:
+        raise ValueError("cu_seqlens must be a 1-D tensor [S+1]")

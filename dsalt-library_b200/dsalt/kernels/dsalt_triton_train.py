@@ -1,0 +1,109 @@
+"""DSALT training attention op on B200 (module name kept from the reference).
+
+Drop-in for ``dsalt/kernels/dsalt_triton_train.py`` of the reference: the same
+``DSALTTrainFunction`` signature (11 positional arguments, 11 gradients) and the
+same public wrapper ``dsalt_triton_train_attention``.  The kernels are
+hand-written sm_100a CUDA behind the C ABI of ``libdsalt_b200.so``; there is no
+Triton and no CPU fallback.
+
+Semantics (reference ``_train_fwd_kernel``, dsalt_triton_train.py:116-214):
+query ``i`` attends the band ``0 ≤ i − j ≤ w̃(i)`` with the soft-edge log-bias
+``log σ((w̃ − d)/τ_win)`` outside the core ``d ≤ w̃ − win_edge``, plus the
+landmarks ``p`` of its (head, sequence) with ``p ≤ i`` and ``p < i − w̃(i)``,
+biased by ``lmk_logw``.  The backward returns ``d_w̃`` (summed over heads) and
+``d_logw``, which autograd carries to ``win_gate`` and ``α``.
+
+Differences from the reference, all deliberate:
+  * fp32 inputs are computed in exact fp32 (SIMT kernels) instead of being cast
+    to fp16 (reference :601-604), so fp32 results match the fp32 dense path;
+  * the key-parallel dK/dV scan covers each sequence's actual largest window,
+    so gradients stay exact even when ``w̃ > n_max`` (the reference bounds the
+    scan with ``n_max``, :439-444); ``n_max`` is accepted and unused;
+  * landmark dK/dV/d_logw and d_w̃ are accumulated without atomics, so the
+    backward is bitwise deterministic (reference :327-333, :382-383);
+  * no autotune: tile shapes are fixed for B200 (see ``autotune``).
+"""
+
+from __future__ import annotations
+
+import torch
+
+from . import _ext
+from . import dsalt_cuda as _cuda
+
+
+def _host_cu(cu_seqlens: torch.Tensor, cu_list):
+    if cu_list is not None:
+        return [int(c) for c in cu_list]
+    return [int(c) for c in cu_seqlens.detach().to("cpu").tolist()]
+
+
+def _validate_cu(cu, T: int) -> None:
+    if len(cu) < 1 or cu[0] != 0 or cu[-1] != T:
+        raise ValueError(f"cu_seqlens must start at 0 and end at T={T}, got {cu[:1]}..{cu[-1:]}")
+    for a, b in zip(cu[:-1], cu[1:]):
+        if b < a:
+            raise ValueError("cu_seqlens must be non-decreasing")
+
+
+class DSALTTrainFunction(torch.autograd.Function):
+    """Autograd Function with the reference signature (dsalt_triton_train.py:585-760)."""
+
+    @staticmethod
+    def forward(ctx, q, k, v, lmk_pos, lmk_logw, w_cont, cu_seqlens,
+                tau_win, win_edge, n_max, cu_list=None):
+        _cuda.check_inputs(q, k, v, cu_seqlens)
+        total_len = q.shape[0]
+        _validate_cu(_host_cu(cu_seqlens, cu_list), total_len)
+        dt = _cuda.compute_dtype(q)
+        q_c = q.contiguous().to(dt)
+        k_c = k.contiguous().to(dt)
+        v_c = v.contiguous().to(dt)
+        impl = _ext.default_impl()
+        with torch.no_grad():
+            prep = _cuda.prepare(k_c, v_c, lmk_pos, lmk_logw, w_cont, cu_seqlens, _ext.TRAIN)
+            o, o_f32, lse = _cuda.forward(q_c, k_c, v_c, prep, float(tau_win), float(win_edge), impl)
+        ctx.save_for_backward(q_c, k_c, v_c, o, lse)
+        ctx.prep = prep
+        ctx.tau_win = float(tau_win)
+        ctx.win_edge = float(win_edge)
+        ctx.impl = impl
+        ctx.out_dtype = q.dtype
+        ctx.w_dtype = w_cont.dtype
+        ctx.lw_dtype = lmk_logw.dtype
+        # fp32 view of the input-dtype output, written by the kernel itself
+        # (the reference returns out.float(), :663)
+        return o_f32
+
+    @staticmethod
+    def backward(ctx, grad_out):
+        q_c, k_c, v_c, o, lse = ctx.saved_tensors
+        do_c = grad_out.contiguous().to(q_c.dtype)
+        dq, dk, dv, d_lw, dw = _cuda.backward(do_c, q_c, k_c, v_c, o, lse, ctx.prep, ctx.tau_win,
+                                              ctx.win_edge, ctx.impl, want_dw=True)
+        od = ctx.out_dtype
+        return (dq.to(od), dk.to(od), dv.to(od),
+                None,                 # lmk_pos
+                d_lw.to(od),          # -> alpha through log σ(s/τ)
+                dw.to(od),            # -> win_gate through w̃
+                None, None, None,     # cu_seqlens, tau_win, win_edge
+                None,                 # n_max
+                None)                 # cu_list
+
+
+def _dynamo_opaque(fn):
+    disable = getattr(getattr(torch, "_dynamo", None), "disable", None)
+    return disable(fn) if disable is not None else fn
+
+
+@_dynamo_opaque
+def dsalt_triton_train_attention(q, k, v, lmk_pos, lmk_logw, w_cont, cu_seqlens,
+                                 tau_win=1.0, win_edge=4.0, n_max=256, cu_list=None):
+    """Differentiable sparse DSALT attention for training (reference :770-782).
+
+    ``q, k, v`` ``[T, H, D]``; ``lmk_pos`` ``[H, S, k]`` positions inside each
+    sequence (-1 = empty); ``lmk_logw`` ``[H, S, k]``; ``w_cont`` ``[T]``;
+    ``cu_seqlens`` ``[S+1]``.  Returns ``O`` ``[T, H, D]`` float32.
+    """
+    return DSALTTrainFunction.apply(q, k, v, lmk_pos, lmk_logw, w_cont, cu_seqlens,
+                                    tau_win, win_edge, n_max, cu_list)

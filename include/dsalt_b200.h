@@ -1,0 +1,238 @@
+/*
+ * dsalt_b200.h — C ABI of the B200 (sm_100a) DSALT sparse-attention library.
+ *
+ * Every entry point takes caller-owned device buffers (plain pointers and
+ * sizes), launches on the caller's CUDA stream (`stream` is a CUstream /
+ * cudaStream_t handle passed as void*), allocates no device memory and returns
+ * a status code (DSALT_OK == 0).  Argument errors are reported before any
+ * launch; a device-side fault report (a bounded wait that gave up, an index
+ * outside its range) is written to the optional device status word
+ * `status` (int32, caller-zeroed) instead of trapping.
+ *
+ * Reference interfaces replaced (paths relative to the reference project,
+ * LeonardoCofone/dsalt-library v1.0.0) are cited beside each entry point.
+ * The Python host package `dsalt` (same module paths as the reference) binds
+ * these with ctypes; INTEGRATION.md shows the binding.
+ */
+#ifndef DSALT_B200_H
+#define DSALT_B200_H
+
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define DSALT_API __attribute__((visibility("default")))
+#else
+#define DSALT_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define DSALT_B200_ABI_VERSION 1
+
+/* ---- status codes ------------------------------------------------------ */
+enum {
+  DSALT_OK = 0,
+  DSALT_ERR_ARG = 1,          /* invalid argument (shape, pointer, range)      */
+  DSALT_ERR_DTYPE = 2,        /* unsupported dtype                             */
+  DSALT_ERR_HEAD_DIM = 3,     /* unsupported head_dim                          */
+  DSALT_ERR_LAUNCH = 4,       /* CUDA launch / API error                       */
+  DSALT_ERR_NO_DEVICE = 5,    /* no sm_100 device / driver entry point missing */
+  DSALT_ERR_ALIGN = 6,        /* pointer not 16-byte aligned                   */
+  DSALT_ERR_TOO_LARGE = 7     /* size beyond a documented limit                */
+};
+
+/* device status word bits (written by kernels, never a trap) */
+enum {
+  DSALT_DEV_WAIT_TIMEOUT = 1, /* an mbarrier wait exceeded its time limit      */
+  DSALT_DEV_BAD_INDEX = 2     /* an index (landmark position, seq id) was out of range */
+};
+
+/* dtype codes */
+enum { DSALT_F16 = 0, DSALT_BF16 = 1, DSALT_F32 = 2 };
+
+/* attention semantics */
+enum {
+  DSALT_TRAIN = 0,  /* continuous window w̃, soft edge, lmk bias = log-weight    */
+  DSALT_INFER = 1   /* integer window w, no edge, additive lmk bias             */
+};
+
+/* kernel family selection */
+enum {
+  DSALT_IMPL_AUTO = 0,    /* tcgen05 for f16/bf16, exact-fp32 SIMT for f32     */
+  DSALT_IMPL_SIMT = 1,    /* exact SIMT kernels for every dtype                */
+  DSALT_IMPL_TCGEN05 = 2  /* tcgen05/TMEM/TMA kernels (f16/bf16 only)          */
+};
+
+/* ---- packed-batch schedule ---------------------------------------------
+ * Replaces selectors._build_seq_block_map (dsalt/kernels/selectors.py:37-67)
+ * and selectors._seq_meta (:15-34).  Built on the device from cu_seqlens and
+ * the window, keyed by content (no host cache), no device-to-host copy.
+ *   block_map [max_blocks][2] int32 = (sequence, block-in-sequence) for
+ *     blocks of `block` query rows; rows past num_blocks are untouched;
+ *   num_blocks [1] int32; seq_wmax [S] int32 = max over the sequence's rows of
+ *     the number of band keys before the diagonal (floor(w̃) train, w-1 infer);
+ *   seq_id [T] int32 = sequence of every packed token (optional, may be NULL).
+ * max_blocks must be >= ceil(T/block) + S.                                    */
+typedef struct DsaltScheduleParams {
+  const int32_t* cu_seqlens;  /* [S+1] */
+  const float* w;             /* [T] window, fp32 */
+  int32_t* block_map;         /* [max_blocks*2] */
+  int32_t* num_blocks;        /* [1] */
+  int32_t* seq_wmax;          /* [S] */
+  int32_t* seq_id;            /* [T] or NULL */
+  int64_t T;
+  int32_t S;
+  int32_t block;
+  int32_t max_blocks;
+  int32_t semantics;
+} DsaltScheduleParams;
+DSALT_API int dsalt_build_schedule(const DsaltScheduleParams* p, void* stream);
+
+/* ---- landmark gather ----------------------------------------------------
+ * Replaces selectors._build_landmark_kv (dsalt/kernels/selectors.py:137-159)
+ * and _pad_landmarks (dsalt/kernels/dsalt_triton_train.py:44-68).  Per
+ * (head, sequence): sorts the k landmark slots by position (invalid slots,
+ * pos < 0 or pos >= len, last), pads to kp, gathers K/V rows into
+ * [H,S,kp,D] (zeros for invalid), copies the log-weight / bias in sorted
+ * order, records the caller's slot of every sorted entry (perm) and writes
+ * the reverse map lmk_slot[T,H] (sorted slot of the first landmark at that
+ * token, else -1; the caller pre-fills it with -1).                         */
+typedef struct DsaltGatherParams {
+  const void* k;              /* [T,H,D] dtype */
+  const void* v;              /* [T,H,D] dtype */
+  const int64_t* lmk_pos;     /* [H,S,k_lmk] caller order, relative positions */
+  const float* lmk_w;         /* [H,S,k] log-weight (train) / bias (infer), fp32 */
+  const int32_t* cu_seqlens;  /* [S+1] */
+  void* lmk_k;                /* [H,S,kp,D] dtype */
+  void* lmk_v;                /* [H,S,kp,D] dtype */
+  int32_t* pos_sorted;        /* [H,S,kp] (-1 = invalid) */
+  float* w_sorted;            /* [H,S,kp] */
+  int32_t* perm;              /* [H,S,kp] caller slot (-1 for padding) */
+  int32_t* lmk_slot;          /* [T,H] */
+  int32_t* status;            /* device status word or NULL */
+  int64_t T;
+  int32_t H, D, S, k_lmk, kp;
+  int32_t dtype;
+} DsaltGatherParams;
+DSALT_API int dsalt_gather_landmarks(const DsaltGatherParams* p, void* stream);
+
+/* ---- attention ------------------------------------------------------------
+ * One parameter block for the forward and the three backward stages.
+ * Layouts: q,k,v,o,dout,dq,dk,dv [T,H,D] contiguous; lse, delta, dw_head
+ * [T,H] fp32; landmark buffers from dsalt_gather_landmarks.                 */
+typedef struct DsaltAttnParams {
+  /* inputs */
+  const void* q; const void* k; const void* v;
+  const float* w;             /* [T] w̃ (train) or w (infer), fp32 */
+  const int32_t* cu_seqlens;  /* [S+1] */
+  const int32_t* block_map;   /* from dsalt_build_schedule (block = 128) */
+  const int32_t* num_blocks;
+  const int32_t* seq_wmax;    /* [S] */
+  const void* lmk_k; const void* lmk_v;
+  const int32_t* pos_sorted; const float* w_sorted; const int32_t* perm;
+  const int32_t* lmk_slot;
+  /* forward outputs */
+  void* o;                    /* [T,H,D] dtype (saved for the backward) */
+  float* o_f32;               /* [T,H,D] fp32 copy of bf16/f16-rounded O, or NULL */
+  float* lse;                 /* [T,H] natural-log LSE, -inf for empty rows */
+  /* backward */
+  const void* dout;           /* [T,H,D] dtype */
+  float* delta;               /* [T,H] scratch */
+  void* dq; void* dk; void* dv;       /* [T,H,D] dtype */
+  float* dw_head;             /* [T,H] scratch (train) */
+  void* dw;                   /* [T] dtype: Σ_h ∂loss/∂w̃ (train) or NULL */
+  float* d_lw;                /* [H,S,k_lmk] fp32, caller slot order: ∂loss/∂lmk_w */
+  int32_t* status;            /* device status word or NULL */
+  /* sizes */
+  int64_t T;
+  int32_t H, D, S, k_lmk, kp;
+  int32_t max_blocks;
+  float scale;                /* 1/sqrt(D) */
+  float tau_win, win_edge;
+  int32_t semantics;          /* DSALT_TRAIN / DSALT_INFER */
+  int32_t dtype;              /* DSALT_F16 / DSALT_BF16 / DSALT_F32 */
+  int32_t impl;               /* DSALT_IMPL_* */
+} DsaltAttnParams;
+
+/* Replaces _train_fwd_kernel (dsalt/kernels/dsalt_triton_train.py:74-214) and
+ * _dsalt_fwd_kernel (dsalt/kernels/dsalt_triton_attn.py:27-169).             */
+DSALT_API int dsalt_attn_fwd(const DsaltAttnParams* p, void* stream);
+/* Replaces _train_bwd_preprocess (dsalt_triton_train.py:220-237) and
+ * _dsalt_bwd_preprocess (dsalt/kernels/dsalt_triton_bwd.py:17-49).           */
+DSALT_API int dsalt_attn_bwd_preprocess(const DsaltAttnParams* p, void* stream);
+/* Replaces _train_bwd_dkdv_kernel (dsalt_triton_train.py:386-481) plus the
+ * landmark dK/dV/d_logw atomics of _train_bwd_kernel (:302-333) and of
+ * _dsalt_bwd_kernel (dsalt_triton_bwd.py:121-162, 198-207): key-parallel,
+ * atomic-free, deterministic.                                               */
+DSALT_API int dsalt_attn_bwd_dkdv(const DsaltAttnParams* p, void* stream);
+/* Replaces the dQ / d_w̃ part of _train_bwd_kernel (dsalt_triton_train.py:
+ * 335-383) and the dQ of _dsalt_bwd_kernel; writes dq, dw_head and dw.      */
+DSALT_API int dsalt_attn_bwd_dq(const DsaltAttnParams* p, void* stream);
+
+/* ---- selection ------------------------------------------------------------
+ * Replaces the norm / z-standardisation / mix of hybrid_scores_per_head
+ * (dsalt/kernels/landmark_tokens_ker.py:19-61).  xwv is the caller's
+ * x @ W_V^T GEMM output [T, n_kv*dh] (any library GEMM).                    */
+typedef struct DsaltScoreParams {
+  const void* x;              /* [T, d_model] dtype */
+  const void* xwv;            /* [T, n_kv*dh] dtype */
+  const float* alpha;         /* [H] */
+  float* scores;              /* [T,H] fp32 */
+  float* z_x;                 /* [T] fp32 */
+  float* z_v;                 /* [T,H] fp32 */
+  float* stats;               /* scratch [2 + 2*n_kv] fp32 */
+  float* norms;               /* scratch [T*(1+n_kv)] fp32 */
+  int64_t T;
+  int32_t d_model, H, n_kv, dh;
+  int32_t dtype;
+} DsaltScoreParams;
+DSALT_API int dsalt_hybrid_scores(const DsaltScoreParams* p, void* stream);
+
+/* Replaces the exclusion + top-k of _compute_landmark_indices
+ * (dsalt/kernels/selectors.py:103-134): per (head, sequence) the k largest
+ * scores among tokens with seq_off >= w_sizes (own window), -1 when fewer are
+ * finite.  Ties go to the lower position.  idx is written sorted by
+ * descending score.                                                         */
+typedef struct DsaltTopkParams {
+  const float* scores;        /* [T,H] */
+  const float* w_sizes;       /* [T] (floored window, any float) */
+  const int32_t* cu_seqlens;  /* [S+1] */
+  int64_t* idx;               /* [H,S,k] */
+  int64_t T;
+  int32_t H, S, k;
+  int32_t max_len;            /* upper bound on sequence length (<= 1<<20) */
+} DsaltTopkParams;
+DSALT_API int dsalt_select_topk(const DsaltTopkParams* p, void* stream);
+
+/* Replaces DSALTAttention._window_continuous / _window_sizes
+ * (dsalt/modules/dsalt_attention.py:270-284): w̃ = n_min + σ(x·W + b)·(n_max −
+ * n_min), with torch's autocast rounding when dtype is bf16/f16 (logit,
+ * sigmoid, product and sum each rounded), plus w_disc = max(floor(w̃), 1).   */
+typedef struct DsaltWinGateParams {
+  const void* x;              /* [T, d_model] dtype */
+  const void* weight;         /* [d_model] dtype */
+  const void* bias;           /* [1] dtype */
+  void* w_cont;               /* [T] dtype */
+  float* w_f32;               /* [T] fp32 copy of w_cont, or NULL */
+  float* w_disc;              /* [T] fp32, or NULL */
+  float* logits;              /* [T] fp32 (pre-rounding), or NULL */
+  int64_t T;
+  int32_t d_model;
+  float n_min, n_max;
+  int32_t dtype;
+} DsaltWinGateParams;
+DSALT_API int dsalt_win_gate(const DsaltWinGateParams* p, void* stream);
+
+/* ---- introspection ------------------------------------------------------- */
+DSALT_API int dsalt_b200_abi_version(void);
+DSALT_API const char* dsalt_b200_status_string(int status);
+/* sizeof of the parameter structs, for bindings to check their mirrors:
+ * which = 0 schedule, 1 gather, 2 attn, 3 score, 4 topk, 5 win_gate        */
+DSALT_API int dsalt_b200_params_sizeof(int which);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* DSALT_B200_H */

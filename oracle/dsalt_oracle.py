@@ -224,10 +224,11 @@ def _sequence_bias(L, w_seq, pos_h, lw_h, tau_win, win_edge, semantics):
         band = (d >= 0) & (d <= w32)
         core = d <= (w32 - np.float32(win_edge))
         z = (w32.astype(np.float64) - d.astype(np.float64)) / tau_win
-        logedge = -np.log1p(np.exp(-z))
+        with np.errstate(over="ignore"):
+            logedge = -np.log1p(np.exp(-z))
+            sig = 1.0 / (1.0 + np.exp(-z))
         edge_b = np.where(core, 0.0, logedge)
         bias = np.where(band, edge_b, -np.inf)
-        sig = 1.0 / (1.0 + np.exp(-z))
         dbias_dw = np.where(band & ~core, (1.0 - sig) / tau_win, 0.0)
         win_lo = i.astype(np.float32) - np.asarray(w_seq, dtype=np.float32)   # float32, as the kernel
     else:

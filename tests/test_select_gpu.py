@@ -1,0 +1,121 @@
+"""GPU tests of the selection and gating kernels against reference goldens."""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+from conftest import load_golden
+from oracle import dsalt_oracle as O
+
+pytestmark = pytest.mark.gpu
+
+
+def _win_gate(x, weight, bias, n_min, n_max):
+    from dsalt.kernels import _ext
+    T, d = x.shape
+    w_cont = torch.empty(T, dtype=x.dtype, device=x.device)
+    w_f32 = torch.empty(T, dtype=torch.float32, device=x.device)
+    w_disc = torch.empty(T, dtype=torch.float32, device=x.device)
+    p = _ext.WinGateParams(x=_ext.ptr(x), weight=_ext.ptr(weight), bias=_ext.ptr(bias),
+                           w_cont=_ext.ptr(w_cont), w_f32=_ext.ptr(w_f32), w_disc=_ext.ptr(w_disc),
+                           logits=0, T=T, d_model=d, n_min=float(n_min), n_max=float(n_max),
+                           dtype=_ext.dtype_code(x.dtype))
+    _ext.call("dsalt_win_gate", p)
+    torch.cuda.synchronize()
+    return w_cont, w_f32, w_disc
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
+def test_win_gate_bit_exact_at_fixed_logits(dtype):
+    g = load_golden("window.pt")
+    logits = g["logits"]
+    T, d = logits.shape[0], 8
+    x = torch.zeros(T, d)
+    x[:, 0] = logits
+    weight = torch.zeros(d)
+    weight[0] = 1.0
+    dev = torch.device("cuda")
+    xd = x.to(dev, dtype).contiguous()
+    w_cont, w_f32, w_disc = _win_gate(xd, weight.to(dev, dtype), torch.zeros(1, device=dev, dtype=dtype),
+                                      int(g["n_min"]), int(g["n_max"]))
+    ref = g["w_bf16"] if dtype == torch.bfloat16 else g["w_fp32"]
+    got = w_cont.float().cpu()
+    if dtype == torch.bfloat16:
+        assert torch.equal(got, ref.float())
+    else:
+        ulp = (got - ref).abs() / torch.from_numpy(np.spacing(ref.numpy()))
+        assert ulp.max() <= 2
+    assert torch.equal(w_disc.cpu(), got.floor().clamp(min=1))
+
+
+@pytest.mark.parametrize("case", ["varlen", "uniform", "gqa"])
+def test_hybrid_scores_match_reference(golden_selectors, case):
+    from dsalt.kernels.landmark_tokens_ker import hybrid_scores_per_head
+    g = golden_selectors[case]
+    dev = torch.device("cuda")
+    H = g["alpha"].shape[0]
+    s, zx, zv = hybrid_scores_per_head(g["x"].to(dev), g["W_V"].to(dev), g["alpha"].to(dev), H, int(g["dh"]))
+    torch.testing.assert_close(s.cpu(), g["scores"], rtol=1e-5, atol=1e-5)
+    torch.testing.assert_close(zx.cpu(), g["z_x"], rtol=1e-5, atol=1e-5)
+    torch.testing.assert_close(zv.cpu(), g["z_v"], rtol=1e-5, atol=1e-5)
+
+
+def test_hybrid_scores_alpha_and_x_gradients():
+    """The analytic backward matches autograd through the reference formula."""
+    from dsalt.kernels.landmark_tokens_ker import hybrid_scores_per_head
+    torch.manual_seed(0)
+    dev = torch.device("cuda")
+    T, dm, H, n_kv, dh = 97, 32, 4, 2, 8
+    x = torch.randn(T, dm, device=dev, dtype=torch.float64).float().requires_grad_(True)
+    W = (torch.randn(n_kv * dh, dm, device=dev) * 0.3).requires_grad_(True)
+    a = torch.rand(H, device=dev).requires_grad_(True)
+    gs = torch.randn(T, H, device=dev)
+    s, _, _ = hybrid_scores_per_head(x, W, a, H, dh)
+    (s * gs).sum().backward()
+    x2 = x.detach().clone().requires_grad_(True)
+    W2 = W.detach().clone().requires_grad_(True)
+    a2 = a.detach().clone().requires_grad_(True)
+    xn = x2.norm(dim=-1)
+    zx = (xn - xn.mean()) / xn.std().clamp(min=1e-6)
+    xv = (x2 @ W2.T).view(T, n_kv, dh).norm(dim=-1)
+    zv = ((xv - xv.mean(0, keepdim=True)) / xv.std(0, keepdim=True).clamp(min=1e-6)).repeat_interleave(H // n_kv, 1)
+    s2 = a2 * zv + (1 - a2) * zx[:, None]
+    (s2 * gs).sum().backward()
+    torch.testing.assert_close(a.grad, a2.grad, rtol=1e-4, atol=1e-4)
+    torch.testing.assert_close(x.grad, x2.grad, rtol=1e-4, atol=1e-4)
+    torch.testing.assert_close(W.grad, W2.grad, rtol=1e-4, atol=1e-4)
+
+
+@pytest.mark.parametrize("case", ["varlen", "uniform", "gqa"])
+def test_landmark_sets_match_reference(golden_selectors, case):
+    from dsalt.kernels.selectors import _compute_landmark_indices
+    g = golden_selectors[case]
+    dev = torch.device("cuda")
+    H = g["alpha"].shape[0]
+    cu = g["cu"]
+    idx, _, _ = _compute_landmark_indices(g["x"].to(dev), g["W_V"].to(dev), g["alpha"].to(dev),
+                                          g["w_disc"].to(dev), cu.to(dev), int(g["k"]), 4,
+                                          int(cu[-1]), cu.tolist(), head_dim=int(g["dh"]))
+    idx = idx.cpu().numpy()
+    ref = g["idx"].numpy()
+    for h in range(ref.shape[0]):
+        for b in range(ref.shape[1]):
+            assert sorted(idx[h, b].tolist()) == sorted(ref[h, b].tolist()), (h, b)
+
+
+@pytest.mark.parametrize("L,k", [(4096, 64), (32768, 256), (37, 64), (5000, 1)])
+def test_topk_full_size_vs_oracle(L, k):
+    """Bit-exact index sets at the BASELINE sizes (scores given), ties to the lower position."""
+    from dsalt.kernels.selectors import select_topk
+    g = torch.Generator().manual_seed(L + k)
+    lens = [L, max(L // 3, 1)]
+    T, H = sum(lens), 2
+    scores = torch.randn(T, H, generator=g)
+    scores[5, 0] = scores[6, 0] = scores[7, 0] = 3.5   # ties
+    w = (32 + torch.rand(T, generator=g) * 480).floor()
+    cu = torch.tensor([0, lens[0], T], dtype=torch.int32)
+    idx = select_topk(scores.cuda(), w.cuda(), cu.cuda(), k, max(lens)).cpu().numpy()
+    ref = O.landmark_indices(scores.numpy(), w.numpy(), cu.numpy(), k)
+    assert np.array_equal(idx, ref)

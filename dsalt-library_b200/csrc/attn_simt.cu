@@ -290,6 +290,9 @@ static cudaError_t launch_simt(int stage, const DsaltAttnParams& p, cudaStream_t
       if (p.dw && p.dw_head)
         dw_reduce_kernel<T><<<(unsigned)((p.T + 255) / 256), 256, 0, st>>>(p.dw_head, reinterpret_cast<T*>(p.dw), p.T, p.H);
       break;
+    case 4:  // d_w̃ head reduction only (after the tensor-core dQ kernel)
+      dw_reduce_kernel<T><<<(unsigned)((p.T + 255) / 256), 256, 0, st>>>(p.dw_head, reinterpret_cast<T*>(p.dw), p.T, p.H);
+      break;
   }
   return cudaGetLastError();
 }

@@ -168,8 +168,10 @@ def backward(do_c, q_c, k_c, v_c, o, lse, prep: Prepared, tau_win: float, win_ed
     d_lw = torch.zeros(H, prep.S, prep.k_lmk, dtype=torch.float32, device=dev)
     dw_head = torch.empty(T, H, dtype=torch.float32, device=dev) if want_dw else None
     dw = torch.empty(T, dtype=q_c.dtype, device=dev) if want_dw else None
+    lmk_grad = torch.empty(2, H, prep.S, prep.kp, prep.D, dtype=torch.float32, device=dev) \
+        if prep.kp > 0 else None
     p = _params(prep, q_c, k_c, v_c, tau_win, win_edge, impl, o=o, lse=lse, dout=do_c,
-                delta=delta, dq=dq, dk=dk, dv=dv, dw_head=dw_head, dw=dw, d_lw=d_lw)
+                delta=delta, dq=dq, dk=dk, dv=dv, dw_head=dw_head, dw=dw, d_lw=d_lw, lmk_grad=lmk_grad)
     _ext.call("dsalt_attn_bwd_preprocess", p)
     _ext.call("dsalt_attn_bwd_dkdv", p)
     _ext.call("dsalt_attn_bwd_dq", p)

@@ -144,6 +144,8 @@ typedef struct DsaltAttnParams {
   float* dw_head;             /* [T,H] scratch (train) */
   void* dw;                   /* [T] dtype: Σ_h ∂loss/∂w̃ (train) or NULL */
   float* d_lw;                /* [H,S,k_lmk] fp32, caller slot order: ∂loss/∂lmk_w */
+  float* lmk_grad;            /* [2,H,S,kp,D] fp32 scratch of the tensor-core dK/dV
+                                 stage (landmark-slot dK, dV); unused by the SIMT family */
   int32_t* status;            /* device status word or NULL */
   /* sizes */
   int64_t T;

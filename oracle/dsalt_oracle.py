@@ -201,23 +201,19 @@ def landmark_logw_grad_alpha(d_logw, scores, z_x, z_v, lmk_pos, cu, tau_lmk: flo
 # --------------------------------------------------------------------------- #
 #  attention: attended set and log-bias
 # --------------------------------------------------------------------------- #
-def _sequence_bias(L, w_seq, pos_h, lw_h, tau_win, win_edge, semantics):
-    """Dense ``[L, L]`` log-bias of one (sequence, head) plus d(bias)/d(w̃).
+def _band_bias(L, w_seq, tau_win, win_edge, semantics):
+    """Dense ``[L, L]`` band log-bias of one sequence, d(bias)/d(w̃) and the landmark threshold.
 
-    Training semantics (dsalt/kernels/dsalt_triton_train.py:145-156, 182-198;
-    dense twin dsalt/modules/dsalt_attention.py:520-563):
-      band ``0 ≤ d ≤ w̃`` with ``d = i − j``; bias 0 in the core ``d ≤ w̃ − win_edge``,
-      ``log σ((w̃ − d)/τ_win)`` on the edge; landmark ``p`` valid iff
-      ``p ≤ i`` and ``float32(p) < float32(i) − w̃`` with bias ``lmk_logw``.
-    Inference semantics (dsalt/kernels/dsalt_triton_attn.py:102-105, 132-141):
-      band ``i − w + 1 ≤ j ≤ i`` with integer ``w = max(int(w), 1)``, no edge bias;
-      landmark valid iff ``p ≤ i`` and ``p < i − w + 1``, additive ``lmk_bias``.
-    Band and landmark sets are disjoint, so the union is a plain overwrite
-    (the dense twin's elementwise max).
+    Training semantics (dsalt/kernels/dsalt_triton_train.py:145-156; dense twin
+    dsalt/modules/dsalt_attention.py:534-541): band ``0 ≤ d ≤ w̃`` with ``d = i − j``,
+    bias 0 in the core ``d ≤ w̃ − win_edge`` and ``log σ((w̃ − d)/τ_win)`` on the edge.
+    Inference semantics (dsalt/kernels/dsalt_triton_attn.py:102-105): band
+    ``i − w + 1 ≤ j ≤ i`` with ``w = max(int(w), 1)`` and no bias.
+    Also returns, per query, the bound ``win_lo`` of the landmark rule
+    (train: ``float32(i) − w̃``, :183; infer: ``i − w + 1``, dsalt_triton_attn.py:133).
     """
     i = np.arange(L)
     d = (i[:, None] - i[None, :]).astype(np.float32)
-    bias = np.full((L, L), -np.inf)
     dbias_dw = np.zeros((L, L))
     if semantics == "train":
         w32 = np.asarray(w_seq, dtype=np.float32)[:, None]
@@ -227,8 +223,7 @@ def _sequence_bias(L, w_seq, pos_h, lw_h, tau_win, win_edge, semantics):
         with np.errstate(over="ignore"):
             logedge = -np.log1p(np.exp(-z))
             sig = 1.0 / (1.0 + np.exp(-z))
-        edge_b = np.where(core, 0.0, logedge)
-        bias = np.where(band, edge_b, -np.inf)
+        bias = np.where(band, np.where(core, 0.0, logedge), -np.inf)
         dbias_dw = np.where(band & ~core, (1.0 - sig) / tau_win, 0.0)
         win_lo = i.astype(np.float32) - np.asarray(w_seq, dtype=np.float32)   # float32, as the kernel
     else:
@@ -237,7 +232,22 @@ def _sequence_bias(L, w_seq, pos_h, lw_h, tau_win, win_edge, semantics):
         band = (jj >= i[:, None] - w_int + 1) & (jj <= i[:, None])
         bias = np.where(band, 0.0, -np.inf)
         win_lo = (i - w_int[:, 0] + 1)
-    for p, lw in zip(pos_h, lw_h):
+    return bias, dbias_dw, win_lo
+
+
+def _landmark_bias(L, pos_h, lw_h, win_lo, semantics):
+    """``[L, k]`` log-bias of the landmark slots of one (sequence, head).
+
+    Slot ``c`` at position ``p`` is a separate key column (as in the reference
+    kernels, dsalt_triton_train.py:168-198, where each landmark slot is a column
+    of the landmark tile), valid for query ``i`` iff ``0 ≤ p < len``, ``p ≤ i`` and
+    ``p < win_lo(i)`` (train: compared in float32), with bias ``lmk_logw[c]``.
+    Band and landmark keys are disjoint for every query.
+    """
+    i = np.arange(L)
+    k = len(pos_h)
+    bias = np.full((L, k), -np.inf)
+    for c, (p, lw) in enumerate(zip(pos_h, lw_h)):
         p = int(p)
         if p < 0 or p >= L:
             continue
@@ -245,8 +255,8 @@ def _sequence_bias(L, w_seq, pos_h, lw_h, tau_win, win_edge, semantics):
             ok = (p <= i) & (np.float32(p) < win_lo)
         else:
             ok = (p <= i) & (p < win_lo)
-        bias[ok, p] = float(lw)
-    return bias, dbias_dw
+        bias[ok, c] = float(lw)
+    return bias
 
 
 def _rows_softmax(logits):
@@ -312,45 +322,39 @@ def _attention(q, k, v, do, lmk_pos, lmk_logw, w, cu, tau_win, win_edge, semanti
         if L == 0:
             continue
         w_seq = np.asarray(w)[s0:s1]
+        band_bias, dbias_dw, win_lo = _band_bias(L, w_seq, tau_win, win_edge, semantics)
         for h in range(H):
-            bias, dbias_dw = _sequence_bias(L, w_seq, lmk_pos[h, b], lmk_logw[h, b],
-                                            tau_win, win_edge, semantics)
+            pos = lmk_pos[h, b]
+            lmk_bias = _landmark_bias(L, pos, lmk_logw[h, b], win_lo, semantics)
+            pc = np.clip(pos, 0, L - 1)
             qs, ks, vs = q[s0:s1, h], k[s0:s1, h], v[s0:s1, h]
-            logits = (qs @ ks.T) * scale + bias
+            kl, vl = ks[pc], vs[pc]                       # landmark slot keys / values [k, D]
+            logits = np.concatenate([(qs @ ks.T) * scale + band_bias,
+                                     (qs @ kl.T) * scale + lmk_bias], axis=1)
             P, lse_h = _rows_softmax(logits)
-            oh = P @ vs
+            Pb, Pl = P[:, :L], P[:, L:]
+            oh = Pb @ vs + Pl @ vl
             o[s0:s1, h] = oh
             lse[s0:s1, h] = lse_h
             if not want_bwd:
                 continue
             dos = do[s0:s1, h]
-            dv[s0:s1, h] += P.T @ dos
-            dP = dos @ vs.T
             delta = (dos * oh).sum(axis=1, keepdims=True)
-            dS = P * (dP - delta)
-            dq[s0:s1, h] += (dS @ ks) * scale
-            dk[s0:s1, h] += (dS.T @ qs) * scale
-            d_w[s0:s1, h] = (dS * dbias_dw).sum(axis=1)
-            for kk, p in enumerate(lmk_pos[h, b]):
-                p = int(p)
-                if 0 <= p < L:
-                    col_is_lmk = np.isfinite(bias[:, p]) & ~(
-                        _band_member(L, w_seq, p, semantics))
-                    d_logw[h, b, kk] = dS[col_is_lmk, p].sum()
+            dSb = Pb * (dos @ vs.T - delta)
+            dSl = Pl * (dos @ vl.T - delta)
+            dq[s0:s1, h] += (dSb @ ks + dSl @ kl) * scale
+            dkh = (dSb.T @ qs) * scale
+            dvh = Pb.T @ dos
+            np.add.at(dkh, pc, (dSl.T @ qs) * scale)
+            np.add.at(dvh, pc, Pl.T @ dos)
+            dk[s0:s1, h] += dkh
+            dv[s0:s1, h] += dvh
+            d_w[s0:s1, h] = (dSb * dbias_dw).sum(axis=1)
+            d_logw[h, b] = dSl.sum(axis=0)
     res = {"o": o, "lse": lse}
     if want_bwd:
         res.update(dq=dq, dk=dk, dv=dv, d_logw=d_logw, d_w=d_w.sum(axis=1), d_w_head=d_w)
     return res
-
-
-def _band_member(L, w_seq, p, semantics):
-    """Rows ``i`` whose band contains key ``p`` (used to separate band and landmark columns)."""
-    i = np.arange(L)
-    d = (i - p).astype(np.float32)
-    if semantics == "train":
-        return (d >= 0) & (d <= np.asarray(w_seq, dtype=np.float32))
-    w_int = np.maximum(np.asarray(w_seq).astype(np.int64), 1)
-    return (p >= i - w_int + 1) & (p <= i)
 
 
 # --------------------------------------------------------------------------- #

@@ -1,0 +1,136 @@
+"""DSALT causal language model (reference ``dsalt/model/dsalt_lm.py``).
+
+Same constructor, module tree, parameter names and initialisation order as the
+reference, so a seeded construction and reference checkpoints give identical
+weights.  The attention layers run the B200 CUDA ops.  ``loss_fn="liger"``
+(a Triton fused-CE kernel outside the attention path) is not provided;
+``"auto"`` resolves to ``"chunked"``.
+"""
+
+from __future__ import annotations
+
+import math
+
+import torch
+import torch.nn as nn
+import torch.nn.functional as F
+
+from ..kernels.RMSENorm import RMSENorm
+from ..modules.dsalt_transformer import DSALTTransformerBlock
+from .config import DSALTConfig
+
+
+def _chunked_cross_entropy(x: torch.Tensor, weight: torch.Tensor, labels: torch.Tensor,
+                           chunk_size: int = 512) -> torch.Tensor:
+    """Mean CE over non-ignored labels, the LM head applied chunk by chunk (reference :19-39)."""
+    total = x.shape[0]
+    loss_acc = torch.zeros((), device=x.device, dtype=torch.float32)
+    valid_acc = torch.zeros((), device=x.device, dtype=torch.float32)
+    for start in range(0, total, chunk_size):
+        end = min(start + chunk_size, total)
+        y = labels[start:end]
+        logits = F.linear(x[start:end], weight)
+        loss_acc = loss_acc + F.cross_entropy(logits, y, ignore_index=-100, reduction="sum")
+        valid_acc = valid_acc + (y != -100).sum()
+    return loss_acc / valid_acc.clamp(min=1.0)
+
+
+_LOSS_FN = {"auto": None, "liger": None, "chunked": _chunked_cross_entropy}
+
+
+class DSALTLMHeadModel(nn.Module):
+    """Causal LM: embedding → DSALT blocks → RMSNorm → (tied) LM head (reference :64-285)."""
+
+    def __init__(self, vocab_size, d_model, n_layers, n_heads, n_min, n_max, k_lmk, max_seq_len, d_ff=None,
+                 dropout=0.0, yarn_scale=1.0, tie_weights=True, padding_idx=None, lm_head_chunk_size=2048,
+                 loss_fn="chunked", aux_loss_weight=0.0, n_kv_heads=None, qkv_bias=False, rope_base=10000.0):
+        super().__init__()
+        assert loss_fn in _LOSS_FN, f"loss_fn must be one of {list(_LOSS_FN)}"
+        if loss_fn == "liger":
+            raise RuntimeError("loss_fn='liger' needs the Triton fused cross-entropy, which this B200 build "
+                               "does not provide; use loss_fn='chunked'")
+        self.d_model = d_model
+        self.n_layers = n_layers
+        self.vocab_size = vocab_size
+        self.lm_head_chunk_size = lm_head_chunk_size
+        self.loss_fn = loss_fn
+        self.aux_loss_weight = aux_loss_weight
+        if d_ff is None:
+            hidden = int(8 / 3 * d_model)
+            d_ff = ((hidden + 127) // 128) * 128
+        self.embed_tokens = nn.Embedding(vocab_size, d_model, padding_idx=padding_idx)
+        self.embed_dropout = nn.Dropout(dropout)
+        self.layers = nn.ModuleList([
+            DSALTTransformerBlock(d_model=d_model, n_heads=n_heads, n_min=n_min, n_max=n_max, k_lmk=k_lmk,
+                                  max_seq_len=max_seq_len, d_ff=d_ff, dropout=dropout, yarn_scale=yarn_scale,
+                                  layer_idx=i, n_kv_heads=n_kv_heads, qkv_bias=qkv_bias, rope_base=rope_base)
+            for i in range(n_layers)
+        ])
+        self.final_norm = RMSENorm(d_model)
+        self.lm_head = nn.Linear(d_model, vocab_size, bias=False)
+        if tie_weights:
+            self.lm_head.weight = self.embed_tokens.weight
+        self._init_weights()
+
+    @classmethod
+    def from_config(cls, config: DSALTConfig) -> "DSALTLMHeadModel":
+        return cls(**config.to_dict())
+
+    def _init_weights(self):
+        nn.init.normal_(self.embed_tokens.weight, std=0.02)
+        residual_std = 0.02 / math.sqrt(2 * self.n_layers)
+        for name, module in self.named_modules():
+            if isinstance(module, nn.Linear):
+                std = residual_std if any(k in name for k in ("out_proj", "down_proj")) else 0.02
+                nn.init.normal_(module.weight, std=std)
+                if module.bias is not None:
+                    nn.init.zeros_(module.bias)
+
+    def _compute_loss(self, x: torch.Tensor, labels: torch.Tensor) -> torch.Tensor:
+        flat_x = x.reshape(-1, self.d_model)
+        flat_labels = labels.reshape(-1).long()
+        return _chunked_cross_entropy(flat_x, self.lm_head.weight, flat_labels, self.lm_head_chunk_size)
+
+    @staticmethod
+    def _to_autocast_dtype(x: torch.Tensor) -> torch.Tensor:
+        dev = x.device.type
+        if torch.is_autocast_enabled(dev):
+            dt = torch.get_autocast_dtype(dev)
+            return x.to(dt) if x.dtype != dt else x
+        return x
+
+    @staticmethod
+    def _packed_rope_meta(cu_seqlens: torch.Tensor, total_len: int, attn0):
+        """RoPE cos/sin gathered per packed position and a host copy of cu_seqlens (reference :218-235)."""
+        device = cu_seqlens.device
+        cu = cu_seqlens.long()
+        lens = cu[1:] - cu[:-1]
+        seq_ids = torch.repeat_interleave(torch.arange(cu.shape[0] - 1, device=device), lens)
+        pos_ids = torch.arange(total_len, device=device) - cu[:-1][seq_ids]
+        rope_cs = (attn0.rope_cos.to(device)[pos_ids], attn0.rope_sin.to(device)[pos_ids])
+        return rope_cs, cu_seqlens.detach().to("cpu").tolist()
+
+    def forward(self, input_ids, cu_seqlens=None, max_seqlen=None, labels=None, gradient_checkpointing=False,
+                padding_mask=None) -> dict:
+        if max_seqlen is None:
+            max_seqlen = input_ids.shape[-1]
+        x = self.embed_dropout(self.embed_tokens(input_ids))
+        x = self._to_autocast_dtype(x)
+        aux_loss = torch.zeros((), device=input_ids.device, dtype=x.dtype)
+        rope_cs = cu_list = None
+        if cu_seqlens is not None:
+            rope_cs, cu_list = self._packed_rope_meta(cu_seqlens, input_ids.shape[0], self.layers[0].attn)
+        for layer in self.layers:
+            x, layer_aux = layer(x, cu_seqlens=cu_seqlens, max_seqlen=max_seqlen,
+                                 gradient_checkpointing=gradient_checkpointing, rope_cs=rope_cs, cu_list=cu_list)
+            aux_loss = aux_loss + layer_aux
+        x = self.final_norm(x)
+        if labels is not None:
+            loss = self._compute_loss(x, labels) + self.aux_loss_weight * aux_loss
+            return {"loss": loss, "logits": None, "aux_loss": aux_loss.detach()}
+        return {"loss": None, "logits": self.lm_head(x), "aux_loss": None}
+
+    def num_parameters(self, trainable_only: bool = True) -> int:
+        if trainable_only:
+            return sum(p.numel() for p in self.parameters() if p.requires_grad)
+        return sum(p.numel() for p in self.parameters())

@@ -9,6 +9,7 @@ cudaError_t simt_attention_stage(int stage, const DsaltAttnParams& p, cudaStream
 cudaError_t launch_win_gate(const DsaltWinGateParams& p, cudaStream_t st);
 cudaError_t launch_hybrid_scores(const DsaltScoreParams& p, cudaStream_t st);
 cudaError_t launch_topk(const DsaltTopkParams& p, cudaStream_t st);
+cudaError_t noalloc_score_scratch(float** out);
 // tcgen05 path (attn_tc.cu); returns cudaErrorNotSupported when the shape is
 // outside what the tensor-core kernels cover, so the caller can report it.
 cudaError_t tc_attention_stage(int stage, const DsaltAttnParams& p, cudaStream_t st);
@@ -130,6 +131,25 @@ int dsalt_hybrid_scores(const DsaltScoreParams* p, void* stream) {
   if (p->T == 0) return DSALT_OK;
   if (!p->x || !p->xwv || !p->alpha || !p->scores || !p->stats || !p->norms) return DSALT_ERR_ARG;
   return status_of(launch_hybrid_scores(*p, (cudaStream_t)stream));
+}
+
+// See dsalt_b200.h: the same pipeline as dsalt_hybrid_scores with its scratch in
+// the library's fixed device array (select.cu); nothing is allocated here.
+int dsalt_hybrid_scores_noalloc(const DsaltScoreParams* p, void* stream) {
+  if (!p || p->T < 0 || p->H <= 0 || p->n_kv <= 0 || p->H % p->n_kv != 0 || p->dh <= 0 || p->d_model <= 0)
+    return DSALT_ERR_ARG;
+  if (p->dtype != DSALT_F16 && p->dtype != DSALT_BF16 && p->dtype != DSALT_F32) return DSALT_ERR_DTYPE;
+  const int64_t need = p->T * (int64_t)(1 + p->n_kv) + 2 + 2 * (int64_t)p->n_kv;
+  if (need > (int64_t)DSALT_NOALLOC_SCORE_MAX_FLOATS) return DSALT_ERR_TOO_LARGE;
+  if (p->T == 0) return DSALT_OK;
+  if (!p->x || !p->xwv || !p->alpha || !p->scores) return DSALT_ERR_ARG;
+  float* scratch = nullptr;
+  cudaError_t e = noalloc_score_scratch(&scratch);
+  if (e != cudaSuccess) return status_of(e);
+  DsaltScoreParams q = *p;
+  q.stats = scratch;                      // [2 + 2*n_kv]
+  q.norms = scratch + 2 + 2 * p->n_kv;    // [T * (1 + n_kv)]
+  return status_of(launch_hybrid_scores(q, (cudaStream_t)stream));
 }
 
 int dsalt_select_topk(const DsaltTopkParams* p, void* stream) {

@@ -6,6 +6,8 @@
 //   top-k           _compute_landmark_indices           (dsalt/kernels/selectors.py:75-134)
 // All three are HBM/latency-bound byte work: coalesced 16-byte loads, one warp
 // per token for the row reductions, shared-memory radix select for top-k.
+#include <mutex>
+
 #include "common.cuh"
 
 namespace dsalt {
@@ -263,6 +265,45 @@ cudaError_t launch_topk(const DsaltTopkParams& p, cudaStream_t st) {
   if (e != cudaSuccess) return e;
   topk_kernel<<<p.H * p.S, kTopkThreads, smem, st>>>(p);
   return cudaGetLastError();
+}
+
+// ------------------------------------------------ no-allocation score variant
+// dsalt_hybrid_scores_noalloc runs the same three kernels as
+// dsalt_hybrid_scores, but keeps their scratch (the per-token norms and the
+// mean/std statistics) in the fixed array below instead of in buffers the
+// caller allocates.  It is meant for callers that are not allowed to allocate
+// device memory themselves: for example a host application that plans and
+// owns every device buffer and gives plugins only their inputs and outputs.
+//
+// The array is a file-scope __device__ variable: every GPU that loads this
+// library holds DSALT_NOALLOC_SCORE_MAX_FLOATS floats (8 MiB) of it until the
+// process exits.  All calls on a device share it and it keeps the previous
+// call's contents; the kernels overwrite every element they read, so nothing
+// has to be cleared between calls.  Two calls that overlap on the GPU (on
+// different streams, or from different host threads) race on the array.
+static __device__ __align__(256) float g_score_scratch[DSALT_NOALLOC_SCORE_MAX_FLOATS];
+
+// Device address of g_score_scratch on the current device.  In host code the
+// symbol names a host-side stand-in, never the device array, so the address is
+// fetched with cudaGetSymbolAddress once per device (with that device
+// current) and cached.
+cudaError_t noalloc_score_scratch(float** out) {
+  constexpr int kMaxDevices = 64;
+  static float* cache[kMaxDevices] = {};
+  static std::mutex mu;
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  if (dev < 0 || dev >= kMaxDevices) return cudaErrorInvalidDevice;
+  std::lock_guard<std::mutex> lock(mu);
+  if (!cache[dev]) {
+    void* ptr = nullptr;
+    e = cudaGetSymbolAddress(&ptr, g_score_scratch);
+    if (e != cudaSuccess) return e;
+    cache[dev] = static_cast<float*>(ptr);
+  }
+  *out = cache[dev];
+  return cudaSuccess;
 }
 
 }  // namespace dsalt

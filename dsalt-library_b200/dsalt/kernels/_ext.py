@@ -87,6 +87,7 @@ _ENTRY = {
     "dsalt_attn_bwd_dkdv": AttnParams,
     "dsalt_attn_bwd_dq": AttnParams,
     "dsalt_hybrid_scores": ScoreParams,
+    "dsalt_hybrid_scores_noalloc": ScoreParams,
     "dsalt_select_topk": TopkParams,
     "dsalt_win_gate": WinGateParams,
 }

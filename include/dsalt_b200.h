@@ -192,6 +192,20 @@ typedef struct DsaltScoreParams {
 } DsaltScoreParams;
 DSALT_API int dsalt_hybrid_scores(const DsaltScoreParams* p, void* stream);
 
+/* No counterpart in the reference.  Same result as dsalt_hybrid_scores for
+ * callers that may not allocate device memory (for example a host runtime that
+ * owns and plans every device buffer and hands a plugin only its inputs and
+ * outputs): p->stats and p->norms are ignored, and the scratch lives in a
+ * fixed array inside the library, DSALT_NOALLOC_SCORE_MAX_FLOATS floats (8 MiB)
+ * held on every GPU that loads the library until the process exits.  Sizes
+ * with T*(1+n_kv) + 2 + 2*n_kv > DSALT_NOALLOC_SCORE_MAX_FLOATS return
+ * DSALT_ERR_TOO_LARGE.  The first call on a device looks up the array's device
+ * address (cudaGetSymbolAddress, with that device current) and caches it;
+ * make that first call before any stream capture.  All calls on a device share
+ * the array, so calls that overlap on the GPU race.  Nothing is allocated.   */
+#define DSALT_NOALLOC_SCORE_MAX_FLOATS (1 << 21)
+DSALT_API int dsalt_hybrid_scores_noalloc(const DsaltScoreParams* p, void* stream);
+
 /* Replaces the exclusion + top-k of _compute_landmark_indices
  * (dsalt/kernels/selectors.py:103-134): per (head, sequence) the k largest
  * scores among tokens with seq_off >= w_sizes (own window), -1 when fewer are

@@ -62,7 +62,7 @@ def build(jobs: int | None = None, verbose: bool = False, extra: list[str] | Non
     if LIB.exists() and all(LIB.stat().st_mtime >= o.stat().st_mtime for o in objs):
         return LIB
     tmp = LIB.with_suffix(".so.tmp")
-    cmd = [nvcc(), *ARCH, "-shared", "-o", str(tmp), *map(str, objs), "-lcuda"]
+    cmd = [nvcc(), *ARCH, "-shared", "-o", str(tmp), *map(str, objs)]
     res = subprocess.run(cmd, capture_output=True, text=True)
     if res.returncode != 0:
         raise RuntimeError(f"link failed:\n{res.stdout}\n{res.stderr}")

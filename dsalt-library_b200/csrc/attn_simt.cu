@@ -16,24 +16,26 @@ namespace dsalt {
 
 constexpr int kSimtWarps = 8;  // warps per CTA
 
-template <typename T, int D>
+// Lane `lane` holds elements lane + 32 r (r < R = ceil(D/32)) of a head row;
+// elements past the runtime head dim D read as zero.
+template <typename T, int R>
 struct RowVec {
-  static constexpr int R = D / 32;
   float x[R];
-  __device__ __forceinline__ void load(const T* __restrict__ p, int lane) {
+  __device__ __forceinline__ void load(const T* __restrict__ p, int lane, int D) {
 #pragma unroll
-    for (int r = 0; r < R; ++r) x[r] = to_f32<T>(p[lane + 32 * r]);
+    for (int r = 0; r < R; ++r) x[r] = (lane + 32 * r < D) ? to_f32<T>(p[lane + 32 * r]) : 0.f;
   }
-  __device__ __forceinline__ float dot(const T* __restrict__ p, int lane) const {
+  __device__ __forceinline__ float dot(const T* __restrict__ p, int lane, int D) const {
     float s = 0.f;
 #pragma unroll
-    for (int r = 0; r < R; ++r) s = fmaf(x[r], to_f32<T>(p[lane + 32 * r]), s);
+    for (int r = 0; r < R; ++r)
+      if (lane + 32 * r < D) s = fmaf(x[r], to_f32<T>(p[lane + 32 * r]), s);
     return warp_sum(s);
   }
 };
 
 // ------------------------------------------------------------------ forward
-template <typename T, int D>
+template <typename T, int R>
 __global__ void __launch_bounds__(kSimtWarps * 32)
 simt_fwd_kernel(const DsaltAttnParams p) {
   const int lane = threadIdx.x & 31;
@@ -46,22 +48,22 @@ simt_fwd_kernel(const DsaltAttnParams p) {
   const int i = (int)(t - s0);
   const RowWindow rw = row_window(p.w[t], i, p.semantics, p.win_edge);
   const float inv_tau = 1.0f / p.tau_win;
+  const int D = p.D;
   const int64_t HD = (int64_t)p.H * D;
 
   const T* q = reinterpret_cast<const T*>(p.q) + t * HD + (int64_t)h * D;
   const T* kb = reinterpret_cast<const T*>(p.k) + (int64_t)h * D;
   const T* vb = reinterpret_cast<const T*>(p.v) + (int64_t)h * D;
-  RowVec<T, D> qv;
-  qv.load(q, lane);
+  RowVec<T, R> qv;
+  qv.load(q, lane, D);
 
-  constexpr int R = D / 32;
   float acc[R];
 #pragma unroll
   for (int r = 0; r < R; ++r) acc[r] = 0.f;
   float m = -INFINITY, l = 0.f;
 
   auto visit = [&](const T* kp, const T* vp, float bias) {
-    const float sc = fmaf(qv.dot(kp, lane), p.scale, bias);
+    const float sc = fmaf(qv.dot(kp, lane, D), p.scale, bias);
     if (sc > m) {
       const float corr = (m == -INFINITY) ? 0.f : expf(m - sc);
       l *= corr;
@@ -72,7 +74,8 @@ simt_fwd_kernel(const DsaltAttnParams p) {
     const float pr = expf(sc - m);
     l += pr;
 #pragma unroll
-    for (int r = 0; r < R; ++r) acc[r] = fmaf(pr, to_f32<T>(vp[lane + 32 * r]), acc[r]);
+    for (int r = 0; r < R; ++r)
+      if (lane + 32 * r < D) acc[r] = fmaf(pr, to_f32<T>(vp[lane + 32 * r]), acc[r]);
   };
 
   if (rw.W >= 0) {
@@ -98,6 +101,7 @@ simt_fwd_kernel(const DsaltAttnParams p) {
   float* of = p.o_f32 ? p.o_f32 + t * HD + (int64_t)h * D : nullptr;
 #pragma unroll
   for (int r = 0; r < R; ++r) {
+    if (lane + 32 * r >= D) continue;
     const T ov = from_f32<T>(acc[r] * inv_l);
     o[lane + 32 * r] = ov;
     if (of) of[lane + 32 * r] = to_f32<T>(ov);
@@ -106,25 +110,42 @@ simt_fwd_kernel(const DsaltAttnParams p) {
 }
 
 // ------------------------------------------------------------- preprocess
-// Delta[t,h] = Σ_d O·dO with O the stored (input-dtype) output
-// (dsalt_triton_train.py:220-237, 674).
-template <typename T, int D>
+// Delta[t,h] = Σ_d O·dO with O the stored (input-dtype) output and dO rounded to
+// the input dtype (dsalt_triton_train.py:220-237, 673-674).  When the caller
+// passes the fp32 upstream gradient (dout_f32), this kernel also writes its
+// input-dtype copy to dout for the tensor-core stages.
+template <typename T, int R>
 __global__ void __launch_bounds__(kSimtWarps * 32)
 bwd_preprocess_kernel(const DsaltAttnParams p) {
   const int lane = threadIdx.x & 31;
   const int64_t row = (int64_t)blockIdx.x * kSimtWarps + (threadIdx.x >> 5);
   if (row >= p.T * p.H) return;
+  const int D = p.D;
   const T* o = reinterpret_cast<const T*>(p.o) + row * D;
   const T* g = reinterpret_cast<const T*>(p.dout) + row * D;
+  const float* gf = p.dout_f32 ? p.dout_f32 + row * D : nullptr;
+  T* gw = const_cast<T*>(g);
   float s = 0.f;
 #pragma unroll
-  for (int r = 0; r < D / 32; ++r) s = fmaf(to_f32<T>(o[lane + 32 * r]), to_f32<T>(g[lane + 32 * r]), s);
+  for (int r = 0; r < R; ++r) {
+    const int e = lane + 32 * r;
+    if (e >= D) continue;
+    float gv;
+    if (gf) {
+      const T gt = from_f32<T>(gf[e]);
+      gw[e] = gt;
+      gv = to_f32<T>(gt);
+    } else {
+      gv = to_f32<T>(g[e]);
+    }
+    s = fmaf(to_f32<T>(o[e]), gv, s);
+  }
   s = warp_sum(s);
   if (lane == 0) p.delta[row] = s;
 }
 
 // ---------------------------------------------------------------- dQ, d_w̃
-template <typename T, int D>
+template <typename T, int R>
 __global__ void __launch_bounds__(kSimtWarps * 32)
 simt_bwd_dq_kernel(const DsaltAttnParams p) {
   const int lane = threadIdx.x & 31;
@@ -137,8 +158,8 @@ simt_bwd_dq_kernel(const DsaltAttnParams p) {
   const int i = (int)(t - s0);
   const RowWindow rw = row_window(p.w[t], i, p.semantics, p.win_edge);
   const float inv_tau = 1.0f / p.tau_win;
+  const int D = p.D;
   const int64_t HD = (int64_t)p.H * D;
-  constexpr int R = D / 32;
 
   const float lse = p.lse[row];
   const float delta = p.delta[row];
@@ -148,20 +169,21 @@ simt_bwd_dq_kernel(const DsaltAttnParams p) {
   float dw = 0.f;
 
   if (lse != -INFINITY) {
-    RowVec<T, D> qv, gv;
-    qv.load(reinterpret_cast<const T*>(p.q) + t * HD + (int64_t)h * D, lane);
-    gv.load(reinterpret_cast<const T*>(p.dout) + t * HD + (int64_t)h * D, lane);
+    RowVec<T, R> qv, gv;
+    qv.load(reinterpret_cast<const T*>(p.q) + t * HD + (int64_t)h * D, lane, D);
+    gv.load(reinterpret_cast<const T*>(p.dout) + t * HD + (int64_t)h * D, lane, D);
     const T* kb = reinterpret_cast<const T*>(p.k) + (int64_t)h * D;
     const T* vb = reinterpret_cast<const T*>(p.v) + (int64_t)h * D;
     auto visit = [&](const T* kp, const T* vp, float bias, float dbias) {
-      const float sc = fmaf(qv.dot(kp, lane), p.scale, bias);
+      const float sc = fmaf(qv.dot(kp, lane, D), p.scale, bias);
       const float pr = expf(sc - lse);
-      const float dp = gv.dot(vp, lane);
+      const float dp = gv.dot(vp, lane, D);
       const float ds = pr * (dp - delta);
       dw = fmaf(ds, dbias, dw);
       const float dss = ds * p.scale;
 #pragma unroll
-      for (int r = 0; r < R; ++r) dq[r] = fmaf(dss, to_f32<T>(kp[lane + 32 * r]), dq[r]);
+      for (int r = 0; r < R; ++r)
+        if (lane + 32 * r < D) dq[r] = fmaf(dss, to_f32<T>(kp[lane + 32 * r]), dq[r]);
     };
     if (rw.W >= 0) {
       const int jlo = i - min(rw.W, i);
@@ -181,7 +203,8 @@ simt_bwd_dq_kernel(const DsaltAttnParams p) {
   }
   T* out = reinterpret_cast<T*>(p.dq) + t * HD + (int64_t)h * D;
 #pragma unroll
-  for (int r = 0; r < R; ++r) out[lane + 32 * r] = from_f32<T>(dq[r]);
+  for (int r = 0; r < R; ++r)
+    if (lane + 32 * r < D) out[lane + 32 * r] = from_f32<T>(dq[r]);
   if (lane == 0 && p.dw_head) p.dw_head[row] = dw;
 }
 
@@ -190,7 +213,7 @@ simt_bwd_dq_kernel(const DsaltAttnParams p) {
 // query that attends it, through the band (i in [j, j + wmax]) and, when j is
 // a landmark of (h, seq), through the landmark rule (all later queries whose
 // window no longer covers j).  d_lw of that landmark is a plain warp sum.
-template <typename T, int D>
+template <typename T, int R>
 __global__ void __launch_bounds__(kSimtWarps * 32)
 simt_bwd_dkdv_kernel(const DsaltAttnParams p) {
   const int lane = threadIdx.x & 31;
@@ -203,12 +226,12 @@ simt_bwd_dkdv_kernel(const DsaltAttnParams p) {
   const int L = (int)(p.cu_seqlens[s + 1] - s0);
   const int j = (int)(t - s0);
   const float inv_tau = 1.0f / p.tau_win;
+  const int D = p.D;
   const int64_t HD = (int64_t)p.H * D;
-  constexpr int R = D / 32;
 
-  RowVec<T, D> kv, vv;
-  kv.load(reinterpret_cast<const T*>(p.k) + t * HD + (int64_t)h * D, lane);
-  vv.load(reinterpret_cast<const T*>(p.v) + t * HD + (int64_t)h * D, lane);
+  RowVec<T, R> kv, vv;
+  kv.load(reinterpret_cast<const T*>(p.k) + t * HD + (int64_t)h * D, lane, D);
+  vv.load(reinterpret_cast<const T*>(p.v) + t * HD + (int64_t)h * D, lane, D);
   const T* qb = reinterpret_cast<const T*>(p.q) + (int64_t)h * D;
   const T* gb = reinterpret_cast<const T*>(p.dout) + (int64_t)h * D;
   float dk[R], dv[R];
@@ -220,13 +243,14 @@ simt_bwd_dkdv_kernel(const DsaltAttnParams p) {
     if (lse == -INFINITY) return 0.f;
     const T* qp = qb + qt * HD;
     const T* gp = gb + qt * HD;
-    const float sc = fmaf(kv.dot(qp, lane), p.scale, bias);
+    const float sc = fmaf(kv.dot(qp, lane, D), p.scale, bias);
     const float pr = expf(sc - lse);
-    const float dp = vv.dot(gp, lane);
+    const float dp = vv.dot(gp, lane, D);
     const float ds = pr * (dp - p.delta[qt * p.H + h]);
     const float dss = ds * p.scale;
 #pragma unroll
     for (int r = 0; r < R; ++r) {
+      if (lane + 32 * r >= D) continue;
       dv[r] = fmaf(pr, to_f32<T>(gp[lane + 32 * r]), dv[r]);
       dk[r] = fmaf(dss, to_f32<T>(qp[lane + 32 * r]), dk[r]);
     }
@@ -259,6 +283,7 @@ simt_bwd_dkdv_kernel(const DsaltAttnParams p) {
   T* dvo = reinterpret_cast<T*>(p.dv) + t * HD + (int64_t)h * D;
 #pragma unroll
   for (int r = 0; r < R; ++r) {
+    if (lane + 32 * r >= D) continue;
     dko[lane + 32 * r] = from_f32<T>(dk[r]);
     dvo[lane + 32 * r] = from_f32<T>(dv[r]);
   }
@@ -275,18 +300,18 @@ __global__ void dw_reduce_kernel(const float* __restrict__ dw_head, T* __restric
 }
 
 // ------------------------------------------------------------------ launchers
-template <typename T, int D>
+template <typename T, int R>
 static cudaError_t launch_simt(int stage, const DsaltAttnParams& p, cudaStream_t st) {
   const int64_t rows = p.T * p.H;
   if (rows == 0) return cudaSuccess;
   const dim3 grid((unsigned)((rows + kSimtWarps - 1) / kSimtWarps));
   const dim3 block(kSimtWarps * 32);
   switch (stage) {
-    case 0: simt_fwd_kernel<T, D><<<grid, block, 0, st>>>(p); break;
-    case 1: bwd_preprocess_kernel<T, D><<<grid, block, 0, st>>>(p); break;
-    case 2: simt_bwd_dkdv_kernel<T, D><<<grid, block, 0, st>>>(p); break;
+    case 0: simt_fwd_kernel<T, R><<<grid, block, 0, st>>>(p); break;
+    case 1: bwd_preprocess_kernel<T, R><<<grid, block, 0, st>>>(p); break;
+    case 2: simt_bwd_dkdv_kernel<T, R><<<grid, block, 0, st>>>(p); break;
     case 3:
-      simt_bwd_dq_kernel<T, D><<<grid, block, 0, st>>>(p);
+      simt_bwd_dq_kernel<T, R><<<grid, block, 0, st>>>(p);
       if (p.dw && p.dw_head)
         dw_reduce_kernel<T><<<(unsigned)((p.T + 255) / 256), 256, 0, st>>>(p.dw_head, reinterpret_cast<T*>(p.dw), p.T, p.H);
       break;
@@ -297,13 +322,19 @@ static cudaError_t launch_simt(int stage, const DsaltAttnParams& p, cudaStream_t
   return cudaGetLastError();
 }
 
+// R = ceil(D/32) values per lane; any head dim that is a multiple of 8 up to 256
 template <typename T>
 static cudaError_t launch_simt_d(int stage, const DsaltAttnParams& p, cudaStream_t st) {
-  switch (p.D) {
-    case 32: return launch_simt<T, 32>(stage, p, st);
-    case 64: return launch_simt<T, 64>(stage, p, st);
-    case 128: return launch_simt<T, 128>(stage, p, st);
-    case 256: return launch_simt<T, 256>(stage, p, st);
+  if (p.D <= 0 || p.D > 256 || p.D % 8 != 0) return cudaErrorInvalidValue;
+  switch ((p.D + 31) / 32) {
+    case 1: return launch_simt<T, 1>(stage, p, st);
+    case 2: return launch_simt<T, 2>(stage, p, st);
+    case 3: return launch_simt<T, 3>(stage, p, st);
+    case 4: return launch_simt<T, 4>(stage, p, st);
+    case 5: return launch_simt<T, 5>(stage, p, st);
+    case 6: return launch_simt<T, 6>(stage, p, st);
+    case 7: return launch_simt<T, 7>(stage, p, st);
+    case 8: return launch_simt<T, 8>(stage, p, st);
   }
   return cudaErrorInvalidValue;
 }

@@ -40,8 +40,8 @@ constexpr float kLn2 = 0.6931471805599453f;
 constexpr float kRescaleThreshold = 8.0f;  // log2 units
 
 enum Bar {
-  Q_FULL = 0, K_FULL = 1, V_FULL = 3, KV_EMPTY = 5, S_FULL = 7, S_EMPTY = 9, P_FULL = 11, O_DONE = 12,
-  FINAL = 13, NUM_BARS = 14
+  Q_FULL = 0, K_FULL = 1, V_FULL = 3, K_EMPTY = 5, V_EMPTY = 7, S_FULL = 9, S_EMPTY = 11, P_FULL = 13,
+  O_DONE = 14, FINAL = 15, NUM_BARS = 16
 };
 
 template <int D>
@@ -93,7 +93,8 @@ __global__ void __launch_bounds__(kThreads, 1) tc_fwd_kernel(const __grid_consta
     for (int st = 0; st < 2; ++st) {
       mbar_init(bar[K_FULL + st], 1);
       mbar_init(bar[V_FULL + st], 1);
-      mbar_init(bar[KV_EMPTY + st], 1);
+      mbar_init(bar[K_EMPTY + st], 1);
+      mbar_init(bar[V_EMPTY + st], 1);
       mbar_init(bar[S_FULL + st], 1);
       mbar_init(bar[S_EMPTY + st], BM);
     }
@@ -167,68 +168,50 @@ __global__ void __launch_bounds__(kThreads, 1) tc_fwd_kernel(const __grid_consta
   const uint32_t tO = tmem + 2 * BN;   // O: columns [256, 256 + D)
 
   if (warp == 4) {
-    // ------------------------------------------------------------ producer
-    if (lane == 0 && n_tiles > 0) {
-      mbar_expect_tx(bar[Q_FULL], BM * D * 2);
+    // ------------------------------------------------------------ producers
+    // lane 0: Q, then K tiles (a K stage frees as soon as its S = Q·Kᵀ is done);
+    // lane 1: V tiles (a V stage frees when its P·V is done).
+    if (lane < 2 && n_tiles > 0) {
+      const bool is_k = lane == 0;
+      if (is_k) {
+        mbar_expect_tx(bar[Q_FULL], BM * D * 2);
 #pragma unroll
-      for (int c = 0; c < D / 64; ++c) tma_load_3d(smem_u32(sm.q + c * (BM * 128)), &a.tm_q, bar[Q_FULL], c * 64, h, (int)(s0 + m0));
+        for (int c = 0; c < D / 64; ++c)
+          tma_load_3d(smem_u32(sm.q + c * (BM * 128)), &a.tm_q, bar[Q_FULL], c * 64, h, (int)(s0 + m0));
+      }
+      const int FULL = is_k ? K_FULL : V_FULL, EMPTY = is_k ? K_EMPTY : V_EMPTY;
       int issued = 0;
       for (int t = 0; t < n_tiles; ++t) {
         const int st = t & 1;
-        if (t >= 2 && !mbar_wait(bar[KV_EMPTY + st], ((t >> 1) - 1) & 1, abort_flag, p.status)) break;
+        if (t >= 2 && !mbar_wait(bar[EMPTY + st], ((t >> 1) - 1) & 1, abort_flag, p.status)) break;
         const bool lmk = t < n_lt;
-        const uint32_t bytes = (lmk ? a.lmk_box : BN) * D * 2;
-        mbar_expect_tx(bar[K_FULL + st], bytes);
+        mbar_expect_tx(bar[FULL + st], (lmk ? a.lmk_box : BN) * D * 2);
+        uint8_t* dst = is_k ? sm.k[st] : sm.v[st];
+        const CUtensorMap* map = lmk ? (is_k ? &a.tm_lk : &a.tm_lv) : (is_k ? &a.tm_k : &a.tm_v);
 #pragma unroll
         for (int c = 0; c < D / 64; ++c) {
-          if (lmk) tma_load_3d(smem_u32(sm.k[st] + c * (BN * 128)), &a.tm_lk, bar[K_FULL + st], c * 64, BN * t, h * p.S + s);
-          else tma_load_3d(smem_u32(sm.k[st] + c * (BN * 128)), &a.tm_k, bar[K_FULL + st], c * 64, h,
-                           (int)(s0 + band_lo + BN * (t - n_lt)));
-        }
-        mbar_expect_tx(bar[V_FULL + st], bytes);
-#pragma unroll
-        for (int c = 0; c < D / 64; ++c) {
-          if (lmk) tma_load_3d(smem_u32(sm.v[st] + c * (BN * 128)), &a.tm_lv, bar[V_FULL + st], c * 64, BN * t, h * p.S + s);
-          else tma_load_3d(smem_u32(sm.v[st] + c * (BN * 128)), &a.tm_v, bar[V_FULL + st], c * 64, h,
+          if (lmk) tma_load_3d(smem_u32(dst + c * (BN * 128)), map, bar[FULL + st], c * 64, BN * t, h * p.S + s);
+          else tma_load_3d(smem_u32(dst + c * (BN * 128)), map, bar[FULL + st], c * 64, h,
                            (int)(s0 + band_lo + BN * (t - n_lt)));
         }
         issued = t + 1;
       }
       // drain: never leave a TMA write in flight into shared memory
-      for (int t = max(0, issued - 2); t < issued; ++t) {
-        const int st = t & 1;
-        mbar_drain(bar[K_FULL + st], (t >> 1) & 1);
-        mbar_drain(bar[V_FULL + st], (t >> 1) & 1);
-      }
-      mbar_drain(bar[Q_FULL], 0);
+      for (int t = max(0, issued - 2); t < issued; ++t) mbar_drain(bar[FULL + (t & 1)], (t >> 1) & 1);
+      if (is_k) mbar_drain(bar[Q_FULL], 0);
     }
   } else if (warp == 5) {
     // ------------------------------------------------------------ MMA issuer
+    // order: S_0, S_1, then for every t: P_t·V_t as soon as P_t is ready, then S_{t+2}
     if (lane == 0 && n_tiles > 0) {
       const uint32_t id_o = idesc_f16(kBF16, BM, D, false, true);
       const uint32_t q_addr = smem_u32(sm.q);
       const uint32_t p_addr = smem_u32(sm.p);
       bool ok = mbar_wait(bar[Q_FULL], 0, abort_flag, p.status);
-      auto issue_pv = [&](int tp) -> bool {
-        const int st = tp & 1;
-        if (!mbar_wait(bar[P_FULL], tp & 1, abort_flag, p.status)) return false;
-        if (!mbar_wait(bar[V_FULL + st], (tp >> 1) & 1, abort_flag, p.status)) return false;
-        tc_fence_after();
-        const uint32_t v_addr = smem_u32(sm.v[st]);
-        const int nk = tile_n(tp) / 16;
-        for (int kk = 0; kk < nk; ++kk) {
-          const uint64_t ad = sdesc_sw128(p_addr + (kk >> 2) * (BM * 128) + (kk & 3) * 32, 16, 1024);
-          const uint64_t bd = sdesc_sw128(v_addr + kk * 2048, BN * 128, 1024);
-          mma_f16(tO, ad, bd, id_o, (tp > 0 || kk > 0) ? 1u : 0u);
-        }
-        mma_commit(bar[O_DONE]);
-        mma_commit(bar[KV_EMPTY + st]);
-        return true;
-      };
-      for (int t = 0; ok && t < n_tiles; ++t) {
+      auto issue_s = [&](int t) -> bool {
         const int st = t & 1;
-        if (!mbar_wait(bar[K_FULL + st], (t >> 1) & 1, abort_flag, p.status)) { ok = false; break; }
-        if (t >= 2 && !mbar_wait(bar[S_EMPTY + st], ((t >> 1) - 1) & 1, abort_flag, p.status)) { ok = false; break; }
+        if (!mbar_wait(bar[K_FULL + st], (t >> 1) & 1, abort_flag, p.status)) return false;
+        if (t >= 2 && !mbar_wait(bar[S_EMPTY + st], ((t >> 1) - 1) & 1, abort_flag, p.status)) return false;
         tc_fence_after();
         const uint32_t k_addr = smem_u32(sm.k[st]);
         const uint32_t id_s = idesc_f16(kBF16, BM, tile_n(t), false, false);
@@ -240,9 +223,27 @@ __global__ void __launch_bounds__(kThreads, 1) tc_fwd_kernel(const __grid_consta
           mma_f16(tS + st * BN, ad, bd, id_s, kk > 0 ? 1u : 0u);
         }
         mma_commit(bar[S_FULL + st]);
-        if (t >= 1 && !issue_pv(t - 1)) { ok = false; break; }
+        mma_commit(bar[K_EMPTY + st]);
+        return true;
+      };
+      if (ok) ok = issue_s(0);
+      if (ok && n_tiles > 1) ok = issue_s(1);
+      for (int t = 0; ok && t < n_tiles; ++t) {
+        const int st = t & 1;
+        if (!mbar_wait(bar[P_FULL], t & 1, abort_flag, p.status)) { ok = false; break; }
+        if (!mbar_wait(bar[V_FULL + st], (t >> 1) & 1, abort_flag, p.status)) { ok = false; break; }
+        tc_fence_after();
+        const uint32_t v_addr = smem_u32(sm.v[st]);
+        const int nk = tile_n(t) / 16;
+        for (int kk = 0; kk < nk; ++kk) {
+          const uint64_t ad = sdesc_sw128(p_addr + (kk >> 2) * (BM * 128) + (kk & 3) * 32, 16, 1024);
+          const uint64_t bd = sdesc_sw128(v_addr + kk * 2048, BN * 128, 1024);
+          mma_f16(tO, ad, bd, id_o, (t > 0 || kk > 0) ? 1u : 0u);
+        }
+        mma_commit(bar[O_DONE]);
+        mma_commit(bar[V_EMPTY + st]);
+        if (t + 2 < n_tiles && !issue_s(t + 2)) { ok = false; break; }
       }
-      if (ok) issue_pv(n_tiles - 1);
       // drain: every issued MMA completes before TMEM is released
       mma_commit(bar[FINAL]);
       mbar_drain(bar[FINAL], 0);
@@ -420,13 +421,7 @@ __global__ void __launch_bounds__(kThreads, 1) tc_fwd_kernel(const __grid_consta
 // ---------------------------------------------------------------- host side
 CUresult encode_3d(CUtensorMap* m, CUtensorMapDataType dt, const void* base, uint64_t d0, uint64_t d1, uint64_t d2,
                    uint64_t stride1_bytes, uint64_t stride2_bytes, uint32_t box0, uint32_t box1, uint32_t box2) {
-  cuuint64_t dims[3] = {d0, d1, d2};
-  cuuint64_t strides[2] = {stride1_bytes, stride2_bytes};
-  cuuint32_t box[3] = {box0, box1, box2};
-  cuuint32_t es[3] = {1, 1, 1};
-  return cuTensorMapEncodeTiled(m, dt, 3, const_cast<void*>(base), dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                                CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                                CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return encode_tensor_map_3d(m, dt, base, d0, d1, d2, stride1_bytes, stride2_bytes, box0, box1, box2);
 }
 
 template <typename T, int D>

@@ -1,23 +1,27 @@
 // tcgen05 / TMEM / TMA backward kernels of the DSALT attention for sm_100a.
 //
-// dQ (query-parallel, reference _train_bwd_kernel dsalt_triton_train.py:240-383):
-//   one CTA = 128 query rows of one (sequence, head); 64-key tiles (landmark
-//   tiles first, then the rows' band).  Per tile the MMA warp computes
-//   S = Q·Kᵀ and dP = dO·Vᵀ into TMEM (double buffered); the softmax warps form
-//   P = exp(S·scale + bias − LSE) and dS = P·(dP − Δ) row by row, apply the soft
-//   window edge to their ≤ ceil(win_edge)+1 edge keys (and accumulate
-//   ∂loss/∂w̃ from them), and write dS to shared memory; the MMA warp then adds
-//   dQ += dS·K in TMEM.
+// Both kernels use 320 threads: warps 0-7 are "row" warps (warp w and w+4
+// share TMEM lanes 32·(w%4)…+31 and split each tile's 64 columns in halves of
+// 32), warp 8 is the producer (TMA + per-tile column data), warp 9 allocates
+// TMEM and issues every tcgen05.mma from one thread.  The MMA issue order is
+// "S/dP two tiles ahead, the accumulating MMAs as soon as their operand tile
+// is ready", with every buffer guarded by its own full/empty mbarrier.
 //
-// dK/dV (key-parallel, atomic-free; reference _train_bwd_dkdv_kernel :386-481 and
-//   the landmark atomics of :302-333):
-//   one CTA = 128 keys and the 64-query tiles that can attend them.  Per tile:
-//   Sᵀ = K·Qᵀ, dPᵀ = V·dOᵀ (TMEM), then Pᵀ, dSᵀ (shared memory) and
-//   dV += Pᵀ·dO, dK += dSᵀ·Q (TMEM).  Two passes: landmark items (the sorted
-//   landmark slots of one (head, sequence) as the 128 "keys", every later query
-//   as columns) write fp32 dK/dV per slot and d_lw (a row sum, no atomics);
-//   band items (128 consecutive keys) then add those slot rows into their
-//   own dK/dV before the single store.  The backward is therefore deterministic.
+// dQ (query-parallel, reference _train_bwd_kernel dsalt_triton_train.py:240-383):
+//   rows = 128 queries; tiles = 64 keys (landmark tiles, then the rows' band).
+//   S = Q·Kᵀ, dP = dO·Vᵀ (TMEM) -> P = exp(S·scale + bias − LSE),
+//   dS = P·(dP − Δ) (registers) -> dS (bf16, smem), soft-edge fix-up on the
+//   row's edge keys, which also accumulates ∂loss/∂w̃ -> dQ += dS·K (TMEM).
+//
+// dK/dV (key-parallel, atomic-free; reference _train_bwd_dkdv_kernel :386-481
+//   and the landmark atomics of :302-333):
+//   rows = 128 keys; tiles = 64 queries.  Sᵀ = K·Qᵀ, dPᵀ = V·dOᵀ (TMEM) ->
+//   Pᵀ, dSᵀ (bf16, smem; soft-edge fix-up per query column) ->
+//   dV += Pᵀ·dO, dK += dSᵀ·Q (TMEM).  Landmark items (the sorted landmark slots
+//   of one (head, sequence) as the keys, every later query as columns) write
+//   fp32 dK/dV per slot and d_lw (a row sum: no atomics); band items (128
+//   consecutive keys) add those slot rows into their own before the single
+//   store.  The backward is deterministic.
 //
 // All waits are bounded (sm100::mbar_wait); see attn_tc.cu.
 #include "common.cuh"
@@ -29,7 +33,10 @@ cudaError_t simt_attention_stage(int stage, const DsaltAttnParams& p, cudaStream
 
 namespace bwd {
 
-constexpr int kThreads = 192;
+constexpr int kThreads = 320;
+constexpr int kRowThreads = 256;
+constexpr int kProducerWarp = 8;
+constexpr int kMmaWarp = 9;
 constexpr int kMaxLmk = 512;
 constexpr float kLog2e = 1.4426950408889634f;
 
@@ -43,11 +50,25 @@ struct alignas(64) BwdArgs {
   int lmk_box;    // rows of one landmark TMA box
 };
 
+// store 32 values of one row as four 16-byte bf16/fp16 units of a 128B-swizzled tile
+template <bool BF16>
+__device__ __forceinline__ void store_row32(uint8_t* base, int row, int col0, const float* v) {
+#pragma unroll
+  for (int g = 0; g < 4; ++g) {
+    uint4 u;
+    u.x = sm100::pack2(v[8 * g + 0], v[8 * g + 1], BF16);
+    u.y = sm100::pack2(v[8 * g + 2], v[8 * g + 3], BF16);
+    u.z = sm100::pack2(v[8 * g + 4], v[8 * g + 5], BF16);
+    u.w = sm100::pack2(v[8 * g + 6], v[8 * g + 7], BF16);
+    *reinterpret_cast<uint4*>(base + sm100::sw128_offset(row, col0 + 8 * g)) = u;
+  }
+}
+
 // ======================================================================= dQ
 namespace dq {
 constexpr int BM = 128, BN = 64;
-enum { QD_FULL = 0, K_FULL = 1, V_FULL = 3, KV_EMPTY = 5, SD_FULL = 7, SD_EMPTY = 9, DS_FULL = 11, DS_EMPTY = 13,
-       DQ_DONE = 15, FINAL = 16, NB = 17 };
+enum { QD_FULL = 0, K_FULL = 1, V_FULL = 3, K_EMPTY = 5, V_EMPTY = 7, SD_FULL = 9, SD_EMPTY = 11, DS_FULL = 13,
+       DS_EMPTY = 15, DQ_DONE = 17, FINAL = 18, EPI = 19, NB = 20 };
 
 template <int D>
 struct alignas(1024) Smem {
@@ -59,6 +80,7 @@ struct alignas(1024) Smem {
   uint64_t bars[NB];
   uint32_t tmem_base;
   int abort_flag, band_lo, band_hi, cnt_max, n_valid;
+  float dw_half[BM];
   int lmk_pos[kMaxLmk];
   float lmk_lw2[kMaxLmk];
 };
@@ -83,14 +105,16 @@ __global__ void __launch_bounds__(kThreads, 1) tc_bwd_dq_kernel(const __grid_con
     for (int st = 0; st < 2; ++st) {
       mbar_init(bar[K_FULL + st], 1);
       mbar_init(bar[V_FULL + st], 1);
-      mbar_init(bar[KV_EMPTY + st], 1);
+      mbar_init(bar[K_EMPTY + st], 1);
+      mbar_init(bar[V_EMPTY + st], 1);
       mbar_init(bar[SD_FULL + st], 1);
-      mbar_init(bar[SD_EMPTY + st], BM);
-      mbar_init(bar[DS_FULL + st], BM);
+      mbar_init(bar[SD_EMPTY + st], kRowThreads);
+      mbar_init(bar[DS_FULL + st], kRowThreads);
       mbar_init(bar[DS_EMPTY + st], 1);
     }
     mbar_init(bar[DQ_DONE], 1);
     mbar_init(bar[FINAL], 1);
+    mbar_init(bar[EPI], kRowThreads);
     fence_mbar_init();
     sm.abort_flag = 0;
     sm.band_lo = INT_MAX;
@@ -98,7 +122,7 @@ __global__ void __launch_bounds__(kThreads, 1) tc_bwd_dq_kernel(const __grid_con
     sm.cnt_max = 0;
     sm.n_valid = 0;
   }
-  if (warp == 5) tmem_alloc(smem_u32(&sm.tmem_base), 512);
+  if (warp == kMmaWarp) tmem_alloc(smem_u32(&sm.tmem_base), 512);
   const int kp = p.kp;
   const int64_t lbase = ((int64_t)h * p.S + s) * kp;
   for (int c = tid; c < kp; c += kThreads) {
@@ -108,8 +132,11 @@ __global__ void __launch_bounds__(kThreads, 1) tc_bwd_dq_kernel(const __grid_con
     if (ps >= 0) atomicAdd(&sm.n_valid, 1);
   }
   __syncthreads();
-  const int i = m0 + tid;
-  const bool row_ok = tid < BM && i < L;
+  // row r (TMEM lane) = 32·(warp % 4) + lane; column half = warp / 4
+  const int r = 32 * (warp & 3) + lane;
+  const int half = (warp >> 2) & 1;
+  const int i = m0 + r;
+  const bool row_ok = warp < 8 && i < L;
   RowWindow rw = {};
   int lo = INT_MAX, hi = -1, cnt = 0;
   float lse2 = -INFINITY, delta = 0.f;
@@ -127,8 +154,10 @@ __global__ void __launch_bounds__(kThreads, 1) tc_bwd_dq_kernel(const __grid_con
     }
     cnt = a0;
     if (lse2 == -INFINITY) { lo = INT_MAX; hi = -1; cnt = 0; }  // empty row: no gradient
-    if (lo <= hi) { atomicMin(&sm.band_lo, lo); atomicMax(&sm.band_hi, hi); }
-    if (cnt > 0) atomicMax(&sm.cnt_max, cnt);
+    if (half == 0) {
+      if (lo <= hi) { atomicMin(&sm.band_lo, lo); atomicMax(&sm.band_hi, hi); }
+      if (cnt > 0) atomicMax(&sm.cnt_max, cnt);
+    }
   }
   tc_fence_before();
   __syncthreads();
@@ -139,74 +168,57 @@ __global__ void __launch_bounds__(kThreads, 1) tc_bwd_dq_kernel(const __grid_con
   const int n_bt = band_hi >= band_lo ? (band_hi - band_lo + BN) / BN : 0;
   const int n_tiles = n_lt + n_bt;
   volatile int* abort_flag = &sm.abort_flag;
+  // valid key rows of tile t (landmark tiles may hold fewer than BN loaded rows)
   auto tile_n = [&](int t) -> int {
     if (t < n_lt) return round16(min(BN, cnt_max - BN * t));
-    return round16(min(BN, band_hi - (band_lo + BN * (t - n_lt)) + 1));
+    return BN;
   };
   const uint32_t tS = tmem, tdP = tmem + 2 * BN, tdQ = tmem + 4 * BN;
 
-  if (warp == 4) {
-    if (lane == 0 && n_tiles > 0) {
-      mbar_expect_tx(bar[QD_FULL], 2 * BM * D * 2);
+  if (warp == kProducerWarp) {
+    // lane 0: Q, dO, K tiles; lane 1: V tiles
+    if (lane < 2 && n_tiles > 0) {
+      const bool is_k = lane == 0;
+      if (is_k) {
+        mbar_expect_tx(bar[QD_FULL], 2 * BM * D * 2);
 #pragma unroll
-      for (int c = 0; c < D / 64; ++c) {
-        tma_load_3d(smem_u32(sm.q + c * (BM * 128)), &a.tm_q, bar[QD_FULL], c * 64, h, (int)(s0 + m0));
-        tma_load_3d(smem_u32(sm.dO + c * (BM * 128)), &a.tm_do, bar[QD_FULL], c * 64, h, (int)(s0 + m0));
+        for (int c = 0; c < D / 64; ++c) {
+          tma_load_3d(smem_u32(sm.q + c * (BM * 128)), &a.tm_q, bar[QD_FULL], c * 64, h, (int)(s0 + m0));
+          tma_load_3d(smem_u32(sm.dO + c * (BM * 128)), &a.tm_do, bar[QD_FULL], c * 64, h, (int)(s0 + m0));
+        }
       }
+      const int FULL = is_k ? K_FULL : V_FULL, EMPTY = is_k ? K_EMPTY : V_EMPTY;
       int issued = 0;
       for (int t = 0; t < n_tiles; ++t) {
         const int st = t & 1;
-        if (t >= 2 && !mbar_wait(bar[KV_EMPTY + st], ((t >> 1) - 1) & 1, abort_flag, p.status)) break;
+        if (t >= 2 && !mbar_wait(bar[EMPTY + st], ((t >> 1) - 1) & 1, abort_flag, p.status)) break;
         const bool lmk = t < n_lt;
-        const uint32_t bytes = (lmk ? a.lmk_box : BN) * D * 2;
-        const int z = (int)(s0 + band_lo + BN * (t - n_lt));
-        mbar_expect_tx(bar[K_FULL + st], bytes);
+        mbar_expect_tx(bar[FULL + st], (lmk ? a.lmk_box : BN) * D * 2);
+        uint8_t* dst = is_k ? sm.k[st] : sm.v[st];
+        const CUtensorMap* map = lmk ? (is_k ? &a.tm_lk : &a.tm_lv) : (is_k ? &a.tm_k : &a.tm_v);
 #pragma unroll
         for (int c = 0; c < D / 64; ++c) {
-          if (lmk) tma_load_3d(smem_u32(sm.k[st] + c * (BN * 128)), &a.tm_lk, bar[K_FULL + st], c * 64, BN * t, h * p.S + s);
-          else tma_load_3d(smem_u32(sm.k[st] + c * (BN * 128)), &a.tm_k, bar[K_FULL + st], c * 64, h, z);
-        }
-        mbar_expect_tx(bar[V_FULL + st], bytes);
-#pragma unroll
-        for (int c = 0; c < D / 64; ++c) {
-          if (lmk) tma_load_3d(smem_u32(sm.v[st] + c * (BN * 128)), &a.tm_lv, bar[V_FULL + st], c * 64, BN * t, h * p.S + s);
-          else tma_load_3d(smem_u32(sm.v[st] + c * (BN * 128)), &a.tm_v, bar[V_FULL + st], c * 64, h, z);
+          if (lmk) tma_load_3d(smem_u32(dst + c * (BN * 128)), map, bar[FULL + st], c * 64, BN * t, h * p.S + s);
+          else tma_load_3d(smem_u32(dst + c * (BN * 128)), map, bar[FULL + st], c * 64, h,
+                           (int)(s0 + band_lo + BN * (t - n_lt)));
         }
         issued = t + 1;
       }
-      for (int t = max(0, issued - 2); t < issued; ++t) {
-        mbar_drain(bar[K_FULL + (t & 1)], (t >> 1) & 1);
-        mbar_drain(bar[V_FULL + (t & 1)], (t >> 1) & 1);
-      }
-      mbar_drain(bar[QD_FULL], 0);
+      for (int t = max(0, issued - 2); t < issued; ++t) mbar_drain(bar[FULL + (t & 1)], (t >> 1) & 1);
+      if (is_k) mbar_drain(bar[QD_FULL], 0);
     }
-  } else if (warp == 5) {
+  } else if (warp == kMmaWarp) {
     if (lane == 0 && n_tiles > 0) {
+      const uint32_t id_s = idesc_f16(kBF16, BM, BN, false, false);
       const uint32_t id_dq = idesc_f16(kBF16, BM, D, false, true);
       const uint32_t q_addr = smem_u32(sm.q), do_addr = smem_u32(sm.dO);
       bool ok = mbar_wait(bar[QD_FULL], 0, abort_flag, p.status);
-      auto issue_dq = [&](int tp) -> bool {
-        const int st = tp & 1;
-        if (!mbar_wait(bar[DS_FULL + st], (tp >> 1) & 1, abort_flag, p.status)) return false;
-        tc_fence_after();
-        const uint32_t ds_addr = smem_u32(sm.ds[st]), k_addr = smem_u32(sm.k[st]);
-        const int nk = tile_n(tp) / 16;
-        for (int kk = 0; kk < nk; ++kk) {
-          const uint64_t ad = sdesc_sw128(ds_addr + kk * 32, 16, 1024);
-          const uint64_t bd = sdesc_sw128(k_addr + kk * 2048, BN * 128, 1024);
-          mma_f16(tdQ, ad, bd, id_dq, (tp > 0 || kk > 0) ? 1u : 0u);
-        }
-        mma_commit(bar[DS_EMPTY + st]);
-        mma_commit(bar[KV_EMPTY + st]);
-        return true;
-      };
-      for (int t = 0; ok && t < n_tiles; ++t) {
+      auto issue_sd = [&](int t) -> bool {
         const int st = t & 1;
-        if (!mbar_wait(bar[K_FULL + st], (t >> 1) & 1, abort_flag, p.status)) { ok = false; break; }
-        if (!mbar_wait(bar[V_FULL + st], (t >> 1) & 1, abort_flag, p.status)) { ok = false; break; }
-        if (t >= 2 && !mbar_wait(bar[SD_EMPTY + st], ((t >> 1) - 1) & 1, abort_flag, p.status)) { ok = false; break; }
+        if (!mbar_wait(bar[K_FULL + st], (t >> 1) & 1, abort_flag, p.status)) return false;
+        if (!mbar_wait(bar[V_FULL + st], (t >> 1) & 1, abort_flag, p.status)) return false;
+        if (t >= 2 && !mbar_wait(bar[SD_EMPTY + st], ((t >> 1) - 1) & 1, abort_flag, p.status)) return false;
         tc_fence_after();
-        const uint32_t id_s = idesc_f16(kBF16, BM, tile_n(t), false, false);
         const uint32_t k_addr = smem_u32(sm.k[st]), v_addr = smem_u32(sm.v[st]);
 #pragma unroll
         for (int kk = 0; kk < D / 16; ++kk) {
@@ -214,25 +226,36 @@ __global__ void __launch_bounds__(kThreads, 1) tc_bwd_dq_kernel(const __grid_con
           const uint32_t boff = (kk >> 2) * (BN * 128) + (kk & 3) * 32;
           mma_f16(tS + st * BN, sdesc_sw128(q_addr + aoff, 16, 1024), sdesc_sw128(k_addr + boff, 16, 1024), id_s,
                   kk > 0 ? 1u : 0u);
-        }
-#pragma unroll
-        for (int kk = 0; kk < D / 16; ++kk) {
-          const uint32_t aoff = (kk >> 2) * (BM * 128) + (kk & 3) * 32;
-          const uint32_t boff = (kk >> 2) * (BN * 128) + (kk & 3) * 32;
-          mma_f16(tdP + st * BN, sdesc_sw128(do_addr + aoff, 16, 1024), sdesc_sw128(v_addr + boff, 16, 1024), id_s,
-                  kk > 0 ? 1u : 0u);
+          mma_f16(tdP + st * BN, sdesc_sw128(do_addr + aoff, 16, 1024), sdesc_sw128(v_addr + boff, 16, 1024),
+                  id_s, kk > 0 ? 1u : 0u);
         }
         mma_commit(bar[SD_FULL + st]);
-        if (t >= 1 && !issue_dq(t - 1)) { ok = false; break; }
+        mma_commit(bar[V_EMPTY + st]);
+        return true;
+      };
+      if (ok) ok = issue_sd(0);
+      if (ok && n_tiles > 1) ok = issue_sd(1);
+      for (int t = 0; ok && t < n_tiles; ++t) {
+        const int st = t & 1;
+        if (!mbar_wait(bar[DS_FULL + st], (t >> 1) & 1, abort_flag, p.status)) { ok = false; break; }
+        tc_fence_after();
+        const uint32_t ds_addr = smem_u32(sm.ds[st]), k_addr = smem_u32(sm.k[st]);
+        const int nk = tile_n(t) / 16;
+        for (int kk = 0; kk < nk; ++kk)
+          mma_f16(tdQ, sdesc_sw128(ds_addr + kk * 32, 16, 1024), sdesc_sw128(k_addr + kk * 2048, BN * 128, 1024),
+                  id_dq, (t > 0 || kk > 0) ? 1u : 0u);
+        mma_commit(bar[DS_EMPTY + st]);
+        mma_commit(bar[K_EMPTY + st]);
+        if (t + 2 < n_tiles && !issue_sd(t + 2)) { ok = false; break; }
       }
-      if (ok) ok = issue_dq(n_tiles - 1);
       mma_commit(bar[DQ_DONE]);
       mma_commit(bar[FINAL]);
       mbar_drain(bar[FINAL], 0);
     }
   } else {
-    const int r = tid;
-    const uint32_t lane_addr = ((uint32_t)(warp * 32) << 16);
+    // --------------------------------------------------------- row warps
+    const uint32_t lane_addr = ((uint32_t)(32 * (warp & 3)) << 16);
+    const int c0 = BN / 2 * half;  // first tile column of this thread
     const float sl2 = p.scale * kLog2e;
     const float inv_tau = 1.0f / p.tau_win;
     int d_e0 = INT_MAX;
@@ -244,38 +267,30 @@ __global__ void __launch_bounds__(kThreads, 1) tc_bwd_dq_kernel(const __grid_con
       ok = mbar_wait(bar[SD_FULL + st], (t >> 1) & 1, abort_flag, p.status);
       if (!__all_sync(0xffffffffu, ok)) { ok = false; break; }
       tc_fence_after();
-      const int N = tile_n(t);
-      float sv[BN], dpv[BN];
-#pragma unroll
-      for (int ch = 0; ch < BN / 32; ++ch) {
-        if (ch * 32 < N) {
-          tmem_ld32(tS + lane_addr + st * BN + ch * 32, sv + ch * 32);
-          tmem_ld32(tdP + lane_addr + st * BN + ch * 32, dpv + ch * 32);
-        }
-      }
+      float sv[32], dpv[32];
+      tmem_ld32(tS + lane_addr + st * BN + c0, sv);
+      tmem_ld32(tdP + lane_addr + st * BN + c0, dpv);
       tmem_wait_ld();
       tc_fence_before();
       mbar_arrive(bar[SD_EMPTY + st]);
       const bool lmk = t < n_lt;
       const int n0 = lmk ? 0 : band_lo + BN * (t - n_lt);
       if (lmk) {
-        const int climit = cnt - BN * t;
-        const float* lw2 = sm.lmk_lw2 + BN * t;
+        const int climit = cnt - BN * t - c0;
+        const float* lw2 = sm.lmk_lw2 + BN * t + c0;
 #pragma unroll
-        for (int c = 0; c < BN; ++c) {
-          if (c < N) {
-            const float pr = (c < climit) ? fast_exp2(fmaf(sv[c], sl2, lw2[c] - lse2)) : 0.f;
-            sv[c] = pr * (dpv[c] - delta);
-          }
+        for (int c = 0; c < 32; ++c) {
+          const float pr = fast_exp2(fmaf(sv[c], sl2, lw2[c] - lse2));
+          const float dsv = pr * (dpv[c] - delta);
+          sv[c] = (c < climit) ? dsv : 0.f;
         }
       } else {
-        const int clo = lo - n0, chi = hi - n0;
+        const int clo = lo - n0 - c0, chi = hi - n0 - c0;
 #pragma unroll
-        for (int c = 0; c < BN; ++c) {
-          if (c < N) {
-            const float pr = (c >= clo && c <= chi) ? fast_exp2(fmaf(sv[c], sl2, -lse2)) : 0.f;
-            sv[c] = pr * (dpv[c] - delta);
-          }
+        for (int c = 0; c < 32; ++c) {
+          const float pr = fast_exp2(fmaf(sv[c], sl2, -lse2));
+          const float dsv = pr * (dpv[c] - delta);
+          sv[c] = (c >= clo && c <= chi) ? dsv : 0.f;
         }
       }
       if (t >= 2) {
@@ -283,30 +298,19 @@ __global__ void __launch_bounds__(kThreads, 1) tc_bwd_dq_kernel(const __grid_con
         if (!__all_sync(0xffffffffu, ok)) { ok = false; break; }
       }
       uint8_t* dsb = sm.ds[st];
-#pragma unroll
-      for (int c8 = 0; c8 < BN / 8; ++c8) {
-        if (c8 * 8 < N) {
-          const int c = c8 * 8;
-          uint4 u;
-          u.x = pack2(sv[c + 0], sv[c + 1], kBF16);
-          u.y = pack2(sv[c + 2], sv[c + 3], kBF16);
-          u.z = pack2(sv[c + 4], sv[c + 5], kBF16);
-          u.w = pack2(sv[c + 6], sv[c + 7], kBF16);
-          *reinterpret_cast<uint4*>(dsb + sw128_offset(r, c)) = u;
-        }
-      }
+      store_row32<kBF16>(dsb, r, c0, sv);
       if (!lmk && row_ok && lo <= hi && d_e0 <= rw.W) {
-        // soft window edge: P and dS scale by σ((w̃ − d)/τ); ∂loss/∂w̃ += dS·(1 − σ)/τ
-        const int d_hi = min(min(rw.W, i), i - n0);
-        const int d_lo = max(d_e0, i - (n0 + N - 1));
+        // soft window edge on this thread's half: dS *= σ((w̃ − d)/τ); ∂loss/∂w̃ += dS·(1 − σ)/τ
+        const int d_hi = min(min(rw.W, i), i - n0 - c0);
+        const int d_lo = max(d_e0, i - (n0 + c0 + 31));
         for (int d = d_lo; d <= d_hi; ++d) {
           const int c = i - d - n0;
           T* e = reinterpret_cast<T*>(dsb + sw128_offset(r, c));
           const float z = (rw.wt - (float)d) * inv_tau;
           const float sg = 1.0f / (1.0f + expf(-z));
-          const float dsb_v = to_f32<T>(*e) * sg;
-          *e = from_f32<T>(dsb_v);
-          dw = fmaf(dsb_v, (1.0f - sg) * inv_tau, dw);
+          const float v = to_f32<T>(*e) * sg;
+          *e = from_f32<T>(v);
+          dw = fmaf(v, (1.0f - sg) * inv_tau, dw);
         }
       }
       fence_async_smem();
@@ -317,13 +321,15 @@ __global__ void __launch_bounds__(kThreads, 1) tc_bwd_dq_kernel(const __grid_con
       ok = __all_sync(0xffffffffu, ok);
       tc_fence_after();
     }
+    // dQ columns [half·D/2, (half+1)·D/2) of row r
     const int64_t row_off = (s0 + i) * (int64_t)p.H * D + (int64_t)h * D;
-    T* dq = reinterpret_cast<T*>(p.dq) + row_off;
+    T* dqo = reinterpret_cast<T*>(p.dq) + row_off;
 #pragma unroll
-    for (int ch = 0; ch < D / 32; ++ch) {
+    for (int ch = 0; ch < D / 64; ++ch) {
+      const int col = half * (D / 2) + ch * 32;
       float o[32];
       if (ok && n_tiles > 0) {
-        tmem_ld32(tdQ + lane_addr + ch * 32, o);
+        tmem_ld32(tdQ + lane_addr + col, o);
         tmem_wait_ld();
       } else {
 #pragma unroll
@@ -337,24 +343,28 @@ __global__ void __launch_bounds__(kThreads, 1) tc_bwd_dq_kernel(const __grid_con
           u.y = pack2(o[j + 2] * p.scale, o[j + 3] * p.scale, kBF16);
           u.z = pack2(o[j + 4] * p.scale, o[j + 5] * p.scale, kBF16);
           u.w = pack2(o[j + 6] * p.scale, o[j + 7] * p.scale, kBF16);
-          *reinterpret_cast<uint4*>(dq + ch * 32 + j) = u;
+          *reinterpret_cast<uint4*>(dqo + col + j) = u;
         }
       }
     }
-    if (row_ok && p.dw_head) p.dw_head[(s0 + i) * p.H + h] = ok ? dw : 0.f;
+    // ∂loss/∂w̃ of the row: sum of the two halves
+    if (half == 1) sm.dw_half[r] = dw;
+    mbar_arrive(bar[EPI]);
+    const bool ok2 = mbar_wait(bar[EPI], 0, abort_flag, p.status);
+    if (half == 0 && row_ok && p.dw_head) p.dw_head[(s0 + i) * p.H + h] = (ok && ok2) ? dw + sm.dw_half[r] : 0.f;
   }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
-  if (warp == 5) tmem_dealloc(tmem, 512);
+  if (warp == kMmaWarp) tmem_dealloc(tmem, 512);
 }
 }  // namespace dq
 
 // ==================================================================== dK / dV
 namespace dkv {
 constexpr int BM = 128, BN = 64;  // BM keys (TMEM lanes), BN queries per tile
-enum { KV_FULL = 0, Q_FULL = 1, DO_FULL = 3, QDO_EMPTY = 5, SD_FULL = 7, SD_EMPTY = 9, PDS_FULL = 11,
-       PDS_EMPTY = 13, KV_DONE = 15, FINAL = 16, ROWS_DONE = 17, NB = 18 };
+enum { KV_FULL = 0, Q_FULL = 1, DO_FULL = 3, QDO_EMPTY = 5, COL_FULL = 7, SD_FULL = 9, SD_EMPTY = 11,
+       PDS_FULL = 13, PDS_EMPTY = 15, ROWS = 17, KV_DONE = 19, FINAL = 20, EPI = 21, NB = 22 };
 
 template <int D>
 struct alignas(1024) Smem {
@@ -367,15 +377,15 @@ struct alignas(1024) Smem {
   uint64_t bars[NB];
   uint32_t tmem_base;
   int abort_flag;
-  // per query column of the current / next tile
-  float c_lse2[2][BN], c_delta[2][BN], c_wt[2][BN], c_wlo[2][BN];
-  int c_lo[2][BN], c_i[2][BN], c_ehi[2][BN];
-};
-
-// Column data of query q (sequence position) for head h.
-struct ColInfo {
-  float lse2, delta, wt, wlo;
-  int lo, i, ehi;  // band start of the query, its position, last edge key (< lo: no edge)
+  // per query column of a tile (double-buffered by tile parity)
+  alignas(16) float c_nlse2[2][BN];  // −LSE·log2(e) (0 for columns excluded by c_lo / c_i)
+  alignas(16) float c_delta[2][BN];
+  alignas(16) float c_wlo[2][BN];    // float(i) − w̃ (landmark rule)
+  alignas(16) float c_wt[2][BN];     // w̃ (edge bias)
+  alignas(16) int c_lo[2][BN];       // band start key of the query (INT_MAX: none)
+  alignas(16) int c_i[2][BN];        // query position (INT_MIN: no query / empty row)
+  alignas(16) int c_ehi[2][BN];      // last edge key (INT_MIN: none)
+  float dlw_half[BM];
 };
 
 template <bool LMK, typename T, int D>
@@ -384,11 +394,9 @@ __global__ void __launch_bounds__(kThreads, 1) tc_bwd_dkdv_kernel(const __grid_c
   const DsaltAttnParams& p = a.p;
   const int h = blockIdx.y;
   int s, key0, nkeys, q_start;
-  int64_t s0;
+  int64_t s0, lbase;
   int L;
-  int64_t lbase = 0;
   if (LMK) {
-    // item = (h, s, chunk of 128 sorted landmark slots)
     const int nch = (p.kp + BM - 1) / BM;
     s = blockIdx.x / nch;
     const int chunk = blockIdx.x % nch;
@@ -425,115 +433,111 @@ __global__ void __launch_bounds__(kThreads, 1) tc_bwd_dkdv_kernel(const __grid_c
       mbar_init(bar[Q_FULL + st], 1);
       mbar_init(bar[DO_FULL + st], 1);
       mbar_init(bar[QDO_EMPTY + st], 1);
+      mbar_init(bar[COL_FULL + st], 32);
       mbar_init(bar[SD_FULL + st], 1);
-      mbar_init(bar[SD_EMPTY + st], BM);
-      mbar_init(bar[PDS_FULL + st], BM);
+      mbar_init(bar[SD_EMPTY + st], kRowThreads);
+      mbar_init(bar[PDS_FULL + st], kRowThreads);
       mbar_init(bar[PDS_EMPTY + st], 1);
+      mbar_init(bar[ROWS + st], kRowThreads);
     }
     mbar_init(bar[KV_DONE], 1);
     mbar_init(bar[FINAL], 1);
-    mbar_init(bar[ROWS_DONE], BM);
+    mbar_init(bar[EPI], kRowThreads);
     fence_mbar_init();
     sm.abort_flag = 0;
   }
-  if (warp == 5) tmem_alloc(smem_u32(&sm.tmem_base), 512);
-  const float inv_tau = 1.0f / p.tau_win;
-  auto col_info = [&](int q) -> ColInfo {
-    ColInfo ci;
-    ci.i = q;
-    ci.lse2 = -INFINITY; ci.delta = 0.f; ci.wt = 0.f; ci.wlo = -INFINITY; ci.lo = INT_MAX; ci.ehi = INT_MIN;
-    if (q >= 0 && q < L) {
-      const int64_t row = (s0 + q) * p.H + h;
-      ci.lse2 = __ldg(p.lse + row) * kLog2e;
-      ci.delta = __ldg(p.delta + row);
-      const RowWindow rw = row_window(__ldg(p.w + s0 + q), q, p.semantics, p.win_edge);
-      ci.wt = rw.wt;
-      ci.wlo = rw.win_lo;
-      if (rw.W >= 0 && ci.lse2 != -INFINITY) {
-        ci.lo = q - min(rw.W, q);
-        const int d_e0 = max((int)floorf(rw.core) + 1, 0);
-        ci.ehi = d_e0 <= rw.W ? q - d_e0 : INT_MIN;
-      }
-      if (ci.lse2 == -INFINITY) ci.wlo = -INFINITY;  // empty rows take no landmark gradient either
-    }
-    return ci;
-  };
-  auto store_col = [&](int buf, int c, const ColInfo& ci) {
-    sm.c_lse2[buf][c] = ci.lse2; sm.c_delta[buf][c] = ci.delta; sm.c_wt[buf][c] = ci.wt; sm.c_wlo[buf][c] = ci.wlo;
-    sm.c_lo[buf][c] = ci.lo; sm.c_i[buf][c] = ci.i; sm.c_ehi[buf][c] = ci.ehi;
-  };
-  if (tid < BN && n_tiles > 0) store_col(0, tid, col_info(q_start + tid));
+  if (warp == kMmaWarp) tmem_alloc(smem_u32(&sm.tmem_base), 512);
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = sm.tmem_base;
   volatile int* abort_flag = &sm.abort_flag;
   const uint32_t tS = tmem, tdP = tmem + 2 * BN, tdK = tmem + 4 * BN, tdV = tmem + 4 * BN + D;
-  auto tile_n = [&](int u) -> int { return round16(min(BN, q_end - (q_start + BN * u) + 1)); };
+  const float inv_tau = 1.0f / p.tau_win;
 
-  if (warp == 4) {
-    if (lane == 0 && n_tiles > 0) {
-      const uint32_t kv_bytes = (LMK ? a.lmk_box : BM) * D * 2;
-      mbar_expect_tx(bar[KV_FULL], 2 * kv_bytes);
+  if (warp == kProducerWarp) {
+    // ---------------------------------------------------- producer warp
+    // per tile: the 64 queries' column data (2 per lane), then Q and dO tiles (lane 0)
+    if (n_tiles > 0) {
+      if (lane == 0) {
+        const uint32_t kv_bytes = (LMK ? a.lmk_box : BM) * D * 2;
+        mbar_expect_tx(bar[KV_FULL], 2 * kv_bytes);
 #pragma unroll
-      for (int c = 0; c < D / 64; ++c) {
-        if (LMK) {
-          tma_load_3d(smem_u32(sm.k + c * (BM * 128)), &a.tm_lk, bar[KV_FULL], c * 64, key0, h * p.S + s);
-          tma_load_3d(smem_u32(sm.v + c * (BM * 128)), &a.tm_lv, bar[KV_FULL], c * 64, key0, h * p.S + s);
-        } else {
-          tma_load_3d(smem_u32(sm.k + c * (BM * 128)), &a.tm_k, bar[KV_FULL], c * 64, h, (int)(s0 + key0));
-          tma_load_3d(smem_u32(sm.v + c * (BM * 128)), &a.tm_v, bar[KV_FULL], c * 64, h, (int)(s0 + key0));
+        for (int c = 0; c < D / 64; ++c) {
+          if (LMK) {
+            tma_load_3d(smem_u32(sm.k + c * (BM * 128)), &a.tm_lk, bar[KV_FULL], c * 64, key0, h * p.S + s);
+            tma_load_3d(smem_u32(sm.v + c * (BM * 128)), &a.tm_lv, bar[KV_FULL], c * 64, key0, h * p.S + s);
+          } else {
+            tma_load_3d(smem_u32(sm.k + c * (BM * 128)), &a.tm_k, bar[KV_FULL], c * 64, h, (int)(s0 + key0));
+            tma_load_3d(smem_u32(sm.v + c * (BM * 128)), &a.tm_v, bar[KV_FULL], c * 64, h, (int)(s0 + key0));
+          }
         }
       }
       int issued = 0;
       for (int u = 0; u < n_tiles; ++u) {
         const int st = u & 1;
         if (u >= 2 && !mbar_wait(bar[QDO_EMPTY + st], ((u >> 1) - 1) & 1, abort_flag, p.status)) break;
-        const int z = (int)(s0 + q_start + BN * u);
-        mbar_expect_tx(bar[Q_FULL + st], BN * D * 2);
+        const int q0 = q_start + BN * u;
 #pragma unroll
-        for (int c = 0; c < D / 64; ++c)
-          tma_load_3d(smem_u32(sm.q[st] + c * (BN * 128)), &a.tm_q, bar[Q_FULL + st], c * 64, h, z);
-        mbar_expect_tx(bar[DO_FULL + st], BN * D * 2);
+        for (int k2 = 0; k2 < 2; ++k2) {
+          const int c = lane + 32 * k2;
+          const int q = q0 + c;
+          float nl2 = 0.f, dl = 0.f, wt = 0.f, wlo = -INFINITY;
+          int clo = INT_MAX, ci = INT_MIN, ehi = INT_MIN;
+          if (q < L) {
+            const int64_t row = (s0 + q) * p.H + h;
+            const float lse = __ldg(p.lse + row);
+            if (lse != -INFINITY) {
+              nl2 = -lse * kLog2e;
+              dl = __ldg(p.delta + row);
+              const RowWindow rw = row_window(__ldg(p.w + s0 + q), q, p.semantics, p.win_edge);
+              wt = rw.wt;
+              wlo = rw.win_lo;
+              ci = q;
+              if (rw.W >= 0) {
+                clo = q - min(rw.W, q);
+                const int d_e0 = max((int)floorf(rw.core) + 1, 0);
+                ehi = d_e0 <= rw.W ? q - d_e0 : INT_MIN;
+              }
+            }
+          }
+          sm.c_nlse2[st][c] = nl2; sm.c_delta[st][c] = dl; sm.c_wt[st][c] = wt; sm.c_wlo[st][c] = wlo;
+          sm.c_lo[st][c] = clo; sm.c_i[st][c] = ci; sm.c_ehi[st][c] = ehi;
+        }
+        mbar_arrive(bar[COL_FULL + st]);
+        if (lane == 0) {
+          mbar_expect_tx(bar[Q_FULL + st], BN * D * 2);
 #pragma unroll
-        for (int c = 0; c < D / 64; ++c)
-          tma_load_3d(smem_u32(sm.dO[st] + c * (BN * 128)), &a.tm_do, bar[DO_FULL + st], c * 64, h, z);
+          for (int c = 0; c < D / 64; ++c)
+            tma_load_3d(smem_u32(sm.q[st] + c * (BN * 128)), &a.tm_q, bar[Q_FULL + st], c * 64, h, (int)(s0 + q0));
+          mbar_expect_tx(bar[DO_FULL + st], BN * D * 2);
+#pragma unroll
+          for (int c = 0; c < D / 64; ++c)
+            tma_load_3d(smem_u32(sm.dO[st] + c * (BN * 128)), &a.tm_do, bar[DO_FULL + st], c * 64, h,
+                        (int)(s0 + q0));
+        }
         issued = u + 1;
       }
-      for (int u = max(0, issued - 2); u < issued; ++u) {
-        mbar_drain(bar[Q_FULL + (u & 1)], (u >> 1) & 1);
-        mbar_drain(bar[DO_FULL + (u & 1)], (u >> 1) & 1);
+      if (lane == 0) {
+        for (int u = max(0, issued - 2); u < issued; ++u) {
+          mbar_drain(bar[Q_FULL + (u & 1)], (u >> 1) & 1);
+          mbar_drain(bar[DO_FULL + (u & 1)], (u >> 1) & 1);
+        }
+        mbar_drain(bar[KV_FULL], 0);
       }
-      mbar_drain(bar[KV_FULL], 0);
     }
-  } else if (warp == 5) {
+  } else if (warp == kMmaWarp) {
+    // ---------------------------------------------------- MMA issuer
     if (lane == 0 && n_tiles > 0) {
       const uint32_t id_s = idesc_f16(kBF16, BM, BN, false, false);
       const uint32_t id_kv = idesc_f16(kBF16, BM, D, false, true);
       const uint32_t k_addr = smem_u32(sm.k), v_addr = smem_u32(sm.v);
       bool ok = mbar_wait(bar[KV_FULL], 0, abort_flag, p.status);
-      auto issue_kv = [&](int up) -> bool {
-        const int st = up & 1;
-        if (!mbar_wait(bar[PDS_FULL + st], (up >> 1) & 1, abort_flag, p.status)) return false;
-        tc_fence_after();
-        const uint32_t pt = smem_u32(sm.pt[st]), dst = smem_u32(sm.dst[st]);
-        const uint32_t qa = smem_u32(sm.q[st]), da = smem_u32(sm.dO[st]);
-        const int nk = tile_n(up) / 16;
-        for (int kk = 0; kk < nk; ++kk) {
-          mma_f16(tdV, sdesc_sw128(pt + kk * 32, 16, 1024), sdesc_sw128(da + kk * 2048, BN * 128, 1024), id_kv,
-                  (up > 0 || kk > 0) ? 1u : 0u);
-          mma_f16(tdK, sdesc_sw128(dst + kk * 32, 16, 1024), sdesc_sw128(qa + kk * 2048, BN * 128, 1024), id_kv,
-                  (up > 0 || kk > 0) ? 1u : 0u);
-        }
-        mma_commit(bar[PDS_EMPTY + st]);
-        mma_commit(bar[QDO_EMPTY + st]);
-        return true;
-      };
-      for (int u = 0; ok && u < n_tiles; ++u) {
+      auto issue_sd = [&](int u) -> bool {
         const int st = u & 1;
-        if (!mbar_wait(bar[Q_FULL + st], (u >> 1) & 1, abort_flag, p.status)) { ok = false; break; }
-        if (!mbar_wait(bar[DO_FULL + st], (u >> 1) & 1, abort_flag, p.status)) { ok = false; break; }
-        if (u >= 2 && !mbar_wait(bar[SD_EMPTY + st], ((u >> 1) - 1) & 1, abort_flag, p.status)) { ok = false; break; }
+        if (!mbar_wait(bar[Q_FULL + st], (u >> 1) & 1, abort_flag, p.status)) return false;
+        if (!mbar_wait(bar[DO_FULL + st], (u >> 1) & 1, abort_flag, p.status)) return false;
+        if (u >= 2 && !mbar_wait(bar[SD_EMPTY + st], ((u >> 1) - 1) & 1, abort_flag, p.status)) return false;
         tc_fence_after();
         const uint32_t qa = smem_u32(sm.q[st]), da = smem_u32(sm.dO[st]);
 #pragma unroll
@@ -542,63 +546,83 @@ __global__ void __launch_bounds__(kThreads, 1) tc_bwd_dkdv_kernel(const __grid_c
           const uint32_t boff = (kk >> 2) * (BN * 128) + (kk & 3) * 32;
           mma_f16(tS + st * BN, sdesc_sw128(k_addr + aoff, 16, 1024), sdesc_sw128(qa + boff, 16, 1024), id_s,
                   kk > 0 ? 1u : 0u);
-        }
-#pragma unroll
-        for (int kk = 0; kk < D / 16; ++kk) {
-          const uint32_t aoff = (kk >> 2) * (BM * 128) + (kk & 3) * 32;
-          const uint32_t boff = (kk >> 2) * (BN * 128) + (kk & 3) * 32;
           mma_f16(tdP + st * BN, sdesc_sw128(v_addr + aoff, 16, 1024), sdesc_sw128(da + boff, 16, 1024), id_s,
                   kk > 0 ? 1u : 0u);
         }
         mma_commit(bar[SD_FULL + st]);
-        if (u >= 1 && !issue_kv(u - 1)) { ok = false; break; }
+        return true;
+      };
+      if (ok) ok = issue_sd(0);
+      if (ok && n_tiles > 1) ok = issue_sd(1);
+      for (int u = 0; ok && u < n_tiles; ++u) {
+        const int st = u & 1;
+        if (!mbar_wait(bar[PDS_FULL + st], (u >> 1) & 1, abort_flag, p.status)) { ok = false; break; }
+        tc_fence_after();
+        const uint32_t pt = smem_u32(sm.pt[st]), dst = smem_u32(sm.dst[st]);
+        const uint32_t qa = smem_u32(sm.q[st]), da = smem_u32(sm.dO[st]);
+#pragma unroll
+        for (int kk = 0; kk < BN / 16; ++kk) {
+          mma_f16(tdV, sdesc_sw128(pt + kk * 32, 16, 1024), sdesc_sw128(da + kk * 2048, BN * 128, 1024), id_kv,
+                  (u > 0 || kk > 0) ? 1u : 0u);
+          mma_f16(tdK, sdesc_sw128(dst + kk * 32, 16, 1024), sdesc_sw128(qa + kk * 2048, BN * 128, 1024), id_kv,
+                  (u > 0 || kk > 0) ? 1u : 0u);
+        }
+        mma_commit(bar[PDS_EMPTY + st]);
+        mma_commit(bar[QDO_EMPTY + st]);
+        if (u + 2 < n_tiles && !issue_sd(u + 2)) { ok = false; break; }
       }
-      if (ok) ok = issue_kv(n_tiles - 1);
       mma_commit(bar[KV_DONE]);
       mma_commit(bar[FINAL]);
       mbar_drain(bar[FINAL], 0);
     }
   } else {
-    // --------------------------------------------------- key rows (Pᵀ, dSᵀ)
-    const int r = tid;
-    const uint32_t lane_addr = ((uint32_t)(warp * 32) << 16);
+    // ---------------------------------------------------- key-row warps (Pᵀ, dSᵀ)
+    const int r = 32 * (warp & 3) + lane;  // key row / TMEM lane
+    const int half = (warp >> 2) & 1;
+    const int c0 = BN / 2 * half;          // this thread's first column of a tile
+    const uint32_t lane_addr = ((uint32_t)(32 * (warp & 3)) << 16);
     const float sl2 = p.scale * kLog2e;
     const bool key_ok = r < nkeys;
-    const int j = LMK ? (key_ok ? p.pos_sorted[lbase + key0 + r] : INT_MAX) : key0 + r;  // key position
+    const int j = LMK ? (key_ok ? __ldg(p.pos_sorted + lbase + key0 + r) : INT_MAX) : key0 + r;
     const float lw2 = (LMK && key_ok) ? __ldg(p.w_sorted + lbase + key0 + r) * kLog2e : 0.f;
     float dlw = 0.f;
     bool ok = true;
-    ColInfo nxt;
     for (int u = 0; u < n_tiles; ++u) {
       const int st = u & 1;
-      ok = mbar_wait(bar[SD_FULL + st], (u >> 1) & 1, abort_flag, p.status);
+      ok = mbar_wait(bar[SD_FULL + st], (u >> 1) & 1, abort_flag, p.status) &&
+           mbar_wait(bar[COL_FULL + st], (u >> 1) & 1, abort_flag, p.status);
       if (!__all_sync(0xffffffffu, ok)) { ok = false; break; }
       tc_fence_after();
-      if (r < BN && u + 1 < n_tiles) nxt = col_info(q_start + BN * (u + 1) + r);  // prefetch next columns
-      const int N = tile_n(u);
-      float sv[BN], dpv[BN];
-#pragma unroll
-      for (int ch = 0; ch < BN / 32; ++ch) {
-        if (ch * 32 < N) {
-          tmem_ld32(tS + lane_addr + st * BN + ch * 32, sv + ch * 32);
-          tmem_ld32(tdP + lane_addr + st * BN + ch * 32, dpv + ch * 32);
-        }
-      }
+      float sv[32], dpv[32];
+      tmem_ld32(tS + lane_addr + st * BN + c0, sv);
+      tmem_ld32(tdP + lane_addr + st * BN + c0, dpv);
       tmem_wait_ld();
       tc_fence_before();
       mbar_arrive(bar[SD_EMPTY + st]);
+      const float* cnl = sm.c_nlse2[st] + c0;
+      const float* cdl = sm.c_delta[st] + c0;
+      const int* cci = sm.c_i[st] + c0;
+      if (LMK) {
+        const float* cwlo = sm.c_wlo[st] + c0;
+        const float jf = (float)j;
 #pragma unroll
-      for (int c = 0; c < BN; ++c) {
-        if (c < N) {
-          const float l2 = sm.c_lse2[st][c];
-          bool valid;
-          if (LMK) valid = key_ok && j <= sm.c_i[st][c] && (float)j < sm.c_wlo[st][c];
-          else valid = key_ok && j >= sm.c_lo[st][c] && j <= sm.c_i[st][c];
-          const float pr = valid ? fast_exp2(fmaf(sv[c], sl2, lw2 - l2)) : 0.f;
-          const float dsv = pr * (dpv[c] - sm.c_delta[st][c]);
-          sv[c] = pr;
-          dpv[c] = dsv;
-          if (LMK) dlw += dsv;
+        for (int c = 0; c < 32; ++c) {
+          const bool valid = key_ok && j <= cci[c] && jf < cwlo[c];
+          const float pr = fast_exp2(fmaf(sv[c], sl2, lw2 + cnl[c]));
+          const float dsv = pr * (dpv[c] - cdl[c]);
+          sv[c] = valid ? pr : 0.f;
+          dpv[c] = valid ? dsv : 0.f;
+          dlw += dpv[c];
+        }
+      } else {
+        const int* clo = sm.c_lo[st] + c0;
+#pragma unroll
+        for (int c = 0; c < 32; ++c) {
+          const bool valid = j >= clo[c] && j <= cci[c];
+          const float pr = fast_exp2(fmaf(sv[c], sl2, cnl[c]));
+          const float dsv = pr * (dpv[c] - cdl[c]);
+          sv[c] = valid ? pr : 0.f;
+          dpv[c] = valid ? dsv : 0.f;
         }
       }
       if (u >= 2) {
@@ -607,39 +631,28 @@ __global__ void __launch_bounds__(kThreads, 1) tc_bwd_dkdv_kernel(const __grid_c
       }
       uint8_t* ptb = sm.pt[st];
       uint8_t* dsb = sm.dst[st];
-#pragma unroll
-      for (int c8 = 0; c8 < BN / 8; ++c8) {
-        if (c8 * 8 < N) {
-          const int c = c8 * 8;
-          uint4 u0, u1;
-          u0.x = pack2(sv[c + 0], sv[c + 1], kBF16); u0.y = pack2(sv[c + 2], sv[c + 3], kBF16);
-          u0.z = pack2(sv[c + 4], sv[c + 5], kBF16); u0.w = pack2(sv[c + 6], sv[c + 7], kBF16);
-          u1.x = pack2(dpv[c + 0], dpv[c + 1], kBF16); u1.y = pack2(dpv[c + 2], dpv[c + 3], kBF16);
-          u1.z = pack2(dpv[c + 4], dpv[c + 5], kBF16); u1.w = pack2(dpv[c + 6], dpv[c + 7], kBF16);
-          *reinterpret_cast<uint4*>(ptb + sw128_offset(r, c)) = u0;
-          *reinterpret_cast<uint4*>(dsb + sw128_offset(r, c)) = u1;
-        }
-      }
-      if (r < BN && u + 1 < n_tiles) store_col(st ^ 1, r, nxt);
-      // all rows written and next columns stored (bounded mbarrier sync of the 128 row threads)
-      mbar_arrive(bar[ROWS_DONE]);
-      ok = mbar_wait(bar[ROWS_DONE], u & 1, abort_flag, p.status);
-      if (!__all_sync(0xffffffffu, ok)) { ok = false; break; }
-      if (!LMK && r < N) {
-        // soft window edge of query column r: its edge keys [lo, ehi] inside this key block
-        const int ehi = sm.c_ehi[st][r];
-        const int jlo = max(sm.c_lo[st][r], key0);
-        const int jhi = min(ehi, key0 + nkeys - 1);
-        const float wt = sm.c_wt[st][r];
-        const int qi = sm.c_i[st][r];
-        for (int jj = jlo; jj <= jhi; ++jj) {
-          const int rr = jj - key0;
-          const float z = (wt - (float)(qi - jj)) * inv_tau;
-          const float sg = 1.0f / (1.0f + expf(-z));
-          T* e1 = reinterpret_cast<T*>(ptb + sw128_offset(rr, r));
-          T* e2 = reinterpret_cast<T*>(dsb + sw128_offset(rr, r));
-          *e1 = from_f32<T>(to_f32<T>(*e1) * sg);
-          *e2 = from_f32<T>(to_f32<T>(*e2) * sg);
+      store_row32<kBF16>(ptb, r, c0, sv);
+      store_row32<kBF16>(dsb, r, c0, dpv);
+      if (!LMK) {
+        // soft window edge, one query column per thread (tid < 64): its edge keys in this block
+        mbar_arrive(bar[ROWS + st]);
+        ok = mbar_wait(bar[ROWS + st], (u >> 1) & 1, abort_flag, p.status);
+        if (!__all_sync(0xffffffffu, ok)) { ok = false; break; }
+        if (tid < BN) {
+          const int col = tid;
+          const int jlo = max(sm.c_lo[st][col], key0);
+          const int jhi = min(sm.c_ehi[st][col], key0 + nkeys - 1);
+          const float wt = sm.c_wt[st][col];
+          const int qi = sm.c_i[st][col];
+          for (int jj = jlo; jj <= jhi; ++jj) {
+            const int rr = jj - key0;
+            const float z = (wt - (float)(qi - jj)) * inv_tau;
+            const float sg = 1.0f / (1.0f + expf(-z));
+            T* e1 = reinterpret_cast<T*>(ptb + sw128_offset(rr, col));
+            T* e2 = reinterpret_cast<T*>(dsb + sw128_offset(rr, col));
+            *e1 = from_f32<T>(to_f32<T>(*e1) * sg);
+            *e2 = from_f32<T>(to_f32<T>(*e2) * sg);
+          }
         }
       }
       fence_async_smem();
@@ -651,47 +664,54 @@ __global__ void __launch_bounds__(kThreads, 1) tc_bwd_dkdv_kernel(const __grid_c
       tc_fence_after();
     }
     const bool have = ok && n_tiles > 0;
+    // this thread stores dK/dV columns [half·D/2, (half+1)·D/2) of key row r
     if (LMK) {
       const int64_t slot = lbase + key0 + r;
       float* dkl = a.dk_lmk + slot * D;
       float* dvl = a.dv_lmk + slot * D;
 #pragma unroll
-      for (int ch = 0; ch < D / 32; ++ch) {
-        float ok_[32], ov[32];
+      for (int ch = 0; ch < D / 64; ++ch) {
+        const int col = half * (D / 2) + ch * 32;
+        float kk_[32], vv[32];
         if (have) {
-          tmem_ld32(tdK + lane_addr + ch * 32, ok_);
-          tmem_ld32(tdV + lane_addr + ch * 32, ov);
+          tmem_ld32(tdK + lane_addr + col, kk_);
+          tmem_ld32(tdV + lane_addr + col, vv);
           tmem_wait_ld();
         } else {
 #pragma unroll
-          for (int e = 0; e < 32; ++e) { ok_[e] = 0.f; ov[e] = 0.f; }
+          for (int e = 0; e < 32; ++e) { kk_[e] = 0.f; vv[e] = 0.f; }
         }
         if (key_ok) {
 #pragma unroll
           for (int e = 0; e < 32; e += 4) {
-            *reinterpret_cast<float4*>(dkl + ch * 32 + e) =
-                make_float4(ok_[e] * p.scale, ok_[e + 1] * p.scale, ok_[e + 2] * p.scale, ok_[e + 3] * p.scale);
-            *reinterpret_cast<float4*>(dvl + ch * 32 + e) = make_float4(ov[e], ov[e + 1], ov[e + 2], ov[e + 3]);
+            *reinterpret_cast<float4*>(dkl + col + e) =
+                make_float4(kk_[e] * p.scale, kk_[e + 1] * p.scale, kk_[e + 2] * p.scale, kk_[e + 3] * p.scale);
+            *reinterpret_cast<float4*>(dvl + col + e) = make_float4(vv[e], vv[e + 1], vv[e + 2], vv[e + 3]);
           }
         }
       }
-      if (key_ok && p.d_lw) {
+      // d_lw of the slot: sum of the two column halves
+      if (half == 1) sm.dlw_half[r] = dlw;
+      mbar_arrive(bar[EPI]);
+      const bool ok2 = mbar_wait(bar[EPI], 0, abort_flag, p.status);
+      if (half == 0 && key_ok && p.d_lw) {
         const int slot_c = __ldg(p.perm + lbase + key0 + r);
-        if (slot_c >= 0) p.d_lw[((int64_t)h * p.S + s) * p.k_lmk + slot_c] = have ? dlw : 0.f;
+        if (slot_c >= 0) p.d_lw[((int64_t)h * p.S + s) * p.k_lmk + slot_c] = (have && ok2) ? dlw + sm.dlw_half[r] : 0.f;
       }
     } else {
       // landmark slots at this key (sorted, duplicates adjacent) add their fp32 rows
-      int c0 = -1;
-      if (key_ok && p.lmk_slot) c0 = __ldg(p.lmk_slot + (s0 + j) * p.H + h);
+      int cl = -1;
+      if (key_ok && p.lmk_slot) cl = __ldg(p.lmk_slot + (s0 + j) * p.H + h);
       const int64_t row_off = (s0 + j) * (int64_t)p.H * D + (int64_t)h * D;
       T* dko = reinterpret_cast<T*>(p.dk) + row_off;
       T* dvo = reinterpret_cast<T*>(p.dv) + row_off;
 #pragma unroll
-      for (int ch = 0; ch < D / 32; ++ch) {
+      for (int ch = 0; ch < D / 64; ++ch) {
+        const int col = half * (D / 2) + ch * 32;
         float kk_[32], vv[32];
         if (have) {
-          tmem_ld32(tdK + lane_addr + ch * 32, kk_);
-          tmem_ld32(tdV + lane_addr + ch * 32, vv);
+          tmem_ld32(tdK + lane_addr + col, kk_);
+          tmem_ld32(tdV + lane_addr + col, vv);
           tmem_wait_ld();
         } else {
 #pragma unroll
@@ -700,9 +720,9 @@ __global__ void __launch_bounds__(kThreads, 1) tc_bwd_dkdv_kernel(const __grid_c
         if (key_ok) {
 #pragma unroll
           for (int e = 0; e < 32; ++e) kk_[e] *= p.scale;
-          for (int c = c0; c >= 0 && c < p.kp && __ldg(p.pos_sorted + lbase + c) == j; ++c) {
-            const float* lk = a.dk_lmk + (lbase + c) * D + ch * 32;
-            const float* lv = a.dv_lmk + (lbase + c) * D + ch * 32;
+          for (int c = cl; c >= 0 && c < p.kp && __ldg(p.pos_sorted + lbase + c) == j; ++c) {
+            const float* lk = a.dk_lmk + (lbase + c) * D + col;
+            const float* lv = a.dv_lmk + (lbase + c) * D + col;
 #pragma unroll
             for (int e = 0; e < 32; ++e) { kk_[e] += __ldg(lk + e); vv[e] += __ldg(lv + e); }
           }
@@ -713,8 +733,8 @@ __global__ void __launch_bounds__(kThreads, 1) tc_bwd_dkdv_kernel(const __grid_c
             u0.z = pack2(kk_[e + 4], kk_[e + 5], kBF16); u0.w = pack2(kk_[e + 6], kk_[e + 7], kBF16);
             u1.x = pack2(vv[e], vv[e + 1], kBF16); u1.y = pack2(vv[e + 2], vv[e + 3], kBF16);
             u1.z = pack2(vv[e + 4], vv[e + 5], kBF16); u1.w = pack2(vv[e + 6], vv[e + 7], kBF16);
-            *reinterpret_cast<uint4*>(dko + ch * 32 + e) = u0;
-            *reinterpret_cast<uint4*>(dvo + ch * 32 + e) = u1;
+            *reinterpret_cast<uint4*>(dko + col + e) = u0;
+            *reinterpret_cast<uint4*>(dvo + col + e) = u1;
           }
         }
       }
@@ -723,20 +743,14 @@ __global__ void __launch_bounds__(kThreads, 1) tc_bwd_dkdv_kernel(const __grid_c
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
-  if (warp == 5) tmem_dealloc(tmem, 512);
+  if (warp == kMmaWarp) tmem_dealloc(tmem, 512);
 }
 }  // namespace dkv
 
 // ---------------------------------------------------------------- host side
 CUresult encode_3d(CUtensorMap* m, CUtensorMapDataType dt, const void* base, uint64_t d0, uint64_t d1, uint64_t d2,
                    uint64_t stride1_bytes, uint64_t stride2_bytes, uint32_t box0, uint32_t box1, uint32_t box2) {
-  cuuint64_t dims[3] = {d0, d1, d2};
-  cuuint64_t strides[2] = {stride1_bytes, stride2_bytes};
-  cuuint32_t box[3] = {box0, box1, box2};
-  cuuint32_t es[3] = {1, 1, 1};
-  return cuTensorMapEncodeTiled(m, dt, 3, const_cast<void*>(base), dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                                CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                                CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return encode_tensor_map_3d(m, dt, base, d0, d1, d2, stride1_bytes, stride2_bytes, box0, box1, box2);
 }
 
 // q/do boxes: rows_q; k/v boxes: rows_k; landmark boxes: min(kp, rows_l)

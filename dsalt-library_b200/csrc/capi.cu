@@ -1,6 +1,33 @@
 // extern "C" entry points of libdsalt_b200.so: argument checks, then launches.
 // No entry point allocates device memory; every buffer belongs to the caller.
+#include <cudaTypedefs.h>
+#include <mutex>
+
 #include "common.cuh"
+#include "sm100.cuh"
+
+namespace dsalt {
+CUresult encode_tensor_map_3d(CUtensorMap* m, CUtensorMapDataType dt, const void* base, uint64_t d0, uint64_t d1,
+                              uint64_t d2, uint64_t stride1_bytes, uint64_t stride2_bytes, uint32_t box0,
+                              uint32_t box1, uint32_t box2) {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
+  });
+  if (!fn) return CUDA_ERROR_NOT_FOUND;
+  cuuint64_t dims[3] = {d0, d1, d2};
+  cuuint64_t strides[2] = {stride1_bytes, stride2_bytes};
+  cuuint32_t box[3] = {box0, box1, box2};
+  cuuint32_t es[3] = {1, 1, 1};
+  return fn(m, dt, 3, const_cast<void*>(base), dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
+            CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+}
+}  // namespace dsalt
 
 namespace dsalt {
 cudaError_t launch_schedule(const DsaltScheduleParams& p, cudaStream_t st);
@@ -31,7 +58,7 @@ static bool aligned16(const void* p) { return ((uintptr_t)p & 15u) == 0; }
 static int check_attn(const DsaltAttnParams* p, int stage) {
   if (!p) return DSALT_ERR_ARG;
   if (p->dtype != DSALT_F16 && p->dtype != DSALT_BF16 && p->dtype != DSALT_F32) return DSALT_ERR_DTYPE;
-  if (p->D != 32 && p->D != 64 && p->D != 128 && p->D != 256) return DSALT_ERR_HEAD_DIM;
+  if (p->D <= 0 || p->D > 256 || p->D % 8 != 0) return DSALT_ERR_HEAD_DIM;
   if (p->T < 0 || p->H <= 0 || p->S < 0 || p->k_lmk < 0 || p->kp < p->k_lmk) return DSALT_ERR_ARG;
   if (p->semantics != DSALT_TRAIN && p->semantics != DSALT_INFER) return DSALT_ERR_ARG;
   if (!(p->tau_win > 0.f)) return DSALT_ERR_ARG;
@@ -75,7 +102,7 @@ const char* dsalt_b200_status_string(int status) {
     case DSALT_OK: return "ok";
     case DSALT_ERR_ARG: return "invalid argument";
     case DSALT_ERR_DTYPE: return "unsupported dtype for this kernel family";
-    case DSALT_ERR_HEAD_DIM: return "unsupported head_dim (32, 64, 128, 256)";
+    case DSALT_ERR_HEAD_DIM: return "unsupported head_dim (multiples of 8 up to 256)";
     case DSALT_ERR_LAUNCH: return "CUDA launch or API error";
     case DSALT_ERR_NO_DEVICE: return "no usable sm_100 device";
     case DSALT_ERR_ALIGN: return "pointer not 16-byte aligned";

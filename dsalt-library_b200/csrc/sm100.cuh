@@ -191,4 +191,12 @@ __device__ __forceinline__ float fast_exp2(float x) {
 }
 
 }  // namespace sm100
+
+// Host: cuTensorMapEncodeTiled for a 3-D, 128-byte-swizzled, 2-byte-element
+// tensor map.  The driver function is resolved at run time through the CUDA
+// runtime (so the library itself does not link libcuda and loads on machines
+// without a driver).
+CUresult encode_tensor_map_3d(CUtensorMap* m, CUtensorMapDataType dt, const void* base, uint64_t d0, uint64_t d1,
+                              uint64_t d2, uint64_t stride1_bytes, uint64_t stride2_bytes, uint32_t box0,
+                              uint32_t box1, uint32_t box2);
 }  // namespace dsalt

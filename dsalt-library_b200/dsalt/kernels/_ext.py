@@ -51,7 +51,7 @@ class AttnParams(ctypes.Structure):
                 ("pos_sorted", _c_void_p), ("w_sorted", _c_void_p), ("perm", _c_void_p),
                 ("lmk_slot", _c_void_p),
                 ("o", _c_void_p), ("o_f32", _c_void_p), ("lse", _c_void_p),
-                ("dout", _c_void_p), ("delta", _c_void_p), ("dq", _c_void_p), ("dk", _c_void_p),
+                ("dout", _c_void_p), ("dout_f32", _c_void_p), ("delta", _c_void_p), ("dq", _c_void_p), ("dk", _c_void_p),
                 ("dv", _c_void_p), ("dw_head", _c_void_p), ("dw", _c_void_p), ("d_lw", _c_void_p),
                 ("lmk_grad", _c_void_p), ("status", _c_void_p),
                 ("T", _i64), ("H", _i32), ("D", _i32), ("S", _i32), ("k_lmk", _i32), ("kp", _i32),

@@ -156,10 +156,19 @@ def forward(q_c, k_c, v_c, prep: Prepared, tau_win: float, win_edge: float, impl
     return o, (o_f32 if o_f32 is not None else o), lse
 
 
-def backward(do_c, q_c, k_c, v_c, o, lse, prep: Prepared, tau_win: float, win_edge: float,
+def backward(grad_out, q_c, k_c, v_c, o, lse, prep: Prepared, tau_win: float, win_edge: float,
              impl: int, want_dw: bool):
-    """Run the backward stages; returns ``(dq, dk, dv, d_lw [H,S,k] fp32, dw [T] or None)``."""
+    """Run the backward stages; returns ``(dq, dk, dv, d_lw [H,S,k] fp32, dw [T] or None)``.
+
+    ``grad_out`` may be fp32 (the op's output dtype) or the input dtype; an fp32
+    gradient is rounded to the input dtype by the preprocess kernel itself.
+    """
     dev = q_c.device
+    grad_out = grad_out.contiguous()
+    if grad_out.dtype == torch.float32 and q_c.dtype != torch.float32:
+        do_f32, do_c = grad_out, torch.empty_like(q_c)
+    else:
+        do_f32, do_c = None, grad_out.to(q_c.dtype)
     T, H = prep.T, prep.H
     delta = torch.empty(T, H, dtype=torch.float32, device=dev)
     dq = torch.empty_like(q_c)
@@ -170,7 +179,7 @@ def backward(do_c, q_c, k_c, v_c, o, lse, prep: Prepared, tau_win: float, win_ed
     dw = torch.empty(T, dtype=q_c.dtype, device=dev) if want_dw else None
     lmk_grad = torch.empty(2, H, prep.S, prep.kp, prep.D, dtype=torch.float32, device=dev) \
         if prep.kp > 0 else None
-    p = _params(prep, q_c, k_c, v_c, tau_win, win_edge, impl, o=o, lse=lse, dout=do_c,
+    p = _params(prep, q_c, k_c, v_c, tau_win, win_edge, impl, o=o, lse=lse, dout=do_c, dout_f32=do_f32,
                 delta=delta, dq=dq, dk=dk, dv=dv, dw_head=dw_head, dw=dw, d_lw=d_lw, lmk_grad=lmk_grad)
     _ext.call("dsalt_attn_bwd_preprocess", p)
     _ext.call("dsalt_attn_bwd_dkdv", p)
@@ -192,7 +201,7 @@ def check_inputs(q, k, v, cu_seqlens):
             raise ValueError(f"{name} must be [T, H, D], got {tuple(t.shape)}")
     if k.shape != q.shape or v.shape != q.shape:
         raise ValueError(f"q/k/v shapes differ: {tuple(q.shape)} {tuple(k.shape)} {tuple(v.shape)}")
-    if q.shape[2] not in (32, 64, 128, 256):
-        raise ValueError(f"head_dim {q.shape[2]} not supported (32, 64, 128, 256)")
+    if q.shape[2] % 8 != 0 or not 8 <= q.shape[2] <= 256:
+        raise ValueError(f"head_dim {q.shape[2]} not supported (multiples of 8 up to 256)")
     if cu_seqlens.dim() != 1 or cu_seqlens.shape[0] < 1:
         raise ValueError("cu_seqlens must be a 1-D tensor [S+1]")

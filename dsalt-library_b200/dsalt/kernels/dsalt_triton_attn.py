@@ -51,8 +51,7 @@ class DSALTAttentionFunction(torch.autograd.Function):
     @staticmethod
     def backward(ctx, grad_out):
         q_c, k_c, v_c, o, lse = ctx.saved_tensors
-        do_c = grad_out.contiguous().to(q_c.dtype)
-        dq, dk, dv, d_bias, _ = _cuda.backward(do_c, q_c, k_c, v_c, o, lse, ctx.prep, 1.0, 0.0,
+        dq, dk, dv, d_bias, _ = _cuda.backward(grad_out, q_c, k_c, v_c, o, lse, ctx.prep, 1.0, 0.0,
                                                ctx.impl, want_dw=False)
         od = ctx.out_dtype
         return dq.to(od), dk.to(od), dv.to(od), None, d_bias.to(od), None, None

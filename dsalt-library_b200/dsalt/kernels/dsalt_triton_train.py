@@ -78,8 +78,7 @@ class DSALTTrainFunction(torch.autograd.Function):
     @staticmethod
     def backward(ctx, grad_out):
         q_c, k_c, v_c, o, lse = ctx.saved_tensors
-        do_c = grad_out.contiguous().to(q_c.dtype)
-        dq, dk, dv, d_lw, dw = _cuda.backward(do_c, q_c, k_c, v_c, o, lse, ctx.prep, ctx.tau_win,
+        dq, dk, dv, d_lw, dw = _cuda.backward(grad_out, q_c, k_c, v_c, o, lse, ctx.prep, ctx.tau_win,
                                               ctx.win_edge, ctx.impl, want_dw=True)
         od = ctx.out_dtype
         return (dq.to(od), dk.to(od), dv.to(od),

@@ -138,7 +138,9 @@ typedef struct DsaltAttnParams {
   float* o_f32;               /* [T,H,D] fp32 copy of bf16/f16-rounded O, or NULL */
   float* lse;                 /* [T,H] natural-log LSE, -inf for empty rows */
   /* backward */
-  const void* dout;           /* [T,H,D] dtype */
+  const void* dout;           /* [T,H,D] dtype (written by the preprocess stage when
+                                 dout_f32 is given) */
+  const float* dout_f32;      /* [T,H,D] fp32 upstream gradient, or NULL */
   float* delta;               /* [T,H] scratch */
   void* dq; void* dk; void* dv;       /* [T,H,D] dtype */
   float* dw_head;             /* [T,H] scratch (train) */

@@ -57,7 +57,7 @@ def test_argument_errors_without_launch():
     from dsalt.kernels import _ext
     import ctypes
     lib = _ext.load()
-    p = _ext.AttnParams(T=16, H=1, D=48, S=1, k_lmk=0, kp=0, tau_win=1.0, dtype=_ext.BF16)
+    p = _ext.AttnParams(T=16, H=1, D=12, S=1, k_lmk=0, kp=0, tau_win=1.0, dtype=_ext.BF16)
     assert lib.dsalt_attn_fwd(ctypes.byref(p), None) == 3  # head_dim
     p.D = 64
     p.dtype = 7

@@ -77,6 +77,7 @@ def make_workload(wl, seed, device):
     T, H, D, k = sum(lens), wl["H"], wl["D"], wl["k"]
     g = torch.Generator(device=device).manual_seed(seed)
     q, kk, v, do = (torch.randn(T, H, D, generator=g, device=device).to(torch.bfloat16) for _ in range(4))
+    do = do.float()  # the op returns fp32, so its upstream gradient arrives in fp32
     gate = torch.randn(T, generator=g, device=device)
     w = wl["n_min"] + torch.sigmoid(gate) * (wl["n_max"] - wl["n_min"])
     scores = torch.randn(T, H, generator=g, device=device)
@@ -295,6 +296,7 @@ def main():
     if not args.no_e2e:
         host = {kk: d[kk].detach().cpu().pin_memory() for kk in ("q", "k", "v", "do", "w", "lmk_logw", "lmk_pos")}
         outs = [torch.empty(d["q"].shape, dtype=torch.bfloat16).pin_memory() for _ in range(3)]
+        host["do"] = d["do"].to(torch.bfloat16).cpu().pin_memory()  # shipped as bf16, widened on device
         dwh = torch.empty(d["T"], dtype=torch.float32).pin_memory()
         dlh = torch.empty(d["lmk_logw"].shape, dtype=torch.float32).pin_memory()
         h2d = sum(x.numel() * x.element_size() for x in host.values())
@@ -308,7 +310,7 @@ def main():
             w = host["w"].to(dev, non_blocking=True).requires_grad_(True)
             lw = host["lmk_logw"].to(dev, non_blocking=True).requires_grad_(True)
             pos = host["lmk_pos"].to(dev, non_blocking=True)
-            do = host["do"].to(dev, non_blocking=True)
+            do = host["do"].to(dev, non_blocking=True).float()
             o = dsalt_triton_train_attention(q, k, v, pos, lw, w, d["cu"], 1.0, 4.0, d["n_max"], d["cu_list"])
             gq, gk, gv, gw, glw = torch.autograd.grad(o, (q, k, v, w, lw), do)
             outs[0].copy_(gq, non_blocking=True)
@@ -346,7 +348,7 @@ def main():
                 "config": {"workload": wl["desc"], "global_batch": len(d["lens"]) * world,
                            "seq_len": max(d["lens"]), "tokens_per_gpu": d["T"],
                            "parallelism": f"dp{world} (batch x heads shards, no collective)",
-                           "l2": "inputs larger than L2 (q,k,v,dO = 256 MiB per step), no flush"},
+                           "l2": "inputs larger than L2 (q,k,v bf16 + dO fp32 = 320 MiB per step), no flush"},
                 "roofline": roof,
                 "kernels_ms": {n: round(v[0], 4) for n, v in kern.items()},
                 "attended_pairs_per_gpu": pairs,

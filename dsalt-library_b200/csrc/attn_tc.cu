@@ -2,16 +2,23 @@
 //
 // One CTA computes 128 query rows of one (sequence, head): the rows' landmark
 // tile(s) and their band of keys [min_i(i − W_i), max_i i], in 128-key tiles.
+// 320 threads:
+//   warps 0-7   softmax: TMEM lane r = 32·(warp % 4) + lane is query row r;
+//               warps 0-3 own key columns 0-63 of every tile, warps 4-7 columns
+//               64-127.  Each half keeps its own running max / sum and its own
+//               O accumulator in TMEM, so the two halves of a row exchange
+//               nothing until the epilogue merges them.  Online softmax in the
+//               exp2 domain with a lazy rescale (the running max only moves when
+//               it grows by more than 2^8); P (bf16/fp16) goes to a 128B-swizzled
+//               K-major smem tile (chunk h = half h), where each thread applies
+//               the soft window edge to its ≤ ceil(win_edge)+1 edge keys in place.
+//   warp 8      TMA producers: lane 0 loads Q and the K tiles (a K stage frees
+//               when its S is done), lane 1 the V tiles (freed by P·V).
+//   warp 9      TMEM allocator + single-thread tcgen05.mma issuer:
+//               S[t%2] = Q·K_tᵀ two tiles ahead; O_h += P_t,h·V_t,h for each half
+//               h as soon as that half's P is written.
 //
-//   warp 4      TMA producer: Q once, then K/V tiles into a 2-stage ring
-//   warp 5      TMEM allocator + single-thread tcgen05.mma issuer:
-//                 S[t%2] = Q·K_tᵀ (TMEM, fp32), then O += P_{t−1}·V_{t−1} (TMEM)
-//   warps 0-3   softmax: thread r owns query row r (TMEM lane r): masks its row,
-//               online softmax in the exp2 domain with a lazy rescale (the
-//               running max only moves when it grows by more than 2^8), writes
-//               P (bf16/fp16, 128B-swizzled K-major) to shared memory, applies
-//               the soft window edge to its ≤ ceil(win_edge)+1 edge keys in place,
-//               and finally normalises O and writes O, O(fp32) and LSE.
+// TMEM (512 columns): S double buffer [0, 256), O_0 [256, 256 + D), O_1 after it.
 //
 // Semantics follow the reference's _train_fwd_kernel
 // (dsalt/kernels/dsalt_triton_train.py:116-214): band 0 ≤ d ≤ w̃, edge bias
@@ -33,15 +40,19 @@ namespace {
 
 constexpr int BM = 128;              // query rows per CTA
 constexpr int BN = 128;              // keys per tile
+constexpr int HALF = BN / 2;         // key columns per softmax thread
 constexpr int kMaxLmk = 512;         // landmark slots held in shared memory
-constexpr int kThreads = 192;
+constexpr int kThreads = 320;
+constexpr int kRowThreads = 256;
+constexpr int kProducerWarp = 8;
+constexpr int kMmaWarp = 9;
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr float kLn2 = 0.6931471805599453f;
 constexpr float kRescaleThreshold = 8.0f;  // log2 units
 
 enum Bar {
   Q_FULL = 0, K_FULL = 1, V_FULL = 3, K_EMPTY = 5, V_EMPTY = 7, S_FULL = 9, S_EMPTY = 11, P_FULL = 13,
-  O_DONE = 14, FINAL = 15, NUM_BARS = 16
+  O_DONE = 15, FINAL = 17, EPI = 18, NUM_BARS = 19
 };
 
 template <int D>
@@ -49,11 +60,13 @@ struct alignas(1024) FwdSmem {
   uint8_t q[BM * D * 2];
   uint8_t k[2][BN * D * 2];
   uint8_t v[2][BN * D * 2];
-  uint8_t p[BM * BN * 2];
+  uint8_t p[BM * BN * 2];       // chunk h (64 keys) is written by softmax half h
   uint64_t bars[NUM_BARS];
   uint32_t tmem_base;
   int abort_flag;
   int band_lo, band_hi, cnt_max, n_valid;
+  float m_half[2][BM];          // epilogue: per-half running max (log2) and sum
+  float l_half[2][BM];
   int lmk_pos[kMaxLmk];
   float lmk_lw2[kMaxLmk];
 };
@@ -85,7 +98,7 @@ __global__ void __launch_bounds__(kThreads, 1) tc_fwd_kernel(const __grid_consta
   const int tid = threadIdx.x;
   const int warp = tid >> 5;
   const int lane = tid & 31;
-  constexpr bool kBF16 = sizeof(T) == 2 && !std::is_same<T, __half>::value;
+  constexpr bool kBF16 = !std::is_same<T, __half>::value;
   const BarArray bar{smem_u32(&sm.bars[0])};
 
   if (tid == 0) {
@@ -96,11 +109,12 @@ __global__ void __launch_bounds__(kThreads, 1) tc_fwd_kernel(const __grid_consta
       mbar_init(bar[K_EMPTY + st], 1);
       mbar_init(bar[V_EMPTY + st], 1);
       mbar_init(bar[S_FULL + st], 1);
-      mbar_init(bar[S_EMPTY + st], BM);
+      mbar_init(bar[S_EMPTY + st], kRowThreads);
+      mbar_init(bar[P_FULL + st], kRowThreads / 2);  // index = softmax half
+      mbar_init(bar[O_DONE + st], 1);                // index = softmax half
     }
-    mbar_init(bar[P_FULL], BM);
-    mbar_init(bar[O_DONE], 1);
     mbar_init(bar[FINAL], 1);
+    mbar_init(bar[EPI], kRowThreads);
     fence_mbar_init();
     sm.abort_flag = 0;
     sm.band_lo = INT_MAX;
@@ -108,12 +122,12 @@ __global__ void __launch_bounds__(kThreads, 1) tc_fwd_kernel(const __grid_consta
     sm.cnt_max = 0;
     sm.n_valid = 0;
   }
-  if (warp == 4 && lane == 0) {
+  if (warp == kProducerWarp && lane == 0) {
     prefetch_tmap(&a.tm_q);
     prefetch_tmap(&a.tm_k);
     prefetch_tmap(&a.tm_v);
   }
-  if (warp == 5) tmem_alloc(smem_u32(&sm.tmem_base), 512);
+  if (warp == kMmaWarp) tmem_alloc(smem_u32(&sm.tmem_base), 512);
   const int kp = p.kp;
   const int64_t lbase = ((int64_t)h * p.S + s) * kp;
   for (int c = tid; c < kp; c += kThreads) {
@@ -124,9 +138,11 @@ __global__ void __launch_bounds__(kThreads, 1) tc_fwd_kernel(const __grid_consta
   }
   __syncthreads();
 
-  // ---- per-row window (threads 0..127 own rows m0 + tid)
-  const int i = m0 + tid;
-  const bool row_ok = tid < BM && i < L;
+  // ---- per-row window: row r = 32·(warp % 4) + lane, key-column half = warp / 4
+  const int r = 32 * (warp & 3) + lane;
+  const int half = (warp >> 2) & 1;
+  const int i = m0 + r;
+  const bool row_ok = warp < 8 && i < L;
   RowWindow rw = {};
   int lo = INT_MAX, hi = -1, cnt = 0;
   if (row_ok) {
@@ -143,11 +159,13 @@ __global__ void __launch_bounds__(kThreads, 1) tc_fwd_kernel(const __grid_consta
       if (ps <= i && (float)ps < rw.win_lo) a0 = mid + 1; else a1 = mid;
     }
     cnt = a0;
-    if (lo <= hi) {
-      atomicMin(&sm.band_lo, lo);
-      atomicMax(&sm.band_hi, hi);
+    if (half == 0) {
+      if (lo <= hi) {
+        atomicMin(&sm.band_lo, lo);
+        atomicMax(&sm.band_hi, hi);
+      }
+      if (cnt > 0) atomicMax(&sm.cnt_max, cnt);
     }
-    if (cnt > 0) atomicMax(&sm.cnt_max, cnt);
   }
   tc_fence_before();
   __syncthreads();
@@ -165,12 +183,10 @@ __global__ void __launch_bounds__(kThreads, 1) tc_fwd_kernel(const __grid_consta
     return round16(min(BN, band_hi - (band_lo + BN * (t - n_lt)) + 1));
   };
   const uint32_t tS = tmem;            // S buffers: columns [0,128) and [128,256)
-  const uint32_t tO = tmem + 2 * BN;   // O: columns [256, 256 + D)
+  const uint32_t tO = tmem + 2 * BN;   // O_h: columns [256 + h·D, 256 + (h+1)·D)
 
-  if (warp == 4) {
+  if (warp == kProducerWarp) {
     // ------------------------------------------------------------ producers
-    // lane 0: Q, then K tiles (a K stage frees as soon as its S = Q·Kᵀ is done);
-    // lane 1: V tiles (a V stage frees when its P·V is done).
     if (lane < 2 && n_tiles > 0) {
       const bool is_k = lane == 0;
       if (is_k) {
@@ -200,9 +216,11 @@ __global__ void __launch_bounds__(kThreads, 1) tc_fwd_kernel(const __grid_consta
       for (int t = max(0, issued - 2); t < issued; ++t) mbar_drain(bar[FULL + (t & 1)], (t >> 1) & 1);
       if (is_k) mbar_drain(bar[Q_FULL], 0);
     }
-  } else if (warp == 5) {
+  } else if (warp == kMmaWarp) {
     // ------------------------------------------------------------ MMA issuer
-    // order: S_0, S_1, then for every t: P_t·V_t as soon as P_t is ready, then S_{t+2}
+    // order: S_0, S_1, then for every t: P_t,0·V_t,0, P_t,1·V_t,1 (each as soon as
+    // that half of P is written), then S_{t+2}.  O_DONE[h] is committed once per
+    // tile and half, also when the half had no valid key (its P·V is skipped).
     if (lane == 0 && n_tiles > 0) {
       const uint32_t id_o = idesc_f16(kBF16, BM, D, false, true);
       const uint32_t q_addr = smem_u32(sm.q);
@@ -226,21 +244,29 @@ __global__ void __launch_bounds__(kThreads, 1) tc_fwd_kernel(const __grid_consta
         mma_commit(bar[K_EMPTY + st]);
         return true;
       };
+      bool o_written0 = false, o_written1 = false;
       if (ok) ok = issue_s(0);
       if (ok && n_tiles > 1) ok = issue_s(1);
       for (int t = 0; ok && t < n_tiles; ++t) {
         const int st = t & 1;
-        if (!mbar_wait(bar[P_FULL], t & 1, abort_flag, p.status)) { ok = false; break; }
+        const int nvalid = tile_n(t);
         if (!mbar_wait(bar[V_FULL + st], (t >> 1) & 1, abort_flag, p.status)) { ok = false; break; }
-        tc_fence_after();
         const uint32_t v_addr = smem_u32(sm.v[st]);
-        const int nk = tile_n(t) / 16;
-        for (int kk = 0; kk < nk; ++kk) {
-          const uint64_t ad = sdesc_sw128(p_addr + (kk >> 2) * (BM * 128) + (kk & 3) * 32, 16, 1024);
-          const uint64_t bd = sdesc_sw128(v_addr + kk * 2048, BN * 128, 1024);
-          mma_f16(tO, ad, bd, id_o, (t > 0 || kk > 0) ? 1u : 0u);
+#pragma unroll
+        for (int hh = 0; hh < 2; ++hh) {
+          if (!mbar_wait(bar[P_FULL + hh], t & 1, abort_flag, p.status)) { ok = false; break; }
+          tc_fence_after();
+          const int nk = min(max(nvalid - HALF * hh, 0), HALF) / 16;  // valid 16-key steps of this half
+          bool& written = hh == 0 ? o_written0 : o_written1;
+          for (int kk = 0; kk < nk; ++kk) {
+            const uint64_t ad = sdesc_sw128(p_addr + hh * (BM * 128) + kk * 32, 16, 1024);
+            const uint64_t bd = sdesc_sw128(v_addr + (HALF / 16 * hh + kk) * 2048, BN * 128, 1024);
+            mma_f16(tO + hh * D, ad, bd, id_o, (written || kk > 0) ? 1u : 0u);
+          }
+          if (nk > 0) written = true;
+          mma_commit(bar[O_DONE + hh]);
         }
-        mma_commit(bar[O_DONE]);
+        if (!ok) break;
         mma_commit(bar[V_EMPTY + st]);
         if (t + 2 < n_tiles && !issue_s(t + 2)) { ok = false; break; }
       }
@@ -249,27 +275,27 @@ __global__ void __launch_bounds__(kThreads, 1) tc_fwd_kernel(const __grid_consta
       mbar_drain(bar[FINAL], 0);
     }
   } else {
-    // ------------------------------------------------------------ softmax (rows)
-    const int r = tid;
-    const uint32_t lane_addr = ((uint32_t)(warp * 32) << 16);
+    // ------------------------------------------------------------ softmax (row halves)
+    const uint32_t lane_addr = ((uint32_t)(32 * (warp & 3)) << 16);
+    const int c0 = HALF * half;          // first tile column owned by this thread
+    const uint32_t tOh = tO + half * D;  // this half's O accumulator
     const float sl2 = p.scale * kLog2e;
     const float inv_tau = 1.0f / p.tau_win;
     // edge keys of this row: d in [d_e0, min(W, i)] (soft-edge bias), empty when d_e0 > W
     int d_e0 = INT_MAX;
     if (row_ok && rw.W >= 0) d_e0 = max((int)floorf(rw.core) + 1, 0);
-    float m = -INFINITY, l = 0.f;
+    float m = -INFINITY, l = 0.f;  // this half's running max (log2 units) and sum
     bool ok = true;
-    uint8_t* sp = sm.p;
+    uint8_t* sp = sm.p + half * (BM * 128);  // this half's P chunk: 128 rows x 64 keys
     for (int t = 0; t < n_tiles; ++t) {
       const int st = t & 1;
       ok = mbar_wait(bar[S_FULL + st], (t >> 1) & 1, abort_flag, p.status);
       if (!__all_sync(0xffffffffu, ok)) { ok = false; break; }
       tc_fence_after();
-      const int N = tile_n(t);
-      // all 128 columns are read: columns past N hold stale values and are masked below
-      float x[BN];
-#pragma unroll
-      for (int ch = 0; ch < BN / 32; ++ch) tmem_ld32(tS + lane_addr + st * BN + ch * 32, x + ch * 32);
+      // columns past the tile's valid keys hold stale values and are masked below
+      float x[HALF];
+      tmem_ld32(tS + lane_addr + st * BN + c0, x);
+      tmem_ld32(tS + lane_addr + st * BN + c0 + 32, x + 32);
       tmem_wait_ld();
       tc_fence_before();
       mbar_arrive(bar[S_EMPTY + st]);
@@ -281,19 +307,19 @@ __global__ void __launch_bounds__(kThreads, 1) tc_fwd_kernel(const __grid_consta
 #pragma unroll
       for (int g = 0; g < 8; ++g) mx[g] = -INFINITY;
       if (lmk) {
-        const int climit = cnt - BN * t;
-        const float* lw2 = sm.lmk_lw2 + BN * t;
+        const int climit = cnt - BN * t - c0;
+        const float* lw2 = sm.lmk_lw2 + BN * t + c0;
 #pragma unroll
-        for (int c = 0; c < BN; ++c) {
+        for (int c = 0; c < HALF; ++c) {
           x[c] = (c < climit) ? fmaf(x[c], sl2, lw2[c]) : -INFINITY;
           mx[c & 7] = fmaxf(mx[c & 7], x[c]);
         }
         xs = 1.0f;
       } else {
         n0 = band_lo + BN * (t - n_lt);
-        const int clo = lo - n0, chi = hi - n0;
+        const int clo = lo - n0 - c0, chi = hi - n0 - c0;
 #pragma unroll
-        for (int c = 0; c < BN; ++c) {
+        for (int c = 0; c < HALF; ++c) {
           x[c] = (c >= clo && c <= chi) ? x[c] : -INFINITY;
           mx[c & 7] = fmaxf(mx[c & 7], x[c]);
         }
@@ -316,49 +342,36 @@ __global__ void __launch_bounds__(kThreads, 1) tc_fwd_kernel(const __grid_consta
 #pragma unroll
       for (int g = 0; g < 8; ++g) sm8[g] = 0.f;
 #pragma unroll
-      for (int c = 0; c < BN; ++c) {
+      for (int c = 0; c < HALF; ++c) {
         x[c] = fast_exp2(fmaf(x[c], xs, -ms));
         sm8[c & 7] += x[c];
       }
       const float sum = ((sm8[0] + sm8[1]) + (sm8[2] + sm8[3])) + ((sm8[4] + sm8[5]) + (sm8[6] + sm8[7]));
       l = l * factor + sum;
 
-      // P buffer and O are free once the previous P·V has completed
+      // this half's P chunk and O_h are free once its previous P·V has completed
       if (t >= 1) {
-        ok = mbar_wait(bar[O_DONE], (t - 1) & 1, abort_flag, p.status);
+        ok = mbar_wait(bar[O_DONE + half], (t - 1) & 1, abort_flag, p.status);
         if (!__all_sync(0xffffffffu, ok)) { ok = false; break; }
         tc_fence_after();
       }
-      if (__any_sync(0xffffffffu, rescale && t >= 1)) {
 #pragma unroll
-        for (int ch = 0; ch < D / 32; ++ch) {
-          float o[32];
-          tmem_ld32(tO + lane_addr + ch * 32, o);
-          tmem_wait_ld();
-          const float f = (rescale && t >= 1) ? factor : 1.0f;
-#pragma unroll
-          for (int j = 0; j < 32; ++j) o[j] *= f;
-          tmem_st32(tO + lane_addr + ch * 32, o);
-        }
-        tmem_wait_st();
-      }
-#pragma unroll
-      for (int c8 = 0; c8 < BN / 8; ++c8) {
+      for (int c8 = 0; c8 < HALF / 8; ++c8) {
         const int c = c8 * 8;
         uint4 u;
         u.x = pack2(x[c + 0], x[c + 1], kBF16);
         u.y = pack2(x[c + 2], x[c + 3], kBF16);
         u.z = pack2(x[c + 4], x[c + 5], kBF16);
         u.w = pack2(x[c + 6], x[c + 7], kBF16);
-        *reinterpret_cast<uint4*>(sp + (c >> 6) * (BM * 128) + sw128_offset(r, c & 63)) = u;
+        *reinterpret_cast<uint4*>(sp + sw128_offset(r, c)) = u;
       }
       if (!lmk && row_ok && d_e0 <= rw.W) {
-        // soft window edge on this row's edge keys inside the tile: p *= σ((w̃ − d)/τ)
-        const int d_hi = min(min(rw.W, i), i - n0);
-        const int d_lo = max(d_e0, i - (n0 + N - 1));
+        // soft window edge on this row's edge keys in this thread's columns: p *= σ((w̃ − d)/τ)
+        const int d_hi = min(min(rw.W, i), i - n0 - c0);
+        const int d_lo = max(d_e0, i - (n0 + c0 + HALF - 1));
         for (int d = d_lo; d <= d_hi; ++d) {
-          const int c = i - d - n0;
-          T* e = reinterpret_cast<T*>(sp + (c >> 6) * (BM * 128) + sw128_offset(r, c & 63));
+          const int c = i - d - n0 - c0;
+          T* e = reinterpret_cast<T*>(sp + sw128_offset(r, c));
           const float pv = to_f32<T>(*e);
           const float z = (rw.wt - (float)d) * inv_tau;
           const float sg = 1.0f / (1.0f + expf(-z));
@@ -366,56 +379,88 @@ __global__ void __launch_bounds__(kThreads, 1) tc_fwd_kernel(const __grid_consta
           l -= pv * (1.0f - sg);
         }
       }
+      // rescale O_h once P is out of registers; a finite running max implies an
+      // earlier tile had valid keys in this half, so O_h has been written
+      // whenever a rescale happens
+      if (__any_sync(0xffffffffu, rescale)) {
+#pragma unroll
+        for (int ch = 0; ch < D / 32; ++ch) {
+          float o[32];
+          tmem_ld32(tOh + lane_addr + ch * 32, o);
+          tmem_wait_ld();
+          const float f = rescale ? factor : 1.0f;
+#pragma unroll
+          for (int j = 0; j < 32; ++j) o[j] *= f;
+          tmem_st32(tOh + lane_addr + ch * 32, o);
+        }
+        tmem_wait_st();
+      }
       fence_async_smem();
       tc_fence_before();
-      mbar_arrive(bar[P_FULL]);
+      mbar_arrive(bar[P_FULL + half]);
     }
-    // ---- epilogue: O / l, LSE
+    // ---- epilogue: merge the two halves of each row, O / l, LSE
     if (ok && n_tiles > 0) {
-      ok = mbar_wait(bar[O_DONE], (n_tiles - 1) & 1, abort_flag, p.status);
+      ok = mbar_wait(bar[O_DONE], (n_tiles - 1) & 1, abort_flag, p.status) &&
+           mbar_wait(bar[O_DONE + 1], (n_tiles - 1) & 1, abort_flag, p.status);
       ok = __all_sync(0xffffffffu, ok);
       tc_fence_after();
     }
-    const bool nonempty = ok && l > 1e-9f && n_tiles > 0;
-    const float inv_l = nonempty ? 1.0f / l : 0.f;
+    sm.m_half[half][r] = m;
+    sm.l_half[half][r] = l;
+    mbar_arrive(bar[EPI]);
+    ok = __all_sync(0xffffffffu, mbar_wait(bar[EPI], 0, abort_flag, p.status) && ok);
+    const float mh0 = sm.m_half[0][r], mh1 = sm.m_half[1][r];
+    const float lh0 = sm.l_half[0][r], lh1 = sm.l_half[1][r];
+    const float mm = fmaxf(mh0, mh1);
+    // a half with l = 0 never had a valid key and its O_h may be unwritten
+    const float f0 = lh0 > 0.f ? exp2f(mh0 - mm) : 0.f;
+    const float f1 = lh1 > 0.f ? exp2f(mh1 - mm) : 0.f;
+    const float lt = lh0 * f0 + lh1 * f1;
+    const bool nonempty = ok && lt > 1e-9f && n_tiles > 0;
+    const float inv_l = nonempty ? 1.0f / lt : 0.f;
+    const bool use0 = nonempty && lh0 > 0.f, use1 = nonempty && lh1 > 0.f;
     const int64_t row_off = (s0 + i) * (int64_t)p.H * D + (int64_t)h * D;
     T* og = reinterpret_cast<T*>(p.o) + row_off;
     float* of = p.o_f32 ? p.o_f32 + row_off : nullptr;
+    // this thread writes output columns [half·D/2, (half+1)·D/2), 16 at a time
 #pragma unroll
     for (int ch = 0; ch < D / 32; ++ch) {
-      float o[32];
+      const int col = half * (D / 2) + ch * 16;
+      float o0[16], o1[16];
       if (ok && n_tiles > 0) {
-        tmem_ld32(tO + lane_addr + ch * 32, o);
+        tmem_ld16(tO + lane_addr + col, o0);
+        tmem_ld16(tO + D + lane_addr + col, o1);
         tmem_wait_ld();
-      } else {
+      }
 #pragma unroll
-        for (int j = 0; j < 32; ++j) o[j] = 0.f;
+      for (int j = 0; j < 16; ++j) {
+        const float a0 = use0 ? o0[j] * f0 : 0.f;
+        const float a1 = use1 ? o1[j] * f1 : 0.f;
+        o0[j] = round_to<T>((a0 + a1) * inv_l);
       }
       if (row_ok) {
 #pragma unroll
-        for (int j = 0; j < 32; j += 8) {
-          float rv[8];
-#pragma unroll
-          for (int e = 0; e < 8; ++e) rv[e] = round_to<T>(o[j + e] * inv_l);
+        for (int j = 0; j < 16; j += 8) {
           uint4 u;
-          u.x = pack2(rv[0], rv[1], kBF16);
-          u.y = pack2(rv[2], rv[3], kBF16);
-          u.z = pack2(rv[4], rv[5], kBF16);
-          u.w = pack2(rv[6], rv[7], kBF16);
-          *reinterpret_cast<uint4*>(og + ch * 32 + j) = u;
+          u.x = pack2(o0[j + 0], o0[j + 1], kBF16);
+          u.y = pack2(o0[j + 2], o0[j + 3], kBF16);
+          u.z = pack2(o0[j + 4], o0[j + 5], kBF16);
+          u.w = pack2(o0[j + 6], o0[j + 7], kBF16);
+          *reinterpret_cast<uint4*>(og + col + j) = u;
           if (of) {
-            *reinterpret_cast<float4*>(of + ch * 32 + j) = make_float4(rv[0], rv[1], rv[2], rv[3]);
-            *reinterpret_cast<float4*>(of + ch * 32 + j + 4) = make_float4(rv[4], rv[5], rv[6], rv[7]);
+            *reinterpret_cast<float4*>(of + col + j) = make_float4(o0[j], o0[j + 1], o0[j + 2], o0[j + 3]);
+            *reinterpret_cast<float4*>(of + col + j + 4) = make_float4(o0[j + 4], o0[j + 5], o0[j + 6], o0[j + 7]);
           }
         }
       }
     }
-    if (row_ok) p.lse[(s0 + i) * p.H + h] = nonempty ? (m + log2f(l)) * kLn2 : -INFINITY;
+    if (row_ok && half == 0) p.lse[(s0 + i) * p.H + h] = nonempty ? (mm + log2f(lt)) * kLn2 : -INFINITY;
   }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
-  if (warp == 5) tmem_dealloc(tmem, 512);
+  if (warp == kMmaWarp) tmem_dealloc(tmem, 512);
 }
 
 // ---------------------------------------------------------------- host side
@@ -445,7 +490,8 @@ cudaError_t launch_tc_fwd(const DsaltAttnParams& p, cudaStream_t stream) {
     return cudaErrorInvalidValue;
   if (encode_3d(&a.tm_lv, dt, lv, D, kp, hs, row, (uint64_t)kp * row, 64, a.lmk_box, 1) != CUDA_SUCCESS)
     return cudaErrorInvalidValue;
-  const size_t smem = sizeof(FwdSmem<D>) + 1024;
+  // at least ~116 KB so that one CTA (and its 512 TMEM columns) owns the SM
+  const size_t smem = std::max(sizeof(FwdSmem<D>) + 1024, (size_t)(116 * 1024));
   cudaError_t e = cudaFuncSetAttribute(tc_fwd_kernel<T, D>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;
   dim3 grid((unsigned)p.max_blocks, (unsigned)p.H);

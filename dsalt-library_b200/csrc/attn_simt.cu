@@ -11,6 +11,7 @@
 //   landmarks the sorted landmark prefix with p <= i and float(p) < float(i) - w̃
 //                                                            (dsalt_triton_train.py:182-185)
 #include "common.cuh"
+#include "sm100.cuh"
 
 namespace dsalt {
 
@@ -141,7 +142,10 @@ bwd_preprocess_kernel(const DsaltAttnParams p) {
     s = fmaf(to_f32<T>(o[e]), gv, s);
   }
   s = warp_sum(s);
-  if (lane == 0) p.delta[row] = s;
+  if (lane == 0) {
+    p.delta[row] = s;
+    if (p.qrec) write_qrec(p, row / p.H, (int)(row % p.H), s);
+  }
 }
 
 // ---------------------------------------------------------------- dQ, d_w̃
@@ -289,6 +293,66 @@ simt_bwd_dkdv_kernel(const DsaltAttnParams p) {
   }
 }
 
+// The same Delta with 16-byte accesses: one thread per 8 consecutive elements
+// (bf16/fp16 inputs), G = D/8 lanes per (t, h) row, G a power of two ≤ 32, so a
+// row's lanes are an aligned group of one warp.  The fp32 dO is read with
+// streaming loads (it is not read again).
+template <typename T, int G>
+__global__ void __launch_bounds__(256)
+bwd_preprocess_vec_kernel(const DsaltAttnParams p) {
+  static_assert(sizeof(T) == 2, "16-bit inputs only");
+  const int64_t chunk = (int64_t)blockIdx.x * 256 + threadIdx.x;
+  const int64_t n_chunks = p.T * p.H * G;
+  float s = 0.f;
+  if (chunk < n_chunks) {
+    const uint4 ov = __ldg(reinterpret_cast<const uint4*>(p.o) + chunk);
+    uint4 gv;
+    if (p.dout_f32) {
+      const float4 a = __ldcs(reinterpret_cast<const float4*>(p.dout_f32) + 2 * chunk);
+      const float4 b = __ldcs(reinterpret_cast<const float4*>(p.dout_f32) + 2 * chunk + 1);
+      constexpr bool kBF16 = !std::is_same<T, __half>::value;
+      gv.x = sm100::pack2(a.x, a.y, kBF16);
+      gv.y = sm100::pack2(a.z, a.w, kBF16);
+      gv.z = sm100::pack2(b.x, b.y, kBF16);
+      gv.w = sm100::pack2(b.z, b.w, kBF16);
+      reinterpret_cast<uint4*>(const_cast<void*>(p.dout))[chunk] = gv;
+    } else {
+      gv = __ldg(reinterpret_cast<const uint4*>(p.dout) + chunk);
+    }
+    const T* o8 = reinterpret_cast<const T*>(&ov);
+    const T* g8 = reinterpret_cast<const T*>(&gv);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) s = fmaf(to_f32<T>(o8[e]), to_f32<T>(g8[e]), s);
+  }
+#pragma unroll
+  for (int off = G / 2; off > 0; off >>= 1) s += __shfl_xor_sync(0xffffffffu, s, off);
+  if (chunk < n_chunks && (threadIdx.x & (G - 1)) == 0) {
+    const int64_t row = chunk / G;
+    p.delta[row] = s;
+    if (p.qrec) write_qrec(p, row / p.H, (int)(row % p.H), s);
+  }
+}
+
+template <typename T>
+static bool launch_preprocess_vec(const DsaltAttnParams& p, cudaStream_t st) {
+  if constexpr (sizeof(T) != 2) {
+    return false;
+  } else {
+  const auto aligned = [](const void* q) { return (reinterpret_cast<uintptr_t>(q) & 15u) == 0; };
+  if (!aligned(p.o) || !aligned(p.dout) || (p.dout_f32 && !aligned(p.dout_f32))) return false;
+  const int G = p.D / 8;
+  const int64_t n_chunks = p.T * p.H * G;
+  const dim3 grid((unsigned)((n_chunks + 255) / 256));
+  switch (G) {
+    case 4: bwd_preprocess_vec_kernel<T, 4><<<grid, 256, 0, st>>>(p); return true;
+    case 8: bwd_preprocess_vec_kernel<T, 8><<<grid, 256, 0, st>>>(p); return true;
+    case 16: bwd_preprocess_vec_kernel<T, 16><<<grid, 256, 0, st>>>(p); return true;
+    case 32: bwd_preprocess_vec_kernel<T, 32><<<grid, 256, 0, st>>>(p); return true;
+    default: return false;
+  }
+  }
+}
+
 // d_w̃[t] = Σ_h dw_head[t,h], cast to the input dtype (dsalt_triton_train.py:748,756)
 template <typename T>
 __global__ void dw_reduce_kernel(const float* __restrict__ dw_head, T* __restrict__ dw, int64_t T_, int H) {
@@ -308,7 +372,9 @@ static cudaError_t launch_simt(int stage, const DsaltAttnParams& p, cudaStream_t
   const dim3 block(kSimtWarps * 32);
   switch (stage) {
     case 0: simt_fwd_kernel<T, R><<<grid, block, 0, st>>>(p); break;
-    case 1: bwd_preprocess_kernel<T, R><<<grid, block, 0, st>>>(p); break;
+    case 1:
+      if (!launch_preprocess_vec<T>(p, st)) bwd_preprocess_kernel<T, R><<<grid, block, 0, st>>>(p);
+      break;
     case 2: simt_bwd_dkdv_kernel<T, R><<<grid, block, 0, st>>>(p); break;
     case 3:
       simt_bwd_dq_kernel<T, R><<<grid, block, 0, st>>>(p);

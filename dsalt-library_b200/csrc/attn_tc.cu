@@ -42,17 +42,19 @@ constexpr int BM = 128;              // query rows per CTA
 constexpr int BN = 128;              // keys per tile
 constexpr int HALF = BN / 2;         // key columns per softmax thread
 constexpr int kMaxLmk = 512;         // landmark slots held in shared memory
-constexpr int kThreads = 320;
+constexpr int kThreads = 352;
 constexpr int kRowThreads = 256;
 constexpr int kProducerWarp = 8;
-constexpr int kMmaWarp = 9;
+constexpr int kMmaWarp = 9;    // TMEM owner; issues S = Q·Kᵀ
+constexpr int kMmaWarpB = 10;  // issues O_h += P_h·V_h
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr float kLn2 = 0.6931471805599453f;
 constexpr float kRescaleThreshold = 8.0f;  // log2 units
+constexpr int kMaxEdge = 8;                // soft-edge keys per row handled with precomputed factors
 
 enum Bar {
   Q_FULL = 0, K_FULL = 1, V_FULL = 3, K_EMPTY = 5, V_EMPTY = 7, S_FULL = 9, S_EMPTY = 11, P_FULL = 13,
-  O_DONE = 15, FINAL = 17, EPI = 18, NUM_BARS = 19
+  O_DONE = 15, FINAL = 17, EPI = 19, EPI2 = 20, NUM_BARS = 21
 };
 
 template <int D>
@@ -64,7 +66,7 @@ struct alignas(1024) FwdSmem {
   uint64_t bars[NUM_BARS];
   uint32_t tmem_base;
   int abort_flag;
-  int band_lo, band_hi, cnt_max, n_valid;
+  int band_lo, band_hi, cnt_max, n_valid, slow_edge;
   float m_half[2][BM];          // epilogue: per-half running max (log2) and sum
   float l_half[2][BM];
   int lmk_pos[kMaxLmk];
@@ -114,13 +116,16 @@ __global__ void __launch_bounds__(kThreads, 1) tc_fwd_kernel(const __grid_consta
       mbar_init(bar[O_DONE + st], 1);                // index = softmax half
     }
     mbar_init(bar[FINAL], 1);
+    mbar_init(bar[FINAL + 1], 1);
     mbar_init(bar[EPI], kRowThreads);
+    mbar_init(bar[EPI2], kRowThreads);
     fence_mbar_init();
     sm.abort_flag = 0;
     sm.band_lo = INT_MAX;
     sm.band_hi = -1;
     sm.cnt_max = 0;
     sm.n_valid = 0;
+    sm.slow_edge = 0;
   }
   if (warp == kProducerWarp && lane == 0) {
     prefetch_tmap(&a.tm_q);
@@ -128,6 +133,13 @@ __global__ void __launch_bounds__(kThreads, 1) tc_fwd_kernel(const __grid_consta
     prefetch_tmap(&a.tm_v);
   }
   if (warp == kMmaWarp) tmem_alloc(smem_u32(&sm.tmem_base), 512);
+  // row r = 32·(warp % 4) + lane, key-column half = warp / 4; the window load is
+  // issued here so that its latency overlaps the landmark loads below
+  const int r = 32 * (warp & 3) + lane;
+  const int half = (warp >> 2) & 1;
+  const int i = m0 + r;
+  const bool row_ok = warp < 8 && i < L;
+  const float w_raw = row_ok ? __ldg(p.w + s0 + i) : 0.f;
   const int kp = p.kp;
   const int64_t lbase = ((int64_t)h * p.S + s) * kp;
   for (int c = tid; c < kp; c += kThreads) {
@@ -137,16 +149,21 @@ __global__ void __launch_bounds__(kThreads, 1) tc_fwd_kernel(const __grid_consta
     if (ps >= 0) atomicAdd(&sm.n_valid, 1);
   }
   __syncthreads();
+  if (warp == kProducerWarp && lane == 0) {
+    // Q depends only on the block: load it while the windows are being resolved
+    mbar_expect_tx(bar[Q_FULL], BM * D * 2);
+#pragma unroll
+    for (int c = 0; c < D / 64; ++c)
+      tma_load_3d(smem_u32(sm.q + c * (BM * 128)), &a.tm_q, bar[Q_FULL], c * 64, h, (int)(s0 + m0));
+  }
 
-  // ---- per-row window: row r = 32·(warp % 4) + lane, key-column half = warp / 4
-  const int r = 32 * (warp & 3) + lane;
-  const int half = (warp >> 2) & 1;
-  const int i = m0 + r;
-  const bool row_ok = warp < 8 && i < L;
+  // ---- per-row window
   RowWindow rw = {};
   int lo = INT_MAX, hi = -1, cnt = 0;
+  // soft-edge keys of the row: distances d_e0 .. d_e0 + ne − 1, factors σ((w̃ − d)/τ)
+  int d_e0 = INT_MAX, ne = 0;
   if (row_ok) {
-    rw = row_window(__ldg(p.w + s0 + i), i, p.semantics, p.win_edge);
+    rw = row_window(w_raw, i, p.semantics, p.win_edge);
     if (rw.W >= 0) {
       lo = i - min(rw.W, i);
       hi = i;
@@ -159,12 +176,17 @@ __global__ void __launch_bounds__(kThreads, 1) tc_fwd_kernel(const __grid_consta
       if (ps <= i && (float)ps < rw.win_lo) a0 = mid + 1; else a1 = mid;
     }
     cnt = a0;
+    if (rw.W >= 0) {
+      d_e0 = max((int)floorf(rw.core) + 1, 0);
+      ne = max(min(rw.W, i) - d_e0 + 1, 0);
+    }
     if (half == 0) {
       if (lo <= hi) {
         atomicMin(&sm.band_lo, lo);
         atomicMax(&sm.band_hi, hi);
       }
       if (cnt > 0) atomicMax(&sm.cnt_max, cnt);
+      if (ne > kMaxEdge) atomicOr(&sm.slow_edge, 1);
     }
   }
   tc_fence_before();
@@ -189,12 +211,6 @@ __global__ void __launch_bounds__(kThreads, 1) tc_fwd_kernel(const __grid_consta
     // ------------------------------------------------------------ producers
     if (lane < 2 && n_tiles > 0) {
       const bool is_k = lane == 0;
-      if (is_k) {
-        mbar_expect_tx(bar[Q_FULL], BM * D * 2);
-#pragma unroll
-        for (int c = 0; c < D / 64; ++c)
-          tma_load_3d(smem_u32(sm.q + c * (BM * 128)), &a.tm_q, bar[Q_FULL], c * 64, h, (int)(s0 + m0));
-      }
       const int FULL = is_k ? K_FULL : V_FULL, EMPTY = is_k ? K_EMPTY : V_EMPTY;
       int issued = 0;
       for (int t = 0; t < n_tiles; ++t) {
@@ -214,22 +230,20 @@ __global__ void __launch_bounds__(kThreads, 1) tc_fwd_kernel(const __grid_consta
       }
       // drain: never leave a TMA write in flight into shared memory
       for (int t = max(0, issued - 2); t < issued; ++t) mbar_drain(bar[FULL + (t & 1)], (t >> 1) & 1);
-      if (is_k) mbar_drain(bar[Q_FULL], 0);
     }
+    if (lane == 0) mbar_drain(bar[Q_FULL], 0);
   } else if (warp == kMmaWarp) {
-    // ------------------------------------------------------------ MMA issuer
-    // order: S_0, S_1, then for every t: P_t,0·V_t,0, P_t,1·V_t,1 (each as soon as
-    // that half of P is written), then S_{t+2}.  O_DONE[h] is committed once per
-    // tile and half, also when the half had no valid key (its P·V is skipped).
+    // ------------------------------------------------------------ S issuer
+    // S_t = Q·K_tᵀ as soon as K_t is in and the softmax has read S_{t−2}.  The
+    // P·V products come from warp 10: one issuing thread sustains only about
+    // one MMA per 110 cycles, two overlap.
     if (lane == 0 && n_tiles > 0) {
-      const uint32_t id_o = idesc_f16(kBF16, BM, D, false, true);
       const uint32_t q_addr = smem_u32(sm.q);
-      const uint32_t p_addr = smem_u32(sm.p);
       bool ok = mbar_wait(bar[Q_FULL], 0, abort_flag, p.status);
-      auto issue_s = [&](int t) -> bool {
+      for (int t = 0; ok && t < n_tiles; ++t) {
         const int st = t & 1;
-        if (!mbar_wait(bar[K_FULL + st], (t >> 1) & 1, abort_flag, p.status)) return false;
-        if (t >= 2 && !mbar_wait(bar[S_EMPTY + st], ((t >> 1) - 1) & 1, abort_flag, p.status)) return false;
+        if (!mbar_wait(bar[K_FULL + st], (t >> 1) & 1, abort_flag, p.status)) break;
+        if (t >= 2 && !mbar_wait(bar[S_EMPTY + st], ((t >> 1) - 1) & 1, abort_flag, p.status)) break;
         tc_fence_after();
         const uint32_t k_addr = smem_u32(sm.k[st]);
         const uint32_t id_s = idesc_f16(kBF16, BM, tile_n(t), false, false);
@@ -242,15 +256,25 @@ __global__ void __launch_bounds__(kThreads, 1) tc_fwd_kernel(const __grid_consta
         }
         mma_commit(bar[S_FULL + st]);
         mma_commit(bar[K_EMPTY + st]);
-        return true;
-      };
+      }
+      // drain: every issued MMA completes before TMEM is released
+      mma_commit(bar[FINAL]);
+      mbar_drain(bar[FINAL], 0);
+    }
+  } else if (warp == kMmaWarpB) {
+    // ------------------------------------------------------------ P·V issuer
+    // O_h += P_t,h·V_t,h for each half h as soon as that half of P is written.
+    // O_DONE[h] is committed once per tile and half, also when the half had no
+    // valid key (its P·V is skipped).
+    if (lane == 0 && n_tiles > 0) {
+      const uint32_t id_o = idesc_f16(kBF16, BM, D, false, true);
+      const uint32_t p_addr = smem_u32(sm.p);
+      bool ok = true;
       bool o_written0 = false, o_written1 = false;
-      if (ok) ok = issue_s(0);
-      if (ok && n_tiles > 1) ok = issue_s(1);
       for (int t = 0; ok && t < n_tiles; ++t) {
         const int st = t & 1;
         const int nvalid = tile_n(t);
-        if (!mbar_wait(bar[V_FULL + st], (t >> 1) & 1, abort_flag, p.status)) { ok = false; break; }
+        if (!mbar_wait(bar[V_FULL + st], (t >> 1) & 1, abort_flag, p.status)) break;
         const uint32_t v_addr = smem_u32(sm.v[st]);
 #pragma unroll
         for (int hh = 0; hh < 2; ++hh) {
@@ -268,11 +292,9 @@ __global__ void __launch_bounds__(kThreads, 1) tc_fwd_kernel(const __grid_consta
         }
         if (!ok) break;
         mma_commit(bar[V_EMPTY + st]);
-        if (t + 2 < n_tiles && !issue_s(t + 2)) { ok = false; break; }
       }
-      // drain: every issued MMA completes before TMEM is released
-      mma_commit(bar[FINAL]);
-      mbar_drain(bar[FINAL], 0);
+      mma_commit(bar[FINAL + 1]);
+      mbar_drain(bar[FINAL + 1], 0);
     }
   } else {
     // ------------------------------------------------------------ softmax (row halves)
@@ -281,9 +303,12 @@ __global__ void __launch_bounds__(kThreads, 1) tc_fwd_kernel(const __grid_consta
     const uint32_t tOh = tO + half * D;  // this half's O accumulator
     const float sl2 = p.scale * kLog2e;
     const float inv_tau = 1.0f / p.tau_win;
-    // edge keys of this row: d in [d_e0, min(W, i)] (soft-edge bias), empty when d_e0 > W
-    int d_e0 = INT_MAX;
-    if (row_ok && rw.W >= 0) d_e0 = max((int)floorf(rw.core) + 1, 0);
+    const bool slow_edge = sm.slow_edge != 0;
+    // soft-edge factors of the row's edge keys (same expression as the per-key form)
+    float eg[kMaxEdge];
+#pragma unroll
+    for (int e = 0; e < kMaxEdge; ++e)
+      eg[e] = (e < ne) ? 1.0f / (1.0f + expf(-((rw.wt - (float)(d_e0 + e)) * inv_tau))) : 1.0f;
     float m = -INFINITY, l = 0.f;  // this half's running max (log2 units) and sum
     bool ok = true;
     uint8_t* sp = sm.p + half * (BM * 128);  // this half's P chunk: 128 rows x 64 keys
@@ -301,32 +326,42 @@ __global__ void __launch_bounds__(kThreads, 1) tc_fwd_kernel(const __grid_consta
       mbar_arrive(bar[S_EMPTY + st]);
 
       const bool lmk = t < n_lt;
-      float xs;  // multiplier applied inside exp2
-      int n0 = 0;
-      float mx[8];
-#pragma unroll
-      for (int g = 0; g < 8; ++g) mx[g] = -INFINITY;
+      const int n0 = lmk ? 0 : band_lo + BN * (t - n_lt);
+      // valid columns of this thread: [vlo, vhi] (band) or [0, vhi] (landmarks)
+      int vlo, vhi;
       if (lmk) {
-        const int climit = cnt - BN * t - c0;
+        vlo = 0;
+        vhi = cnt - BN * t - c0 - 1;
+      } else {
+        vlo = lo - n0 - c0;  // lo = INT_MAX for a row without band: stays positive
+        vhi = hi - n0 - c0;
+      }
+      const bool all_in = __all_sync(0xffffffffu, vlo <= 0 && vhi >= HALF - 1);
+      const bool all_out = __all_sync(0xffffffffu, vhi < 0 || vlo > HALF - 1 || vlo > vhi);
+      float xs = lmk ? 1.0f : sl2;  // multiplier applied inside exp2
+      if (lmk) {
         const float* lw2 = sm.lmk_lw2 + BN * t + c0;
 #pragma unroll
-        for (int c = 0; c < HALF; ++c) {
-          x[c] = (c < climit) ? fmaf(x[c], sl2, lw2[c]) : -INFINITY;
-          mx[c & 7] = fmaxf(mx[c & 7], x[c]);
-        }
-        xs = 1.0f;
-      } else {
-        n0 = band_lo + BN * (t - n_lt);
-        const int clo = lo - n0 - c0, chi = hi - n0 - c0;
-#pragma unroll
-        for (int c = 0; c < HALF; ++c) {
-          x[c] = (c >= clo && c <= chi) ? x[c] : -INFINITY;
-          mx[c & 7] = fmaxf(mx[c & 7], x[c]);
-        }
-        xs = sl2;
+        for (int c = 0; c < HALF; ++c) x[c] = fmaf(x[c], sl2, lw2[c]);
       }
-      float mt = fmaxf(fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])), fmaxf(fmaxf(mx[4], mx[5]), fmaxf(mx[6], mx[7])));
-      if (!lmk) mt *= sl2;
+      float mt = -INFINITY;
+      if (!all_out) {
+        if (!all_in) {
+#pragma unroll
+          for (int c = 0; c < HALF; ++c) x[c] = (c >= vlo && c <= vhi) ? x[c] : -INFINITY;
+        }
+        float mx[8];
+#pragma unroll
+        for (int g = 0; g < 8; ++g) mx[g] = max3(x[2 * g], x[2 * g + 1], x[16 + 2 * g]);
+#pragma unroll
+        for (int c = 32; c < HALF; c += 16)
+#pragma unroll
+          for (int g = 0; g < 8; ++g) mx[g] = max3(mx[g], x[c + 2 * g], x[c + 2 * g + 1]);
+#pragma unroll
+        for (int g = 0; g < 8; ++g) mx[g] = fmaxf(mx[g], x[16 + 2 * g + 1]);
+        mt = max3(max3(mx[0], mx[1], mx[2]), max3(mx[3], mx[4], mx[5]), fmaxf(mx[6], mx[7]));
+        if (!lmk) mt *= sl2;
+      }
       const float m_new = fmaxf(m, mt);
       bool rescale = false;
       float factor = 1.0f;
@@ -337,17 +372,21 @@ __global__ void __launch_bounds__(kThreads, 1) tc_fwd_kernel(const __grid_consta
         m = m_new;
         rescale = true;
       }
-      const float ms = (m == -INFINITY) ? 0.f : m;
-      float sm8[8];
+      if (!all_out) {
+        const float ms = (m == -INFINITY) ? 0.f : m;
+        float sm8[8];
 #pragma unroll
-      for (int g = 0; g < 8; ++g) sm8[g] = 0.f;
+        for (int g = 0; g < 8; ++g) sm8[g] = 0.f;
 #pragma unroll
-      for (int c = 0; c < HALF; ++c) {
-        x[c] = fast_exp2(fmaf(x[c], xs, -ms));
-        sm8[c & 7] += x[c];
+        for (int c = 0; c < HALF; ++c) {
+          x[c] = fast_exp2(fmaf(x[c], xs, -ms));
+          sm8[c & 7] += x[c];
+        }
+        const float sum = ((sm8[0] + sm8[1]) + (sm8[2] + sm8[3])) + ((sm8[4] + sm8[5]) + (sm8[6] + sm8[7]));
+        l = l * factor + sum;
+      } else {
+        l = l * factor;
       }
-      const float sum = ((sm8[0] + sm8[1]) + (sm8[2] + sm8[3])) + ((sm8[4] + sm8[5]) + (sm8[6] + sm8[7]));
-      l = l * factor + sum;
 
       // this half's P chunk and O_h are free once its previous P·V has completed
       if (t >= 1) {
@@ -355,28 +394,56 @@ __global__ void __launch_bounds__(kThreads, 1) tc_fwd_kernel(const __grid_consta
         if (!__all_sync(0xffffffffu, ok)) { ok = false; break; }
         tc_fence_after();
       }
+      if (all_out) {
+        const uint4 z = make_uint4(0u, 0u, 0u, 0u);
 #pragma unroll
-      for (int c8 = 0; c8 < HALF / 8; ++c8) {
-        const int c = c8 * 8;
-        uint4 u;
-        u.x = pack2(x[c + 0], x[c + 1], kBF16);
-        u.y = pack2(x[c + 2], x[c + 3], kBF16);
-        u.z = pack2(x[c + 4], x[c + 5], kBF16);
-        u.w = pack2(x[c + 6], x[c + 7], kBF16);
-        *reinterpret_cast<uint4*>(sp + sw128_offset(r, c)) = u;
+        for (int c8 = 0; c8 < HALF / 8; ++c8) *reinterpret_cast<uint4*>(sp + sw128_offset(r, c8 * 8)) = z;
+      } else {
+#pragma unroll
+        for (int c8 = 0; c8 < HALF / 8; ++c8) {
+          const int c = c8 * 8;
+          uint4 u;
+          u.x = pack2(x[c + 0], x[c + 1], kBF16);
+          u.y = pack2(x[c + 2], x[c + 3], kBF16);
+          u.z = pack2(x[c + 4], x[c + 5], kBF16);
+          u.w = pack2(x[c + 6], x[c + 7], kBF16);
+          *reinterpret_cast<uint4*>(sp + sw128_offset(r, c)) = u;
+        }
       }
-      if (!lmk && row_ok && d_e0 <= rw.W) {
-        // soft window edge on this row's edge keys in this thread's columns: p *= σ((w̃ − d)/τ)
-        const int d_hi = min(min(rw.W, i), i - n0 - c0);
-        const int d_lo = max(d_e0, i - (n0 + c0 + HALF - 1));
-        for (int d = d_lo; d <= d_hi; ++d) {
-          const int c = i - d - n0 - c0;
-          T* e = reinterpret_cast<T*>(sp + sw128_offset(r, c));
-          const float pv = to_f32<T>(*e);
-          const float z = (rw.wt - (float)d) * inv_tau;
-          const float sg = 1.0f / (1.0f + expf(-z));
-          *e = from_f32<T>(pv * sg);
-          l -= pv * (1.0f - sg);
+      if (!lmk && !all_out) {
+        // soft window edge on this row's edge keys in this thread's columns:
+        // p *= σ((w̃ − d)/τ); the key at distance d_e0 + e sits in column ce0 − e
+        const int ce0 = i - d_e0 - n0 - c0;
+        const bool has = ne > 0 && ce0 >= 0 && ce0 - (ne - 1) <= HALF - 1;
+        if (!slow_edge) {
+          if (__any_sync(0xffffffffu, has)) {
+            // all loads first, then all stores: the entries are distinct
+            float pv[kMaxEdge];
+#pragma unroll
+            for (int e = 0; e < kMaxEdge; ++e) {
+              const int c = ce0 - e;
+              const bool in = has && e < ne && c >= 0 && c < HALF;
+              pv[e] = in ? to_f32<T>(*reinterpret_cast<const T*>(sp + sw128_offset(r, c))) : 0.f;
+            }
+#pragma unroll
+            for (int e = 0; e < kMaxEdge; ++e) {
+              const int c = ce0 - e;
+              if (has && e < ne && c >= 0 && c < HALF) {
+                *reinterpret_cast<T*>(sp + sw128_offset(r, c)) = from_f32<T>(pv[e] * eg[e]);
+                l -= pv[e] * (1.0f - eg[e]);
+              }
+            }
+          }
+        } else if (has) {
+          for (int e = max(0, ce0 - (HALF - 1)); e < ne && ce0 - e >= 0; ++e) {
+            const int c = ce0 - e;
+            T* ep = reinterpret_cast<T*>(sp + sw128_offset(r, c));
+            const float pv = to_f32<T>(*ep);
+            const float z = (rw.wt - (float)(d_e0 + e)) * inv_tau;
+            const float sg = 1.0f / (1.0f + expf(-z));
+            *ep = from_f32<T>(pv * sg);
+            l -= pv * (1.0f - sg);
+          }
         }
       }
       // rescale O_h once P is out of registers; a finite running max implies an
@@ -417,45 +484,68 @@ __global__ void __launch_bounds__(kThreads, 1) tc_fwd_kernel(const __grid_consta
     const float f0 = lh0 > 0.f ? exp2f(mh0 - mm) : 0.f;
     const float f1 = lh1 > 0.f ? exp2f(mh1 - mm) : 0.f;
     const float lt = lh0 * f0 + lh1 * f1;
-    const bool nonempty = ok && lt > 1e-9f && n_tiles > 0;
+    const bool nonempty = lt > 1e-9f && n_tiles > 0;
     const float inv_l = nonempty ? 1.0f / lt : 0.f;
     const bool use0 = nonempty && lh0 > 0.f, use1 = nonempty && lh1 > 0.f;
-    const int64_t row_off = (s0 + i) * (int64_t)p.H * D + (int64_t)h * D;
-    T* og = reinterpret_cast<T*>(p.o) + row_off;
-    float* of = p.o_f32 ? p.o_f32 + row_off : nullptr;
-    // this thread writes output columns [half·D/2, (half+1)·D/2), 16 at a time
+    if (ok) {
+      // Stage the block's O rows in shared memory (all MMAs and loads are done, so
+      // the K / V buffers are free), then store them row-contiguously: bf16 rows
+      // in sm.v, fp32 rows in sm.k, 16-byte units XOR-swizzled by row % 8.
+      uint8_t* stage_h = sm.v[0];
+      uint8_t* stage_f = sm.k[0];
+      constexpr int kUnitsH = D * 2 / 16, kUnitsF = D * 4 / 16;  // 16-byte units per row
 #pragma unroll
-    for (int ch = 0; ch < D / 32; ++ch) {
-      const int col = half * (D / 2) + ch * 16;
-      float o0[16], o1[16];
-      if (ok && n_tiles > 0) {
-        tmem_ld16(tO + lane_addr + col, o0);
-        tmem_ld16(tO + D + lane_addr + col, o1);
-        tmem_wait_ld();
-      }
+      for (int ch = 0; ch < D / 32; ++ch) {  // 16 columns at a time
+        const int col = half * (D / 2) + ch * 16;
+        float o0[16], o1[16];
+        if (n_tiles > 0) {
+          tmem_ld16(tO + lane_addr + col, o0);
+          tmem_ld16(tO + D + lane_addr + col, o1);
+          tmem_wait_ld();
+        }
 #pragma unroll
-      for (int j = 0; j < 16; ++j) {
-        const float a0 = use0 ? o0[j] * f0 : 0.f;
-        const float a1 = use1 ? o1[j] * f1 : 0.f;
-        o0[j] = round_to<T>((a0 + a1) * inv_l);
-      }
-      if (row_ok) {
+        for (int j = 0; j < 16; ++j) {
+          const float a0 = use0 ? o0[j] * f0 : 0.f;
+          const float a1 = use1 ? o1[j] * f1 : 0.f;
+          o0[j] = round_to<T>((a0 + a1) * inv_l);
+        }
 #pragma unroll
         for (int j = 0; j < 16; j += 8) {
+          const int uh = (col + j) / 8;
           uint4 u;
           u.x = pack2(o0[j + 0], o0[j + 1], kBF16);
           u.y = pack2(o0[j + 2], o0[j + 3], kBF16);
           u.z = pack2(o0[j + 4], o0[j + 5], kBF16);
           u.w = pack2(o0[j + 6], o0[j + 7], kBF16);
-          *reinterpret_cast<uint4*>(og + col + j) = u;
-          if (of) {
-            *reinterpret_cast<float4*>(of + col + j) = make_float4(o0[j], o0[j + 1], o0[j + 2], o0[j + 3]);
-            *reinterpret_cast<float4*>(of + col + j + 4) = make_float4(o0[j + 4], o0[j + 5], o0[j + 6], o0[j + 7]);
+          *reinterpret_cast<uint4*>(stage_h + r * (kUnitsH * 16) + ((uh ^ (r & 7)) << 4)) = u;
+          const int uf = (col + j) / 4;
+          *reinterpret_cast<float4*>(stage_f + r * (kUnitsF * 16) + ((uf ^ (r & 7)) << 4)) =
+              make_float4(o0[j], o0[j + 1], o0[j + 2], o0[j + 3]);
+          *reinterpret_cast<float4*>(stage_f + r * (kUnitsF * 16) + (((uf + 1) ^ (r & 7)) << 4)) =
+              make_float4(o0[j + 4], o0[j + 5], o0[j + 6], o0[j + 7]);
+        }
+      }
+      if (row_ok && half == 0) p.lse[(s0 + i) * p.H + h] = nonempty ? (mm + log2f(lt)) * kLn2 : -INFINITY;
+      mbar_arrive(bar[EPI2]);
+      if (__all_sync(0xffffffffu, mbar_wait(bar[EPI2], 0, abort_flag, p.status))) {
+        const int rows = min(BM, L - m0);
+        const int64_t HD = (int64_t)p.H * D;
+        uint8_t* og = reinterpret_cast<uint8_t*>(p.o) + ((s0 + m0) * HD + (int64_t)h * D) * 2;
+        for (int u = tid; u < rows * kUnitsH; u += kRowThreads) {
+          const int rr = u / kUnitsH, uu = u % kUnitsH;
+          *reinterpret_cast<uint4*>(og + rr * HD * 2 + uu * 16) =
+              *reinterpret_cast<const uint4*>(stage_h + rr * (kUnitsH * 16) + ((uu ^ (rr & 7)) << 4));
+        }
+        if (p.o_f32) {
+          uint8_t* ofg = reinterpret_cast<uint8_t*>(p.o_f32) + ((s0 + m0) * HD + (int64_t)h * D) * 4;
+          for (int u = tid; u < rows * kUnitsF; u += kRowThreads) {
+            const int rr = u / kUnitsF, uu = u % kUnitsF;
+            *reinterpret_cast<uint4*>(ofg + rr * HD * 4 + uu * 16) =
+                *reinterpret_cast<const uint4*>(stage_f + rr * (kUnitsF * 16) + ((uu ^ (rr & 7)) << 4));
           }
         }
       }
     }
-    if (row_ok && half == 0) p.lse[(s0 + i) * p.H + h] = nonempty ? (mm + log2f(lt)) * kLn2 : -INFINITY;
   }
   tc_fence_before();
   __syncthreads();

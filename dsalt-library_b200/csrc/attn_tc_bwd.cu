@@ -38,6 +38,7 @@ constexpr int kRowThreads = 256;
 constexpr int kProducerWarp = 8;
 constexpr int kMmaWarp = 9;
 constexpr int kMaxLmk = 512;
+constexpr int kMaxEdge = kQRecEdge;  // soft-edge keys per query handled with precomputed factors
 constexpr float kLog2e = 1.4426950408889634f;
 
 __device__ __forceinline__ int round16(int n) { return (n + 15) & ~15; }
@@ -45,8 +46,10 @@ __device__ __forceinline__ int round16(int n) { return (n + 15) & ~15; }
 struct alignas(64) BwdArgs {
   CUtensorMap tm_q, tm_do, tm_k, tm_v, tm_lk, tm_lv;
   DsaltAttnParams p;
-  float* dk_lmk;  // [H,S,kp,D] fp32 scratch: landmark-slot dK / dV
+  float* dk_lmk;   // [DSALT_LMK_SPLIT,H,S,kp,D] fp32 scratch: partial landmark-slot dK / dV
   float* dv_lmk;
+  float* dlw_lmk;  // [DSALT_LMK_SPLIT,H,S,kp] fp32 scratch: partial landmark-slot d_lw
+  int64_t part_stride;  // H·S·kp: slots per partial
   int lmk_box;    // rows of one landmark TMA box
 };
 
@@ -64,11 +67,21 @@ __device__ __forceinline__ void store_row32(uint8_t* base, int row, int col0, co
   }
 }
 
+// store 32 packed bf16/fp16 values (16 words) of one row into a 128B-swizzled tile
+__device__ __forceinline__ void store_row32_packed(uint8_t* base, int row, int col0, const uint32_t* pk) {
+#pragma unroll
+  for (int g = 0; g < 4; ++g)
+    *reinterpret_cast<uint4*>(base + sm100::sw128_offset(row, col0 + 8 * g)) =
+        make_uint4(pk[4 * g], pk[4 * g + 1], pk[4 * g + 2], pk[4 * g + 3]);
+}
+
 // ======================================================================= dQ
 namespace dq {
 constexpr int BM = 128, BN = 64;
+constexpr int kThreadsDQ = 352;  // row warps 0-7, TMA warp 8, MMA warps 9 (S, dQ) and 10 (dP)
+constexpr int kMmaWarpB = 10;
 enum { QD_FULL = 0, K_FULL = 1, V_FULL = 3, K_EMPTY = 5, V_EMPTY = 7, SD_FULL = 9, SD_EMPTY = 11, DS_FULL = 13,
-       DS_EMPTY = 15, DQ_DONE = 17, FINAL = 18, EPI = 19, NB = 20 };
+       DS_EMPTY = 15, DQ_DONE = 17, FINAL = 18, EPI = 20, NB = 21 };
 
 template <int D>
 struct alignas(1024) Smem {
@@ -86,7 +99,7 @@ struct alignas(1024) Smem {
 };
 
 template <typename T, int D>
-__global__ void __launch_bounds__(kThreads, 1) tc_bwd_dq_kernel(const __grid_constant__ BwdArgs a) {
+__global__ void __launch_bounds__(kThreadsDQ, 1) tc_bwd_dq_kernel(const __grid_constant__ BwdArgs a) {
   using namespace sm100;
   const DsaltAttnParams& p = a.p;
   const int blk = blockIdx.x, h = blockIdx.y;
@@ -107,13 +120,14 @@ __global__ void __launch_bounds__(kThreads, 1) tc_bwd_dq_kernel(const __grid_con
       mbar_init(bar[V_FULL + st], 1);
       mbar_init(bar[K_EMPTY + st], 1);
       mbar_init(bar[V_EMPTY + st], 1);
-      mbar_init(bar[SD_FULL + st], 1);
+      mbar_init(bar[SD_FULL + st], 2);  // S (warp 9) and dP (warp 10)
       mbar_init(bar[SD_EMPTY + st], kRowThreads);
       mbar_init(bar[DS_FULL + st], kRowThreads);
       mbar_init(bar[DS_EMPTY + st], 1);
     }
     mbar_init(bar[DQ_DONE], 1);
     mbar_init(bar[FINAL], 1);
+    mbar_init(bar[FINAL + 1], 1);
     mbar_init(bar[EPI], kRowThreads);
     fence_mbar_init();
     sm.abort_flag = 0;
@@ -125,7 +139,7 @@ __global__ void __launch_bounds__(kThreads, 1) tc_bwd_dq_kernel(const __grid_con
   if (warp == kMmaWarp) tmem_alloc(smem_u32(&sm.tmem_base), 512);
   const int kp = p.kp;
   const int64_t lbase = ((int64_t)h * p.S + s) * kp;
-  for (int c = tid; c < kp; c += kThreads) {
+  for (int c = tid; c < kp; c += kThreadsDQ) {
     const int ps = __ldg(p.pos_sorted + lbase + c);
     sm.lmk_pos[c] = ps;
     sm.lmk_lw2[c] = __ldg(p.w_sorted + lbase + c) * kLog2e;
@@ -208,33 +222,30 @@ __global__ void __launch_bounds__(kThreads, 1) tc_bwd_dq_kernel(const __grid_con
       if (is_k) mbar_drain(bar[QD_FULL], 0);
     }
   } else if (warp == kMmaWarp) {
+    // S = Q·Kᵀ two tiles ahead and dQ += dS·K (warp 10 issues dP = dO·Vᵀ alongside)
     if (lane == 0 && n_tiles > 0) {
       const uint32_t id_s = idesc_f16(kBF16, BM, BN, false, false);
       const uint32_t id_dq = idesc_f16(kBF16, BM, D, false, true);
-      const uint32_t q_addr = smem_u32(sm.q), do_addr = smem_u32(sm.dO);
+      const uint32_t q_addr = smem_u32(sm.q);
       bool ok = mbar_wait(bar[QD_FULL], 0, abort_flag, p.status);
-      auto issue_sd = [&](int t) -> bool {
+      auto issue_s = [&](int t) -> bool {
         const int st = t & 1;
         if (!mbar_wait(bar[K_FULL + st], (t >> 1) & 1, abort_flag, p.status)) return false;
-        if (!mbar_wait(bar[V_FULL + st], (t >> 1) & 1, abort_flag, p.status)) return false;
         if (t >= 2 && !mbar_wait(bar[SD_EMPTY + st], ((t >> 1) - 1) & 1, abort_flag, p.status)) return false;
         tc_fence_after();
-        const uint32_t k_addr = smem_u32(sm.k[st]), v_addr = smem_u32(sm.v[st]);
+        const uint32_t k_addr = smem_u32(sm.k[st]);
 #pragma unroll
         for (int kk = 0; kk < D / 16; ++kk) {
           const uint32_t aoff = (kk >> 2) * (BM * 128) + (kk & 3) * 32;
           const uint32_t boff = (kk >> 2) * (BN * 128) + (kk & 3) * 32;
           mma_f16(tS + st * BN, sdesc_sw128(q_addr + aoff, 16, 1024), sdesc_sw128(k_addr + boff, 16, 1024), id_s,
                   kk > 0 ? 1u : 0u);
-          mma_f16(tdP + st * BN, sdesc_sw128(do_addr + aoff, 16, 1024), sdesc_sw128(v_addr + boff, 16, 1024),
-                  id_s, kk > 0 ? 1u : 0u);
         }
         mma_commit(bar[SD_FULL + st]);
-        mma_commit(bar[V_EMPTY + st]);
         return true;
       };
-      if (ok) ok = issue_sd(0);
-      if (ok && n_tiles > 1) ok = issue_sd(1);
+      if (ok) ok = issue_s(0);
+      if (ok && n_tiles > 1) ok = issue_s(1);
       for (int t = 0; ok && t < n_tiles; ++t) {
         const int st = t & 1;
         if (!mbar_wait(bar[DS_FULL + st], (t >> 1) & 1, abort_flag, p.status)) { ok = false; break; }
@@ -246,11 +257,36 @@ __global__ void __launch_bounds__(kThreads, 1) tc_bwd_dq_kernel(const __grid_con
                   id_dq, (t > 0 || kk > 0) ? 1u : 0u);
         mma_commit(bar[DS_EMPTY + st]);
         mma_commit(bar[K_EMPTY + st]);
-        if (t + 2 < n_tiles && !issue_sd(t + 2)) { ok = false; break; }
+        if (t + 2 < n_tiles && !issue_s(t + 2)) { ok = false; break; }
       }
       mma_commit(bar[DQ_DONE]);
       mma_commit(bar[FINAL]);
       mbar_drain(bar[FINAL], 0);
+    }
+  } else if (warp == kMmaWarpB) {
+    // dP = dO·Vᵀ, as soon as the V tile is in and the rows have read the previous dP of the stage
+    if (lane == 0 && n_tiles > 0) {
+      const uint32_t id_s = idesc_f16(kBF16, BM, BN, false, false);
+      const uint32_t do_addr = smem_u32(sm.dO);
+      bool ok = mbar_wait(bar[QD_FULL], 0, abort_flag, p.status);
+      for (int t = 0; ok && t < n_tiles; ++t) {
+        const int st = t & 1;
+        if (!mbar_wait(bar[V_FULL + st], (t >> 1) & 1, abort_flag, p.status)) break;
+        if (t >= 2 && !mbar_wait(bar[SD_EMPTY + st], ((t >> 1) - 1) & 1, abort_flag, p.status)) break;
+        tc_fence_after();
+        const uint32_t v_addr = smem_u32(sm.v[st]);
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk) {
+          const uint32_t aoff = (kk >> 2) * (BM * 128) + (kk & 3) * 32;
+          const uint32_t boff = (kk >> 2) * (BN * 128) + (kk & 3) * 32;
+          mma_f16(tdP + st * BN, sdesc_sw128(do_addr + aoff, 16, 1024), sdesc_sw128(v_addr + boff, 16, 1024),
+                  id_s, kk > 0 ? 1u : 0u);
+        }
+        mma_commit(bar[SD_FULL + st]);
+        mma_commit(bar[V_EMPTY + st]);
+      }
+      mma_commit(bar[FINAL + 1]);
+      mbar_drain(bar[FINAL + 1], 0);
     }
   } else {
     // --------------------------------------------------------- row warps
@@ -363,43 +399,55 @@ __global__ void __launch_bounds__(kThreads, 1) tc_bwd_dq_kernel(const __grid_con
 // ==================================================================== dK / dV
 namespace dkv {
 constexpr int BM = 128, BN = 64;  // BM keys (TMEM lanes), BN queries per tile
-enum { KV_FULL = 0, Q_FULL = 1, DO_FULL = 3, QDO_EMPTY = 5, COL_FULL = 7, SD_FULL = 9, SD_EMPTY = 11,
-       PDS_FULL = 13, PDS_EMPTY = 15, ROWS = 17, KV_DONE = 19, FINAL = 20, EPI = 21, NB = 22 };
+constexpr int kQStages = 3;       // Q / dO tile ring
+constexpr int kColStages = 4;     // per-tile column data ring
+constexpr int kThreadsKV = 384;   // row warps 0-7, TMA warp 8, MMA warps 9 and 11, column warp 10
+constexpr int kColWarp = 10;
+constexpr int kMmaWarpB = 11;     // issues dPᵀ and dK (warp 9: Sᵀ and dV)
+enum { KV_FULL = 0, Q_FULL = 1, DO_FULL = Q_FULL + kQStages, QDO_EMPTY = DO_FULL + kQStages,
+       REC_FULL = QDO_EMPTY + kQStages, COL_FULL = REC_FULL + kColStages, COL_EMPTY = COL_FULL + kColStages,
+       SD_FULL = COL_EMPTY + kColStages,
+       SD_EMPTY = SD_FULL + 2, PDS_FULL = SD_EMPTY + 2, PDS_EMPTY = PDS_FULL + 1, ROWS = PDS_EMPTY + 1,
+       KV_DONE = ROWS + 1, FINAL = KV_DONE + 1, EPI = FINAL + 2, EPI2 = EPI + 1, NB = EPI2 + 1 };
+
+// per-tile summary of the query records, written by the column warp
+struct alignas(16) ColStats {
+  int lo_max[2], lo_min[2], qi_min[2], qi_max[2];  // per column half: mask skipping
+  float wlo_min[2];
+  int has_edge;  // some soft-edge key of the tile falls in this block's keys
+};
 
 template <int D>
 struct alignas(1024) Smem {
   uint8_t k[BM * D * 2];
   uint8_t v[BM * D * 2];
-  uint8_t q[2][BN * D * 2];
-  uint8_t dO[2][BN * D * 2];
-  uint8_t pt[2][BM * BN * 2];
-  uint8_t dst[2][BM * BN * 2];
+  uint8_t q[kQStages][BN * D * 2];
+  uint8_t dO[kQStages][BN * D * 2];
+  uint8_t pt[BM * BN * 2];
+  uint8_t dst[BM * BN * 2];
   uint64_t bars[NB];
   uint32_t tmem_base;
   int abort_flag;
-  // per query column of a tile (double-buffered by tile parity)
-  alignas(16) float c_nlse2[2][BN];  // −LSE·log2(e) (0 for columns excluded by c_lo / c_i)
-  alignas(16) float c_delta[2][BN];
-  alignas(16) float c_wlo[2][BN];    // float(i) − w̃ (landmark rule)
-  alignas(16) float c_wt[2][BN];     // w̃ (edge bias)
-  alignas(16) int c_lo[2][BN];       // band start key of the query (INT_MAX: none)
-  alignas(16) int c_i[2][BN];        // query position (INT_MIN: no query / empty row)
-  alignas(16) int c_ehi[2][BN];      // last edge key (INT_MIN: none)
+  QRec rec[kColStages][BN];  // the tile's query records (bulk-copied, then fixed up)
+  ColStats stats[kColStages];
   float dlw_half[BM];
 };
 
 template <bool LMK, typename T, int D>
-__global__ void __launch_bounds__(kThreads, 1) tc_bwd_dkdv_kernel(const __grid_constant__ BwdArgs a) {
+__global__ void __launch_bounds__(kThreadsKV, 1) tc_bwd_dkdv_kernel(const __grid_constant__ BwdArgs a) {
   using namespace sm100;
   const DsaltAttnParams& p = a.p;
   const int h = blockIdx.y;
   int s, key0, nkeys, q_start;
   int64_t s0, lbase;
   int L;
+  int part = 0;
   if (LMK) {
+    // blockIdx.x = (s·nch + chunk)·DSALT_LMK_SPLIT + part
     const int nch = (p.kp + BM - 1) / BM;
-    s = blockIdx.x / nch;
-    const int chunk = blockIdx.x % nch;
+    part = blockIdx.x % DSALT_LMK_SPLIT;
+    s = blockIdx.x / DSALT_LMK_SPLIT / nch;
+    const int chunk = blockIdx.x / DSALT_LMK_SPLIT % nch;
     s0 = __ldg(p.cu_seqlens + s);
     L = (int)(__ldg(p.cu_seqlens + s + 1) - s0);
     lbase = ((int64_t)h * p.S + s) * p.kp;
@@ -420,7 +468,14 @@ __global__ void __launch_bounds__(kThreads, 1) tc_bwd_dkdv_kernel(const __grid_c
     lbase = ((int64_t)h * p.S + s) * p.kp;
   }
   const int q_end = LMK ? L - 1 : min(L - 1, key0 + BM - 1 + max(__ldg(p.seq_wmax + s), 0));
-  const int n_tiles = q_end >= q_start ? (q_end - q_start + BN) / BN : 0;
+  int n_tiles = q_end >= q_start ? (q_end - q_start + BN) / BN : 0;
+  if (LMK) {
+    // this part's share of the query tiles (possibly none: it then writes zeros)
+    const int per = (n_tiles + DSALT_LMK_SPLIT - 1) / DSALT_LMK_SPLIT;
+    const int u0 = per * part;
+    n_tiles = max(0, min(n_tiles, u0 + per) - u0);
+    q_start += BN * u0;
+  }
 
   extern __shared__ uint8_t smem_raw[];
   Smem<D>& sm = *reinterpret_cast<Smem<D>*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
@@ -429,20 +484,29 @@ __global__ void __launch_bounds__(kThreads, 1) tc_bwd_dkdv_kernel(const __grid_c
   const BarArray bar{smem_u32(&sm.bars[0])};
   if (tid == 0) {
     mbar_init(bar[KV_FULL], 1);
-    for (int st = 0; st < 2; ++st) {
+    // barriers completed by tcgen05.commit get one arrival from each MMA warp
+    for (int st = 0; st < kQStages; ++st) {
       mbar_init(bar[Q_FULL + st], 1);
       mbar_init(bar[DO_FULL + st], 1);
-      mbar_init(bar[QDO_EMPTY + st], 1);
-      mbar_init(bar[COL_FULL + st], 32);
-      mbar_init(bar[SD_FULL + st], 1);
-      mbar_init(bar[SD_EMPTY + st], kRowThreads);
-      mbar_init(bar[PDS_FULL + st], kRowThreads);
-      mbar_init(bar[PDS_EMPTY + st], 1);
-      mbar_init(bar[ROWS + st], kRowThreads);
+      mbar_init(bar[QDO_EMPTY + st], 2);
     }
-    mbar_init(bar[KV_DONE], 1);
+    for (int st = 0; st < kColStages; ++st) {
+      mbar_init(bar[REC_FULL + st], 1);
+      mbar_init(bar[COL_FULL + st], 32);
+      mbar_init(bar[COL_EMPTY + st], kRowThreads);
+    }
+    for (int st = 0; st < 2; ++st) {
+      mbar_init(bar[SD_FULL + st], 2);
+      mbar_init(bar[SD_EMPTY + st], kRowThreads);
+    }
+    mbar_init(bar[PDS_FULL], kRowThreads);
+    mbar_init(bar[PDS_EMPTY], 2);
+    mbar_init(bar[ROWS], kRowThreads);
+    mbar_init(bar[KV_DONE], 2);
     mbar_init(bar[FINAL], 1);
+    mbar_init(bar[FINAL + 1], 1);
     mbar_init(bar[EPI], kRowThreads);
+    mbar_init(bar[EPI2], kRowThreads);
     fence_mbar_init();
     sm.abort_flag = 0;
   }
@@ -456,97 +520,142 @@ __global__ void __launch_bounds__(kThreads, 1) tc_bwd_dkdv_kernel(const __grid_c
   const float inv_tau = 1.0f / p.tau_win;
 
   if (warp == kProducerWarp) {
-    // ---------------------------------------------------- producer warp
-    // per tile: the 64 queries' column data (2 per lane), then Q and dO tiles (lane 0)
-    if (n_tiles > 0) {
-      if (lane == 0) {
-        const uint32_t kv_bytes = (LMK ? a.lmk_box : BM) * D * 2;
-        mbar_expect_tx(bar[KV_FULL], 2 * kv_bytes);
+    // ---------------------------------------------------- TMA warp: K/V once, then the Q/dO ring
+    if (lane == 0 && n_tiles > 0) {
+      const uint32_t kv_bytes = (LMK ? a.lmk_box : BM) * D * 2;
+      mbar_expect_tx(bar[KV_FULL], 2 * kv_bytes);
 #pragma unroll
-        for (int c = 0; c < D / 64; ++c) {
-          if (LMK) {
-            tma_load_3d(smem_u32(sm.k + c * (BM * 128)), &a.tm_lk, bar[KV_FULL], c * 64, key0, h * p.S + s);
-            tma_load_3d(smem_u32(sm.v + c * (BM * 128)), &a.tm_lv, bar[KV_FULL], c * 64, key0, h * p.S + s);
-          } else {
-            tma_load_3d(smem_u32(sm.k + c * (BM * 128)), &a.tm_k, bar[KV_FULL], c * 64, h, (int)(s0 + key0));
-            tma_load_3d(smem_u32(sm.v + c * (BM * 128)), &a.tm_v, bar[KV_FULL], c * 64, h, (int)(s0 + key0));
-          }
+      for (int c = 0; c < D / 64; ++c) {
+        if (LMK) {
+          tma_load_3d(smem_u32(sm.k + c * (BM * 128)), &a.tm_lk, bar[KV_FULL], c * 64, key0, h * p.S + s);
+          tma_load_3d(smem_u32(sm.v + c * (BM * 128)), &a.tm_lv, bar[KV_FULL], c * 64, key0, h * p.S + s);
+        } else {
+          tma_load_3d(smem_u32(sm.k + c * (BM * 128)), &a.tm_k, bar[KV_FULL], c * 64, h, (int)(s0 + key0));
+          tma_load_3d(smem_u32(sm.v + c * (BM * 128)), &a.tm_v, bar[KV_FULL], c * 64, h, (int)(s0 + key0));
         }
       }
       int issued = 0;
       for (int u = 0; u < n_tiles; ++u) {
-        const int st = u & 1;
-        if (u >= 2 && !mbar_wait(bar[QDO_EMPTY + st], ((u >> 1) - 1) & 1, abort_flag, p.status)) break;
+        const int st = u % kQStages;
+        if (u >= kQStages && !mbar_wait(bar[QDO_EMPTY + st], (u / kQStages - 1) & 1, abort_flag, p.status)) break;
         const int q0 = q_start + BN * u;
+        mbar_expect_tx(bar[Q_FULL + st], BN * D * 2);
 #pragma unroll
-        for (int k2 = 0; k2 < 2; ++k2) {
-          const int c = lane + 32 * k2;
-          const int q = q0 + c;
-          float nl2 = 0.f, dl = 0.f, wt = 0.f, wlo = -INFINITY;
-          int clo = INT_MAX, ci = INT_MIN, ehi = INT_MIN;
-          if (q < L) {
-            const int64_t row = (s0 + q) * p.H + h;
-            const float lse = __ldg(p.lse + row);
-            if (lse != -INFINITY) {
-              nl2 = -lse * kLog2e;
-              dl = __ldg(p.delta + row);
-              const RowWindow rw = row_window(__ldg(p.w + s0 + q), q, p.semantics, p.win_edge);
-              wt = rw.wt;
-              wlo = rw.win_lo;
-              ci = q;
-              if (rw.W >= 0) {
-                clo = q - min(rw.W, q);
-                const int d_e0 = max((int)floorf(rw.core) + 1, 0);
-                ehi = d_e0 <= rw.W ? q - d_e0 : INT_MIN;
-              }
-            }
-          }
-          sm.c_nlse2[st][c] = nl2; sm.c_delta[st][c] = dl; sm.c_wt[st][c] = wt; sm.c_wlo[st][c] = wlo;
-          sm.c_lo[st][c] = clo; sm.c_i[st][c] = ci; sm.c_ehi[st][c] = ehi;
-        }
-        mbar_arrive(bar[COL_FULL + st]);
-        if (lane == 0) {
-          mbar_expect_tx(bar[Q_FULL + st], BN * D * 2);
+        for (int c = 0; c < D / 64; ++c)
+          tma_load_3d(smem_u32(sm.q[st] + c * (BN * 128)), &a.tm_q, bar[Q_FULL + st], c * 64, h, (int)(s0 + q0));
+        mbar_expect_tx(bar[DO_FULL + st], BN * D * 2);
 #pragma unroll
-          for (int c = 0; c < D / 64; ++c)
-            tma_load_3d(smem_u32(sm.q[st] + c * (BN * 128)), &a.tm_q, bar[Q_FULL + st], c * 64, h, (int)(s0 + q0));
-          mbar_expect_tx(bar[DO_FULL + st], BN * D * 2);
-#pragma unroll
-          for (int c = 0; c < D / 64; ++c)
-            tma_load_3d(smem_u32(sm.dO[st] + c * (BN * 128)), &a.tm_do, bar[DO_FULL + st], c * 64, h,
-                        (int)(s0 + q0));
-        }
+        for (int c = 0; c < D / 64; ++c)
+          tma_load_3d(smem_u32(sm.dO[st] + c * (BN * 128)), &a.tm_do, bar[DO_FULL + st], c * 64, h, (int)(s0 + q0));
         issued = u + 1;
       }
-      if (lane == 0) {
-        for (int u = max(0, issued - 2); u < issued; ++u) {
-          mbar_drain(bar[Q_FULL + (u & 1)], (u >> 1) & 1);
-          mbar_drain(bar[DO_FULL + (u & 1)], (u >> 1) & 1);
+      for (int u = max(0, issued - kQStages); u < issued; ++u) {
+        mbar_drain(bar[Q_FULL + u % kQStages], (u / kQStages) & 1);
+        mbar_drain(bar[DO_FULL + u % kQStages], (u / kQStages) & 1);
+      }
+      mbar_drain(bar[KV_FULL], 0);
+    }
+  } else if (warp == kColWarp) {
+    // ---------------------------------------------------- column warp: per-tile query records
+    // Lane 0 bulk-copies each tile's records (written by the preprocess stage)
+    // kColStages − 1 tiles ahead; the warp then masks the columns past the
+    // sequence end and summarises the tile for the row warps' mask skipping.
+    const int key_last = key0 + nkeys - 1;
+    const QRec* recg = reinterpret_cast<const QRec*>(p.qrec) + (int64_t)h * p.T + s0;
+    auto issue = [&](int u) {
+      const int st = u % kColStages;
+      const int q0 = q_start + BN * u;
+      const int nrec = (int)min((int64_t)BN, p.T - (s0 + q0));  // never read past the array
+      mbar_expect_tx(bar[REC_FULL + st], nrec * (uint32_t)sizeof(QRec));
+      bulk_load(smem_u32(&sm.rec[st][0]), recg + q0, nrec * (uint32_t)sizeof(QRec), bar[REC_FULL + st]);
+    };
+    if (lane == 0)
+      for (int u = 0; u < min(n_tiles, kColStages - 1); ++u) issue(u);
+    int issued = min(n_tiles, kColStages - 1);
+    for (int u = 0; u < n_tiles; ++u) {
+      const int st = u % kColStages;
+      if (!__all_sync(0xffffffffu, mbar_wait(bar[REC_FULL + st], (u / kColStages) & 1, abort_flag, p.status)))
+        break;
+      const int q0 = q_start + BN * u;
+      int st_lo_max[2], st_lo_min[2], st_qi_min[2], st_qi_max[2];
+      float st_wlo_min[2];
+      bool edge_here = false;
+#pragma unroll
+      for (int k2 = 0; k2 < 2; ++k2) {
+        const int c = lane + 32 * k2;
+        QRec& rc = sm.rec[st][c];
+        if (q0 + c >= L) {  // another sequence's query (or past the array): no pairs
+          rc.nlse2 = 0.f; rc.delta = 0.f; rc.lo = INT_MAX; rc.qi = INT_MIN;
+          rc.wlo = -INFINITY; rc.ehi = INT_MIN; rc.ne = 0;
         }
-        mbar_drain(bar[KV_FULL], 0);
+        const int clo = rc.lo, ci = rc.qi, ehi = rc.ehi, ne = rc.ne;
+        if (!LMK && ne > 0 && ehi >= key0 && ehi - (ne - 1) <= key_last) edge_here = true;
+        st_lo_max[k2] = clo; st_lo_min[k2] = clo; st_qi_min[k2] = ci; st_qi_max[k2] = ci; st_wlo_min[k2] = rc.wlo;
+      }
+#pragma unroll
+      for (int off = 16; off > 0; off >>= 1) {
+#pragma unroll
+        for (int k2 = 0; k2 < 2; ++k2) {
+          st_lo_max[k2] = max(st_lo_max[k2], __shfl_xor_sync(0xffffffffu, st_lo_max[k2], off));
+          st_lo_min[k2] = min(st_lo_min[k2], __shfl_xor_sync(0xffffffffu, st_lo_min[k2], off));
+          st_qi_min[k2] = min(st_qi_min[k2], __shfl_xor_sync(0xffffffffu, st_qi_min[k2], off));
+          st_qi_max[k2] = max(st_qi_max[k2], __shfl_xor_sync(0xffffffffu, st_qi_max[k2], off));
+          st_wlo_min[k2] = fminf(st_wlo_min[k2], __shfl_xor_sync(0xffffffffu, st_wlo_min[k2], off));
+        }
+      }
+      edge_here = __any_sync(0xffffffffu, edge_here);
+      if (lane == 0) {
+        ColStats& cs = sm.stats[st];
+#pragma unroll
+        for (int k2 = 0; k2 < 2; ++k2) {
+          cs.lo_max[k2] = st_lo_max[k2]; cs.lo_min[k2] = st_lo_min[k2];
+          cs.qi_min[k2] = st_qi_min[k2]; cs.qi_max[k2] = st_qi_max[k2]; cs.wlo_min[k2] = st_wlo_min[k2];
+        }
+        cs.has_edge = edge_here ? 1 : 0;
+      }
+      mbar_arrive(bar[COL_FULL + st]);
+      // refill the stage of tile u − 1 with tile u + kColStages − 1 once the rows released it
+      if (issued < n_tiles) {
+        const int nu = issued;  // == u + kColStages − 1
+        if (nu >= kColStages &&
+            !__all_sync(0xffffffffu,
+                        mbar_wait(bar[COL_EMPTY + nu % kColStages], (nu / kColStages - 1) & 1, abort_flag, p.status)))
+          break;
+        if (lane == 0) issue(nu);
+        ++issued;
       }
     }
-  } else if (warp == kMmaWarp) {
-    // ---------------------------------------------------- MMA issuer
+    if (lane == 0)
+      for (int u = max(0, issued - kColStages); u < issued; ++u)
+        mbar_drain(bar[REC_FULL + u % kColStages], (u / kColStages) & 1);
+  } else if (warp == kMmaWarp || warp == kMmaWarpB) {
+    // ---------------------------------------------------- MMA issuers
+    // Two warps issue so that their MMAs overlap (one issuing thread sustains
+    // only about one MMA per 110 cycles): warp 9 issues Sᵀ = K·Qᵀ and
+    // dV += Pᵀ·dO, warp 11 dPᵀ = V·dOᵀ and dK += dSᵀ·Q.  Barriers they both
+    // complete count two arrivals.
+    const bool is_a = warp == kMmaWarp;
     if (lane == 0 && n_tiles > 0) {
       const uint32_t id_s = idesc_f16(kBF16, BM, BN, false, false);
       const uint32_t id_kv = idesc_f16(kBF16, BM, D, false, true);
-      const uint32_t k_addr = smem_u32(sm.k), v_addr = smem_u32(sm.v);
+      const uint32_t kv_addr = smem_u32(is_a ? sm.k : sm.v);
+      const uint32_t pds = smem_u32(is_a ? sm.pt : sm.dst);
+      const uint32_t t_sd = is_a ? tS : tdP, t_acc = is_a ? tdV : tdK;
       bool ok = mbar_wait(bar[KV_FULL], 0, abort_flag, p.status);
+      // operand tiles: Sᵀ reads Q, dPᵀ reads dO; dV reads dO, dK reads Q
+      auto tile_sd = [&](int qs) { return smem_u32(is_a ? sm.q[qs] : sm.dO[qs]); };
+      auto tile_acc = [&](int qs) { return smem_u32(is_a ? sm.dO[qs] : sm.q[qs]); };
       auto issue_sd = [&](int u) -> bool {
-        const int st = u & 1;
-        if (!mbar_wait(bar[Q_FULL + st], (u >> 1) & 1, abort_flag, p.status)) return false;
-        if (!mbar_wait(bar[DO_FULL + st], (u >> 1) & 1, abort_flag, p.status)) return false;
+        const int st = u & 1, qs = u % kQStages;
+        if (!mbar_wait(bar[(is_a ? Q_FULL : DO_FULL) + qs], (u / kQStages) & 1, abort_flag, p.status)) return false;
         if (u >= 2 && !mbar_wait(bar[SD_EMPTY + st], ((u >> 1) - 1) & 1, abort_flag, p.status)) return false;
         tc_fence_after();
-        const uint32_t qa = smem_u32(sm.q[st]), da = smem_u32(sm.dO[st]);
+        const uint32_t ba = tile_sd(qs);
 #pragma unroll
         for (int kk = 0; kk < D / 16; ++kk) {
           const uint32_t aoff = (kk >> 2) * (BM * 128) + (kk & 3) * 32;
           const uint32_t boff = (kk >> 2) * (BN * 128) + (kk & 3) * 32;
-          mma_f16(tS + st * BN, sdesc_sw128(k_addr + aoff, 16, 1024), sdesc_sw128(qa + boff, 16, 1024), id_s,
-                  kk > 0 ? 1u : 0u);
-          mma_f16(tdP + st * BN, sdesc_sw128(v_addr + aoff, 16, 1024), sdesc_sw128(da + boff, 16, 1024), id_s,
+          mma_f16(t_sd + st * BN, sdesc_sw128(kv_addr + aoff, 16, 1024), sdesc_sw128(ba + boff, 16, 1024), id_s,
                   kk > 0 ? 1u : 0u);
         }
         mma_commit(bar[SD_FULL + st]);
@@ -555,25 +664,25 @@ __global__ void __launch_bounds__(kThreads, 1) tc_bwd_dkdv_kernel(const __grid_c
       if (ok) ok = issue_sd(0);
       if (ok && n_tiles > 1) ok = issue_sd(1);
       for (int u = 0; ok && u < n_tiles; ++u) {
-        const int st = u & 1;
-        if (!mbar_wait(bar[PDS_FULL + st], (u >> 1) & 1, abort_flag, p.status)) { ok = false; break; }
-        tc_fence_after();
-        const uint32_t pt = smem_u32(sm.pt[st]), dst = smem_u32(sm.dst[st]);
-        const uint32_t qa = smem_u32(sm.q[st]), da = smem_u32(sm.dO[st]);
-#pragma unroll
-        for (int kk = 0; kk < BN / 16; ++kk) {
-          mma_f16(tdV, sdesc_sw128(pt + kk * 32, 16, 1024), sdesc_sw128(da + kk * 2048, BN * 128, 1024), id_kv,
-                  (u > 0 || kk > 0) ? 1u : 0u);
-          mma_f16(tdK, sdesc_sw128(dst + kk * 32, 16, 1024), sdesc_sw128(qa + kk * 2048, BN * 128, 1024), id_kv,
-                  (u > 0 || kk > 0) ? 1u : 0u);
+        const int qs = u % kQStages;
+        if (!mbar_wait(bar[PDS_FULL], u & 1, abort_flag, p.status)) { ok = false; break; }
+        if (!mbar_wait(bar[(is_a ? DO_FULL : Q_FULL) + qs], (u / kQStages) & 1, abort_flag, p.status)) {
+          ok = false;
+          break;
         }
-        mma_commit(bar[PDS_EMPTY + st]);
-        mma_commit(bar[QDO_EMPTY + st]);
+        tc_fence_after();
+        const uint32_t ba = tile_acc(qs);
+#pragma unroll
+        for (int kk = 0; kk < BN / 16; ++kk)
+          mma_f16(t_acc, sdesc_sw128(pds + kk * 32, 16, 1024), sdesc_sw128(ba + kk * 2048, BN * 128, 1024), id_kv,
+                  (u > 0 || kk > 0) ? 1u : 0u);
+        mma_commit(bar[PDS_EMPTY]);
+        mma_commit(bar[QDO_EMPTY + qs]);
         if (u + 2 < n_tiles && !issue_sd(u + 2)) { ok = false; break; }
       }
       mma_commit(bar[KV_DONE]);
-      mma_commit(bar[FINAL]);
-      mbar_drain(bar[FINAL], 0);
+      mma_commit(bar[FINAL + (is_a ? 0 : 1)]);
+      mbar_drain(bar[FINAL + (is_a ? 0 : 1)], 0);
     }
   } else {
     // ---------------------------------------------------- key-row warps (Pᵀ, dSᵀ)
@@ -585,78 +694,132 @@ __global__ void __launch_bounds__(kThreads, 1) tc_bwd_dkdv_kernel(const __grid_c
     const bool key_ok = r < nkeys;
     const int j = LMK ? (key_ok ? __ldg(p.pos_sorted + lbase + key0 + r) : INT_MAX) : key0 + r;
     const float lw2 = (LMK && key_ok) ? __ldg(p.w_sorted + lbase + key0 + r) * kLog2e : 0.f;
+    // key range of this warp's 32 rows (band: consecutive; landmarks: sorted positions)
+    const int jf = LMK ? __shfl_sync(0xffffffffu, j, 0) : key0 + 32 * (warp & 3);
+    const int jl = LMK ? __reduce_max_sync(0xffffffffu, key_ok ? j : INT_MIN) : jf + 31;
+    const bool warp_keys_ok = __all_sync(0xffffffffu, key_ok);
     float dlw = 0.f;
     bool ok = true;
+    int rows_phase = 0;
     for (int u = 0; u < n_tiles; ++u) {
-      const int st = u & 1;
+      const int st = u & 1, cs = u % kColStages;
       ok = mbar_wait(bar[SD_FULL + st], (u >> 1) & 1, abort_flag, p.status) &&
-           mbar_wait(bar[COL_FULL + st], (u >> 1) & 1, abort_flag, p.status);
+           mbar_wait(bar[COL_FULL + cs], (u / kColStages) & 1, abort_flag, p.status);
       if (!__all_sync(0xffffffffu, ok)) { ok = false; break; }
       tc_fence_after();
-      float sv[32], dpv[32];
-      tmem_ld32(tS + lane_addr + st * BN + c0, sv);
-      tmem_ld32(tdP + lane_addr + st * BN + c0, dpv);
-      tmem_wait_ld();
-      tc_fence_before();
-      mbar_arrive(bar[SD_EMPTY + st]);
-      const float* cnl = sm.c_nlse2[st] + c0;
-      const float* cdl = sm.c_delta[st] + c0;
-      const int* cci = sm.c_i[st] + c0;
+      const QRec* rec = &sm.rec[cs][c0];
+      const ColStats& cst = sm.stats[cs];
+      bool all_in, all_out;
       if (LMK) {
-        const float* cwlo = sm.c_wlo[st] + c0;
-        const float jf = (float)j;
-#pragma unroll
-        for (int c = 0; c < 32; ++c) {
-          const bool valid = key_ok && j <= cci[c] && jf < cwlo[c];
-          const float pr = fast_exp2(fmaf(sv[c], sl2, lw2 + cnl[c]));
-          const float dsv = pr * (dpv[c] - cdl[c]);
-          sv[c] = valid ? pr : 0.f;
-          dpv[c] = valid ? dsv : 0.f;
-          dlw += dpv[c];
-        }
+        all_in = warp_keys_ok && cst.qi_min[half] >= jl && cst.wlo_min[half] > (float)jl;
+        all_out = false;
       } else {
-        const int* clo = sm.c_lo[st] + c0;
+        all_in = cst.lo_max[half] <= jf && cst.qi_min[half] >= jl;
+        all_out = cst.lo_min[half] > jl || cst.qi_max[half] < jf;
+      }
+      // Pᵀ and dSᵀ of this thread's 32 columns, 16 at a time, packed to the input
+      // dtype as they are produced (keeps the live register set small)
+      uint32_t pk_p[16], pk_d[16];
+      const float jfl = (float)j;
 #pragma unroll
-        for (int c = 0; c < 32; ++c) {
-          const bool valid = j >= clo[c] && j <= cci[c];
-          const float pr = fast_exp2(fmaf(sv[c], sl2, cnl[c]));
-          const float dsv = pr * (dpv[c] - cdl[c]);
-          sv[c] = valid ? pr : 0.f;
-          dpv[c] = valid ? dsv : 0.f;
+      for (int hh = 0; hh < 2; ++hh) {
+        float sv[16], dpv[16];
+        if (!all_out) {
+          tmem_ld16(tS + lane_addr + st * BN + c0 + 16 * hh, sv);
+          tmem_ld16(tdP + lane_addr + st * BN + c0 + 16 * hh, dpv);
+          tmem_wait_ld();
+        }
+        if (hh == 1) {
+          tc_fence_before();
+          mbar_arrive(bar[SD_EMPTY + st]);
+        }
+        if (all_out) {
+#pragma unroll
+          for (int g = 0; g < 8; ++g) { pk_p[8 * hh + g] = 0u; pk_d[8 * hh + g] = 0u; }
+          continue;
+        }
+#pragma unroll
+        for (int c = 0; c < 16; c += 2) {
+          float pr2[2], ds2[2];
+#pragma unroll
+          for (int e = 0; e < 2; ++e) {
+            const QRec& rq = rec[16 * hh + c + e];
+            const float4 r0 = *reinterpret_cast<const float4*>(&rq.nlse2);  // nlse2, delta, lo, qi
+            bool valid;
+            float pr;
+            if (LMK) {
+              pr = fast_exp2(fmaf(sv[c + e], sl2, lw2 + r0.x));
+              valid = all_in || (key_ok && j <= __float_as_int(r0.w) && jfl < rq.wlo);
+            } else {
+              pr = fast_exp2(fmaf(sv[c + e], sl2, r0.x));
+              valid = all_in || (j >= __float_as_int(r0.z) && j <= __float_as_int(r0.w));
+            }
+            const float dsv = pr * (dpv[c + e] - r0.y);
+            pr2[e] = valid ? pr : 0.f;
+            ds2[e] = valid ? dsv : 0.f;
+            if (LMK) dlw += ds2[e];
+          }
+          pk_p[8 * hh + c / 2] = pack2(pr2[0], pr2[1], kBF16);
+          pk_d[8 * hh + c / 2] = pack2(ds2[0], ds2[1], kBF16);
         }
       }
-      if (u >= 2) {
-        ok = mbar_wait(bar[PDS_EMPTY + st], ((u >> 1) - 1) & 1, abort_flag, p.status);
+      // the single Pᵀ / dSᵀ buffer is free once the previous tile's dV / dK MMAs completed
+      if (u >= 1) {
+        ok = mbar_wait(bar[PDS_EMPTY], (u - 1) & 1, abort_flag, p.status);
         if (!__all_sync(0xffffffffu, ok)) { ok = false; break; }
       }
-      uint8_t* ptb = sm.pt[st];
-      uint8_t* dsb = sm.dst[st];
-      store_row32<kBF16>(ptb, r, c0, sv);
-      store_row32<kBF16>(dsb, r, c0, dpv);
-      if (!LMK) {
-        // soft window edge, one query column per thread (tid < 64): its edge keys in this block
-        mbar_arrive(bar[ROWS + st]);
-        ok = mbar_wait(bar[ROWS + st], (u >> 1) & 1, abort_flag, p.status);
+      store_row32_packed(sm.pt, r, c0, pk_p);
+      store_row32_packed(sm.dst, r, c0, pk_d);
+      if (!LMK && cst.has_edge) {
+        // soft window edge: Pᵀ, dSᵀ *= σ((w̃ − d)/τ) on each query column's edge keys,
+        // spread over the 256 row threads: column tid % 64, edge indices tid / 64 and + 4
+        mbar_arrive(bar[ROWS]);
+        ok = mbar_wait(bar[ROWS], rows_phase & 1, abort_flag, p.status);
+        ++rows_phase;
         if (!__all_sync(0xffffffffu, ok)) { ok = false; break; }
-        if (tid < BN) {
-          const int col = tid;
-          const int jlo = max(sm.c_lo[st][col], key0);
-          const int jhi = min(sm.c_ehi[st][col], key0 + nkeys - 1);
-          const float wt = sm.c_wt[st][col];
-          const int qi = sm.c_i[st][col];
-          for (int jj = jlo; jj <= jhi; ++jj) {
-            const int rr = jj - key0;
-            const float z = (wt - (float)(qi - jj)) * inv_tau;
+        const int col = tid & (BN - 1);
+        const QRec& rc = sm.rec[cs][col];
+        const int ne = rc.ne, ehi = rc.ehi;
+        float a1[2], a2[2];
+        uint32_t off[2];
+        bool in[2];
+#pragma unroll
+        for (int k2 = 0; k2 < 2; ++k2) {
+          const int e = (tid >> 6) + 4 * k2;
+          const int rr = ehi - e - key0;
+          in[k2] = e < ne && rr >= 0 && rr < nkeys;
+          off[k2] = in[k2] ? sw128_offset(rr, col) : 0u;
+          a1[k2] = in[k2] ? to_f32<T>(*reinterpret_cast<const T*>(sm.pt + off[k2])) : 0.f;
+          a2[k2] = in[k2] ? to_f32<T>(*reinterpret_cast<const T*>(sm.dst + off[k2])) : 0.f;
+        }
+#pragma unroll
+        for (int k2 = 0; k2 < 2; ++k2) {
+          if (in[k2]) {
+            const float g = rc.eg[(tid >> 6) + 4 * k2];
+            *reinterpret_cast<T*>(sm.pt + off[k2]) = from_f32<T>(a1[k2] * g);
+            *reinterpret_cast<T*>(sm.dst + off[k2]) = from_f32<T>(a2[k2] * g);
+          }
+        }
+        if (tid < BN && ne > kMaxEdge) {
+          // wider soft edges than the precomputed factors: the rest one key at a time
+          const float wt = rc.wt;
+          const int qi = rc.qi;
+          for (int e = kMaxEdge; e < ne; ++e) {
+            const int rr = ehi - e - key0;
+            if (rr < 0) break;
+            if (rr >= nkeys) continue;
+            const float z = (wt - (float)(qi - (ehi - e))) * inv_tau;
             const float sg = 1.0f / (1.0f + expf(-z));
-            T* e1 = reinterpret_cast<T*>(ptb + sw128_offset(rr, col));
-            T* e2 = reinterpret_cast<T*>(dsb + sw128_offset(rr, col));
+            T* e1 = reinterpret_cast<T*>(sm.pt + sw128_offset(rr, col));
+            T* e2 = reinterpret_cast<T*>(sm.dst + sw128_offset(rr, col));
             *e1 = from_f32<T>(to_f32<T>(*e1) * sg);
             *e2 = from_f32<T>(to_f32<T>(*e2) * sg);
           }
         }
       }
       fence_async_smem();
-      mbar_arrive(bar[PDS_FULL + st]);
+      mbar_arrive(bar[PDS_FULL]);
+      mbar_arrive(bar[COL_EMPTY + cs]);
     }
     if (ok && n_tiles > 0) {
       ok = mbar_wait(bar[KV_DONE], 0, abort_flag, p.status);
@@ -664,26 +827,26 @@ __global__ void __launch_bounds__(kThreads, 1) tc_bwd_dkdv_kernel(const __grid_c
       tc_fence_after();
     }
     const bool have = ok && n_tiles > 0;
-    // this thread stores dK/dV columns [half·D/2, (half+1)·D/2) of key row r
+    // this thread handles dK/dV columns [half·D/2, (half+1)·D/2) of key row r
     if (LMK) {
-      const int64_t slot = lbase + key0 + r;
+      const int64_t slot = part * a.part_stride + lbase + key0 + r;
       float* dkl = a.dk_lmk + slot * D;
       float* dvl = a.dv_lmk + slot * D;
 #pragma unroll
-      for (int ch = 0; ch < D / 64; ++ch) {
-        const int col = half * (D / 2) + ch * 32;
-        float kk_[32], vv[32];
+      for (int ch = 0; ch < D / 32; ++ch) {
+        const int col = half * (D / 2) + ch * 16;
+        float kk_[16], vv[16];
         if (have) {
-          tmem_ld32(tdK + lane_addr + col, kk_);
-          tmem_ld32(tdV + lane_addr + col, vv);
+          tmem_ld16(tdK + lane_addr + col, kk_);
+          tmem_ld16(tdV + lane_addr + col, vv);
           tmem_wait_ld();
         } else {
 #pragma unroll
-          for (int e = 0; e < 32; ++e) { kk_[e] = 0.f; vv[e] = 0.f; }
+          for (int e = 0; e < 16; ++e) { kk_[e] = 0.f; vv[e] = 0.f; }
         }
         if (key_ok) {
 #pragma unroll
-          for (int e = 0; e < 32; e += 4) {
+          for (int e = 0; e < 16; e += 4) {
             *reinterpret_cast<float4*>(dkl + col + e) =
                 make_float4(kk_[e] * p.scale, kk_[e + 1] * p.scale, kk_[e + 2] * p.scale, kk_[e + 3] * p.scale);
             *reinterpret_cast<float4*>(dvl + col + e) = make_float4(vv[e], vv[e + 1], vv[e + 2], vv[e + 3]);
@@ -694,48 +857,74 @@ __global__ void __launch_bounds__(kThreads, 1) tc_bwd_dkdv_kernel(const __grid_c
       if (half == 1) sm.dlw_half[r] = dlw;
       mbar_arrive(bar[EPI]);
       const bool ok2 = mbar_wait(bar[EPI], 0, abort_flag, p.status);
-      if (half == 0 && key_ok && p.d_lw) {
-        const int slot_c = __ldg(p.perm + lbase + key0 + r);
-        if (slot_c >= 0) p.d_lw[((int64_t)h * p.S + s) * p.k_lmk + slot_c] = (have && ok2) ? dlw + sm.dlw_half[r] : 0.f;
-      }
-    } else {
-      // landmark slots at this key (sorted, duplicates adjacent) add their fp32 rows
+      if (half == 0 && key_ok) a.dlw_lmk[slot] = (have && ok2) ? dlw + sm.dlw_half[r] : 0.f;
+    } else if (ok) {
+      // landmark slots at this key (sorted, duplicates adjacent) add their fp32 rows;
+      // the rows are staged (dK in the Q ring, dV in the dO ring, 16-byte units
+      // XOR-swizzled by row % 8) and stored row-contiguously
       int cl = -1;
       if (key_ok && p.lmk_slot) cl = __ldg(p.lmk_slot + (s0 + j) * p.H + h);
-      const int64_t row_off = (s0 + j) * (int64_t)p.H * D + (int64_t)h * D;
-      T* dko = reinterpret_cast<T*>(p.dk) + row_off;
-      T* dvo = reinterpret_cast<T*>(p.dv) + row_off;
+      constexpr int kUnits = D * 2 / 16;
+      uint8_t* stage_k = sm.q[0];
+      uint8_t* stage_v = sm.dO[0];
 #pragma unroll
-      for (int ch = 0; ch < D / 64; ++ch) {
-        const int col = half * (D / 2) + ch * 32;
-        float kk_[32], vv[32];
-        if (have) {
-          tmem_ld32(tdK + lane_addr + col, kk_);
-          tmem_ld32(tdV + lane_addr + col, vv);
+      for (int ch = 0; ch < D / 32; ++ch) {  // 16 columns at a time
+        const int col = half * (D / 2) + ch * 16;
+        float kk_[16], vv[16];
+        if (n_tiles > 0) {
+          tmem_ld16(tdK + lane_addr + col, kk_);
+          tmem_ld16(tdV + lane_addr + col, vv);
           tmem_wait_ld();
         } else {
 #pragma unroll
-          for (int e = 0; e < 32; ++e) { kk_[e] = 0.f; vv[e] = 0.f; }
+          for (int e = 0; e < 16; ++e) { kk_[e] = 0.f; vv[e] = 0.f; }
         }
-        if (key_ok) {
 #pragma unroll
-          for (int e = 0; e < 32; ++e) kk_[e] *= p.scale;
-          for (int c = cl; c >= 0 && c < p.kp && __ldg(p.pos_sorted + lbase + c) == j; ++c) {
-            const float* lk = a.dk_lmk + (lbase + c) * D + col;
-            const float* lv = a.dv_lmk + (lbase + c) * D + col;
+        for (int e = 0; e < 16; ++e) kk_[e] *= p.scale;
+        for (int c = cl; key_ok && c >= 0 && c < p.kp && __ldg(p.pos_sorted + lbase + c) == j; ++c) {
+          for (int pp = 0; pp < DSALT_LMK_SPLIT; ++pp) {
+            const float* lk = a.dk_lmk + (pp * a.part_stride + lbase + c) * D + col;
+            const float* lv = a.dv_lmk + (pp * a.part_stride + lbase + c) * D + col;
 #pragma unroll
-            for (int e = 0; e < 32; ++e) { kk_[e] += __ldg(lk + e); vv[e] += __ldg(lv + e); }
+            for (int e = 0; e < 16; e += 4) {
+              const float4 k4 = __ldg(reinterpret_cast<const float4*>(lk + e));
+              const float4 v4 = __ldg(reinterpret_cast<const float4*>(lv + e));
+              kk_[e] += k4.x; kk_[e + 1] += k4.y; kk_[e + 2] += k4.z; kk_[e + 3] += k4.w;
+              vv[e] += v4.x; vv[e + 1] += v4.y; vv[e + 2] += v4.z; vv[e + 3] += v4.w;
+            }
           }
+        }
 #pragma unroll
-          for (int e = 0; e < 32; e += 8) {
-            uint4 u0, u1;
-            u0.x = pack2(kk_[e], kk_[e + 1], kBF16); u0.y = pack2(kk_[e + 2], kk_[e + 3], kBF16);
-            u0.z = pack2(kk_[e + 4], kk_[e + 5], kBF16); u0.w = pack2(kk_[e + 6], kk_[e + 7], kBF16);
-            u1.x = pack2(vv[e], vv[e + 1], kBF16); u1.y = pack2(vv[e + 2], vv[e + 3], kBF16);
-            u1.z = pack2(vv[e + 4], vv[e + 5], kBF16); u1.w = pack2(vv[e + 6], vv[e + 7], kBF16);
-            *reinterpret_cast<uint4*>(dko + col + e) = u0;
-            *reinterpret_cast<uint4*>(dvo + col + e) = u1;
-          }
+        for (int e = 0; e < 16; e += 8) {
+          const int un = (col + e) / 8;
+          uint4 u0, u1;
+          u0.x = pack2(kk_[e], kk_[e + 1], kBF16); u0.y = pack2(kk_[e + 2], kk_[e + 3], kBF16);
+          u0.z = pack2(kk_[e + 4], kk_[e + 5], kBF16); u0.w = pack2(kk_[e + 6], kk_[e + 7], kBF16);
+          u1.x = pack2(vv[e], vv[e + 1], kBF16); u1.y = pack2(vv[e + 2], vv[e + 3], kBF16);
+          u1.z = pack2(vv[e + 4], vv[e + 5], kBF16); u1.w = pack2(vv[e + 6], vv[e + 7], kBF16);
+          *reinterpret_cast<uint4*>(stage_k + r * (kUnits * 16) + ((un ^ (r & 7)) << 4)) = u0;
+          *reinterpret_cast<uint4*>(stage_v + r * (kUnits * 16) + ((un ^ (r & 7)) << 4)) = u1;
+        }
+      }
+      // d_lw of the landmark slots at this key: sum of the query-range parts
+      if (half == 0 && key_ok && p.d_lw) {
+        for (int c = cl; c >= 0 && c < p.kp && __ldg(p.pos_sorted + lbase + c) == j; ++c) {
+          float g = 0.f;
+          for (int pp = 0; pp < DSALT_LMK_SPLIT; ++pp) g += __ldg(a.dlw_lmk + pp * a.part_stride + lbase + c);
+          const int slot_c = __ldg(p.perm + lbase + c);
+          if (slot_c >= 0) p.d_lw[((int64_t)h * p.S + s) * p.k_lmk + slot_c] = g;
+        }
+      }
+      mbar_arrive(bar[EPI2]);
+      if (__all_sync(0xffffffffu, mbar_wait(bar[EPI2], 0, abort_flag, p.status))) {
+        const int64_t HD = (int64_t)p.H * D;
+        uint8_t* dkg = reinterpret_cast<uint8_t*>(p.dk) + ((s0 + key0) * HD + (int64_t)h * D) * 2;
+        uint8_t* dvg = reinterpret_cast<uint8_t*>(p.dv) + ((s0 + key0) * HD + (int64_t)h * D) * 2;
+        for (int un = tid; un < nkeys * kUnits; un += kRowThreads) {
+          const int rr = un / kUnits, uu = un % kUnits;
+          const uint32_t so = rr * (kUnits * 16) + ((uu ^ (rr & 7)) << 4);
+          *reinterpret_cast<uint4*>(dkg + rr * HD * 2 + uu * 16) = *reinterpret_cast<const uint4*>(stage_k + so);
+          *reinterpret_cast<uint4*>(dvg + rr * HD * 2 + uu * 16) = *reinterpret_cast<const uint4*>(stage_v + so);
         }
       }
     }
@@ -783,7 +972,7 @@ cudaError_t launch_dq(const DsaltAttnParams& p, cudaStream_t st) {
   const size_t smem = std::max(sizeof(dq::Smem<D>) + 1024, (size_t)(116 * 1024));
   cudaError_t e = cudaFuncSetAttribute(dq::tc_bwd_dq_kernel<T, D>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;
-  dq::tc_bwd_dq_kernel<T, D><<<dim3((unsigned)p.max_blocks, (unsigned)p.H), kThreads, smem, st>>>(a);
+  dq::tc_bwd_dq_kernel<T, D><<<dim3((unsigned)p.max_blocks, (unsigned)p.H), dq::kThreadsDQ, smem, st>>>(a);
   e = cudaGetLastError();
   if (e != cudaSuccess) return e;
   if (p.dw && p.dw_head) return simt_attention_stage(4, p, st);  // dw = Σ_h dw_head
@@ -791,45 +980,48 @@ cudaError_t launch_dq(const DsaltAttnParams& p, cudaStream_t st) {
 }
 
 template <typename T, int D>
-cudaError_t launch_dkdv(const DsaltAttnParams& p, float* dk_lmk, float* dv_lmk, cudaStream_t st) {
+cudaError_t launch_dkdv(const DsaltAttnParams& p, float* lmk_scratch, cudaStream_t st) {
   BwdArgs a;
   if (!make_args<T, D>(a, p, dkv::BN, dkv::BM, dkv::BM)) return cudaErrorInvalidValue;
-  a.dk_lmk = dk_lmk;
-  a.dv_lmk = dv_lmk;
+  a.part_stride = (int64_t)p.H * p.S * p.kp;
+  const int64_t part_floats = DSALT_LMK_SPLIT * a.part_stride * D;
+  a.dk_lmk = lmk_scratch;
+  a.dv_lmk = lmk_scratch ? lmk_scratch + part_floats : nullptr;
+  a.dlw_lmk = lmk_scratch ? lmk_scratch + 2 * part_floats : nullptr;
   const size_t smem = std::max(sizeof(dkv::Smem<D>) + 1024, (size_t)(116 * 1024));
   cudaError_t e;
   if (p.kp > 0 && p.S > 0) {
     e = cudaFuncSetAttribute(dkv::tc_bwd_dkdv_kernel<true, T, D>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return e;
     const int nch = (p.kp + dkv::BM - 1) / dkv::BM;
-    dkv::tc_bwd_dkdv_kernel<true, T, D><<<dim3((unsigned)(p.S * nch), (unsigned)p.H), kThreads, smem, st>>>(a);
+    const unsigned items = (unsigned)(p.S * nch * DSALT_LMK_SPLIT);
+    dkv::tc_bwd_dkdv_kernel<true, T, D><<<dim3(items, (unsigned)p.H), dkv::kThreadsKV, smem, st>>>(a);
     e = cudaGetLastError();
     if (e != cudaSuccess) return e;
   }
   e = cudaFuncSetAttribute(dkv::tc_bwd_dkdv_kernel<false, T, D>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;
-  dkv::tc_bwd_dkdv_kernel<false, T, D><<<dim3((unsigned)p.max_blocks, (unsigned)p.H), kThreads, smem, st>>>(a);
+  dkv::tc_bwd_dkdv_kernel<false, T, D><<<dim3((unsigned)p.max_blocks, (unsigned)p.H), dkv::kThreadsKV, smem, st>>>(a);
   return cudaGetLastError();
 }
 
 }  // namespace bwd
 
-// lmk_scratch: the caller's [2,H,S,kp,D] fp32 buffer for the landmark-slot dK / dV
-// that the landmark items of the key-parallel pass hand to the band items.
+// lmk_scratch: the caller's fp32 buffer ((2·D + 1)·DSALT_LMK_SPLIT·H·S·kp floats) for
+// the partial landmark-slot dK / dV / d_lw that the landmark items of the
+// key-parallel pass hand to the band items.
 cudaError_t tc_bwd_stage(int stage, const DsaltAttnParams& p, float* lmk_scratch, cudaStream_t st) {
   const bool bf = p.dtype == DSALT_BF16;
-  const size_t half = (size_t)p.H * p.S * p.kp * p.D;
   if (stage == 3) {
     if (bf) return p.D == 64 ? bwd::launch_dq<__nv_bfloat16, 64>(p, st) : bwd::launch_dq<__nv_bfloat16, 128>(p, st);
     return p.D == 64 ? bwd::launch_dq<__half, 64>(p, st) : bwd::launch_dq<__half, 128>(p, st);
   }
   if (stage == 2) {
-    float* dk = lmk_scratch;
-    float* dv = lmk_scratch ? lmk_scratch + half : nullptr;
     if (p.kp > 0 && !lmk_scratch) return cudaErrorInvalidValue;
-    if (bf) return p.D == 64 ? bwd::launch_dkdv<__nv_bfloat16, 64>(p, dk, dv, st)
-                             : bwd::launch_dkdv<__nv_bfloat16, 128>(p, dk, dv, st);
-    return p.D == 64 ? bwd::launch_dkdv<__half, 64>(p, dk, dv, st) : bwd::launch_dkdv<__half, 128>(p, dk, dv, st);
+    if (bf) return p.D == 64 ? bwd::launch_dkdv<__nv_bfloat16, 64>(p, lmk_scratch, st)
+                             : bwd::launch_dkdv<__nv_bfloat16, 128>(p, lmk_scratch, st);
+    return p.D == 64 ? bwd::launch_dkdv<__half, 64>(p, lmk_scratch, st)
+                     : bwd::launch_dkdv<__half, 128>(p, lmk_scratch, st);
   }
   return simt_attention_stage(stage, p, st);
 }

@@ -6,6 +6,7 @@
 #include <cuda_fp16.h>
 #include <stdint.h>
 #include <math.h>
+#include <climits>
 
 #include "dsalt_b200.h"
 
@@ -111,6 +112,60 @@ __device__ __forceinline__ float edge_dbias(const RowWindow& r, float d, float i
   float z = (r.wt - d) * inv_tau;
   float sig = 1.0f / (1.0f + expf(-z));
   return (1.0f - sig) * inv_tau;
+}
+
+// ------------------------------------------------------ backward query records
+// One record per (head, query token) of the backward, written by the preprocess
+// stage next to Delta and read by the tensor-core dK/dV and dQ stages, so that
+// the per-query window / soft-edge work is done once instead of once per tile.
+constexpr int kQRecEdge = 8;  // soft-edge factors stored per record
+struct alignas(16) QRec {
+  float nlse2;  // −LSE·log2(e) (0 for a row without keys)
+  float delta;  // Δ = Σ_d O·dO
+  int lo;       // first band key (INT_MAX: none)
+  int qi;       // query position in its sequence (INT_MIN: row without keys)
+  float wlo;    // float(i) − w̃ (landmark rule)
+  float wt;     // w̃
+  int ehi;      // last soft-edge key (INT_MIN: none)
+  int ne;       // soft-edge keys ehi, ehi − 1, …, ehi − ne + 1 (d = i − key)
+  float eg[kQRecEdge];  // σ((w̃ − d)/τ) of edge key ehi − e, e < min(ne, kQRecEdge)
+};
+static_assert(sizeof(QRec) == DSALT_QREC_FLOATS * 4, "record size");
+
+// Record of query token t (global index), head h, given its Δ.
+__device__ __forceinline__ void write_qrec(const DsaltAttnParams& p, int64_t t, int h, float delta) {
+  QRec rec;
+  rec.nlse2 = 0.f; rec.delta = 0.f; rec.lo = INT_MAX; rec.qi = INT_MIN;
+  rec.wlo = -INFINITY; rec.wt = 0.f; rec.ehi = INT_MIN; rec.ne = 0;
+#pragma unroll
+  for (int e = 0; e < kQRecEdge; ++e) rec.eg[e] = 1.0f;
+  const float lse = p.lse[t * p.H + h];
+  if (lse != -INFINITY) {
+    const int s = find_seq(p.cu_seqlens, p.S, t);
+    const int i = (int)(t - __ldg(p.cu_seqlens + s));
+    const RowWindow rw = row_window(__ldg(p.w + t), i, p.semantics, p.win_edge);
+    rec.nlse2 = -lse * 1.4426950408889634f;
+    rec.delta = delta;
+    rec.qi = i;
+    rec.wlo = rw.win_lo;
+    rec.wt = rw.wt;
+    if (rw.W >= 0) {
+      rec.lo = i - min(rw.W, i);
+      const int d_e0 = max((int)floorf(rw.core) + 1, 0);
+      if (d_e0 <= rw.W) {
+        rec.ehi = i - d_e0;
+        rec.ne = max(rec.ehi - rec.lo + 1, 0);
+        const float inv_tau = 1.0f / p.tau_win;
+#pragma unroll
+        for (int e = 0; e < kQRecEdge; ++e)
+          if (e < rec.ne) rec.eg[e] = 1.0f / (1.0f + expf(-((rw.wt - (float)(d_e0 + e)) * inv_tau)));
+      }
+    }
+  }
+  float4* dst = reinterpret_cast<float4*>(p.qrec + ((int64_t)h * p.T + t) * DSALT_QREC_FLOATS);
+  const float4* src = reinterpret_cast<const float4*>(&rec);
+#pragma unroll
+  for (int k = 0; k < DSALT_QREC_FLOATS / 4; ++k) dst[k] = src[k];
 }
 
 }  // namespace dsalt

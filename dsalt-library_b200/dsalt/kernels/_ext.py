@@ -21,6 +21,9 @@ F16, BF16, F32 = 0, 1, 2
 TRAIN, INFER = 0, 1
 IMPL_AUTO, IMPL_SIMT, IMPL_TCGEN05 = 0, 1, 2
 DEV_WAIT_TIMEOUT, DEV_BAD_INDEX = 1, 2
+ABI_VERSION = 3
+QREC_FLOATS = 16  # DSALT_QREC_FLOATS
+LMK_SPLIT = 4  # DSALT_LMK_SPLIT
 
 _c_void_p = ctypes.c_void_p
 _i32 = ctypes.c_int32
@@ -53,7 +56,7 @@ class AttnParams(ctypes.Structure):
                 ("o", _c_void_p), ("o_f32", _c_void_p), ("lse", _c_void_p),
                 ("dout", _c_void_p), ("dout_f32", _c_void_p), ("delta", _c_void_p), ("dq", _c_void_p), ("dk", _c_void_p),
                 ("dv", _c_void_p), ("dw_head", _c_void_p), ("dw", _c_void_p), ("d_lw", _c_void_p),
-                ("lmk_grad", _c_void_p), ("status", _c_void_p),
+                ("lmk_grad", _c_void_p), ("qrec", _c_void_p), ("status", _c_void_p),
                 ("T", _i64), ("H", _i32), ("D", _i32), ("S", _i32), ("k_lmk", _i32), ("kp", _i32),
                 ("max_blocks", _i32), ("scale", _f32), ("tau_win", _f32), ("win_edge", _f32),
                 ("semantics", _i32), ("dtype", _i32), ("impl", _i32)]
@@ -115,7 +118,7 @@ def load() -> ctypes.CDLL:
     lib.dsalt_b200_status_string.argtypes = [ctypes.c_int]
     lib.dsalt_b200_params_sizeof.restype = ctypes.c_int
     lib.dsalt_b200_params_sizeof.argtypes = [ctypes.c_int]
-    if lib.dsalt_b200_abi_version() != 1:
+    if lib.dsalt_b200_abi_version() != ABI_VERSION:
         raise RuntimeError("libdsalt_b200.so ABI version mismatch; rebuild the library")
     for i, st in enumerate(_STRUCTS):
         n = lib.dsalt_b200_params_sizeof(i)

@@ -177,10 +177,14 @@ def backward(grad_out, q_c, k_c, v_c, o, lse, prep: Prepared, tau_win: float, wi
     d_lw = torch.zeros(H, prep.S, prep.k_lmk, dtype=torch.float32, device=dev)
     dw_head = torch.empty(T, H, dtype=torch.float32, device=dev) if want_dw else None
     dw = torch.empty(T, dtype=q_c.dtype, device=dev) if want_dw else None
-    lmk_grad = torch.empty(2, H, prep.S, prep.kp, prep.D, dtype=torch.float32, device=dev) \
-        if prep.kp > 0 else None
+    # partial landmark-slot dK, dV, d_lw of the tensor-core dK/dV stage
+    lmk_grad = torch.empty((2 * prep.D + 1) * _ext.LMK_SPLIT * H * prep.S * prep.kp,
+                           dtype=torch.float32, device=dev) if prep.kp > 0 else None
+    # per-query records (LSE, Delta, window, soft-edge factors) of the tensor-core stages
+    qrec = torch.empty(H, T, _ext.QREC_FLOATS, dtype=torch.float32, device=dev)
     p = _params(prep, q_c, k_c, v_c, tau_win, win_edge, impl, o=o, lse=lse, dout=do_c, dout_f32=do_f32,
-                delta=delta, dq=dq, dk=dk, dv=dv, dw_head=dw_head, dw=dw, d_lw=d_lw, lmk_grad=lmk_grad)
+                delta=delta, dq=dq, dk=dk, dv=dv, dw_head=dw_head, dw=dw, d_lw=d_lw, lmk_grad=lmk_grad,
+                qrec=qrec)
     _ext.call("dsalt_attn_bwd_preprocess", p)
     _ext.call("dsalt_attn_bwd_dkdv", p)
     _ext.call("dsalt_attn_bwd_dq", p)

@@ -29,7 +29,15 @@
 extern "C" {
 #endif
 
-#define DSALT_B200_ABI_VERSION 1
+#define DSALT_B200_ABI_VERSION 3
+
+/* The tensor-core dK/dV stage splits each landmark chunk's query range into
+ * this many parts that run as separate CTAs; their fp32 partial sums are added
+ * in a fixed order (deterministic) by the band pass. */
+#define DSALT_LMK_SPLIT 4
+
+/* fp32 words per query record of the backward (DsaltAttnParams.qrec) */
+#define DSALT_QREC_FLOATS 16
 
 /* ---- status codes ------------------------------------------------------ */
 enum {
@@ -146,8 +154,13 @@ typedef struct DsaltAttnParams {
   float* dw_head;             /* [T,H] scratch (train) */
   void* dw;                   /* [T] dtype: Σ_h ∂loss/∂w̃ (train) or NULL */
   float* d_lw;                /* [H,S,k_lmk] fp32, caller slot order: ∂loss/∂lmk_w */
-  float* lmk_grad;            /* [2,H,S,kp,D] fp32 scratch of the tensor-core dK/dV
-                                 stage (landmark-slot dK, dV); unused by the SIMT family */
+  float* lmk_grad;            /* fp32 scratch of the tensor-core dK/dV stage:
+                                 (2·D + 1)·DSALT_LMK_SPLIT·H·S·kp floats (partial
+                                 landmark-slot dK, dV and d_lw); unused by the SIMT family */
+  float* qrec;                /* [H,T,DSALT_QREC_FLOATS] fp32 scratch: per-query records
+                                 (LSE, Delta, window, soft-edge factors) written by the
+                                 preprocess stage and read by the tensor-core dK/dV and dQ
+                                 stages; unused by the SIMT family */
   int32_t* status;            /* device status word or NULL */
   /* sizes */
   int64_t T;

@@ -46,6 +46,16 @@ def test_struct_layouts_match():
         assert lib.dsalt_b200_params_sizeof(i) == ctypes.sizeof(st), st.__name__
 
 
+def test_header_constants_match_mirror():
+    """ABI version and the landmark-split constant that sizes the dK/dV scratch."""
+    from dsalt.kernels import _ext
+    txt = HEADER.read_text()
+    assert int(re.search(r"#define DSALT_B200_ABI_VERSION (\d+)", txt).group(1)) == _ext.ABI_VERSION
+    assert int(re.search(r"#define DSALT_LMK_SPLIT (\d+)", txt).group(1)) == _ext.LMK_SPLIT
+    assert int(re.search(r"#define DSALT_QREC_FLOATS (\d+)", txt).group(1)) == _ext.QREC_FLOATS
+    assert _ext.load().dsalt_b200_abi_version() == _ext.ABI_VERSION
+
+
 def test_status_strings():
     from dsalt.kernels import _ext
     assert _ext.status_string(0) == "ok"

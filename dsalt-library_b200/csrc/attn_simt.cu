@@ -326,10 +326,34 @@ bwd_preprocess_vec_kernel(const DsaltAttnParams p) {
   }
 #pragma unroll
   for (int off = G / 2; off > 0; off >>= 1) s += __shfl_xor_sync(0xffffffffu, s, off);
-  if (chunk < n_chunks && (threadIdx.x & (G - 1)) == 0) {
-    const int64_t row = chunk / G;
-    p.delta[row] = s;
-    if (p.qrec) write_qrec(p, row / p.H, (int)(row % p.H), s);
+  const int gl = threadIdx.x & (G - 1);  // lane within the row's group
+  const int64_t row = chunk / G;
+  if (chunk < n_chunks && gl == 0) p.delta[row] = s;
+  if (!p.qrec) return;  // uniform over the grid
+  if constexpr (G >= 8) {
+    // the row's record: lane gl < 8 computes edge factor gl, lanes 0-3 write its four 16-byte parts
+    const bool in = chunk < n_chunks;
+    const int64_t t = in ? row / p.H : 0;
+    const int h = in ? (int)(row % p.H) : 0;
+    int d_e0 = 0;
+    QRec rec;
+    if (in) rec = qrec_fields(p, t, h, s, &d_e0);
+    const float eg = (in && gl < rec.ne && gl < kQRecEdge) ? qrec_edge_factor(rec.wt, d_e0 + gl, 1.0f / p.tau_win)
+                                                           : 1.0f;
+    const int base = threadIdx.x & 31 & ~(G - 1);
+    const int src = base + (gl == 3 ? 4 : 0);
+    float4 egv;
+    egv.x = __shfl_sync(0xffffffffu, eg, src + 0);
+    egv.y = __shfl_sync(0xffffffffu, eg, src + 1);
+    egv.z = __shfl_sync(0xffffffffu, eg, src + 2);
+    egv.w = __shfl_sync(0xffffffffu, eg, src + 3);
+    if (in && gl < 4) {
+      const float4 h0 = make_float4(rec.nlse2, rec.delta, __int_as_float(rec.lo), __int_as_float(rec.qi));
+      const float4 h1 = make_float4(rec.wlo, rec.wt, __int_as_float(rec.ehi), __int_as_float(rec.ne));
+      qrec_ptr(p, t, h)[gl] = gl == 0 ? h0 : gl == 1 ? h1 : egv;
+    }
+  } else {
+    if (chunk < n_chunks && gl == 0) write_qrec(p, row / p.H, (int)(row % p.H), s);
   }
 }
 

@@ -78,21 +78,23 @@ __device__ __forceinline__ void store_row32_packed(uint8_t* base, int row, int c
 // ======================================================================= dQ
 namespace dq {
 constexpr int BM = 128, BN = 64;
+constexpr int kKV = 3;           // K / V tile ring
 constexpr int kThreadsDQ = 352;  // row warps 0-7, TMA warp 8, MMA warps 9 (S, dQ) and 10 (dP)
 constexpr int kMmaWarpB = 10;
-enum { QD_FULL = 0, K_FULL = 1, V_FULL = 3, K_EMPTY = 5, V_EMPTY = 7, SD_FULL = 9, SD_EMPTY = 11, DS_FULL = 13,
-       DS_EMPTY = 15, DQ_DONE = 17, FINAL = 18, EPI = 20, NB = 21 };
+enum { QD_FULL = 0, K_FULL = 1, V_FULL = K_FULL + kKV, K_EMPTY = V_FULL + kKV, V_EMPTY = K_EMPTY + kKV,
+       SD_FULL = V_EMPTY + kKV, SD_EMPTY = SD_FULL + 2, DS_FULL = SD_EMPTY + 2, DS_EMPTY = DS_FULL + 2,
+       DQ_DONE = DS_EMPTY + 2, FINAL = DQ_DONE + 1, EPI = FINAL + 2, EPI2 = EPI + 1, NB = EPI2 + 1 };
 
 template <int D>
 struct alignas(1024) Smem {
   uint8_t q[BM * D * 2];
   uint8_t dO[BM * D * 2];
-  uint8_t k[2][BN * D * 2];
-  uint8_t v[2][BN * D * 2];
+  uint8_t k[kKV][BN * D * 2];
+  uint8_t v[kKV][BN * D * 2];
   uint8_t ds[2][BM * BN * 2];
   uint64_t bars[NB];
   uint32_t tmem_base;
-  int abort_flag, band_lo, band_hi, cnt_max, n_valid;
+  int abort_flag, band_lo, band_hi, cnt_max, n_valid, slow_edge;
   float dw_half[BM];
   int lmk_pos[kMaxLmk];
   float lmk_lw2[kMaxLmk];
@@ -115,11 +117,13 @@ __global__ void __launch_bounds__(kThreadsDQ, 1) tc_bwd_dq_kernel(const __grid_c
   const BarArray bar{smem_u32(&sm.bars[0])};
   if (tid == 0) {
     mbar_init(bar[QD_FULL], 1);
-    for (int st = 0; st < 2; ++st) {
+    for (int st = 0; st < kKV; ++st) {
       mbar_init(bar[K_FULL + st], 1);
       mbar_init(bar[V_FULL + st], 1);
       mbar_init(bar[K_EMPTY + st], 1);
       mbar_init(bar[V_EMPTY + st], 1);
+    }
+    for (int st = 0; st < 2; ++st) {
       mbar_init(bar[SD_FULL + st], 2);  // S (warp 9) and dP (warp 10)
       mbar_init(bar[SD_EMPTY + st], kRowThreads);
       mbar_init(bar[DS_FULL + st], kRowThreads);
@@ -129,14 +133,32 @@ __global__ void __launch_bounds__(kThreadsDQ, 1) tc_bwd_dq_kernel(const __grid_c
     mbar_init(bar[FINAL], 1);
     mbar_init(bar[FINAL + 1], 1);
     mbar_init(bar[EPI], kRowThreads);
+    mbar_init(bar[EPI2], kRowThreads);
     fence_mbar_init();
     sm.abort_flag = 0;
     sm.band_lo = INT_MAX;
     sm.band_hi = -1;
     sm.cnt_max = 0;
     sm.n_valid = 0;
+    sm.slow_edge = 0;
   }
   if (warp == kMmaWarp) tmem_alloc(smem_u32(&sm.tmem_base), 512);
+  // row r (TMEM lane) = 32·(warp % 4) + lane; column half = warp / 4.  The row's
+  // record (LSE, Δ, window, soft-edge factors) is loaded while the landmark
+  // positions are staged.
+  const int r = 32 * (warp & 3) + lane;
+  const int half = (warp >> 2) & 1;
+  const int i = m0 + r;
+  const bool row_ok = warp < 8 && i < L;
+  QRec rec;
+  if (row_ok) {
+    const float4* src = reinterpret_cast<const float4*>(p.qrec + ((int64_t)h * p.T + s0 + i) * DSALT_QREC_FLOATS);
+    float4* dst = reinterpret_cast<float4*>(&rec);
+#pragma unroll
+    for (int k = 0; k < DSALT_QREC_FLOATS / 4; ++k) dst[k] = __ldg(src + k);
+  } else {
+    rec.qi = INT_MIN;
+  }
   const int kp = p.kp;
   const int64_t lbase = ((int64_t)h * p.S + s) * kp;
   for (int c = tid; c < kp; c += kThreadsDQ) {
@@ -146,31 +168,30 @@ __global__ void __launch_bounds__(kThreadsDQ, 1) tc_bwd_dq_kernel(const __grid_c
     if (ps >= 0) atomicAdd(&sm.n_valid, 1);
   }
   __syncthreads();
-  // row r (TMEM lane) = 32·(warp % 4) + lane; column half = warp / 4
-  const int r = 32 * (warp & 3) + lane;
-  const int half = (warp >> 2) & 1;
-  const int i = m0 + r;
-  const bool row_ok = warp < 8 && i < L;
-  RowWindow rw = {};
+  if (warp == kProducerWarp && lane == 0) {
+    // Q and dO depend only on the block
+    mbar_expect_tx(bar[QD_FULL], 2 * BM * D * 2);
+#pragma unroll
+    for (int c = 0; c < D / 64; ++c) {
+      tma_load_3d(smem_u32(sm.q + c * (BM * 128)), &a.tm_q, bar[QD_FULL], c * 64, h, (int)(s0 + m0));
+      tma_load_3d(smem_u32(sm.dO + c * (BM * 128)), &a.tm_do, bar[QD_FULL], c * 64, h, (int)(s0 + m0));
+    }
+  }
+  const bool row_live = row_ok && rec.qi != INT_MIN;  // a row without keys has no gradient
   int lo = INT_MAX, hi = -1, cnt = 0;
-  float lse2 = -INFINITY, delta = 0.f;
-  if (row_ok) {
-    const int64_t row = (s0 + i) * p.H + h;
-    lse2 = __ldg(p.lse + row) * kLog2e;
-    delta = __ldg(p.delta + row);
-    rw = row_window(__ldg(p.w + s0 + i), i, p.semantics, p.win_edge);
-    if (rw.W >= 0) { lo = i - min(rw.W, i); hi = i; }
+  if (row_live) {
+    if (rec.lo != INT_MAX) { lo = rec.lo; hi = i; }
     int a0 = 0, a1 = sm.n_valid;
     while (a0 < a1) {
       const int mid = (a0 + a1) >> 1;
       const int ps = sm.lmk_pos[mid];
-      if (ps <= i && (float)ps < rw.win_lo) a0 = mid + 1; else a1 = mid;
+      if (ps <= i && (float)ps < rec.wlo) a0 = mid + 1; else a1 = mid;
     }
     cnt = a0;
-    if (lse2 == -INFINITY) { lo = INT_MAX; hi = -1; cnt = 0; }  // empty row: no gradient
     if (half == 0) {
       if (lo <= hi) { atomicMin(&sm.band_lo, lo); atomicMax(&sm.band_hi, hi); }
       if (cnt > 0) atomicMax(&sm.cnt_max, cnt);
+      if (rec.ne > kMaxEdge) atomicOr(&sm.slow_edge, 1);
     }
   }
   tc_fence_before();
@@ -190,22 +211,14 @@ __global__ void __launch_bounds__(kThreadsDQ, 1) tc_bwd_dq_kernel(const __grid_c
   const uint32_t tS = tmem, tdP = tmem + 2 * BN, tdQ = tmem + 4 * BN;
 
   if (warp == kProducerWarp) {
-    // lane 0: Q, dO, K tiles; lane 1: V tiles
+    // lane 0: K tiles; lane 1: V tiles
     if (lane < 2 && n_tiles > 0) {
       const bool is_k = lane == 0;
-      if (is_k) {
-        mbar_expect_tx(bar[QD_FULL], 2 * BM * D * 2);
-#pragma unroll
-        for (int c = 0; c < D / 64; ++c) {
-          tma_load_3d(smem_u32(sm.q + c * (BM * 128)), &a.tm_q, bar[QD_FULL], c * 64, h, (int)(s0 + m0));
-          tma_load_3d(smem_u32(sm.dO + c * (BM * 128)), &a.tm_do, bar[QD_FULL], c * 64, h, (int)(s0 + m0));
-        }
-      }
       const int FULL = is_k ? K_FULL : V_FULL, EMPTY = is_k ? K_EMPTY : V_EMPTY;
       int issued = 0;
       for (int t = 0; t < n_tiles; ++t) {
-        const int st = t & 1;
-        if (t >= 2 && !mbar_wait(bar[EMPTY + st], ((t >> 1) - 1) & 1, abort_flag, p.status)) break;
+        const int st = t % kKV;
+        if (t >= kKV && !mbar_wait(bar[EMPTY + st], (t / kKV - 1) & 1, abort_flag, p.status)) break;
         const bool lmk = t < n_lt;
         mbar_expect_tx(bar[FULL + st], (lmk ? a.lmk_box : BN) * D * 2);
         uint8_t* dst = is_k ? sm.k[st] : sm.v[st];
@@ -218,9 +231,9 @@ __global__ void __launch_bounds__(kThreadsDQ, 1) tc_bwd_dq_kernel(const __grid_c
         }
         issued = t + 1;
       }
-      for (int t = max(0, issued - 2); t < issued; ++t) mbar_drain(bar[FULL + (t & 1)], (t >> 1) & 1);
-      if (is_k) mbar_drain(bar[QD_FULL], 0);
+      for (int t = max(0, issued - kKV); t < issued; ++t) mbar_drain(bar[FULL + t % kKV], (t / kKV) & 1);
     }
+    if (lane == 0) mbar_drain(bar[QD_FULL], 0);
   } else if (warp == kMmaWarp) {
     // S = Q·Kᵀ two tiles ahead and dQ += dS·K (warp 10 issues dP = dO·Vᵀ alongside)
     if (lane == 0 && n_tiles > 0) {
@@ -229,11 +242,11 @@ __global__ void __launch_bounds__(kThreadsDQ, 1) tc_bwd_dq_kernel(const __grid_c
       const uint32_t q_addr = smem_u32(sm.q);
       bool ok = mbar_wait(bar[QD_FULL], 0, abort_flag, p.status);
       auto issue_s = [&](int t) -> bool {
-        const int st = t & 1;
-        if (!mbar_wait(bar[K_FULL + st], (t >> 1) & 1, abort_flag, p.status)) return false;
+        const int st = t & 1, ks = t % kKV;
+        if (!mbar_wait(bar[K_FULL + ks], (t / kKV) & 1, abort_flag, p.status)) return false;
         if (t >= 2 && !mbar_wait(bar[SD_EMPTY + st], ((t >> 1) - 1) & 1, abort_flag, p.status)) return false;
         tc_fence_after();
-        const uint32_t k_addr = smem_u32(sm.k[st]);
+        const uint32_t k_addr = smem_u32(sm.k[ks]);
 #pragma unroll
         for (int kk = 0; kk < D / 16; ++kk) {
           const uint32_t aoff = (kk >> 2) * (BM * 128) + (kk & 3) * 32;
@@ -247,16 +260,16 @@ __global__ void __launch_bounds__(kThreadsDQ, 1) tc_bwd_dq_kernel(const __grid_c
       if (ok) ok = issue_s(0);
       if (ok && n_tiles > 1) ok = issue_s(1);
       for (int t = 0; ok && t < n_tiles; ++t) {
-        const int st = t & 1;
+        const int st = t & 1, ks = t % kKV;
         if (!mbar_wait(bar[DS_FULL + st], (t >> 1) & 1, abort_flag, p.status)) { ok = false; break; }
         tc_fence_after();
-        const uint32_t ds_addr = smem_u32(sm.ds[st]), k_addr = smem_u32(sm.k[st]);
+        const uint32_t ds_addr = smem_u32(sm.ds[st]), k_addr = smem_u32(sm.k[ks]);
         const int nk = tile_n(t) / 16;
         for (int kk = 0; kk < nk; ++kk)
           mma_f16(tdQ, sdesc_sw128(ds_addr + kk * 32, 16, 1024), sdesc_sw128(k_addr + kk * 2048, BN * 128, 1024),
                   id_dq, (t > 0 || kk > 0) ? 1u : 0u);
         mma_commit(bar[DS_EMPTY + st]);
-        mma_commit(bar[K_EMPTY + st]);
+        mma_commit(bar[K_EMPTY + ks]);
         if (t + 2 < n_tiles && !issue_s(t + 2)) { ok = false; break; }
       }
       mma_commit(bar[DQ_DONE]);
@@ -270,11 +283,11 @@ __global__ void __launch_bounds__(kThreadsDQ, 1) tc_bwd_dq_kernel(const __grid_c
       const uint32_t do_addr = smem_u32(sm.dO);
       bool ok = mbar_wait(bar[QD_FULL], 0, abort_flag, p.status);
       for (int t = 0; ok && t < n_tiles; ++t) {
-        const int st = t & 1;
-        if (!mbar_wait(bar[V_FULL + st], (t >> 1) & 1, abort_flag, p.status)) break;
+        const int st = t & 1, ks = t % kKV;
+        if (!mbar_wait(bar[V_FULL + ks], (t / kKV) & 1, abort_flag, p.status)) break;
         if (t >= 2 && !mbar_wait(bar[SD_EMPTY + st], ((t >> 1) - 1) & 1, abort_flag, p.status)) break;
         tc_fence_after();
-        const uint32_t v_addr = smem_u32(sm.v[st]);
+        const uint32_t v_addr = smem_u32(sm.v[ks]);
 #pragma unroll
         for (int kk = 0; kk < D / 16; ++kk) {
           const uint32_t aoff = (kk >> 2) * (BM * 128) + (kk & 3) * 32;
@@ -283,7 +296,7 @@ __global__ void __launch_bounds__(kThreadsDQ, 1) tc_bwd_dq_kernel(const __grid_c
                   id_s, kk > 0 ? 1u : 0u);
         }
         mma_commit(bar[SD_FULL + st]);
-        mma_commit(bar[V_EMPTY + st]);
+        mma_commit(bar[V_EMPTY + ks]);
       }
       mma_commit(bar[FINAL + 1]);
       mbar_drain(bar[FINAL + 1], 0);
@@ -294,8 +307,10 @@ __global__ void __launch_bounds__(kThreadsDQ, 1) tc_bwd_dq_kernel(const __grid_c
     const int c0 = BN / 2 * half;  // first tile column of this thread
     const float sl2 = p.scale * kLog2e;
     const float inv_tau = 1.0f / p.tau_win;
-    int d_e0 = INT_MAX;
-    if (row_ok && rw.W >= 0) d_e0 = max((int)floorf(rw.core) + 1, 0);
+    const bool slow_edge = sm.slow_edge != 0;
+    const float nlse2 = row_live ? rec.nlse2 : 0.f;
+    const float delta = row_live ? rec.delta : 0.f;
+    const int ne = row_live ? rec.ne : 0, ehi = rec.ehi;
     float dw = 0.f;
     bool ok = true;
     for (int t = 0; t < n_tiles; ++t) {
@@ -303,30 +318,38 @@ __global__ void __launch_bounds__(kThreadsDQ, 1) tc_bwd_dq_kernel(const __grid_c
       ok = mbar_wait(bar[SD_FULL + st], (t >> 1) & 1, abort_flag, p.status);
       if (!__all_sync(0xffffffffu, ok)) { ok = false; break; }
       tc_fence_after();
-      float sv[32], dpv[32];
-      tmem_ld32(tS + lane_addr + st * BN + c0, sv);
-      tmem_ld32(tdP + lane_addr + st * BN + c0, dpv);
-      tmem_wait_ld();
-      tc_fence_before();
-      mbar_arrive(bar[SD_EMPTY + st]);
       const bool lmk = t < n_lt;
       const int n0 = lmk ? 0 : band_lo + BN * (t - n_lt);
-      if (lmk) {
-        const int climit = cnt - BN * t - c0;
+      // valid columns of this thread: [vlo, vhi]
+      const int vlo = lmk ? 0 : lo - n0 - c0;  // lo = INT_MAX for a row without band: stays positive
+      const int vhi = lmk ? cnt - BN * t - c0 - 1 : hi - n0 - c0;
+      const bool all_in = __all_sync(0xffffffffu, vlo <= 0 && vhi >= 31);
+      const bool all_out = __all_sync(0xffffffffu, vhi < 0 || vlo > 31 || vlo > vhi);
+      uint32_t pk[16];
+      if (all_out) {
+        tc_fence_before();
+        mbar_arrive(bar[SD_EMPTY + st]);
+#pragma unroll
+        for (int g = 0; g < 16; ++g) pk[g] = 0u;
+      } else {
+        float sv[32], dpv[32];
+        tmem_ld32(tS + lane_addr + st * BN + c0, sv);
+        tmem_ld32(tdP + lane_addr + st * BN + c0, dpv);
+        tmem_wait_ld();
+        tc_fence_before();
+        mbar_arrive(bar[SD_EMPTY + st]);
         const float* lw2 = sm.lmk_lw2 + BN * t + c0;
 #pragma unroll
-        for (int c = 0; c < 32; ++c) {
-          const float pr = fast_exp2(fmaf(sv[c], sl2, lw2[c] - lse2));
-          const float dsv = pr * (dpv[c] - delta);
-          sv[c] = (c < climit) ? dsv : 0.f;
-        }
-      } else {
-        const int clo = lo - n0 - c0, chi = hi - n0 - c0;
+        for (int c = 0; c < 32; c += 2) {
+          float d2[2];
 #pragma unroll
-        for (int c = 0; c < 32; ++c) {
-          const float pr = fast_exp2(fmaf(sv[c], sl2, -lse2));
-          const float dsv = pr * (dpv[c] - delta);
-          sv[c] = (c >= clo && c <= chi) ? dsv : 0.f;
+          for (int e = 0; e < 2; ++e) {
+            const float bias = lmk ? lw2[c + e] + nlse2 : nlse2;
+            const float pr = fast_exp2(fmaf(sv[c + e], sl2, bias));
+            const float dsv = pr * (dpv[c + e] - delta);
+            d2[e] = (all_in || (c + e >= vlo && c + e <= vhi)) ? dsv : 0.f;
+          }
+          pk[c / 2] = pack2(d2[0], d2[1], kBF16);
         }
       }
       if (t >= 2) {
@@ -334,19 +357,41 @@ __global__ void __launch_bounds__(kThreadsDQ, 1) tc_bwd_dq_kernel(const __grid_c
         if (!__all_sync(0xffffffffu, ok)) { ok = false; break; }
       }
       uint8_t* dsb = sm.ds[st];
-      store_row32<kBF16>(dsb, r, c0, sv);
-      if (!lmk && row_ok && lo <= hi && d_e0 <= rw.W) {
-        // soft window edge on this thread's half: dS *= σ((w̃ − d)/τ); ∂loss/∂w̃ += dS·(1 − σ)/τ
-        const int d_hi = min(min(rw.W, i), i - n0 - c0);
-        const int d_lo = max(d_e0, i - (n0 + c0 + 31));
-        for (int d = d_lo; d <= d_hi; ++d) {
-          const int c = i - d - n0;
-          T* e = reinterpret_cast<T*>(dsb + sw128_offset(r, c));
-          const float z = (rw.wt - (float)d) * inv_tau;
-          const float sg = 1.0f / (1.0f + expf(-z));
-          const float v = to_f32<T>(*e) * sg;
-          *e = from_f32<T>(v);
-          dw = fmaf(v, (1.0f - sg) * inv_tau, dw);
+      store_row32_packed(dsb, r, c0, pk);
+      if (!lmk && !all_out) {
+        // soft window edge on this thread's half: dS *= σ((w̃ − d)/τ); ∂loss/∂w̃ += dS·(1 − σ)/τ.
+        // The key at edge index e (distance d_e0 + e) sits in column ehi − e − n0 − c0.
+        const int ce0 = ehi - n0 - c0;
+        const bool has = ne > 0 && ce0 >= 0 && ce0 - (ne - 1) <= 31;
+        if (!slow_edge) {
+          if (__any_sync(0xffffffffu, has)) {
+            float pv[kMaxEdge];
+#pragma unroll
+            for (int e = 0; e < kMaxEdge; ++e) {
+              const int c = ce0 - e;
+              const bool in = has && e < ne && c >= 0 && c < 32;
+              pv[e] = in ? to_f32<T>(*reinterpret_cast<const T*>(dsb + sw128_offset(r, c0 + c))) : 0.f;
+            }
+#pragma unroll
+            for (int e = 0; e < kMaxEdge; ++e) {
+              const int c = ce0 - e;
+              if (has && e < ne && c >= 0 && c < 32) {
+                const float v = pv[e] * rec.eg[e];
+                *reinterpret_cast<T*>(dsb + sw128_offset(r, c0 + c)) = from_f32<T>(v);
+                dw = fmaf(v, (1.0f - rec.eg[e]) * inv_tau, dw);
+              }
+            }
+          }
+        } else if (has) {
+          const int d_e0 = i - ehi;
+          for (int e = max(0, ce0 - 31); e < ne && ce0 - e >= 0; ++e) {
+            const int c = ce0 - e;
+            T* ep = reinterpret_cast<T*>(dsb + sw128_offset(r, c0 + c));
+            const float sg = qrec_edge_factor(rec.wt, d_e0 + e, inv_tau);
+            const float v = to_f32<T>(*ep) * sg;
+            *ep = from_f32<T>(v);
+            dw = fmaf(v, (1.0f - sg) * inv_tau, dw);
+          }
         }
       }
       fence_async_smem();
@@ -357,37 +402,50 @@ __global__ void __launch_bounds__(kThreadsDQ, 1) tc_bwd_dq_kernel(const __grid_c
       ok = __all_sync(0xffffffffu, ok);
       tc_fence_after();
     }
-    // dQ columns [half·D/2, (half+1)·D/2) of row r
-    const int64_t row_off = (s0 + i) * (int64_t)p.H * D + (int64_t)h * D;
-    T* dqo = reinterpret_cast<T*>(p.dq) + row_off;
-#pragma unroll
-    for (int ch = 0; ch < D / 64; ++ch) {
-      const int col = half * (D / 2) + ch * 32;
-      float o[32];
-      if (ok && n_tiles > 0) {
-        tmem_ld32(tdQ + lane_addr + col, o);
-        tmem_wait_ld();
-      } else {
-#pragma unroll
-        for (int j = 0; j < 32; ++j) o[j] = 0.f;
-      }
-      if (row_ok) {
-#pragma unroll
-        for (int j = 0; j < 32; j += 8) {
-          uint4 u;
-          u.x = pack2(o[j + 0] * p.scale, o[j + 1] * p.scale, kBF16);
-          u.y = pack2(o[j + 2] * p.scale, o[j + 3] * p.scale, kBF16);
-          u.z = pack2(o[j + 4] * p.scale, o[j + 5] * p.scale, kBF16);
-          u.w = pack2(o[j + 6] * p.scale, o[j + 7] * p.scale, kBF16);
-          *reinterpret_cast<uint4*>(dqo + col + j) = u;
-        }
-      }
-    }
     // ∂loss/∂w̃ of the row: sum of the two halves
     if (half == 1) sm.dw_half[r] = dw;
     mbar_arrive(bar[EPI]);
     const bool ok2 = mbar_wait(bar[EPI], 0, abort_flag, p.status);
     if (half == 0 && row_ok && p.dw_head) p.dw_head[(s0 + i) * p.H + h] = (ok && ok2) ? dw + sm.dw_half[r] : 0.f;
+    if (ok && ok2) {
+      // dQ rows staged in the (now idle) K ring, 16-byte units XOR-swizzled by
+      // row % 8, then stored row-contiguously
+      constexpr int kUnits = D * 2 / 16;
+      uint8_t* stage = sm.k[0];
+#pragma unroll
+      for (int ch = 0; ch < D / 32; ++ch) {  // 16 columns at a time
+        const int col = half * (D / 2) + ch * 16;
+        float o[16];
+        if (n_tiles > 0) {
+          tmem_ld16(tdQ + lane_addr + col, o);
+          tmem_wait_ld();
+        } else {
+#pragma unroll
+          for (int j = 0; j < 16; ++j) o[j] = 0.f;
+        }
+#pragma unroll
+        for (int j = 0; j < 16; j += 8) {
+          const int un = (col + j) / 8;
+          uint4 u;
+          u.x = pack2(o[j + 0] * p.scale, o[j + 1] * p.scale, kBF16);
+          u.y = pack2(o[j + 2] * p.scale, o[j + 3] * p.scale, kBF16);
+          u.z = pack2(o[j + 4] * p.scale, o[j + 5] * p.scale, kBF16);
+          u.w = pack2(o[j + 6] * p.scale, o[j + 7] * p.scale, kBF16);
+          *reinterpret_cast<uint4*>(stage + r * (kUnits * 16) + ((un ^ (r & 7)) << 4)) = u;
+        }
+      }
+      mbar_arrive(bar[EPI2]);
+      if (__all_sync(0xffffffffu, mbar_wait(bar[EPI2], 0, abort_flag, p.status))) {
+        const int rows = min(BM, L - m0);
+        const int64_t HD = (int64_t)p.H * D;
+        uint8_t* dqg = reinterpret_cast<uint8_t*>(p.dq) + ((s0 + m0) * HD + (int64_t)h * D) * 2;
+        for (int un = tid; un < rows * kUnits; un += kRowThreads) {
+          const int rr = un / kUnits, uu = un % kUnits;
+          *reinterpret_cast<uint4*>(dqg + rr * HD * 2 + uu * 16) =
+              *reinterpret_cast<const uint4*>(stage + rr * (kUnits * 16) + ((uu ^ (rr & 7)) << 4));
+        }
+      }
+    }
   }
   tc_fence_before();
   __syncthreads();

@@ -132,13 +132,13 @@ struct alignas(16) QRec {
 };
 static_assert(sizeof(QRec) == DSALT_QREC_FLOATS * 4, "record size");
 
-// Record of query token t (global index), head h, given its Δ.
-__device__ __forceinline__ void write_qrec(const DsaltAttnParams& p, int64_t t, int h, float delta) {
+// Record fields of query token t (global index), head h, given its Δ; the
+// soft-edge factors are left to qrec_edge_factor (d_e0: first edge distance).
+__device__ __forceinline__ QRec qrec_fields(const DsaltAttnParams& p, int64_t t, int h, float delta, int* d_e0) {
   QRec rec;
   rec.nlse2 = 0.f; rec.delta = 0.f; rec.lo = INT_MAX; rec.qi = INT_MIN;
   rec.wlo = -INFINITY; rec.wt = 0.f; rec.ehi = INT_MIN; rec.ne = 0;
-#pragma unroll
-  for (int e = 0; e < kQRecEdge; ++e) rec.eg[e] = 1.0f;
+  *d_e0 = 0;
   const float lse = p.lse[t * p.H + h];
   if (lse != -INFINITY) {
     const int s = find_seq(p.cu_seqlens, p.S, t);
@@ -151,18 +151,32 @@ __device__ __forceinline__ void write_qrec(const DsaltAttnParams& p, int64_t t, 
     rec.wt = rw.wt;
     if (rw.W >= 0) {
       rec.lo = i - min(rw.W, i);
-      const int d_e0 = max((int)floorf(rw.core) + 1, 0);
-      if (d_e0 <= rw.W) {
-        rec.ehi = i - d_e0;
+      const int de = max((int)floorf(rw.core) + 1, 0);
+      if (de <= rw.W) {
+        rec.ehi = i - de;
         rec.ne = max(rec.ehi - rec.lo + 1, 0);
-        const float inv_tau = 1.0f / p.tau_win;
-#pragma unroll
-        for (int e = 0; e < kQRecEdge; ++e)
-          if (e < rec.ne) rec.eg[e] = 1.0f / (1.0f + expf(-((rw.wt - (float)(d_e0 + e)) * inv_tau)));
+        *d_e0 = de;
       }
     }
   }
-  float4* dst = reinterpret_cast<float4*>(p.qrec + ((int64_t)h * p.T + t) * DSALT_QREC_FLOATS);
+  return rec;
+}
+// σ((w̃ − d)/τ) of the soft-edge key at distance d
+__device__ __forceinline__ float qrec_edge_factor(float wt, int d, float inv_tau) {
+  return 1.0f / (1.0f + expf(-((wt - (float)d) * inv_tau)));
+}
+__device__ __forceinline__ float4* qrec_ptr(const DsaltAttnParams& p, int64_t t, int h) {
+  return reinterpret_cast<float4*>(p.qrec + ((int64_t)h * p.T + t) * DSALT_QREC_FLOATS);
+}
+
+// The whole record of one (token, head) from one thread.
+__device__ __forceinline__ void write_qrec(const DsaltAttnParams& p, int64_t t, int h, float delta) {
+  int d_e0;
+  QRec rec = qrec_fields(p, t, h, delta, &d_e0);
+  const float inv_tau = 1.0f / p.tau_win;
+#pragma unroll
+  for (int e = 0; e < kQRecEdge; ++e) rec.eg[e] = e < rec.ne ? qrec_edge_factor(rec.wt, d_e0 + e, inv_tau) : 1.0f;
+  float4* dst = qrec_ptr(p, t, h);
   const float4* src = reinterpret_cast<const float4*>(&rec);
 #pragma unroll
   for (int k = 0; k < DSALT_QREC_FLOATS / 4; ++k) dst[k] = src[k];

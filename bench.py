@@ -47,7 +47,12 @@ WORKLOADS = {
 FLOPS_PER_PAIR = {"dsalt_attn_fwd": 4, "dsalt_attn_bwd_dkdv": 8, "dsalt_attn_bwd_dq": 2}
 # kernels launched by each C-ABI entry point
 KERNELS_PER_CALL = {"dsalt_build_schedule": 2, "dsalt_gather_landmarks": 1, "dsalt_attn_fwd": 1,
-                    "dsalt_attn_bwd_preprocess": 1, "dsalt_attn_bwd_dkdv": 1, "dsalt_attn_bwd_dq": 2}
+                    "dsalt_attn_bwd_preprocess": 1, "dsalt_attn_bwd_dkdv": 2, "dsalt_attn_bwd_dq": 2}
+# DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) per call of each entry point,
+# summed over its kernels, from one ncu capture of a config-2 step; the capture and the
+# command are in profiles/traffic_step_config2.txt
+NCU_TRAFFIC_BYTES = {"config2": {"dsalt_attn_fwd": 361505280, "dsalt_attn_bwd_preprocess": 240444928,
+                                 "dsalt_attn_bwd_dkdv": 555088128, "dsalt_attn_bwd_dq": 338497024}}
 CLOCK_REASONS = {0x1: "gpu_idle", 0x2: "applications_clocks_setting", 0x4: "sw_power_cap",
                  0x8: "hw_slowdown", 0x10: "sync_boost", 0x20: "sw_thermal_slowdown",
                  0x40: "hw_thermal_slowdown", 0x80: "hw_power_brake_slowdown", 0x100: "display_clock_setting"}
@@ -339,8 +344,9 @@ def main():
         kern = {n: (sum(v) / len(v), sum(v)) for n, v in per_kernel.items()}
         dom = max((n for n in kern if n in FLOPS_PER_PAIR), key=lambda n: kern[n][1])
         ach = FLOPS_PER_PAIR[dom] * d["D"] * pairs / (kern[dom][0] / 1e3) / 1e12
+        traffic = NCU_TRAFFIC_BYTES.get(args.workload, {}).get(dom)
         roof = {"bound": "tensor", "kernel": dom, "achieved": ach, "peak": sustained, "unit": UNIT,
-                "frac": ach / sustained, "traffic": None,
+                "frac": ach / sustained, "traffic": traffic, "traffic_unit": "bytes per call (ncu dram read+write)",
                 "peak_source": f"{src} bf16_tflops_sustained (kernel timed inside a long step loop)"}
         line = {"metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
                 "warmup": max(args.warmup, 3), "ms_per_step": ms_max / args.steps, "higher_is_better": True,

@@ -338,7 +338,7 @@ bwd_preprocess_vec_kernel(const DsaltAttnParams p) {
     int d_e0 = 0;
     QRec rec;
     if (in) rec = qrec_fields(p, t, h, s, &d_e0);
-    const float eg = (in && gl < rec.ne && gl < kQRecEdge) ? qrec_edge_factor(rec.wt, d_e0 + gl, 1.0f / p.tau_win)
+    const float eg = (in && gl < qrec_ne(rec) && gl < kQRecEdge) ? qrec_edge_factor(rec.wt, d_e0 + gl, 1.0f / p.tau_win)
                                                            : 1.0f;
     const int base = threadIdx.x & 31 & ~(G - 1);
     const int src = base + (gl == 3 ? 4 : 0);
@@ -349,7 +349,7 @@ bwd_preprocess_vec_kernel(const DsaltAttnParams p) {
     egv.w = __shfl_sync(0xffffffffu, eg, src + 3);
     if (in && gl < 4) {
       const float4 h0 = make_float4(rec.nlse2, rec.delta, __int_as_float(rec.lo), __int_as_float(rec.qi));
-      const float4 h1 = make_float4(rec.wlo, rec.wt, __int_as_float(rec.ehi), __int_as_float(rec.ne));
+      const float4 h1 = make_float4(__int_as_float(rec.ehi), __int_as_float(rec.elo), rec.wlo, rec.wt);
       qrec_ptr(p, t, h)[gl] = gl == 0 ? h0 : gl == 1 ? h1 : egv;
     }
   } else {

@@ -33,7 +33,6 @@ cudaError_t simt_attention_stage(int stage, const DsaltAttnParams& p, cudaStream
 
 namespace bwd {
 
-constexpr int kThreads = 320;
 constexpr int kRowThreads = 256;
 constexpr int kProducerWarp = 8;
 constexpr int kMmaWarp = 9;
@@ -191,7 +190,7 @@ __global__ void __launch_bounds__(kThreadsDQ, 1) tc_bwd_dq_kernel(const __grid_c
     if (half == 0) {
       if (lo <= hi) { atomicMin(&sm.band_lo, lo); atomicMax(&sm.band_hi, hi); }
       if (cnt > 0) atomicMax(&sm.cnt_max, cnt);
-      if (rec.ne > kMaxEdge) atomicOr(&sm.slow_edge, 1);
+      if (qrec_ne(rec) > kMaxEdge) atomicOr(&sm.slow_edge, 1);
     }
   }
   tc_fence_before();
@@ -310,7 +309,7 @@ __global__ void __launch_bounds__(kThreadsDQ, 1) tc_bwd_dq_kernel(const __grid_c
     const bool slow_edge = sm.slow_edge != 0;
     const float nlse2 = row_live ? rec.nlse2 : 0.f;
     const float delta = row_live ? rec.delta : 0.f;
-    const int ne = row_live ? rec.ne : 0, ehi = rec.ehi;
+    const int ne = row_live ? qrec_ne(rec) : 0, ehi = rec.ehi;
     float dw = 0.f;
     bool ok = true;
     for (int t = 0; t < n_tiles; ++t) {
@@ -459,9 +458,18 @@ namespace dkv {
 constexpr int BM = 128, BN = 64;  // BM keys (TMEM lanes), BN queries per tile
 constexpr int kQStages = 3;       // Q / dO tile ring
 constexpr int kColStages = 4;     // per-tile column data ring
-constexpr int kThreadsKV = 384;   // row warps 0-7, TMA warp 8, MMA warps 9 and 11, column warp 10
-constexpr int kColWarp = 10;
-constexpr int kMmaWarpB = 11;     // issues dPᵀ and dK (warp 9: Sᵀ and dV)
+// 16 row warps: warp w reads TMEM lanes 32·(w % 4)… and owns the 16-column
+// quarter w / 4 of every tile (four warps per scheduler hide the latencies of
+// the element-wise work); then the TMA warp, MMA warp A (TMEM owner: Sᵀ, dV),
+// the column warp and MMA warp B (dPᵀ, dK)
+constexpr int kRowWarps = 16;
+constexpr int kRowThreads = 32 * kRowWarps;
+constexpr int kProducerWarp = 16;
+constexpr int kMmaWarp = 17;
+constexpr int kColWarp = 18;
+constexpr int kMmaWarpB = 19;
+constexpr int kThreadsKV = 640;
+constexpr int kQuarter = BN / 4;  // tile columns per row thread
 enum { KV_FULL = 0, Q_FULL = 1, DO_FULL = Q_FULL + kQStages, QDO_EMPTY = DO_FULL + kQStages,
        REC_FULL = QDO_EMPTY + kQStages, COL_FULL = REC_FULL + kColStages, COL_EMPTY = COL_FULL + kColStages,
        SD_FULL = COL_EMPTY + kColStages,
@@ -470,9 +478,9 @@ enum { KV_FULL = 0, Q_FULL = 1, DO_FULL = Q_FULL + kQStages, QDO_EMPTY = DO_FULL
 
 // per-tile summary of the query records, written by the column warp
 struct alignas(16) ColStats {
-  int lo_max[2], lo_min[2], qi_min[2], qi_max[2];  // per column half: mask skipping
-  float wlo_min[2];
-  int has_edge;  // some soft-edge key of the tile falls in this block's keys
+  int lo_max[4], lo_min[4], qi_min[4], qi_max[4];  // per 16-column quarter: mask skipping
+  float wlo_min[4];
+  int elo_min[4], ehi_max[4];  // per quarter: the soft-edge keys of its columns lie in [elo_min, ehi_max]
 };
 
 template <int D>
@@ -488,7 +496,7 @@ struct alignas(1024) Smem {
   int abort_flag;
   QRec rec[kColStages][BN];  // the tile's query records (bulk-copied, then fixed up)
   ColStats stats[kColStages];
-  float dlw_half[BM];
+  float dlw_part[4][BM];  // landmark items: d_lw partial sums of the four column quarters
 };
 
 template <bool LMK, typename T, int D>
@@ -618,7 +626,6 @@ __global__ void __launch_bounds__(kThreadsKV, 1) tc_bwd_dkdv_kernel(const __grid
     // Lane 0 bulk-copies each tile's records (written by the preprocess stage)
     // kColStages − 1 tiles ahead; the warp then masks the columns past the
     // sequence end and summarises the tile for the row warps' mask skipping.
-    const int key_last = key0 + nkeys - 1;
     const QRec* recg = reinterpret_cast<const QRec*>(p.qrec) + (int64_t)h * p.T + s0;
     auto issue = [&](int u) {
       const int st = u % kColStages;
@@ -635,23 +642,23 @@ __global__ void __launch_bounds__(kThreadsKV, 1) tc_bwd_dkdv_kernel(const __grid
       if (!__all_sync(0xffffffffu, mbar_wait(bar[REC_FULL + st], (u / kColStages) & 1, abort_flag, p.status)))
         break;
       const int q0 = q_start + BN * u;
-      int st_lo_max[2], st_lo_min[2], st_qi_min[2], st_qi_max[2];
+      // per lane: columns lane (quarter lane/16) and lane + 32 (quarter 2 + lane/16)
+      int st_lo_max[2], st_lo_min[2], st_qi_min[2], st_qi_max[2], st_elo_min[2], st_ehi_max[2];
       float st_wlo_min[2];
-      bool edge_here = false;
 #pragma unroll
       for (int k2 = 0; k2 < 2; ++k2) {
         const int c = lane + 32 * k2;
         QRec& rc = sm.rec[st][c];
         if (q0 + c >= L) {  // another sequence's query (or past the array): no pairs
           rc.nlse2 = 0.f; rc.delta = 0.f; rc.lo = INT_MAX; rc.qi = INT_MIN;
-          rc.wlo = -INFINITY; rc.ehi = INT_MIN; rc.ne = 0;
+          rc.wlo = -INFINITY; rc.ehi = INT_MIN; rc.elo = INT_MAX;
         }
-        const int clo = rc.lo, ci = rc.qi, ehi = rc.ehi, ne = rc.ne;
-        if (!LMK && ne > 0 && ehi >= key0 && ehi - (ne - 1) <= key_last) edge_here = true;
+        const int clo = rc.lo, ci = rc.qi;
         st_lo_max[k2] = clo; st_lo_min[k2] = clo; st_qi_min[k2] = ci; st_qi_max[k2] = ci; st_wlo_min[k2] = rc.wlo;
+        st_elo_min[k2] = rc.elo; st_ehi_max[k2] = rc.ehi;
       }
 #pragma unroll
-      for (int off = 16; off > 0; off >>= 1) {
+      for (int off = 8; off > 0; off >>= 1) {  // within 16-lane groups
 #pragma unroll
         for (int k2 = 0; k2 < 2; ++k2) {
           st_lo_max[k2] = max(st_lo_max[k2], __shfl_xor_sync(0xffffffffu, st_lo_max[k2], off));
@@ -659,17 +666,19 @@ __global__ void __launch_bounds__(kThreadsKV, 1) tc_bwd_dkdv_kernel(const __grid
           st_qi_min[k2] = min(st_qi_min[k2], __shfl_xor_sync(0xffffffffu, st_qi_min[k2], off));
           st_qi_max[k2] = max(st_qi_max[k2], __shfl_xor_sync(0xffffffffu, st_qi_max[k2], off));
           st_wlo_min[k2] = fminf(st_wlo_min[k2], __shfl_xor_sync(0xffffffffu, st_wlo_min[k2], off));
+          st_elo_min[k2] = min(st_elo_min[k2], __shfl_xor_sync(0xffffffffu, st_elo_min[k2], off));
+          st_ehi_max[k2] = max(st_ehi_max[k2], __shfl_xor_sync(0xffffffffu, st_ehi_max[k2], off));
         }
       }
-      edge_here = __any_sync(0xffffffffu, edge_here);
-      if (lane == 0) {
+      if ((lane & 15) == 0) {
         ColStats& cs = sm.stats[st];
 #pragma unroll
         for (int k2 = 0; k2 < 2; ++k2) {
-          cs.lo_max[k2] = st_lo_max[k2]; cs.lo_min[k2] = st_lo_min[k2];
-          cs.qi_min[k2] = st_qi_min[k2]; cs.qi_max[k2] = st_qi_max[k2]; cs.wlo_min[k2] = st_wlo_min[k2];
+          const int qq = 2 * k2 + (lane >> 4);
+          cs.lo_max[qq] = st_lo_max[k2]; cs.lo_min[qq] = st_lo_min[k2];
+          cs.qi_min[qq] = st_qi_min[k2]; cs.qi_max[qq] = st_qi_max[k2]; cs.wlo_min[qq] = st_wlo_min[k2];
+          cs.elo_min[qq] = st_elo_min[k2]; cs.ehi_max[qq] = st_ehi_max[k2];
         }
-        cs.has_edge = edge_here ? 1 : 0;
       }
       mbar_arrive(bar[COL_FULL + st]);
       // refill the stage of tile u − 1 with tile u + kColStages − 1 once the rows released it
@@ -745,8 +754,8 @@ __global__ void __launch_bounds__(kThreadsKV, 1) tc_bwd_dkdv_kernel(const __grid
   } else {
     // ---------------------------------------------------- key-row warps (Pᵀ, dSᵀ)
     const int r = 32 * (warp & 3) + lane;  // key row / TMEM lane
-    const int half = (warp >> 2) & 1;
-    const int c0 = BN / 2 * half;          // this thread's first column of a tile
+    const int quarter = warp >> 2;
+    const int c0 = kQuarter * quarter;     // this thread's first column of a tile
     const uint32_t lane_addr = ((uint32_t)(32 * (warp & 3)) << 16);
     const float sl2 = p.scale * kLog2e;
     const bool key_ok = r < nkeys;
@@ -769,39 +778,33 @@ __global__ void __launch_bounds__(kThreadsKV, 1) tc_bwd_dkdv_kernel(const __grid
       const ColStats& cst = sm.stats[cs];
       bool all_in, all_out;
       if (LMK) {
-        all_in = warp_keys_ok && cst.qi_min[half] >= jl && cst.wlo_min[half] > (float)jl;
+        all_in = warp_keys_ok && cst.qi_min[quarter] >= jl && cst.wlo_min[quarter] > (float)jl;
         all_out = false;
       } else {
-        all_in = cst.lo_max[half] <= jf && cst.qi_min[half] >= jl;
-        all_out = cst.lo_min[half] > jl || cst.qi_max[half] < jf;
+        all_in = cst.lo_max[quarter] <= jf && cst.qi_min[quarter] >= jl;
+        all_out = cst.lo_min[quarter] > jl || cst.qi_max[quarter] < jf;
       }
-      // Pᵀ and dSᵀ of this thread's 32 columns, 16 at a time, packed to the input
-      // dtype as they are produced (keeps the live register set small)
-      uint32_t pk_p[16], pk_d[16];
+      // Pᵀ and dSᵀ of this thread's 16 columns, packed to the input dtype
+      uint32_t pk_p[8], pk_d[8];
       const float jfl = (float)j;
+      if (all_out) {
+        tc_fence_before();
+        mbar_arrive(bar[SD_EMPTY + st]);
 #pragma unroll
-      for (int hh = 0; hh < 2; ++hh) {
+        for (int g = 0; g < 8; ++g) { pk_p[g] = 0u; pk_d[g] = 0u; }
+      } else {
         float sv[16], dpv[16];
-        if (!all_out) {
-          tmem_ld16(tS + lane_addr + st * BN + c0 + 16 * hh, sv);
-          tmem_ld16(tdP + lane_addr + st * BN + c0 + 16 * hh, dpv);
-          tmem_wait_ld();
-        }
-        if (hh == 1) {
-          tc_fence_before();
-          mbar_arrive(bar[SD_EMPTY + st]);
-        }
-        if (all_out) {
-#pragma unroll
-          for (int g = 0; g < 8; ++g) { pk_p[8 * hh + g] = 0u; pk_d[8 * hh + g] = 0u; }
-          continue;
-        }
+        tmem_ld16(tS + lane_addr + st * BN + c0, sv);
+        tmem_ld16(tdP + lane_addr + st * BN + c0, dpv);
+        tmem_wait_ld();
+        tc_fence_before();
+        mbar_arrive(bar[SD_EMPTY + st]);
 #pragma unroll
         for (int c = 0; c < 16; c += 2) {
           float pr2[2], ds2[2];
 #pragma unroll
           for (int e = 0; e < 2; ++e) {
-            const QRec& rq = rec[16 * hh + c + e];
+            const QRec& rq = rec[c + e];
             const float4 r0 = *reinterpret_cast<const float4*>(&rq.nlse2);  // nlse2, delta, lo, qi
             bool valid;
             float pr;
@@ -817,8 +820,8 @@ __global__ void __launch_bounds__(kThreadsKV, 1) tc_bwd_dkdv_kernel(const __grid
             ds2[e] = valid ? dsv : 0.f;
             if (LMK) dlw += ds2[e];
           }
-          pk_p[8 * hh + c / 2] = pack2(pr2[0], pr2[1], kBF16);
-          pk_d[8 * hh + c / 2] = pack2(ds2[0], ds2[1], kBF16);
+          pk_p[c / 2] = pack2(pr2[0], pr2[1], kBF16);
+          pk_d[c / 2] = pack2(ds2[0], ds2[1], kBF16);
         }
       }
       // the single Pᵀ / dSᵀ buffer is free once the previous tile's dV / dK MMAs completed
@@ -826,48 +829,46 @@ __global__ void __launch_bounds__(kThreadsKV, 1) tc_bwd_dkdv_kernel(const __grid
         ok = mbar_wait(bar[PDS_EMPTY], (u - 1) & 1, abort_flag, p.status);
         if (!__all_sync(0xffffffffu, ok)) { ok = false; break; }
       }
-      store_row32_packed(sm.pt, r, c0, pk_p);
-      store_row32_packed(sm.dst, r, c0, pk_d);
-      if (!LMK && cst.has_edge) {
-        // soft window edge: Pᵀ, dSᵀ *= σ((w̃ − d)/τ) on each query column's edge keys,
-        // spread over the 256 row threads: column tid % 64, edge indices tid / 64 and + 4
+#pragma unroll
+      for (int g = 0; g < 2; ++g) {
+        *reinterpret_cast<uint4*>(sm.pt + sw128_offset(r, c0 + 8 * g)) =
+            make_uint4(pk_p[4 * g], pk_p[4 * g + 1], pk_p[4 * g + 2], pk_p[4 * g + 3]);
+        *reinterpret_cast<uint4*>(sm.dst + sw128_offset(r, c0 + 8 * g)) =
+            make_uint4(pk_d[4 * g], pk_d[4 * g + 1], pk_d[4 * g + 2], pk_d[4 * g + 3]);
+      }
+      // soft window edge (band items): Pᵀ, dSᵀ *= σ((w̃ − d)/τ) on each query
+      // column's edge keys, spread over the 512 row threads (column tid % 64, edge
+      // index tid / 64) once every row has stored its entries
+      const bool tile_edge = !LMK && min(min(cst.elo_min[0], cst.elo_min[1]), min(cst.elo_min[2], cst.elo_min[3])) <=
+                                         key0 + nkeys - 1 &&
+                             max(max(cst.ehi_max[0], cst.ehi_max[1]), max(cst.ehi_max[2], cst.ehi_max[3])) >= key0;
+      if (tile_edge) {
         mbar_arrive(bar[ROWS]);
         ok = mbar_wait(bar[ROWS], rows_phase & 1, abort_flag, p.status);
         ++rows_phase;
         if (!__all_sync(0xffffffffu, ok)) { ok = false; break; }
         const int col = tid & (BN - 1);
         const QRec& rc = sm.rec[cs][col];
-        const int ne = rc.ne, ehi = rc.ehi;
-        float a1[2], a2[2];
-        uint32_t off[2];
-        bool in[2];
-#pragma unroll
-        for (int k2 = 0; k2 < 2; ++k2) {
-          const int e = (tid >> 6) + 4 * k2;
+        const int ne = qrec_ne(rc), ehi = rc.ehi;
+        {
+          const int e = tid >> 6;
           const int rr = ehi - e - key0;
-          in[k2] = e < ne && rr >= 0 && rr < nkeys;
-          off[k2] = in[k2] ? sw128_offset(rr, col) : 0u;
-          a1[k2] = in[k2] ? to_f32<T>(*reinterpret_cast<const T*>(sm.pt + off[k2])) : 0.f;
-          a2[k2] = in[k2] ? to_f32<T>(*reinterpret_cast<const T*>(sm.dst + off[k2])) : 0.f;
-        }
-#pragma unroll
-        for (int k2 = 0; k2 < 2; ++k2) {
-          if (in[k2]) {
-            const float g = rc.eg[(tid >> 6) + 4 * k2];
-            *reinterpret_cast<T*>(sm.pt + off[k2]) = from_f32<T>(a1[k2] * g);
-            *reinterpret_cast<T*>(sm.dst + off[k2]) = from_f32<T>(a2[k2] * g);
+          if (e < ne && rr >= 0 && rr < nkeys) {
+            const uint32_t off = sw128_offset(rr, col);
+            const float a1 = to_f32<T>(*reinterpret_cast<const T*>(sm.pt + off));
+            const float a2 = to_f32<T>(*reinterpret_cast<const T*>(sm.dst + off));
+            const float g = rc.eg[e];
+            *reinterpret_cast<T*>(sm.pt + off) = from_f32<T>(a1 * g);
+            *reinterpret_cast<T*>(sm.dst + off) = from_f32<T>(a2 * g);
           }
         }
         if (tid < BN && ne > kMaxEdge) {
           // wider soft edges than the precomputed factors: the rest one key at a time
-          const float wt = rc.wt;
-          const int qi = rc.qi;
           for (int e = kMaxEdge; e < ne; ++e) {
             const int rr = ehi - e - key0;
             if (rr < 0) break;
             if (rr >= nkeys) continue;
-            const float z = (wt - (float)(qi - (ehi - e))) * inv_tau;
-            const float sg = 1.0f / (1.0f + expf(-z));
+            const float sg = qrec_edge_factor(rc.wt, rc.qi - (ehi - e), inv_tau);
             T* e1 = reinterpret_cast<T*>(sm.pt + sw128_offset(rr, col));
             T* e2 = reinterpret_cast<T*>(sm.dst + sw128_offset(rr, col));
             *e1 = from_f32<T>(to_f32<T>(*e1) * sg);
@@ -885,14 +886,14 @@ __global__ void __launch_bounds__(kThreadsKV, 1) tc_bwd_dkdv_kernel(const __grid
       tc_fence_after();
     }
     const bool have = ok && n_tiles > 0;
-    // this thread handles dK/dV columns [half·D/2, (half+1)·D/2) of key row r
+    // this thread handles dK/dV columns [quarter·D/4, (quarter+1)·D/4) of key row r
     if (LMK) {
       const int64_t slot = part * a.part_stride + lbase + key0 + r;
       float* dkl = a.dk_lmk + slot * D;
       float* dvl = a.dv_lmk + slot * D;
 #pragma unroll
-      for (int ch = 0; ch < D / 32; ++ch) {
-        const int col = half * (D / 2) + ch * 16;
+      for (int ch = 0; ch < D / 64; ++ch) {
+        const int col = quarter * (D / 4) + ch * 16;
         float kk_[16], vv[16];
         if (have) {
           tmem_ld16(tdK + lane_addr + col, kk_);
@@ -911,11 +912,13 @@ __global__ void __launch_bounds__(kThreadsKV, 1) tc_bwd_dkdv_kernel(const __grid
           }
         }
       }
-      // d_lw of the slot: sum of the two column halves
-      if (half == 1) sm.dlw_half[r] = dlw;
+      // d_lw of the slot: sum of the four column quarters, in quarter order
+      sm.dlw_part[quarter][r] = dlw;
       mbar_arrive(bar[EPI]);
       const bool ok2 = mbar_wait(bar[EPI], 0, abort_flag, p.status);
-      if (half == 0 && key_ok) a.dlw_lmk[slot] = (have && ok2) ? dlw + sm.dlw_half[r] : 0.f;
+      if (quarter == 0 && key_ok)
+        a.dlw_lmk[slot] = (have && ok2)
+            ? ((sm.dlw_part[0][r] + sm.dlw_part[1][r]) + (sm.dlw_part[2][r] + sm.dlw_part[3][r])) : 0.f;
     } else if (ok) {
       // landmark slots at this key (sorted, duplicates adjacent) add their fp32 rows;
       // the rows are staged (dK in the Q ring, dV in the dO ring, 16-byte units
@@ -925,26 +928,26 @@ __global__ void __launch_bounds__(kThreadsKV, 1) tc_bwd_dkdv_kernel(const __grid
       constexpr int kUnits = D * 2 / 16;
       uint8_t* stage_k = sm.q[0];
       uint8_t* stage_v = sm.dO[0];
-#pragma unroll
-      for (int ch = 0; ch < D / 32; ++ch) {  // 16 columns at a time
-        const int col = half * (D / 2) + ch * 16;
-        float kk_[16], vv[16];
+#pragma unroll 1
+      for (int ch = 0; ch < D / 32; ++ch) {  // 8 columns at a time
+        const int col = quarter * (D / 4) + ch * 8;
+        float kk_[8], vv[8];
         if (n_tiles > 0) {
-          tmem_ld16(tdK + lane_addr + col, kk_);
-          tmem_ld16(tdV + lane_addr + col, vv);
+          tmem_ld8(tdK + lane_addr + col, kk_);
+          tmem_ld8(tdV + lane_addr + col, vv);
           tmem_wait_ld();
         } else {
 #pragma unroll
-          for (int e = 0; e < 16; ++e) { kk_[e] = 0.f; vv[e] = 0.f; }
+          for (int e = 0; e < 8; ++e) { kk_[e] = 0.f; vv[e] = 0.f; }
         }
 #pragma unroll
-        for (int e = 0; e < 16; ++e) kk_[e] *= p.scale;
+        for (int e = 0; e < 8; ++e) kk_[e] *= p.scale;
         for (int c = cl; key_ok && c >= 0 && c < p.kp && __ldg(p.pos_sorted + lbase + c) == j; ++c) {
           for (int pp = 0; pp < DSALT_LMK_SPLIT; ++pp) {
             const float* lk = a.dk_lmk + (pp * a.part_stride + lbase + c) * D + col;
             const float* lv = a.dv_lmk + (pp * a.part_stride + lbase + c) * D + col;
 #pragma unroll
-            for (int e = 0; e < 16; e += 4) {
+            for (int e = 0; e < 8; e += 4) {
               const float4 k4 = __ldg(reinterpret_cast<const float4*>(lk + e));
               const float4 v4 = __ldg(reinterpret_cast<const float4*>(lv + e));
               kk_[e] += k4.x; kk_[e + 1] += k4.y; kk_[e + 2] += k4.z; kk_[e + 3] += k4.w;
@@ -952,20 +955,17 @@ __global__ void __launch_bounds__(kThreadsKV, 1) tc_bwd_dkdv_kernel(const __grid
             }
           }
         }
-#pragma unroll
-        for (int e = 0; e < 16; e += 8) {
-          const int un = (col + e) / 8;
-          uint4 u0, u1;
-          u0.x = pack2(kk_[e], kk_[e + 1], kBF16); u0.y = pack2(kk_[e + 2], kk_[e + 3], kBF16);
-          u0.z = pack2(kk_[e + 4], kk_[e + 5], kBF16); u0.w = pack2(kk_[e + 6], kk_[e + 7], kBF16);
-          u1.x = pack2(vv[e], vv[e + 1], kBF16); u1.y = pack2(vv[e + 2], vv[e + 3], kBF16);
-          u1.z = pack2(vv[e + 4], vv[e + 5], kBF16); u1.w = pack2(vv[e + 6], vv[e + 7], kBF16);
-          *reinterpret_cast<uint4*>(stage_k + r * (kUnits * 16) + ((un ^ (r & 7)) << 4)) = u0;
-          *reinterpret_cast<uint4*>(stage_v + r * (kUnits * 16) + ((un ^ (r & 7)) << 4)) = u1;
-        }
+        const int un = col / 8;
+        uint4 u0, u1;
+        u0.x = pack2(kk_[0], kk_[1], kBF16); u0.y = pack2(kk_[2], kk_[3], kBF16);
+        u0.z = pack2(kk_[4], kk_[5], kBF16); u0.w = pack2(kk_[6], kk_[7], kBF16);
+        u1.x = pack2(vv[0], vv[1], kBF16); u1.y = pack2(vv[2], vv[3], kBF16);
+        u1.z = pack2(vv[4], vv[5], kBF16); u1.w = pack2(vv[6], vv[7], kBF16);
+        *reinterpret_cast<uint4*>(stage_k + r * (kUnits * 16) + ((un ^ (r & 7)) << 4)) = u0;
+        *reinterpret_cast<uint4*>(stage_v + r * (kUnits * 16) + ((un ^ (r & 7)) << 4)) = u1;
       }
       // d_lw of the landmark slots at this key: sum of the query-range parts
-      if (half == 0 && key_ok && p.d_lw) {
+      if (quarter == 0 && key_ok && p.d_lw) {
         for (int c = cl; c >= 0 && c < p.kp && __ldg(p.pos_sorted + lbase + c) == j; ++c) {
           float g = 0.f;
           for (int pp = 0; pp < DSALT_LMK_SPLIT; ++pp) g += __ldg(a.dlw_lmk + pp * a.part_stride + lbase + c);

@@ -124,20 +124,21 @@ struct alignas(16) QRec {
   float delta;  // Δ = Σ_d O·dO
   int lo;       // first band key (INT_MAX: none)
   int qi;       // query position in its sequence (INT_MIN: row without keys)
+  int ehi;      // last soft-edge key (INT_MIN: none)
+  int elo;      // first soft-edge key (INT_MAX: none); the edge keys are elo … ehi
   float wlo;    // float(i) − w̃ (landmark rule)
   float wt;     // w̃
-  int ehi;      // last soft-edge key (INT_MIN: none)
-  int ne;       // soft-edge keys ehi, ehi − 1, …, ehi − ne + 1 (d = i − key)
-  float eg[kQRecEdge];  // σ((w̃ − d)/τ) of edge key ehi − e, e < min(ne, kQRecEdge)
+  float eg[kQRecEdge];  // σ((w̃ − d)/τ) of edge key ehi − e (d = i − ehi + e), e < kQRecEdge
 };
 static_assert(sizeof(QRec) == DSALT_QREC_FLOATS * 4, "record size");
+__device__ __forceinline__ int qrec_ne(const QRec& r) { return r.elo <= r.ehi ? r.ehi - r.elo + 1 : 0; }
 
 // Record fields of query token t (global index), head h, given its Δ; the
 // soft-edge factors are left to qrec_edge_factor (d_e0: first edge distance).
 __device__ __forceinline__ QRec qrec_fields(const DsaltAttnParams& p, int64_t t, int h, float delta, int* d_e0) {
   QRec rec;
   rec.nlse2 = 0.f; rec.delta = 0.f; rec.lo = INT_MAX; rec.qi = INT_MIN;
-  rec.wlo = -INFINITY; rec.wt = 0.f; rec.ehi = INT_MIN; rec.ne = 0;
+  rec.wlo = -INFINITY; rec.wt = 0.f; rec.ehi = INT_MIN; rec.elo = INT_MAX;
   *d_e0 = 0;
   const float lse = p.lse[t * p.H + h];
   if (lse != -INFINITY) {
@@ -154,7 +155,7 @@ __device__ __forceinline__ QRec qrec_fields(const DsaltAttnParams& p, int64_t t,
       const int de = max((int)floorf(rw.core) + 1, 0);
       if (de <= rw.W) {
         rec.ehi = i - de;
-        rec.ne = max(rec.ehi - rec.lo + 1, 0);
+        rec.elo = rec.lo;  // the edge runs down to the band start (d = min(W, i))
         *d_e0 = de;
       }
     }
@@ -175,7 +176,9 @@ __device__ __forceinline__ void write_qrec(const DsaltAttnParams& p, int64_t t, 
   QRec rec = qrec_fields(p, t, h, delta, &d_e0);
   const float inv_tau = 1.0f / p.tau_win;
 #pragma unroll
-  for (int e = 0; e < kQRecEdge; ++e) rec.eg[e] = e < rec.ne ? qrec_edge_factor(rec.wt, d_e0 + e, inv_tau) : 1.0f;
+  const int ne = qrec_ne(rec);
+#pragma unroll
+  for (int e = 0; e < kQRecEdge; ++e) rec.eg[e] = e < ne ? qrec_edge_factor(rec.wt, d_e0 + e, inv_tau) : 1.0f;
   float4* dst = qrec_ptr(p, t, h);
   const float4* src = reinterpret_cast<const float4*>(&rec);
 #pragma unroll

@@ -186,9 +186,28 @@ def backward(grad_out, q_c, k_c, v_c, o, lse, prep: Prepared, tau_win: float, wi
                 delta=delta, dq=dq, dk=dk, dv=dv, dw_head=dw_head, dw=dw, d_lw=d_lw, lmk_grad=lmk_grad,
                 qrec=qrec)
     _ext.call("dsalt_attn_bwd_preprocess", p)
+    # dK/dV and dQ are independent once Δ and the records exist: dQ runs on a side
+    # stream so that each kernel's tail waves (and the under-filled landmark pass)
+    # overlap the other's work
+    main = torch.cuda.current_stream(dev)
+    side = _side_stream(dev)
+    side.wait_stream(main)
+    with torch.cuda.stream(side):
+        _ext.call("dsalt_attn_bwd_dq", p)
     _ext.call("dsalt_attn_bwd_dkdv", p)
-    _ext.call("dsalt_attn_bwd_dq", p)
+    main.wait_stream(side)
     return dq, dk, dv, d_lw, dw
+
+
+_SIDE_STREAMS: dict = {}
+
+
+def _side_stream(dev: torch.device) -> torch.cuda.Stream:
+    key = dev.index if dev.index is not None else torch.cuda.current_device()
+    st = _SIDE_STREAMS.get(key)
+    if st is None:
+        st = _SIDE_STREAMS[key] = torch.cuda.Stream(device=dev)
+    return st
 
 
 def compute_dtype(q: torch.Tensor) -> torch.dtype:

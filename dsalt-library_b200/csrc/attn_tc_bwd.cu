@@ -78,8 +78,16 @@ __device__ __forceinline__ void store_row32_packed(uint8_t* base, int row, int c
 namespace dq {
 constexpr int BM = 128, BN = 64;
 constexpr int kKV = 3;           // K / V tile ring
-constexpr int kThreadsDQ = 352;  // row warps 0-7, TMA warp 8, MMA warps 9 (S, dQ) and 10 (dP)
-constexpr int kMmaWarpB = 10;
+// 16 row warps: warp w reads TMEM lanes 32·(w % 4)… and owns the 16-column
+// quarter w / 4 of every 64-key tile; then the TMA warp, MMA warp A (TMEM
+// owner: S, dQ) and MMA warp B (dP)
+constexpr int kRowWarps = 16;
+constexpr int kRowThreads = 32 * kRowWarps;
+constexpr int kProducerWarp = 16;
+constexpr int kMmaWarp = 17;
+constexpr int kMmaWarpB = 18;
+constexpr int kThreadsDQ = 608;
+constexpr int kQuarter = BN / 4;  // tile columns per row thread
 enum { QD_FULL = 0, K_FULL = 1, V_FULL = K_FULL + kKV, K_EMPTY = V_FULL + kKV, V_EMPTY = K_EMPTY + kKV,
        SD_FULL = V_EMPTY + kKV, SD_EMPTY = SD_FULL + 2, DS_FULL = SD_EMPTY + 2, DS_EMPTY = DS_FULL + 2,
        DQ_DONE = DS_EMPTY + 2, FINAL = DQ_DONE + 1, EPI = FINAL + 2, EPI2 = EPI + 1, NB = EPI2 + 1 };
@@ -94,7 +102,7 @@ struct alignas(1024) Smem {
   uint64_t bars[NB];
   uint32_t tmem_base;
   int abort_flag, band_lo, band_hi, cnt_max, n_valid, slow_edge;
-  float dw_half[BM];
+  float dw_part[4][BM];  // ∂loss/∂w̃ partial sums of the four column quarters
   int lmk_pos[kMaxLmk];
   float lmk_lw2[kMaxLmk];
 };
@@ -142,22 +150,24 @@ __global__ void __launch_bounds__(kThreadsDQ, 1) tc_bwd_dq_kernel(const __grid_c
     sm.slow_edge = 0;
   }
   if (warp == kMmaWarp) tmem_alloc(smem_u32(&sm.tmem_base), 512);
-  // row r (TMEM lane) = 32·(warp % 4) + lane; column half = warp / 4.  The row's
+  // row r (TMEM lane) = 32·(warp % 4) + lane; column quarter = warp / 4.  The row's
   // record (LSE, Δ, window, soft-edge factors) is loaded while the landmark
   // positions are staged.
   const int r = 32 * (warp & 3) + lane;
-  const int half = (warp >> 2) & 1;
+  const int quarter = warp >> 2;
   const int i = m0 + r;
-  const bool row_ok = warp < 8 && i < L;
-  QRec rec;
+  const bool row_ok = warp < kRowWarps && i < L;
+  // header of the row's record (the soft-edge factors are read when needed)
+  const QRec* recg = reinterpret_cast<const QRec*>(p.qrec) + (int64_t)h * p.T + s0 + i;
+  float4 rh0 = make_float4(0.f, 0.f, __int_as_float(INT_MAX), __int_as_float(INT_MIN));
+  float4 rh1 = make_float4(__int_as_float(INT_MIN), __int_as_float(INT_MAX), -INFINITY, 0.f);
   if (row_ok) {
-    const float4* src = reinterpret_cast<const float4*>(p.qrec + ((int64_t)h * p.T + s0 + i) * DSALT_QREC_FLOATS);
-    float4* dst = reinterpret_cast<float4*>(&rec);
-#pragma unroll
-    for (int k = 0; k < DSALT_QREC_FLOATS / 4; ++k) dst[k] = __ldg(src + k);
-  } else {
-    rec.qi = INT_MIN;
+    rh0 = __ldg(reinterpret_cast<const float4*>(recg));      // nlse2, delta, lo, qi
+    rh1 = __ldg(reinterpret_cast<const float4*>(recg) + 1);  // ehi, elo, wlo, wt
   }
+  const int rec_lo = __float_as_int(rh0.z), rec_qi = __float_as_int(rh0.w);
+  const int rec_ehi = __float_as_int(rh1.x), rec_elo = __float_as_int(rh1.y);
+  const int rec_ne = rec_elo <= rec_ehi ? rec_ehi - rec_elo + 1 : 0;
   const int kp = p.kp;
   const int64_t lbase = ((int64_t)h * p.S + s) * kp;
   for (int c = tid; c < kp; c += kThreadsDQ) {
@@ -176,21 +186,21 @@ __global__ void __launch_bounds__(kThreadsDQ, 1) tc_bwd_dq_kernel(const __grid_c
       tma_load_3d(smem_u32(sm.dO + c * (BM * 128)), &a.tm_do, bar[QD_FULL], c * 64, h, (int)(s0 + m0));
     }
   }
-  const bool row_live = row_ok && rec.qi != INT_MIN;  // a row without keys has no gradient
+  const bool row_live = row_ok && rec_qi != INT_MIN;  // a row without keys has no gradient
   int lo = INT_MAX, hi = -1, cnt = 0;
   if (row_live) {
-    if (rec.lo != INT_MAX) { lo = rec.lo; hi = i; }
+    if (rec_lo != INT_MAX) { lo = rec_lo; hi = i; }
     int a0 = 0, a1 = sm.n_valid;
     while (a0 < a1) {
       const int mid = (a0 + a1) >> 1;
       const int ps = sm.lmk_pos[mid];
-      if (ps <= i && (float)ps < rec.wlo) a0 = mid + 1; else a1 = mid;
+      if (ps <= i && (float)ps < rh1.z) a0 = mid + 1; else a1 = mid;
     }
     cnt = a0;
-    if (half == 0) {
+    if (quarter == 0) {
       if (lo <= hi) { atomicMin(&sm.band_lo, lo); atomicMax(&sm.band_hi, hi); }
       if (cnt > 0) atomicMax(&sm.cnt_max, cnt);
-      if (qrec_ne(rec) > kMaxEdge) atomicOr(&sm.slow_edge, 1);
+      if (rec_ne > kMaxEdge) atomicOr(&sm.slow_edge, 1);
     }
   }
   tc_fence_before();
@@ -303,13 +313,13 @@ __global__ void __launch_bounds__(kThreadsDQ, 1) tc_bwd_dq_kernel(const __grid_c
   } else {
     // --------------------------------------------------------- row warps
     const uint32_t lane_addr = ((uint32_t)(32 * (warp & 3)) << 16);
-    const int c0 = BN / 2 * half;  // first tile column of this thread
+    const int c0 = kQuarter * quarter;  // first tile column of this thread
     const float sl2 = p.scale * kLog2e;
     const float inv_tau = 1.0f / p.tau_win;
     const bool slow_edge = sm.slow_edge != 0;
-    const float nlse2 = row_live ? rec.nlse2 : 0.f;
-    const float delta = row_live ? rec.delta : 0.f;
-    const int ne = row_live ? qrec_ne(rec) : 0, ehi = rec.ehi;
+    const float nlse2 = row_live ? rh0.x : 0.f;
+    const float delta = row_live ? rh0.y : 0.f;
+    const int ne = row_live ? rec_ne : 0, ehi = rec_ehi;
     float dw = 0.f;
     bool ok = true;
     for (int t = 0; t < n_tiles; ++t) {
@@ -322,24 +332,24 @@ __global__ void __launch_bounds__(kThreadsDQ, 1) tc_bwd_dq_kernel(const __grid_c
       // valid columns of this thread: [vlo, vhi]
       const int vlo = lmk ? 0 : lo - n0 - c0;  // lo = INT_MAX for a row without band: stays positive
       const int vhi = lmk ? cnt - BN * t - c0 - 1 : hi - n0 - c0;
-      const bool all_in = __all_sync(0xffffffffu, vlo <= 0 && vhi >= 31);
-      const bool all_out = __all_sync(0xffffffffu, vhi < 0 || vlo > 31 || vlo > vhi);
-      uint32_t pk[16];
+      const bool all_in = __all_sync(0xffffffffu, vlo <= 0 && vhi >= kQuarter - 1);
+      const bool all_out = __all_sync(0xffffffffu, vhi < 0 || vlo > kQuarter - 1 || vlo > vhi);
+      uint32_t pk[8];
       if (all_out) {
         tc_fence_before();
         mbar_arrive(bar[SD_EMPTY + st]);
 #pragma unroll
-        for (int g = 0; g < 16; ++g) pk[g] = 0u;
+        for (int g = 0; g < 8; ++g) pk[g] = 0u;
       } else {
-        float sv[32], dpv[32];
-        tmem_ld32(tS + lane_addr + st * BN + c0, sv);
-        tmem_ld32(tdP + lane_addr + st * BN + c0, dpv);
+        float sv[16], dpv[16];
+        tmem_ld16(tS + lane_addr + st * BN + c0, sv);
+        tmem_ld16(tdP + lane_addr + st * BN + c0, dpv);
         tmem_wait_ld();
         tc_fence_before();
         mbar_arrive(bar[SD_EMPTY + st]);
         const float* lw2 = sm.lmk_lw2 + BN * t + c0;
 #pragma unroll
-        for (int c = 0; c < 32; c += 2) {
+        for (int c = 0; c < kQuarter; c += 2) {
           float d2[2];
 #pragma unroll
           for (int e = 0; e < 2; ++e) {
@@ -356,37 +366,41 @@ __global__ void __launch_bounds__(kThreadsDQ, 1) tc_bwd_dq_kernel(const __grid_c
         if (!__all_sync(0xffffffffu, ok)) { ok = false; break; }
       }
       uint8_t* dsb = sm.ds[st];
-      store_row32_packed(dsb, r, c0, pk);
+#pragma unroll
+      for (int g = 0; g < 2; ++g)
+        *reinterpret_cast<uint4*>(dsb + sw128_offset(r, c0 + 8 * g)) =
+            make_uint4(pk[4 * g], pk[4 * g + 1], pk[4 * g + 2], pk[4 * g + 3]);
       if (!lmk && !all_out) {
-        // soft window edge on this thread's half: dS *= σ((w̃ − d)/τ); ∂loss/∂w̃ += dS·(1 − σ)/τ.
+        // soft window edge on this thread's quarter: dS *= σ((w̃ − d)/τ); ∂loss/∂w̃ += dS·(1 − σ)/τ.
         // The key at edge index e (distance d_e0 + e) sits in column ehi − e − n0 − c0.
         const int ce0 = ehi - n0 - c0;
-        const bool has = ne > 0 && ce0 >= 0 && ce0 - (ne - 1) <= 31;
+        const bool has = ne > 0 && ce0 >= 0 && ce0 - (ne - 1) <= kQuarter - 1;
         if (!slow_edge) {
           if (__any_sync(0xffffffffu, has)) {
             float pv[kMaxEdge];
 #pragma unroll
             for (int e = 0; e < kMaxEdge; ++e) {
               const int c = ce0 - e;
-              const bool in = has && e < ne && c >= 0 && c < 32;
+              const bool in = has && e < ne && c >= 0 && c < kQuarter;
               pv[e] = in ? to_f32<T>(*reinterpret_cast<const T*>(dsb + sw128_offset(r, c0 + c))) : 0.f;
             }
 #pragma unroll
             for (int e = 0; e < kMaxEdge; ++e) {
               const int c = ce0 - e;
-              if (has && e < ne && c >= 0 && c < 32) {
-                const float v = pv[e] * rec.eg[e];
+              if (has && e < ne && c >= 0 && c < kQuarter) {
+                const float g = __ldg(recg->eg + e);
+                const float v = pv[e] * g;
                 *reinterpret_cast<T*>(dsb + sw128_offset(r, c0 + c)) = from_f32<T>(v);
-                dw = fmaf(v, (1.0f - rec.eg[e]) * inv_tau, dw);
+                dw = fmaf(v, (1.0f - g) * inv_tau, dw);
               }
             }
           }
         } else if (has) {
           const int d_e0 = i - ehi;
-          for (int e = max(0, ce0 - 31); e < ne && ce0 - e >= 0; ++e) {
+          for (int e = max(0, ce0 - (kQuarter - 1)); e < ne && ce0 - e >= 0; ++e) {
             const int c = ce0 - e;
             T* ep = reinterpret_cast<T*>(dsb + sw128_offset(r, c0 + c));
-            const float sg = qrec_edge_factor(rec.wt, d_e0 + e, inv_tau);
+            const float sg = qrec_edge_factor(rh1.w, d_e0 + e, inv_tau);
             const float v = to_f32<T>(*ep) * sg;
             *ep = from_f32<T>(v);
             dw = fmaf(v, (1.0f - sg) * inv_tau, dw);
@@ -401,19 +415,21 @@ __global__ void __launch_bounds__(kThreadsDQ, 1) tc_bwd_dq_kernel(const __grid_c
       ok = __all_sync(0xffffffffu, ok);
       tc_fence_after();
     }
-    // ∂loss/∂w̃ of the row: sum of the two halves
-    if (half == 1) sm.dw_half[r] = dw;
+    // ∂loss/∂w̃ of the row: sum of the four column quarters, in quarter order
+    sm.dw_part[quarter][r] = dw;
     mbar_arrive(bar[EPI]);
     const bool ok2 = mbar_wait(bar[EPI], 0, abort_flag, p.status);
-    if (half == 0 && row_ok && p.dw_head) p.dw_head[(s0 + i) * p.H + h] = (ok && ok2) ? dw + sm.dw_half[r] : 0.f;
+    if (quarter == 0 && row_ok && p.dw_head)
+      p.dw_head[(s0 + i) * p.H + h] =
+          (ok && ok2) ? (sm.dw_part[0][r] + sm.dw_part[1][r]) + (sm.dw_part[2][r] + sm.dw_part[3][r]) : 0.f;
     if (ok && ok2) {
       // dQ rows staged in the (now idle) K ring, 16-byte units XOR-swizzled by
       // row % 8, then stored row-contiguously
       constexpr int kUnits = D * 2 / 16;
       uint8_t* stage = sm.k[0];
 #pragma unroll
-      for (int ch = 0; ch < D / 32; ++ch) {  // 16 columns at a time
-        const int col = half * (D / 2) + ch * 16;
+      for (int ch = 0; ch < D / 64; ++ch) {  // 16 columns at a time
+        const int col = quarter * (D / 4) + ch * 16;
         float o[16];
         if (n_tiles > 0) {
           tmem_ld16(tdQ + lane_addr + col, o);

@@ -47,7 +47,7 @@ WORKLOADS = {
 FLOPS_PER_PAIR = {"dsalt_attn_fwd": 4, "dsalt_attn_bwd_dkdv": 8, "dsalt_attn_bwd_dq": 2}
 # kernels launched by each C-ABI entry point
 KERNELS_PER_CALL = {"dsalt_build_schedule": 2, "dsalt_gather_landmarks": 1, "dsalt_attn_fwd": 1,
-                    "dsalt_attn_bwd_preprocess": 1, "dsalt_attn_bwd_dkdv": 2, "dsalt_attn_bwd_dq": 2}
+                    "dsalt_attn_bwd_preprocess": 1, "dsalt_attn_bwd_dkdv": 3, "dsalt_attn_bwd_dq": 2}
 # DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) per call of each entry point,
 # summed over its kernels, from one ncu capture of a config-2 step; the capture and the
 # command are in profiles/traffic_step_config2.txt

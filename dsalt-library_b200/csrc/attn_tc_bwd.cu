@@ -24,6 +24,8 @@
 //   store.  The backward is deterministic.
 //
 // All waits are bounded (sm100::mbar_wait); see attn_tc.cu.
+#include <mutex>
+
 #include "common.cuh"
 #include "sm100.cuh"
 
@@ -48,6 +50,7 @@ struct alignas(64) BwdArgs {
   float* dk_lmk;   // [DSALT_LMK_SPLIT,H,S,kp,D] fp32 scratch: partial landmark-slot dK / dV
   float* dv_lmk;
   float* dlw_lmk;  // [DSALT_LMK_SPLIT,H,S,kp] fp32 scratch: partial landmark-slot d_lw
+  float* band_lmk;  // [2,H,S,kp,D] fp32 scratch: band-pass dK / dV of keys holding landmark slots
   int64_t part_stride;  // H·S·kp: slots per partial
   int lmk_box;    // rows of one landmark TMA box
 };
@@ -778,6 +781,8 @@ __global__ void __launch_bounds__(kThreadsKV, 1) tc_bwd_dkdv_kernel(const __grid
     const int j = LMK ? (key_ok ? __ldg(p.pos_sorted + lbase + key0 + r) : INT_MAX) : key0 + r;
     const float lw2 = (LMK && key_ok) ? __ldg(p.w_sorted + lbase + key0 + r) * kLog2e : 0.f;
     // key range of this warp's 32 rows (band: consecutive; landmarks: sorted positions)
+    // first landmark slot at this key (band items; -1: none), used by the epilogue
+    const int cl_first = (!LMK && key_ok && p.lmk_slot) ? __ldg(p.lmk_slot + (s0 + j) * p.H + h) : -1;
     const int jf = LMK ? __shfl_sync(0xffffffffu, j, 0) : key0 + 32 * (warp & 3);
     const int jl = LMK ? __reduce_max_sync(0xffffffffu, key_ok ? j : INT_MIN) : jf + 31;
     const bool warp_keys_ok = __all_sync(0xffffffffu, key_ok);
@@ -936,14 +941,16 @@ __global__ void __launch_bounds__(kThreadsKV, 1) tc_bwd_dkdv_kernel(const __grid
         a.dlw_lmk[slot] = (have && ok2)
             ? ((sm.dlw_part[0][r] + sm.dlw_part[1][r]) + (sm.dlw_part[2][r] + sm.dlw_part[3][r])) : 0.f;
     } else if (ok) {
-      // landmark slots at this key (sorted, duplicates adjacent) add their fp32 rows;
-      // the rows are staged (dK in the Q ring, dV in the dO ring, 16-byte units
-      // XOR-swizzled by row % 8) and stored row-contiguously
-      int cl = -1;
-      if (key_ok && p.lmk_slot) cl = __ldg(p.lmk_slot + (s0 + j) * p.H + h);
+      // The rows are staged (dK in the Q ring, dV in the dO ring, 16-byte units
+      // XOR-swizzled by row % 8) and stored row-contiguously.  A key that holds
+      // landmark slots (first slot cl_first) also leaves its fp32 rows in the
+      // band scratch: lmk_fixup_kernel adds the landmark pass's parts to them and
+      // rounds once.
       constexpr int kUnits = D * 2 / 16;
       uint8_t* stage_k = sm.q[0];
       uint8_t* stage_v = sm.dO[0];
+      float* bk = cl_first >= 0 ? a.band_lmk + (lbase + cl_first) * D : nullptr;
+      float* bv = cl_first >= 0 ? a.band_lmk + a.part_stride * D + (lbase + cl_first) * D : nullptr;
 #pragma unroll 1
       for (int ch = 0; ch < D / 32; ++ch) {  // 8 columns at a time
         const int col = quarter * (D / 4) + ch * 8;
@@ -958,18 +965,11 @@ __global__ void __launch_bounds__(kThreadsKV, 1) tc_bwd_dkdv_kernel(const __grid
         }
 #pragma unroll
         for (int e = 0; e < 8; ++e) kk_[e] *= p.scale;
-        for (int c = cl; key_ok && c >= 0 && c < p.kp && __ldg(p.pos_sorted + lbase + c) == j; ++c) {
-          for (int pp = 0; pp < DSALT_LMK_SPLIT; ++pp) {
-            const float* lk = a.dk_lmk + (pp * a.part_stride + lbase + c) * D + col;
-            const float* lv = a.dv_lmk + (pp * a.part_stride + lbase + c) * D + col;
-#pragma unroll
-            for (int e = 0; e < 8; e += 4) {
-              const float4 k4 = __ldg(reinterpret_cast<const float4*>(lk + e));
-              const float4 v4 = __ldg(reinterpret_cast<const float4*>(lv + e));
-              kk_[e] += k4.x; kk_[e + 1] += k4.y; kk_[e + 2] += k4.z; kk_[e + 3] += k4.w;
-              vv[e] += v4.x; vv[e + 1] += v4.y; vv[e + 2] += v4.z; vv[e + 3] += v4.w;
-            }
-          }
+        if (bk) {
+          *reinterpret_cast<float4*>(bk + col) = make_float4(kk_[0], kk_[1], kk_[2], kk_[3]);
+          *reinterpret_cast<float4*>(bk + col + 4) = make_float4(kk_[4], kk_[5], kk_[6], kk_[7]);
+          *reinterpret_cast<float4*>(bv + col) = make_float4(vv[0], vv[1], vv[2], vv[3]);
+          *reinterpret_cast<float4*>(bv + col + 4) = make_float4(vv[4], vv[5], vv[6], vv[7]);
         }
         const int un = col / 8;
         uint4 u0, u1;
@@ -979,15 +979,6 @@ __global__ void __launch_bounds__(kThreadsKV, 1) tc_bwd_dkdv_kernel(const __grid
         u1.z = pack2(vv[4], vv[5], kBF16); u1.w = pack2(vv[6], vv[7], kBF16);
         *reinterpret_cast<uint4*>(stage_k + r * (kUnits * 16) + ((un ^ (r & 7)) << 4)) = u0;
         *reinterpret_cast<uint4*>(stage_v + r * (kUnits * 16) + ((un ^ (r & 7)) << 4)) = u1;
-      }
-      // d_lw of the landmark slots at this key: sum of the query-range parts
-      if (quarter == 0 && key_ok && p.d_lw) {
-        for (int c = cl; c >= 0 && c < p.kp && __ldg(p.pos_sorted + lbase + c) == j; ++c) {
-          float g = 0.f;
-          for (int pp = 0; pp < DSALT_LMK_SPLIT; ++pp) g += __ldg(a.dlw_lmk + pp * a.part_stride + lbase + c);
-          const int slot_c = __ldg(p.perm + lbase + c);
-          if (slot_c >= 0) p.d_lw[((int64_t)h * p.S + s) * p.k_lmk + slot_c] = g;
-        }
       }
       mbar_arrive(bar[EPI2]);
       if (__all_sync(0xffffffffu, mbar_wait(bar[EPI2], 0, abort_flag, p.status))) {
@@ -1007,6 +998,54 @@ __global__ void __launch_bounds__(kThreadsKV, 1) tc_bwd_dkdv_kernel(const __grid
   __syncthreads();
   tc_fence_after();
   if (warp == kMmaWarp) tmem_dealloc(tmem, 512);
+}
+
+// Keys holding landmark slots: dK / dV = round(band rows + Σ over the key's slots
+// (duplicates are adjacent) and over the landmark pass's query-range parts, in
+// that fixed order); d_lw of every slot = Σ over its parts.  One warp per
+// (slot, sequence, head): blockIdx.x = s·ceil(kp/4) + slot/4; D/32 columns per lane.
+template <typename T, int D>
+__global__ void __launch_bounds__(128) lmk_fixup_kernel(const BwdArgs a) {
+  const DsaltAttnParams& p = a.p;
+  const int nq = (p.kp + 3) / 4;
+  const int s = blockIdx.x / nq, h = blockIdx.y;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int c = 4 * (blockIdx.x % nq) + warp;
+  if (c >= p.kp) return;
+  const int64_t lbase = ((int64_t)h * p.S + s) * p.kp;
+  const int64_t s0 = __ldg(p.cu_seqlens + s);
+  constexpr int kCols = D / 32;
+  const float* band_v = a.band_lmk + a.part_stride * D;
+  {
+    const int pos = __ldg(p.pos_sorted + lbase + c);
+    if (pos < 0) return;  // an invalid slot
+    if (lane == 0 && p.d_lw) {
+      float g = 0.f;
+      for (int pp = 0; pp < DSALT_LMK_SPLIT; ++pp) g += __ldg(a.dlw_lmk + pp * a.part_stride + lbase + c);
+      const int slot_c = __ldg(p.perm + lbase + c);
+      if (slot_c >= 0) p.d_lw[((int64_t)h * p.S + s) * p.k_lmk + slot_c] = g;
+    }
+    if (c > 0 && __ldg(p.pos_sorted + lbase + c - 1) == pos) return;  // not the first slot of its key
+    float kk[kCols], vv[kCols];
+    const int col0 = lane * kCols;
+#pragma unroll
+    for (int e = 0; e < kCols; ++e) {
+      kk[e] = __ldg(a.band_lmk + (lbase + c) * D + col0 + e);
+      vv[e] = __ldg(band_v + (lbase + c) * D + col0 + e);
+    }
+    for (int cc = c; cc < p.kp && __ldg(p.pos_sorted + lbase + cc) == pos; ++cc)
+      for (int pp = 0; pp < DSALT_LMK_SPLIT; ++pp) {
+        const float* lk = a.dk_lmk + (pp * a.part_stride + lbase + cc) * D + col0;
+        const float* lv = a.dv_lmk + (pp * a.part_stride + lbase + cc) * D + col0;
+#pragma unroll
+        for (int e = 0; e < kCols; ++e) { kk[e] += __ldg(lk + e); vv[e] += __ldg(lv + e); }
+      }
+    const int64_t row = ((s0 + pos) * p.H + h) * D + col0;
+    T* dk = reinterpret_cast<T*>(p.dk) + row;
+    T* dv = reinterpret_cast<T*>(p.dv) + row;
+#pragma unroll
+    for (int e = 0; e < kCols; ++e) { dk[e] = from_f32<T>(kk[e]); dv[e] = from_f32<T>(vv[e]); }
+  }
 }
 }  // namespace dkv
 
@@ -1053,6 +1092,24 @@ cudaError_t launch_dq(const DsaltAttnParams& p, cudaStream_t st) {
   return cudaSuccess;
 }
 
+// Non-blocking stream per device on which the landmark pass runs next to the band
+// pass (forked from and joined back into the caller's stream with events).
+static cudaError_t side_stream(cudaStream_t* out) {
+  static std::mutex mu;
+  static cudaStream_t streams[64] = {};
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+  std::lock_guard<std::mutex> lock(mu);
+  if (!streams[dev]) {
+    e = cudaStreamCreateWithFlags(&streams[dev], cudaStreamNonBlocking);
+    if (e != cudaSuccess) return e;
+  }
+  *out = streams[dev];
+  return cudaSuccess;
+}
+
 template <typename T, int D>
 cudaError_t launch_dkdv(const DsaltAttnParams& p, float* lmk_scratch, cudaStream_t st) {
   BwdArgs a;
@@ -1062,28 +1119,59 @@ cudaError_t launch_dkdv(const DsaltAttnParams& p, float* lmk_scratch, cudaStream
   a.dk_lmk = lmk_scratch;
   a.dv_lmk = lmk_scratch ? lmk_scratch + part_floats : nullptr;
   a.dlw_lmk = lmk_scratch ? lmk_scratch + 2 * part_floats : nullptr;
+  a.band_lmk = lmk_scratch ? a.dlw_lmk + DSALT_LMK_SPLIT * a.part_stride : nullptr;
   const size_t smem = std::max(sizeof(dkv::Smem<D>) + 1024, (size_t)(116 * 1024));
   cudaError_t e;
-  if (p.kp > 0 && p.S > 0) {
-    e = cudaFuncSetAttribute(dkv::tc_bwd_dkdv_kernel<true, T, D>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    if (e != cudaSuccess) return e;
-    const int nch = (p.kp + dkv::BM - 1) / dkv::BM;
-    const unsigned items = (unsigned)(p.S * nch * DSALT_LMK_SPLIT);
-    dkv::tc_bwd_dkdv_kernel<true, T, D><<<dim3(items, (unsigned)p.H), dkv::kThreadsKV, smem, st>>>(a);
-    e = cudaGetLastError();
-    if (e != cudaSuccess) return e;
+  const bool lmk = p.kp > 0 && p.S > 0;
+  // the landmark pass (under-filled grid) runs on a side stream next to the band pass
+  cudaEvent_t fork = nullptr, join = nullptr;
+  if (lmk) {
+    cudaStream_t side;
+    e = side_stream(&side);
+    if (e == cudaSuccess) e = cudaEventCreateWithFlags(&fork, cudaEventDisableTiming);
+    if (e == cudaSuccess) e = cudaEventCreateWithFlags(&join, cudaEventDisableTiming);
+    if (e == cudaSuccess) e = cudaEventRecord(fork, st);
+    if (e == cudaSuccess) e = cudaStreamWaitEvent(side, fork, 0);
+    if (e == cudaSuccess)
+      e = cudaFuncSetAttribute(dkv::tc_bwd_dkdv_kernel<true, T, D>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               (int)smem);
+    if (e == cudaSuccess) {
+      const int nch = (p.kp + dkv::BM - 1) / dkv::BM;
+      const unsigned items = (unsigned)(p.S * nch * DSALT_LMK_SPLIT);
+      dkv::tc_bwd_dkdv_kernel<true, T, D><<<dim3(items, (unsigned)p.H), dkv::kThreadsKV, smem, side>>>(a);
+      e = cudaGetLastError();
+    }
+    if (e == cudaSuccess) e = cudaEventRecord(join, side);
+    if (e != cudaSuccess) {
+      if (fork) cudaEventDestroy(fork);
+      if (join) cudaEventDestroy(join);
+      return e;
+    }
   }
   e = cudaFuncSetAttribute(dkv::tc_bwd_dkdv_kernel<false, T, D>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-  if (e != cudaSuccess) return e;
-  dkv::tc_bwd_dkdv_kernel<false, T, D><<<dim3((unsigned)p.max_blocks, (unsigned)p.H), dkv::kThreadsKV, smem, st>>>(a);
-  return cudaGetLastError();
+  if (e == cudaSuccess) {
+    dkv::tc_bwd_dkdv_kernel<false, T, D><<<dim3((unsigned)p.max_blocks, (unsigned)p.H), dkv::kThreadsKV, smem, st>>>(a);
+    e = cudaGetLastError();
+  }
+  if (lmk) {
+    // join before anything can fail past this point, so the caller's stream never runs ahead of the side work
+    const cudaError_t ej = cudaStreamWaitEvent(st, join, 0);
+    cudaEventDestroy(fork);
+    cudaEventDestroy(join);
+    if (e == cudaSuccess) e = ej;
+    if (e == cudaSuccess) {
+      dkv::lmk_fixup_kernel<T, D><<<dim3((unsigned)(p.S * ((p.kp + 3) / 4)), (unsigned)p.H), 128, 0, st>>>(a);
+      e = cudaGetLastError();
+    }
+  }
+  return e;
 }
 
 }  // namespace bwd
 
-// lmk_scratch: the caller's fp32 buffer ((2·D + 1)·DSALT_LMK_SPLIT·H·S·kp floats) for
-// the partial landmark-slot dK / dV / d_lw that the landmark items of the
-// key-parallel pass hand to the band items.
+// lmk_scratch: the caller's fp32 buffer (((2·D + 1)·DSALT_LMK_SPLIT + 2·D)·H·S·kp
+// floats) for the partial landmark-slot dK / dV / d_lw of the landmark pass and
+// the band pass's fp32 rows of the keys that hold landmark slots.
 cudaError_t tc_bwd_stage(int stage, const DsaltAttnParams& p, float* lmk_scratch, cudaStream_t st) {
   const bool bf = p.dtype == DSALT_BF16;
   if (stage == 3) {

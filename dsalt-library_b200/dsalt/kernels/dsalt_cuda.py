@@ -178,7 +178,7 @@ def backward(grad_out, q_c, k_c, v_c, o, lse, prep: Prepared, tau_win: float, wi
     dw_head = torch.empty(T, H, dtype=torch.float32, device=dev) if want_dw else None
     dw = torch.empty(T, dtype=q_c.dtype, device=dev) if want_dw else None
     # partial landmark-slot dK, dV, d_lw of the tensor-core dK/dV stage
-    lmk_grad = torch.empty((2 * prep.D + 1) * _ext.LMK_SPLIT * H * prep.S * prep.kp,
+    lmk_grad = torch.empty(((2 * prep.D + 1) * _ext.LMK_SPLIT + 2 * prep.D) * H * prep.S * prep.kp,
                            dtype=torch.float32, device=dev) if prep.kp > 0 else None
     # per-query records (LSE, Delta, window, soft-edge factors) of the tensor-core stages
     qrec = torch.empty(H, T, _ext.QREC_FLOATS, dtype=torch.float32, device=dev)

@@ -155,8 +155,9 @@ typedef struct DsaltAttnParams {
   void* dw;                   /* [T] dtype: Σ_h ∂loss/∂w̃ (train) or NULL */
   float* d_lw;                /* [H,S,k_lmk] fp32, caller slot order: ∂loss/∂lmk_w */
   float* lmk_grad;            /* fp32 scratch of the tensor-core dK/dV stage:
-                                 (2·D + 1)·DSALT_LMK_SPLIT·H·S·kp floats (partial
-                                 landmark-slot dK, dV and d_lw); unused by the SIMT family */
+                                 ((2·D + 1)·DSALT_LMK_SPLIT + 2·D)·H·S·kp floats
+                                 (partial landmark-slot dK, dV, d_lw and the band
+                                 rows of landmark keys); unused by the SIMT family */
   float* qrec;                /* [H,T,DSALT_QREC_FLOATS] fp32 scratch: per-query records
                                  (LSE, Delta, window, soft-edge factors) written by the
                                  preprocess stage and read by the tensor-core dK/dV and dQ

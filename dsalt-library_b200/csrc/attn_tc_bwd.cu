@@ -489,11 +489,11 @@ constexpr int kColWarp = 18;
 constexpr int kMmaWarpB = 19;
 constexpr int kThreadsKV = 640;
 constexpr int kQuarter = BN / 4;  // tile columns per row thread
-enum { KV_FULL = 0, Q_FULL = 1, DO_FULL = Q_FULL + kQStages, QDO_EMPTY = DO_FULL + kQStages,
+enum { KV_FULL = 0, KV_EMPTY = 1, Q_FULL = 2, DO_FULL = Q_FULL + kQStages, QDO_EMPTY = DO_FULL + kQStages,
        REC_FULL = QDO_EMPTY + kQStages, COL_FULL = REC_FULL + kColStages, COL_EMPTY = COL_FULL + kColStages,
-       SD_FULL = COL_EMPTY + kColStages,
-       SD_EMPTY = SD_FULL + 2, PDS_FULL = SD_EMPTY + 2, PDS_EMPTY = PDS_FULL + 1, ROWS = PDS_EMPTY + 1,
-       KV_DONE = ROWS + 1, FINAL = KV_DONE + 1, EPI = FINAL + 2, EPI2 = EPI + 1, NB = EPI2 + 1 };
+       SD_FULL = COL_EMPTY + kColStages, SD_EMPTY = SD_FULL + 2, PDS_FULL = SD_EMPTY + 2, PDS_EMPTY = PDS_FULL + 1,
+       ROWS = PDS_EMPTY + 1, KV_DONE = ROWS + 1, ACC_EMPTY = KV_DONE + 1, FINAL = ACC_EMPTY + 1, EPI = FINAL + 2,
+       NB = EPI + 1 };
 
 // per-tile summary of the query records, written by the column warp
 struct alignas(16) ColStats {
@@ -508,8 +508,8 @@ struct alignas(1024) Smem {
   uint8_t v[BM * D * 2];
   uint8_t q[kQStages][BN * D * 2];
   uint8_t dO[kQStages][BN * D * 2];
-  uint8_t pt[BM * BN * 2];
-  uint8_t dst[BM * BN * 2];
+  uint8_t pt[BM * BN * 2];   // Pᵀ; with dst also the staging area of the band epilogue
+  uint8_t dst[BM * BN * 2];  // dSᵀ
   uint64_t bars[NB];
   uint32_t tmem_base;
   int abort_flag;
@@ -517,50 +517,80 @@ struct alignas(1024) Smem {
   ColStats stats[kColStages];
   float dlw_part[4][BM];  // landmark items: d_lw partial sums of the four column quarters
 };
+static_assert(2 * BM * BN * 2 >= BM * 128 * 2, "the Pᵀ/dSᵀ buffers hold one staged dK or dV block (D ≤ 128)");
+
+// One work item: 128 keys (a band block, or a chunk of sorted landmark slots with
+// one part of its query range) of one (sequence, head), and its query tiles.
+// Every role of the persistent CTA decodes the same items in the same order.
+struct Item {
+  int h, s, key0, nkeys, q_start, n_tiles, part, L;
+  int64_t s0, lbase;
+};
+
+template <bool LMK>
+__device__ __forceinline__ int num_items(const DsaltAttnParams& p) {
+  if (LMK) return p.S * ((p.kp + BM - 1) / BM) * DSALT_LMK_SPLIT * p.H;
+  return __ldg(p.num_blocks) * p.H;
+}
+
+// Decode item idx; called by whole warps (the landmark slot count is a ballot).
+template <bool LMK>
+__device__ __forceinline__ Item decode_item(const DsaltAttnParams& p, int idx) {
+  Item it;
+  it.part = 0;
+  if (LMK) {
+    const int nch = (p.kp + BM - 1) / BM;
+    const int per_h = p.S * nch * DSALT_LMK_SPLIT;
+    it.h = idx / per_h;
+    const int x = idx % per_h;
+    it.part = x % DSALT_LMK_SPLIT;
+    it.s = x / DSALT_LMK_SPLIT / nch;
+    const int chunk = x / DSALT_LMK_SPLIT % nch;
+    it.s0 = __ldg(p.cu_seqlens + it.s);
+    it.L = (int)(__ldg(p.cu_seqlens + it.s + 1) - it.s0);
+    it.lbase = ((int64_t)it.h * p.S + it.s) * p.kp;
+    it.key0 = chunk * BM;
+    // valid slots are a prefix of the sorted list: count them 32 at a time
+    const int lane = threadIdx.x & 31;
+    int nv = 0;
+#pragma unroll
+    for (int k = 0; k < BM / 32; ++k) {
+      const int c = it.key0 + 32 * k + lane;
+      const bool v = c < p.kp && __ldg(p.pos_sorted + it.lbase + c) >= 0;
+      nv += __popc(__ballot_sync(0xffffffffu, v));
+    }
+    it.nkeys = nv;
+    it.q_start = nv > 0 ? __ldg(p.pos_sorted + it.lbase + it.key0) : 0;
+    const int q_end = it.L - 1;
+    int n = (nv > 0 && q_end >= it.q_start) ? (q_end - it.q_start + BN) / BN : 0;
+    const int per = (n + DSALT_LMK_SPLIT - 1) / DSALT_LMK_SPLIT;
+    const int u0 = per * it.part;
+    it.n_tiles = max(0, min(n, u0 + per) - u0);
+    it.q_start += BN * u0;
+  } else {
+    const int nb = __ldg(p.num_blocks);
+    const int blk = idx % nb;
+    it.h = idx / nb;
+    it.s = __ldg(p.block_map + 2 * blk);
+    it.s0 = __ldg(p.cu_seqlens + it.s);
+    it.L = (int)(__ldg(p.cu_seqlens + it.s + 1) - it.s0);
+    it.key0 = __ldg(p.block_map + 2 * blk + 1) * BM;
+    it.nkeys = min(BM, it.L - it.key0);
+    it.q_start = it.key0;
+    it.lbase = ((int64_t)it.h * p.S + it.s) * p.kp;
+    const int q_end = min(it.L - 1, it.key0 + BM - 1 + max(__ldg(p.seq_wmax + it.s), 0));
+    it.n_tiles = q_end >= it.q_start ? (q_end - it.q_start + BN) / BN : 0;
+  }
+  return it;
+}
 
 template <bool LMK, typename T, int D>
 __global__ void __launch_bounds__(kThreadsKV, 1) tc_bwd_dkdv_kernel(const __grid_constant__ BwdArgs a) {
   using namespace sm100;
   const DsaltAttnParams& p = a.p;
-  const int h = blockIdx.y;
-  int s, key0, nkeys, q_start;
-  int64_t s0, lbase;
-  int L;
-  int part = 0;
-  if (LMK) {
-    // blockIdx.x = (s·nch + chunk)·DSALT_LMK_SPLIT + part
-    const int nch = (p.kp + BM - 1) / BM;
-    part = blockIdx.x % DSALT_LMK_SPLIT;
-    s = blockIdx.x / DSALT_LMK_SPLIT / nch;
-    const int chunk = blockIdx.x / DSALT_LMK_SPLIT % nch;
-    s0 = __ldg(p.cu_seqlens + s);
-    L = (int)(__ldg(p.cu_seqlens + s + 1) - s0);
-    lbase = ((int64_t)h * p.S + s) * p.kp;
-    key0 = chunk * BM;
-    int nv = 0;  // valid slots of this chunk
-    while (key0 + nv < p.kp && nv < BM && __ldg(p.pos_sorted + lbase + key0 + nv) >= 0) ++nv;
-    nkeys = nv;
-    if (nkeys == 0) return;
-    q_start = __ldg(p.pos_sorted + lbase + key0);
-  } else {
-    if ((int)blockIdx.x >= __ldg(p.num_blocks)) return;
-    s = __ldg(p.block_map + 2 * blockIdx.x);
-    s0 = __ldg(p.cu_seqlens + s);
-    L = (int)(__ldg(p.cu_seqlens + s + 1) - s0);
-    key0 = __ldg(p.block_map + 2 * blockIdx.x + 1) * BM;
-    nkeys = min(BM, L - key0);
-    q_start = key0;
-    lbase = ((int64_t)h * p.S + s) * p.kp;
-  }
-  const int q_end = LMK ? L - 1 : min(L - 1, key0 + BM - 1 + max(__ldg(p.seq_wmax + s), 0));
-  int n_tiles = q_end >= q_start ? (q_end - q_start + BN) / BN : 0;
-  if (LMK) {
-    // this part's share of the query tiles (possibly none: it then writes zeros)
-    const int per = (n_tiles + DSALT_LMK_SPLIT - 1) / DSALT_LMK_SPLIT;
-    const int u0 = per * part;
-    n_tiles = max(0, min(n_tiles, u0 + per) - u0);
-    q_start += BN * u0;
-  }
+  // persistent CTA: items blockIdx.x, blockIdx.x + gridDim.x, …
+  const int n_items = num_items<LMK>(p);
+  if ((int)blockIdx.x >= n_items) return;  // CTA-uniform, before any barrier or TMEM use
 
   extern __shared__ uint8_t smem_raw[];
   Smem<D>& sm = *reinterpret_cast<Smem<D>*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
@@ -568,8 +598,9 @@ __global__ void __launch_bounds__(kThreadsKV, 1) tc_bwd_dkdv_kernel(const __grid
   constexpr bool kBF16 = !std::is_same<T, __half>::value;
   const BarArray bar{smem_u32(&sm.bars[0])};
   if (tid == 0) {
-    mbar_init(bar[KV_FULL], 1);
     // barriers completed by tcgen05.commit get one arrival from each MMA warp
+    mbar_init(bar[KV_FULL], 1);
+    mbar_init(bar[KV_EMPTY], 2);
     for (int st = 0; st < kQStages; ++st) {
       mbar_init(bar[Q_FULL + st], 1);
       mbar_init(bar[DO_FULL + st], 1);
@@ -588,10 +619,10 @@ __global__ void __launch_bounds__(kThreadsKV, 1) tc_bwd_dkdv_kernel(const __grid
     mbar_init(bar[PDS_EMPTY], 2);
     mbar_init(bar[ROWS], kRowThreads);
     mbar_init(bar[KV_DONE], 2);
+    mbar_init(bar[ACC_EMPTY], kRowThreads);
     mbar_init(bar[FINAL], 1);
     mbar_init(bar[FINAL + 1], 1);
     mbar_init(bar[EPI], kRowThreads);
-    mbar_init(bar[EPI2], kRowThreads);
     fence_mbar_init();
     sm.abort_flag = 0;
   }
@@ -603,64 +634,105 @@ __global__ void __launch_bounds__(kThreadsKV, 1) tc_bwd_dkdv_kernel(const __grid
   volatile int* abort_flag = &sm.abort_flag;
   const uint32_t tS = tmem, tdP = tmem + 2 * BN, tdK = tmem + 4 * BN, tdV = tmem + 4 * BN + D;
   const float inv_tau = 1.0f / p.tau_win;
+  const int stride = gridDim.x;
 
   if (warp == kProducerWarp) {
-    // ---------------------------------------------------- TMA warp: K/V once, then the Q/dO ring
-    if (lane == 0 && n_tiles > 0) {
-      const uint32_t kv_bytes = (LMK ? a.lmk_box : BM) * D * 2;
-      mbar_expect_tx(bar[KV_FULL], 2 * kv_bytes);
+    // ---------------------------------------------------- TMA warp: per item K/V, then the global Q/dO ring
+    int gt = 0, gi = 0, g_issued = 0, kv_issued = 0;
+    bool ok = true;
+    for (int idx = blockIdx.x; ok && idx < n_items; idx += stride) {
+      const Item it = decode_item<LMK>(p, idx);
+      if (it.n_tiles == 0) continue;
+      if (lane == 0) {
+        if (gi >= 1) ok = mbar_wait(bar[KV_EMPTY], (gi - 1) & 1, abort_flag, p.status);
+        if (ok) {
+          const uint32_t kv_bytes = (LMK ? a.lmk_box : BM) * D * 2;
+          mbar_expect_tx(bar[KV_FULL], 2 * kv_bytes);
 #pragma unroll
-      for (int c = 0; c < D / 64; ++c) {
-        if (LMK) {
-          tma_load_3d(smem_u32(sm.k + c * (BM * 128)), &a.tm_lk, bar[KV_FULL], c * 64, key0, h * p.S + s);
-          tma_load_3d(smem_u32(sm.v + c * (BM * 128)), &a.tm_lv, bar[KV_FULL], c * 64, key0, h * p.S + s);
-        } else {
-          tma_load_3d(smem_u32(sm.k + c * (BM * 128)), &a.tm_k, bar[KV_FULL], c * 64, h, (int)(s0 + key0));
-          tma_load_3d(smem_u32(sm.v + c * (BM * 128)), &a.tm_v, bar[KV_FULL], c * 64, h, (int)(s0 + key0));
+          for (int c = 0; c < D / 64; ++c) {
+            if (LMK) {
+              tma_load_3d(smem_u32(sm.k + c * (BM * 128)), &a.tm_lk, bar[KV_FULL], c * 64, it.key0, it.h * p.S + it.s);
+              tma_load_3d(smem_u32(sm.v + c * (BM * 128)), &a.tm_lv, bar[KV_FULL], c * 64, it.key0, it.h * p.S + it.s);
+            } else {
+              tma_load_3d(smem_u32(sm.k + c * (BM * 128)), &a.tm_k, bar[KV_FULL], c * 64, it.h, (int)(it.s0 + it.key0));
+              tma_load_3d(smem_u32(sm.v + c * (BM * 128)), &a.tm_v, bar[KV_FULL], c * 64, it.h, (int)(it.s0 + it.key0));
+            }
+          }
+          kv_issued = gi + 1;
+        }
+        for (int u = 0; ok && u < it.n_tiles; ++u) {
+          const int g = gt + u, st = g % kQStages;
+          if (g >= kQStages && !mbar_wait(bar[QDO_EMPTY + st], (g / kQStages - 1) & 1, abort_flag, p.status)) {
+            ok = false;
+            break;
+          }
+          const int q0 = it.q_start + BN * u;
+          mbar_expect_tx(bar[Q_FULL + st], BN * D * 2);
+#pragma unroll
+          for (int c = 0; c < D / 64; ++c)
+            tma_load_3d(smem_u32(sm.q[st] + c * (BN * 128)), &a.tm_q, bar[Q_FULL + st], c * 64, it.h,
+                        (int)(it.s0 + q0));
+          mbar_expect_tx(bar[DO_FULL + st], BN * D * 2);
+#pragma unroll
+          for (int c = 0; c < D / 64; ++c)
+            tma_load_3d(smem_u32(sm.dO[st] + c * (BN * 128)), &a.tm_do, bar[DO_FULL + st], c * 64, it.h,
+                        (int)(it.s0 + q0));
+          g_issued = g + 1;
         }
       }
-      int issued = 0;
-      for (int u = 0; u < n_tiles; ++u) {
-        const int st = u % kQStages;
-        if (u >= kQStages && !mbar_wait(bar[QDO_EMPTY + st], (u / kQStages - 1) & 1, abort_flag, p.status)) break;
-        const int q0 = q_start + BN * u;
-        mbar_expect_tx(bar[Q_FULL + st], BN * D * 2);
-#pragma unroll
-        for (int c = 0; c < D / 64; ++c)
-          tma_load_3d(smem_u32(sm.q[st] + c * (BN * 128)), &a.tm_q, bar[Q_FULL + st], c * 64, h, (int)(s0 + q0));
-        mbar_expect_tx(bar[DO_FULL + st], BN * D * 2);
-#pragma unroll
-        for (int c = 0; c < D / 64; ++c)
-          tma_load_3d(smem_u32(sm.dO[st] + c * (BN * 128)), &a.tm_do, bar[DO_FULL + st], c * 64, h, (int)(s0 + q0));
-        issued = u + 1;
+      ok = __shfl_sync(0xffffffffu, ok, 0);
+      gt += it.n_tiles;
+      ++gi;
+    }
+    if (lane == 0) {
+      // never leave a TMA write in flight into shared memory
+      for (int g = max(0, g_issued - kQStages); g < g_issued; ++g) {
+        mbar_drain(bar[Q_FULL + g % kQStages], (g / kQStages) & 1);
+        mbar_drain(bar[DO_FULL + g % kQStages], (g / kQStages) & 1);
       }
-      for (int u = max(0, issued - kQStages); u < issued; ++u) {
-        mbar_drain(bar[Q_FULL + u % kQStages], (u / kQStages) & 1);
-        mbar_drain(bar[DO_FULL + u % kQStages], (u / kQStages) & 1);
-      }
-      mbar_drain(bar[KV_FULL], 0);
+      if (kv_issued > 0) mbar_drain(bar[KV_FULL], (kv_issued - 1) & 1);
     }
   } else if (warp == kColWarp) {
     // ---------------------------------------------------- column warp: per-tile query records
     // Lane 0 bulk-copies each tile's records (written by the preprocess stage)
-    // kColStages − 1 tiles ahead; the warp then masks the columns past the
-    // sequence end and summarises the tile for the row warps' mask skipping.
-    const QRec* recg = reinterpret_cast<const QRec*>(p.qrec) + (int64_t)h * p.T + s0;
-    auto issue = [&](int u) {
-      const int st = u % kColStages;
-      const int q0 = q_start + BN * u;
-      const int nrec = (int)min((int64_t)BN, p.T - (s0 + q0));  // never read past the array
+    // kColStages − 1 tiles ahead, across items; the warp then masks the columns
+    // past the sequence end and summarises the tile for the row warps.
+    struct Cur {
+      int idx, u;
+      Item it;
+    };
+    auto seek = [&](Cur& c) {  // first item with tiles at or after c.idx
+      while (c.idx < n_items) {
+        c.it = decode_item<LMK>(p, c.idx);
+        if (c.it.n_tiles > 0) return;
+        c.idx += stride;
+      }
+    };
+    auto advance = [&](Cur& c) {
+      if (++c.u < c.it.n_tiles) return;
+      c.u = 0;
+      c.idx += stride;
+      seek(c);
+    };
+    auto issue = [&](const Cur& c, int g) {
+      const int st = g % kColStages;
+      const int q0 = c.it.q_start + BN * c.u;
+      const QRec* recg = reinterpret_cast<const QRec*>(p.qrec) + (int64_t)c.it.h * p.T + c.it.s0;
+      const int nrec = (int)min((int64_t)BN, p.T - (c.it.s0 + q0));  // never read past the array
       mbar_expect_tx(bar[REC_FULL + st], nrec * (uint32_t)sizeof(QRec));
       bulk_load(smem_u32(&sm.rec[st][0]), recg + q0, nrec * (uint32_t)sizeof(QRec), bar[REC_FULL + st]);
     };
-    if (lane == 0)
-      for (int u = 0; u < min(n_tiles, kColStages - 1); ++u) issue(u);
-    int issued = min(n_tiles, kColStages - 1);
-    for (int u = 0; u < n_tiles; ++u) {
-      const int st = u % kColStages;
-      if (!__all_sync(0xffffffffu, mbar_wait(bar[REC_FULL + st], (u / kColStages) & 1, abort_flag, p.status)))
+    Cur ci{(int)blockIdx.x, 0, Item{}}, cp{(int)blockIdx.x, 0, Item{}};
+    seek(ci);
+    seek(cp);
+    int g_issued = 0;
+    for (; ci.idx < n_items && g_issued < kColStages - 1; ++g_issued, advance(ci))
+      if (lane == 0) issue(ci, g_issued);
+    for (int g = 0; cp.idx < n_items; ++g, advance(cp)) {
+      const int st = g % kColStages;
+      if (!__all_sync(0xffffffffu, mbar_wait(bar[REC_FULL + st], (g / kColStages) & 1, abort_flag, p.status)))
         break;
-      const int q0 = q_start + BN * u;
+      const int q0 = cp.it.q_start + BN * cp.u;
       // per lane: columns lane (quarter lane/16) and lane + 32 (quarter 2 + lane/16)
       int st_lo_max[2], st_lo_min[2], st_qi_min[2], st_qi_max[2], st_elo_min[2], st_ehi_max[2];
       float st_wlo_min[2];
@@ -668,12 +740,12 @@ __global__ void __launch_bounds__(kThreadsKV, 1) tc_bwd_dkdv_kernel(const __grid
       for (int k2 = 0; k2 < 2; ++k2) {
         const int c = lane + 32 * k2;
         QRec& rc = sm.rec[st][c];
-        if (q0 + c >= L) {  // another sequence's query (or past the array): no pairs
+        if (q0 + c >= cp.it.L) {  // another sequence's query (or past the array): no pairs
           rc.nlse2 = 0.f; rc.delta = 0.f; rc.lo = INT_MAX; rc.qi = INT_MIN;
           rc.wlo = -INFINITY; rc.ehi = INT_MIN; rc.elo = INT_MAX;
         }
-        const int clo = rc.lo, ci = rc.qi;
-        st_lo_max[k2] = clo; st_lo_min[k2] = clo; st_qi_min[k2] = ci; st_qi_max[k2] = ci; st_wlo_min[k2] = rc.wlo;
+        const int clo = rc.lo, ci_ = rc.qi;
+        st_lo_max[k2] = clo; st_lo_min[k2] = clo; st_qi_min[k2] = ci_; st_qi_max[k2] = ci_; st_wlo_min[k2] = rc.wlo;
         st_elo_min[k2] = rc.elo; st_ehi_max[k2] = rc.ehi;
       }
 #pragma unroll
@@ -700,73 +772,92 @@ __global__ void __launch_bounds__(kThreadsKV, 1) tc_bwd_dkdv_kernel(const __grid
         }
       }
       mbar_arrive(bar[COL_FULL + st]);
-      // refill the stage of tile u − 1 with tile u + kColStages − 1 once the rows released it
-      if (issued < n_tiles) {
-        const int nu = issued;  // == u + kColStages − 1
-        if (nu >= kColStages &&
+      // refill the stage of tile g − 1 with the next tile once the rows released it
+      if (ci.idx < n_items) {
+        const int ng = g_issued;  // == g + kColStages − 1
+        if (ng >= kColStages &&
             !__all_sync(0xffffffffu,
-                        mbar_wait(bar[COL_EMPTY + nu % kColStages], (nu / kColStages - 1) & 1, abort_flag, p.status)))
+                        mbar_wait(bar[COL_EMPTY + ng % kColStages], (ng / kColStages - 1) & 1, abort_flag, p.status)))
           break;
-        if (lane == 0) issue(nu);
-        ++issued;
+        if (lane == 0) issue(ci, ng);
+        ++g_issued;
+        advance(ci);
       }
     }
     if (lane == 0)
-      for (int u = max(0, issued - kColStages); u < issued; ++u)
-        mbar_drain(bar[REC_FULL + u % kColStages], (u / kColStages) & 1);
+      for (int g = max(0, g_issued - kColStages); g < g_issued; ++g)
+        mbar_drain(bar[REC_FULL + g % kColStages], (g / kColStages) & 1);
   } else if (warp == kMmaWarp || warp == kMmaWarpB) {
     // ---------------------------------------------------- MMA issuers
     // Two warps issue so that their MMAs overlap (one issuing thread sustains
-    // only about one MMA per 110 cycles): warp 9 issues Sᵀ = K·Qᵀ and
-    // dV += Pᵀ·dO, warp 11 dPᵀ = V·dOᵀ and dK += dSᵀ·Q.  Barriers they both
-    // complete count two arrivals.
+    // only about one MMA per 110 cycles): warp A issues Sᵀ = K·Qᵀ and
+    // dV += Pᵀ·dO, warp B dPᵀ = V·dOᵀ and dK += dSᵀ·Q.  Barriers they both
+    // complete count two arrivals.  An item's first two Sᵀ / dPᵀ run while the
+    // row warps still store the previous item (its accumulators are only
+    // overwritten after the epilogue released them: ACC_EMPTY).
     const bool is_a = warp == kMmaWarp;
-    if (lane == 0 && n_tiles > 0) {
-      const uint32_t id_s = idesc_f16(kBF16, BM, BN, false, false);
-      const uint32_t id_kv = idesc_f16(kBF16, BM, D, false, true);
-      const uint32_t kv_addr = smem_u32(is_a ? sm.k : sm.v);
-      const uint32_t pds = smem_u32(is_a ? sm.pt : sm.dst);
-      const uint32_t t_sd = is_a ? tS : tdP, t_acc = is_a ? tdV : tdK;
-      bool ok = mbar_wait(bar[KV_FULL], 0, abort_flag, p.status);
-      // operand tiles: Sᵀ reads Q, dPᵀ reads dO; dV reads dO, dK reads Q
-      auto tile_sd = [&](int qs) { return smem_u32(is_a ? sm.q[qs] : sm.dO[qs]); };
-      auto tile_acc = [&](int qs) { return smem_u32(is_a ? sm.dO[qs] : sm.q[qs]); };
-      auto issue_sd = [&](int u) -> bool {
-        const int st = u & 1, qs = u % kQStages;
-        if (!mbar_wait(bar[(is_a ? Q_FULL : DO_FULL) + qs], (u / kQStages) & 1, abort_flag, p.status)) return false;
-        if (u >= 2 && !mbar_wait(bar[SD_EMPTY + st], ((u >> 1) - 1) & 1, abort_flag, p.status)) return false;
-        tc_fence_after();
-        const uint32_t ba = tile_sd(qs);
+    const uint32_t id_s = idesc_f16(kBF16, BM, BN, false, false);
+    const uint32_t id_kv = idesc_f16(kBF16, BM, D, false, true);
+    const uint32_t kv_addr = smem_u32(is_a ? sm.k : sm.v);
+    const uint32_t pds = smem_u32(is_a ? sm.pt : sm.dst);
+    const uint32_t t_sd = is_a ? tS : tdP, t_acc = is_a ? tdV : tdK;
+    // operand tiles: Sᵀ reads Q, dPᵀ reads dO; dV reads dO, dK reads Q
+    auto tile_sd = [&](int qs) { return smem_u32(is_a ? sm.q[qs] : sm.dO[qs]); };
+    auto tile_acc = [&](int qs) { return smem_u32(is_a ? sm.dO[qs] : sm.q[qs]); };
+    auto issue_sd = [&](int g) -> bool {
+      const int st = g & 1, qs = g % kQStages;
+      if (!mbar_wait(bar[(is_a ? Q_FULL : DO_FULL) + qs], (g / kQStages) & 1, abort_flag, p.status)) return false;
+      if (g >= 2 && !mbar_wait(bar[SD_EMPTY + st], ((g >> 1) - 1) & 1, abort_flag, p.status)) return false;
+      tc_fence_after();
+      const uint32_t ba = tile_sd(qs);
 #pragma unroll
-        for (int kk = 0; kk < D / 16; ++kk) {
-          const uint32_t aoff = (kk >> 2) * (BM * 128) + (kk & 3) * 32;
-          const uint32_t boff = (kk >> 2) * (BN * 128) + (kk & 3) * 32;
-          mma_f16(t_sd + st * BN, sdesc_sw128(kv_addr + aoff, 16, 1024), sdesc_sw128(ba + boff, 16, 1024), id_s,
-                  kk > 0 ? 1u : 0u);
-        }
-        mma_commit(bar[SD_FULL + st]);
-        return true;
-      };
-      if (ok) ok = issue_sd(0);
-      if (ok && n_tiles > 1) ok = issue_sd(1);
-      for (int u = 0; ok && u < n_tiles; ++u) {
-        const int qs = u % kQStages;
-        if (!mbar_wait(bar[PDS_FULL], u & 1, abort_flag, p.status)) { ok = false; break; }
-        if (!mbar_wait(bar[(is_a ? DO_FULL : Q_FULL) + qs], (u / kQStages) & 1, abort_flag, p.status)) {
-          ok = false;
-          break;
-        }
-        tc_fence_after();
-        const uint32_t ba = tile_acc(qs);
-#pragma unroll
-        for (int kk = 0; kk < BN / 16; ++kk)
-          mma_f16(t_acc, sdesc_sw128(pds + kk * 32, 16, 1024), sdesc_sw128(ba + kk * 2048, BN * 128, 1024), id_kv,
-                  (u > 0 || kk > 0) ? 1u : 0u);
-        mma_commit(bar[PDS_EMPTY]);
-        mma_commit(bar[QDO_EMPTY + qs]);
-        if (u + 2 < n_tiles && !issue_sd(u + 2)) { ok = false; break; }
+      for (int kk = 0; kk < D / 16; ++kk) {
+        const uint32_t aoff = (kk >> 2) * (BM * 128) + (kk & 3) * 32;
+        const uint32_t boff = (kk >> 2) * (BN * 128) + (kk & 3) * 32;
+        mma_f16(t_sd + st * BN, sdesc_sw128(kv_addr + aoff, 16, 1024), sdesc_sw128(ba + boff, 16, 1024), id_s,
+                kk > 0 ? 1u : 0u);
       }
-      mma_commit(bar[KV_DONE]);
+      mma_commit(bar[SD_FULL + st]);
+      return true;
+    };
+    int gt = 0, gi = 0;
+    bool ok = true;
+    for (int idx = blockIdx.x; ok && idx < n_items; idx += stride) {
+      const Item it = decode_item<LMK>(p, idx);
+      const int n = it.n_tiles;
+      if (n == 0) continue;
+      if (lane == 0) {
+        ok = mbar_wait(bar[KV_FULL], gi & 1, abort_flag, p.status);
+        if (ok) ok = issue_sd(gt);
+        if (ok && n > 1) ok = issue_sd(gt + 1);
+        if (ok && n <= 2) mma_commit(bar[KV_EMPTY]);  // every Sᵀ / dPᵀ of the item is issued
+        for (int u = 0; ok && u < n; ++u) {
+          const int g = gt + u, qs = g % kQStages;
+          ok = mbar_wait(bar[PDS_FULL], g & 1, abort_flag, p.status) &&
+               mbar_wait(bar[(is_a ? DO_FULL : Q_FULL) + qs], (g / kQStages) & 1, abort_flag, p.status) &&
+               (u > 0 || gi == 0 || mbar_wait(bar[ACC_EMPTY], (gi - 1) & 1, abort_flag, p.status));
+          if (!ok) break;
+          tc_fence_after();
+          const uint32_t ba = tile_acc(qs);
+#pragma unroll
+          for (int kk = 0; kk < BN / 16; ++kk)
+            mma_f16(t_acc, sdesc_sw128(pds + kk * 32, 16, 1024), sdesc_sw128(ba + kk * 2048, BN * 128, 1024),
+                    id_kv, (u > 0 || kk > 0) ? 1u : 0u);
+          mma_commit(bar[PDS_EMPTY]);
+          mma_commit(bar[QDO_EMPTY + qs]);
+          if (u + 2 < n) {
+            ok = issue_sd(g + 2);
+            if (ok && u + 2 == n - 1) mma_commit(bar[KV_EMPTY]);
+          }
+        }
+        if (ok) mma_commit(bar[KV_DONE]);
+      }
+      ok = __shfl_sync(0xffffffffu, ok, 0);
+      gt += n;
+      ++gi;
+    }
+    if (lane == 0) {
+      // every issued MMA completes before TMEM is released
       mma_commit(bar[FINAL + (is_a ? 0 : 1)]);
       mbar_drain(bar[FINAL + (is_a ? 0 : 1)], 0);
     }
@@ -777,221 +868,243 @@ __global__ void __launch_bounds__(kThreadsKV, 1) tc_bwd_dkdv_kernel(const __grid
     const int c0 = kQuarter * quarter;     // this thread's first column of a tile
     const uint32_t lane_addr = ((uint32_t)(32 * (warp & 3)) << 16);
     const float sl2 = p.scale * kLog2e;
-    const bool key_ok = r < nkeys;
-    const int j = LMK ? (key_ok ? __ldg(p.pos_sorted + lbase + key0 + r) : INT_MAX) : key0 + r;
-    const float lw2 = (LMK && key_ok) ? __ldg(p.w_sorted + lbase + key0 + r) * kLog2e : 0.f;
-    // key range of this warp's 32 rows (band: consecutive; landmarks: sorted positions)
-    // first landmark slot at this key (band items; -1: none), used by the epilogue
-    const int cl_first = (!LMK && key_ok && p.lmk_slot) ? __ldg(p.lmk_slot + (s0 + j) * p.H + h) : -1;
-    const int jf = LMK ? __shfl_sync(0xffffffffu, j, 0) : key0 + 32 * (warp & 3);
-    const int jl = LMK ? __reduce_max_sync(0xffffffffu, key_ok ? j : INT_MIN) : jf + 31;
-    const bool warp_keys_ok = __all_sync(0xffffffffu, key_ok);
-    float dlw = 0.f;
+    int gt = 0, gi = 0, rows_phase = 0, epi_phase = 0;
     bool ok = true;
-    int rows_phase = 0;
-    for (int u = 0; u < n_tiles; ++u) {
-      const int st = u & 1, cs = u % kColStages;
-      ok = mbar_wait(bar[SD_FULL + st], (u >> 1) & 1, abort_flag, p.status) &&
-           mbar_wait(bar[COL_FULL + cs], (u / kColStages) & 1, abort_flag, p.status);
-      if (!__all_sync(0xffffffffu, ok)) { ok = false; break; }
-      tc_fence_after();
-      const QRec* rec = &sm.rec[cs][c0];
-      const ColStats& cst = sm.stats[cs];
-      bool all_in, all_out;
-      if (LMK) {
-        all_in = warp_keys_ok && cst.qi_min[quarter] >= jl && cst.wlo_min[quarter] > (float)jl;
-        all_out = false;
-      } else {
-        all_in = cst.lo_max[quarter] <= jf && cst.qi_min[quarter] >= jl;
-        all_out = cst.lo_min[quarter] > jl || cst.qi_max[quarter] < jf;
+    // all row threads meet (bounded wait on the EPI barrier)
+    auto rows_sync = [&]() -> bool {
+      mbar_arrive(bar[EPI]);
+      const bool w = mbar_wait(bar[EPI], epi_phase & 1, abort_flag, p.status);
+      ++epi_phase;
+      return __all_sync(0xffffffffu, w);
+    };
+    for (int idx = blockIdx.x; ok && idx < n_items; idx += stride) {
+      const Item it = decode_item<LMK>(p, idx);
+      const int n = it.n_tiles, key0 = it.key0, nkeys = it.nkeys, h = it.h;
+      const int64_t s0 = it.s0, lbase = it.lbase;
+      const bool key_ok = r < nkeys;
+      const int j = LMK ? (key_ok ? __ldg(p.pos_sorted + lbase + key0 + r) : INT_MAX) : key0 + r;
+      if (n == 0) {
+        // a landmark part without queries: its partial sums are zero
+        if (LMK && key_ok) {
+          const int64_t slot = it.part * a.part_stride + lbase + key0 + r;
+          const float4 z = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+          for (int e = 0; e < D / 4; e += 4) {
+            *reinterpret_cast<float4*>(a.dk_lmk + slot * D + quarter * (D / 4) + e) = z;
+            *reinterpret_cast<float4*>(a.dv_lmk + slot * D + quarter * (D / 4) + e) = z;
+          }
+          if (quarter == 0) a.dlw_lmk[slot] = 0.f;
+        }
+        continue;
       }
-      // Pᵀ and dSᵀ of this thread's 16 columns, packed to the input dtype
-      uint32_t pk_p[8], pk_d[8];
+      const float lw2 = (LMK && key_ok) ? __ldg(p.w_sorted + lbase + key0 + r) * kLog2e : 0.f;
+      // first landmark slot at this key (band items; -1: none), used by the epilogue
+      const int cl_first = (!LMK && key_ok && p.lmk_slot) ? __ldg(p.lmk_slot + (s0 + j) * p.H + h) : -1;
+      // key range of this warp's 32 rows (band: consecutive; landmarks: sorted positions)
+      const int jf = LMK ? __shfl_sync(0xffffffffu, j, 0) : key0 + 32 * (warp & 3);
+      const int jl = LMK ? __reduce_max_sync(0xffffffffu, key_ok ? j : INT_MIN) : jf + 31;
+      const bool warp_keys_ok = __all_sync(0xffffffffu, key_ok);
       const float jfl = (float)j;
-      if (all_out) {
-        tc_fence_before();
-        mbar_arrive(bar[SD_EMPTY + st]);
+      float dlw = 0.f;
+      for (int u = 0; u < n; ++u) {
+        const int g = gt + u, st = g & 1, cs = g % kColStages;
+        ok = mbar_wait(bar[SD_FULL + st], (g >> 1) & 1, abort_flag, p.status) &&
+             mbar_wait(bar[COL_FULL + cs], (g / kColStages) & 1, abort_flag, p.status);
+        if (!__all_sync(0xffffffffu, ok)) { ok = false; break; }
+        tc_fence_after();
+        const QRec* rec = &sm.rec[cs][c0];
+        const ColStats& cst = sm.stats[cs];
+        bool all_in, all_out;
+        if (LMK) {
+          all_in = warp_keys_ok && cst.qi_min[quarter] >= jl && cst.wlo_min[quarter] > (float)jl;
+          all_out = false;
+        } else {
+          all_in = cst.lo_max[quarter] <= jf && cst.qi_min[quarter] >= jl;
+          all_out = cst.lo_min[quarter] > jl || cst.qi_max[quarter] < jf;
+        }
+        // Pᵀ and dSᵀ of this thread's 16 columns, packed to the input dtype
+        uint32_t pk_p[8], pk_d[8];
+        if (all_out) {
+          tc_fence_before();
+          mbar_arrive(bar[SD_EMPTY + st]);
 #pragma unroll
-        for (int g = 0; g < 8; ++g) { pk_p[g] = 0u; pk_d[g] = 0u; }
-      } else {
-        float sv[16], dpv[16];
-        tmem_ld16(tS + lane_addr + st * BN + c0, sv);
-        tmem_ld16(tdP + lane_addr + st * BN + c0, dpv);
-        tmem_wait_ld();
-        tc_fence_before();
-        mbar_arrive(bar[SD_EMPTY + st]);
+          for (int q = 0; q < 8; ++q) { pk_p[q] = 0u; pk_d[q] = 0u; }
+        } else {
+          float sv[16], dpv[16];
+          tmem_ld16(tS + lane_addr + st * BN + c0, sv);
+          tmem_ld16(tdP + lane_addr + st * BN + c0, dpv);
+          tmem_wait_ld();
+          tc_fence_before();
+          mbar_arrive(bar[SD_EMPTY + st]);
 #pragma unroll
-        for (int c = 0; c < 16; c += 2) {
-          float pr2[2], ds2[2];
+          for (int c = 0; c < 16; c += 2) {
+            float pr2[2], ds2[2];
 #pragma unroll
-          for (int e = 0; e < 2; ++e) {
-            const QRec& rq = rec[c + e];
-            const float4 r0 = *reinterpret_cast<const float4*>(&rq.nlse2);  // nlse2, delta, lo, qi
-            bool valid;
-            float pr;
-            if (LMK) {
-              pr = fast_exp2(fmaf(sv[c + e], sl2, lw2 + r0.x));
-              valid = all_in || (key_ok && j <= __float_as_int(r0.w) && jfl < rq.wlo);
-            } else {
-              pr = fast_exp2(fmaf(sv[c + e], sl2, r0.x));
-              valid = all_in || (j >= __float_as_int(r0.z) && j <= __float_as_int(r0.w));
+            for (int e = 0; e < 2; ++e) {
+              const QRec& rq = rec[c + e];
+              const float4 r0 = *reinterpret_cast<const float4*>(&rq.nlse2);  // nlse2, delta, lo, qi
+              bool valid;
+              float pr;
+              if (LMK) {
+                pr = fast_exp2(fmaf(sv[c + e], sl2, lw2 + r0.x));
+                valid = all_in || (key_ok && j <= __float_as_int(r0.w) && jfl < rq.wlo);
+              } else {
+                pr = fast_exp2(fmaf(sv[c + e], sl2, r0.x));
+                valid = all_in || (j >= __float_as_int(r0.z) && j <= __float_as_int(r0.w));
+              }
+              const float dsv = pr * (dpv[c + e] - r0.y);
+              pr2[e] = valid ? pr : 0.f;
+              ds2[e] = valid ? dsv : 0.f;
+              if (LMK) dlw += ds2[e];
             }
-            const float dsv = pr * (dpv[c + e] - r0.y);
-            pr2[e] = valid ? pr : 0.f;
-            ds2[e] = valid ? dsv : 0.f;
-            if (LMK) dlw += ds2[e];
+            pk_p[c / 2] = pack2(pr2[0], pr2[1], kBF16);
+            pk_d[c / 2] = pack2(ds2[0], ds2[1], kBF16);
           }
-          pk_p[c / 2] = pack2(pr2[0], pr2[1], kBF16);
-          pk_d[c / 2] = pack2(ds2[0], ds2[1], kBF16);
         }
-      }
-      // the single Pᵀ / dSᵀ buffer is free once the previous tile's dV / dK MMAs completed
-      if (u >= 1) {
-        ok = mbar_wait(bar[PDS_EMPTY], (u - 1) & 1, abort_flag, p.status);
-        if (!__all_sync(0xffffffffu, ok)) { ok = false; break; }
-      }
+        // the single Pᵀ / dSᵀ buffer is free once the previous tile's dV / dK MMAs completed
+        if (g >= 1) {
+          ok = mbar_wait(bar[PDS_EMPTY], (g - 1) & 1, abort_flag, p.status);
+          if (!__all_sync(0xffffffffu, ok)) { ok = false; break; }
+        }
 #pragma unroll
-      for (int g = 0; g < 2; ++g) {
-        *reinterpret_cast<uint4*>(sm.pt + sw128_offset(r, c0 + 8 * g)) =
-            make_uint4(pk_p[4 * g], pk_p[4 * g + 1], pk_p[4 * g + 2], pk_p[4 * g + 3]);
-        *reinterpret_cast<uint4*>(sm.dst + sw128_offset(r, c0 + 8 * g)) =
-            make_uint4(pk_d[4 * g], pk_d[4 * g + 1], pk_d[4 * g + 2], pk_d[4 * g + 3]);
-      }
-      // soft window edge (band items): Pᵀ, dSᵀ *= σ((w̃ − d)/τ) on each query
-      // column's edge keys, spread over the 512 row threads (column tid % 64, edge
-      // index tid / 64) once every row has stored its entries
-      const bool tile_edge = !LMK && min(min(cst.elo_min[0], cst.elo_min[1]), min(cst.elo_min[2], cst.elo_min[3])) <=
-                                         key0 + nkeys - 1 &&
-                             max(max(cst.ehi_max[0], cst.ehi_max[1]), max(cst.ehi_max[2], cst.ehi_max[3])) >= key0;
-      if (tile_edge) {
-        mbar_arrive(bar[ROWS]);
-        ok = mbar_wait(bar[ROWS], rows_phase & 1, abort_flag, p.status);
-        ++rows_phase;
-        if (!__all_sync(0xffffffffu, ok)) { ok = false; break; }
-        const int col = tid & (BN - 1);
-        const QRec& rc = sm.rec[cs][col];
-        const int ne = qrec_ne(rc), ehi = rc.ehi;
-        {
-          const int e = tid >> 6;
-          const int rr = ehi - e - key0;
-          if (e < ne && rr >= 0 && rr < nkeys) {
-            const uint32_t off = sw128_offset(rr, col);
-            const float a1 = to_f32<T>(*reinterpret_cast<const T*>(sm.pt + off));
-            const float a2 = to_f32<T>(*reinterpret_cast<const T*>(sm.dst + off));
-            const float g = rc.eg[e];
-            *reinterpret_cast<T*>(sm.pt + off) = from_f32<T>(a1 * g);
-            *reinterpret_cast<T*>(sm.dst + off) = from_f32<T>(a2 * g);
-          }
+        for (int q = 0; q < 2; ++q) {
+          *reinterpret_cast<uint4*>(sm.pt + sw128_offset(r, c0 + 8 * q)) =
+              make_uint4(pk_p[4 * q], pk_p[4 * q + 1], pk_p[4 * q + 2], pk_p[4 * q + 3]);
+          *reinterpret_cast<uint4*>(sm.dst + sw128_offset(r, c0 + 8 * q)) =
+              make_uint4(pk_d[4 * q], pk_d[4 * q + 1], pk_d[4 * q + 2], pk_d[4 * q + 3]);
         }
-        if (tid < BN && ne > kMaxEdge) {
-          // wider soft edges than the precomputed factors: the rest one key at a time
-          for (int e = kMaxEdge; e < ne; ++e) {
+        // soft window edge (band items): Pᵀ, dSᵀ *= σ((w̃ − d)/τ) on each query
+        // column's edge keys, spread over the 512 row threads (column tid % 64, edge
+        // index tid / 64) once every row has stored its entries
+        const bool tile_edge =
+            !LMK && min(min(cst.elo_min[0], cst.elo_min[1]), min(cst.elo_min[2], cst.elo_min[3])) <= key0 + nkeys - 1 &&
+            max(max(cst.ehi_max[0], cst.ehi_max[1]), max(cst.ehi_max[2], cst.ehi_max[3])) >= key0;
+        if (tile_edge) {
+          mbar_arrive(bar[ROWS]);
+          ok = mbar_wait(bar[ROWS], rows_phase & 1, abort_flag, p.status);
+          ++rows_phase;
+          if (!__all_sync(0xffffffffu, ok)) { ok = false; break; }
+          const int col = tid & (BN - 1);
+          const QRec& rc = sm.rec[cs][col];
+          const int ne = qrec_ne(rc), ehi = rc.ehi;
+          {
+            const int e = tid >> 6;
             const int rr = ehi - e - key0;
-            if (rr < 0) break;
-            if (rr >= nkeys) continue;
-            const float sg = qrec_edge_factor(rc.wt, rc.qi - (ehi - e), inv_tau);
-            T* e1 = reinterpret_cast<T*>(sm.pt + sw128_offset(rr, col));
-            T* e2 = reinterpret_cast<T*>(sm.dst + sw128_offset(rr, col));
-            *e1 = from_f32<T>(to_f32<T>(*e1) * sg);
-            *e2 = from_f32<T>(to_f32<T>(*e2) * sg);
+            if (e < ne && rr >= 0 && rr < nkeys) {
+              const uint32_t off = sw128_offset(rr, col);
+              const float a1 = to_f32<T>(*reinterpret_cast<const T*>(sm.pt + off));
+              const float a2 = to_f32<T>(*reinterpret_cast<const T*>(sm.dst + off));
+              const float gf = rc.eg[e];
+              *reinterpret_cast<T*>(sm.pt + off) = from_f32<T>(a1 * gf);
+              *reinterpret_cast<T*>(sm.dst + off) = from_f32<T>(a2 * gf);
+            }
+          }
+          if (tid < BN && ne > kMaxEdge) {
+            // wider soft edges than the precomputed factors: the rest one key at a time
+            for (int e = kMaxEdge; e < ne; ++e) {
+              const int rr = ehi - e - key0;
+              if (rr < 0) break;
+              if (rr >= nkeys) continue;
+              const float sg = qrec_edge_factor(rc.wt, rc.qi - (ehi - e), inv_tau);
+              T* e1 = reinterpret_cast<T*>(sm.pt + sw128_offset(rr, col));
+              T* e2 = reinterpret_cast<T*>(sm.dst + sw128_offset(rr, col));
+              *e1 = from_f32<T>(to_f32<T>(*e1) * sg);
+              *e2 = from_f32<T>(to_f32<T>(*e2) * sg);
+            }
           }
         }
+        fence_async_smem();
+        mbar_arrive(bar[PDS_FULL]);
+        mbar_arrive(bar[COL_EMPTY + cs]);
       }
-      fence_async_smem();
-      mbar_arrive(bar[PDS_FULL]);
-      mbar_arrive(bar[COL_EMPTY + cs]);
-    }
-    if (ok && n_tiles > 0) {
-      ok = mbar_wait(bar[KV_DONE], 0, abort_flag, p.status);
-      ok = __all_sync(0xffffffffu, ok);
+      if (!ok) break;
+      ok = __all_sync(0xffffffffu, mbar_wait(bar[KV_DONE], gi & 1, abort_flag, p.status));
+      if (!ok) break;
       tc_fence_after();
-    }
-    const bool have = ok && n_tiles > 0;
-    // this thread handles dK/dV columns [quarter·D/4, (quarter+1)·D/4) of key row r
-    if (LMK) {
-      const int64_t slot = part * a.part_stride + lbase + key0 + r;
-      float* dkl = a.dk_lmk + slot * D;
-      float* dvl = a.dv_lmk + slot * D;
+      // this thread handles dK/dV columns [quarter·D/4, (quarter+1)·D/4) of key row r
+      if (LMK) {
+        const int64_t slot = it.part * a.part_stride + lbase + key0 + r;
+        float* dkl = a.dk_lmk + slot * D;
+        float* dvl = a.dv_lmk + slot * D;
 #pragma unroll
-      for (int ch = 0; ch < D / 64; ++ch) {
-        const int col = quarter * (D / 4) + ch * 16;
-        float kk_[16], vv[16];
-        if (have) {
+        for (int ch = 0; ch < D / 64; ++ch) {
+          const int col = quarter * (D / 4) + ch * 16;
+          float kk_[16], vv[16];
           tmem_ld16(tdK + lane_addr + col, kk_);
           tmem_ld16(tdV + lane_addr + col, vv);
           tmem_wait_ld();
-        } else {
+          if (key_ok) {
 #pragma unroll
-          for (int e = 0; e < 16; ++e) { kk_[e] = 0.f; vv[e] = 0.f; }
-        }
-        if (key_ok) {
-#pragma unroll
-          for (int e = 0; e < 16; e += 4) {
-            *reinterpret_cast<float4*>(dkl + col + e) =
-                make_float4(kk_[e] * p.scale, kk_[e + 1] * p.scale, kk_[e + 2] * p.scale, kk_[e + 3] * p.scale);
-            *reinterpret_cast<float4*>(dvl + col + e) = make_float4(vv[e], vv[e + 1], vv[e + 2], vv[e + 3]);
+            for (int e = 0; e < 16; e += 4) {
+              *reinterpret_cast<float4*>(dkl + col + e) =
+                  make_float4(kk_[e] * p.scale, kk_[e + 1] * p.scale, kk_[e + 2] * p.scale, kk_[e + 3] * p.scale);
+              *reinterpret_cast<float4*>(dvl + col + e) = make_float4(vv[e], vv[e + 1], vv[e + 2], vv[e + 3]);
+            }
           }
         }
-      }
-      // d_lw of the slot: sum of the four column quarters, in quarter order
-      sm.dlw_part[quarter][r] = dlw;
-      mbar_arrive(bar[EPI]);
-      const bool ok2 = mbar_wait(bar[EPI], 0, abort_flag, p.status);
-      if (quarter == 0 && key_ok)
-        a.dlw_lmk[slot] = (have && ok2)
-            ? ((sm.dlw_part[0][r] + sm.dlw_part[1][r]) + (sm.dlw_part[2][r] + sm.dlw_part[3][r])) : 0.f;
-    } else if (ok) {
-      // The rows are staged (dK in the Q ring, dV in the dO ring, 16-byte units
-      // XOR-swizzled by row % 8) and stored row-contiguously.  A key that holds
-      // landmark slots (first slot cl_first) also leaves its fp32 rows in the
-      // band scratch: lmk_fixup_kernel adds the landmark pass's parts to them and
-      // rounds once.
-      constexpr int kUnits = D * 2 / 16;
-      uint8_t* stage_k = sm.q[0];
-      uint8_t* stage_v = sm.dO[0];
-      float* bk = cl_first >= 0 ? a.band_lmk + (lbase + cl_first) * D : nullptr;
-      float* bv = cl_first >= 0 ? a.band_lmk + a.part_stride * D + (lbase + cl_first) * D : nullptr;
-#pragma unroll 1
-      for (int ch = 0; ch < D / 32; ++ch) {  // 8 columns at a time
-        const int col = quarter * (D / 4) + ch * 8;
-        float kk_[8], vv[8];
-        if (n_tiles > 0) {
-          tmem_ld8(tdK + lane_addr + col, kk_);
-          tmem_ld8(tdV + lane_addr + col, vv);
-          tmem_wait_ld();
-        } else {
-#pragma unroll
-          for (int e = 0; e < 8; ++e) { kk_[e] = 0.f; vv[e] = 0.f; }
-        }
-#pragma unroll
-        for (int e = 0; e < 8; ++e) kk_[e] *= p.scale;
-        if (bk) {
-          *reinterpret_cast<float4*>(bk + col) = make_float4(kk_[0], kk_[1], kk_[2], kk_[3]);
-          *reinterpret_cast<float4*>(bk + col + 4) = make_float4(kk_[4], kk_[5], kk_[6], kk_[7]);
-          *reinterpret_cast<float4*>(bv + col) = make_float4(vv[0], vv[1], vv[2], vv[3]);
-          *reinterpret_cast<float4*>(bv + col + 4) = make_float4(vv[4], vv[5], vv[6], vv[7]);
-        }
-        const int un = col / 8;
-        uint4 u0, u1;
-        u0.x = pack2(kk_[0], kk_[1], kBF16); u0.y = pack2(kk_[2], kk_[3], kBF16);
-        u0.z = pack2(kk_[4], kk_[5], kBF16); u0.w = pack2(kk_[6], kk_[7], kBF16);
-        u1.x = pack2(vv[0], vv[1], kBF16); u1.y = pack2(vv[2], vv[3], kBF16);
-        u1.z = pack2(vv[4], vv[5], kBF16); u1.w = pack2(vv[6], vv[7], kBF16);
-        *reinterpret_cast<uint4*>(stage_k + r * (kUnits * 16) + ((un ^ (r & 7)) << 4)) = u0;
-        *reinterpret_cast<uint4*>(stage_v + r * (kUnits * 16) + ((un ^ (r & 7)) << 4)) = u1;
-      }
-      mbar_arrive(bar[EPI2]);
-      if (__all_sync(0xffffffffu, mbar_wait(bar[EPI2], 0, abort_flag, p.status))) {
+        tc_fence_before();
+        mbar_arrive(bar[ACC_EMPTY]);
+        // d_lw of the slot: sum of the four column quarters, in quarter order
+        sm.dlw_part[quarter][r] = dlw;
+        ok = rows_sync();
+        if (quarter == 0 && key_ok)
+          a.dlw_lmk[slot] = ok ? ((sm.dlw_part[0][r] + sm.dlw_part[1][r]) + (sm.dlw_part[2][r] + sm.dlw_part[3][r]))
+                               : 0.f;
+        ok = ok && rows_sync();  // dlw_part is reused by the next item
+      } else {
+        // dK, then dV: the rows are staged in the (idle) Pᵀ/dSᵀ buffers, 16-byte
+        // units XOR-swizzled by row % 8, and stored row-contiguously.  A key that
+        // holds landmark slots (first slot cl_first) also leaves its fp32 rows in
+        // the band scratch: lmk_fixup_kernel adds the landmark pass's parts to them
+        // and rounds once.
+        constexpr int kUnits = D * 2 / 16;
+        uint8_t* stage = sm.pt;
         const int64_t HD = (int64_t)p.H * D;
-        uint8_t* dkg = reinterpret_cast<uint8_t*>(p.dk) + ((s0 + key0) * HD + (int64_t)h * D) * 2;
-        uint8_t* dvg = reinterpret_cast<uint8_t*>(p.dv) + ((s0 + key0) * HD + (int64_t)h * D) * 2;
-        for (int un = tid; un < nkeys * kUnits; un += kRowThreads) {
-          const int rr = un / kUnits, uu = un % kUnits;
-          const uint32_t so = rr * (kUnits * 16) + ((uu ^ (rr & 7)) << 4);
-          *reinterpret_cast<uint4*>(dkg + rr * HD * 2 + uu * 16) = *reinterpret_cast<const uint4*>(stage_k + so);
-          *reinterpret_cast<uint4*>(dvg + rr * HD * 2 + uu * 16) = *reinterpret_cast<const uint4*>(stage_v + so);
+#pragma unroll 1
+        for (int m = 0; ok && m < 2; ++m) {
+          const uint32_t tacc = m == 0 ? tdK : tdV;
+          const float mul = m == 0 ? p.scale : 1.0f;
+          float* bl = cl_first >= 0 ? a.band_lmk + (m == 0 ? 0 : a.part_stride * D) + (lbase + cl_first) * D
+                                    : nullptr;
+#pragma unroll 1
+          for (int ch = 0; ch < D / 64; ++ch) {  // 16 columns at a time
+            const int col = quarter * (D / 4) + ch * 16;
+            float x[16];
+            tmem_ld16(tacc + lane_addr + col, x);
+            tmem_wait_ld();
+#pragma unroll
+            for (int e = 0; e < 16; ++e) x[e] *= mul;
+            if (bl) {
+#pragma unroll
+              for (int e = 0; e < 16; e += 4)
+                *reinterpret_cast<float4*>(bl + col + e) = make_float4(x[e], x[e + 1], x[e + 2], x[e + 3]);
+            }
+#pragma unroll
+            for (int e = 0; e < 16; e += 8) {
+              const int un = (col + e) / 8;
+              uint4 u0;
+              u0.x = pack2(x[e], x[e + 1], kBF16); u0.y = pack2(x[e + 2], x[e + 3], kBF16);
+              u0.z = pack2(x[e + 4], x[e + 5], kBF16); u0.w = pack2(x[e + 6], x[e + 7], kBF16);
+              *reinterpret_cast<uint4*>(stage + r * (kUnits * 16) + ((un ^ (r & 7)) << 4)) = u0;
+            }
+          }
+          if (m == 1) {
+            tc_fence_before();
+            mbar_arrive(bar[ACC_EMPTY]);  // both accumulators are read
+          }
+          ok = rows_sync();
+          if (!ok) break;
+          uint8_t* dst = reinterpret_cast<uint8_t*>(m == 0 ? p.dk : p.dv) + ((s0 + key0) * HD + (int64_t)h * D) * 2;
+          for (int un = tid; un < nkeys * kUnits; un += kRowThreads) {
+            const int rr = un / kUnits, uu = un % kUnits;
+            *reinterpret_cast<uint4*>(dst + rr * HD * 2 + uu * 16) =
+                *reinterpret_cast<const uint4*>(stage + rr * (kUnits * 16) + ((uu ^ (rr & 7)) << 4));
+          }
+          ok = rows_sync();  // the staging area is reused (dV, or the next item's Pᵀ / dSᵀ)
         }
       }
+      gt += n;
+      ++gi;
     }
   }
   tc_fence_before();
@@ -1110,6 +1223,21 @@ static cudaError_t side_stream(cudaStream_t* out) {
   return cudaSuccess;
 }
 
+// multiprocessor count of the current device (cached)
+static cudaError_t sm_count(int* out) {
+  static int counts[64] = {};
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+  if (counts[dev] <= 0) {
+    e = cudaDeviceGetAttribute(&counts[dev], cudaDevAttrMultiProcessorCount, dev);
+    if (e != cudaSuccess) return e;
+  }
+  *out = counts[dev];
+  return cudaSuccess;
+}
+
 template <typename T, int D>
 cudaError_t launch_dkdv(const DsaltAttnParams& p, float* lmk_scratch, cudaStream_t st) {
   BwdArgs a;
@@ -1137,8 +1265,8 @@ cudaError_t launch_dkdv(const DsaltAttnParams& p, float* lmk_scratch, cudaStream
                                (int)smem);
     if (e == cudaSuccess) {
       const int nch = (p.kp + dkv::BM - 1) / dkv::BM;
-      const unsigned items = (unsigned)(p.S * nch * DSALT_LMK_SPLIT);
-      dkv::tc_bwd_dkdv_kernel<true, T, D><<<dim3(items, (unsigned)p.H), dkv::kThreadsKV, smem, side>>>(a);
+      const unsigned items = (unsigned)(p.S * nch * DSALT_LMK_SPLIT * p.H);  // one item per CTA
+      dkv::tc_bwd_dkdv_kernel<true, T, D><<<items, dkv::kThreadsKV, smem, side>>>(a);
       e = cudaGetLastError();
     }
     if (e == cudaSuccess) e = cudaEventRecord(join, side);
@@ -1150,8 +1278,15 @@ cudaError_t launch_dkdv(const DsaltAttnParams& p, float* lmk_scratch, cudaStream
   }
   e = cudaFuncSetAttribute(dkv::tc_bwd_dkdv_kernel<false, T, D>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e == cudaSuccess) {
-    dkv::tc_bwd_dkdv_kernel<false, T, D><<<dim3((unsigned)p.max_blocks, (unsigned)p.H), dkv::kThreadsKV, smem, st>>>(a);
-    e = cudaGetLastError();
+    // persistent: one CTA per SM walks the band items (block, head) round-robin
+    int sms = 0;
+    e = sm_count(&sms);
+    if (e == cudaSuccess) {
+      const long long items = (long long)p.max_blocks * p.H;
+      const unsigned grid = (unsigned)std::min<long long>(items, sms);
+      dkv::tc_bwd_dkdv_kernel<false, T, D><<<grid, dkv::kThreadsKV, smem, st>>>(a);
+      e = cudaGetLastError();
+    }
   }
   if (lmk) {
     // join before anything can fail past this point, so the caller's stream never runs ahead of the side work

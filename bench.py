@@ -50,9 +50,9 @@ KERNELS_PER_CALL = {"dsalt_build_schedule": 2, "dsalt_gather_landmarks": 1, "dsa
                     "dsalt_attn_bwd_preprocess": 1, "dsalt_attn_bwd_dkdv": 3, "dsalt_attn_bwd_dq": 2}
 # DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) per call of each entry point,
 # summed over its kernels, from one ncu capture of a config-2 step; the capture and the
-# command are in profiles/traffic_step_config2.txt
-NCU_TRAFFIC_BYTES = {"config2": {"dsalt_attn_fwd": 361505280, "dsalt_attn_bwd_preprocess": 240444928,
-                                 "dsalt_attn_bwd_dkdv": 555088128, "dsalt_attn_bwd_dq": 338497024}}
+# command are in profiles/launches_traffic_step_config2.txt
+NCU_TRAFFIC_BYTES = {"config2": {"dsalt_attn_fwd": 361824768, "dsalt_attn_bwd_preprocess": 240091136,
+                                 "dsalt_attn_bwd_dkdv": 560660096, "dsalt_attn_bwd_dq": 339012864}}
 CLOCK_REASONS = {0x1: "gpu_idle", 0x2: "applications_clocks_setting", 0x4: "sw_power_cap",
                  0x8: "hw_slowdown", 0x10: "sync_boost", 0x20: "sw_thermal_slowdown",
                  0x40: "hw_thermal_slowdown", 0x80: "hw_power_brake_slowdown", 0x100: "display_clock_setting"}
@@ -280,10 +280,22 @@ def main():
         rec, _ext.RECORD = _ext.RECORD, None
         barrier()
     ms = e0.elapsed_time(e1)
-    per_kernel = {}
-    for name, a, b in rec:
-        per_kernel.setdefault(name, []).append(a.elapsed_time(b))
     launches = sum(KERNELS_PER_CALL.get(n, 1) for n, _, _ in rec)
+    # per-kernel durations for the roofline: the same steps with dK/dV and dQ on one
+    # stream, so that each entry point's events bracket its own kernels only
+    from dsalt.kernels import dsalt_cuda
+    dsalt_cuda.CONCURRENT_BACKWARD = False
+    step()
+    torch.cuda.synchronize()
+    _ext.RECORD = []
+    for _ in range(max(3, min(args.steps, 10))):
+        step()
+    torch.cuda.synchronize()
+    rec2, _ext.RECORD = _ext.RECORD, None
+    dsalt_cuda.CONCURRENT_BACKWARD = True
+    per_kernel = {}
+    for name, a, b in rec2:
+        per_kernel.setdefault(name, []).append(a.elapsed_time(b))
 
     t = torch.tensor([ms, 14.0 * d["D"] * pairs], dtype=torch.float64, device=dev)
     if world > 1:
@@ -357,6 +369,7 @@ def main():
                            "l2": "inputs larger than L2 (q,k,v bf16 + dO fp32 = 320 MiB per step), no flush"},
                 "roofline": roof,
                 "kernels_ms": {n: round(v[0], 4) for n, v in kern.items()},
+                "kernels_ms_note": "entry points timed alone (dK/dV and dQ serialised); the timed steps run them on two streams",
                 "attended_pairs_per_gpu": pairs,
                 "gpu_launches": launches,
                 "clocks": clk.summary()}

@@ -189,6 +189,10 @@ def backward(grad_out, q_c, k_c, v_c, o, lse, prep: Prepared, tau_win: float, wi
     # dK/dV and dQ are independent once Δ and the records exist: dQ runs on a side
     # stream so that each kernel's tail waves (and the under-filled landmark pass)
     # overlap the other's work
+    if not CONCURRENT_BACKWARD:
+        _ext.call("dsalt_attn_bwd_dkdv", p)
+        _ext.call("dsalt_attn_bwd_dq", p)
+        return dq, dk, dv, d_lw, dw
     main = torch.cuda.current_stream(dev)
     side = _side_stream(dev)
     side.wait_stream(main)
@@ -197,6 +201,11 @@ def backward(grad_out, q_c, k_c, v_c, o, lse, prep: Prepared, tau_win: float, wi
     _ext.call("dsalt_attn_bwd_dkdv", p)
     main.wait_stream(side)
     return dq, dk, dv, d_lw, dw
+
+
+# dK/dV and dQ on two streams (True); False runs them one after the other on the
+# caller's stream, e.g. to time each kernel alone
+CONCURRENT_BACKWARD = True
 
 
 _SIDE_STREAMS: dict = {}

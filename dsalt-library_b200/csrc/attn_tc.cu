@@ -347,8 +347,11 @@ __global__ void __launch_bounds__(kThreads, 1) tc_fwd_kernel(const __grid_consta
       float mt = -INFINITY;
       if (!all_out) {
         if (!all_in) {
+          const uint32_t m_lo = range_mask32(vlo, vhi), m_hi = range_mask32(vlo - 32, vhi - 32);
 #pragma unroll
-          for (int c = 0; c < HALF; ++c) x[c] = (c >= vlo && c <= vhi) ? x[c] : -INFINITY;
+          for (int c = 0; c < 32; ++c) x[c] = (m_lo >> c) & 1u ? x[c] : -INFINITY;
+#pragma unroll
+          for (int c = 0; c < 32; ++c) x[32 + c] = (m_hi >> c) & 1u ? x[32 + c] : -INFINITY;
         }
         float mx[8];
 #pragma unroll

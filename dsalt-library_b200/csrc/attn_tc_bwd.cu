@@ -351,6 +351,7 @@ __global__ void __launch_bounds__(kThreadsDQ, 1) tc_bwd_dq_kernel(const __grid_c
         tc_fence_before();
         mbar_arrive(bar[SD_EMPTY + st]);
         const float* lw2 = sm.lmk_lw2 + BN * t + c0;
+        const uint32_t vmask = all_in ? 0xffffffffu : range_mask32(vlo, vhi);
 #pragma unroll
         for (int c = 0; c < kQuarter; c += 2) {
           float d2[2];
@@ -359,7 +360,7 @@ __global__ void __launch_bounds__(kThreadsDQ, 1) tc_bwd_dq_kernel(const __grid_c
             const float bias = lmk ? lw2[c + e] + nlse2 : nlse2;
             const float pr = fast_exp2(fmaf(sv[c + e], sl2, bias));
             const float dsv = pr * (dpv[c + e] - delta);
-            d2[e] = (all_in || (c + e >= vlo && c + e <= vhi)) ? dsv : 0.f;
+            d2[e] = (vmask >> (c + e)) & 1u ? dsv : 0.f;
           }
           pk[c / 2] = pack2(d2[0], d2[1], kBF16);
         }

@@ -185,4 +185,14 @@ __device__ __forceinline__ void write_qrec(const DsaltAttnParams& p, int64_t t, 
   for (int k = 0; k < DSALT_QREC_FLOATS / 4; ++k) dst[k] = src[k];
 }
 
+// Bit c (0 ≤ c < 32) set iff lo ≤ c ≤ hi: a per-thread column mask, so that an
+// unrolled loop tests one bit per element instead of two compares.
+__device__ __forceinline__ uint32_t range_mask32(int lo, int hi) {
+  lo = max(lo, 0);
+  hi = min(hi, 31);
+  if (lo > hi) return 0u;
+  const uint32_t up = hi >= 31 ? 0xffffffffu : ((1u << (hi + 1)) - 1u);
+  return up & ~((1u << lo) - 1u);
+}
+
 }  // namespace dsalt

@@ -66,7 +66,7 @@ struct alignas(1024) FwdSmem {
   uint64_t bars[NUM_BARS];
   uint32_t tmem_base;
   int abort_flag;
-  int band_lo, band_hi, cnt_max, n_valid, slow_edge;
+  int band_lo, band_hi, n_valid, slow_edge;
   float m_half[2][BM];          // epilogue: per-half running max (log2) and sum
   float l_half[2][BM];
   int lmk_pos[kMaxLmk];
@@ -123,7 +123,6 @@ __global__ void __launch_bounds__(kThreads, 1) tc_fwd_kernel(const __grid_consta
     sm.abort_flag = 0;
     sm.band_lo = INT_MAX;
     sm.band_hi = -1;
-    sm.cnt_max = 0;
     sm.n_valid = 0;
     sm.slow_edge = 0;
   }
@@ -149,12 +148,27 @@ __global__ void __launch_bounds__(kThreads, 1) tc_fwd_kernel(const __grid_consta
     if (ps >= 0) atomicAdd(&sm.n_valid, 1);
   }
   __syncthreads();
-  if (warp == kProducerWarp && lane == 0) {
-    // Q depends only on the block: load it while the windows are being resolved
-    mbar_expect_tx(bar[Q_FULL], BM * D * 2);
+  // The landmark tiles (every valid slot of the sequence, sorted) come first; they
+  // and Q depend only on the block, so their loads start while the windows are
+  // being resolved.
+  const int n_valid = sm.n_valid;
+  const int n_lt = (n_valid + BN - 1) / BN;
+  if (warp == kProducerWarp && lane < 2) {
+    if (lane == 0) {
+      mbar_expect_tx(bar[Q_FULL], BM * D * 2);
 #pragma unroll
-    for (int c = 0; c < D / 64; ++c)
-      tma_load_3d(smem_u32(sm.q + c * (BM * 128)), &a.tm_q, bar[Q_FULL], c * 64, h, (int)(s0 + m0));
+      for (int c = 0; c < D / 64; ++c)
+        tma_load_3d(smem_u32(sm.q + c * (BM * 128)), &a.tm_q, bar[Q_FULL], c * 64, h, (int)(s0 + m0));
+    }
+    if (n_lt > 0) {
+      const int FULL = lane == 0 ? K_FULL : V_FULL;
+      mbar_expect_tx(bar[FULL], a.lmk_box * D * 2);
+      uint8_t* dst = lane == 0 ? sm.k[0] : sm.v[0];
+      const CUtensorMap* map = lane == 0 ? &a.tm_lk : &a.tm_lv;
+#pragma unroll
+      for (int c = 0; c < D / 64; ++c)
+        tma_load_3d(smem_u32(dst + c * (BN * 128)), map, bar[FULL], c * 64, 0, h * p.S + s);
+    }
   }
 
   // ---- per-row window
@@ -185,7 +199,6 @@ __global__ void __launch_bounds__(kThreads, 1) tc_fwd_kernel(const __grid_consta
         atomicMin(&sm.band_lo, lo);
         atomicMax(&sm.band_hi, hi);
       }
-      if (cnt > 0) atomicMax(&sm.cnt_max, cnt);
       if (ne > kMaxEdge) atomicOr(&sm.slow_edge, 1);
     }
   }
@@ -193,15 +206,13 @@ __global__ void __launch_bounds__(kThreads, 1) tc_fwd_kernel(const __grid_consta
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = sm.tmem_base;
-  const int cnt_max = sm.cnt_max;
   const int band_lo = sm.band_lo, band_hi = sm.band_hi;
-  const int n_lt = (cnt_max + BN - 1) / BN;
   const int n_bt = band_hi >= band_lo ? (band_hi - band_lo + BN) / BN : 0;
   const int n_tiles = n_lt + n_bt;
   volatile int* abort_flag = &sm.abort_flag;
   // tile t: landmark tile (t < n_lt) or band tile starting at key band_lo + BN*(t - n_lt)
   auto tile_n = [&](int t) -> int {
-    if (t < n_lt) return round16(min(BN, cnt_max - BN * t));
+    if (t < n_lt) return round16(min(BN, n_valid - BN * t));
     return round16(min(BN, band_hi - (band_lo + BN * (t - n_lt)) + 1));
   };
   const uint32_t tS = tmem;            // S buffers: columns [0,128) and [128,256)
@@ -212,8 +223,9 @@ __global__ void __launch_bounds__(kThreads, 1) tc_fwd_kernel(const __grid_consta
     if (lane < 2 && n_tiles > 0) {
       const bool is_k = lane == 0;
       const int FULL = is_k ? K_FULL : V_FULL, EMPTY = is_k ? K_EMPTY : V_EMPTY;
-      int issued = 0;
-      for (int t = 0; t < n_tiles; ++t) {
+      // tile 0 of a sequence with landmarks was issued before the windows were resolved
+      int issued = n_lt > 0 ? 1 : 0;
+      for (int t = issued; t < n_tiles; ++t) {
         const int st = t & 1;
         if (t >= 2 && !mbar_wait(bar[EMPTY + st], ((t >> 1) - 1) & 1, abort_flag, p.status)) break;
         const bool lmk = t < n_lt;

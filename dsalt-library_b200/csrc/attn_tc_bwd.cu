@@ -104,7 +104,7 @@ struct alignas(1024) Smem {
   uint8_t ds[2][BM * BN * 2];
   uint64_t bars[NB];
   uint32_t tmem_base;
-  int abort_flag, band_lo, band_hi, cnt_max, n_valid, slow_edge;
+  int abort_flag, band_lo, band_hi, n_valid, slow_edge;
   float dw_part[4][BM];  // ∂loss/∂w̃ partial sums of the four column quarters
   int lmk_pos[kMaxLmk];
   float lmk_lw2[kMaxLmk];
@@ -148,7 +148,6 @@ __global__ void __launch_bounds__(kThreadsDQ, 1) tc_bwd_dq_kernel(const __grid_c
     sm.abort_flag = 0;
     sm.band_lo = INT_MAX;
     sm.band_hi = -1;
-    sm.cnt_max = 0;
     sm.n_valid = 0;
     sm.slow_edge = 0;
   }
@@ -180,13 +179,28 @@ __global__ void __launch_bounds__(kThreadsDQ, 1) tc_bwd_dq_kernel(const __grid_c
     if (ps >= 0) atomicAdd(&sm.n_valid, 1);
   }
   __syncthreads();
-  if (warp == kProducerWarp && lane == 0) {
-    // Q and dO depend only on the block
-    mbar_expect_tx(bar[QD_FULL], 2 * BM * D * 2);
+  // Q, dO and the first landmark tile (the landmark tiles cover every valid slot
+  // of the sequence, sorted) depend only on the block: their loads start while
+  // the windows are being resolved
+  const int n_valid = sm.n_valid;
+  const int n_lt = (n_valid + BN - 1) / BN;
+  if (warp == kProducerWarp && lane < 2) {
+    if (lane == 0) {
+      mbar_expect_tx(bar[QD_FULL], 2 * BM * D * 2);
 #pragma unroll
-    for (int c = 0; c < D / 64; ++c) {
-      tma_load_3d(smem_u32(sm.q + c * (BM * 128)), &a.tm_q, bar[QD_FULL], c * 64, h, (int)(s0 + m0));
-      tma_load_3d(smem_u32(sm.dO + c * (BM * 128)), &a.tm_do, bar[QD_FULL], c * 64, h, (int)(s0 + m0));
+      for (int c = 0; c < D / 64; ++c) {
+        tma_load_3d(smem_u32(sm.q + c * (BM * 128)), &a.tm_q, bar[QD_FULL], c * 64, h, (int)(s0 + m0));
+        tma_load_3d(smem_u32(sm.dO + c * (BM * 128)), &a.tm_do, bar[QD_FULL], c * 64, h, (int)(s0 + m0));
+      }
+    }
+    if (n_lt > 0) {
+      const int FULL = lane == 0 ? K_FULL : V_FULL;
+      mbar_expect_tx(bar[FULL], a.lmk_box * D * 2);
+      uint8_t* dst = lane == 0 ? sm.k[0] : sm.v[0];
+      const CUtensorMap* map = lane == 0 ? &a.tm_lk : &a.tm_lv;
+#pragma unroll
+      for (int c = 0; c < D / 64; ++c)
+        tma_load_3d(smem_u32(dst + c * (BN * 128)), map, bar[FULL], c * 64, 0, h * p.S + s);
     }
   }
   const bool row_live = row_ok && rec_qi != INT_MIN;  // a row without keys has no gradient
@@ -202,7 +216,6 @@ __global__ void __launch_bounds__(kThreadsDQ, 1) tc_bwd_dq_kernel(const __grid_c
     cnt = a0;
     if (quarter == 0) {
       if (lo <= hi) { atomicMin(&sm.band_lo, lo); atomicMax(&sm.band_hi, hi); }
-      if (cnt > 0) atomicMax(&sm.cnt_max, cnt);
       if (rec_ne > kMaxEdge) atomicOr(&sm.slow_edge, 1);
     }
   }
@@ -210,14 +223,13 @@ __global__ void __launch_bounds__(kThreadsDQ, 1) tc_bwd_dq_kernel(const __grid_c
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = sm.tmem_base;
-  const int cnt_max = sm.cnt_max, band_lo = sm.band_lo, band_hi = sm.band_hi;
-  const int n_lt = (cnt_max + BN - 1) / BN;
+  const int band_lo = sm.band_lo, band_hi = sm.band_hi;
   const int n_bt = band_hi >= band_lo ? (band_hi - band_lo + BN) / BN : 0;
   const int n_tiles = n_lt + n_bt;
   volatile int* abort_flag = &sm.abort_flag;
   // valid key rows of tile t (landmark tiles may hold fewer than BN loaded rows)
   auto tile_n = [&](int t) -> int {
-    if (t < n_lt) return round16(min(BN, cnt_max - BN * t));
+    if (t < n_lt) return round16(min(BN, n_valid - BN * t));
     return BN;
   };
   const uint32_t tS = tmem, tdP = tmem + 2 * BN, tdQ = tmem + 4 * BN;
@@ -227,8 +239,9 @@ __global__ void __launch_bounds__(kThreadsDQ, 1) tc_bwd_dq_kernel(const __grid_c
     if (lane < 2 && n_tiles > 0) {
       const bool is_k = lane == 0;
       const int FULL = is_k ? K_FULL : V_FULL, EMPTY = is_k ? K_EMPTY : V_EMPTY;
-      int issued = 0;
-      for (int t = 0; t < n_tiles; ++t) {
+      // tile 0 of a sequence with landmarks was issued before the windows were resolved
+      int issued = n_lt > 0 ? 1 : 0;
+      for (int t = issued; t < n_tiles; ++t) {
         const int st = t % kKV;
         if (t >= kKV && !mbar_wait(bar[EMPTY + st], (t / kKV - 1) & 1, abort_flag, p.status)) break;
         const bool lmk = t < n_lt;

@@ -85,17 +85,23 @@ def hybrid_scores_per_head(
     alpha:   torch.Tensor,
     n_heads: int,
     dh:      int,
+    xwv:     torch.Tensor | None = None,
 ) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
     """Per-head hybrid score and the standardised signals (reference :19-61).
 
     Returns ``(scores [T, n_heads], z_x [T], z_v [T, n_heads])`` in fp32.  Under
     GQA (``W_V`` has ``n_kv_heads·dh`` rows) the kv-head value norm is shared by
-    the query heads of its group.
+    the query heads of its group.  ``xwv`` (``[T, n_kv·dh]``) may pass the value
+    projection the caller already has: without a bias ``x·W_Vᵀ`` is exactly the
+    pre-RoPE ``v``, so the ``T·d·n_kv·dh`` GEMM is not repeated.
     """
     n_kv = W_V.shape[0] // dh
     if n_heads % n_kv != 0:
         raise ValueError(f"n_heads={n_heads} is not a multiple of n_kv={n_kv}")
-    xwv = x @ W_V.T.to(x.dtype)  # library GEMM; autocast gives the reference's bf16 product
+    if xwv is None:
+        xwv = x @ W_V.T.to(x.dtype)  # library GEMM; autocast gives the reference's bf16 product
+    elif xwv.shape != (x.shape[0], W_V.shape[0]):
+        raise ValueError(f"xwv must be [T, {W_V.shape[0]}], got {tuple(xwv.shape)}")
     return _HybridScore.apply(x, xwv, alpha, n_heads, n_kv, dh)
 
 

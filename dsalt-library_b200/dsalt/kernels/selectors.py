@@ -96,15 +96,17 @@ def _compute_landmark_indices(
     total_len:  int,
     cu_list:    list | None = None,
     head_dim:   int | None = None,
+    xwv:        torch.Tensor | None = None,
 ):
     """Hard top-k landmark indices per (head, sequence) (reference :75-134).
 
     Returns ``(idx [H, S, k_lmk] int64, z_x, z_v)``; the selection is detached.
+    ``xwv`` optionally passes ``x·W_Vᵀ`` (see ``hybrid_scores_per_head``).
     """
     n_heads = alpha.shape[0]
     dh = head_dim if head_dim is not None else W_V.shape[0] // n_heads
     with torch.no_grad():
-        scores, z_x, z_v = hybrid_scores_per_head(x, W_V, alpha, n_heads, dh)
+        scores, z_x, z_v = hybrid_scores_per_head(x, W_V, alpha, n_heads, dh, xwv=xwv)
         hc = _host_cu(cu_seqlens, cu_list)
         max_len = max((hc[b + 1] - hc[b] for b in range(len(hc) - 1)), default=0)
         idx = select_topk(scores, w_sizes, cu_seqlens, k_lmk, max_len)

@@ -164,15 +164,15 @@ class DSALTAttention(nn.Module):
         out, aux = self._packed(x.reshape(B * T, self.d_model), cu, B * T, device, None, cu_list)
         return out.view(B, T, self.d_model), aux
 
-    def _packed_train_triton(self, q, k, v, x, cu_seqlens, total_len, device, cu_list=None):
+    def _packed_train_triton(self, q, k, v, x, cu_seqlens, total_len, device, cu_list=None, xwv=None):
         """Training attention on the CUDA op, carrying the window and α gradients (reference :440-455)."""
-        w_cont, lmk_pos, lmk_logw = self._train_selectors(x, cu_seqlens, total_len, device, cu_list)
+        w_cont, lmk_pos, lmk_logw = self._train_selectors(x, cu_seqlens, total_len, device, cu_list, xwv)
         return dsalt_triton_train_attention(q, k, v, lmk_pos, lmk_logw, w_cont, cu_seqlens,
                                             tau_win=self.tau_win, win_edge=float(self.win_edge),
                                             n_max=self.n_max, cu_list=cu_list)
 
     @_dynamo_opaque
-    def _train_selectors(self, x, cu_seqlens, total_len, device, cu_list=None):
+    def _train_selectors(self, x, cu_seqlens, total_len, device, cu_list=None, xwv=None):
         """``(w_cont [T], lmk_pos [H,S,k], lmk_logw [H,S,k])`` (reference :457-487).
 
         The hybrid score is computed once: its detached value drives the hard top-k
@@ -181,7 +181,7 @@ class DSALTAttention(nn.Module):
         """
         w_cont = self._window_continuous(x)
         alpha = self._alpha()
-        scores, _, _ = hybrid_scores_per_head(x, self.v_proj.weight, alpha, self.n_heads, self.head_dim)
+        scores, _, _ = hybrid_scores_per_head(x, self.v_proj.weight, alpha, self.n_heads, self.head_dim, xwv=xwv)
         cu_h = cu_list if cu_list is not None else cu_seqlens.detach().to("cpu").tolist()
         max_len = max((cu_h[b + 1] - cu_h[b] for b in range(len(cu_h) - 1)), default=0)
         with torch.no_grad():
@@ -199,6 +199,9 @@ class DSALTAttention(nn.Module):
         q = self.q_proj(x).view(total_len, self.n_heads, self.head_dim)
         k = self.k_proj(x).view(total_len, self.n_kv_heads, self.head_dim)
         v = self.v_proj(x).view(total_len, self.n_kv_heads, self.head_dim)
+        # without a bias the value projection is x·W_Vᵀ, the landmark scorer's GEMM:
+        # hand it over instead of recomputing it (v carries no RoPE)
+        xwv = v.view(total_len, self.kv_dim) if self.v_proj.bias is None else None
         if rope_cs is None:
             num_seqs = cu_seqlens.shape[0] - 1
             cu = cu_seqlens.to(device).long()
@@ -218,14 +221,15 @@ class DSALTAttention(nn.Module):
 
         if self.training:
             self._last_P = None
-            out = self._packed_train_triton(q, k, v, x, cu_seqlens, total_len, device, cu_list)
+            out = self._packed_train_triton(q, k, v, x, cu_seqlens, total_len, device, cu_list, xwv)
             return self._apply_out_proj(out.view(total_len, self.d_model)), aux
 
         w_sizes = self._window_sizes(x, floor=True)
         alpha = self._alpha()
         lmk_indices, _, _ = _compute_landmark_indices(
             x.detach(), self.v_proj.weight.detach(), alpha.detach().float(), w_sizes, cu_seqlens,
-            self.k_lmk, self.n_min, total_len, cu_list, head_dim=self.head_dim)
+            self.k_lmk, self.n_min, total_len, cu_list, head_dim=self.head_dim,
+            xwv=None if xwv is None else xwv.detach())
         lmk_bias = torch.zeros_like(lmk_indices, dtype=torch.float32)
         out = dsalt_triton_attention(q, k, v, lmk_indices, lmk_bias, w_sizes, cu_seqlens)
         self._last_P = self._dense_first_sequence(q, k, w_sizes, lmk_indices, cu_seqlens) \

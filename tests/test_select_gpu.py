@@ -119,3 +119,25 @@ def test_topk_full_size_vs_oracle(L, k):
     idx = select_topk(scores.cuda(), w.cuda(), cu.cuda(), k, max(lens)).cpu().numpy()
     ref = O.landmark_indices(scores.numpy(), w.numpy(), cu.numpy(), k)
     assert np.array_equal(idx, ref)
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+def test_hybrid_scores_from_value_projection(dtype):
+    """Scoring from the module's value projection (no bias: v = x·W_Vᵀ) gives the
+    same scores and gradients as the scorer's own GEMM."""
+    from dsalt.kernels.landmark_tokens_ker import hybrid_scores_per_head
+    g = torch.Generator(device="cuda").manual_seed(3)
+    T, d, H, n_kv, dh = 777, 256, 8, 4, 32
+    x = torch.randn(T, d, generator=g, device="cuda").to(dtype).requires_grad_(True)
+    W = (torch.randn(n_kv * dh, d, generator=g, device="cuda") / d ** 0.5).requires_grad_(True)
+    alpha = torch.rand(H, generator=g, device="cuda").requires_grad_(True)
+    with torch.autocast("cuda", dtype=torch.bfloat16, enabled=dtype == torch.bfloat16):
+        s_ref, _, _ = hybrid_scores_per_head(x, W, alpha, H, dh)
+        v = torch.nn.functional.linear(x, W)
+        s_v, _, _ = hybrid_scores_per_head(x, W, alpha, H, dh, xwv=v)
+    assert torch.equal(s_ref, s_v)
+    go = torch.randn_like(s_ref)
+    ga = torch.autograd.grad(s_ref, (x, W, alpha), go)
+    gb = torch.autograd.grad(s_v, (x, W, alpha), go)
+    for a, b in zip(ga, gb):
+        torch.testing.assert_close(a.float(), b.float(), rtol=1e-5, atol=1e-5)

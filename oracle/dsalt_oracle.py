@@ -357,6 +357,68 @@ def _attention(q, k, v, do, lmk_pos, lmk_logw, w, cu, tau_win, win_edge, semanti
     return res
 
 
+def attention_fwd_rows(q, k, v, lmk_pos, lmk_logw, w, cu, rows, tau_win=1.0, win_edge=4.0,
+                       semantics="train", dtype=np.float64):
+    """``O`` and ``LSE`` of selected ``(token, head)`` rows only, for sequences too long
+    for the dense per-sequence matrices of ``attention_fwd``.  Same definitions as
+    ``_band_bias`` / ``_landmark_bias`` (dsalt/kernels/dsalt_triton_train.py:145-198,
+    dsalt/kernels/dsalt_triton_attn.py:102-135), one row at a time.  Returns
+    ``(o [n, D], lse [n])``.
+    """
+    cu = np.asarray(cu, dtype=np.int64)
+    lmk_pos = np.asarray(lmk_pos, dtype=np.int64)
+    lmk_logw = np.asarray(lmk_logw, dtype=np.float64)
+    w = np.asarray(w)
+    D = q.shape[2]
+    scale = 1.0 / math.sqrt(D)
+    out_o = np.zeros((len(rows), D))
+    out_lse = np.full(len(rows), -np.inf)
+    for n, (t, h) in enumerate(rows):
+        b = int(np.searchsorted(cu, t, side="right") - 1)
+        s0, L = int(cu[b]), int(cu[b + 1] - cu[b])
+        i = t - s0
+        j = np.arange(i + 1)
+        d = (i - j).astype(np.float32)
+        if semantics == "train":
+            w32 = np.float32(w[t])
+            band = (d >= 0) & (d <= w32)
+            core = d <= (w32 - np.float32(win_edge))
+            z = (np.float64(w32) - d.astype(np.float64)) / tau_win
+            with np.errstate(over="ignore"):
+                logedge = -np.log1p(np.exp(-z))
+            bb = np.where(band, np.where(core, 0.0, logedge), -np.inf)
+            win_lo = np.float32(i) - w32
+        else:
+            w_int = max(int(np.int64(w[t])), 1)
+            bb = np.where(j >= i - w_int + 1, 0.0, -np.inf)
+            win_lo = i - w_int + 1
+        qi = np.asarray(q[t, h], dtype=dtype)
+        ks = np.asarray(k[s0:s0 + i + 1, h], dtype=dtype)
+        vs = np.asarray(v[s0:s0 + i + 1, h], dtype=dtype)
+        logits = [(ks @ qi) * scale + bb]
+        vals = [vs]
+        pos = lmk_pos[h, b]
+        lb = np.full(len(pos), -np.inf)
+        for c, p in enumerate(pos):
+            p = int(p)
+            if p < 0 or p >= L:
+                continue
+            ok = p <= i and ((np.float32(p) < win_lo) if semantics == "train" else (p < win_lo))
+            if ok:
+                lb[c] = lmk_logw[h, b, c]
+        pc = np.clip(pos, 0, L - 1) + s0
+        logits.append((np.asarray(k[pc, h], dtype=dtype) @ qi) * scale + lb)
+        vals.append(np.asarray(v[pc, h], dtype=dtype))
+        lg = np.concatenate(logits)
+        m = lg.max()
+        if not np.isfinite(m):
+            continue
+        e = np.exp(lg - m)
+        out_o[n] = (e[:, None] * np.concatenate(vals)).sum(axis=0) / e.sum()
+        out_lse[n] = m + np.log(e.sum())
+    return out_o, out_lse
+
+
 # --------------------------------------------------------------------------- #
 #  work accounting (roofline denominator)
 # --------------------------------------------------------------------------- #

@@ -188,3 +188,39 @@ def test_bad_cu_seqlens_rejected_before_launch():
         dsalt_triton_train_attention(q, q, q, pos, torch.zeros(1, 2, 1, device="cuda"),
                                      torch.ones(16, device="cuda"),
                                      torch.tensor([0, 4, 12], dtype=torch.int32, device="cuda"))
+
+
+@pytest.mark.parametrize("semantics", ["infer", "train"])
+def test_config5_long_context_rows_vs_oracle(semantics):
+    """Config-5 shapes (one sequence of 32,768, D=128, k=256, windows 128…2048; 4 of
+    the 32 heads, which are independent): sampled rows against the row-wise oracle."""
+    from dsalt.kernels.dsalt_triton_attn import dsalt_triton_attention
+    from dsalt.kernels.dsalt_triton_train import dsalt_triton_train_attention
+    from dsalt.kernels.selectors import select_topk
+    dev = torch.device("cuda")
+    g = torch.Generator(device=dev).manual_seed(21)
+    N, H, D, k = 32768, 4, 128, 256
+    q, kk, v = (torch.randn(N, H, D, generator=g, device=dev).to(torch.bfloat16) for _ in range(3))
+    w = 128.0 + torch.sigmoid(torch.randn(N, generator=g, device=dev)) * (2048.0 - 128.0)
+    cu = torch.tensor([0, N], dtype=torch.int32, device=dev)
+    scores = torch.randn(N, H, generator=g, device=dev)
+    pos = select_topk(scores, w.floor().clamp(min=1), cu, k, N)
+    if semantics == "infer":
+        w_in = w.floor()
+        bias = torch.zeros(H, 1, k, device=dev)
+        o = dsalt_triton_attention(q, kk, v, pos, bias, w_in, cu)
+        lw = bias
+    else:
+        w_in = w
+        lw = torch.log(torch.sigmoid(torch.randn(H, 1, k, generator=g, device=dev) / 2))
+        lw = torch.where(pos >= 0, lw, torch.full_like(lw, float("-inf")))
+        o = dsalt_triton_train_attention(q, kk, v, pos, lw, w_in, cu, 1.0, 4.0, 2048)
+    torch.cuda.synchronize()
+    rng = np.random.default_rng(0)
+    rows = [(int(t), int(h)) for t, h in zip(rng.integers(0, N, 48), rng.integers(0, H, 48))]
+    rows += [(0, 0), (1, 1), (N - 1, 3), (2047, 2), (2048, 0)]
+    qf, kf, vf = (x.float().cpu().numpy() for x in (q, kk, v))
+    ref, _ = O.attention_fwd_rows(qf, kf, vf, pos.cpu().numpy(), lw.float().cpu().numpy(),
+                                  w_in.float().cpu().numpy(), cu.cpu().numpy(), rows, semantics=semantics)
+    got = np.stack([o[t, h].float().cpu().numpy() for t, h in rows])
+    _close(got, ref, torch.bfloat16, f"o ({semantics})")

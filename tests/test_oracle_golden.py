@@ -102,3 +102,24 @@ def test_attended_pairs_small():
     pos = np.array([[[0]]])
     # band sizes min(floor(1.5), i)+1 = 1,2,2,2,2 ; landmark 0 valid for i with 0 < i-1.5 → i ≥ 2
     assert O.attended_pairs(w, pos, [0, 5]) == 9 + 3
+
+
+@pytest.mark.parametrize("semantics", ["train", "infer"])
+def test_rowwise_oracle_matches_dense(semantics):
+    """The row-at-a-time restatement used for long sequences equals the dense one."""
+    rng = np.random.default_rng(5)
+    lens = [70, 33]
+    T, H, D, k = sum(lens), 2, 16, 6
+    q, kk, v = (rng.standard_normal((T, H, D)) for _ in range(3))
+    w = rng.uniform(1.0, 40.0, T)
+    cu = np.array([0, 70, 103])
+    pos = np.full((H, 2, k), -1)
+    for h in range(H):
+        for b, L in enumerate(lens):
+            pos[h, b, :4] = rng.choice(L, 4, replace=False)
+    lw = np.where(pos >= 0, np.log(1 / (1 + np.exp(-rng.standard_normal((H, 2, k))))), -np.inf)
+    o, lse = O.attention_fwd(q, kk, v, pos, lw, w, cu, semantics=semantics)
+    rows = [(t, h) for t in range(T) for h in range(H)]
+    o_r, lse_r = O.attention_fwd_rows(q, kk, v, pos, lw, w, cu, rows, semantics=semantics)
+    np.testing.assert_allclose(o_r, np.array([o[t, h] for t, h in rows]), rtol=1e-12, atol=1e-12)
+    np.testing.assert_allclose(lse_r, np.array([lse[t, h] for t, h in rows]), rtol=1e-12, atol=1e-12)

@@ -35,9 +35,6 @@ cudaError_t simt_attention_stage(int stage, const DsaltAttnParams& p, cudaStream
 
 namespace bwd {
 
-constexpr int kRowThreads = 256;
-constexpr int kProducerWarp = 8;
-constexpr int kMmaWarp = 9;
 constexpr int kMaxLmk = 512;
 constexpr int kMaxEdge = kQRecEdge;  // soft-edge keys per query handled with precomputed factors
 constexpr float kLog2e = 1.4426950408889634f;
@@ -81,16 +78,17 @@ __device__ __forceinline__ void store_row32_packed(uint8_t* base, int row, int c
 namespace dq {
 constexpr int BM = 128, BN = 64;
 constexpr int kKV = 3;           // K / V tile ring
-// 16 row warps: warp w reads TMEM lanes 32·(w % 4)… and owns the 16-column
-// quarter w / 4 of every 64-key tile; then the TMA warp, MMA warp A (TMEM
-// owner: S, dQ) and MMA warp B (dP)
+// 16 row warps in two groups of eight that take alternate 64-key tiles: warp w
+// reads TMEM lanes 32·(w % 4)… and owns the 32-column half (w / 4) % 2 of its
+// group's tiles; then the TMA warp, MMA warp A (TMEM owner: S) and MMA warp B
+// (dP, dQ)
 constexpr int kRowWarps = 16;
 constexpr int kRowThreads = 32 * kRowWarps;
 constexpr int kProducerWarp = 16;
 constexpr int kMmaWarp = 17;
 constexpr int kMmaWarpB = 18;
 constexpr int kThreadsDQ = 608;
-constexpr int kQuarter = BN / 4;  // tile columns per row thread
+constexpr int kHalfCols = BN / 2;  // tile columns per row thread
 enum { QD_FULL = 0, K_FULL = 1, V_FULL = K_FULL + kKV, K_EMPTY = V_FULL + kKV, V_EMPTY = K_EMPTY + kKV,
        SD_FULL = V_EMPTY + kKV, SD_EMPTY = SD_FULL + 2, DS_FULL = SD_EMPTY + 2, DS_EMPTY = DS_FULL + 2,
        DQ_DONE = DS_EMPTY + 2, FINAL = DQ_DONE + 1, EPI = FINAL + 2, EPI2 = EPI + 1, NB = EPI2 + 1 };
@@ -106,9 +104,11 @@ struct alignas(1024) Smem {
   uint32_t tmem_base;
   int abort_flag, band_lo, band_hi, n_valid, slow_edge;
   float dw_part[4][BM];  // ∂loss/∂w̃ partial sums of the four column quarters
+  alignas(16) float eg[BM][kMaxEdge];  // each row's soft-edge factors (its record's eg), float4 stores
   int lmk_pos[kMaxLmk];
   float lmk_lw2[kMaxLmk];
 };
+static_assert(offsetof(Smem<128>, eg) % 16 == 0 && offsetof(Smem<64>, eg) % 16 == 0, "eg rows take float4 stores");
 
 template <typename T, int D>
 __global__ void __launch_bounds__(kThreadsDQ, 1) tc_bwd_dq_kernel(const __grid_constant__ BwdArgs a) {
@@ -130,13 +130,13 @@ __global__ void __launch_bounds__(kThreadsDQ, 1) tc_bwd_dq_kernel(const __grid_c
     for (int st = 0; st < kKV; ++st) {
       mbar_init(bar[K_FULL + st], 1);
       mbar_init(bar[V_FULL + st], 1);
-      mbar_init(bar[K_EMPTY + st], 1);
+      mbar_init(bar[K_EMPTY + st], 2);  // read by S (MMA warp A) and dQ (MMA warp B)
       mbar_init(bar[V_EMPTY + st], 1);
     }
-    for (int st = 0; st < 2; ++st) {
-      mbar_init(bar[SD_FULL + st], 2);  // S (warp 9) and dP (warp 10)
-      mbar_init(bar[SD_EMPTY + st], kRowThreads);
-      mbar_init(bar[DS_FULL + st], kRowThreads);
+    for (int st = 0; st < 2; ++st) {  // st = tile % 2 = row group
+      mbar_init(bar[SD_FULL + st], 2);  // S (MMA warp A) and dP (MMA warp B)
+      mbar_init(bar[SD_EMPTY + st], kRowThreads / 2);
+      mbar_init(bar[DS_FULL + st], kRowThreads / 2);
       mbar_init(bar[DS_EMPTY + st], 1);
     }
     mbar_init(bar[DQ_DONE], 1);
@@ -166,6 +166,10 @@ __global__ void __launch_bounds__(kThreadsDQ, 1) tc_bwd_dq_kernel(const __grid_c
   if (row_ok) {
     rh0 = __ldg(reinterpret_cast<const float4*>(recg));      // nlse2, delta, lo, qi
     rh1 = __ldg(reinterpret_cast<const float4*>(recg) + 1);  // ehi, elo, wlo, wt
+  }
+  if (warp < kRowWarps && quarter < 2) {  // the row's soft-edge factors, for the fix-up of its dS
+    const float4 e4 = row_ok ? __ldg(reinterpret_cast<const float4*>(recg) + 2 + quarter) : make_float4(1.f, 1.f, 1.f, 1.f);
+    *reinterpret_cast<float4*>(&sm.eg[r][4 * quarter]) = e4;
   }
   const int rec_lo = __float_as_int(rh0.z), rec_qi = __float_as_int(rh0.w);
   const int rec_ehi = __float_as_int(rh1.x), rec_elo = __float_as_int(rh1.y);
@@ -260,16 +264,16 @@ __global__ void __launch_bounds__(kThreadsDQ, 1) tc_bwd_dq_kernel(const __grid_c
     }
     if (lane == 0) mbar_drain(bar[QD_FULL], 0);
   } else if (warp == kMmaWarp) {
-    // S = Q·Kᵀ two tiles ahead and dQ += dS·K (warp 10 issues dP = dO·Vᵀ alongside)
+    // S = Q·Kᵀ up to two tiles ahead (a TMEM buffer is free once its row group has read it)
     if (lane == 0 && n_tiles > 0) {
       const uint32_t id_s = idesc_f16(kBF16, BM, BN, false, false);
-      const uint32_t id_dq = idesc_f16(kBF16, BM, D, false, true);
       const uint32_t q_addr = smem_u32(sm.q);
       bool ok = mbar_wait(bar[QD_FULL], 0, abort_flag, p.status);
-      auto issue_s = [&](int t) -> bool {
+      for (int t = 0; ok && t < n_tiles; ++t) {
         const int st = t & 1, ks = t % kKV;
-        if (!mbar_wait(bar[K_FULL + ks], (t / kKV) & 1, abort_flag, p.status)) return false;
-        if (t >= 2 && !mbar_wait(bar[SD_EMPTY + st], ((t >> 1) - 1) & 1, abort_flag, p.status)) return false;
+        ok = mbar_wait(bar[K_FULL + ks], (t / kKV) & 1, abort_flag, p.status) &&
+             (t < 2 || mbar_wait(bar[SD_EMPTY + st], ((t >> 1) - 1) & 1, abort_flag, p.status));
+        if (!ok) break;
         tc_fence_after();
         const uint32_t k_addr = smem_u32(sm.k[ks]);
 #pragma unroll
@@ -280,37 +284,23 @@ __global__ void __launch_bounds__(kThreadsDQ, 1) tc_bwd_dq_kernel(const __grid_c
                   kk > 0 ? 1u : 0u);
         }
         mma_commit(bar[SD_FULL + st]);
-        return true;
-      };
-      if (ok) ok = issue_s(0);
-      if (ok && n_tiles > 1) ok = issue_s(1);
-      for (int t = 0; ok && t < n_tiles; ++t) {
-        const int st = t & 1, ks = t % kKV;
-        if (!mbar_wait(bar[DS_FULL + st], (t >> 1) & 1, abort_flag, p.status)) { ok = false; break; }
-        tc_fence_after();
-        const uint32_t ds_addr = smem_u32(sm.ds[st]), k_addr = smem_u32(sm.k[ks]);
-        const int nk = tile_n(t) / 16;
-        for (int kk = 0; kk < nk; ++kk)
-          mma_f16(tdQ, sdesc_sw128(ds_addr + kk * 32, 16, 1024), sdesc_sw128(k_addr + kk * 2048, BN * 128, 1024),
-                  id_dq, (t > 0 || kk > 0) ? 1u : 0u);
-        mma_commit(bar[DS_EMPTY + st]);
         mma_commit(bar[K_EMPTY + ks]);
-        if (t + 2 < n_tiles && !issue_s(t + 2)) { ok = false; break; }
       }
-      mma_commit(bar[DQ_DONE]);
       mma_commit(bar[FINAL]);
       mbar_drain(bar[FINAL], 0);
     }
   } else if (warp == kMmaWarpB) {
-    // dP = dO·Vᵀ, as soon as the V tile is in and the rows have read the previous dP of the stage
+    // dP = dO·Vᵀ up to two tiles ahead, and dQ += dS·K once a row group has stored
+    // its tile's dS (tiles in order: the accumulation order is fixed)
     if (lane == 0 && n_tiles > 0) {
       const uint32_t id_s = idesc_f16(kBF16, BM, BN, false, false);
+      const uint32_t id_dq = idesc_f16(kBF16, BM, D, false, true);
       const uint32_t do_addr = smem_u32(sm.dO);
       bool ok = mbar_wait(bar[QD_FULL], 0, abort_flag, p.status);
-      for (int t = 0; ok && t < n_tiles; ++t) {
+      auto issue_dp = [&](int t) -> bool {
         const int st = t & 1, ks = t % kKV;
-        if (!mbar_wait(bar[V_FULL + ks], (t / kKV) & 1, abort_flag, p.status)) break;
-        if (t >= 2 && !mbar_wait(bar[SD_EMPTY + st], ((t >> 1) - 1) & 1, abort_flag, p.status)) break;
+        if (!mbar_wait(bar[V_FULL + ks], (t / kKV) & 1, abort_flag, p.status)) return false;
+        if (t >= 2 && !mbar_wait(bar[SD_EMPTY + st], ((t >> 1) - 1) & 1, abort_flag, p.status)) return false;
         tc_fence_after();
         const uint32_t v_addr = smem_u32(sm.v[ks]);
 #pragma unroll
@@ -322,14 +312,36 @@ __global__ void __launch_bounds__(kThreadsDQ, 1) tc_bwd_dq_kernel(const __grid_c
         }
         mma_commit(bar[SD_FULL + st]);
         mma_commit(bar[V_EMPTY + ks]);
+        return true;
+      };
+      if (ok) ok = issue_dp(0);
+      if (ok && n_tiles > 1) ok = issue_dp(1);
+      for (int t = 0; ok && t < n_tiles; ++t) {
+        const int st = t & 1, ks = t % kKV;
+        if (t + 2 < n_tiles && !(ok = issue_dp(t + 2))) break;
+        if (!(ok = mbar_wait(bar[DS_FULL + st], (t >> 1) & 1, abort_flag, p.status))) break;
+        tc_fence_after();
+        const uint32_t ds_addr = smem_u32(sm.ds[st]), k_addr = smem_u32(sm.k[ks]);
+        const int nk = tile_n(t) / 16;
+        for (int kk = 0; kk < nk; ++kk)
+          mma_f16(tdQ, sdesc_sw128(ds_addr + kk * 32, 16, 1024), sdesc_sw128(k_addr + kk * 2048, BN * 128, 1024),
+                  id_dq, (t > 0 || kk > 0) ? 1u : 0u);
+        mma_commit(bar[DS_EMPTY + st]);
+        mma_commit(bar[K_EMPTY + ks]);
       }
+      mma_commit(bar[DQ_DONE]);
       mma_commit(bar[FINAL + 1]);
       mbar_drain(bar[FINAL + 1], 0);
     }
   } else {
     // --------------------------------------------------------- row warps
+    // Two groups of eight warps take alternate key tiles (group = t % 2, which is
+    // also the tile's S/dP TMEM buffer and dS smem buffer), so that one group's
+    // element-wise work overlaps the other's waits; within a group, warp w reads
+    // TMEM lanes 32·(w % 4)… and owns the 32-column half (w / 4) % 2 of its tiles.
     const uint32_t lane_addr = ((uint32_t)(32 * (warp & 3)) << 16);
-    const int c0 = kQuarter * quarter;  // first tile column of this thread
+    const int grp = quarter >> 1;
+    const int ch0 = kHalfCols * (quarter & 1);  // first tile column of this thread
     const float sl2 = p.scale * kLog2e;
     const float inv_tau = 1.0f / p.tau_win;
     const bool slow_edge = sm.slow_edge != 0;
@@ -338,86 +350,89 @@ __global__ void __launch_bounds__(kThreadsDQ, 1) tc_bwd_dq_kernel(const __grid_c
     const int ne = row_live ? rec_ne : 0, ehi = rec_ehi;
     float dw = 0.f;
     bool ok = true;
-    for (int t = 0; t < n_tiles; ++t) {
+    for (int t = grp; t < n_tiles; t += 2) {
       const int st = t & 1;
-      ok = mbar_wait(bar[SD_FULL + st], (t >> 1) & 1, abort_flag, p.status);
+      // the tile's S/dP, and its dS buffer (free once the dQ MMAs of tile t − 2 completed)
+      ok = mbar_wait(bar[SD_FULL + st], (t >> 1) & 1, abort_flag, p.status) &&
+           (t < 2 || mbar_wait(bar[DS_EMPTY + st], ((t >> 1) - 1) & 1, abort_flag, p.status));
       if (!__all_sync(0xffffffffu, ok)) { ok = false; break; }
       tc_fence_after();
       const bool lmk = t < n_lt;
       const int n0 = lmk ? 0 : band_lo + BN * (t - n_lt);
-      // valid columns of this thread: [vlo, vhi]
-      const int vlo = lmk ? 0 : lo - n0 - c0;  // lo = INT_MAX for a row without band: stays positive
-      const int vhi = lmk ? cnt - BN * t - c0 - 1 : hi - n0 - c0;
-      const bool all_in = __all_sync(0xffffffffu, vlo <= 0 && vhi >= kQuarter - 1);
-      const bool all_out = __all_sync(0xffffffffu, vhi < 0 || vlo > kQuarter - 1 || vlo > vhi);
-      uint32_t pk[8];
-      if (all_out) {
-        tc_fence_before();
-        mbar_arrive(bar[SD_EMPTY + st]);
-#pragma unroll
-        for (int g = 0; g < 8; ++g) pk[g] = 0u;
-      } else {
-        float sv[16], dpv[16];
-        tmem_ld16(tS + lane_addr + st * BN + c0, sv);
-        tmem_ld16(tdP + lane_addr + st * BN + c0, dpv);
-        tmem_wait_ld();
-        tc_fence_before();
-        mbar_arrive(bar[SD_EMPTY + st]);
-        const float* lw2 = sm.lmk_lw2 + BN * t + c0;
-        const uint32_t vmask = all_in ? 0xffffffffu : range_mask32(vlo, vhi);
-#pragma unroll
-        for (int c = 0; c < kQuarter; c += 2) {
-          float d2[2];
-#pragma unroll
-          for (int e = 0; e < 2; ++e) {
-            const float bias = lmk ? lw2[c + e] + nlse2 : nlse2;
-            const float pr = fast_exp2(fmaf(sv[c + e], sl2, bias));
-            const float dsv = pr * (dpv[c + e] - delta);
-            d2[e] = (vmask >> (c + e)) & 1u ? dsv : 0.f;
-          }
-          pk[c / 2] = pack2(d2[0], d2[1], kBF16);
-        }
-      }
-      if (t >= 2) {
-        ok = mbar_wait(bar[DS_EMPTY + st], ((t >> 1) - 1) & 1, abort_flag, p.status);
-        if (!__all_sync(0xffffffffu, ok)) { ok = false; break; }
-      }
       uint8_t* dsb = sm.ds[st];
+      bool any_in = false;
 #pragma unroll
-      for (int g = 0; g < 2; ++g)
-        *reinterpret_cast<uint4*>(dsb + sw128_offset(r, c0 + 8 * g)) =
-            make_uint4(pk[4 * g], pk[4 * g + 1], pk[4 * g + 2], pk[4 * g + 3]);
-      if (!lmk && !all_out) {
-        // soft window edge on this thread's quarter: dS *= σ((w̃ − d)/τ); ∂loss/∂w̃ += dS·(1 − σ)/τ.
-        // The key at edge index e (distance d_e0 + e) sits in column ehi − e − n0 − c0.
-        const int ce0 = ehi - n0 - c0;
-        const bool has = ne > 0 && ce0 >= 0 && ce0 - (ne - 1) <= kQuarter - 1;
+      for (int k = 0; k < kHalfCols / 16; ++k) {  // 16 columns at a time
+        const int c0 = ch0 + 16 * k;
+        // valid columns of this chunk: [vlo, vhi]
+        const int vlo = lmk ? 0 : lo - n0 - c0;  // lo = INT_MAX for a row without band: stays positive
+        const int vhi = lmk ? cnt - BN * t - c0 - 1 : hi - n0 - c0;
+        const bool all_in = __all_sync(0xffffffffu, vlo <= 0 && vhi >= 15);
+        const bool all_out = __all_sync(0xffffffffu, vhi < 0 || vlo > 15 || vlo > vhi);
+        uint32_t pk[8];
+        if (all_out) {
+#pragma unroll
+          for (int g = 0; g < 8; ++g) pk[g] = 0u;
+        } else {
+          any_in = true;
+          float sv[16], dpv[16];
+          tmem_ld16(tS + lane_addr + st * BN + c0, sv);
+          tmem_ld16(tdP + lane_addr + st * BN + c0, dpv);
+          tmem_wait_ld();
+          const float* lw2 = sm.lmk_lw2 + BN * t + c0;
+          const uint32_t vmask = all_in ? 0xffffffffu : range_mask32(vlo, vhi);
+#pragma unroll
+          for (int c = 0; c < 16; c += 2) {
+            float d2[2];
+#pragma unroll
+            for (int e = 0; e < 2; ++e) {
+              const float bias = lmk ? lw2[c + e] + nlse2 : nlse2;
+              const float pr = fast_exp2(fmaf(sv[c + e], sl2, bias));
+              const float dsv = pr * (dpv[c + e] - delta);
+              d2[e] = (vmask >> (c + e)) & 1u ? dsv : 0.f;
+            }
+            pk[c / 2] = pack2(d2[0], d2[1], kBF16);
+          }
+        }
+#pragma unroll
+        for (int g = 0; g < 2; ++g)
+          *reinterpret_cast<uint4*>(dsb + sw128_offset(r, c0 + 8 * g)) =
+              make_uint4(pk[4 * g], pk[4 * g + 1], pk[4 * g + 2], pk[4 * g + 3]);
+      }
+      // every TMEM read of the tile is done: S/dP buffer st is free for tile t + 2
+      tc_fence_before();
+      mbar_arrive(bar[SD_EMPTY + st]);
+      if (!lmk && any_in) {
+        // soft window edge on this thread's half: dS *= σ((w̃ − d)/τ); ∂loss/∂w̃ += dS·(1 − σ)/τ.
+        // The key at edge index e (distance d_e0 + e) sits in column ehi − e − n0 − ch0.
+        const int ce0 = ehi - n0 - ch0;
+        const bool has = ne > 0 && ce0 >= 0 && ce0 - (ne - 1) <= kHalfCols - 1;
         if (!slow_edge) {
           if (__any_sync(0xffffffffu, has)) {
             float pv[kMaxEdge];
 #pragma unroll
             for (int e = 0; e < kMaxEdge; ++e) {
               const int c = ce0 - e;
-              const bool in = has && e < ne && c >= 0 && c < kQuarter;
-              pv[e] = in ? to_f32<T>(*reinterpret_cast<const T*>(dsb + sw128_offset(r, c0 + c))) : 0.f;
+              const bool in = has && e < ne && c >= 0 && c < kHalfCols;
+              pv[e] = in ? to_f32<T>(*reinterpret_cast<const T*>(dsb + sw128_offset(r, ch0 + c))) : 0.f;
             }
 #pragma unroll
             for (int e = 0; e < kMaxEdge; ++e) {
               const int c = ce0 - e;
-              if (has && e < ne && c >= 0 && c < kQuarter) {
-                const float g = __ldg(recg->eg + e);
+              if (has && e < ne && c >= 0 && c < kHalfCols) {
+                const float g = sm.eg[r][e];
                 const float v = pv[e] * g;
-                *reinterpret_cast<T*>(dsb + sw128_offset(r, c0 + c)) = from_f32<T>(v);
+                *reinterpret_cast<T*>(dsb + sw128_offset(r, ch0 + c)) = from_f32<T>(v);
                 dw = fmaf(v, (1.0f - g) * inv_tau, dw);
               }
             }
           }
         } else if (has) {
-          const int d_e0 = i - ehi;
-          for (int e = max(0, ce0 - (kQuarter - 1)); e < ne && ce0 - e >= 0; ++e) {
+          // edges wider than the precomputed factors: key by key
+          for (int e = max(0, ce0 - (kHalfCols - 1)); e < ne && ce0 - e >= 0; ++e) {
             const int c = ce0 - e;
-            T* ep = reinterpret_cast<T*>(dsb + sw128_offset(r, c0 + c));
-            const float sg = qrec_edge_factor(rh1.w, d_e0 + e, inv_tau);
+            T* ep = reinterpret_cast<T*>(dsb + sw128_offset(r, ch0 + c));
+            const float sg = e < kMaxEdge ? sm.eg[r][e] : qrec_edge_factor(rh1.w, i - ehi + e, inv_tau);
             const float v = to_f32<T>(*ep) * sg;
             *ep = from_f32<T>(v);
             dw = fmaf(v, (1.0f - sg) * inv_tau, dw);

@@ -175,7 +175,6 @@ __device__ __forceinline__ void write_qrec(const DsaltAttnParams& p, int64_t t, 
   int d_e0;
   QRec rec = qrec_fields(p, t, h, delta, &d_e0);
   const float inv_tau = 1.0f / p.tau_win;
-#pragma unroll
   const int ne = qrec_ne(rec);
 #pragma unroll
   for (int e = 0; e < kQRecEdge; ++e) rec.eg[e] = e < ne ? qrec_edge_factor(rec.wt, d_e0 + e, inv_tau) : 1.0f;

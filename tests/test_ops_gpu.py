@@ -155,6 +155,14 @@ def test_train_seeded_vs_oracle(case, dtype):
     _compare(res, ref, dtype)
 
 
+def test_wide_soft_edge():
+    """A soft edge wider than the precomputed factors (win_edge 20 > 8 keys): the
+    key-by-key fix-up paths of the dQ and dK/dV kernels."""
+    inp = make_inputs([400, 150], 2, 128, 16, 24.0, 120.0, seed=31)
+    res = run_train(inp, torch.bfloat16, edge=20.0)
+    _compare(res, oracle_train(inp, torch.bfloat16, edge=20.0), torch.bfloat16)
+
+
 def test_duplicate_landmark_positions():
     inp = make_inputs([150, 90], 2, 64, 8, 4.0, 40.0, seed=5, dup=True)
     _compare(run_train(inp, torch.float32), oracle_train(inp, torch.float32), torch.float32)

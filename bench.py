@@ -194,6 +194,87 @@ def cpu_time_unit(u):
     return time.perf_counter() - t0
 
 
+def prologue_bench(dev, hbm_gbs, reps=20):
+    """The fused attention prologue (RoPE on q/k + GQA expansion, forward and
+    backward) on config 4's per-GPU attention shape (8 x 2048 tokens, 16 heads,
+    head_dim 64, bf16), and with 4 kv heads; timed with CUDA events against the
+    torch expression it replaces.  Bytes are the algorithmic HBM bytes of the
+    fused kernels (each tensor read or written once)."""
+    import torch
+    from dsalt.kernels.rope_gqa import rope_gqa
+    from dsalt.kernels.window_utils import apply_rotary_emb, build_rope_cache
+    T, H, D = 8 * 2048, 16, 64
+    out = {"workload": "config4 attention prologue: T=16384 (8 x 2048), H=16, D=64, bf16, fwd+bwd"}
+    cos_c, sin_c = build_rope_cache(2048, D, dev)
+    pos = torch.arange(T, device=dev) % 2048
+    cos, sin = cos_c[pos].to(torch.bfloat16), sin_c[pos].to(torch.bfloat16)
+    for hkv in (16, 4):
+        g = torch.Generator(device=dev).manual_seed(hkv)
+        q = torch.randn(T, H, D, generator=g, device=dev).to(torch.bfloat16).requires_grad_(True)
+        k = torch.randn(T, hkv, D, generator=g, device=dev).to(torch.bfloat16).requires_grad_(True)
+        v = torch.randn(T, hkv, D, generator=g, device=dev).to(torch.bfloat16).requires_grad_(True)
+        grads = [torch.randn(T, H, D, generator=g, device=dev).to(torch.bfloat16) for _ in range(3)]
+        n_rep = H // hkv
+
+        def torch_path():
+            qr, kr = apply_rotary_emb(q, k, cos.unsqueeze(1), sin.unsqueeze(1))
+            vr = v
+            if n_rep > 1:
+                kr = kr.unsqueeze(2).expand(T, hkv, n_rep, D).reshape(T, H, D)
+                vr = v.unsqueeze(2).expand(T, hkv, n_rep, D).reshape(T, H, D)
+            return qr, kr, vr
+
+        def run(fn):
+            outs = fn()
+            torch.autograd.backward(outs, grads)
+
+        # the two kernels alone through the C ABI (buffers allocated once)
+        from dsalt.kernels import _ext
+        from dsalt.kernels.rope_gqa import _params
+        qo, ko = torch.empty_like(grads[0]), torch.empty_like(grads[0])
+        vo = torch.empty_like(grads[0]) if n_rep > 1 else None
+        dq, dk = torch.empty_like(q), torch.empty_like(k)
+        dvv = torch.empty_like(v) if n_rep > 1 else None
+        pf = _params(q, k, cos, sin, q=q, k=k, v=v if n_rep > 1 else None, q_out=qo, k_out=ko, v_out=vo)
+        pb = _params(grads[0], k, cos, sin, dq_out=grads[0], dk_out=grads[1], dv_out=grads[2] if n_rep > 1 else None,
+                     dq=dq, dk=dk, dv=dvv)
+        for _ in range(3):
+            _ext.call("dsalt_rope_gqa_fwd", pf)
+            _ext.call("dsalt_rope_gqa_bwd", pb)
+        ka, kb = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda.synchronize()
+        ka.record()
+        for _ in range(reps):
+            _ext.call("dsalt_rope_gqa_fwd", pf)
+            _ext.call("dsalt_rope_gqa_bwd", pb)
+        kb.record()
+        torch.cuda.synchronize()
+        res = {"kernels": ka.elapsed_time(kb) / reps * 1e3}
+        for name, fn in (("fused", lambda: rope_gqa(q, k, v, cos, sin)), ("torch", torch_path)):
+            for _ in range(3):
+                run(fn)
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            torch.cuda.synchronize()
+            a.record()
+            for _ in range(reps):
+                run(fn)
+            b.record()
+            torch.cuda.synchronize()
+            res[name] = a.elapsed_time(b) / reps * 1e3  # us per fwd+bwd
+        e = 2  # bytes per element
+        th, tkv, cs = T * H * D * e, T * hkv * D * e, 2 * T * D * e
+        exp = n_rep > 1  # v is expanded (else it passes through untouched)
+        fwd = th + th + tkv + th + cs + ((tkv + th) if exp else 0)   # q, q_out, k, k_out, cos/sin, v, v_out
+        bwd = th + th + cs + th + tkv + ((th + tkv) if exp else 0)   # dq_out, dk_out, cos/sin, dq, dk, dv_out, dv
+        gbs = (fwd + bwd) / (res["kernels"] * 1e-6) / 1e9
+        out[f"hkv{hkv}"] = {"kernels_us": round(res["kernels"], 2), "bytes": int(fwd + bwd),
+                            "achieved_gbs": round(gbs, 1), "frac_of_hbm": round(gbs / hbm_gbs, 3),
+                            "op_fused_us": round(res["fused"], 2), "op_torch_us": round(res["torch"], 2)}
+    out["note"] = ("kernels_us: the forward and backward kernels through the C ABI; op_*_us: forward + "
+                   "autograd backward through the fused op and through the torch expression it replaces")
+    return out
+
+
 def cpu_baseline(wl, units=2):
     us = [cpu_unit(wl, s) for s in range(units)]
     cpu_time_unit(us[0])  # warm-up (BLAS threads, page faults)
@@ -410,6 +491,7 @@ def main():
                 "clocks": clk.summary()}
         if e2e is not None:
             line["e2e"] = e2e
+        line["prologue"] = prologue_bench(dev, hbm)
         if not args.no_cpu_baseline:
             line["cpu_baseline"] = cpu_baseline(wl)
         print(json.dumps(line), flush=True)

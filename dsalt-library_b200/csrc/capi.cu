@@ -34,6 +34,8 @@ cudaError_t launch_schedule(const DsaltScheduleParams& p, cudaStream_t st);
 cudaError_t launch_gather(const DsaltGatherParams& p, cudaStream_t st);
 cudaError_t simt_attention_stage(int stage, const DsaltAttnParams& p, cudaStream_t st);
 cudaError_t launch_win_gate(const DsaltWinGateParams& p, cudaStream_t st);
+cudaError_t launch_rope_gqa(const DsaltRopeParams& p, bool bwd, cudaStream_t st);
+bool rope_gqa_fits(const DsaltRopeParams& p);
 cudaError_t launch_hybrid_scores(const DsaltScoreParams& p, cudaStream_t st);
 cudaError_t launch_topk(const DsaltTopkParams& p, cudaStream_t st);
 cudaError_t noalloc_score_scratch(float** out);
@@ -119,6 +121,7 @@ int dsalt_b200_params_sizeof(int which) {
     case 3: return (int)sizeof(DsaltScoreParams);
     case 4: return (int)sizeof(DsaltTopkParams);
     case 5: return (int)sizeof(DsaltWinGateParams);
+    case 6: return (int)sizeof(DsaltRopeParams);
   }
   return -1;
 }
@@ -193,6 +196,38 @@ int dsalt_win_gate(const DsaltWinGateParams* p, void* stream) {
   if (p->T == 0) return DSALT_OK;
   if (!p->x || !p->weight || !p->bias || !p->w_cont) return DSALT_ERR_ARG;
   return status_of(launch_win_gate(*p, (cudaStream_t)stream));
+}
+
+static int check_rope(const DsaltRopeParams* p, bool bwd) {
+  if (!p || p->T < 0 || p->H <= 0 || p->Hkv <= 0 || p->H % p->Hkv != 0) return DSALT_ERR_ARG;
+  if (p->dtype != DSALT_F16 && p->dtype != DSALT_BF16 && p->dtype != DSALT_F32) return DSALT_ERR_DTYPE;
+  if (p->D <= 0 || p->D > 256 || p->D % 16 != 0) return DSALT_ERR_HEAD_DIM;
+  if (p->T == 0) return DSALT_OK;
+  if (!rope_gqa_fits(*p)) return DSALT_ERR_TOO_LARGE;
+  if (!p->cos || !p->sin) return DSALT_ERR_ARG;
+  if (!aligned16(p->cos) || !aligned16(p->sin)) return DSALT_ERR_ALIGN;
+  const void* need[] = {bwd ? p->dq_out : p->q, bwd ? p->dk_out : p->k, bwd ? p->dq : p->q_out, bwd ? p->dk : p->k_out};
+  for (const void* ptr : need) {
+    if (!ptr) return DSALT_ERR_ARG;
+    if (!aligned16(ptr)) return DSALT_ERR_ALIGN;
+  }
+  const void* opt[] = {bwd ? p->dv_out : p->v_out, bwd ? p->dv : p->v};
+  if ((opt[0] != nullptr) != (opt[1] != nullptr)) return DSALT_ERR_ARG;  // both or neither
+  for (const void* ptr : opt)
+    if (ptr && !aligned16(ptr)) return DSALT_ERR_ALIGN;
+  return DSALT_OK;
+}
+
+int dsalt_rope_gqa_fwd(const DsaltRopeParams* p, void* stream) {
+  const int st = check_rope(p, false);
+  if (st != DSALT_OK || p->T == 0) return st;
+  return status_of(launch_rope_gqa(*p, false, (cudaStream_t)stream));
+}
+
+int dsalt_rope_gqa_bwd(const DsaltRopeParams* p, void* stream) {
+  const int st = check_rope(p, true);
+  if (st != DSALT_OK || p->T == 0) return st;
+  return status_of(launch_rope_gqa(*p, true, (cudaStream_t)stream));
 }
 
 }  // extern "C"

@@ -81,7 +81,15 @@ class WinGateParams(ctypes.Structure):
                 ("T", _i64), ("d_model", _i32), ("n_min", _f32), ("n_max", _f32), ("dtype", _i32)]
 
 
-_STRUCTS = [ScheduleParams, GatherParams, AttnParams, ScoreParams, TopkParams, WinGateParams]
+class RopeParams(ctypes.Structure):
+    _fields_ = [("q", _c_void_p), ("k", _c_void_p), ("v", _c_void_p), ("cos", _c_void_p), ("sin", _c_void_p),
+                ("q_out", _c_void_p), ("k_out", _c_void_p), ("v_out", _c_void_p),
+                ("dq_out", _c_void_p), ("dk_out", _c_void_p), ("dv_out", _c_void_p),
+                ("dq", _c_void_p), ("dk", _c_void_p), ("dv", _c_void_p),
+                ("T", _i64), ("H", _i32), ("Hkv", _i32), ("D", _i32), ("dtype", _i32)]
+
+
+_STRUCTS = [ScheduleParams, GatherParams, AttnParams, ScoreParams, TopkParams, WinGateParams, RopeParams]
 _ENTRY = {
     "dsalt_build_schedule": ScheduleParams,
     "dsalt_gather_landmarks": GatherParams,
@@ -93,6 +101,8 @@ _ENTRY = {
     "dsalt_hybrid_scores_noalloc": ScoreParams,
     "dsalt_select_topk": TopkParams,
     "dsalt_win_gate": WinGateParams,
+    "dsalt_rope_gqa_fwd": RopeParams,
+    "dsalt_rope_gqa_bwd": RopeParams,
 }
 
 _lib = None

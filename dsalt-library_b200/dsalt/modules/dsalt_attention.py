@@ -29,7 +29,8 @@ import warnings
 import torch
 import torch.nn as nn
 
-from ..kernels.window_utils import build_rope_cache, apply_rotary_emb
+from ..kernels.rope_gqa import rope_gqa
+from ..kernels.window_utils import build_rope_cache
 from ..kernels.landmark_tokens_ker import hybrid_scores_per_head
 from ..kernels.selectors import select_topk, _compute_landmark_indices
 from ..kernels.window_gate import window_continuous
@@ -214,9 +215,9 @@ class DSALTAttention(nn.Module):
             cos, sin = rope_cs
         cos = cos.to(q.dtype)
         sin = sin.to(q.dtype)
-        q, k = apply_rotary_emb(q, k, cos.unsqueeze(1), sin.unsqueeze(1))
-        k = self._repeat_kv(k)
-        v = self._repeat_kv(v)
+        # RoPE on q and k and the GQA expansion of k and v, fused (reference
+        # apply_rotary_emb + _repeat_kv, bitwise equal)
+        q, k, v = rope_gqa(q, k, v, cos, sin)
         aux = self._aux_zero(x.device, x.dtype)
 
         if self.training:

@@ -257,11 +257,42 @@ typedef struct DsaltWinGateParams {
 } DsaltWinGateParams;
 DSALT_API int dsalt_win_gate(const DsaltWinGateParams* p, void* stream);
 
+/* ---- attention prologue ---------------------------------------------------
+ * Replaces apply_rotary_emb (dsalt/kernels/window_utils.py:73-88) on q and k
+ * plus _repeat_kv (dsalt/modules/dsalt_attention.py:254-268) on k and v, as
+ * DSALTAttention._packed calls them, in one pass:
+ *   q_out = q·cos + rot(q)·sin, k_out[:, h] = (k·cos + rot(k)·sin)[:, h / n_rep],
+ *   v_out[:, h] = v[:, h / n_rep],  rot(x) = cat(−x[D/2:], x[:D/2])
+ * with the reference's rounding: each product, and the sum, rounded to dtype.
+ * The backward stage maps dq_out, dk_out, dv_out back: the sum over the n_rep
+ * copies of a kv head (rounded once), then the transposed rotation.         */
+typedef struct DsaltRopeParams {
+  const void* q;              /* [T, H, D] dtype                 (forward) */
+  const void* k;              /* [T, Hkv, D]                               */
+  const void* v;              /* [T, Hkv, D]                               */
+  const void* cos;            /* [T, D] dtype: the row of each token's position */
+  const void* sin;            /* [T, D] dtype                              */
+  void* q_out;                /* [T, H, D]                                 */
+  void* k_out;                /* [T, H, D]                                 */
+  void* v_out;                /* [T, H, D], or NULL (v not expanded)       */
+  const void* dq_out;         /* [T, H, D]                      (backward) */
+  const void* dk_out;         /* [T, H, D]                                 */
+  const void* dv_out;         /* [T, H, D], or NULL                        */
+  void* dq;                   /* [T, H, D]                                 */
+  void* dk;                   /* [T, Hkv, D]                               */
+  void* dv;                   /* [T, Hkv, D], or NULL                      */
+  int64_t T;
+  int32_t H, Hkv, D;          /* D a multiple of 16 up to 256; H a multiple of Hkv */
+  int32_t dtype;
+} DsaltRopeParams;
+DSALT_API int dsalt_rope_gqa_fwd(const DsaltRopeParams* p, void* stream);
+DSALT_API int dsalt_rope_gqa_bwd(const DsaltRopeParams* p, void* stream);
+
 /* ---- introspection ------------------------------------------------------- */
 DSALT_API int dsalt_b200_abi_version(void);
 DSALT_API const char* dsalt_b200_status_string(int status);
 /* sizeof of the parameter structs, for bindings to check their mirrors:
- * which = 0 schedule, 1 gather, 2 attn, 3 score, 4 topk, 5 win_gate        */
+ * which = 0 schedule, 1 gather, 2 attn, 3 score, 4 topk, 5 win_gate, 6 rope */
 DSALT_API int dsalt_b200_params_sizeof(int which);
 
 #ifdef __cplusplus

@@ -178,7 +178,7 @@ int dsalt_hybrid_scores_noalloc(const DsaltScoreParams* p, void* stream) {
   if (e != cudaSuccess) return status_of(e);
   DsaltScoreParams q = *p;
   q.stats = scratch;                      // [2 + 2*n_kv]
-  q.norms = scratch + 2 + 2 * p->n_kv;    // [T * (1 + n_kv)]
+  q.norms = scratch + 2 + 2 * p->n_kv;    // [(1 + n_kv), T], column-major
   return status_of(launch_hybrid_scores(q, (cudaStream_t)stream));
 }
 

@@ -61,6 +61,8 @@ cudaError_t launch_win_gate(const DsaltWinGateParams& p, cudaStream_t st) {
 // ------------------------------------------------------------- hybrid score
 // Pass 1: per token ‖x‖ and per kv-head ‖x W_Vᵀ‖, rounded to the dtype as
 // torch's norm on a dtype tensor is, then widened (landmark_tokens_ker.py:47,52).
+// The norms are stored column-major, [1 + n_kv][T], so that the statistics of a
+// column read contiguous memory.
 template <typename T>
 __global__ void __launch_bounds__(256) score_norms_kernel(DsaltScoreParams p) {
   const int lane = threadIdx.x & 31;
@@ -70,25 +72,28 @@ __global__ void __launch_bounds__(256) score_norms_kernel(DsaltScoreParams p) {
   float a = 0.f;
   for (int d = lane; d < p.d_model; d += 32) { const float v = to_f32<T>(x[d]); a = fmaf(v, v, a); }
   a = warp_sum(a);
-  const int ncols = 1 + p.n_kv;
-  if (lane == 0) p.norms[t * ncols] = round_to<T>(sqrtf(a));
+  if (lane == 0) p.norms[t] = round_to<T>(sqrtf(a));
   const T* xv = reinterpret_cast<const T*>(p.xwv) + t * (int64_t)p.n_kv * p.dh;
   for (int g = 0; g < p.n_kv; ++g) {
     float b = 0.f;
     for (int d = lane; d < p.dh; d += 32) { const float v = to_f32<T>(xv[g * p.dh + d]); b = fmaf(v, v, b); }
     b = warp_sum(b);
-    if (lane == 0) p.norms[t * ncols + 1 + g] = round_to<T>(sqrtf(b));
+    if (lane == 0) p.norms[(1 + g) * p.T + t] = round_to<T>(sqrtf(b));
   }
 }
 
 // Pass 2 (one CTA): mean and unbiased std of every norm column over all T
-// packed tokens, accumulated in fp64 (landmark_tokens_ker.py:48, 53-54).
+// packed tokens, accumulated in fp64 (landmark_tokens_ker.py:48, 53-54): thread i
+// sums tokens i, i + 1024, … of the (contiguous) column, then a fixed shuffle tree
+// and a fixed sum over the warps: one sweep for the mean, one for the centred
+// squares.
 __global__ void __launch_bounds__(1024) score_stats_kernel(DsaltScoreParams p) {
   __shared__ double red[32];
   const int ncols = 1 + p.n_kv;
   for (int c = 0; c < ncols; ++c) {
+    const float* col = p.norms + (int64_t)c * p.T;
     double acc = 0.0;
-    for (int64_t t = threadIdx.x; t < p.T; t += blockDim.x) acc += p.norms[t * ncols + c];
+    for (int64_t t = threadIdx.x; t < p.T; t += blockDim.x) acc += col[t];
     acc = warp_sum_d(acc);
     if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = acc;
     __syncthreads();
@@ -98,7 +103,7 @@ __global__ void __launch_bounds__(1024) score_stats_kernel(DsaltScoreParams p) {
     const double mean = tot / (double)p.T;
     double sq = 0.0;
     for (int64_t t = threadIdx.x; t < p.T; t += blockDim.x) {
-      const double d = p.norms[t * ncols + c] - mean;
+      const double d = col[t] - mean;
       sq += d * d;
     }
     sq = warp_sum_d(sq);
@@ -123,10 +128,9 @@ __global__ void score_mix_kernel(DsaltScoreParams p) {
   if (e >= p.T * p.H) return;
   const int64_t t = e / p.H;
   const int h = (int)(e % p.H);
-  const int ncols = 1 + p.n_kv;
   const int g = h / (p.H / p.n_kv);
-  const float zx = __fdiv_rn(__fsub_rn(p.norms[t * ncols], p.stats[0]), p.stats[1]);
-  const float zv = __fdiv_rn(__fsub_rn(p.norms[t * ncols + 1 + g], p.stats[2 + 2 * g]), p.stats[3 + 2 * g]);
+  const float zx = __fdiv_rn(__fsub_rn(p.norms[t], p.stats[0]), p.stats[1]);
+  const float zv = __fdiv_rn(__fsub_rn(p.norms[(1 + g) * p.T + t], p.stats[2 + 2 * g]), p.stats[3 + 2 * g]);
   const float a = p.alpha[h];
   p.scores[e] = __fadd_rn(__fmul_rn(a, zv), __fmul_rn(__fsub_rn(1.0f, a), zx));
   if (p.z_v) p.z_v[e] = zv;

@@ -34,7 +34,7 @@ class _HybridScore(torch.autograd.Function):
         z_x = torch.empty(T, dtype=torch.float32, device=dev)
         z_v = torch.empty(T, n_heads, dtype=torch.float32, device=dev)
         stats = torch.empty(2 + 2 * n_kv, dtype=torch.float32, device=dev)
-        norms = torch.empty(T, 1 + n_kv, dtype=torch.float32, device=dev)
+        norms = torch.empty(1 + n_kv, T, dtype=torch.float32, device=dev)  # column-major (library layout)
         if T > 0:
             p = _ext.ScoreParams(x=_ext.ptr(x_c), xwv=_ext.ptr(xv), alpha=_ext.ptr(a),
                                  scores=_ext.ptr(scores), z_x=_ext.ptr(z_x), z_v=_ext.ptr(z_v),
@@ -50,7 +50,8 @@ class _HybridScore(torch.autograd.Function):
 
     @staticmethod
     def backward(ctx, g_s, g_zx, g_zv):
-        x_c, xv, a, norms, stats, z_x, z_v = ctx.saved_tensors
+        x_c, xv, a, norms_cm, stats, z_x, z_v = ctx.saved_tensors
+        norms = norms_cm.t()  # [T, 1 + n_kv]
         H, n_kv, dh = ctx.shape
         T = x_c.shape[0]
         rep = H // n_kv

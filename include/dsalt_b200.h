@@ -201,7 +201,7 @@ typedef struct DsaltScoreParams {
   float* z_x;                 /* [T] fp32 */
   float* z_v;                 /* [T,H] fp32 */
   float* stats;               /* scratch [2 + 2*n_kv] fp32 */
-  float* norms;               /* scratch [T*(1+n_kv)] fp32 */
+  float* norms;               /* scratch [(1+n_kv), T] fp32, column-major */
   int64_t T;
   int32_t d_model, H, n_kv, dh;
   int32_t dtype;

@@ -36,6 +36,8 @@ cudaError_t simt_attention_stage(int stage, const DsaltAttnParams& p, cudaStream
 cudaError_t launch_win_gate(const DsaltWinGateParams& p, cudaStream_t st);
 cudaError_t launch_rope_gqa(const DsaltRopeParams& p, bool bwd, cudaStream_t st);
 bool rope_gqa_fits(const DsaltRopeParams& p);
+cudaError_t launch_rmsnorm(const DsaltRmsNormParams& p, bool bwd, cudaStream_t st);
+bool rmsnorm_supported(int d);
 cudaError_t launch_hybrid_scores(const DsaltScoreParams& p, cudaStream_t st);
 cudaError_t launch_topk(const DsaltTopkParams& p, cudaStream_t st);
 cudaError_t noalloc_score_scratch(float** out);
@@ -122,6 +124,7 @@ int dsalt_b200_params_sizeof(int which) {
     case 4: return (int)sizeof(DsaltTopkParams);
     case 5: return (int)sizeof(DsaltWinGateParams);
     case 6: return (int)sizeof(DsaltRopeParams);
+    case 7: return (int)sizeof(DsaltRmsNormParams);
   }
   return -1;
 }
@@ -228,6 +231,33 @@ int dsalt_rope_gqa_bwd(const DsaltRopeParams* p, void* stream) {
   const int st = check_rope(p, true);
   if (st != DSALT_OK || p->T == 0) return st;
   return status_of(launch_rope_gqa(*p, true, (cudaStream_t)stream));
+}
+
+static int check_rmsnorm(const DsaltRmsNormParams* p, bool bwd) {
+  if (!p || p->T < 0) return DSALT_ERR_ARG;
+  if (p->dtype != DSALT_F16 && p->dtype != DSALT_BF16 && p->dtype != DSALT_F32) return DSALT_ERR_DTYPE;
+  if (!rmsnorm_supported(p->d)) return DSALT_ERR_HEAD_DIM;
+  if (!(p->eps >= 0.f)) return DSALT_ERR_ARG;
+  if (p->T == 0) return DSALT_OK;
+  const void* need[] = {p->x, bwd ? p->dy : p->y, bwd ? p->dx : p->x};
+  for (const void* ptr : need) {
+    if (!ptr) return DSALT_ERR_ARG;
+    if (!aligned16(ptr)) return DSALT_ERR_ALIGN;
+  }
+  if (!p->w || (bwd && (!p->rstd || !p->dw_part))) return DSALT_ERR_ARG;
+  return DSALT_OK;
+}
+
+int dsalt_rmsnorm_fwd(const DsaltRmsNormParams* p, void* stream) {
+  const int st = check_rmsnorm(p, false);
+  if (st != DSALT_OK || p->T == 0) return st;
+  return status_of(launch_rmsnorm(*p, false, (cudaStream_t)stream));
+}
+
+int dsalt_rmsnorm_bwd(const DsaltRmsNormParams* p, void* stream) {
+  const int st = check_rmsnorm(p, true);
+  if (st != DSALT_OK || p->T == 0) return st;
+  return status_of(launch_rmsnorm(*p, true, (cudaStream_t)stream));
 }
 
 }  // extern "C"

@@ -1,8 +1,14 @@
-"""RMSNorm (reference ``dsalt/kernels/RMSENorm.py``), used by the model blocks."""
+"""RMSNorm (reference ``dsalt/kernels/RMSENorm.py``), used by the model blocks.
+
+On CUDA tensors of a supported width it runs the library's fused kernels
+(``rmsnorm_cuda``); elsewhere ``F.rms_norm``, the reference's own computation.
+"""
 
 import torch
 import torch.nn as nn
 import torch.nn.functional as F
+
+from . import rmsnorm_cuda
 
 
 class RMSENorm(nn.Module):
@@ -15,4 +21,6 @@ class RMSENorm(nn.Module):
         self.normalized_shape = (d_model,)
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
+        if rmsnorm_cuda.supported(x):
+            return rmsnorm_cuda.rms_norm(x, self.weight, self.eps)
         return F.rms_norm(x, self.normalized_shape, self.weight, self.eps).to(x.dtype)

@@ -89,7 +89,16 @@ class RopeParams(ctypes.Structure):
                 ("T", _i64), ("H", _i32), ("Hkv", _i32), ("D", _i32), ("dtype", _i32)]
 
 
-_STRUCTS = [ScheduleParams, GatherParams, AttnParams, ScoreParams, TopkParams, WinGateParams, RopeParams]
+class RmsNormParams(ctypes.Structure):
+    _fields_ = [("x", _c_void_p), ("w", _c_void_p), ("y", _c_void_p), ("rstd", _c_void_p),
+                ("dy", _c_void_p), ("dx", _c_void_p), ("dw_part", _c_void_p),
+                ("T", _i64), ("d", _i32), ("eps", _f32), ("dtype", _i32)]
+
+
+RMSNORM_ROWS_PER_PART = 64  # DSALT_RMSNORM_ROWS_PER_PART
+
+_STRUCTS = [ScheduleParams, GatherParams, AttnParams, ScoreParams, TopkParams, WinGateParams, RopeParams,
+            RmsNormParams]
 _ENTRY = {
     "dsalt_build_schedule": ScheduleParams,
     "dsalt_gather_landmarks": GatherParams,
@@ -103,6 +112,8 @@ _ENTRY = {
     "dsalt_win_gate": WinGateParams,
     "dsalt_rope_gqa_fwd": RopeParams,
     "dsalt_rope_gqa_bwd": RopeParams,
+    "dsalt_rmsnorm_fwd": RmsNormParams,
+    "dsalt_rmsnorm_bwd": RmsNormParams,
 }
 
 _lib = None

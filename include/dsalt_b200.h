@@ -288,11 +288,36 @@ typedef struct DsaltRopeParams {
 DSALT_API int dsalt_rope_gqa_fwd(const DsaltRopeParams* p, void* stream);
 DSALT_API int dsalt_rope_gqa_bwd(const DsaltRopeParams* p, void* stream);
 
+/* ---- model helpers --------------------------------------------------------
+ * RMSNorm of the model blocks (dsalt/kernels/RMSENorm.py: F.rms_norm, fp32 math
+ * under autocast, result in the input dtype), forward and backward, for
+ * d = 256, 512, 768 or 1024:
+ *   y = x·r·w, r = 1/sqrt(mean(x²) + eps);  dx = r·(g − x·r²·mean(g·x)), g = dy·w.
+ * The backward writes dw as ceil(T / DSALT_RMSNORM_ROWS_PER_PART) partial rows
+ * (each the fixed-order sum over its rows); the caller adds them.           */
+#define DSALT_RMSNORM_ROWS_PER_PART 64
+typedef struct DsaltRmsNormParams {
+  const void* x;              /* [T, d] dtype */
+  const float* w;             /* [d] fp32 */
+  void* y;                    /* [T, d] dtype                    (forward) */
+  float* rstd;                /* [T] fp32: written by the forward, read by the backward */
+  const void* dy;             /* [T, d] dtype                   (backward) */
+  void* dx;                   /* [T, d] dtype */
+  float* dw_part;             /* [ceil(T / DSALT_RMSNORM_ROWS_PER_PART), d] fp32 */
+  int64_t T;
+  int32_t d;
+  float eps;
+  int32_t dtype;
+} DsaltRmsNormParams;
+DSALT_API int dsalt_rmsnorm_fwd(const DsaltRmsNormParams* p, void* stream);
+DSALT_API int dsalt_rmsnorm_bwd(const DsaltRmsNormParams* p, void* stream);
+
 /* ---- introspection ------------------------------------------------------- */
 DSALT_API int dsalt_b200_abi_version(void);
 DSALT_API const char* dsalt_b200_status_string(int status);
 /* sizeof of the parameter structs, for bindings to check their mirrors:
- * which = 0 schedule, 1 gather, 2 attn, 3 score, 4 topk, 5 win_gate, 6 rope */
+ * which = 0 schedule, 1 gather, 2 attn, 3 score, 4 topk, 5 win_gate, 6 rope,
+ * 7 rmsnorm                                                                 */
 DSALT_API int dsalt_b200_params_sizeof(int which);
 
 #ifdef __cplusplus

@@ -38,6 +38,7 @@ cudaError_t launch_rope_gqa(const DsaltRopeParams& p, bool bwd, cudaStream_t st)
 bool rope_gqa_fits(const DsaltRopeParams& p);
 cudaError_t launch_rmsnorm(const DsaltRmsNormParams& p, bool bwd, cudaStream_t st);
 bool rmsnorm_supported(int d);
+cudaError_t launch_scale_rows(const DsaltScaleRowsParams& p, cudaStream_t st);
 cudaError_t launch_hybrid_scores(const DsaltScoreParams& p, cudaStream_t st);
 cudaError_t launch_topk(const DsaltTopkParams& p, cudaStream_t st);
 cudaError_t noalloc_score_scratch(float** out);
@@ -125,6 +126,7 @@ int dsalt_b200_params_sizeof(int which) {
     case 5: return (int)sizeof(DsaltWinGateParams);
     case 6: return (int)sizeof(DsaltRopeParams);
     case 7: return (int)sizeof(DsaltRmsNormParams);
+    case 8: return (int)sizeof(DsaltScaleRowsParams);
   }
   return -1;
 }
@@ -258,6 +260,15 @@ int dsalt_rmsnorm_bwd(const DsaltRmsNormParams* p, void* stream) {
   const int st = check_rmsnorm(p, true);
   if (st != DSALT_OK || p->T == 0) return st;
   return status_of(launch_rmsnorm(*p, true, (cudaStream_t)stream));
+}
+
+int dsalt_scale_rows(const DsaltScaleRowsParams* p, void* stream) {
+  if (!p || p->T < 0 || p->groups <= 0 || p->width <= 0 || p->width % 8 != 0) return DSALT_ERR_ARG;
+  if (p->dtype != DSALT_F16 && p->dtype != DSALT_BF16 && p->dtype != DSALT_F32) return DSALT_ERR_DTYPE;
+  if (p->T == 0) return DSALT_OK;
+  if (!p->x || !p->coef || !p->out) return DSALT_ERR_ARG;
+  if (!aligned16(p->x) || !aligned16(p->out)) return DSALT_ERR_ALIGN;
+  return status_of(launch_scale_rows(*p, (cudaStream_t)stream));
 }
 
 }  // extern "C"

@@ -151,6 +151,47 @@ cudaError_t launch_hybrid_scores(const DsaltScoreParams& p, cudaStream_t st) {
   return cudaGetLastError();
 }
 
+// Backward of the norms (landmark_tokens_ker.py:47,52 through the z-scores):
+// out[t, g·width + j] = round(coef[t·groups + g] · x[t, g·width + j]), the fp32
+// product rounded once to the dtype, as (coef · x.float()).to(dtype) computes it.
+template <typename T>
+__global__ void __launch_bounds__(256) scale_rows_kernel(DsaltScaleRowsParams p) {
+  const int64_t n8 = p.T * p.groups * (p.width / 8);
+  const int64_t i = (int64_t)blockIdx.x * 256 + threadIdx.x;
+  if (i >= n8) return;
+  const int64_t tg = i / (p.width / 8);  // t·groups + g
+  const float c = __ldg(p.coef + tg);
+  if constexpr (sizeof(T) == 2) {
+    const uint4 u = __ldg(reinterpret_cast<const uint4*>(p.x) + i);
+    const T* e = reinterpret_cast<const T*>(&u);
+    uint4 o;
+    T* oe = reinterpret_cast<T*>(&o);
+#pragma unroll
+    for (int k = 0; k < 8; ++k) oe[k] = from_f32<T>(__fmul_rn(c, to_f32<T>(e[k])));
+    reinterpret_cast<uint4*>(p.out)[i] = o;
+  } else {
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      float4 v = __ldg(reinterpret_cast<const float4*>(p.x) + 2 * i + h);
+      v.x = __fmul_rn(c, v.x); v.y = __fmul_rn(c, v.y); v.z = __fmul_rn(c, v.z); v.w = __fmul_rn(c, v.w);
+      reinterpret_cast<float4*>(p.out)[2 * i + h] = v;
+    }
+  }
+}
+
+cudaError_t launch_scale_rows(const DsaltScaleRowsParams& p, cudaStream_t st) {
+  const int64_t n8 = p.T * p.groups * (p.width / 8);
+  if (n8 == 0) return cudaSuccess;
+  const unsigned grid = (unsigned)((n8 + 255) / 256);
+  switch (p.dtype) {
+    case DSALT_F16: scale_rows_kernel<__half><<<grid, 256, 0, st>>>(p); break;
+    case DSALT_BF16: scale_rows_kernel<__nv_bfloat16><<<grid, 256, 0, st>>>(p); break;
+    case DSALT_F32: scale_rows_kernel<float><<<grid, 256, 0, st>>>(p); break;
+    default: return cudaErrorInvalidValue;
+  }
+  return cudaGetLastError();
+}
+
 // -------------------------------------------------------------------- top-k
 // Orderable key: larger float -> larger unsigned; excluded / -inf -> 0.
 __device__ __forceinline__ uint32_t order_key(float f) {

@@ -95,10 +95,15 @@ class RmsNormParams(ctypes.Structure):
                 ("T", _i64), ("d", _i32), ("eps", _f32), ("dtype", _i32)]
 
 
+class ScaleRowsParams(ctypes.Structure):
+    _fields_ = [("x", _c_void_p), ("coef", _c_void_p), ("out", _c_void_p), ("T", _i64), ("groups", _i32),
+                ("width", _i32), ("dtype", _i32)]
+
+
 RMSNORM_ROWS_PER_PART = 64  # DSALT_RMSNORM_ROWS_PER_PART
 
 _STRUCTS = [ScheduleParams, GatherParams, AttnParams, ScoreParams, TopkParams, WinGateParams, RopeParams,
-            RmsNormParams]
+            RmsNormParams, ScaleRowsParams]
 _ENTRY = {
     "dsalt_build_schedule": ScheduleParams,
     "dsalt_gather_landmarks": GatherParams,
@@ -114,6 +119,7 @@ _ENTRY = {
     "dsalt_rope_gqa_bwd": RopeParams,
     "dsalt_rmsnorm_fwd": RmsNormParams,
     "dsalt_rmsnorm_bwd": RmsNormParams,
+    "dsalt_scale_rows": ScaleRowsParams,
 }
 
 _lib = None

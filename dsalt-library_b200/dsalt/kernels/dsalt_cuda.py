@@ -145,11 +145,14 @@ def _params(prep: Prepared, q_c, k_c, v_c, tau_win: float, win_edge: float, impl
     return p
 
 
-def forward(q_c, k_c, v_c, prep: Prepared, tau_win: float, win_edge: float, impl: int):
-    """Run the forward; returns ``(o [T,H,D] input dtype, o_f32 [T,H,D] fp32, lse [T,H] fp32)``."""
+def forward(q_c, k_c, v_c, prep: Prepared, tau_win: float, win_edge: float, impl: int, f32_out: bool = True):
+    """Run the forward; returns ``(o [T,H,D] input dtype, o_f32 [T,H,D] fp32, lse [T,H] fp32)``.
+
+    With ``f32_out=False`` no fp32 copy is written and the second item is ``o``.
+    """
     o = torch.empty_like(q_c)
     o_f32 = torch.empty(q_c.shape, dtype=torch.float32, device=q_c.device) \
-        if q_c.dtype != torch.float32 else None
+        if q_c.dtype != torch.float32 and f32_out else None
     lse = torch.empty(prep.T, prep.H, dtype=torch.float32, device=q_c.device)
     p = _params(prep, q_c, k_c, v_c, tau_win, win_edge, impl, o=o, o_f32=o_f32, lse=lse)
     _ext.call("dsalt_attn_fwd", p)

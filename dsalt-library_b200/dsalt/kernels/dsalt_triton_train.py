@@ -46,48 +46,72 @@ def _validate_cu(cu, T: int) -> None:
             raise ValueError("cu_seqlens must be non-decreasing")
 
 
+def _train_forward(ctx, q, k, v, lmk_pos, lmk_logw, w_cont, cu_seqlens, tau_win, win_edge, cu_list, f32_out):
+    _cuda.check_inputs(q, k, v, cu_seqlens)
+    total_len = q.shape[0]
+    _validate_cu(_host_cu(cu_seqlens, cu_list), total_len)
+    dt = _cuda.compute_dtype(q)
+    q_c = q.contiguous().to(dt)
+    k_c = k.contiguous().to(dt)
+    v_c = v.contiguous().to(dt)
+    impl = _ext.default_impl()
+    with torch.no_grad():
+        prep = _cuda.prepare(k_c, v_c, lmk_pos, lmk_logw, w_cont, cu_seqlens, _ext.TRAIN)
+        o, o_out, lse = _cuda.forward(q_c, k_c, v_c, prep, float(tau_win), float(win_edge), impl, f32_out=f32_out)
+    ctx.save_for_backward(q_c, k_c, v_c, o, lse)
+    ctx.prep = prep
+    ctx.tau_win = float(tau_win)
+    ctx.win_edge = float(win_edge)
+    ctx.impl = impl
+    ctx.out_dtype = q.dtype
+    return o_out
+
+
+def _train_backward(ctx, grad_out):
+    q_c, k_c, v_c, o, lse = ctx.saved_tensors
+    dq, dk, dv, d_lw, dw = _cuda.backward(grad_out, q_c, k_c, v_c, o, lse, ctx.prep, ctx.tau_win,
+                                          ctx.win_edge, ctx.impl, want_dw=True)
+    od = ctx.out_dtype
+    return dq.to(od), dk.to(od), dv.to(od), d_lw.to(od), dw.to(od)
+
+
 class DSALTTrainFunction(torch.autograd.Function):
     """Autograd Function with the reference signature (dsalt_triton_train.py:585-760)."""
 
     @staticmethod
     def forward(ctx, q, k, v, lmk_pos, lmk_logw, w_cont, cu_seqlens,
                 tau_win, win_edge, n_max, cu_list=None):
-        _cuda.check_inputs(q, k, v, cu_seqlens)
-        total_len = q.shape[0]
-        _validate_cu(_host_cu(cu_seqlens, cu_list), total_len)
-        dt = _cuda.compute_dtype(q)
-        q_c = q.contiguous().to(dt)
-        k_c = k.contiguous().to(dt)
-        v_c = v.contiguous().to(dt)
-        impl = _ext.default_impl()
-        with torch.no_grad():
-            prep = _cuda.prepare(k_c, v_c, lmk_pos, lmk_logw, w_cont, cu_seqlens, _ext.TRAIN)
-            o, o_f32, lse = _cuda.forward(q_c, k_c, v_c, prep, float(tau_win), float(win_edge), impl)
-        ctx.save_for_backward(q_c, k_c, v_c, o, lse)
-        ctx.prep = prep
-        ctx.tau_win = float(tau_win)
-        ctx.win_edge = float(win_edge)
-        ctx.impl = impl
-        ctx.out_dtype = q.dtype
-        ctx.w_dtype = w_cont.dtype
-        ctx.lw_dtype = lmk_logw.dtype
         # fp32 view of the input-dtype output, written by the kernel itself
         # (the reference returns out.float(), :663)
-        return o_f32
+        return _train_forward(ctx, q, k, v, lmk_pos, lmk_logw, w_cont, cu_seqlens, tau_win, win_edge, cu_list,
+                              f32_out=True)
 
     @staticmethod
     def backward(ctx, grad_out):
-        q_c, k_c, v_c, o, lse = ctx.saved_tensors
-        dq, dk, dv, d_lw, dw = _cuda.backward(grad_out, q_c, k_c, v_c, o, lse, ctx.prep, ctx.tau_win,
-                                              ctx.win_edge, ctx.impl, want_dw=True)
-        od = ctx.out_dtype
-        return (dq.to(od), dk.to(od), dv.to(od),
+        dq, dk, dv, d_lw, dw = _train_backward(ctx, grad_out)
+        return (dq, dk, dv,
                 None,                 # lmk_pos
-                d_lw.to(od),          # -> alpha through log σ(s/τ)
-                dw.to(od),            # -> win_gate through w̃
+                d_lw,                 # -> alpha through log σ(s/τ)
+                dw,                   # -> win_gate through w̃
                 None, None, None,     # cu_seqlens, tau_win, win_edge
                 None,                 # n_max
                 None)                 # cu_list
+
+
+class _DSALTTrainFunctionInputDtype(torch.autograd.Function):
+    """The same op returning O in the (16-bit) input dtype: the values of the
+    reference's fp32 output exactly (it holds input-dtype-rounded values), for
+    callers that would cast it back at once (DSALTAttention under autocast)."""
+
+    @staticmethod
+    def forward(ctx, q, k, v, lmk_pos, lmk_logw, w_cont, cu_seqlens, tau_win, win_edge, n_max, cu_list=None):
+        return _train_forward(ctx, q, k, v, lmk_pos, lmk_logw, w_cont, cu_seqlens, tau_win, win_edge, cu_list,
+                              f32_out=False)
+
+    @staticmethod
+    def backward(ctx, grad_out):
+        dq, dk, dv, d_lw, dw = _train_backward(ctx, grad_out)
+        return dq, dk, dv, None, d_lw, dw, None, None, None, None, None
 
 
 def _dynamo_opaque(fn):
@@ -97,12 +121,17 @@ def _dynamo_opaque(fn):
 
 @_dynamo_opaque
 def dsalt_triton_train_attention(q, k, v, lmk_pos, lmk_logw, w_cont, cu_seqlens,
-                                 tau_win=1.0, win_edge=4.0, n_max=256, cu_list=None):
+                                 tau_win=1.0, win_edge=4.0, n_max=256, cu_list=None, out_dtype=None):
     """Differentiable sparse DSALT attention for training (reference :770-782).
 
     ``q, k, v`` ``[T, H, D]``; ``lmk_pos`` ``[H, S, k]`` positions inside each
     sequence (-1 = empty); ``lmk_logw`` ``[H, S, k]``; ``w_cont`` ``[T]``;
-    ``cu_seqlens`` ``[S+1]``.  Returns ``O`` ``[T, H, D]`` float32.
+    ``cu_seqlens`` ``[S+1]``.  Returns ``O`` ``[T, H, D]`` float32 (the reference's
+    output), or in q's 16-bit dtype when ``out_dtype`` is that dtype (the same
+    values, without the fp32 copy; an extension, not in the reference).
     """
+    if out_dtype is not None and out_dtype == q.dtype and q.dtype != torch.float32:
+        return _DSALTTrainFunctionInputDtype.apply(q, k, v, lmk_pos, lmk_logw, w_cont, cu_seqlens,
+                                                   tau_win, win_edge, n_max, cu_list)
     return DSALTTrainFunction.apply(q, k, v, lmk_pos, lmk_logw, w_cont, cu_seqlens,
                                     tau_win, win_edge, n_max, cu_list)

@@ -21,6 +21,16 @@ import torch.nn as nn
 from . import _ext
 
 
+def _scale_rows(x: torch.Tensor, coef: torch.Tensor, groups: int) -> torch.Tensor:
+    """``(coef[:, g, None] · x.float().view(T, groups, -1)).to(x.dtype)`` in one CUDA pass."""
+    T, width = x.shape[0], x.shape[1] // groups
+    out = torch.empty_like(x)
+    p = _ext.ScaleRowsParams(x=_ext.ptr(x), coef=_ext.ptr(coef), out=_ext.ptr(out), T=T, groups=groups,
+                             width=width, dtype=_ext.dtype_code(x.dtype))
+    _ext.call("dsalt_scale_rows", p)
+    return out
+
+
 class _HybridScore(torch.autograd.Function):
     @staticmethod
     def forward(ctx, x, xwv, alpha, n_heads: int, n_kv: int, dh: int):
@@ -71,12 +81,12 @@ class _HybridScore(torch.autograd.Function):
             if T > 1:
                 dn = dn - unclamped * z * (dz * z).sum(0, keepdim=True) / ((T - 1) * sd)
             safe = torch.where(norms > 0, norms, torch.ones_like(norms))
+            # d‖r‖/dr = r/‖r‖: each row (group) of x / x·W_Vᵀ scaled by its coefficient,
+            # the fp32 product rounded once to the dtype (dsalt_scale_rows)
             if ctx.needs_input_grad[0]:
-                dx = (dn[:, :1] / safe[:, :1]) * x_c.float()
-                dx = dx.to(x_c.dtype)
+                dx = _scale_rows(x_c, (dn[:, :1] / safe[:, :1]).contiguous(), 1)
             if ctx.needs_input_grad[1]:
-                dxwv = ((dn[:, 1:] / safe[:, 1:])[:, :, None] * xv.float().view(T, n_kv, dh))
-                dxwv = dxwv.view(T, n_kv * dh).to(xv.dtype)
+                dxwv = _scale_rows(xv, (dn[:, 1:] / safe[:, 1:]).contiguous(), n_kv)
         return dx, dxwv, d_alpha.to(ctx.alpha_dtype), None, None, None
 
 

@@ -106,7 +106,22 @@ class DSALTAttention(nn.Module):
         return torch.sigmoid(self.alpha_w)
 
     def _apply_out_proj(self, out: torch.Tensor) -> torch.Tensor:
+        # under autocast the linear casts its input itself (a 16-bit output of the
+        # op then goes in unchanged)
+        if torch.is_autocast_enabled(out.device.type):
+            return self.out_proj(out)
         return self.out_proj(out.to(self.out_proj.weight.dtype))
+
+    def _op_out_dtype(self, q: torch.Tensor):
+        """The dtype the attention op may return O in: q's 16-bit dtype when out_proj
+        computes in it (autocast, or 16-bit weights), so that the fp32 output and its
+        casts are skipped; None (the reference's fp32 output) otherwise."""
+        if q.dtype == torch.float32:
+            return None
+        dev = q.device.type
+        if torch.is_autocast_enabled(dev) and torch.get_autocast_dtype(dev) == q.dtype:
+            return q.dtype
+        return q.dtype if self.out_proj.weight.dtype == q.dtype else None
 
     def _repeat_kv(self, t: torch.Tensor) -> torch.Tensor:
         if self.n_rep == 1:
@@ -170,7 +185,7 @@ class DSALTAttention(nn.Module):
         w_cont, lmk_pos, lmk_logw = self._train_selectors(x, cu_seqlens, total_len, device, cu_list, xwv)
         return dsalt_triton_train_attention(q, k, v, lmk_pos, lmk_logw, w_cont, cu_seqlens,
                                             tau_win=self.tau_win, win_edge=float(self.win_edge),
-                                            n_max=self.n_max, cu_list=cu_list)
+                                            n_max=self.n_max, cu_list=cu_list, out_dtype=self._op_out_dtype(q))
 
     @_dynamo_opaque
     def _train_selectors(self, x, cu_seqlens, total_len, device, cu_list=None, xwv=None):

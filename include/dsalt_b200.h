@@ -257,6 +257,19 @@ typedef struct DsaltWinGateParams {
 } DsaltWinGateParams;
 DSALT_API int dsalt_win_gate(const DsaltWinGateParams* p, void* stream);
 
+/* Backward of hybrid_scores_per_head's norms (landmark_tokens_ker.py:47,52):
+ * out[t, g·width + j] = coef[t·groups + g] · x[t, g·width + j], fp32 product
+ * rounded once to dtype (width a multiple of 8; x, out 16-byte aligned).      */
+typedef struct DsaltScaleRowsParams {
+  const void* x;              /* [T, groups·width] dtype */
+  const float* coef;          /* [T, groups] fp32 */
+  void* out;                  /* [T, groups·width] dtype */
+  int64_t T;
+  int32_t groups, width;
+  int32_t dtype;
+} DsaltScaleRowsParams;
+DSALT_API int dsalt_scale_rows(const DsaltScaleRowsParams* p, void* stream);
+
 /* ---- attention prologue ---------------------------------------------------
  * Replaces apply_rotary_emb (dsalt/kernels/window_utils.py:73-88) on q and k
  * plus _repeat_kv (dsalt/modules/dsalt_attention.py:254-268) on k and v, as
@@ -317,7 +330,7 @@ DSALT_API int dsalt_b200_abi_version(void);
 DSALT_API const char* dsalt_b200_status_string(int status);
 /* sizeof of the parameter structs, for bindings to check their mirrors:
  * which = 0 schedule, 1 gather, 2 attn, 3 score, 4 topk, 5 win_gate, 6 rope,
- * 7 rmsnorm                                                                 */
+ * 7 rmsnorm, 8 scale_rows                                                   */
 DSALT_API int dsalt_b200_params_sizeof(int which);
 
 #ifdef __cplusplus

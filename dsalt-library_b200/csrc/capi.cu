@@ -39,6 +39,7 @@ bool rope_gqa_fits(const DsaltRopeParams& p);
 cudaError_t launch_rmsnorm(const DsaltRmsNormParams& p, bool bwd, cudaStream_t st);
 bool rmsnorm_supported(int d);
 cudaError_t launch_scale_rows(const DsaltScaleRowsParams& p, cudaStream_t st);
+cudaError_t launch_xent(const DsaltXentParams& p, cudaStream_t st);
 cudaError_t launch_hybrid_scores(const DsaltScoreParams& p, cudaStream_t st);
 cudaError_t launch_topk(const DsaltTopkParams& p, cudaStream_t st);
 cudaError_t noalloc_score_scratch(float** out);
@@ -127,6 +128,7 @@ int dsalt_b200_params_sizeof(int which) {
     case 6: return (int)sizeof(DsaltRopeParams);
     case 7: return (int)sizeof(DsaltRmsNormParams);
     case 8: return (int)sizeof(DsaltScaleRowsParams);
+    case 9: return (int)sizeof(DsaltXentParams);
   }
   return -1;
 }
@@ -269,6 +271,15 @@ int dsalt_scale_rows(const DsaltScaleRowsParams* p, void* stream) {
   if (!p->x || !p->coef || !p->out) return DSALT_ERR_ARG;
   if (!aligned16(p->x) || !aligned16(p->out)) return DSALT_ERR_ALIGN;
   return status_of(launch_scale_rows(*p, (cudaStream_t)stream));
+}
+
+int dsalt_xent_fwd_grad(const DsaltXentParams* p, void* stream) {
+  if (!p || p->rows < 0 || p->vocab <= 0 || p->rows > INT32_MAX) return DSALT_ERR_ARG;
+  if (p->dtype != DSALT_F16 && p->dtype != DSALT_BF16) return DSALT_ERR_DTYPE;
+  if (p->rows == 0) return DSALT_OK;
+  if (!p->logits || !p->labels || !p->row_loss || !p->scale) return DSALT_ERR_ARG;
+  if (!aligned16(p->logits)) return DSALT_ERR_ALIGN;
+  return status_of(launch_xent(*p, (cudaStream_t)stream));
 }
 
 }  // extern "C"

@@ -100,10 +100,15 @@ class ScaleRowsParams(ctypes.Structure):
                 ("width", _i32), ("dtype", _i32)]
 
 
+class XentParams(ctypes.Structure):
+    _fields_ = [("logits", _c_void_p), ("labels", _c_void_p), ("row_loss", _c_void_p), ("scale", _c_void_p),
+                ("rows", _i64), ("vocab", _i32), ("ignore_index", _i32), ("dtype", _i32)]
+
+
 RMSNORM_ROWS_PER_PART = 64  # DSALT_RMSNORM_ROWS_PER_PART
 
 _STRUCTS = [ScheduleParams, GatherParams, AttnParams, ScoreParams, TopkParams, WinGateParams, RopeParams,
-            RmsNormParams, ScaleRowsParams]
+            RmsNormParams, ScaleRowsParams, XentParams]
 _ENTRY = {
     "dsalt_build_schedule": ScheduleParams,
     "dsalt_gather_landmarks": GatherParams,
@@ -120,6 +125,7 @@ _ENTRY = {
     "dsalt_rmsnorm_fwd": RmsNormParams,
     "dsalt_rmsnorm_bwd": RmsNormParams,
     "dsalt_scale_rows": ScaleRowsParams,
+    "dsalt_xent_fwd_grad": XentParams,
 }
 
 _lib = None

@@ -4,7 +4,9 @@ Same constructor, module tree, parameter names and initialisation order as the
 reference, so a seeded construction and reference checkpoints give identical
 weights.  The attention layers run the B200 CUDA ops.  ``loss_fn="liger"``
 (a Triton fused-CE kernel outside the attention path) is not provided;
-``"auto"`` resolves to ``"chunked"``.
+``"auto"`` resolves to ``"chunked"``, which on CUDA in 16-bit compute runs the
+fused chunked loss of ``kernels/fused_ce.py`` (loss and gradient per chunk in
+one pass over the logits).
 """
 
 from __future__ import annotations
@@ -16,6 +18,7 @@ import torch.nn as nn
 import torch.nn.functional as F
 
 from ..kernels.RMSENorm import RMSENorm
+from ..kernels.fused_ce import fused_chunked_cross_entropy
 from ..modules.dsalt_transformer import DSALTTransformerBlock
 from .config import DSALTConfig
 
@@ -33,6 +36,18 @@ def _chunked_cross_entropy(x: torch.Tensor, weight: torch.Tensor, labels: torch.
         loss_acc = loss_acc + F.cross_entropy(logits, y, ignore_index=-100, reduction="sum")
         valid_acc = valid_acc + (y != -100).sum()
     return loss_acc / valid_acc.clamp(min=1.0)
+
+
+def _fused_ce_dtype(x: torch.Tensor, weight: torch.Tensor):
+    """The 16-bit dtype the chunk logits are computed in on CUDA (autocast's, or the
+    common dtype of x and the weight), for the fused loss; None: the torch path."""
+    if not x.is_cuda:
+        return None
+    half = (torch.float16, torch.bfloat16)
+    if torch.is_autocast_enabled("cuda"):
+        dt = torch.get_autocast_dtype("cuda")
+        return dt if dt in half else None
+    return x.dtype if x.dtype in half and weight.dtype == x.dtype else None
 
 
 _LOSS_FN = {"auto": None, "liger": None, "chunked": _chunked_cross_entropy}
@@ -89,6 +104,9 @@ class DSALTLMHeadModel(nn.Module):
     def _compute_loss(self, x: torch.Tensor, labels: torch.Tensor) -> torch.Tensor:
         flat_x = x.reshape(-1, self.d_model)
         flat_labels = labels.reshape(-1).long()
+        dt = _fused_ce_dtype(flat_x, self.lm_head.weight)
+        if dt is not None:
+            return fused_chunked_cross_entropy(flat_x, self.lm_head.weight, flat_labels, self.lm_head_chunk_size, dt)
         return _chunked_cross_entropy(flat_x, self.lm_head.weight, flat_labels, self.lm_head_chunk_size)
 
     @staticmethod

@@ -325,12 +325,29 @@ typedef struct DsaltRmsNormParams {
 DSALT_API int dsalt_rmsnorm_fwd(const DsaltRmsNormParams* p, void* stream);
 DSALT_API int dsalt_rmsnorm_bwd(const DsaltRmsNormParams* p, void* stream);
 
+/* Cross-entropy of one chunk of LM-head logits (dsalt/model/dsalt_lm.py:19-39:
+ * F.cross_entropy, fp32 math, sum reduction) with its gradient written over
+ * the logits: row_loss[r] = logsumexp(l_r) − l_r[y_r] (0 when y_r is
+ * ignore_index), l_r := (softmax(l_r) − onehot(y_r)) · *scale (0 for ignored
+ * rows), rounded to dtype (f16 / bf16).  *scale is typically 1 / #valid labels. */
+typedef struct DsaltXentParams {
+  void* logits;               /* [rows, vocab] dtype, 16-byte aligned; overwritten */
+  const int64_t* labels;      /* [rows] */
+  float* row_loss;            /* [rows] fp32 */
+  const float* scale;         /* device scalar */
+  int64_t rows;
+  int32_t vocab;
+  int32_t ignore_index;
+  int32_t dtype;
+} DsaltXentParams;
+DSALT_API int dsalt_xent_fwd_grad(const DsaltXentParams* p, void* stream);
+
 /* ---- introspection ------------------------------------------------------- */
 DSALT_API int dsalt_b200_abi_version(void);
 DSALT_API const char* dsalt_b200_status_string(int status);
 /* sizeof of the parameter structs, for bindings to check their mirrors:
  * which = 0 schedule, 1 gather, 2 attn, 3 score, 4 topk, 5 win_gate, 6 rope,
- * 7 rmsnorm, 8 scale_rows                                                   */
+ * 7 rmsnorm, 8 scale_rows, 9 xent                                           */
 DSALT_API int dsalt_b200_params_sizeof(int which);
 
 #ifdef __cplusplus

@@ -40,6 +40,7 @@ cudaError_t launch_rmsnorm(const DsaltRmsNormParams& p, bool bwd, cudaStream_t s
 bool rmsnorm_supported(int d);
 cudaError_t launch_scale_rows(const DsaltScaleRowsParams& p, cudaStream_t st);
 cudaError_t launch_xent(const DsaltXentParams& p, cudaStream_t st);
+cudaError_t launch_swiglu(const DsaltSwigluParams& p, bool bwd, cudaStream_t st);
 cudaError_t launch_hybrid_scores(const DsaltScoreParams& p, cudaStream_t st);
 cudaError_t launch_topk(const DsaltTopkParams& p, cudaStream_t st);
 cudaError_t noalloc_score_scratch(float** out);
@@ -129,6 +130,7 @@ int dsalt_b200_params_sizeof(int which) {
     case 7: return (int)sizeof(DsaltRmsNormParams);
     case 8: return (int)sizeof(DsaltScaleRowsParams);
     case 9: return (int)sizeof(DsaltXentParams);
+    case 10: return (int)sizeof(DsaltSwigluParams);
   }
   return -1;
 }
@@ -280,6 +282,36 @@ int dsalt_xent_fwd_grad(const DsaltXentParams* p, void* stream) {
   if (!p->logits || !p->labels || !p->row_loss || !p->scale) return DSALT_ERR_ARG;
   if (!aligned16(p->logits)) return DSALT_ERR_ALIGN;
   return status_of(launch_xent(*p, (cudaStream_t)stream));
+}
+
+static int check_swiglu(const DsaltSwigluParams* p, bool bwd) {
+  if (!p || p->T < 0 || p->F <= 0 || p->F % 8 != 0) return DSALT_ERR_ARG;
+  if (p->ld_in < p->F || p->ld_in % 8 != 0) return DSALT_ERR_ARG;
+  if (bwd && (p->ld_out < p->F || p->ld_out % 8 != 0)) return DSALT_ERR_ARG;
+  if (p->dtype != DSALT_F16 && p->dtype != DSALT_BF16) return DSALT_ERR_DTYPE;
+  if (p->T == 0) return DSALT_OK;
+  if (p->T > INT64_MAX / p->ld_in || (p->T * (p->F / 8) + 255) / 256 > (int64_t)UINT32_MAX) return DSALT_ERR_TOO_LARGE;
+  const void* fwd_ptrs[] = {p->g, p->u, p->h};
+  const void* bwd_ptrs[] = {p->g, p->u, p->dh, p->dg, p->du};
+  const void* const* need = bwd ? bwd_ptrs : fwd_ptrs;
+  const int n = bwd ? 5 : 3;
+  for (int i = 0; i < n; ++i) {
+    if (!need[i]) return DSALT_ERR_ARG;
+    if (!aligned16(need[i])) return DSALT_ERR_ALIGN;
+  }
+  return DSALT_OK;
+}
+
+int dsalt_swiglu_fwd(const DsaltSwigluParams* p, void* stream) {
+  const int st = check_swiglu(p, false);
+  if (st != DSALT_OK || p->T == 0) return st;
+  return status_of(launch_swiglu(*p, false, (cudaStream_t)stream));
+}
+
+int dsalt_swiglu_bwd(const DsaltSwigluParams* p, void* stream) {
+  const int st = check_swiglu(p, true);
+  if (st != DSALT_OK || p->T == 0) return st;
+  return status_of(launch_swiglu(*p, true, (cudaStream_t)stream));
 }
 
 }  // extern "C"

@@ -105,10 +105,15 @@ class XentParams(ctypes.Structure):
                 ("rows", _i64), ("vocab", _i32), ("ignore_index", _i32), ("dtype", _i32)]
 
 
+class SwigluParams(ctypes.Structure):
+    _fields_ = [("g", _c_void_p), ("u", _c_void_p), ("h", _c_void_p), ("dh", _c_void_p), ("dg", _c_void_p),
+                ("du", _c_void_p), ("T", _i64), ("F", _i64), ("ld_in", _i64), ("ld_out", _i64), ("dtype", _i32)]
+
+
 RMSNORM_ROWS_PER_PART = 64  # DSALT_RMSNORM_ROWS_PER_PART
 
 _STRUCTS = [ScheduleParams, GatherParams, AttnParams, ScoreParams, TopkParams, WinGateParams, RopeParams,
-            RmsNormParams, ScaleRowsParams, XentParams]
+            RmsNormParams, ScaleRowsParams, XentParams, SwigluParams]
 _ENTRY = {
     "dsalt_build_schedule": ScheduleParams,
     "dsalt_gather_landmarks": GatherParams,
@@ -126,6 +131,8 @@ _ENTRY = {
     "dsalt_rmsnorm_bwd": RmsNormParams,
     "dsalt_scale_rows": ScaleRowsParams,
     "dsalt_xent_fwd_grad": XentParams,
+    "dsalt_swiglu_fwd": SwigluParams,
+    "dsalt_swiglu_bwd": SwigluParams,
 }
 
 _lib = None
@@ -212,6 +219,19 @@ def require_cuda(t: torch.Tensor, what: str = "input") -> None:
         raise RuntimeError(
             f"dsalt (B200 build) runs on CUDA devices only; {what} is on {t.device} "
             "(there is no CPU fallback)")
+
+
+def half_compute_dtype(x: torch.Tensor, *weights: torch.Tensor):
+    """The 16-bit dtype a CUDA layer computes in: autocast's when it is on and
+    16-bit, else x's when x and every weight share one 16-bit dtype; None when the
+    layer computes in fp32 (the callers then keep the reference's torch ops)."""
+    if not x.is_cuda:
+        return None
+    half = (torch.float16, torch.bfloat16)
+    if torch.is_autocast_enabled("cuda"):
+        dt = torch.get_autocast_dtype("cuda")
+        return dt if dt in half else None
+    return x.dtype if x.dtype in half and all(w.dtype == x.dtype for w in weights) else None
 
 
 def default_impl() -> int:

@@ -5,9 +5,9 @@ of tokens, the LM-head GEMM, ``F.cross_entropy`` on fp32 copies of the logits
 and, in the backward, the log-softmax backward and casts, keeping every chunk's
 logits alive.  Here each chunk's logits (input dtype, cuBLAS GEMM) are turned in
 place into their gradient by one CUDA kernel (``dsalt_xent_fwd_grad``) and
-consumed at once by the two gradient GEMMs: dx (input dtype) and dW (each
-chunk's product rounded to the input dtype and summed in fp32, as autograd sums
-the reference's per-chunk weight gradients).  Only dx and dW are kept for the
+consumed at once by the two gradient GEMMs: dx (input dtype) and dW, summed
+over the chunks in fp32 by the GEMM epilogue (autograd sums the reference's
+per-chunk weight gradients in the compute dtype, which rounds more).  Only dx and dW are kept for the
 backward, which scales them by the incoming gradient.
 """
 
@@ -34,7 +34,7 @@ class FusedChunkedCE(torch.autograd.Function):
         scale = (1.0 / n_valid.clamp(min=1).float()).reshape(1)
         row_loss = torch.empty(N, dtype=torch.float32, device=dev)
         dx = torch.empty_like(x_c)
-        dw = torch.zeros(V, d, dtype=torch.float32, device=dev)
+        dw = None
         for s in range(0, N, chunk):
             e = min(s + chunk, N)
             logits = torch.mm(x_c[s:e], w_c.t())
@@ -43,7 +43,13 @@ class FusedChunkedCE(torch.autograd.Function):
                                 dtype=_ext.dtype_code(dtype))
             _ext.call("dsalt_xent_fwd_grad", p)
             torch.mm(logits, w_c, out=dx[s:e])
-            dw += torch.mm(logits.t(), x_c[s:e]).float()
+            # dW accumulated in fp32 by the GEMM epilogue
+            if dw is None:
+                dw = torch.mm(logits.t(), x_c[s:e], out_dtype=torch.float32)
+            else:
+                torch.addmm(dw, logits.t(), x_c[s:e], out_dtype=torch.float32, out=dw)
+        if dw is None:
+            dw = torch.zeros(V, d, dtype=torch.float32, device=dev)
         ctx.save_for_backward(dx, dw)
         ctx.x_dtype, ctx.w_dtype = x.dtype, weight.dtype
         return row_loss.sum() * scale[0]

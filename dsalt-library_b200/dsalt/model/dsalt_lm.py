@@ -18,6 +18,7 @@ import torch.nn as nn
 import torch.nn.functional as F
 
 from ..kernels.RMSENorm import RMSENorm
+from ..kernels import _ext
 from ..kernels.fused_ce import fused_chunked_cross_entropy
 from ..modules.dsalt_transformer import DSALTTransformerBlock
 from .config import DSALTConfig
@@ -39,15 +40,8 @@ def _chunked_cross_entropy(x: torch.Tensor, weight: torch.Tensor, labels: torch.
 
 
 def _fused_ce_dtype(x: torch.Tensor, weight: torch.Tensor):
-    """The 16-bit dtype the chunk logits are computed in on CUDA (autocast's, or the
-    common dtype of x and the weight), for the fused loss; None: the torch path."""
-    if not x.is_cuda:
-        return None
-    half = (torch.float16, torch.bfloat16)
-    if torch.is_autocast_enabled("cuda"):
-        dt = torch.get_autocast_dtype("cuda")
-        return dt if dt in half else None
-    return x.dtype if x.dtype in half and weight.dtype == x.dtype else None
+    """The 16-bit dtype of the chunk logits for the fused loss; None: the torch path."""
+    return _ext.half_compute_dtype(x, weight)
 
 
 _LOSS_FN = {"auto": None, "liger": None, "chunked": _chunked_cross_entropy}

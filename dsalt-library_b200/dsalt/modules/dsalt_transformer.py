@@ -7,12 +7,19 @@ import torch.nn as nn
 import torch.nn.functional as F
 import torch.utils.checkpoint
 
+from ..kernels import _ext
+from ..kernels import swiglu as swiglu_cuda
 from ..kernels.RMSENorm import RMSENorm
 from .dsalt_attention import DSALTAttention
 
 
 class SwiGLUFFN(nn.Module):
-    """``down(silu(gate(x)) * up(x))`` (reference :10-21)."""
+    """``down(silu(gate(x)) * up(x))`` (reference :10-21).
+
+    On CUDA in 16-bit compute (autocast, or 16-bit input and weights) the block
+    runs as ``kernels/swiglu.py``'s fused function: one gate+up GEMM, the CUDA
+    activation each way, one GEMM per gradient.  Elsewhere the reference's ops.
+    """
 
     def __init__(self, d_model: int, d_ff: int, dropout: float = 0.0):
         super().__init__()
@@ -22,6 +29,10 @@ class SwiGLUFFN(nn.Module):
         self.drop = nn.Dropout(dropout)
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
+        w_g, w_u, w_d = self.gate_proj.weight, self.up_proj.weight, self.down_proj.weight
+        dt = _ext.half_compute_dtype(x, w_g, w_u, w_d)
+        if dt is not None and swiglu_cuda.supported(x, w_g):
+            return self.drop(swiglu_cuda.swiglu_ffn(x, w_g, w_u, w_d, dt))
         return self.drop(self.down_proj(F.silu(self.gate_proj(x)) * self.up_proj(x)))
 
 

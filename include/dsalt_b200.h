@@ -342,12 +342,36 @@ typedef struct DsaltXentParams {
 } DsaltXentParams;
 DSALT_API int dsalt_xent_fwd_grad(const DsaltXentParams* p, void* stream);
 
+/* SwiGLU activation of the feed-forward blocks (dsalt/modules/dsalt_transformer.py:
+ * 10-21, silu(gate(x)) * up(x) under autocast), f16 / bf16, fp32 math with the
+ * rounding of the torch ops it replaces:
+ *   forward   s = R(g / (1 + exp(-g))), h = R(s·u)
+ *   backward  du = R(dh·s), dg = R(R(dh·u)·σ·(1 + g·(1 − σ))), σ = sigmoid(g)
+ * g and u are [T, F] with row stride ld_in (the two halves of a [T, 2F] GEMM
+ * output when ld_in = 2F); dg and du use row stride ld_out; h and dh are dense
+ * [T, F].  F, ld_in and ld_out are multiples of 8; pointers 16-byte aligned. */
+typedef struct DsaltSwigluParams {
+  const void* g;              /* [T, F] stride ld_in */
+  const void* u;              /* [T, F] stride ld_in */
+  void* h;                    /* [T, F]                          (forward) */
+  const void* dh;             /* [T, F]                         (backward) */
+  void* dg;                   /* [T, F] stride ld_out           (backward) */
+  void* du;                   /* [T, F] stride ld_out           (backward) */
+  int64_t T;
+  int64_t F;
+  int64_t ld_in;
+  int64_t ld_out;
+  int32_t dtype;
+} DsaltSwigluParams;
+DSALT_API int dsalt_swiglu_fwd(const DsaltSwigluParams* p, void* stream);
+DSALT_API int dsalt_swiglu_bwd(const DsaltSwigluParams* p, void* stream);
+
 /* ---- introspection ------------------------------------------------------- */
 DSALT_API int dsalt_b200_abi_version(void);
 DSALT_API const char* dsalt_b200_status_string(int status);
 /* sizeof of the parameter structs, for bindings to check their mirrors:
  * which = 0 schedule, 1 gather, 2 attn, 3 score, 4 topk, 5 win_gate, 6 rope,
- * 7 rmsnorm, 8 scale_rows, 9 xent                                           */
+ * 7 rmsnorm, 8 scale_rows, 9 xent, 10 swiglu                                */
 DSALT_API int dsalt_b200_params_sizeof(int which);
 
 #ifdef __cplusplus

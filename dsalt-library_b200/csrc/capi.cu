@@ -41,6 +41,7 @@ bool rmsnorm_supported(int d);
 cudaError_t launch_scale_rows(const DsaltScaleRowsParams& p, cudaStream_t st);
 cudaError_t launch_xent(const DsaltXentParams& p, cudaStream_t st);
 cudaError_t launch_swiglu(const DsaltSwigluParams& p, bool bwd, cudaStream_t st);
+cudaError_t launch_win_gate_bwd(const DsaltWinGateBwdParams& p, cudaStream_t st);
 cudaError_t launch_hybrid_scores(const DsaltScoreParams& p, cudaStream_t st);
 cudaError_t launch_topk(const DsaltTopkParams& p, cudaStream_t st);
 cudaError_t noalloc_score_scratch(float** out);
@@ -131,6 +132,7 @@ int dsalt_b200_params_sizeof(int which) {
     case 8: return (int)sizeof(DsaltScaleRowsParams);
     case 9: return (int)sizeof(DsaltXentParams);
     case 10: return (int)sizeof(DsaltSwigluParams);
+    case 11: return (int)sizeof(DsaltWinGateBwdParams);
   }
   return -1;
 }
@@ -300,6 +302,19 @@ static int check_swiglu(const DsaltSwigluParams* p, bool bwd) {
     if (!aligned16(need[i])) return DSALT_ERR_ALIGN;
   }
   return DSALT_OK;
+}
+
+int dsalt_win_gate_bwd(const DsaltWinGateBwdParams* p, void* stream) {
+  if (!p || p->T < 0 || p->d_model <= 0 || p->d_model % 8 != 0) return DSALT_ERR_ARG;
+  if (p->dtype != DSALT_F16 && p->dtype != DSALT_BF16) return DSALT_ERR_DTYPE;
+  if (p->T == 0 || (!p->dx && !p->dw_part)) return DSALT_OK;
+  if ((p->T + DSALT_WIN_GATE_ROWS_PER_PART - 1) / DSALT_WIN_GATE_ROWS_PER_PART > (int64_t)UINT32_MAX)
+    return DSALT_ERR_TOO_LARGE;
+  if (!p->weight || !p->dl || (p->dw_part && !p->x)) return DSALT_ERR_ARG;
+  if (!aligned16(p->weight) || (p->dw_part && (!aligned16(p->x) || !aligned16(p->dw_part))) ||
+      (p->dx && !aligned16(p->dx)))
+    return DSALT_ERR_ALIGN;
+  return status_of(launch_win_gate_bwd(*p, (cudaStream_t)stream));
 }
 
 int dsalt_swiglu_fwd(const DsaltSwigluParams* p, void* stream) {

@@ -58,6 +58,63 @@ cudaError_t launch_win_gate(const DsaltWinGateParams& p, cudaStream_t st) {
   return cudaGetLastError();
 }
 
+// Backward of the window gate's Linear (a rank-one product): dx[t, j] =
+// R(dl[t]·w[j]) (the fp32 product rounded once to the dtype) and the weight
+// gradient Σ_t dl[t]·x[t, j] as fp32 partials of DSALT_WIN_GATE_ROWS_PER_PART
+// rows each, accumulated in row order; the caller adds the partials.  A thread
+// owns 8 adjacent columns (16-byte pieces).
+constexpr int kWgRows = DSALT_WIN_GATE_ROWS_PER_PART;
+
+template <typename T>
+__global__ void __launch_bounds__(128) win_gate_bwd_kernel(const DsaltWinGateBwdParams p) {
+  const int64_t r0 = (int64_t)blockIdx.x * kWgRows;
+  const int nrow = (int)(p.T - r0 < kWgRows ? p.T - r0 : kWgRows);
+  const int pieces = p.d_model / 8;
+  for (int c = threadIdx.x; c < pieces; c += blockDim.x) {
+    float wv[8], acc[8];
+    {
+      const uint4 u = __ldg(reinterpret_cast<const uint4*>(p.weight) + c);
+      const T* e = reinterpret_cast<const T*>(&u);
+#pragma unroll
+      for (int k = 0; k < 8; ++k) { wv[k] = to_f32<T>(e[k]); acc[k] = 0.f; }
+    }
+#pragma unroll 4
+    for (int r = 0; r < nrow; ++r) {
+      const int64_t t = r0 + r;
+      const float dl = __ldg(p.dl + t);
+      if (p.dw_part) {
+        const uint4 u = __ldg(reinterpret_cast<const uint4*>(reinterpret_cast<const T*>(p.x) + t * p.d_model) + c);
+        const T* e = reinterpret_cast<const T*>(&u);
+#pragma unroll
+        for (int k = 0; k < 8; ++k) acc[k] = fmaf(dl, to_f32<T>(e[k]), acc[k]);
+      }
+      if (p.dx) {
+        uint4 o;
+        T* oe = reinterpret_cast<T*>(&o);
+#pragma unroll
+        for (int k = 0; k < 8; ++k) oe[k] = from_f32<T>(__fmul_rn(dl, wv[k]));
+        reinterpret_cast<uint4*>(reinterpret_cast<T*>(p.dx) + t * p.d_model)[c] = o;
+      }
+    }
+    if (p.dw_part) {
+      float4* dst = reinterpret_cast<float4*>(p.dw_part + (int64_t)blockIdx.x * p.d_model + 8 * c);
+      dst[0] = make_float4(acc[0], acc[1], acc[2], acc[3]);
+      dst[1] = make_float4(acc[4], acc[5], acc[6], acc[7]);
+    }
+  }
+}
+
+cudaError_t launch_win_gate_bwd(const DsaltWinGateBwdParams& p, cudaStream_t st) {
+  if (p.T == 0) return cudaSuccess;
+  const unsigned grid = (unsigned)((p.T + kWgRows - 1) / kWgRows);
+  switch (p.dtype) {
+    case DSALT_F16: win_gate_bwd_kernel<__half><<<grid, 128, 0, st>>>(p); break;
+    case DSALT_BF16: win_gate_bwd_kernel<__nv_bfloat16><<<grid, 128, 0, st>>>(p); break;
+    default: return cudaErrorInvalidValue;
+  }
+  return cudaGetLastError();
+}
+
 // ------------------------------------------------------------- hybrid score
 // Pass 1: per token ‖x‖ and per kv-head ‖x W_Vᵀ‖, rounded to the dtype as
 // torch's norm on a dtype tensor is, then widened (landmark_tokens_ker.py:47,52).
@@ -82,15 +139,53 @@ __global__ void __launch_bounds__(256) score_norms_kernel(DsaltScoreParams p) {
   }
 }
 
-// Pass 2 (one CTA): mean and unbiased std of every norm column over all T
-// packed tokens, accumulated in fp64 (landmark_tokens_ker.py:48, 53-54): thread i
-// sums tokens i, i + 1024, … of the (contiguous) column, then a fixed shuffle tree
-// and a fixed sum over the warps: one sweep for the mean, one for the centred
-// squares.
+template <typename T>
+__device__ __forceinline__ float sumsq8(const uint4 u) {
+  const T* e = reinterpret_cast<const T*>(&u);
+  float a = 0.f;
+#pragma unroll
+  for (int k = 0; k < 8; ++k) { const float v = to_f32<T>(e[k]); a = fmaf(v, v, a); }
+  return a;
+}
+
+// Pass 1 for 16-bit rows in 16-byte pieces (d_model and dh multiples of 8, dh / 8
+// a power of two up to 32): a value head spans dh / 8 adjacent lanes, reduced by
+// an xor-shuffle tree inside the lane group.
+template <typename T>
+__global__ void __launch_bounds__(256) score_norms_vec_kernel(DsaltScoreParams p) {
+  const int lane = threadIdx.x & 31;
+  const int64_t t = (int64_t)blockIdx.x * 8 + (threadIdx.x >> 5);
+  if (t >= p.T) return;  // warp-uniform
+  const uint4* x = reinterpret_cast<const uint4*>(reinterpret_cast<const T*>(p.x) + t * p.d_model);
+  float a = 0.f;
+  for (int j = lane; j < p.d_model / 8; j += 32) a += sumsq8<T>(__ldg(x + j));
+  a = warp_sum(a);
+  if (lane == 0) p.norms[t] = round_to<T>(sqrtf(a));
+  const int hv = p.dh / 8, nv = p.n_kv * hv;
+  const uint4* xv = reinterpret_cast<const uint4*>(reinterpret_cast<const T*>(p.xwv) + t * (int64_t)p.n_kv * p.dh);
+  for (int j0 = 0; j0 < nv; j0 += 32) {
+    const int j = j0 + lane;
+    float b = j < nv ? sumsq8<T>(__ldg(xv + j)) : 0.f;
+    for (int off = hv / 2; off > 0; off >>= 1) b += __shfl_xor_sync(0xffffffffu, b, off);
+    if (j < nv && (lane & (hv - 1)) == 0) p.norms[(int64_t)(1 + j / hv) * p.T + t] = round_to<T>(sqrtf(b));
+  }
+}
+
+static bool score_norms_vectorizable(const DsaltScoreParams& p) {
+  const int hv = p.dh / 8;
+  return p.dtype != DSALT_F32 && p.d_model % 8 == 0 && p.dh % 8 == 0 && hv >= 1 && hv <= 32 &&
+         (hv & (hv - 1)) == 0 && ((uintptr_t)p.x & 15u) == 0 && ((uintptr_t)p.xwv & 15u) == 0;
+}
+
+// Pass 2 (one CTA per norm column): mean and unbiased std of the column over
+// all T packed tokens, accumulated in fp64 (landmark_tokens_ker.py:48, 53-54):
+// thread i sums tokens i, i + 1024, … of the (contiguous) column, then a fixed
+// shuffle tree and a fixed sum over the warps: one sweep for the mean, one for
+// the centred squares.
 __global__ void __launch_bounds__(1024) score_stats_kernel(DsaltScoreParams p) {
   __shared__ double red[32];
-  const int ncols = 1 + p.n_kv;
-  for (int c = 0; c < ncols; ++c) {
+  {
+    const int c = blockIdx.x;
     const float* col = p.norms + (int64_t)c * p.T;
     double acc = 0.0;
     for (int64_t t = threadIdx.x; t < p.T; t += blockDim.x) acc += col[t];
@@ -140,13 +235,20 @@ __global__ void score_mix_kernel(DsaltScoreParams p) {
 cudaError_t launch_hybrid_scores(const DsaltScoreParams& p, cudaStream_t st) {
   if (p.T == 0) return cudaSuccess;
   const unsigned g1 = (unsigned)((p.T + 7) / 8);
+  const bool vec = score_norms_vectorizable(p);
   switch (p.dtype) {
-    case DSALT_F16: score_norms_kernel<__half><<<g1, 256, 0, st>>>(p); break;
-    case DSALT_BF16: score_norms_kernel<__nv_bfloat16><<<g1, 256, 0, st>>>(p); break;
+    case DSALT_F16:
+      if (vec) score_norms_vec_kernel<__half><<<g1, 256, 0, st>>>(p);
+      else score_norms_kernel<__half><<<g1, 256, 0, st>>>(p);
+      break;
+    case DSALT_BF16:
+      if (vec) score_norms_vec_kernel<__nv_bfloat16><<<g1, 256, 0, st>>>(p);
+      else score_norms_kernel<__nv_bfloat16><<<g1, 256, 0, st>>>(p);
+      break;
     case DSALT_F32: score_norms_kernel<float><<<g1, 256, 0, st>>>(p); break;
     default: return cudaErrorInvalidValue;
   }
-  score_stats_kernel<<<1, 1024, 0, st>>>(p);
+  score_stats_kernel<<<(unsigned)(1 + p.n_kv), 1024, 0, st>>>(p);
   score_mix_kernel<<<(unsigned)((p.T * p.H + 255) / 256), 256, 0, st>>>(p);
   return cudaGetLastError();
 }

@@ -6,7 +6,9 @@ kernel (``dsalt_win_gate``: one warp per token, fp32 accumulation) computes the
 logit and the whole elementwise chain with the rounding torch applies under
 autocast (each op rounded to the compute dtype), so the window equals the
 reference's bit for bit at equal logits.  The backward is analytic:
-``∂w̃/∂logit = (n_max − n_min)·σ·(1 − σ)``.
+``∂w̃/∂logit = (n_max − n_min)·σ·(1 − σ)``; in 16-bit compute the rank-one
+products ``dx = dl ⊗ w`` and ``dW = Σ_t dl·x`` run as one CUDA pass
+(``dsalt_win_gate_bwd``).
 """
 
 from __future__ import annotations
@@ -50,8 +52,23 @@ class _WinGate(torch.autograd.Function):
         xc, wc, logits = ctx.saved_tensors
         sg = torch.sigmoid(logits)
         dl = g.float() * ctx.span * sg * (1.0 - sg)                      # [T]
-        dx = (dl[:, None] * wc.float()[None, :]).to(ctx.dtypes[0]) if ctx.needs_input_grad[0] else None
-        dw = (dl[None, :] @ xc.float()).to(ctx.dtypes[1]) if ctx.needs_input_grad[1] else None
+        need_dx, need_dw = ctx.needs_input_grad[0], ctx.needs_input_grad[1]
+        T, d = xc.shape
+        if xc.dtype != torch.float32 and d % 8 == 0 and T > 0 and (need_dx or need_dw):
+            # one CUDA pass: dx = dl ⊗ w rounded to the dtype, dW as row-block partials
+            dl = dl.contiguous()
+            dx = torch.empty_like(xc) if need_dx else None
+            parts = (torch.empty((T + _ext.WIN_GATE_ROWS_PER_PART - 1) // _ext.WIN_GATE_ROWS_PER_PART, d,
+                                 dtype=torch.float32, device=xc.device) if need_dw else None)
+            p = _ext.WinGateBwdParams(x=_ext.ptr(xc), weight=_ext.ptr(wc), dl=_ext.ptr(dl),
+                                      dx=_ext.ptr(dx) if need_dx else 0, dw_part=_ext.ptr(parts) if need_dw else 0,
+                                      T=T, d_model=d, dtype=_ext.dtype_code(xc.dtype))
+            _ext.call("dsalt_win_gate_bwd", p)
+            dx = dx.to(ctx.dtypes[0]) if need_dx else None
+            dw = parts.sum(0, keepdim=True).to(ctx.dtypes[1]) if need_dw else None
+        else:
+            dx = (dl[:, None] * wc.float()[None, :]).to(ctx.dtypes[0]) if need_dx else None
+            dw = (dl[None, :] @ xc.float()).to(ctx.dtypes[1]) if need_dw else None
         db = dl.sum().reshape(1).to(ctx.dtypes[2]) if (ctx.has_bias and ctx.needs_input_grad[2]) else None
         return dx, dw, db, None, None
 

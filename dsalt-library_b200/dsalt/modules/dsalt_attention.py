@@ -206,7 +206,11 @@ class DSALTAttention(nn.Module):
         starts = cu_seqlens[:-1].to(device).long()
         abs_pos = starts[None, :, None] + lmk_pos.clamp(min=0)
         head_ix = torch.arange(self.n_heads, device=device)[:, None, None]
-        s_sel = scores[abs_pos, head_ix]
+        # scores[abs_pos, head_ix] as a flat gather, whose backward is a scatter-add
+        # instead of index_put's sort: a (position, head) pair repeats only for
+        # padding slots (lmk_pos = -1), whose gradient is exactly zero, so the sum
+        # does not depend on the order of the additions
+        s_sel = scores.reshape(-1).gather(0, (abs_pos * self.n_heads + head_ix).reshape(-1)).view(abs_pos.shape)
         lmk_logw = torch.log(torch.sigmoid(s_sel / self.tau_lmk).clamp(min=1e-20))
         lmk_logw = torch.where(lmk_pos >= 0, lmk_logw, torch.full_like(lmk_logw, float("-inf")))
         return w_cont, lmk_pos, lmk_logw

@@ -257,6 +257,24 @@ typedef struct DsaltWinGateParams {
 } DsaltWinGateParams;
 DSALT_API int dsalt_win_gate(const DsaltWinGateParams* p, void* stream);
 
+/* Backward of the window gate's Linear, d_model a multiple of 8, f16 / bf16:
+ * given dl[t] = d loss / d logit[t] (fp32), dx[t, j] = dl[t]·w[j] rounded once to
+ * dtype, and the weight gradient Σ_t dl[t]·x[t, j] as ceil(T /
+ * DSALT_WIN_GATE_ROWS_PER_PART) fp32 partial rows (each summed in row order; the
+ * caller adds them).  dx or dw_part may be NULL to skip that output.          */
+#define DSALT_WIN_GATE_ROWS_PER_PART 32
+typedef struct DsaltWinGateBwdParams {
+  const void* x;              /* [T, d_model] dtype */
+  const void* weight;         /* [d_model] dtype */
+  const float* dl;            /* [T] fp32 */
+  void* dx;                   /* [T, d_model] dtype, or NULL */
+  float* dw_part;             /* [ceil(T / DSALT_WIN_GATE_ROWS_PER_PART), d_model] fp32, or NULL */
+  int64_t T;
+  int32_t d_model;
+  int32_t dtype;
+} DsaltWinGateBwdParams;
+DSALT_API int dsalt_win_gate_bwd(const DsaltWinGateBwdParams* p, void* stream);
+
 /* Backward of hybrid_scores_per_head's norms (landmark_tokens_ker.py:47,52):
  * out[t, g·width + j] = coef[t·groups + g] · x[t, g·width + j], fp32 product
  * rounded once to dtype (width a multiple of 8; x, out 16-byte aligned).      */
@@ -371,7 +389,7 @@ DSALT_API int dsalt_b200_abi_version(void);
 DSALT_API const char* dsalt_b200_status_string(int status);
 /* sizeof of the parameter structs, for bindings to check their mirrors:
  * which = 0 schedule, 1 gather, 2 attn, 3 score, 4 topk, 5 win_gate, 6 rope,
- * 7 rmsnorm, 8 scale_rows, 9 xent, 10 swiglu                                */
+ * 7 rmsnorm, 8 scale_rows, 9 xent, 10 swiglu, 11 win_gate_bwd              */
 DSALT_API int dsalt_b200_params_sizeof(int which);
 
 #ifdef __cplusplus

@@ -141,3 +141,32 @@ def test_hybrid_scores_from_value_projection(dtype):
     gb = torch.autograd.grad(s_v, (x, W, alpha), go)
     for a, b in zip(ga, gb):
         torch.testing.assert_close(a.float(), b.float(), rtol=1e-5, atol=1e-5)
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+def test_win_gate_backward(dtype):
+    """``window_continuous`` gradients (the rank-one CUDA backward): against the same
+    formulas in fp64 (dl = g·span·σ(1−σ); dx = dl ⊗ w, one rounding; dW = Σ_t dl·x), and
+    against autograd of the reference expression ``n_min + sigmoid(win_gate(x)) *
+    (n_max - n_min)`` under autocast, which rounds dl and dW to the dtype on the way."""
+    from dsalt.kernels.window_gate import window_continuous
+    torch.manual_seed(3)
+    lin = torch.nn.Linear(256, 1).cuda()
+    x = torch.randn(1000, 256, device="cuda").to(dtype)
+    gw = torch.randn(1000, device="cuda")
+    xa, xb = x.clone().requires_grad_(True), x.clone().requires_grad_(True)
+    with torch.autocast("cuda", dtype=dtype):
+        wa = window_continuous(xa, lin, 32, 512)
+        wb = 32 + torch.sigmoid(lin(xb).squeeze(-1)) * (512 - 32)
+    ga = torch.autograd.grad(wa, [xa, lin.weight, lin.bias], gw)
+    gb = torch.autograd.grad(wb, [xb, lin.weight, lin.bias], gw)
+    w16 = lin.weight.detach().reshape(-1).to(dtype).double()
+    logit = x.double() @ w16 + lin.bias.detach().to(dtype).double()
+    sg = torch.sigmoid(logit)
+    dl = gw.to(dtype).double() * 480 * sg * (1 - sg)  # autograd rounds gw to the output's dtype
+    exp = (dl[:, None] * w16[None, :], (dl[None, :] @ x.double()), dl.sum().reshape(1))
+    for name, a, e in zip(("x", "weight", "bias"), ga, exp):
+        torch.testing.assert_close(a.double(), e, rtol=1e-2, atol=1e-3 * e.abs().max().item())
+    for name, a, b in zip(("x", "weight", "bias"), ga, gb):
+        assert a.shape == b.shape and a.dtype == b.dtype, name
+        torch.testing.assert_close(a.float(), b.float(), rtol=5e-2, atol=2e-2 * b.abs().max().item())

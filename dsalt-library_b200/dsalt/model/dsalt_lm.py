@@ -62,6 +62,7 @@ class DSALTLMHeadModel(nn.Module):
         self.n_layers = n_layers
         self.vocab_size = vocab_size
         self.lm_head_chunk_size = lm_head_chunk_size
+        self._cu_host = None  # (cu_seqlens, version, host list): see _host_cu
         self.loss_fn = loss_fn
         self.aux_loss_weight = aux_loss_weight
         if d_ff is None:
@@ -111,16 +112,28 @@ class DSALTLMHeadModel(nn.Module):
             return x.to(dt) if x.dtype != dt else x
         return x
 
-    @staticmethod
-    def _packed_rope_meta(cu_seqlens: torch.Tensor, total_len: int, attn0):
+    def _host_cu(self, cu_seqlens: torch.Tensor) -> list:
+        """Host copy of ``cu_seqlens``.  While the same tensor object comes back with
+        an unchanged version counter (no in-place write since), the previous copy is
+        reused, so a fixed packing costs no device-to-host sync per step."""
+        c = self._cu_host
+        if c is not None and c[0] is cu_seqlens and c[1] == cu_seqlens._version:
+            return c[2]
+        lst = cu_seqlens.detach().to("cpu").tolist()
+        self._cu_host = (cu_seqlens, cu_seqlens._version, lst)
+        return lst
+
+    def _packed_rope_meta(self, cu_seqlens: torch.Tensor, total_len: int, attn0):
         """RoPE cos/sin gathered per packed position and a host copy of cu_seqlens (reference :218-235)."""
         device = cu_seqlens.device
+        cu_list = self._host_cu(cu_seqlens)
         cu = cu_seqlens.long()
         lens = cu[1:] - cu[:-1]
-        seq_ids = torch.repeat_interleave(torch.arange(cu.shape[0] - 1, device=device), lens)
+        seq_ids = torch.repeat_interleave(torch.arange(cu.shape[0] - 1, device=device), lens,
+                                          output_size=int(cu_list[-1]))
         pos_ids = torch.arange(total_len, device=device) - cu[:-1][seq_ids]
         rope_cs = (attn0.rope_cos.to(device)[pos_ids], attn0.rope_sin.to(device)[pos_ids])
-        return rope_cs, cu_seqlens.detach().to("cpu").tolist()
+        return rope_cs, cu_list
 
     def forward(self, input_ids, cu_seqlens=None, max_seqlen=None, labels=None, gradient_checkpointing=False,
                 padding_mask=None) -> dict:

@@ -247,12 +247,16 @@ static int check_rmsnorm(const DsaltRmsNormParams* p, bool bwd) {
   if (!rmsnorm_supported(p->d)) return DSALT_ERR_HEAD_DIM;
   if (!(p->eps >= 0.f)) return DSALT_ERR_ARG;
   if (p->T == 0) return DSALT_OK;
-  const void* need[] = {p->x, bwd ? p->dy : p->y, bwd ? p->dx : p->x};
+  const void* need[] = {p->x, bwd ? p->dy : p->y, bwd ? p->dx : p->x, p->w};
   for (const void* ptr : need) {
     if (!ptr) return DSALT_ERR_ARG;
     if (!aligned16(ptr)) return DSALT_ERR_ALIGN;
   }
-  if (!p->w || (bwd && (!p->rstd || !p->dw_part))) return DSALT_ERR_ARG;
+  if (bwd && (!p->rstd || !p->dw_part)) return DSALT_ERR_ARG;
+  if (!bwd && p->res && (!p->x_sum || !aligned16(p->res) || !aligned16(p->x_sum)))
+    return p->x_sum ? DSALT_ERR_ALIGN : DSALT_ERR_ARG;
+  if (bwd && p->dres && !aligned16(p->dres)) return DSALT_ERR_ALIGN;
+  if ((p->T + DSALT_RMSNORM_ROWS_PER_PART - 1) / DSALT_RMSNORM_ROWS_PER_PART > INT32_MAX) return DSALT_ERR_TOO_LARGE;
   return DSALT_OK;
 }
 
@@ -292,7 +296,8 @@ static int check_swiglu(const DsaltSwigluParams* p, bool bwd) {
   if (bwd && (p->ld_out < p->F || p->ld_out % 8 != 0)) return DSALT_ERR_ARG;
   if (p->dtype != DSALT_F16 && p->dtype != DSALT_BF16) return DSALT_ERR_DTYPE;
   if (p->T == 0) return DSALT_OK;
-  if (p->T > INT64_MAX / p->ld_in || (p->T * (p->F / 8) + 255) / 256 > (int64_t)UINT32_MAX) return DSALT_ERR_TOO_LARGE;
+  if (p->T > INT64_MAX / p->ld_in || (p->T + 7) / 8 > (int64_t)UINT32_MAX || p->F / 8 > INT32_MAX)
+    return DSALT_ERR_TOO_LARGE;
   const void* fwd_ptrs[] = {p->g, p->u, p->h};
   const void* bwd_ptrs[] = {p->g, p->u, p->dh, p->dg, p->du};
   const void* const* need = bwd ? bwd_ptrs : fwd_ptrs;

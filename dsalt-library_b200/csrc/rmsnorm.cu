@@ -3,9 +3,14 @@
 //   y = round(x·r·w),  r = 1/sqrt(mean(x²) + eps)   (x·r and ·w rounded to fp32
 //   separately, the result once to the input dtype),
 //   dx = r·(g − x·r²·mean(g·x)),  g = dy·w,  dw = Σ_t dy·x·r.
+// Optionally with the residual add before it (the block's x + attn(x)): the
+// forward normalises x_sum = round(x + res) and writes x_sum, the backward adds
+// the gradient reaching x_sum from elsewhere (dres): dx = round(round(dx) + dres),
+// as torch's two ops and autograd's sum round them.
 // One warp per token row (d = 256, 512, 768 or 1024), d/32 elements per lane in
-// 16-byte pieces.  dw: each CTA sums its 64 rows in a fixed order
-// into one fp32 partial row; the caller adds the partials (deterministic).
+// 16-byte pieces; the weight row is read as float4s.  dw: each CTA sums its 64
+// rows in a fixed order into one fp32 partial row, and a second kernel adds the
+// partials column by column in a fixed order (deterministic).
 #include "common.cuh"
 
 namespace dsalt {
@@ -53,6 +58,17 @@ __device__ __forceinline__ void store_row(T* dst, int lane, const float* y) {
 // element j of a lane's registers is column (j / 8)·256 + 8·lane + j % 8
 __device__ __forceinline__ int col_of(int j, int lane) { return (j >> 3) * 256 + 8 * lane + (j & 7); }
 
+template <int V>
+__device__ __forceinline__ void load_w(const float* w, int lane, float* wv) {
+#pragma unroll
+  for (int c = 0; c < V / 8; ++c) {
+    const float4 a = __ldg(reinterpret_cast<const float4*>(w) + c * 64 + 2 * lane);
+    const float4 b = __ldg(reinterpret_cast<const float4*>(w) + c * 64 + 2 * lane + 1);
+    wv[8 * c + 0] = a.x; wv[8 * c + 1] = a.y; wv[8 * c + 2] = a.z; wv[8 * c + 3] = a.w;
+    wv[8 * c + 4] = b.x; wv[8 * c + 5] = b.y; wv[8 * c + 6] = b.z; wv[8 * c + 7] = b.w;
+  }
+}
+
 template <typename T, int V>
 __global__ void __launch_bounds__(kWarps * 32) rmsnorm_fwd_kernel(const DsaltRmsNormParams p) {
   const int lane = threadIdx.x & 31;
@@ -60,22 +76,34 @@ __global__ void __launch_bounds__(kWarps * 32) rmsnorm_fwd_kernel(const DsaltRms
   if (row >= p.T) return;
   float x[V];
   load_row<T, V>(reinterpret_cast<const T*>(p.x) + row * p.d, lane, x);
+  if (p.res) {
+    float r[V];
+    load_row<T, V>(reinterpret_cast<const T*>(p.res) + row * p.d, lane, r);
+#pragma unroll
+    for (int j = 0; j < V; ++j) x[j] = round_to<T>(__fadd_rn(x[j], r[j]));
+    store_row<T, V>(reinterpret_cast<T*>(p.x_sum) + row * p.d, lane, x);
+  }
   float ss = 0.f;
 #pragma unroll
   for (int j = 0; j < V; ++j) ss = fmaf(x[j], x[j], ss);
   ss = warp_sum(ss);
   const float r = rsqrtf(__fadd_rn(__fdiv_rn(ss, (float)p.d), p.eps));
   if (lane == 0 && p.rstd) p.rstd[row] = r;
+  float w[V];
+  load_w<V>(p.w, lane, w);
 #pragma unroll
-  for (int j = 0; j < V; ++j) x[j] = __fmul_rn(__fmul_rn(x[j], r), __ldg(p.w + col_of(j, lane)));
+  for (int j = 0; j < V; ++j) x[j] = __fmul_rn(__fmul_rn(x[j], r), w[j]);
   store_row<T, V>(reinterpret_cast<T*>(p.y) + row * p.d, lane, x);
 }
 
+// Backward: one warp per row, kRowsPerWarp rows per warp in turn, the weight row
+// and the dw accumulators in registers (two CTAs per SM).
 template <typename T, int V>
-__global__ void __launch_bounds__(kWarps * 32) rmsnorm_bwd_kernel(const DsaltRmsNormParams p) {
+__global__ void __launch_bounds__(kWarps * 32, 2) rmsnorm_bwd_kernel(const DsaltRmsNormParams p) {
   __shared__ float part[kWarps][V * 32];
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  float dw[V];
+  float w[V], dw[V];
+  load_w<V>(p.w, lane, w);
 #pragma unroll
   for (int j = 0; j < V; ++j) dw[j] = 0.f;
   for (int k = 0; k < kRowsPerWarp; ++k) {
@@ -90,13 +118,18 @@ __global__ void __launch_bounds__(kWarps * 32) rmsnorm_bwd_kernel(const DsaltRms
     for (int j = 0; j < V; ++j) {
       const float xr = x[j] * r;
       dw[j] = fmaf(g[j], xr, dw[j]);
-      g[j] *= __ldg(p.w + col_of(j, lane));
+      g[j] *= w[j];
       dot = fmaf(g[j], x[j], dot);
     }
     dot = warp_sum(dot);
     const float c = r * r * dot / (float)p.d;
 #pragma unroll
     for (int j = 0; j < V; ++j) g[j] = r * fmaf(-x[j], c, g[j]);
+    if (p.dres) {
+      load_row<T, V>(reinterpret_cast<const T*>(p.dres) + row * p.d, lane, x);
+#pragma unroll
+      for (int j = 0; j < V; ++j) g[j] = __fadd_rn(round_to<T>(g[j]), x[j]);
+    }
     store_row<T, V>(reinterpret_cast<T*>(p.dx) + row * p.d, lane, g);
   }
   // the CTA's partial of dw: warps added in order
@@ -106,8 +139,32 @@ __global__ void __launch_bounds__(kWarps * 32) rmsnorm_bwd_kernel(const DsaltRms
   for (int cidx = threadIdx.x; cidx < p.d; cidx += blockDim.x) {
     float s = 0.f;
 #pragma unroll
-    for (int w = 0; w < kWarps; ++w) s += part[w][cidx];
+    for (int w8 = 0; w8 < kWarps; ++w8) s += part[w8][cidx];
     p.dw_part[(int64_t)blockIdx.x * p.d + cidx] = s;
+  }
+}
+
+// dw[c] = Σ_i part[i][c] over the partial rows in a fixed order: a CTA owns 32
+// columns; warp g sums rows g, g + 32, …, then the 32 warp sums are added in order.
+constexpr int kColsumWarps = 32;
+
+__global__ void __launch_bounds__(kColsumWarps * 32) colsum_kernel(const float* __restrict__ part, int nparts, int d,
+                                                                   float* __restrict__ out) {
+  __shared__ float s[kColsumWarps][33];
+  const int lane = threadIdx.x & 31, grp = threadIdx.x >> 5;
+  const int col = blockIdx.x * 32 + lane;
+  float acc = 0.f;
+  if (col < d) {
+#pragma unroll 8
+    for (int i = grp; i < nparts; i += kColsumWarps) acc += __ldg(part + (int64_t)i * d + col);
+  }
+  s[grp][lane] = acc;
+  __syncthreads();
+  if (grp == 0 && col < d) {
+    float t = 0.f;
+#pragma unroll
+    for (int g = 0; g < kColsumWarps; ++g) t += s[g][lane];
+    out[col] = t;
   }
 }
 
@@ -116,6 +173,7 @@ cudaError_t launch_v(const DsaltRmsNormParams& p, bool bwd, cudaStream_t st) {
   if (bwd) {
     const unsigned grid = (unsigned)((p.T + kRowsPerCta - 1) / kRowsPerCta);
     rmsnorm_bwd_kernel<T, V><<<grid, kWarps * 32, 0, st>>>(p);
+    if (p.dw) colsum_kernel<<<(unsigned)((p.d + 31) / 32), kColsumWarps * 32, 0, st>>>(p.dw_part, (int)grid, p.d, p.dw);
   } else {
     const unsigned grid = (unsigned)((p.T + kWarps - 1) / kWarps);
     rmsnorm_fwd_kernel<T, V><<<grid, kWarps * 32, 0, st>>>(p);

@@ -24,3 +24,11 @@ class RMSENorm(nn.Module):
         if rmsnorm_cuda.supported(x):
             return rmsnorm_cuda.rms_norm(x, self.weight, self.eps)
         return F.rms_norm(x, self.normalized_shape, self.weight, self.eps).to(x.dtype)
+
+    def add_forward(self, x: torch.Tensor, res: torch.Tensor):
+        """``(x + res, self(x + res))``: the residual add in front of the norm, fused
+        into the CUDA kernel when x and res share a dtype and shape."""
+        if rmsnorm_cuda.supported(x) and res.dtype == x.dtype and res.shape == x.shape and res.is_cuda:
+            return rmsnorm_cuda.add_rms_norm(x, res, self.weight, self.eps)
+        s = x + res
+        return s, self(s)

@@ -21,7 +21,7 @@ F16, BF16, F32 = 0, 1, 2
 TRAIN, INFER = 0, 1
 IMPL_AUTO, IMPL_SIMT, IMPL_TCGEN05 = 0, 1, 2
 DEV_WAIT_TIMEOUT, DEV_BAD_INDEX = 1, 2
-ABI_VERSION = 3
+ABI_VERSION = 4
 QREC_FLOATS = 16  # DSALT_QREC_FLOATS
 LMK_SPLIT = 4  # DSALT_LMK_SPLIT
 
@@ -90,9 +90,9 @@ class RopeParams(ctypes.Structure):
 
 
 class RmsNormParams(ctypes.Structure):
-    _fields_ = [("x", _c_void_p), ("w", _c_void_p), ("y", _c_void_p), ("rstd", _c_void_p),
-                ("dy", _c_void_p), ("dx", _c_void_p), ("dw_part", _c_void_p),
-                ("T", _i64), ("d", _i32), ("eps", _f32), ("dtype", _i32)]
+    _fields_ = [("x", _c_void_p), ("res", _c_void_p), ("x_sum", _c_void_p), ("w", _c_void_p), ("y", _c_void_p),
+                ("rstd", _c_void_p), ("dy", _c_void_p), ("dres", _c_void_p), ("dx", _c_void_p),
+                ("dw_part", _c_void_p), ("dw", _c_void_p), ("T", _i64), ("d", _i32), ("eps", _f32), ("dtype", _i32)]
 
 
 class ScaleRowsParams(ctypes.Structure):

@@ -145,11 +145,15 @@ class DSALTLMHeadModel(nn.Module):
         rope_cs = cu_list = None
         if cu_seqlens is not None:
             rope_cs, cu_list = self._packed_rope_meta(cu_seqlens, input_ids.shape[0], self.layers[0].attn)
+        # each block leaves its last residual add (x + ffn_out) to the next RMSNorm,
+        # which fuses it: the next block's attn_norm, or final_norm
+        pending = None
         for layer in self.layers:
-            x, layer_aux = layer(x, cu_seqlens=cu_seqlens, max_seqlen=max_seqlen,
-                                 gradient_checkpointing=gradient_checkpointing, rope_cs=rope_cs, cu_list=cu_list)
+            x, layer_aux, pending = layer(x, cu_seqlens=cu_seqlens, max_seqlen=max_seqlen,
+                                          gradient_checkpointing=gradient_checkpointing, rope_cs=rope_cs,
+                                          cu_list=cu_list, pending=pending, defer=True)
             aux_loss = aux_loss + layer_aux
-        x = self.final_norm(x)
+        x = self.final_norm(x) if pending is None else self.final_norm.add_forward(x, pending)[1]
         if labels is not None:
             loss = self._compute_loss(x, labels) + self.aux_loss_weight * aux_loss
             return {"loss": loss, "logits": None, "aux_loss": aux_loss.detach()}

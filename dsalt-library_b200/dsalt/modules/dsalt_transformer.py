@@ -52,21 +52,37 @@ class DSALTTransformerBlock(nn.Module):
         self.ffn = SwiGLUFFN(d_model=d_model, d_ff=d_ff, dropout=dropout)
 
     def forward(self, x, cu_seqlens=None, max_seqlen=None, gradient_checkpointing=False, rope_cs=None,
-                cu_list=None):
-        if gradient_checkpointing and self.training:
-            aux_box = []
+                cu_list=None, pending=None, defer=False):
+        """``(x, aux)`` as the reference block.  ``pending`` / ``defer`` let the model
+        fuse each residual add into the RMSNorm after it: with ``pending`` the block
+        first forms ``x + pending``; with ``defer`` it returns ``(x, aux, ffn_out)``
+        and leaves the final ``x + ffn_out`` to the caller."""
+        if not (gradient_checkpointing and self.training):
+            if pending is not None:
+                x, h = self.attn_norm.add_forward(x, pending)
+            else:
+                h = self.attn_norm(x)
+            x_attn, aux = self.attn(h, cu_seqlens=cu_seqlens, max_seqlen=max_seqlen, rope_cs=rope_cs,
+                                    cu_list=cu_list)
+            x, h = self.ffn_norm.add_forward(x, x_attn)
+            f = self.ffn(h)
+            return (x, aux, f) if defer else (x + f, aux)
+        if pending is not None:
+            x = x + pending
+        x, aux = self._forward_checkpointed(x, cu_seqlens, max_seqlen, rope_cs, cu_list)
+        return (x, aux, None) if defer else (x, aux)
 
-            def attn_fn(h):
-                out, a = self.attn(h, cu_seqlens=cu_seqlens, max_seqlen=max_seqlen, rope_cs=rope_cs,
-                                   cu_list=cu_list)
-                aux_box.append(a)
-                return out
-            x = x + torch.utils.checkpoint.checkpoint(attn_fn, self.attn_norm(x), use_reentrant=False)
-            x = x + torch.utils.checkpoint.checkpoint(self.ffn, self.ffn_norm(x), use_reentrant=False)
-            aux = aux_box[-1] if aux_box else torch.zeros((), device=x.device, dtype=x.dtype)
-            return x, aux
-        x_attn, aux = self.attn(self.attn_norm(x), cu_seqlens=cu_seqlens, max_seqlen=max_seqlen,
-                                rope_cs=rope_cs, cu_list=cu_list)
-        x = x + x_attn
-        x = x + self.ffn(self.ffn_norm(x))
+    def _forward_checkpointed(self, x, cu_seqlens, max_seqlen, rope_cs, cu_list):
+        """The reference's checkpointed path: attention and FFN recomputed in the backward."""
+        aux_box = []
+
+        def attn_fn(h):
+            out, a = self.attn(h, cu_seqlens=cu_seqlens, max_seqlen=max_seqlen, rope_cs=rope_cs,
+                               cu_list=cu_list)
+            aux_box.append(a)
+            return out
+        x = x + torch.utils.checkpoint.checkpoint(attn_fn, self.attn_norm(x), use_reentrant=False)
+        x = x + torch.utils.checkpoint.checkpoint(self.ffn, self.ffn_norm(x), use_reentrant=False)
+        aux = aux_box[-1] if aux_box else torch.zeros((), device=x.device, dtype=x.dtype)
         return x, aux
+

@@ -29,7 +29,7 @@
 extern "C" {
 #endif
 
-#define DSALT_B200_ABI_VERSION 3
+#define DSALT_B200_ABI_VERSION 4
 
 /* The tensor-core dK/dV stage splits each landmark chunk's query range into
  * this many parts that run as separate CTAs; their fp32 partial sums are added
@@ -324,17 +324,25 @@ DSALT_API int dsalt_rope_gqa_bwd(const DsaltRopeParams* p, void* stream);
  * under autocast, result in the input dtype), forward and backward, for
  * d = 256, 512, 768 or 1024:
  *   y = x·r·w, r = 1/sqrt(mean(x²) + eps);  dx = r·(g − x·r²·mean(g·x)), g = dy·w.
- * The backward writes dw as ceil(T / DSALT_RMSNORM_ROWS_PER_PART) partial rows
- * (each the fixed-order sum over its rows); the caller adds them.           */
+ * With res set, the forward first forms x_sum = R(x + res) (the block's residual
+ * add, rounded to dtype), writes it and normalises it; the backward then takes
+ * x = x_sum and, with dres set, returns dx = R(R(dx) + dres), dres being the
+ * gradient reaching x_sum from its other consumers.  The backward writes dw as
+ * ceil(T / DSALT_RMSNORM_ROWS_PER_PART) partial rows (each the fixed-order sum
+ * over its rows) and, with dw set, their fixed-order column sums.           */
 #define DSALT_RMSNORM_ROWS_PER_PART 64
 typedef struct DsaltRmsNormParams {
-  const void* x;              /* [T, d] dtype */
-  const float* w;             /* [d] fp32 */
-  void* y;                    /* [T, d] dtype                    (forward) */
+  const void* x;              /* [T, d] dtype (backward: the normalised input) */
+  const void* res;            /* [T, d] dtype, or NULL                    (forward) */
+  void* x_sum;                /* [T, d] dtype, written when res is set    (forward) */
+  const float* w;             /* [d] fp32, 16-byte aligned */
+  void* y;                    /* [T, d] dtype                             (forward) */
   float* rstd;                /* [T] fp32: written by the forward, read by the backward */
-  const void* dy;             /* [T, d] dtype                   (backward) */
+  const void* dy;             /* [T, d] dtype                            (backward) */
+  const void* dres;           /* [T, d] dtype, or NULL                   (backward) */
   void* dx;                   /* [T, d] dtype */
   float* dw_part;             /* [ceil(T / DSALT_RMSNORM_ROWS_PER_PART), d] fp32 */
+  float* dw;                  /* [d] fp32, or NULL: the partials summed */
   int64_t T;
   int32_t d;
   float eps;

@@ -213,6 +213,8 @@ static int check_rope(const DsaltRopeParams* p, bool bwd) {
   if (!p || p->T < 0 || p->H <= 0 || p->Hkv <= 0 || p->H % p->Hkv != 0) return DSALT_ERR_ARG;
   if (p->dtype != DSALT_F16 && p->dtype != DSALT_BF16 && p->dtype != DSALT_F32) return DSALT_ERR_DTYPE;
   if (p->D <= 0 || p->D > 256 || p->D % 16 != 0) return DSALT_ERR_HEAD_DIM;
+  if (p->ld != 0 && (p->ld < (int64_t)p->H * p->D || p->ld % (p->dtype == DSALT_F32 ? 4 : 8) != 0))
+    return DSALT_ERR_ARG;
   if (p->T == 0) return DSALT_OK;
   if (!rope_gqa_fits(*p)) return DSALT_ERR_TOO_LARGE;
   if (!p->cos || !p->sin) return DSALT_ERR_ARG;

@@ -4,7 +4,9 @@
 // dsalt/modules/dsalt_attention.py:254-268), plus the backward of both.
 //
 // Layout: q [T, H, D], k and v [T, Hkv, D], cos and sin [T, D] (each token's
-// position row, input dtype), outputs [T, H, D].  One thread handles the 8
+// position row, input dtype), outputs [T, H, D].  With ld set, q, k and v (and in
+// the backward dq, dk and dv) are column blocks of one [T, ld] buffer, the output
+// of a single q|k|v projection GEMM.  One thread handles the 8
 // elements j0 … j0+7 of the first half of a row and their partners j0+D/2 …,
 // with 16-byte (fp32: 32-byte) loads and stores.
 //
@@ -103,17 +105,18 @@ __global__ void __launch_bounds__(kThreads, 4) rope_gqa_fwd_kernel(const DsaltRo
   const uint32_t row = idx >> lg;  // t·H + h
   const uint32_t t = row / (uint32_t)p.H;
   const uint32_t h = row - t * (uint32_t)p.H;
-  const uint32_t krow = t * (uint32_t)p.Hkv + h / (uint32_t)n_rep;
+  const int64_t ldq = p.ld ? p.ld : (int64_t)p.H * p.D, ldk = p.ld ? p.ld : (int64_t)p.Hkv * p.D;
+  const int64_t kofs = (int64_t)t * ldk + (int64_t)(h / (uint32_t)n_rep) * p.D + j0;
   float c1[8], c2[8], s1[8], s2[8], a[8], b[8];
   load_cs<T>(p, t, j0, half, c1, c2, s1, s2);
-  const T* q = reinterpret_cast<const T*>(p.q) + (int64_t)row * p.D + j0;
+  const T* q = reinterpret_cast<const T*>(p.q) + (int64_t)t * ldq + (int64_t)h * p.D + j0;
   load8<T>(q, a);
   load8<T>(q + half, b);
   rope8<T>(a, b, c1, c2, s1, s2);
   T* qo = reinterpret_cast<T*>(p.q_out) + (int64_t)row * p.D + j0;
   store8<T>(qo, a);
   store8<T>(qo + half, b);
-  const T* k = reinterpret_cast<const T*>(p.k) + (int64_t)krow * p.D + j0;
+  const T* k = reinterpret_cast<const T*>(p.k) + kofs;
   load8<T>(k, a);
   load8<T>(k + half, b);
   rope8<T>(a, b, c1, c2, s1, s2);
@@ -121,7 +124,7 @@ __global__ void __launch_bounds__(kThreads, 4) rope_gqa_fwd_kernel(const DsaltRo
   store8<T>(ko, a);
   store8<T>(ko + half, b);
   if (p.v_out) {
-    const T* v = reinterpret_cast<const T*>(p.v) + (int64_t)krow * p.D + j0;
+    const T* v = reinterpret_cast<const T*>(p.v) + kofs;
     T* vo = reinterpret_cast<T*>(p.v_out) + (int64_t)row * p.D + j0;
     load8<T>(v, a);
     load8<T>(v + half, b);
@@ -142,12 +145,14 @@ __global__ void __launch_bounds__(kThreads, 4) rope_gqa_bwd_kernel(const DsaltRo
     const int j0 = 8 * (int)(idx & ((1u << lg) - 1));
     const uint32_t row = idx >> lg;
     const uint32_t t = row / (uint32_t)p.H;
+    const uint32_t h = row - t * (uint32_t)p.H;
     load_cs<T>(p, t, j0, half, c1, c2, s1, s2);
     const T* g = reinterpret_cast<const T*>(p.dq_out) + (int64_t)row * p.D + j0;
     load8<T>(g, g1);
     load8<T>(g + half, g2);
     rope8_t<T>(g1, g2, c1, c2, s1, s2);
-    T* dq = reinterpret_cast<T*>(p.dq) + (int64_t)row * p.D + j0;
+    const int64_t ldq = p.ld ? p.ld : (int64_t)p.H * p.D;
+    T* dq = reinterpret_cast<T*>(p.dq) + (int64_t)t * ldq + (int64_t)h * p.D + j0;
     store8<T>(dq, g1);
     store8<T>(dq + half, g2);
     return;
@@ -175,7 +180,8 @@ __global__ void __launch_bounds__(kThreads, 4) rope_gqa_bwd_kernel(const DsaltRo
   for (int i = 0; i < 8; ++i) { g1[i] = round_to<T>(g1[i]); g2[i] = round_to<T>(g2[i]); }
   load_cs<T>(p, t, j0, half, c1, c2, s1, s2);
   rope8_t<T>(g1, g2, c1, c2, s1, s2);
-  T* dk = reinterpret_cast<T*>(p.dk) + (int64_t)krow * p.D + j0;
+  const int64_t kofs = (int64_t)t * (p.ld ? p.ld : (int64_t)p.Hkv * p.D) + (int64_t)hk * p.D + j0;
+  T* dk = reinterpret_cast<T*>(p.dk) + kofs;
   store8<T>(dk, g1);
   store8<T>(dk + half, g2);
   if (p.dv_out && p.dv) {
@@ -190,7 +196,7 @@ __global__ void __launch_bounds__(kThreads, 4) rope_gqa_bwd_kernel(const DsaltRo
 #pragma unroll
       for (int i = 0; i < 8; ++i) g2[i] += x[i];
     }
-    T* dv = reinterpret_cast<T*>(p.dv) + (int64_t)krow * p.D + j0;
+    T* dv = reinterpret_cast<T*>(p.dv) + kofs;
     store8<T>(dv, g1);
     store8<T>(dv + half, g2);
   }

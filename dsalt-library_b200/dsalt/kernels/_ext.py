@@ -86,7 +86,7 @@ class RopeParams(ctypes.Structure):
                 ("q_out", _c_void_p), ("k_out", _c_void_p), ("v_out", _c_void_p),
                 ("dq_out", _c_void_p), ("dk_out", _c_void_p), ("dv_out", _c_void_p),
                 ("dq", _c_void_p), ("dk", _c_void_p), ("dv", _c_void_p),
-                ("T", _i64), ("H", _i32), ("Hkv", _i32), ("D", _i32), ("dtype", _i32)]
+                ("T", _i64), ("ld", _i64), ("H", _i32), ("Hkv", _i32), ("D", _i32), ("dtype", _i32)]
 
 
 class RmsNormParams(ctypes.Structure):

@@ -80,3 +80,87 @@ class RopeGqaFunction(torch.autograd.Function):
 def rope_gqa(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor):
     """RoPE on q and k and the expansion of k and v to q's heads, fused (see the module docstring)."""
     return RopeGqaFunction.apply(q, k, v, cos, sin)
+
+
+class QkvRopeFunction(torch.autograd.Function):
+    """The q/k/v projections (bias-free) plus the prologue, with one GEMM each way.
+
+    ``(x [T, d], w_q [H·D, d], w_k [Hkv·D, d], w_v [Hkv·D, d], cos, sin, H, Hkv, D,
+    dtype) -> (q_rot, k_rot, v)`` ([T, H, D] each, k and v expanded to the query
+    heads), plus under GQA the unexpanded value projection ``[T, Hkv·D]`` as a
+    fourth output.  The three weights are stacked into one ``[(H + 2·Hkv)·D, d]``
+    operand, so the forward is one GEMM whose ``[T, (H + 2·Hkv)·D]`` output the
+    prologue kernel reads in column blocks (``ld``); the backward writes dq, dk and
+    dv into one such buffer and runs one GEMM for dx and one for the three weight
+    gradients (fp32 out).  The rotation and expansion round as in ``rope_gqa``;
+    dx is one GEMM over all three blocks instead of the sum of three rounded ones.
+    """
+
+    @staticmethod
+    def forward(ctx, x, w_q, w_k, w_v, cos, sin, H: int, Hkv: int, D: int, dtype: torch.dtype):
+        _ext.require_cuda(x, "x")
+        T, d = x.shape
+        nq, nk = H * D, Hkv * D
+        W = nq + 2 * nk
+        dev = x.device
+        x2 = x.to(dtype).contiguous()
+        w = torch.empty(W, d, dtype=dtype, device=dev)
+        w[:nq].copy_(w_q.detach())
+        w[nq:nq + nk].copy_(w_k.detach())
+        w[nq + nk:].copy_(w_v.detach())
+        qkv = torch.mm(x2, w.t())
+        cos, sin = cos.to(dtype).contiguous(), sin.to(dtype).contiguous()
+        q_out = torch.empty(T, H, D, dtype=dtype, device=dev)
+        k_out = torch.empty(T, H, D, dtype=dtype, device=dev)
+        v_out = torch.empty(T, H, D, dtype=dtype, device=dev)
+        p = _ext.RopeParams(q=_ext.ptr(qkv), k=_ext.ptr(qkv[:, nq:]), v=_ext.ptr(qkv[:, nq + nk:]), cos=_ext.ptr(cos),
+                            sin=_ext.ptr(sin), q_out=_ext.ptr(q_out), k_out=_ext.ptr(k_out), v_out=_ext.ptr(v_out),
+                            T=T, ld=W, H=H, Hkv=Hkv, D=D, dtype=_ext.dtype_code(dtype))
+        if T > 0:
+            _ext.call("dsalt_rope_gqa_fwd", p)
+        ctx.save_for_backward(x2, w, cos, sin)
+        ctx.dims = (H, Hkv, D)
+        ctx.dtypes = (x.dtype, w_q.dtype, w_k.dtype, w_v.dtype)
+        if H == Hkv:
+            return q_out, k_out, v_out
+        return q_out, k_out, v_out, qkv[:, nq + nk:].contiguous()
+
+    @staticmethod
+    def backward(ctx, dq_out, dk_out, dv_out, *d_xwv):
+        x2, w, cos, sin = ctx.saved_tensors
+        H, Hkv, D = ctx.dims
+        T, d = x2.shape
+        nq, nk = H * D, Hkv * D
+        W = nq + 2 * nk
+        dt, dev = x2.dtype, x2.device
+
+        def dense(g):
+            return torch.zeros(T, H, D, dtype=dt, device=dev) if g is None else g.contiguous().to(dt)
+        dq_out, dk_out, dv_out = dense(dq_out), dense(dk_out), dense(dv_out)
+        dqkv = torch.empty(T, W, dtype=dt, device=dev)
+        p = _ext.RopeParams(cos=_ext.ptr(cos), sin=_ext.ptr(sin), dq_out=_ext.ptr(dq_out), dk_out=_ext.ptr(dk_out),
+                            dv_out=_ext.ptr(dv_out), dq=_ext.ptr(dqkv), dk=_ext.ptr(dqkv[:, nq:]),
+                            dv=_ext.ptr(dqkv[:, nq + nk:]), T=T, ld=W, H=H, Hkv=Hkv, D=D,
+                            dtype=_ext.dtype_code(dt))
+        if T > 0:
+            _ext.call("dsalt_rope_gqa_bwd", p)
+        if d_xwv and d_xwv[0] is not None:
+            dqkv[:, nq + nk:] += d_xwv[0].to(dt)
+        x_dt, wq_dt, wk_dt, wv_dt = ctx.dtypes
+        dx = torch.mm(dqkv, w).to(x_dt) if ctx.needs_input_grad[0] else None
+        dw_q = dw_k = dw_v = None
+        if any(ctx.needs_input_grad[1:4]):
+            dw = torch.mm(dqkv.t(), x2, out_dtype=torch.float32)
+            dw_q, dw_k, dw_v = dw[:nq].to(wq_dt), dw[nq:nq + nk].to(wk_dt), dw[nq + nk:].to(wv_dt)
+        return dx, dw_q, dw_k, dw_v, None, None, None, None, None, None
+
+
+def qkv_rope(x, w_q, w_k, w_v, cos, sin, H: int, Hkv: int, D: int, dtype: torch.dtype):
+    """``(q_rot, k_rot, v, xwv)``: the bias-free q/k/v projections of ``x`` [T, d] in
+    ``dtype`` with RoPE and the GQA expansion fused (see ``QkvRopeFunction``);
+    ``xwv`` [T, Hkv·D] is the unexpanded value projection (a view of ``v`` without GQA)."""
+    out = QkvRopeFunction.apply(x, w_q, w_k, w_v, cos, sin, H, Hkv, D, dtype)
+    if H == Hkv:
+        q, k, v = out
+        return q, k, v, v.view(x.shape[0], Hkv * D)
+    return out

@@ -29,7 +29,8 @@ import warnings
 import torch
 import torch.nn as nn
 
-from ..kernels.rope_gqa import rope_gqa
+from ..kernels import _ext
+from ..kernels.rope_gqa import qkv_rope, rope_gqa
 from ..kernels.window_utils import build_rope_cache
 from ..kernels.landmark_tokens_ker import hybrid_scores_per_head
 from ..kernels.selectors import select_topk, _compute_landmark_indices
@@ -180,6 +181,24 @@ class DSALTAttention(nn.Module):
         out, aux = self._packed(x.reshape(B * T, self.d_model), cu, B * T, device, None, cu_list)
         return out.view(B, T, self.d_model), aux
 
+    def _project_qkv(self, x, total_len, cos, sin):
+        """``(q, k, v, xwv)``: the projections with RoPE on q and k and k, v expanded to
+        the query heads (reference apply_rotary_emb + _repeat_kv, bitwise equal at equal
+        projections), and the value projection x·W_Vᵀ for the landmark scorer (v carries
+        no RoPE), or None with a v bias.  Bias-free in 16-bit compute on CUDA the three
+        projections run as one GEMM feeding the prologue kernel (``qkv_rope``)."""
+        wq, wk, wv = self.q_proj.weight, self.k_proj.weight, self.v_proj.weight
+        no_bias = self.q_proj.bias is None and self.k_proj.bias is None and self.v_proj.bias is None
+        dt = _ext.half_compute_dtype(x, wq, wk, wv) if no_bias else None
+        if dt is not None:
+            return qkv_rope(x, wq, wk, wv, cos, sin, self.n_heads, self.n_kv_heads, self.head_dim, dt)
+        q = self.q_proj(x).view(total_len, self.n_heads, self.head_dim)
+        k = self.k_proj(x).view(total_len, self.n_kv_heads, self.head_dim)
+        v = self.v_proj(x).view(total_len, self.n_kv_heads, self.head_dim)
+        xwv = v.view(total_len, self.kv_dim) if self.v_proj.bias is None else None
+        q, k, v = rope_gqa(q, k, v, cos.to(q.dtype), sin.to(q.dtype))
+        return q, k, v, xwv
+
     def _packed_train_triton(self, q, k, v, x, cu_seqlens, total_len, device, cu_list=None, xwv=None):
         """Training attention on the CUDA op, carrying the window and α gradients (reference :440-455)."""
         w_cont, lmk_pos, lmk_logw = self._train_selectors(x, cu_seqlens, total_len, device, cu_list, xwv)
@@ -216,12 +235,6 @@ class DSALTAttention(nn.Module):
         return w_cont, lmk_pos, lmk_logw
 
     def _packed(self, x, cu_seqlens, total_len, device, rope_cs=None, cu_list=None):
-        q = self.q_proj(x).view(total_len, self.n_heads, self.head_dim)
-        k = self.k_proj(x).view(total_len, self.n_kv_heads, self.head_dim)
-        v = self.v_proj(x).view(total_len, self.n_kv_heads, self.head_dim)
-        # without a bias the value projection is x·W_Vᵀ, the landmark scorer's GEMM:
-        # hand it over instead of recomputing it (v carries no RoPE)
-        xwv = v.view(total_len, self.kv_dim) if self.v_proj.bias is None else None
         if rope_cs is None:
             num_seqs = cu_seqlens.shape[0] - 1
             cu = cu_seqlens.to(device).long()
@@ -232,11 +245,7 @@ class DSALTAttention(nn.Module):
             sin = self.rope_sin.to(device)[pos_ids]
         else:
             cos, sin = rope_cs
-        cos = cos.to(q.dtype)
-        sin = sin.to(q.dtype)
-        # RoPE on q and k and the GQA expansion of k and v, fused (reference
-        # apply_rotary_emb + _repeat_kv, bitwise equal)
-        q, k, v = rope_gqa(q, k, v, cos, sin)
+        q, k, v, xwv = self._project_qkv(x, total_len, cos, sin)
         aux = self._aux_zero(x.device, x.dtype)
 
         if self.training:

@@ -313,6 +313,10 @@ typedef struct DsaltRopeParams {
   void* dk;                   /* [T, Hkv, D]                               */
   void* dv;                   /* [T, Hkv, D], or NULL                      */
   int64_t T;
+  int64_t ld;                 /* 0: q, k, v, dq, dk, dv dense as above; else
+                                 the row stride (elements) of all six, column
+                                 blocks of one [T, ld] buffer (a multiple of 8,
+                                 fp32: 4, and at least H·D)                */
   int32_t H, Hkv, D;          /* D a multiple of 16 up to 256; H a multiple of Hkv */
   int32_t dtype;
 } DsaltRopeParams;

@@ -87,3 +87,42 @@ def test_module_uses_fused_prologue_with_gqa():
     (out.float().square().mean() + aux.float()).backward()
     assert torch.isfinite(out).all() and torch.isfinite(x.grad).all()
     assert m.k_proj.weight.grad is not None and torch.isfinite(m.k_proj.weight.grad).all()
+
+
+@pytest.mark.parametrize("heads", [(8, 8), (8, 2)])
+def test_qkv_rope_matches_separate_projections(heads):
+    """The stacked q|k|v GEMM feeding the strided prologue against the three
+    projections + ``rope_gqa`` under bf16 autocast: outputs, the value projection
+    for the scorer, and the gradients of x and the three weights."""
+    from dsalt.kernels.rope_gqa import qkv_rope, rope_gqa
+    from dsalt.kernels.window_utils import build_rope_cache
+    H, Hkv = heads
+    D, d, T = 64, 256, 300
+    torch.manual_seed(H + Hkv)
+    lin = [torch.nn.Linear(d, n * D, bias=False).cuda() for n in (H, Hkv, Hkv)]
+    x = torch.randn(T, d, device="cuda")
+    cos, sin = build_rope_cache(512, D, torch.device("cuda"))
+    pos = torch.randint(0, 512, (T,), device="cuda")
+    cos, sin = cos[pos], sin[pos]
+    grads = [torch.randn(T, H, D, device="cuda").to(torch.bfloat16) for _ in range(3)]
+    g_xwv = torch.randn(T, Hkv * D, device="cuda").to(torch.bfloat16)
+    res = []
+    for fused in (True, False):
+        xa = x.clone().requires_grad_(True)
+        for m in lin:
+            m.weight.grad = None
+        with torch.autocast("cuda", dtype=torch.bfloat16):
+            if fused:
+                q, k, v, xwv = qkv_rope(xa, *(m.weight for m in lin), cos, sin, H, Hkv, D, torch.bfloat16)
+            else:
+                q0, k0, v0 = (m(xa).view(T, -1, D) for m in lin)
+                xwv = v0.view(T, Hkv * D)
+                q, k, v = rope_gqa(q0, k0, v0, cos.to(torch.bfloat16), sin.to(torch.bfloat16))
+        torch.autograd.backward([q, k, v, xwv], grads + [g_xwv])
+        res.append(([t.detach().float() for t in (q, k, v, xwv)], [xa.grad] + [m.weight.grad for m in lin]))
+    (fa, ga), (fb, gb) = res
+    for a, b in zip(fa, fb):
+        torch.testing.assert_close(a, b, rtol=1e-2, atol=1e-2)
+    for a, b in zip(ga, gb):
+        assert a.dtype == b.dtype
+        torch.testing.assert_close(a, b, rtol=2e-2, atol=1e-2 * b.abs().max().item())

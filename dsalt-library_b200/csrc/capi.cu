@@ -146,7 +146,8 @@ int dsalt_build_schedule(const DsaltScheduleParams* p, void* stream) {
 }
 
 int dsalt_gather_landmarks(const DsaltGatherParams* p, void* stream) {
-  if (!p || p->H <= 0 || p->S < 0 || p->k_lmk < 0 || p->kp < p->k_lmk || p->k_lmk > 1024) return DSALT_ERR_ARG;
+  if (!p || p->H <= 0 || p->S < 0 || p->k_lmk < 0 || p->kp < p->k_lmk || p->k_lmk > 1024 || p->kp > 2048)
+    return DSALT_ERR_ARG;
   if (p->dtype != DSALT_F16 && p->dtype != DSALT_BF16 && p->dtype != DSALT_F32) return DSALT_ERR_DTYPE;
   if ((p->D * (p->dtype == DSALT_F32 ? 4 : 2)) % 16 != 0) return DSALT_ERR_HEAD_DIM;
   if (p->kp == 0 || p->S == 0) return DSALT_OK;

@@ -64,16 +64,28 @@ __global__ void __launch_bounds__(1024) build_block_map_kernel(DsaltSchedulePara
   if (tid == 0) *p.num_blocks = min(carry, p.max_blocks);
 }
 
-// Per token: its sequence id and the running per-sequence max band length.
+// Per token: its sequence id and the running per-sequence max band length.  A
+// warp whose 32 tokens lie in one sequence (the common case) reduces its maximum
+// first and issues one atomic; a warp across a boundary issues one per token.
 __global__ void seq_meta_kernel(DsaltScheduleParams p) {
   const int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-  if (t >= p.T) return;
-  const int s = find_seq(p.cu_seqlens, p.S, t);
-  if (p.seq_id) p.seq_id[t] = s;
-  const int i = (int)(t - p.cu_seqlens[s]);
-  const RowWindow rw = row_window(p.w[t], i, p.semantics, 0.0f);
-  const int W = min(rw.W, i);
-  if (W > 0) atomicMax(p.seq_wmax + s, W);
+  const bool valid = t < p.T;
+  int s = -1, W = 0;
+  if (valid) {
+    s = find_seq(p.cu_seqlens, p.S, t);
+    if (p.seq_id) p.seq_id[t] = s;
+    const int i = (int)(t - p.cu_seqlens[s]);
+    const RowWindow rw = row_window(p.w[t], i, p.semantics, 0.0f);
+    W = max(min(rw.W, i), 0);
+  }
+  if (!p.seq_wmax) return;  // uniform over the grid
+  const int s0 = __shfl_sync(0xffffffffu, s, 0);
+  if (__all_sync(0xffffffffu, s == s0)) {
+    const int m = __reduce_max_sync(0xffffffffu, W);
+    if ((threadIdx.x & 31) == 0 && s0 >= 0 && m > 0) atomicMax(p.seq_wmax + s0, m);
+  } else if (valid && W > 0) {
+    atomicMax(p.seq_wmax + s, W);
+  }
 }
 
 cudaError_t launch_schedule(const DsaltScheduleParams& p, cudaStream_t st) {
@@ -88,12 +100,16 @@ cudaError_t launch_schedule(const DsaltScheduleParams& p, cudaStream_t st) {
 }
 
 // ------------------------------------------------------------------ gather
-// One CTA per (head, sequence).  k <= 1024.
+// gridDim.x = H·S CTAs groups, one per (head, sequence); gridDim.y CTAs share
+// the group's row copies.  Each CTA ranks the k slots itself (k <= 1024, in
+// shared memory); the y = 0 CTA writes the sorted metadata.
 template <typename T>
 __global__ void __launch_bounds__(256) gather_landmarks_kernel(DsaltGatherParams p) {
-  extern __shared__ int64_t sm_keys[];  // [k] sort keys
+  extern __shared__ int64_t sm_keys[];  // [k] sort keys, then [kp] sorted positions (int32)
+  int32_t* spos = reinterpret_cast<int32_t*>(sm_keys + p.k_lmk);
   const int h = blockIdx.x / p.S;
   const int s = blockIdx.x % p.S;
+  const bool meta = blockIdx.y == 0;
   const int64_t s0 = p.cu_seqlens[s];
   const int L = (int)(p.cu_seqlens[s + 1] - s0);
   const int64_t in_base = ((int64_t)h * p.S + s) * p.k_lmk;
@@ -102,7 +118,7 @@ __global__ void __launch_bounds__(256) gather_landmarks_kernel(DsaltGatherParams
   for (int c = threadIdx.x; c < p.k_lmk; c += blockDim.x) {
     const int64_t pos = p.lmk_pos[in_base + c];
     const bool valid = pos >= 0 && pos < L;
-    if (pos >= L) flag_status(p.status, DSALT_DEV_BAD_INDEX);
+    if (meta && pos >= L) flag_status(p.status, DSALT_DEV_BAD_INDEX);
     sm_keys[c] = valid ? pos : (int64_t)1 << 40;
   }
   __syncthreads();
@@ -115,6 +131,8 @@ __global__ void __launch_bounds__(256) gather_landmarks_kernel(DsaltGatherParams
       rank += (k2 < key) || (k2 == key && c2 < c);
     }
     const bool valid = key < ((int64_t)1 << 40);
+    spos[rank] = valid ? (int32_t)key : -1;
+    if (!meta) continue;
     p.pos_sorted[out_base + rank] = valid ? (int32_t)key : -1;
     p.w_sorted[out_base + rank] = p.lmk_w[in_base + c];
     p.perm[out_base + rank] = c;
@@ -129,22 +147,27 @@ __global__ void __launch_bounds__(256) gather_landmarks_kernel(DsaltGatherParams
     }
   }
   for (int c = p.k_lmk + threadIdx.x; c < p.kp; c += blockDim.x) {
+    spos[c] = -1;
+    if (!meta) continue;
     p.pos_sorted[out_base + c] = -1;
     p.w_sorted[out_base + c] = 0.f;
     p.perm[out_base + c] = -1;
   }
   __syncthreads();
-  // gather rows (16-byte vectors): sorted slot r copies token pos_sorted[r]
+  // gather rows (16-byte vectors): sorted slot r copies token spos[r]; this CTA
+  // takes rows [r0, r1) of the group
   const int vec = 16 / (int)sizeof(T);
   const int nvec = p.D / vec;
+  const int per = (p.kp + gridDim.y - 1) / gridDim.y;
+  const int r0 = blockIdx.y * per, r1 = min(p.kp, r0 + per);
   const int64_t HD = (int64_t)p.H * p.D;
   const uint4* ksrc = reinterpret_cast<const uint4*>(p.k);
   const uint4* vsrc = reinterpret_cast<const uint4*>(p.v);
   uint4* kdst = reinterpret_cast<uint4*>(p.lmk_k);
   uint4* vdst = reinterpret_cast<uint4*>(p.lmk_v);
-  for (int e = threadIdx.x; e < p.kp * nvec; e += blockDim.x) {
+  for (int e = r0 * nvec + threadIdx.x; e < r1 * nvec; e += blockDim.x) {
     const int r = e / nvec, c = e % nvec;
-    const int pos = p.pos_sorted[out_base + r];
+    const int pos = spos[r];
     uint4 kv = make_uint4(0, 0, 0, 0), vv = make_uint4(0, 0, 0, 0);
     if (pos >= 0) {
       const int64_t src = ((s0 + pos) * HD + (int64_t)h * p.D) / vec + c;
@@ -159,11 +182,15 @@ __global__ void __launch_bounds__(256) gather_landmarks_kernel(DsaltGatherParams
 
 cudaError_t launch_gather(const DsaltGatherParams& p, cudaStream_t st) {
   if (p.H * p.S == 0) return cudaSuccess;
-  const size_t smem = sizeof(int64_t) * (size_t)max(p.k_lmk, 1);
+  const size_t smem = sizeof(int64_t) * (size_t)max(p.k_lmk, 1) + sizeof(int32_t) * (size_t)max(p.kp, 1);
+  // about two CTAs per SM in all, at least 8 rows per CTA
+  const int groups = p.H * p.S;
+  const int ny = max(1, min((p.kp + 7) / 8, (2 * 148 + groups - 1) / groups));
+  const dim3 grid((unsigned)groups, (unsigned)ny);
   switch (p.dtype) {
-    case DSALT_F16: gather_landmarks_kernel<__half><<<p.H * p.S, 256, smem, st>>>(p); break;
-    case DSALT_BF16: gather_landmarks_kernel<__nv_bfloat16><<<p.H * p.S, 256, smem, st>>>(p); break;
-    case DSALT_F32: gather_landmarks_kernel<float><<<p.H * p.S, 256, smem, st>>>(p); break;
+    case DSALT_F16: gather_landmarks_kernel<__half><<<grid, 256, smem, st>>>(p); break;
+    case DSALT_BF16: gather_landmarks_kernel<__nv_bfloat16><<<grid, 256, smem, st>>>(p); break;
+    case DSALT_F32: gather_landmarks_kernel<float><<<grid, 256, smem, st>>>(p); break;
     default: return cudaErrorInvalidValue;
   }
   return cudaGetLastError();

@@ -106,7 +106,8 @@ DSALT_API int dsalt_build_schedule(const DsaltScheduleParams* p, void* stream);
  * [H,S,kp,D] (zeros for invalid), copies the log-weight / bias in sorted
  * order, records the caller's slot of every sorted entry (perm) and writes
  * the reverse map lmk_slot[T,H] (sorted slot of the first landmark at that
- * token, else -1; the caller pre-fills it with -1).                         */
+ * token, else -1; the caller pre-fills it with -1).  k_lmk <= 1024,
+ * kp <= 2048.                                                               */
 typedef struct DsaltGatherParams {
   const void* k;              /* [T,H,D] dtype */
   const void* v;              /* [T,H,D] dtype */

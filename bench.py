@@ -334,7 +334,13 @@ def run_config4(args):
     ddp = model
     if world > 1:
         from torch.nn.parallel import DistributedDataParallel as DDP
-        ddp = DDP(model, device_ids=[local], bucket_cap_mb=100, gradient_as_bucket_view=True, static_graph=True)
+        # the model's only buffers are the constant RoPE tables: no per-step broadcast
+        ddp = DDP(model, device_ids=[local], bucket_cap_mb=args.bucket_mb, gradient_as_bucket_view=True,
+                  static_graph=True, broadcast_buffers=False)
+        if args.ddp_bf16_grads:
+            # all-reduce the gradient buckets in bf16 (half the NVLink bytes; rounds the summed gradients)
+            from torch.distributed.algorithms.ddp_comm_hooks.default_hooks import bf16_compress_hook
+            ddp.register_comm_hook(None, bf16_compress_hook)
     opt = torch.optim.AdamW(model.parameters(), lr=3e-4, betas=(0.9, 0.95), weight_decay=0.1, fused=True)
     T = CONFIG4_BATCH * CONFIG4_SEQ
     g = torch.Generator().manual_seed(1000 + rank)
@@ -394,7 +400,8 @@ def run_config4(args):
                                        "AdamW, chunked cross-entropy",
                            "global_batch": CONFIG4_BATCH * world, "seq_len": CONFIG4_SEQ, "tokens_per_gpu": T,
                            "parameters": n_params,
-                           "parallelism": f"dp{world} (DDP, NCCL all-reduce of gradients)" if world > 1 else "dp1",
+                           "parallelism": (f"dp{world} (DDP, NCCL all-reduce of gradients, {args.bucket_mb} MB buckets"
+                                           + (", bf16 hook)" if args.ddp_bf16_grads else ")")) if world > 1 else "dp1",
                            "l2": "activations and weights far larger than L2, no flush"},
                 "e2e": {"value": tokens / (ms_e2e / 1e3), "unit": "tokens/s",
                         "h2d_bytes_per_step": int((T + 1) * 8), "d2h_bytes_per_step": 4},
@@ -416,6 +423,8 @@ def main():
     ap.add_argument("--workload", default="config2", choices=list(WORKLOADS) + ["config4"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--bucket-mb", type=int, default=100, help="config4: DDP bucket size (MB)")
+    ap.add_argument("--ddp-bf16-grads", action="store_true", help="config4: bf16 gradient all-reduce hook")
     args = ap.parse_args()
     if args.workload == "config4":
         if args.impl == "reference":

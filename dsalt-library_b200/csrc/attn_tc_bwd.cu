@@ -25,6 +25,7 @@
 //
 // All waits are bounded (sm100::mbar_wait); see attn_tc.cu.
 #include <mutex>
+#include <type_traits>
 
 #include "common.cuh"
 #include "sm100.cuh"
@@ -380,18 +381,31 @@ __global__ void __launch_bounds__(kThreadsDQ, 1) tc_bwd_dq_kernel(const __grid_c
           tmem_ld16(tdP + lane_addr + st * BN + c0, dpv);
           tmem_wait_ld();
           const float* lw2 = sm.lmk_lw2 + BN * t + c0;
-          const uint32_t vmask = all_in ? 0xffffffffu : range_mask32(vlo, vhi);
+          // one straight-line body per (landmark tile, column mask) case: the tile
+          // kind and a warp-wide all-valid chunk are uniform, so the common case
+          // carries no per-element bias load or mask test
+          auto body = [&](auto kLmk, auto kMasked) {
+            constexpr bool kL = decltype(kLmk)::value, kM = decltype(kMasked)::value;
+            const uint32_t vmask = kM ? range_mask32(vlo, vhi) : 0xffffffffu;
 #pragma unroll
-          for (int c = 0; c < 16; c += 2) {
-            float d2[2];
+            for (int c = 0; c < 16; c += 2) {
+              float d2[2];
 #pragma unroll
-            for (int e = 0; e < 2; ++e) {
-              const float bias = lmk ? lw2[c + e] + nlse2 : nlse2;
-              const float pr = fast_exp2(fmaf(sv[c + e], sl2, bias));
-              const float dsv = pr * (dpv[c + e] - delta);
-              d2[e] = (vmask >> (c + e)) & 1u ? dsv : 0.f;
+              for (int e = 0; e < 2; ++e) {
+                const float bias = kL ? lw2[c + e] + nlse2 : nlse2;
+                const float pr = fast_exp2(fmaf(sv[c + e], sl2, bias));
+                const float dsv = pr * (dpv[c + e] - delta);
+                d2[e] = kM ? ((vmask >> (c + e)) & 1u ? dsv : 0.f) : dsv;
+              }
+              pk[c / 2] = pack2(d2[0], d2[1], kBF16);
             }
-            pk[c / 2] = pack2(d2[0], d2[1], kBF16);
+          };
+          using kT = std::true_type;
+          using kF = std::false_type;
+          if (lmk) {
+            if (all_in) body(kT{}, kF{}); else body(kT{}, kT{});
+          } else {
+            if (all_in) body(kF{}, kF{}); else body(kF{}, kT{});
           }
         }
 #pragma unroll
@@ -965,30 +979,35 @@ __global__ void __launch_bounds__(kThreadsKV, 1) tc_bwd_dkdv_kernel(const __grid
           tmem_wait_ld();
           tc_fence_before();
           mbar_arrive(bar[SD_EMPTY + st]);
+          // the all-valid case (warp-uniform) runs without the per-element test
+          auto body = [&](auto kAllIn) {
+            constexpr bool kIn = decltype(kAllIn)::value;
 #pragma unroll
-          for (int c = 0; c < 16; c += 2) {
-            float pr2[2], ds2[2];
+            for (int c = 0; c < 16; c += 2) {
+              float pr2[2], ds2[2];
 #pragma unroll
-            for (int e = 0; e < 2; ++e) {
-              const QRec& rq = rec[c + e];
-              const float4 r0 = *reinterpret_cast<const float4*>(&rq.nlse2);  // nlse2, delta, lo, qi
-              bool valid;
-              float pr;
-              if (LMK) {
-                pr = fast_exp2(fmaf(sv[c + e], sl2, lw2 + r0.x));
-                valid = all_in || (key_ok && j <= __float_as_int(r0.w) && jfl < rq.wlo);
-              } else {
-                pr = fast_exp2(fmaf(sv[c + e], sl2, r0.x));
-                valid = all_in || (j >= __float_as_int(r0.z) && j <= __float_as_int(r0.w));
+              for (int e = 0; e < 2; ++e) {
+                const QRec& rq = rec[c + e];
+                const float4 r0 = *reinterpret_cast<const float4*>(&rq.nlse2);  // nlse2, delta, lo, qi
+                bool valid;
+                float pr;
+                if (LMK) {
+                  pr = fast_exp2(fmaf(sv[c + e], sl2, lw2 + r0.x));
+                  valid = kIn || (key_ok && j <= __float_as_int(r0.w) && jfl < rq.wlo);
+                } else {
+                  pr = fast_exp2(fmaf(sv[c + e], sl2, r0.x));
+                  valid = kIn || (j >= __float_as_int(r0.z) && j <= __float_as_int(r0.w));
+                }
+                const float dsv = pr * (dpv[c + e] - r0.y);
+                pr2[e] = valid ? pr : 0.f;
+                ds2[e] = valid ? dsv : 0.f;
+                if (LMK) dlw += ds2[e];
               }
-              const float dsv = pr * (dpv[c + e] - r0.y);
-              pr2[e] = valid ? pr : 0.f;
-              ds2[e] = valid ? dsv : 0.f;
-              if (LMK) dlw += ds2[e];
+              pk_p[c / 2] = pack2(pr2[0], pr2[1], kBF16);
+              pk_d[c / 2] = pack2(ds2[0], ds2[1], kBF16);
             }
-            pk_p[c / 2] = pack2(pr2[0], pr2[1], kBF16);
-            pk_d[c / 2] = pack2(ds2[0], ds2[1], kBF16);
-          }
+          };
+          if (all_in) body(std::true_type{}); else body(std::false_type{});
         }
         // the single Pᵀ / dSᵀ buffer is free once the previous tile's dV / dK MMAs completed
         if (g >= 1) {

@@ -988,7 +988,14 @@ __global__ void __launch_bounds__(kThreadsKV, 1) tc_bwd_dkdv_kernel(const __grid
 #pragma unroll
               for (int e = 0; e < 2; ++e) {
                 const QRec& rq = rec[c + e];
-                const float4 r0 = *reinterpret_cast<const float4*>(&rq.nlse2);  // nlse2, delta, lo, qi
+                // nlse2, delta (and lo, qi only where a column can be invalid)
+                float4 r0;
+                if (kIn) {
+                  const float2 h2 = *reinterpret_cast<const float2*>(&rq.nlse2);
+                  r0 = make_float4(h2.x, h2.y, 0.f, 0.f);
+                } else {
+                  r0 = *reinterpret_cast<const float4*>(&rq.nlse2);
+                }
                 bool valid;
                 float pr;
                 if (LMK) {

@@ -51,8 +51,8 @@ KERNELS_PER_CALL = {"dsalt_build_schedule": 2, "dsalt_gather_landmarks": 1, "dsa
 # DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) per call of each entry point,
 # summed over its kernels, from one ncu capture of a config-2 step; the capture and the
 # command are in profiles/launches_traffic_step_config2.txt
-NCU_TRAFFIC_BYTES = {"config2": {"dsalt_attn_fwd": 361824768, "dsalt_attn_bwd_preprocess": 240091136,
-                                 "dsalt_attn_bwd_dkdv": 560660096, "dsalt_attn_bwd_dq": 339012864}}
+NCU_TRAFFIC_BYTES = {"config2": {"dsalt_attn_fwd": 361400000, "dsalt_attn_bwd_preprocess": 240800000,
+                                 "dsalt_attn_bwd_dkdv": 559300000, "dsalt_attn_bwd_dq": 339000000}}
 CLOCK_REASONS = {0x1: "gpu_idle", 0x2: "applications_clocks_setting", 0x4: "sw_power_cap",
                  0x8: "hw_slowdown", 0x10: "sync_boost", 0x20: "sw_thermal_slowdown",
                  0x40: "hw_thermal_slowdown", 0x80: "hw_power_brake_slowdown", 0x100: "display_clock_setting"}

@@ -414,13 +414,217 @@ def run_config4(args):
 
 
 # --------------------------------------------------------------------- main
+CONFIG5 = dict(N=32768, H=32, D=128, k=256, n_min=128, n_max=2048)
+METRIC5 = "attended-pair TFLOP/s inference fwd (N=32768, D=128, H=32)"
+
+
+def config5_inputs(heads, seed, device):
+    """Config-5 inputs for ``heads`` of the 32 heads: q, k, v bf16 N(0,1), the per-token
+    integer windows floor(128 + sigmoid(g)·1920) (one draw for all heads: the window
+    gate is head-independent), hybrid scores N(0,1) and their top-256 landmarks."""
+    import torch
+    from dsalt.kernels.selectors import select_topk
+    c = CONFIG5
+    N, D, k = c["N"], c["D"], c["k"]
+    gw = torch.Generator(device=device).manual_seed(5)
+    w = (c["n_min"] + torch.sigmoid(torch.randn(N, generator=gw, device=device)) * (c["n_max"] - c["n_min"])).floor()
+    g = torch.Generator(device=device).manual_seed(500 + seed)
+    q, kk, v = (torch.randn(N, heads, D, generator=g, device=device).to(torch.bfloat16) for _ in range(3))
+    scores = torch.randn(N, heads, generator=g, device=device)
+    cu = torch.tensor([0, N], dtype=torch.int32, device=device)
+    lmk = select_topk(scores, w.clamp(min=1), cu, k, N)
+    bias = torch.zeros(heads, 1, k, device=device)
+    return dict(q=q, k=kk, v=v, w=w, cu=cu, lmk=lmk, bias=bias, N=N, D=D)
+
+
+def config5_cpu(rows_n=512, seed=0):
+    """The oracle's row-wise inference forward on a bounded sample of (token, head) rows of
+    one config-5 head (inputs drawn on the host with the same distributions)."""
+    import numpy as np
+    import torch
+    from oracle import dsalt_oracle as O
+    c = CONFIG5
+    N, D, k = c["N"], c["D"], c["k"]
+    g = torch.Generator().manual_seed(700 + seed)
+    q, kk, v = (torch.randn(N, 1, D, generator=g).to(torch.bfloat16).float().numpy() for _ in range(3))
+    w = (c["n_min"] + torch.sigmoid(torch.randn(N, generator=g)) * (c["n_max"] - c["n_min"])).floor().numpy()
+    scores = torch.randn(N, 1, generator=g).numpy()
+    cu = np.array([0, N])
+    pos = O.landmark_indices(scores, O.window_discrete(w), cu, k)
+    lw = np.zeros(pos.shape, dtype=np.float32)
+    rng = np.random.default_rng(seed)
+    rows = [(int(t), 0) for t in rng.integers(0, N, rows_n)]
+    O.attention_fwd_rows(q, kk, v, pos, lw, w, cu, rows[:8], semantics="infer", dtype=np.float32)  # warm-up
+    t0 = time.perf_counter()
+    O.attention_fwd_rows(q, kk, v, pos, lw, w, cu, rows, semantics="infer", dtype=np.float32)
+    secs = time.perf_counter() - t0
+    # attended pairs of the sampled rows: the window min(w, i + 1) plus the landmarks before it
+    p0 = pos[0, 0]
+    pairs = 0
+    for t, _ in rows:
+        wi = max(int(w[t]), 1)
+        pairs += min(wi, t + 1) + int(((p0 >= 0) & (p0 <= t) & (p0 < t - wi + 1)).sum())
+    return {"value": 4 * D * pairs / secs / 1e12, "unit": UNIT, "cores": os.cpu_count(), "kind": "port",
+            "sample": f"{rows_n} random (token, head) rows of one head, N=32768, D=128, numpy float32 row-wise "
+                      f"inference oracle, {secs:.1f} s"}
+
+
+def run_config5(args):
+    """long-context inference forward of the op (B=1, H=32, N=32,768, D=128,
+    bf16, n_min 128, n_max 2048, k_lmk 256) through dsalt_triton_attention; the 32 heads are
+    sharded over the ranks (32/N per GPU, no collective in the op: strong scaling).  value =
+    4·D·P over all heads (attended pairs, inference semantics) / max-over-ranks time."""
+    import torch
+    import torch.distributed as dist
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        if rank == 0:
+            vals = [config5_cpu(rows_n=256, seed=s) for s in range(max(args.steps, 1))]
+            val = statistics.mean(v["value"] for v in vals)
+            line = {"metric": METRIC5, "value": val, "unit": UNIT, "n_gpus": args.gpus, "steps": args.steps,
+                    "warmup": args.warmup, "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+                    "dtype": "f32", "data": "synthetic", "impl": "reference",
+                    "config": {"workload": "config5 (CPU oracle on sampled rows)"},
+                    "cpu_baseline": dict(vals[0], value=val),
+                    "e2e": {"value": val, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+            print(json.dumps(line), flush=True)
+        return
+    if CONFIG5["H"] % world:
+        raise SystemExit("config5 shards 32 heads: --gpus must divide 32")
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        import datetime
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    from dsalt.kernels import _ext
+    from dsalt.kernels.dsalt_triton_attn import dsalt_triton_attention
+    from dsalt.kernels.flops import attended_pairs
+    heads = CONFIG5["H"] // world
+    d = config5_inputs(heads, rank, dev)
+    pairs = attended_pairs(d["w"], d["lmk"], d["cu"], semantics="infer")
+
+    def step():
+        return dsalt_triton_attention(d["q"], d["k"], d["v"], d["lmk"], d["bias"], d["w"], d["cu"])
+    with torch.no_grad():
+        for _ in range(max(args.warmup, 3)):
+            step()
+        torch.cuda.synchronize()
+        barrier()
+        with ClockSampler(local) as clk:
+            _ext.RECORD = []
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            barrier()
+            torch.cuda.synchronize()
+            e0.record()
+            for _ in range(args.steps):
+                step()
+            e1.record()
+            torch.cuda.synchronize()
+            rec, _ext.RECORD = _ext.RECORD, None
+            barrier()
+        ms = e0.elapsed_time(e1)
+        launches = sum(KERNELS_PER_CALL.get(n, 1) for n, _, _ in rec)
+        fwd = [a.elapsed_time(b) for n, a, b in rec if n == "dsalt_attn_fwd"]
+        flops = 4.0 * d["D"] * pairs
+        t = torch.tensor([ms, flops], dtype=torch.float64, device=dev)
+        if world > 1:
+            tm, tf = t[:1].clone(), t[1:].clone()
+            dist.all_reduce(tm, op=dist.ReduceOp.MAX)
+            dist.all_reduce(tf, op=dist.ReduceOp.SUM)
+            ms_max, flops_all = float(tm.item()), float(tf.item())
+        else:
+            ms_max, flops_all = ms, flops
+        value = flops_all * args.steps / (ms_max / 1e3) / 1e12
+        # end to end: q, k, v and the selection inputs copied from pinned host memory and O
+        # (fp32) read back every step, copies on their own streams pipelined with the compute
+        names = ("q", "k", "v", "w", "lmk", "bias")
+        host = {kk: d[kk].cpu().pin_memory() for kk in names}
+        dbuf = [{kk: torch.empty_like(d[kk]) for kk in names} for _ in range(2)]
+        obuf = [torch.empty(d["q"].shape, dtype=torch.float32).pin_memory() for _ in range(2)]
+        h2d = sum(x.numel() * x.element_size() for x in host.values())
+        d2h = obuf[0].numel() * 4
+        main = torch.cuda.current_stream(dev)
+        cs, os_ = torch.cuda.Stream(device=dev), torch.cuda.Stream(device=dev)
+        ev_in, ev_used = [torch.cuda.Event() for _ in range(2)], [torch.cuda.Event() for _ in range(2)]
+
+        def run(nsteps):
+            cs.wait_stream(main)
+
+            def h2d_step(n):
+                if n >= 2:
+                    cs.wait_event(ev_used[n % 2])
+                with torch.cuda.stream(cs):
+                    for kk in names:
+                        dbuf[n % 2][kk].copy_(host[kk], non_blocking=True)
+                ev_in[n % 2].record(cs)
+            h2d_step(0)
+            for n in range(nsteps):
+                if n + 1 < nsteps:
+                    h2d_step(n + 1)
+                main.wait_event(ev_in[n % 2])
+                x = dbuf[n % 2]
+                o = dsalt_triton_attention(x["q"], x["k"], x["v"], x["lmk"], x["bias"], x["w"], d["cu"])
+                ev_used[n % 2].record(main)
+                os_.wait_stream(main)
+                with torch.cuda.stream(os_):
+                    o.record_stream(os_)
+                    obuf[n % 2].copy_(o, non_blocking=True)
+            main.wait_stream(os_)
+            main.wait_stream(cs)
+        run(2)
+        torch.cuda.synchronize()
+        barrier()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(main)
+        run(args.steps)
+        b.record(main)
+        torch.cuda.synchronize()
+        ems = torch.tensor([a.elapsed_time(b)], dtype=torch.float64, device=dev)
+        if world > 1:
+            dist.all_reduce(ems, op=dist.ReduceOp.MAX)
+    if rank == 0:
+        burst, sustained, hbm, src = peaks()
+        kt = statistics.mean(fwd) if fwd else None
+        roof = None
+        if kt:
+            ach = flops / (kt / 1e3) / 1e12
+            roof = {"bound": "tensor", "kernel": "dsalt_attn_fwd", "achieved": ach, "peak": burst, "unit": UNIT,
+                    "frac": ach / burst, "traffic": None,
+                    "peak_source": f"{src} bf16_tflops (burst: the forward is timed alone)"}
+        line = {"metric": METRIC5, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+                "warmup": max(args.warmup, 3), "ms_per_step": ms_max / args.steps, "higher_is_better": True,
+                "scaling": "strong", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+                "config": {"workload": "config5: B=1, N=32768, H=32, D=128, bf16, n_min 128, n_max 2048, "
+                                       "k_lmk 256, inference forward (integer windows, zero landmark bias)",
+                           "heads_per_gpu": heads, "parallelism": f"heads sharded {heads} per GPU, no collective",
+                           "l2": "inputs larger than L2 (q,k,v bf16 = 805 MB at 32 heads), no flush"},
+                "roofline": roof, "attended_pairs_per_gpu": pairs, "gpu_launches": launches,
+                "e2e": {"value": flops_all * args.steps / (float(ems.item()) / 1e3) / 1e12, "unit": UNIT,
+                        "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h),
+                        "note": "host<->device copies on their own streams, pipelined with the neighbouring steps"},
+                "clocks": clk.summary()}
+        if not args.no_cpu_baseline:
+            line["cpu_baseline"] = config5_cpu()
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        barrier()
+        dist.destroy_process_group()
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--workload", default="config2", choices=list(WORKLOADS) + ["config4"])
+    ap.add_argument("--workload", default="config2", choices=list(WORKLOADS) + ["config4", "config5"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--bucket-mb", type=int, default=100, help="config4: DDP bucket size (MB)")
@@ -434,6 +638,9 @@ def main():
                                   "the CPU reference arm"}), flush=True)
             return
         run_config4(args)
+        return
+    if args.workload == "config5":
+        run_config5(args)
         return
     wl = WORKLOADS[args.workload]
     if args.impl == "reference":

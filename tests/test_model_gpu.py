@@ -80,3 +80,37 @@ def test_model_bf16_autocast_train_step_runs():
         assert p.grad is not None and torch.isfinite(p.grad).all(), name
     assert model.layers[0].attn.alpha_w.grad.abs().sum() > 0
     assert model.layers[0].attn.win_gate.weight.grad.abs().sum() > 0
+
+
+@pytest.mark.parametrize("autocast", [False, True])
+def test_gradient_checkpointing_matches_plain_step(autocast):
+    """The checkpointed block path (reference's torch.utils.checkpoint form, residual adds
+    unfused) gives the loss and gradients of the plain path (fused residual adds)."""
+    from dsalt.model import DSALTLMHeadModel
+    torch.manual_seed(0)
+    model = DSALTLMHeadModel(vocab_size=300, d_model=256, n_layers=2, n_heads=4, n_min=8, n_max=64, k_lmk=8,
+                             max_seq_len=512).cuda().train()
+    # non-uniform norm weights: with the initial all-ones weights every normed token has
+    # the same ‖x‖ up to rounding, and the landmark score's 1/std(‖x‖) would turn
+    # rounding-order differences of the two paths into large gradient differences
+    with torch.no_grad():
+        for n, p in model.named_parameters():
+            if n.endswith("norm.weight"):
+                p.normal_(1.0, 0.3)
+    g = torch.Generator(device="cuda").manual_seed(1)
+    ids = torch.randint(0, 300, (2 * 256 + 1,), generator=g, device="cuda")
+    cu = torch.tensor([0, 256, 512], dtype=torch.int32, device="cuda")
+    res = []
+    for ckpt in (False, True):
+        model.zero_grad(set_to_none=True)
+        with torch.autocast("cuda", dtype=torch.bfloat16, enabled=autocast):
+            out = model(ids[:-1], cu_seqlens=cu, max_seqlen=256, labels=ids[1:], gradient_checkpointing=ckpt)
+        out["loss"].backward()
+        res.append((out["loss"].detach().float(), {n: p.grad.detach().float().clone()
+                                                   for n, p in model.named_parameters()}))
+    (la, ga), (lb, gb) = res
+    tol = 2e-2 if autocast else 1e-4
+    torch.testing.assert_close(la, lb, rtol=tol, atol=tol)
+    for n in ga:
+        torch.testing.assert_close(ga[n], gb[n], rtol=5e-2 if autocast else 1e-3,
+                                   atol=(5e-2 if autocast else 1e-4) * gb[n].abs().max().item() + 1e-8, msg=n)

@@ -27,6 +27,7 @@ class FusedChunkedCE(torch.autograd.Function):
         N, d = x.shape
         V = weight.shape[0]
         dev = x.device
+        chunk = max(int(chunk), 1)
         labels = labels.contiguous().long()
         x_c = x.to(dtype).contiguous()
         w_c = weight.to(dtype).contiguous()

@@ -38,7 +38,9 @@ def _bwd(xn, w32, rstd, dy, dres, need_dw):
     dx = torch.empty_like(xn)
     parts = torch.empty((T + _ext.RMSNORM_ROWS_PER_PART - 1) // _ext.RMSNORM_ROWS_PER_PART, d,
                         dtype=torch.float32, device=xn.device)
-    dw = torch.empty(d, dtype=torch.float32, device=xn.device) if need_dw else None
+    dw = None
+    if need_dw:  # zeros for an empty batch (the library then launches nothing)
+        dw = torch.empty(d, dtype=torch.float32, device=xn.device) if T > 0 else torch.zeros(d, device=xn.device)
     p = _ext.RmsNormParams(x=_ext.ptr(xn), w=_ext.ptr(w32), rstd=_ext.ptr(rstd), dy=_ext.ptr(dy2),
                            dres=_ext.ptr(dres2), dx=_ext.ptr(dx), dw_part=_ext.ptr(parts), dw=_ext.ptr(dw),
                            T=T, d=d, eps=0.0, dtype=_ext.dtype_code(xn.dtype))

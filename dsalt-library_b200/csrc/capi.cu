@@ -42,6 +42,7 @@ cudaError_t launch_scale_rows(const DsaltScaleRowsParams& p, cudaStream_t st);
 cudaError_t launch_xent(const DsaltXentParams& p, cudaStream_t st);
 cudaError_t launch_swiglu(const DsaltSwigluParams& p, bool bwd, cudaStream_t st);
 cudaError_t launch_win_gate_bwd(const DsaltWinGateBwdParams& p, cudaStream_t st);
+cudaError_t launch_hybrid_scores_bwd(const DsaltScoreBwdParams& p, cudaStream_t st);
 cudaError_t launch_hybrid_scores(const DsaltScoreParams& p, cudaStream_t st);
 cudaError_t launch_topk(const DsaltTopkParams& p, cudaStream_t st);
 cudaError_t noalloc_score_scratch(float** out);
@@ -133,6 +134,7 @@ int dsalt_b200_params_sizeof(int which) {
     case 9: return (int)sizeof(DsaltXentParams);
     case 10: return (int)sizeof(DsaltSwigluParams);
     case 11: return (int)sizeof(DsaltWinGateBwdParams);
+    case 12: return (int)sizeof(DsaltScoreBwdParams);
   }
   return -1;
 }
@@ -310,6 +312,13 @@ static int check_swiglu(const DsaltSwigluParams* p, bool bwd) {
     if (!aligned16(need[i])) return DSALT_ERR_ALIGN;
   }
   return DSALT_OK;
+}
+
+int dsalt_hybrid_scores_bwd(const DsaltScoreBwdParams* p, void* stream) {
+  if (!p || p->T < 0 || p->H <= 0 || p->n_kv <= 0 || p->H % p->n_kv != 0 || p->H > 4096) return DSALT_ERR_ARG;
+  if (!p->g_s || !p->alpha || !p->z_x || !p->z_v || !p->stats || !p->sums || !p->d_alpha) return DSALT_ERR_ARG;
+  if (p->T > 0 && (!p->norms || !p->coef_x || !p->coef_v)) return DSALT_ERR_ARG;
+  return status_of(launch_hybrid_scores_bwd(*p, (cudaStream_t)stream));
 }
 
 int dsalt_win_gate_bwd(const DsaltWinGateBwdParams* p, void* stream) {

@@ -253,6 +253,84 @@ cudaError_t launch_hybrid_scores(const DsaltScoreParams& p, cudaStream_t st) {
   return cudaGetLastError();
 }
 
+// --------------------------------------------------------- hybrid score backward
+// The gradient of s = α·z_v + (1−α)·z_x through the z-scores to the norms, as the
+// reference's autograd computes it: per token t and norm column c (c = 0: ‖x‖,
+// c = 1 + g: value head group g)
+//   dz[t,0] = Σ_h g[t,h]·(1 − α_h),  dz[t,1+g] = Σ_{h ∈ g} g[t,h]·α_h,
+//   dn[t,c] = (dz[t,c] − mean_t dz[·,c]) / sd_c
+//             − [sd_c unclamped]·z[t,c]·Σ_t dz[·,c]·z[·,c] / ((T − 1)·sd_c),
+//   coef[t,c] = dn[t,c] / ‖·‖[t,c] (1 where the norm is 0),
+// and d α_h = Σ_t g[t,h]·(z_v[t,h] − z_x[t]).  Pass 1: one CTA per column sum
+// (Σ dz, Σ dz·z per column, d α per head), fixed-order reductions; pass 2: one
+// thread per token writes its coefficients.
+__device__ __forceinline__ float score_dz(const DsaltScoreBwdParams& p, int64_t t, int c) {
+  const float* g = p.g_s + t * p.H;
+  const int rep = p.H / p.n_kv;
+  float acc = 0.f;
+  if (c == 0) {
+    for (int h = 0; h < p.H; ++h) acc = fmaf(g[h], 1.0f - p.alpha[h], acc);
+  } else {
+    const int h0 = (c - 1) * rep;
+    for (int r = 0; r < rep; ++r) acc = fmaf(g[h0 + r], p.alpha[h0 + r], acc);
+  }
+  return acc;
+}
+
+__device__ __forceinline__ float score_z(const DsaltScoreBwdParams& p, int64_t t, int c) {
+  return c == 0 ? p.z_x[t] : p.z_v[t * p.H + (c - 1) * (p.H / p.n_kv)];
+}
+
+__global__ void __launch_bounds__(1024) score_bwd_sums_kernel(DsaltScoreBwdParams p) {
+  __shared__ float red[32];
+  const int ncol = 1 + p.n_kv;
+  const int job = blockIdx.x;  // [0, ncol): Σ dz; [ncol, 2·ncol): Σ dz·z; then d α per head
+  float acc = 0.f;
+  for (int64_t t = threadIdx.x; t < p.T; t += blockDim.x) {
+    if (job < ncol) {
+      acc += score_dz(p, t, job);
+    } else if (job < 2 * ncol) {
+      const int c = job - ncol;
+      acc += score_dz(p, t, c) * score_z(p, t, c);
+    } else {
+      const int h = job - 2 * ncol;
+      acc += p.g_s[t * p.H + h] * (p.z_v[t * p.H + h] - p.z_x[t]);
+    }
+  }
+  acc = warp_sum(acc);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = acc;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float tot = 0.f;
+    for (int w = 0; w < (int)(blockDim.x >> 5); ++w) tot += red[w];
+    if (job < 2 * ncol) p.sums[job] = tot;
+    else p.d_alpha[job - 2 * ncol] = tot;
+  }
+}
+
+__global__ void __launch_bounds__(256) score_bwd_coef_kernel(DsaltScoreBwdParams p) {
+  const int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (t >= p.T) return;
+  const int ncol = 1 + p.n_kv;
+  const float inv_t = 1.0f / (float)p.T;
+  for (int c = 0; c < ncol; ++c) {
+    const float sd = p.stats[2 * c + 1];
+    const float dz = score_dz(p, t, c);
+    float dn = (dz - p.sums[c] * inv_t) / sd;
+    if (p.T > 1 && sd > 1e-6f) dn -= score_z(p, t, c) * p.sums[ncol + c] / ((float)(p.T - 1) * sd);
+    const float nrm = p.norms[(int64_t)c * p.T + t];
+    const float coef = dn / (nrm > 0.f ? nrm : 1.0f);
+    if (c == 0) p.coef_x[t] = coef;
+    else p.coef_v[t * p.n_kv + (c - 1)] = coef;
+  }
+}
+
+cudaError_t launch_hybrid_scores_bwd(const DsaltScoreBwdParams& p, cudaStream_t st) {
+  score_bwd_sums_kernel<<<(unsigned)(2 * (1 + p.n_kv) + p.H), 1024, 0, st>>>(p);
+  if (p.T > 0) score_bwd_coef_kernel<<<(unsigned)((p.T + 255) / 256), 256, 0, st>>>(p);
+  return cudaGetLastError();
+}
+
 // Backward of the norms (landmark_tokens_ker.py:47,52 through the z-scores):
 // out[t, g·width + j] = round(coef[t·groups + g] · x[t, g·width + j]), the fp32
 // product rounded once to the dtype, as (coef · x.float()).to(dtype) computes it.

@@ -110,6 +110,12 @@ class SwigluParams(ctypes.Structure):
                 ("du", _c_void_p), ("T", _i64), ("F", _i64), ("ld_in", _i64), ("ld_out", _i64), ("dtype", _i32)]
 
 
+class ScoreBwdParams(ctypes.Structure):
+    _fields_ = [("g_s", _c_void_p), ("alpha", _c_void_p), ("z_x", _c_void_p), ("z_v", _c_void_p),
+                ("norms", _c_void_p), ("stats", _c_void_p), ("sums", _c_void_p), ("d_alpha", _c_void_p),
+                ("coef_x", _c_void_p), ("coef_v", _c_void_p), ("T", _i64), ("H", _i32), ("n_kv", _i32)]
+
+
 class WinGateBwdParams(ctypes.Structure):
     _fields_ = [("x", _c_void_p), ("weight", _c_void_p), ("dl", _c_void_p), ("dx", _c_void_p),
                 ("dw_part", _c_void_p), ("T", _i64), ("d_model", _i32), ("dtype", _i32)]
@@ -119,7 +125,7 @@ RMSNORM_ROWS_PER_PART = 64  # DSALT_RMSNORM_ROWS_PER_PART
 WIN_GATE_ROWS_PER_PART = 32  # DSALT_WIN_GATE_ROWS_PER_PART
 
 _STRUCTS = [ScheduleParams, GatherParams, AttnParams, ScoreParams, TopkParams, WinGateParams, RopeParams,
-            RmsNormParams, ScaleRowsParams, XentParams, SwigluParams, WinGateBwdParams]
+            RmsNormParams, ScaleRowsParams, XentParams, SwigluParams, WinGateBwdParams, ScoreBwdParams]
 _ENTRY = {
     "dsalt_build_schedule": ScheduleParams,
     "dsalt_gather_landmarks": GatherParams,
@@ -138,6 +144,7 @@ _ENTRY = {
     "dsalt_scale_rows": ScaleRowsParams,
     "dsalt_xent_fwd_grad": XentParams,
     "dsalt_win_gate_bwd": WinGateBwdParams,
+    "dsalt_hybrid_scores_bwd": ScoreBwdParams,
     "dsalt_swiglu_fwd": SwigluParams,
     "dsalt_swiglu_bwd": SwigluParams,
 }

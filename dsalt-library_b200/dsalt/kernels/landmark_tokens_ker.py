@@ -61,32 +61,30 @@ class _HybridScore(torch.autograd.Function):
     @staticmethod
     def backward(ctx, g_s, g_zx, g_zv):
         x_c, xv, a, norms_cm, stats, z_x, z_v = ctx.saved_tensors
-        norms = norms_cm.t()  # [T, 1 + n_kv]
         H, n_kv, dh = ctx.shape
         T = x_c.shape[0]
-        rep = H // n_kv
-        g_s = g_s if g_s is not None else torch.zeros(T, H, device=x_c.device)
-        d_alpha = (g_s * (z_v - z_x[:, None])).sum(0)
+        dev = x_c.device
+        if T == 0:
+            return None, None, torch.zeros(H, dtype=ctx.alpha_dtype, device=dev), None, None, None
+        g = (g_s.float().contiguous() if g_s is not None else torch.zeros(T, H, device=dev))
+        # the chain through the z-scores in one CUDA pass pair (dsalt_hybrid_scores_bwd):
+        # d alpha and the per-row coefficients of d‖r‖/dr = r/‖r‖
+        d_alpha = torch.empty(H, dtype=torch.float32, device=dev)
+        coef_x = torch.empty(T, dtype=torch.float32, device=dev)
+        coef_v = torch.empty(T, n_kv, dtype=torch.float32, device=dev)
+        sums = torch.empty(2 * (1 + n_kv), dtype=torch.float32, device=dev)
+        p = _ext.ScoreBwdParams(g_s=_ext.ptr(g), alpha=_ext.ptr(a), z_x=_ext.ptr(z_x), z_v=_ext.ptr(z_v),
+                                norms=_ext.ptr(norms_cm), stats=_ext.ptr(stats), sums=_ext.ptr(sums),
+                                d_alpha=_ext.ptr(d_alpha), coef_x=_ext.ptr(coef_x), coef_v=_ext.ptr(coef_v),
+                                T=T, H=H, n_kv=n_kv)
+        _ext.call("dsalt_hybrid_scores_bwd", p)
         dx = dxwv = None
-        if ctx.needs_input_grad[0] or ctx.needs_input_grad[1]:
-            dzx = (g_s * (1.0 - a)[None, :]).sum(1)
-            dzv = (g_s * a[None, :]).view(T, n_kv, rep).sum(2)
-            zv_g = z_v.view(T, n_kv, rep)[:, :, 0]
-            dz = torch.cat([dzx[:, None], dzv], dim=1)              # [T, 1+n_kv]
-            z = torch.cat([z_x[:, None], zv_g], dim=1)
-            sd = stats.view(-1, 2)[:, 1][None, :]
-            raw_sd = norms.std(0, keepdim=True) if T > 1 else torch.zeros_like(sd)
-            dn = (dz - dz.mean(0, keepdim=True)) / sd
-            unclamped = (raw_sd > 1e-6).float()
-            if T > 1:
-                dn = dn - unclamped * z * (dz * z).sum(0, keepdim=True) / ((T - 1) * sd)
-            safe = torch.where(norms > 0, norms, torch.ones_like(norms))
-            # d‖r‖/dr = r/‖r‖: each row (group) of x / x·W_Vᵀ scaled by its coefficient,
-            # the fp32 product rounded once to the dtype (dsalt_scale_rows)
-            if ctx.needs_input_grad[0]:
-                dx = _scale_rows(x_c, (dn[:, :1] / safe[:, :1]).contiguous(), 1)
-            if ctx.needs_input_grad[1]:
-                dxwv = _scale_rows(xv, (dn[:, 1:] / safe[:, 1:]).contiguous(), n_kv)
+        # each row (group) of x / x·W_Vᵀ scaled by its coefficient, the fp32 product
+        # rounded once to the dtype (dsalt_scale_rows)
+        if ctx.needs_input_grad[0]:
+            dx = _scale_rows(x_c, coef_x, 1)
+        if ctx.needs_input_grad[1]:
+            dxwv = _scale_rows(xv, coef_v, n_kv)
         return dx, dxwv, d_alpha.to(ctx.alpha_dtype), None, None, None
 
 

@@ -223,6 +223,32 @@ DSALT_API int dsalt_hybrid_scores(const DsaltScoreParams* p, void* stream);
 #define DSALT_NOALLOC_SCORE_MAX_FLOATS (1 << 21)
 DSALT_API int dsalt_hybrid_scores_noalloc(const DsaltScoreParams* p, void* stream);
 
+/* Backward of dsalt_hybrid_scores through the z-scores to the norms, the
+ * gradient of landmark_tokens_ker.py:47-60 (unbiased std, clamp at 1e-6):
+ *   dz[t,0] = Σ_h g_s[t,h]·(1 − α_h), dz[t,1+g] = Σ_{h in group g} g_s[t,h]·α_h,
+ *   dn[t,c] = (dz[t,c] − mean_t dz[·,c]) / sd_c
+ *             − [sd_c > 1e-6]·z[t,c]·Σ_t dz[·,c]·z[·,c] / ((T − 1)·sd_c),
+ *   coef_x[t] = dn[t,0] / ‖x_t‖, coef_v[t,g] = dn[t,1+g] / ‖(x·W_Vᵀ)_t,g‖
+ *   (a zero norm divides by 1), d_alpha[h] = Σ_t g_s[t,h]·(z_v[t,h] − z_x[t]),
+ * with z, sd, the norms taken from the forward's outputs and scratch.  The
+ * input gradients are then coef · x and coef · x·W_Vᵀ row by row
+ * (dsalt_scale_rows).  Sums in a fixed order (deterministic).               */
+typedef struct DsaltScoreBwdParams {
+  const float* g_s;           /* [T,H] gradient of the scores */
+  const float* alpha;         /* [H] */
+  const float* z_x;           /* [T]   (forward output) */
+  const float* z_v;           /* [T,H] (forward output) */
+  const float* norms;         /* [(1+n_kv), T] column-major (forward scratch) */
+  const float* stats;         /* [2 + 2*n_kv] (forward scratch: mean, clamped std) */
+  float* sums;                /* scratch [2*(1+n_kv)] */
+  float* d_alpha;             /* [H] */
+  float* coef_x;              /* [T] */
+  float* coef_v;              /* [T, n_kv] */
+  int64_t T;
+  int32_t H, n_kv;
+} DsaltScoreBwdParams;
+DSALT_API int dsalt_hybrid_scores_bwd(const DsaltScoreBwdParams* p, void* stream);
+
 /* Replaces the exclusion + top-k of _compute_landmark_indices
  * (dsalt/kernels/selectors.py:103-134): per (head, sequence) the k largest
  * scores among tokens with seq_off >= w_sizes (own window), -1 when fewer are
@@ -402,7 +428,8 @@ DSALT_API int dsalt_b200_abi_version(void);
 DSALT_API const char* dsalt_b200_status_string(int status);
 /* sizeof of the parameter structs, for bindings to check their mirrors:
  * which = 0 schedule, 1 gather, 2 attn, 3 score, 4 topk, 5 win_gate, 6 rope,
- * 7 rmsnorm, 8 scale_rows, 9 xent, 10 swiglu, 11 win_gate_bwd              */
+ * 7 rmsnorm, 8 scale_rows, 9 xent, 10 swiglu, 11 win_gate_bwd,
+ * 12 score_bwd                                                              */
 DSALT_API int dsalt_b200_params_sizeof(int which);
 
 #ifdef __cplusplus

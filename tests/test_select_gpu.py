@@ -62,12 +62,14 @@ def test_hybrid_scores_match_reference(golden_selectors, case):
     torch.testing.assert_close(zv.cpu(), g["z_v"], rtol=1e-5, atol=1e-5)
 
 
-def test_hybrid_scores_alpha_and_x_gradients():
-    """The analytic backward matches autograd through the reference formula."""
+@pytest.mark.parametrize("shape", [(97, 32, 4, 2, 8), (4096, 256, 16, 16, 16), (2, 32, 4, 4, 8)])
+def test_hybrid_scores_alpha_and_x_gradients(shape):
+    """The analytic backward (dsalt_hybrid_scores_bwd + row scaling) matches autograd
+    through the reference formula: GQA, an MHA shape with many tokens, two tokens."""
     from dsalt.kernels.landmark_tokens_ker import hybrid_scores_per_head
     torch.manual_seed(0)
     dev = torch.device("cuda")
-    T, dm, H, n_kv, dh = 97, 32, 4, 2, 8
+    T, dm, H, n_kv, dh = shape
     x = torch.randn(T, dm, device=dev, dtype=torch.float64).float().requires_grad_(True)
     W = (torch.randn(n_kv * dh, dm, device=dev) * 0.3).requires_grad_(True)
     a = torch.rand(H, device=dev).requires_grad_(True)

@@ -40,7 +40,9 @@ os.environ.setdefault("TORCHDYNAMO_DISABLE", "1")
 os.environ.setdefault("TRITON_INTERPRET", "1")
 os.environ.setdefault("PYTHONDONTWRITEBYTECODE", "1")
 
-REF = os.environ.get("DSALT_REFERENCE", "/root/reference")
+REF = os.environ.get("DSALT_REFERENCE")
+if not REF:
+    raise SystemExit("set DSALT_REFERENCE to the reference checkout (see the module docstring)")
 OUT = Path(__file__).resolve().parent
 sys.path.insert(0, REF)
 

@@ -24,7 +24,19 @@ __global__ void __launch_bounds__(256) win_gate_kernel(DsaltWinGateParams p) {
   const T* x = reinterpret_cast<const T*>(p.x) + t * p.d_model;
   const T* w = reinterpret_cast<const T*>(p.weight);
   float acc = 0.f;
-  for (int d = lane; d < p.d_model; d += 32) acc = fmaf(to_f32<T>(x[d]), to_f32<T>(w[d]), acc);
+  if (sizeof(T) == 2 && p.d_model % 8 == 0 && ((uintptr_t)p.x & 15u) == 0 && ((uintptr_t)p.weight & 15u) == 0) {
+    // 16-byte pieces (uniform over the launch)
+    for (int j = lane; j < p.d_model / 8; j += 32) {
+      const uint4 xv = __ldg(reinterpret_cast<const uint4*>(x) + j);
+      const uint4 wv = __ldg(reinterpret_cast<const uint4*>(w) + j);
+      const T* xe = reinterpret_cast<const T*>(&xv);
+      const T* we = reinterpret_cast<const T*>(&wv);
+#pragma unroll
+      for (int k = 0; k < 8; ++k) acc = fmaf(to_f32<T>(xe[k]), to_f32<T>(we[k]), acc);
+    }
+  } else {
+    for (int d = lane; d < p.d_model; d += 32) acc = fmaf(to_f32<T>(x[d]), to_f32<T>(w[d]), acc);
+  }
   acc = warp_sum(acc);
   if (lane != 0) return;
   const float b = to_f32<T>(reinterpret_cast<const T*>(p.bias)[0]);

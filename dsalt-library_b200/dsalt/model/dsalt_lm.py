@@ -133,6 +133,10 @@ class DSALTLMHeadModel(nn.Module):
                                           output_size=int(cu_list[-1]))
         pos_ids = torch.arange(total_len, device=device) - cu[:-1][seq_ids]
         rope_cs = (attn0.rope_cos.to(device)[pos_ids], attn0.rope_sin.to(device)[pos_ids])
+        if torch.is_autocast_enabled(device.type):
+            # every layer casts the rows to the compute dtype: do it once
+            dt = torch.get_autocast_dtype(device.type)
+            rope_cs = (rope_cs[0].to(dt), rope_cs[1].to(dt))
         return rope_cs, cu_list
 
     def forward(self, input_ids, cu_seqlens=None, max_seqlen=None, labels=None, gradient_checkpointing=False,

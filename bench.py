@@ -74,6 +74,28 @@ def peaks():
     return 1590.0, 1400.0, 6650.0, "fallback"
 
 
+# ------------------------------------------------------------- multi-rank
+def job_totals(ms: float, work: float, world: int, device) -> tuple[float, float]:
+    """(max over the ranks of the timed milliseconds, sum over the ranks of the work):
+    every rank calls it, two all-reduces in a fixed order (MAX, then SUM)."""
+    if world <= 1:
+        return float(ms), float(work)
+    import torch
+    import torch.distributed as dist
+    tm = torch.tensor([ms], dtype=torch.float64, device=device)
+    tw = torch.tensor([work], dtype=torch.float64, device=device)
+    dist.all_reduce(tm, op=dist.ReduceOp.MAX)
+    dist.all_reduce(tw, op=dist.ReduceOp.SUM)
+    return float(tm.item()), float(tw.item())
+
+
+def config5_shard(world: int) -> int:
+    """Heads per rank of config 5 (its 32 heads split evenly, no collective in the op)."""
+    if world <= 0 or CONFIG5["H"] % world:
+        raise SystemExit("config5 shards 32 heads: --gpus must divide 32")
+    return CONFIG5["H"] // world
+
+
 # ----------------------------------------------------------------- workload
 def make_workload(wl, seed, device):
     import torch
@@ -491,8 +513,7 @@ def run_config5(args):
                     "e2e": {"value": val, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
             print(json.dumps(line), flush=True)
         return
-    if CONFIG5["H"] % world:
-        raise SystemExit("config5 shards 32 heads: --gpus must divide 32")
+    heads = config5_shard(world)
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
     if world > 1:
@@ -506,7 +527,6 @@ def run_config5(args):
     from dsalt.kernels import _ext
     from dsalt.kernels.dsalt_triton_attn import dsalt_triton_attention
     from dsalt.kernels.flops import attended_pairs
-    heads = CONFIG5["H"] // world
     d = config5_inputs(heads, rank, dev)
     pairs = attended_pairs(d["w"], d["lmk"], d["cu"], semantics="infer")
 
@@ -533,14 +553,7 @@ def run_config5(args):
         launches = sum(KERNELS_PER_CALL.get(n, 1) for n, _, _ in rec)
         fwd = [a.elapsed_time(b) for n, a, b in rec if n == "dsalt_attn_fwd"]
         flops = 4.0 * d["D"] * pairs
-        t = torch.tensor([ms, flops], dtype=torch.float64, device=dev)
-        if world > 1:
-            tm, tf = t[:1].clone(), t[1:].clone()
-            dist.all_reduce(tm, op=dist.ReduceOp.MAX)
-            dist.all_reduce(tf, op=dist.ReduceOp.SUM)
-            ms_max, flops_all = float(tm.item()), float(tf.item())
-        else:
-            ms_max, flops_all = ms, flops
+        ms_max, flops_all = job_totals(ms, flops, world, dev)
         value = flops_all * args.steps / (ms_max / 1e3) / 1e12
         # end to end: q, k, v and the selection inputs copied from pinned host memory and O
         # (fp32) read back every step, copies on their own streams pipelined with the compute
@@ -702,15 +715,7 @@ def main():
     for name, a, b in rec2:
         per_kernel.setdefault(name, []).append(a.elapsed_time(b))
 
-    t = torch.tensor([ms, 14.0 * d["D"] * pairs], dtype=torch.float64, device=dev)
-    if world > 1:
-        tm = t[:1].clone()
-        dist.all_reduce(tm, op=dist.ReduceOp.MAX)
-        tf = t[1:].clone()
-        dist.all_reduce(tf, op=dist.ReduceOp.SUM)
-        ms_max, flops_all = float(tm.item()), float(tf.item())
-    else:
-        ms_max, flops_all = ms, float(t[1].item())
+    ms_max, flops_all = job_totals(ms, 14.0 * d["D"] * pairs, world, dev)
     value = flops_all * args.steps / (ms_max / 1e3) / 1e12
 
     # end-to-end through the public op with host buffers: every step copies its

@@ -64,3 +64,39 @@ def test_model_step_entry_points_reject_bad_arguments():
     assert _rc("dsalt_rope_gqa_fwd", _ext.RopeParams(T=4, ld=130, H=2, Hkv=2, D=64, dtype=_ext.BF16)) == ARG
     # cross-entropy: 16-bit logits only
     assert _rc("dsalt_xent_fwd_grad", _ext.XentParams(rows=4, vocab=10, dtype=_ext.F32)) == DT
+
+
+def test_model_step_functions_refuse_cpu_tensors():
+    """The CUDA model-step functions have no CPU path: called directly on CPU tensors
+    they raise (the modules route CPU tensors to the reference's torch ops instead)."""
+    from dsalt.kernels.fused_ce import fused_chunked_cross_entropy
+    from dsalt.kernels.rmsnorm_cuda import add_rms_norm, rms_norm
+    from dsalt.kernels.rope_gqa import qkv_rope
+    from dsalt.kernels.swiglu import swiglu_ffn
+    x = torch.randn(4, 256)
+    w = torch.ones(256)
+    with pytest.raises(RuntimeError, match="CUDA"):
+        rms_norm(x, w, 1e-6)
+    with pytest.raises(RuntimeError, match="CUDA"):
+        add_rms_norm(x, x, w, 1e-6)
+    with pytest.raises(RuntimeError, match="CUDA"):
+        swiglu_ffn(x, torch.randn(512, 256), torch.randn(512, 256), torch.randn(256, 512), torch.bfloat16)
+    with pytest.raises(RuntimeError, match="CUDA"):
+        fused_chunked_cross_entropy(x, torch.randn(10, 256), torch.zeros(4, dtype=torch.long), 2, torch.bfloat16)
+    with pytest.raises(RuntimeError, match="CUDA"):
+        qkv_rope(x, torch.randn(128, 256), torch.randn(128, 256), torch.randn(128, 256), torch.ones(4, 64),
+                 torch.zeros(4, 64), 2, 2, 64, torch.bfloat16)
+
+
+def test_modules_keep_reference_ops_on_cpu():
+    """On CPU the norm and FFN modules compute with the reference's torch ops."""
+    import torch.nn.functional as F
+    from dsalt.kernels.RMSENorm import RMSENorm
+    from dsalt.modules.dsalt_transformer import SwiGLUFFN
+    torch.manual_seed(0)
+    n, ffn = RMSENorm(256), SwiGLUFFN(256, 512)
+    x, r = torch.randn(5, 256), torch.randn(5, 256)
+    s, y = n.add_forward(x, r)
+    torch.testing.assert_close(s, x + r)
+    torch.testing.assert_close(y, F.rms_norm(x + r, (256,), n.weight, n.eps))
+    torch.testing.assert_close(ffn(x), ffn.down_proj(F.silu(ffn.gate_proj(x)) * ffn.up_proj(x)))

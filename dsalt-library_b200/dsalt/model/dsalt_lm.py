@@ -2,11 +2,13 @@
 
 Same constructor, module tree, parameter names and initialisation order as the
 reference, so a seeded construction and reference checkpoints give identical
-weights.  The attention layers run the B200 CUDA ops.  ``loss_fn="liger"``
-(a Triton fused-CE kernel outside the attention path) is not provided;
-``"auto"`` resolves to ``"chunked"``, which on CUDA in 16-bit compute runs the
-fused chunked loss of ``kernels/fused_ce.py`` (loss and gradient per chunk in
-one pass over the logits).
+weights.  The attention layers run the B200 CUDA ops.  The loss: on CUDA in
+16-bit compute every ``loss_fn`` runs the fused chunked loss of
+``kernels/fused_ce.py`` (loss and gradient per chunk in one pass over the
+logits), the B200 counterpart of the reference's Triton fused linear
+cross-entropy (``"liger"``); elsewhere the reference's chunked loss.  ``"auto"``
+(the reference measures chunked against Liger once per device) therefore
+resolves to the same computation.
 """
 
 from __future__ import annotations
@@ -55,9 +57,6 @@ class DSALTLMHeadModel(nn.Module):
                  loss_fn="chunked", aux_loss_weight=0.0, n_kv_heads=None, qkv_bias=False, rope_base=10000.0):
         super().__init__()
         assert loss_fn in _LOSS_FN, f"loss_fn must be one of {list(_LOSS_FN)}"
-        if loss_fn == "liger":
-            raise RuntimeError("loss_fn='liger' needs the Triton fused cross-entropy, which this B200 build "
-                               "does not provide; use loss_fn='chunked'")
         self.d_model = d_model
         self.n_layers = n_layers
         self.vocab_size = vocab_size

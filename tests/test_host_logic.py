@@ -100,3 +100,17 @@ def test_modules_keep_reference_ops_on_cpu():
     torch.testing.assert_close(s, x + r)
     torch.testing.assert_close(y, F.rms_norm(x + r, (256,), n.weight, n.eps))
     torch.testing.assert_close(ffn(x), ffn.down_proj(F.silu(ffn.gate_proj(x)) * ffn.up_proj(x)))
+
+
+@pytest.mark.parametrize("loss_fn", ["chunked", "liger", "auto"])
+def test_every_loss_fn_gives_the_chunked_loss_on_cpu(loss_fn):
+    """All three reference loss options build and, on CPU, give the reference's chunked loss."""
+    from dsalt.model.dsalt_lm import DSALTLMHeadModel, _chunked_cross_entropy
+    torch.manual_seed(0)
+    m = DSALTLMHeadModel(vocab_size=50, d_model=256, n_layers=1, n_heads=4, n_min=8, n_max=32, k_lmk=4,
+                         max_seq_len=256, loss_fn=loss_fn, lm_head_chunk_size=7)
+    x = torch.randn(2, 10, 256)
+    labels = torch.randint(0, 50, (2, 10))
+    labels[0, :3] = -100
+    ref = _chunked_cross_entropy(x.reshape(-1, 256), m.lm_head.weight, labels.reshape(-1), 7)
+    torch.testing.assert_close(m._compute_loss(x, labels), ref)

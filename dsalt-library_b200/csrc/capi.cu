@@ -43,6 +43,7 @@ cudaError_t launch_xent(const DsaltXentParams& p, cudaStream_t st);
 cudaError_t launch_swiglu(const DsaltSwigluParams& p, bool bwd, cudaStream_t st);
 cudaError_t launch_win_gate_bwd(const DsaltWinGateBwdParams& p, cudaStream_t st);
 cudaError_t launch_hybrid_scores_bwd(const DsaltScoreBwdParams& p, cudaStream_t st);
+cudaError_t launch_wait_timeout_probe(int32_t* status, cudaStream_t st);
 cudaError_t launch_hybrid_scores(const DsaltScoreParams& p, cudaStream_t st);
 cudaError_t launch_topk(const DsaltTopkParams& p, cudaStream_t st);
 cudaError_t noalloc_score_scratch(float** out);
@@ -312,6 +313,11 @@ static int check_swiglu(const DsaltSwigluParams* p, bool bwd) {
     if (!aligned16(need[i])) return DSALT_ERR_ALIGN;
   }
   return DSALT_OK;
+}
+
+int dsalt_selftest_wait_timeout(int32_t* status, void* stream) {
+  if (!status) return DSALT_ERR_ARG;
+  return status_of(launch_wait_timeout_probe(status, (cudaStream_t)stream));
 }
 
 int dsalt_hybrid_scores_bwd(const DsaltScoreBwdParams* p, void* stream) {

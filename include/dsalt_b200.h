@@ -423,6 +423,13 @@ typedef struct DsaltSwigluParams {
 DSALT_API int dsalt_swiglu_fwd(const DsaltSwigluParams* p, void* stream);
 DSALT_API int dsalt_swiglu_bwd(const DsaltSwigluParams* p, void* stream);
 
+/* ---- self-test of the failure path ---------------------------------------
+ * Launches one CTA whose mbarrier wait can never complete.  The bounded wait
+ * every tensor-core kernel uses gives up after its limit (about 2 s), ORs
+ * DSALT_DEV_WAIT_TIMEOUT into *status (a device int32) and the kernel returns
+ * normally: the stream and the context stay usable.                          */
+DSALT_API int dsalt_selftest_wait_timeout(int32_t* status, void* stream);
+
 /* ---- introspection ------------------------------------------------------- */
 DSALT_API int dsalt_b200_abi_version(void);
 DSALT_API const char* dsalt_b200_status_string(int status);

@@ -297,7 +297,8 @@ def prologue_bench(dev, hbm_gbs, reps=20):
     return out
 
 
-def cpu_baseline(wl, units=2):
+def cpu_baseline(wl, units=8):
+    """The oracle on ``units`` (sequence, head) units of the workload: about 10 s of host work."""
     us = [cpu_unit(wl, s) for s in range(units)]
     cpu_time_unit(us[0])  # warm-up (BLAS threads, page faults)
     secs = sum(cpu_time_unit(u) for u in us)
@@ -623,8 +624,8 @@ def run_config5(args):
                         "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h),
                         "note": "host<->device copies on their own streams, pipelined with the neighbouring steps"},
                 "clocks": clk.summary()}
-        if not args.no_cpu_baseline:
-            line["cpu_baseline"] = config5_cpu()
+        if not args.no_cpu_baseline and world == 1:  # the host baseline is timed at N = 1 only
+            line["cpu_baseline"] = config5_cpu(rows_n=2048)  # about 10 s of host work
         print(json.dumps(line), flush=True)
     if world > 1:
         barrier()
@@ -821,7 +822,7 @@ def main():
         if e2e is not None:
             line["e2e"] = e2e
         line["prologue"] = prologue_bench(dev, hbm)
-        if not args.no_cpu_baseline:
+        if not args.no_cpu_baseline and world == 1:  # the host baseline is timed at N = 1 only
             line["cpu_baseline"] = cpu_baseline(wl)
         print(json.dumps(line), flush=True)
     if world > 1:

@@ -9,9 +9,13 @@ op ``dsalt_triton_train_attention`` plus its backward over the whole batch.
     python bench.py [--gpus N] [--steps K] [--warmup W] [--workload config2|config3]
     python bench.py --impl reference        # the CPU restatement on the host cores
 
-Multi-GPU (torchrun, one rank per GPU): every rank runs its own full batch
-(weak scaling over batch×heads, no collective in the timed region); ``value``
-sums the attended FLOPs of all ranks over the slowest rank's time.
+Multi-GPU (torchrun, one rank per GPU): the one global batch is split by heads
+(rank r runs heads [r·H/N, (r+1)·H/N) of every sequence: config 2's 64 (sequence,
+head) units become 8 per GPU at N=8), no collective in the timed region (strong
+scaling); ``value`` sums the attended FLOPs of all ranks over the slowest rank's
+time.  The NCCL all-gather that reassembles O along heads is timed apart
+(``allgather_o``).  ``--workload config5`` (inference, heads sharded) and
+``config4`` (model training step, DDP) are the other BASELINE configs.
 """
 
 from __future__ import annotations
@@ -53,6 +57,8 @@ KERNELS_PER_CALL = {"dsalt_build_schedule": 2, "dsalt_gather_landmarks": 1, "dsa
 # command are in profiles/launches_traffic_step_config2.txt
 NCU_TRAFFIC_BYTES = {"config2": {"dsalt_attn_fwd": 361400000, "dsalt_attn_bwd_preprocess": 240800000,
                                  "dsalt_attn_bwd_dkdv": 559300000, "dsalt_attn_bwd_dq": 339000000}}
+# digest of csrc/ (kernel_source_digest) when that capture was taken; other sources -> traffic null
+NCU_TRAFFIC_SRC = "unknown"
 CLOCK_REASONS = {0x1: "gpu_idle", 0x2: "applications_clocks_setting", 0x4: "sw_power_cap",
                  0x8: "hw_slowdown", 0x10: "sync_boost", 0x20: "sw_thermal_slowdown",
                  0x40: "hw_thermal_slowdown", 0x80: "hw_power_brake_slowdown", 0x100: "display_clock_setting"}
@@ -320,7 +326,7 @@ def run_reference(args, wl):
     val = flops / sum(secs) / 1e12
     line = {"metric": METRIC, "value": val, "unit": UNIT, "n_gpus": args.gpus, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": 1e3 * sum(secs) / len(secs), "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
             "impl": "reference",
             "config": {"workload": wl["desc"] + " (one (sequence, head) unit per step)", "seq_len": u[0]["L"]},
             "cpu_baseline": {"value": val, "unit": UNIT, "cores": os.cpu_count(), "kind": "port",
@@ -641,6 +647,7 @@ def main():
     ap.add_argument("--workload", default="config2", choices=list(WORKLOADS) + ["config4", "config5"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-triton-ref", action="store_true", help="skip timing the reference's Triton op")
     ap.add_argument("--bucket-mb", type=int, default=100, help="config4: DDP bucket size (MB)")
     ap.add_argument("--ddp-bf16-grads", action="store_true", help="config4: bf16 gradient all-reduce hook")
     args = ap.parse_args()
@@ -660,10 +667,19 @@ def main():
     if args.impl == "reference":
         run_reference(args, wl)
         return
+    run_op(args, wl)
 
+
+def run_op(args, wl):
+    """Configs 2 and 3: forward + backward of the public training op.  With N ranks the
+    one global batch is split by heads (``dsalt.kernels.head_shard``): rank r runs
+    heads [h0, h1) of every sequence, no collective in the timed region (strong
+    scaling: the whole job's work is fixed).  ``value`` = 14·D·P over all heads /
+    the slowest rank's time."""
     import torch
     import torch.distributed as dist
     from dsalt.kernels import _ext
+    from dsalt.kernels.head_shard import shard_op_inputs
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
@@ -677,9 +693,15 @@ def main():
         if world > 1:
             dist.barrier()
 
-    from dsalt.kernels.flops import attended_pairs
-    d = make_workload(wl, seed=rank, device=dev)
+    from dsalt.kernels.flops import attended_pairs, scanned_pairs_fwd
+    d = make_workload(wl, seed=0, device=dev)   # the same global batch on every rank
+    H_all = d["H"]
+    sh = shard_op_inputs(d["q"], d["k"], d["v"], d["lmk_pos"], d["lmk_logw"], rank, world, extra={"do": d["do"]})
+    d.update(sh)
+    d["H"] = sh["heads"][1] - sh["heads"][0]
+    torch.cuda.empty_cache()
     pairs = attended_pairs(d["w"], d["lmk_pos"], d["cu"])
+    scanned = scanned_pairs_fwd(d["w"], d["lmk_pos"], d["cu"])
     step = step_fn(d)
     for _ in range(max(args.warmup, 3)):
         step()
@@ -717,117 +739,207 @@ def main():
         per_kernel.setdefault(name, []).append(a.elapsed_time(b))
 
     ms_max, flops_all = job_totals(ms, 14.0 * d["D"] * pairs, world, dev)
+    _, scanned_all = job_totals(0.0, float(scanned), world, dev)
+    _, pairs_all = job_totals(0.0, float(pairs), world, dev)
     value = flops_all * args.steps / (ms_max / 1e3) / 1e12
 
-    # end-to-end through the public op with host buffers: every step copies its
-    # inputs from pinned host memory and its gradients back.  The copies run on
-    # their own streams, pipelined with the neighbouring steps' compute (inputs
-    # double-buffered on the device, outputs double-buffered on the host).
-    e2e = None
-    if not args.no_e2e:
-        names = ("q", "k", "v", "w", "lmk_logw", "lmk_pos", "do")
-        host = {kk: d[kk].detach().cpu().pin_memory() for kk in names}
-        host["do"] = d["do"].to(torch.bfloat16).cpu().pin_memory()  # shipped as bf16, widened on device
-        obuf = [[torch.empty(d["q"].shape, dtype=torch.bfloat16).pin_memory() for _ in range(3)]
-                + [torch.empty(d["T"], dtype=torch.float32).pin_memory(),
-                   torch.empty(d["lmk_logw"].shape, dtype=torch.float32).pin_memory()] for _ in range(2)]
-        dbuf = [{kk: torch.empty(host[kk].shape, dtype=host[kk].dtype, device=dev) for kk in names}
-                for _ in range(2)]
-        h2d = sum(x.numel() * x.element_size() for x in host.values())
-        d2h = sum(x.numel() * x.element_size() for x in obuf[0])
+    # the optional reassembly of O along heads (one NCCL all-gather), timed apart
+    gather = None
+    if world > 1:
         from dsalt.kernels.dsalt_triton_train import dsalt_triton_train_attention
-        main = torch.cuda.current_stream(dev)
-        copy_s, out_s = torch.cuda.Stream(device=dev), torch.cuda.Stream(device=dev)
-        ev_in = [torch.cuda.Event() for _ in range(2)]
-        ev_used = [torch.cuda.Event() for _ in range(2)]
-
-        def h2d_step(n):
-            bi = n % 2
-            if n >= 2:
-                copy_s.wait_event(ev_used[bi])  # the step that last read this buffer is done with it
-            with torch.cuda.stream(copy_s):
-                for kk in names:
-                    dbuf[bi][kk].copy_(host[kk], non_blocking=True)
-            ev_in[bi].record(copy_s)
-
-        def compute_step(n):
-            bi = n % 2
-            main.wait_event(ev_in[bi])
-            x = dbuf[bi]
-            q = x["q"].detach().requires_grad_(True)
-            k = x["k"].detach().requires_grad_(True)
-            v = x["v"].detach().requires_grad_(True)
-            w = x["w"].detach().requires_grad_(True)
-            lw = x["lmk_logw"].detach().requires_grad_(True)
-            o = dsalt_triton_train_attention(q, k, v, x["lmk_pos"], lw, w, d["cu"], 1.0, 4.0, d["n_max"],
-                                             d["cu_list"])
-            grads = torch.autograd.grad(o, (q, k, v, w, lw), x["do"].float())
-            ev_used[bi].record(main)
-            return grads
-
-        def d2h_step(n, grads):
-            out_s.wait_stream(main)
-            with torch.cuda.stream(out_s):
-                for dst, g in zip(obuf[n % 2], grads):
-                    g.record_stream(out_s)
-                    dst.copy_(g, non_blocking=True)
-
-        def run(nsteps):
-            copy_s.wait_stream(main)
-            h2d_step(0)
-            for n in range(nsteps):
-                if n + 1 < nsteps:
-                    h2d_step(n + 1)
-                d2h_step(n, compute_step(n))
-            main.wait_stream(out_s)
-            main.wait_stream(copy_s)
-
-        run(3)
+        from dsalt.kernels.head_shard import gather_heads
+        with torch.no_grad():
+            o_sh = dsalt_triton_train_attention(d["q"], d["k"], d["v"], d["lmk_pos"], d["lmk_logw"], d["w"],
+                                                d["cu"], 1.0, 4.0, d["n_max"], d["cu_list"])
+        for _ in range(3):
+            gather_heads(o_sh, H_all)
         torch.cuda.synchronize()
         barrier()
-        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        a.record(main)
-        run(args.steps)
-        b.record(main)
+        ga, gb = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        reps = 10
+        ga.record()
+        for _ in range(reps):
+            gather_heads(o_sh, H_all)
+        gb.record()
         torch.cuda.synchronize()
-        ems = torch.tensor([a.elapsed_time(b)], dtype=torch.float64, device=dev)
-        if world > 1:
-            dist.all_reduce(ems, op=dist.ReduceOp.MAX)
-        e2e = {"value": flops_all * args.steps / (float(ems.item()) / 1e3) / 1e12, "unit": UNIT,
-               "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h),
-               "note": "host<->device copies on their own streams, pipelined with the neighbouring steps"}
+        gms, _ = job_totals(ga.elapsed_time(gb) / reps, 0.0, world, dev)
+        gather = {"ms": gms, "bytes_out_per_rank": int(o_sh.numel() * 4), "dtype": "f32",
+                  "note": "NCCL all_gather_into_tensor of the fp32 O shards along heads, outside the timed op"}
+        del o_sh
+
+    e2e = None
+    if not args.no_e2e:
+        e2e = e2e_op(args, d, dev, world, flops_all)
 
     if rank == 0:
         burst, sustained, hbm, src = peaks()
         kern = {n: (sum(v) / len(v), sum(v)) for n, v in per_kernel.items()}
         dom = max((n for n in kern if n in FLOPS_PER_PAIR), key=lambda n: kern[n][1])
         ach = FLOPS_PER_PAIR[dom] * d["D"] * pairs / (kern[dom][0] / 1e3) / 1e12
-        traffic = NCU_TRAFFIC_BYTES.get(args.workload, {}).get(dom)
-        roof = {"bound": "tensor", "kernel": dom, "achieved": ach, "peak": sustained, "unit": UNIT,
-                "frac": ach / sustained, "traffic": traffic, "traffic_unit": "bytes per call (ncu dram read+write)",
-                "peak_source": f"{src} bf16_tflops_sustained (kernel timed inside a long step loop)"}
+        traffic, traffic_note = ncu_traffic(args.workload, dom, world)
+        roof = {"bound": "tensor", "kernel": dom, "achieved": ach, "peak": burst, "unit": UNIT,
+                "frac": ach / burst, "traffic": traffic, "traffic_unit": "bytes per call (ncu dram read+write)",
+                "traffic_note": traffic_note,
+                "peak_source": f"{src} bf16_tflops (burst: each entry point is timed alone, back to back)"}
+        units = len(d["lens"]) * d["H"]
         line = {"metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
                 "warmup": max(args.warmup, 3), "ms_per_step": ms_max / args.steps, "higher_is_better": True,
-                "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-                "config": {"workload": wl["desc"], "global_batch": len(d["lens"]) * world,
-                           "seq_len": max(d["lens"]), "tokens_per_gpu": d["T"],
-                           "parallelism": f"dp{world} (batch x heads shards, no collective)",
-                           "l2": "inputs larger than L2 (q,k,v bf16 + dO fp32 = 320 MiB per step), no flush"},
+                "scaling": "strong", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+                "config": {"workload": wl["desc"], "global_batch": len(d["lens"]),
+                           "seq_len": max(d["lens"]), "tokens": d["T"], "heads": H_all,
+                           "heads_per_gpu": d["H"], "units_per_gpu": units,
+                           "parallelism": (f"heads sharded {d['H']} per GPU ({units} (sequence, head) units), "
+                                           "no collective in the op") if world > 1 else "single GPU, all 16 heads",
+                           "l2": "inputs larger than L2 (q,k,v bf16 + dO fp32 = 320 MiB per step at N=1), no flush"},
                 "roofline": roof,
                 "kernels_ms": {n: round(v[0], 4) for n, v in kern.items()},
-                "kernels_ms_note": "entry points timed alone (dK/dV and dQ serialised); the timed steps run them on two streams",
-                "attended_pairs_per_gpu": pairs,
+                "kernels_ms_note": "entry points timed alone (dK/dV and dQ serialised); the timed steps run them "
+                                   "on two streams",
+                "attended_pairs": int(pairs_all), "scanned_pairs_fwd": int(scanned_all),
+                "attended_over_scanned": pairs_all / max(scanned_all, 1.0),
                 "gpu_launches": launches,
                 "clocks": clk.summary()}
+        if gather is not None:
+            line["allgather_o"] = gather
         if e2e is not None:
             line["e2e"] = e2e
-        line["prologue"] = prologue_bench(dev, hbm)
+        if world == 1:
+            line["prologue"] = prologue_bench(dev, hbm)
+            if not args.no_triton_ref:
+                line["triton_reference"] = triton_reference(args, d, flops_all, value)
         if not args.no_cpu_baseline and world == 1:  # the host baseline is timed at N = 1 only
             line["cpu_baseline"] = cpu_baseline(wl)
         print(json.dumps(line), flush=True)
     if world > 1:
         barrier()
         dist.destroy_process_group()
+
+
+def e2e_op(args, d, dev, world, flops_all):
+    """The same op end to end through the public API with host buffers: every step
+    copies its inputs (q, k, v bf16, the fp32 upstream gradient dO, w̃, landmark
+    positions and weights) from pinned host memory and its results (O fp32, dQ, dK,
+    dV, d_w̃, d_logw) back.  The copies run on their own streams, pipelined with the
+    neighbouring steps' compute (inputs double-buffered on the device, outputs
+    double-buffered on the host)."""
+    import torch
+    import torch.distributed as dist
+    from dsalt.kernels.dsalt_triton_train import dsalt_triton_train_attention
+    names = ("q", "k", "v", "w", "lmk_logw", "lmk_pos", "do")
+    host = {kk: d[kk].detach().cpu().pin_memory() for kk in names}
+    T = d["q"].shape[0]
+    obuf = [[torch.empty(d["q"].shape, dtype=torch.float32).pin_memory()]
+            + [torch.empty(d["q"].shape, dtype=torch.bfloat16).pin_memory() for _ in range(3)]
+            + [torch.empty(T, dtype=torch.float32).pin_memory(),
+               torch.empty(d["lmk_logw"].shape, dtype=torch.float32).pin_memory()] for _ in range(2)]
+    dbuf = [{kk: torch.empty(host[kk].shape, dtype=host[kk].dtype, device=dev) for kk in names}
+            for _ in range(2)]
+    h2d = sum(x.numel() * x.element_size() for x in host.values())
+    d2h = sum(x.numel() * x.element_size() for x in obuf[0])
+    main = torch.cuda.current_stream(dev)
+    copy_s, out_s = torch.cuda.Stream(device=dev), torch.cuda.Stream(device=dev)
+    ev_in = [torch.cuda.Event() for _ in range(2)]
+    ev_used = [torch.cuda.Event() for _ in range(2)]
+
+    def h2d_step(n):
+        bi = n % 2
+        if n >= 2:
+            copy_s.wait_event(ev_used[bi])  # the step that last read this buffer is done with it
+        with torch.cuda.stream(copy_s):
+            for kk in names:
+                dbuf[bi][kk].copy_(host[kk], non_blocking=True)
+        ev_in[bi].record(copy_s)
+
+    def compute_step(n):
+        bi = n % 2
+        main.wait_event(ev_in[bi])
+        x = dbuf[bi]
+        q = x["q"].detach().requires_grad_(True)
+        k = x["k"].detach().requires_grad_(True)
+        v = x["v"].detach().requires_grad_(True)
+        w = x["w"].detach().requires_grad_(True)
+        lw = x["lmk_logw"].detach().requires_grad_(True)
+        o = dsalt_triton_train_attention(q, k, v, x["lmk_pos"], lw, w, d["cu"], 1.0, 4.0, d["n_max"],
+                                         d["cu_list"])
+        grads = torch.autograd.grad(o, (q, k, v, w, lw), x["do"])
+        ev_used[bi].record(main)
+        return (o.detach(),) + tuple(grads)
+
+    def d2h_step(n, outs):
+        out_s.wait_stream(main)
+        with torch.cuda.stream(out_s):
+            for dst, g in zip(obuf[n % 2], outs):
+                g.record_stream(out_s)
+                dst.copy_(g, non_blocking=True)
+
+    def run(nsteps):
+        copy_s.wait_stream(main)
+        h2d_step(0)
+        for n in range(nsteps):
+            if n + 1 < nsteps:
+                h2d_step(n + 1)
+            d2h_step(n, compute_step(n))
+        main.wait_stream(out_s)
+        main.wait_stream(copy_s)
+
+    run(3)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record(main)
+    run(args.steps)
+    b.record(main)
+    torch.cuda.synchronize()
+    ems = torch.tensor([a.elapsed_time(b)], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(ems, op=dist.ReduceOp.MAX)
+    return {"value": flops_all * args.steps / (float(ems.item()) / 1e3) / 1e12, "unit": UNIT,
+            "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h),
+            "note": "host<->device copies on their own streams, pipelined with the neighbouring steps; "
+                    "dO shipped in fp32 (the op's output dtype), O and every gradient copied back"}
+
+
+def triton_reference(args, d, flops_all, value):
+    """The reference's own Triton training op on this GPU (the B200 speed bar): the
+    unmodified package under baseline/_ref, run in a child process after its
+    one-shot autotune, on the same inputs; forward + backward per step, CUDA events."""
+    from oracle import ref_triton
+    why = ref_triton.available()
+    if why is not None:
+        return {"unavailable": why}
+    inp = {n: d[n] for n in ("q", "k", "v", "do", "w", "lmk_pos", "lmk_logw", "cu")}
+    inp.update(cu_list=d["cu_list"], n_max=d["n_max"])
+    try:
+        r = ref_triton.run("train", inp, steps=max(3, min(args.steps, 10)), warmup=max(args.warmup, 3),
+                           tuned_cache="/tmp/dsalt_ref_triton_tuned.json")
+    except Exception as e:  # report, do not fail the benchmark line
+        return {"unavailable": f"reference Triton run failed: {str(e)[-300:]}"}
+    ref_val = flops_all * 1.0 / (r["ms_per_step"] / 1e3) / 1e12
+    return {"value": ref_val, "unit": UNIT, "ms_per_step": r["ms_per_step"], "steps": r["steps"],
+            "autotuned_config": r["cfg"], "this_build_over_reference": value / ref_val,
+            "note": "dsalt_triton_train_attention from the unmodified reference (baseline/_ref) after its "
+                    "autotune, same inputs, same attended-pair FLOP count"}
+
+
+def ncu_traffic(workload, kernel, world):
+    """DRAM bytes per call of ``kernel`` from the committed ncu capture, or None when the
+    kernel sources changed since that capture (then the figure would be stale)."""
+    rec = NCU_TRAFFIC_BYTES.get(workload, {})
+    if world != 1 or kernel not in rec:
+        return None, "no ncu capture for this workload / shard"
+    if NCU_TRAFFIC_SRC != kernel_source_digest():
+        return None, "stale: the kernel sources changed since the ncu capture"
+    return rec[kernel], f"ncu capture of the same sources (digest {NCU_TRAFFIC_SRC})"
+
+
+def kernel_source_digest() -> str:
+    import hashlib
+    h = hashlib.sha256()
+    for f in sorted((ROOT / "dsalt-library_b200" / "csrc").glob("*.cu*")):
+        h.update(f.name.encode())
+        h.update(f.read_bytes())
+    return h.hexdigest()[:16]
 
 
 if __name__ == "__main__":

@@ -223,7 +223,8 @@ __global__ void __launch_bounds__(1024) score_stats_kernel(DsaltScoreParams p) {
       const float mu = (float)mean;
       const float sd = p.T > 1 ? (float)sqrt(sqt / (double)(p.T - 1)) : NAN;
       p.stats[2 * c] = mu;
-      p.stats[2 * c + 1] = fmaxf(sd, 1e-6f);
+      // clamp(min=1e-6) keeps a NaN (torch.clamp propagates it): one token gives NaN z-scores
+      p.stats[2 * c + 1] = p.T > 1 ? fmaxf(sd, 1e-6f) : NAN;
     }
   }
 }
@@ -385,9 +386,14 @@ cudaError_t launch_scale_rows(const DsaltScaleRowsParams& p, cudaStream_t st) {
 }
 
 // -------------------------------------------------------------------- top-k
-// Orderable key: larger float -> larger unsigned; excluded / -inf -> 0.
+// Orderable key: larger float -> larger unsigned; excluded / -inf -> 0.  torch.topk
+// ranks NaN above +inf above every finite score, and the reference then turns the
+// non-finite winners into -1 slots (selectors.py:117-133): NaN maps to the largest
+// key, +inf to the next one, and both are written out as -1.
+constexpr uint32_t kKeyPosInf = 0xFF800000u;
 __device__ __forceinline__ uint32_t order_key(float f) {
-  if (!(f > -INFINITY)) return 0u;  // -inf and NaN are never selected
+  if (f != f) return 0xFFFFFFFFu;
+  if (f == -INFINITY) return 0u;
   const uint32_t b = __float_as_uint(f);
   return (b & 0x80000000u) ? ~b : (b | 0x80000000u);
 }
@@ -491,7 +497,7 @@ __global__ void __launch_bounds__(kTopkThreads) topk_kernel(DsaltTopkParams p) {
       const uint32_t kb = out_key[b];
       rank += (kb > ka) || (kb == ka && out_pos[b] < pa);
     }
-    out[rank] = ka == 0u ? -1 : (int64_t)pa;  // non-finite scores give -1 (selectors.py:131-132)
+    out[rank] = (ka == 0u || ka >= kKeyPosInf) ? -1 : (int64_t)pa;  // non-finite: -1 (selectors.py:131-132)
   }
 }
 

@@ -128,7 +128,7 @@ def prepare(k_c: torch.Tensor, v_c: torch.Tensor, lmk_pos: torch.Tensor, lmk_w: 
 
 
 def _params(prep: Prepared, q_c, k_c, v_c, tau_win: float, win_edge: float, impl: int,
-            **bufs) -> _ext.AttnParams:
+            scale: float | None = None, **bufs) -> _ext.AttnParams:
     p = _ext.AttnParams(
         q=_ext.ptr(q_c), k=_ext.ptr(k_c), v=_ext.ptr(v_c), w=_ext.ptr(prep.w),
         cu_seqlens=_ext.ptr(prep.cu), block_map=_ext.ptr(prep.block_map),
@@ -137,7 +137,8 @@ def _params(prep: Prepared, q_c, k_c, v_c, tau_win: float, win_edge: float, impl
         w_sorted=_ext.ptr(prep.w_sorted), perm=_ext.ptr(prep.perm), lmk_slot=_ext.ptr(prep.lmk_slot),
         status=_ext.ptr(device_status(q_c.device)),
         T=prep.T, H=prep.H, D=prep.D, S=prep.S, k_lmk=prep.k_lmk, kp=prep.kp,
-        max_blocks=prep.max_blocks, scale=1.0 / math.sqrt(prep.D), tau_win=float(tau_win),
+        max_blocks=prep.max_blocks, scale=1.0 / math.sqrt(prep.D) if scale is None else float(scale),
+        tau_win=float(tau_win),
         win_edge=float(win_edge) if prep.semantics == _ext.TRAIN else 0.0,
         semantics=prep.semantics, dtype=_ext.dtype_code(q_c.dtype), impl=impl)
     for name, t in bufs.items():
@@ -160,11 +161,13 @@ def forward(q_c, k_c, v_c, prep: Prepared, tau_win: float, win_edge: float, impl
 
 
 def backward(grad_out, q_c, k_c, v_c, o, lse, prep: Prepared, tau_win: float, win_edge: float,
-             impl: int, want_dw: bool):
+             impl: int, want_dw: bool, scale: float | None = None):
     """Run the backward stages; returns ``(dq, dk, dv, d_lw [H,S,k] fp32, dw [T] or None)``.
 
     ``grad_out`` may be fp32 (the op's output dtype) or the input dtype; an fp32
     gradient is rounded to the input dtype by the preprocess kernel itself.
+    ``scale`` multiplies q·kᵀ (default ``1/√D``, what every forward of the op uses);
+    ``lse`` is the natural-log LSE of the scaled logits, as the forward writes it.
     """
     dev = q_c.device
     grad_out = grad_out.contiguous()
@@ -185,7 +188,7 @@ def backward(grad_out, q_c, k_c, v_c, o, lse, prep: Prepared, tau_win: float, wi
                            dtype=torch.float32, device=dev) if prep.kp > 0 else None
     # per-query records (LSE, Delta, window, soft-edge factors) of the tensor-core stages
     qrec = torch.empty(H, T, _ext.QREC_FLOATS, dtype=torch.float32, device=dev)
-    p = _params(prep, q_c, k_c, v_c, tau_win, win_edge, impl, o=o, lse=lse, dout=do_c, dout_f32=do_f32,
+    p = _params(prep, q_c, k_c, v_c, tau_win, win_edge, impl, scale, o=o, lse=lse, dout=do_c, dout_f32=do_f32,
                 delta=delta, dq=dq, dk=dk, dv=dv, dw_head=dw_head, dw=dw, d_lw=d_lw, lmk_grad=lmk_grad,
                 qrec=qrec)
     _ext.call("dsalt_attn_bwd_preprocess", p)

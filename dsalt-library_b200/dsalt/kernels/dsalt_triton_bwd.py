@@ -3,12 +3,22 @@
 Reference: ``dsalt/kernels/dsalt_triton_bwd.py:219-324``.  Same signature and
 return value ``(dq, dk, dv, d_bias)`` as float32 tensors.  The reference
 accumulates dK/dV with ``atomic_add`` (:206-207); here dK/dV are key-parallel
-and atomic-free, so the result is deterministic.  The block-size arguments are
-accepted for compatibility and ignored (tiles are fixed for B200), and the
-landmark keys/values are re-gathered from ``k``/``v`` at ``lmk_pos``.
+and atomic-free, so the result is deterministic.
+
+* ``scale`` multiplies q·kᵀ in the recomputed logits, as in the reference kernel;
+  ``lse`` is the natural-log LSE of those scaled logits (the reference forward's
+  ``m + log l``, dsalt_triton_attn.py:164, which is also what this build's forward
+  writes).
+* ``lmk_K`` / ``lmk_V`` are ``k`` / ``v`` gathered at ``lmk_pos`` (the reference's
+  only caller builds them that way, ``_build_landmark_kv``); this build gathers
+  them itself from ``k`` / ``v`` in position order and checks only their shape.
+* The block-size and launch arguments select Triton tiles in the reference and
+  have no meaning for the fixed B200 kernels; they are accepted and ignored.
 """
 
 from __future__ import annotations
+
+import math
 
 import torch
 
@@ -21,6 +31,13 @@ def dsalt_triton_backward(grad_out, q, k, v, out, lse, lmk_K, lmk_V, lmk_pos, lm
                           BLOCK_M=None, BLOCK_N=None, HEAD_DIM_C=None,
                           num_warps=None, num_stages=None):
     _cuda.check_inputs(q, k, v, cu_seqlens)
+    H, S, k_lmk = lmk_pos.shape
+    for name, t in (("lmk_K", lmk_K), ("lmk_V", lmk_V)):
+        if t is not None and (t.dim() != 4 or tuple(t.shape[:3]) != (H, S, k_lmk) or t.shape[3] != q.shape[2]):
+            raise ValueError(f"{name} must be [H, S, k_lmk, D] = {(H, S, k_lmk, q.shape[2])}, "
+                             f"got {tuple(t.shape)}")
+    if not (isinstance(scale, (int, float)) and math.isfinite(scale)):
+        raise ValueError(f"scale must be a finite number, got {scale!r}")
     dt = _cuda.compute_dtype(q)
     q_c = q.contiguous().to(dt)
     k_c = k.contiguous().to(dt)
@@ -29,5 +46,5 @@ def dsalt_triton_backward(grad_out, q, k, v, out, lse, lmk_K, lmk_V, lmk_pos, lm
     lse_c = lse.contiguous().to(torch.float32)
     prep = _cuda.prepare(k_c, v_c, lmk_pos, lmk_bias, w_sizes, cu_seqlens, _ext.INFER)
     dq, dk, dv, d_bias, _ = _cuda.backward(grad_out, q_c, k_c, v_c, o_c, lse_c, prep, 1.0, 0.0,
-                                           _ext.default_impl(), want_dw=False)
+                                           _ext.default_impl(), want_dw=False, scale=float(scale))
     return dq.float(), dk.float(), dv.float(), d_bias

@@ -18,6 +18,40 @@ import torch
 from . import _ext
 
 
+def _prepare(x, weight, labels, dtype):
+    labels = labels.contiguous().long()
+    V = weight.shape[0]
+    # the kernel scores a label only inside [0, V): count exactly those, so the mean is
+    # taken over the rows that carry a loss (ignore_index -100 and out-of-range labels
+    # add nothing to either sum)
+    n_valid = ((labels >= 0) & (labels < V)).sum()
+    scale = (1.0 / n_valid.clamp(min=1).float()).reshape(1)
+    row_loss = torch.empty(x.shape[0], dtype=torch.float32, device=x.device)
+    return labels, x.to(dtype).contiguous(), weight.to(dtype).contiguous(), scale, row_loss
+
+
+def _chunk_loss(x_c, w_c, labels, scale, row_loss, s, e, dtype):
+    """Rows ``s:e``: logits GEMM, then the kernel's row losses; returns the logits
+    buffer, which the kernel has overwritten with their gradient."""
+    logits = torch.mm(x_c[s:e], w_c.t())
+    p = _ext.XentParams(logits=_ext.ptr(logits), labels=_ext.ptr(labels[s:e]), row_loss=_ext.ptr(row_loss[s:e]),
+                        scale=_ext.ptr(scale), rows=e - s, vocab=w_c.shape[0], ignore_index=-100,
+                        dtype=_ext.dtype_code(dtype))
+    _ext.call("dsalt_xent_fwd_grad", p)
+    return logits
+
+
+def _loss_only(x, weight, labels, chunk: int, dtype: torch.dtype) -> torch.Tensor:
+    """Evaluation path (no gradient wanted): the per-chunk logits GEMM and row losses
+    only; neither gradient GEMM runs and nothing is kept."""
+    _ext.require_cuda(x, "x")
+    labels, x_c, w_c, scale, row_loss = _prepare(x, weight, labels, dtype)
+    chunk = max(int(chunk), 1)
+    for s in range(0, x.shape[0], chunk):
+        _chunk_loss(x_c, w_c, labels, scale, row_loss, s, min(s + chunk, x.shape[0]), dtype)
+    return row_loss.sum() * scale[0]
+
+
 class FusedChunkedCE(torch.autograd.Function):
     """``(x [N, d], weight [V, d], labels [N], chunk) -> mean CE over labels != -100``."""
 
@@ -28,21 +62,12 @@ class FusedChunkedCE(torch.autograd.Function):
         V = weight.shape[0]
         dev = x.device
         chunk = max(int(chunk), 1)
-        labels = labels.contiguous().long()
-        x_c = x.to(dtype).contiguous()
-        w_c = weight.to(dtype).contiguous()
-        n_valid = (labels != -100).sum()
-        scale = (1.0 / n_valid.clamp(min=1).float()).reshape(1)
-        row_loss = torch.empty(N, dtype=torch.float32, device=dev)
+        labels, x_c, w_c, scale, row_loss = _prepare(x, weight, labels, dtype)
         dx = torch.empty_like(x_c)
         dw = None
         for s in range(0, N, chunk):
             e = min(s + chunk, N)
-            logits = torch.mm(x_c[s:e], w_c.t())
-            p = _ext.XentParams(logits=_ext.ptr(logits), labels=_ext.ptr(labels[s:e]), row_loss=_ext.ptr(row_loss[s:e]),
-                                scale=_ext.ptr(scale), rows=e - s, vocab=V, ignore_index=-100,
-                                dtype=_ext.dtype_code(dtype))
-            _ext.call("dsalt_xent_fwd_grad", p)
+            logits = _chunk_loss(x_c, w_c, labels, scale, row_loss, s, e, dtype)
             torch.mm(logits, w_c, out=dx[s:e])
             # dW accumulated in fp32 by the GEMM epilogue
             if dw is None:
@@ -64,4 +89,6 @@ class FusedChunkedCE(torch.autograd.Function):
 def fused_chunked_cross_entropy(x: torch.Tensor, weight: torch.Tensor, labels: torch.Tensor,
                                 chunk: int, dtype: torch.dtype) -> torch.Tensor:
     """Mean CE of ``x @ weightᵀ`` against ``labels`` in ``dtype`` (f16 / bf16) chunk by chunk."""
+    if not (torch.is_grad_enabled() and (x.requires_grad or weight.requires_grad)):
+        return _loss_only(x, weight, labels, chunk, dtype)
     return FusedChunkedCE.apply(x, weight, labels, chunk, dtype)

@@ -12,7 +12,7 @@
  * Reference interfaces replaced (paths relative to the reference project,
  * LeonardoCofone/dsalt-library v1.0.0) are cited beside each entry point.
  * The Python host package `dsalt` (same module paths as the reference) binds
- * these with ctypes; INTEGRATION.md shows the binding.
+ * these with ctypes (dsalt/kernels/_ext.py).
  */
 #ifndef DSALT_B200_H
 #define DSALT_B200_H
@@ -219,7 +219,11 @@ DSALT_API int dsalt_hybrid_scores(const DsaltScoreParams* p, void* stream);
  * DSALT_ERR_TOO_LARGE.  The first call on a device looks up the array's device
  * address (cudaGetSymbolAddress, with that device current) and caches it;
  * make that first call before any stream capture.  All calls on a device share
- * the array, so calls that overlap on the GPU race.  Nothing is allocated.   */
+ * the array, so calls that overlap on the GPU race.  Nothing is allocated.
+ * Forward only: the statistics and norms stay in the shared array (the next
+ * call on the device overwrites them), so they cannot feed
+ * dsalt_hybrid_scores_bwd; a caller that needs the backward uses
+ * dsalt_hybrid_scores with its own stats and norms buffers.                 */
 #define DSALT_NOALLOC_SCORE_MAX_FLOATS (1 << 21)
 DSALT_API int dsalt_hybrid_scores_noalloc(const DsaltScoreParams* p, void* stream);
 

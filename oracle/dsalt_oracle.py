@@ -161,7 +161,11 @@ def landmark_indices(scores, w_sizes, cu, k_lmk: int) -> np.ndarray:
         for h in range(H):
             sc = scores[s0:s1, h].copy()
             sc[covered[s0:s1]] = -np.inf
-            order = np.lexsort((np.arange(s1 - s0), -sc))  # score desc, position asc
+            # torch.topk ranks NaN above +inf above every finite score (the
+            # non-finite winners then become -1 slots, selectors.py:131-132)
+            rank_key = np.where(np.isnan(sc), 2.0, np.where(sc == np.inf, 1.0, 0.0))
+            finite_sc = np.where(np.isfinite(sc), sc, np.where(sc == -np.inf, -np.inf, 0.0))
+            order = np.lexsort((np.arange(s1 - s0), -finite_sc, -rank_key))  # score desc, position asc
             sel = order[:k_eff]
             sel = [int(p) for p in sel if np.isfinite(sc[p])]
             out[h, b, :len(sel)] = sel

@@ -43,3 +43,19 @@ def test_model_uses_fused_loss_under_autocast():
     with torch.autocast("cuda", dtype=torch.bfloat16):
         assert _fused_ce_dtype(x, w) == torch.bfloat16
     assert _fused_ce_dtype(x.cpu(), w.cpu()) is None
+
+
+def test_fused_ce_no_grad_loss_only():
+    """Under no_grad (evaluation) only the loss is computed, and it equals the
+    training path's loss bit for bit (same GEMM, same kernel, same sum)."""
+    from dsalt.kernels.fused_ce import fused_chunked_cross_entropy
+    g = torch.Generator(device="cuda").manual_seed(5)
+    x = torch.randn(700, 128, generator=g, device="cuda")
+    w = torch.randn(5000, 128, generator=g, device="cuda") * 0.05
+    labels = torch.randint(0, 5000, (700,), generator=g, device="cuda")
+    labels[::5] = -100
+    with torch.no_grad():
+        l0 = fused_chunked_cross_entropy(x, w, labels, 256, torch.bfloat16)
+    assert not l0.requires_grad
+    l1 = fused_chunked_cross_entropy(x.requires_grad_(True), w, labels, 256, torch.bfloat16)
+    assert torch.equal(l0, l1.detach())

@@ -45,9 +45,52 @@ def test_win_gate_bit_exact_at_fixed_logits(dtype):
     if dtype == torch.bfloat16:
         assert torch.equal(got, ref.float())
     else:
+        # the golden comes from the reference on the host (torch's CPU sigmoid): within
+        # 2 ulp; the same expression on this GPU (torch's CUDA sigmoid, which the
+        # reference's _window_continuous runs on a CUDA device) bit-exactly
         ulp = (got - ref).abs() / torch.from_numpy(np.spacing(ref.numpy()))
         assert ulp.max() <= 2
-    assert torch.equal(w_disc.cpu(), got.floor().clamp(min=1))
+        lg = logits.to(dev, torch.float32)
+        on_gpu = float(g["n_min"]) + torch.sigmoid(lg) * (float(g["n_max"]) - float(g["n_min"]))
+        assert torch.equal(w_cont, on_gpu)
+    # the discrete window sizes against the reference's own floor(w̃).clamp(min=1)
+    # (dsalt_attention.py:471), not against this kernel's output
+    assert torch.equal(w_disc.cpu(), ref.float().floor().clamp(min=1))
+
+
+@pytest.mark.parametrize("noalloc", [False, True])
+def test_hybrid_scores_single_token_is_nan(noalloc):
+    """One packed token: torch's unbiased std of one element is NaN and
+    clamp(min=1e-6) keeps it, so the reference's z-scores and scores are NaN
+    (landmark_tokens_ker.py:47-55) and its top-k leaves every slot at -1."""
+    from dsalt.kernels import _ext
+    from dsalt.kernels.landmark_tokens_ker import hybrid_scores_per_head
+    from dsalt.kernels.selectors import select_topk
+    dev = torch.device("cuda")
+    g = torch.Generator().manual_seed(1)
+    H, dh, dm = 4, 16, 64
+    x = torch.randn(1, dm, generator=g)
+    W = torch.randn(H * dh, dm, generator=g) * 0.2
+    a = torch.rand(H, generator=g)
+    ref, _, _ = O.hybrid_scores(x.numpy(), W.numpy(), a.numpy(), H, dh)
+    assert np.isnan(ref).all()
+    if noalloc:
+        xd, Wd, ad = x.to(dev), W.to(dev), a.to(dev)
+        xwv = xd @ Wd.T
+        s = torch.empty(1, H, device=dev)
+        p = _ext.ScoreParams(x=_ext.ptr(xd), xwv=_ext.ptr(xwv), alpha=_ext.ptr(ad), scores=_ext.ptr(s),
+                             z_x=0, z_v=0, norms=0, stats=0, T=1, d_model=dm, H=H, n_kv=H, dh=dh,
+                             dtype=_ext.dtype_code(torch.float32))
+        _ext.call("dsalt_hybrid_scores_noalloc", p)
+    else:
+        s, _, _ = hybrid_scores_per_head(x.to(dev), W.to(dev), a.to(dev), H, dh)
+    torch.cuda.synchronize()
+    assert torch.isnan(s).all()
+    cu = torch.tensor([0, 1], dtype=torch.int32, device=dev)
+    idx = select_topk(s, torch.ones(1, device=dev), cu, 4, 1)
+    assert (idx == -1).all()
+    ref_idx = O.landmark_indices(ref, np.ones(1, dtype=np.float32), np.array([0, 1]), 4)
+    assert (ref_idx == -1).all()
 
 
 @pytest.mark.parametrize("case", ["varlen", "uniform", "gqa"])

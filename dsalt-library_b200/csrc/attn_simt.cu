@@ -144,6 +144,7 @@ bwd_preprocess_kernel(const DsaltAttnParams p) {
   s = warp_sum(s);
   if (lane == 0) {
     p.delta[row] = s;
+    if (p.qrec && p.dw_head) p.dw_head[row] = 0.f;  // the tensor-core dK/dV stage adds into it
     if (p.qrec) write_qrec(p, row / p.H, (int)(row % p.H), s);
   }
 }
@@ -328,7 +329,10 @@ bwd_preprocess_vec_kernel(const DsaltAttnParams p) {
   for (int off = G / 2; off > 0; off >>= 1) s += __shfl_xor_sync(0xffffffffu, s, off);
   const int gl = threadIdx.x & (G - 1);  // lane within the row's group
   const int64_t row = chunk / G;
-  if (chunk < n_chunks && gl == 0) p.delta[row] = s;
+  if (chunk < n_chunks && gl == 0) {
+    p.delta[row] = s;
+    if (p.dw_head) p.dw_head[row] = 0.f;  // the tensor-core dK/dV stage adds ∂loss/∂w̃ into it
+  }
   if (!p.qrec) return;  // uniform over the grid
   if constexpr (G >= 8) {
     // the row's record: lane gl < 8 computes edge factor gl, lanes 0-3 write its four 16-byte parts

@@ -1,27 +1,24 @@
-// tcgen05 / TMEM / TMA backward kernels of the DSALT attention for sm_100a.
+// tcgen05 / TMEM / TMA dK/dV kernel of the DSALT attention backward for sm_100a
+// (key-parallel, atomic-free for dK/dV; reference _train_bwd_dkdv_kernel
+// dsalt/kernels/dsalt_triton_train.py:386-481 and the landmark atomics of
+// _train_bwd_kernel :302-333).
 //
-// Both kernels use 320 threads: warps 0-7 are "row" warps (warp w and w+4
-// share TMEM lanes 32·(w%4)…+31 and split each tile's 64 columns in halves of
-// 32), warp 8 is the producer (TMA + per-tile column data), warp 9 allocates
-// TMEM and issues every tcgen05.mma from one thread.  The MMA issue order is
-// "S/dP two tiles ahead, the accumulating MMAs as soon as their operand tile
-// is ready", with every buffer guarded by its own full/empty mbarrier.
-//
-// dQ (query-parallel, reference _train_bwd_kernel dsalt_triton_train.py:240-383):
-//   rows = 128 queries; tiles = 64 keys (landmark tiles, then the rows' band).
-//   S = Q·Kᵀ, dP = dO·Vᵀ (TMEM) -> P = exp(S·scale + bias − LSE),
-//   dS = P·(dP − Δ) (registers) -> dS (bf16, smem), soft-edge fix-up on the
-//   row's edge keys, which also accumulates ∂loss/∂w̃ -> dQ += dS·K (TMEM).
-//
-// dK/dV (key-parallel, atomic-free; reference _train_bwd_dkdv_kernel :386-481
-//   and the landmark atomics of :302-333):
 //   rows = 128 keys; tiles = 64 queries.  Sᵀ = K·Qᵀ, dPᵀ = V·dOᵀ (TMEM) ->
 //   Pᵀ, dSᵀ (bf16, smem; soft-edge fix-up per query column) ->
 //   dV += Pᵀ·dO, dK += dSᵀ·Q (TMEM).  Landmark items (the sorted landmark slots
 //   of one (head, sequence) as the keys, every later query as columns) write
 //   fp32 dK/dV per slot and d_lw (a row sum: no atomics); band items (128
 //   consecutive keys) add those slot rows into their own before the single
-//   store.  The backward is deterministic.
+//   store.  dK/dV and d_lw are deterministic.
+//
+// Every finished dSᵀ tile is also stored (one bulk copy of the 16 KB shared
+// buffer) to the ds_tiles scratch, where the dQ stage (attn_tc_dq.cu) reads it:
+// dQ = scale·Σ dS·K without a second computation of S, dP and the exponentials.
+// The soft-edge fix-up also forms ∂loss/∂w̃ = Σ_edge dS·(1 − σ)/τ of each query
+// column (the reference's D_w, :371-383): a fixed-order sum per (key block,
+// query), added to dw_head, which the preprocess stage zeroed.  A query's edge
+// keys lie in at most two key blocks, so each dw_head entry receives at most two
+// additions onto zero, whose result does not depend on their order.
 //
 // All waits are bounded (sm100::mbar_wait); see attn_tc.cu.
 #include <mutex>
@@ -33,6 +30,7 @@
 namespace dsalt {
 
 cudaError_t simt_attention_stage(int stage, const DsaltAttnParams& p, cudaStream_t st);
+cudaError_t tc_bwd_dq_stage(const DsaltAttnParams& p, cudaStream_t st);
 
 namespace bwd {
 
@@ -75,445 +73,6 @@ __device__ __forceinline__ void store_row32_packed(uint8_t* base, int row, int c
         make_uint4(pk[4 * g], pk[4 * g + 1], pk[4 * g + 2], pk[4 * g + 3]);
 }
 
-// ======================================================================= dQ
-namespace dq {
-constexpr int BM = 128, BN = 64;
-constexpr int kKV = 3;           // K / V tile ring
-// 16 row warps in two groups of eight that take alternate 64-key tiles: warp w
-// reads TMEM lanes 32·(w % 4)… and owns the 32-column half (w / 4) % 2 of its
-// group's tiles; then the TMA warp, MMA warp A (TMEM owner: S) and MMA warp B
-// (dP, dQ)
-constexpr int kRowWarps = 16;
-constexpr int kRowThreads = 32 * kRowWarps;
-constexpr int kProducerWarp = 16;
-constexpr int kMmaWarp = 17;
-constexpr int kMmaWarpB = 18;
-constexpr int kThreadsDQ = 608;
-constexpr int kHalfCols = BN / 2;  // tile columns per row thread
-enum { QD_FULL = 0, K_FULL = 1, V_FULL = K_FULL + kKV, K_EMPTY = V_FULL + kKV, V_EMPTY = K_EMPTY + kKV,
-       SD_FULL = V_EMPTY + kKV, SD_EMPTY = SD_FULL + 2, DS_FULL = SD_EMPTY + 2, DS_EMPTY = DS_FULL + 2,
-       DQ_DONE = DS_EMPTY + 2, FINAL = DQ_DONE + 1, EPI = FINAL + 2, EPI2 = EPI + 1, NB = EPI2 + 1 };
-
-template <int D>
-struct alignas(1024) Smem {
-  uint8_t q[BM * D * 2];
-  uint8_t dO[BM * D * 2];
-  uint8_t k[kKV][BN * D * 2];
-  uint8_t v[kKV][BN * D * 2];
-  uint8_t ds[2][BM * BN * 2];
-  uint64_t bars[NB];
-  uint32_t tmem_base;
-  int abort_flag, band_lo, band_hi, n_valid, slow_edge;
-  float dw_part[4][BM];  // ∂loss/∂w̃ partial sums of the four column quarters
-  alignas(16) float eg[BM][kMaxEdge];  // each row's soft-edge factors (its record's eg), float4 stores
-  int lmk_pos[kMaxLmk];
-  float lmk_lw2[kMaxLmk];
-};
-static_assert(offsetof(Smem<128>, eg) % 16 == 0 && offsetof(Smem<64>, eg) % 16 == 0, "eg rows take float4 stores");
-
-template <typename T, int D>
-__global__ void __launch_bounds__(kThreadsDQ, 1) tc_bwd_dq_kernel(const __grid_constant__ BwdArgs a) {
-  using namespace sm100;
-  const DsaltAttnParams& p = a.p;
-  const int blk = blockIdx.x, h = blockIdx.y;
-  if (blk >= __ldg(p.num_blocks)) return;
-  const int s = __ldg(p.block_map + 2 * blk);
-  const int64_t s0 = __ldg(p.cu_seqlens + s);
-  const int L = (int)(__ldg(p.cu_seqlens + s + 1) - s0);
-  const int m0 = __ldg(p.block_map + 2 * blk + 1) * BM;
-  extern __shared__ uint8_t smem_raw[];
-  Smem<D>& sm = *reinterpret_cast<Smem<D>*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
-  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  constexpr bool kBF16 = !std::is_same<T, __half>::value;
-  const BarArray bar{smem_u32(&sm.bars[0])};
-  if (tid == 0) {
-    mbar_init(bar[QD_FULL], 1);
-    for (int st = 0; st < kKV; ++st) {
-      mbar_init(bar[K_FULL + st], 1);
-      mbar_init(bar[V_FULL + st], 1);
-      mbar_init(bar[K_EMPTY + st], 2);  // read by S (MMA warp A) and dQ (MMA warp B)
-      mbar_init(bar[V_EMPTY + st], 1);
-    }
-    for (int st = 0; st < 2; ++st) {  // st = tile % 2 = row group
-      mbar_init(bar[SD_FULL + st], 2);  // S (MMA warp A) and dP (MMA warp B)
-      mbar_init(bar[SD_EMPTY + st], kRowThreads / 2);
-      mbar_init(bar[DS_FULL + st], kRowThreads / 2);
-      mbar_init(bar[DS_EMPTY + st], 1);
-    }
-    mbar_init(bar[DQ_DONE], 1);
-    mbar_init(bar[FINAL], 1);
-    mbar_init(bar[FINAL + 1], 1);
-    mbar_init(bar[EPI], kRowThreads);
-    mbar_init(bar[EPI2], kRowThreads);
-    fence_mbar_init();
-    sm.abort_flag = 0;
-    sm.band_lo = INT_MAX;
-    sm.band_hi = -1;
-    sm.n_valid = 0;
-    sm.slow_edge = 0;
-  }
-  if (warp == kMmaWarp) tmem_alloc(smem_u32(&sm.tmem_base), 512);
-  // row r (TMEM lane) = 32·(warp % 4) + lane; column quarter = warp / 4.  The row's
-  // record (LSE, Δ, window, soft-edge factors) is loaded while the landmark
-  // positions are staged.
-  const int r = 32 * (warp & 3) + lane;
-  const int quarter = warp >> 2;
-  const int i = m0 + r;
-  const bool row_ok = warp < kRowWarps && i < L;
-  // header of the row's record (the soft-edge factors are read when needed)
-  const QRec* recg = reinterpret_cast<const QRec*>(p.qrec) + (int64_t)h * p.T + s0 + i;
-  float4 rh0 = make_float4(0.f, 0.f, __int_as_float(INT_MAX), __int_as_float(INT_MIN));
-  float4 rh1 = make_float4(__int_as_float(INT_MIN), __int_as_float(INT_MAX), -INFINITY, 0.f);
-  if (row_ok) {
-    rh0 = __ldg(reinterpret_cast<const float4*>(recg));      // nlse2, delta, lo, qi
-    rh1 = __ldg(reinterpret_cast<const float4*>(recg) + 1);  // ehi, elo, wlo, wt
-  }
-  if (warp < kRowWarps && quarter < 2) {  // the row's soft-edge factors, for the fix-up of its dS
-    const float4 e4 = row_ok ? __ldg(reinterpret_cast<const float4*>(recg) + 2 + quarter) : make_float4(1.f, 1.f, 1.f, 1.f);
-    *reinterpret_cast<float4*>(&sm.eg[r][4 * quarter]) = e4;
-  }
-  const int rec_lo = __float_as_int(rh0.z), rec_qi = __float_as_int(rh0.w);
-  const int rec_ehi = __float_as_int(rh1.x), rec_elo = __float_as_int(rh1.y);
-  const int rec_ne = rec_elo <= rec_ehi ? rec_ehi - rec_elo + 1 : 0;
-  const int kp = p.kp;
-  const int64_t lbase = ((int64_t)h * p.S + s) * kp;
-  for (int c = tid; c < kp; c += kThreadsDQ) {
-    const int ps = __ldg(p.pos_sorted + lbase + c);
-    sm.lmk_pos[c] = ps;
-    sm.lmk_lw2[c] = __ldg(p.w_sorted + lbase + c) * kLog2e;
-    if (ps >= 0) atomicAdd(&sm.n_valid, 1);
-  }
-  __syncthreads();
-  // Q, dO and the first landmark tile (the landmark tiles cover every valid slot
-  // of the sequence, sorted) depend only on the block: their loads start while
-  // the windows are being resolved
-  const int n_valid = sm.n_valid;
-  const int n_lt = (n_valid + BN - 1) / BN;
-  if (warp == kProducerWarp && lane < 2) {
-    if (lane == 0) {
-      mbar_expect_tx(bar[QD_FULL], 2 * BM * D * 2);
-#pragma unroll
-      for (int c = 0; c < D / 64; ++c) {
-        tma_load_3d(smem_u32(sm.q + c * (BM * 128)), &a.tm_q, bar[QD_FULL], c * 64, h, (int)(s0 + m0));
-        tma_load_3d(smem_u32(sm.dO + c * (BM * 128)), &a.tm_do, bar[QD_FULL], c * 64, h, (int)(s0 + m0));
-      }
-    }
-    if (n_lt > 0) {
-      const int FULL = lane == 0 ? K_FULL : V_FULL;
-      mbar_expect_tx(bar[FULL], a.lmk_box * D * 2);
-      uint8_t* dst = lane == 0 ? sm.k[0] : sm.v[0];
-      const CUtensorMap* map = lane == 0 ? &a.tm_lk : &a.tm_lv;
-#pragma unroll
-      for (int c = 0; c < D / 64; ++c)
-        tma_load_3d(smem_u32(dst + c * (BN * 128)), map, bar[FULL], c * 64, 0, h * p.S + s);
-    }
-  }
-  const bool row_live = row_ok && rec_qi != INT_MIN;  // a row without keys has no gradient
-  int lo = INT_MAX, hi = -1, cnt = 0;
-  if (row_live) {
-    if (rec_lo != INT_MAX) { lo = rec_lo; hi = i; }
-    int a0 = 0, a1 = sm.n_valid;
-    while (a0 < a1) {
-      const int mid = (a0 + a1) >> 1;
-      const int ps = sm.lmk_pos[mid];
-      if (ps <= i && (float)ps < rh1.z) a0 = mid + 1; else a1 = mid;
-    }
-    cnt = a0;
-    if (quarter == 0) {
-      if (lo <= hi) { atomicMin(&sm.band_lo, lo); atomicMax(&sm.band_hi, hi); }
-      if (rec_ne > kMaxEdge) atomicOr(&sm.slow_edge, 1);
-    }
-  }
-  tc_fence_before();
-  __syncthreads();
-  tc_fence_after();
-  const uint32_t tmem = sm.tmem_base;
-  const int band_lo = sm.band_lo, band_hi = sm.band_hi;
-  const int n_bt = band_hi >= band_lo ? (band_hi - band_lo + BN) / BN : 0;
-  const int n_tiles = n_lt + n_bt;
-  volatile int* abort_flag = &sm.abort_flag;
-  // valid key rows of tile t (landmark tiles may hold fewer than BN loaded rows)
-  auto tile_n = [&](int t) -> int {
-    if (t < n_lt) return round16(min(BN, n_valid - BN * t));
-    return BN;
-  };
-  const uint32_t tS = tmem, tdP = tmem + 2 * BN, tdQ = tmem + 4 * BN;
-
-  if (warp == kProducerWarp) {
-    // lane 0: K tiles; lane 1: V tiles
-    if (lane < 2 && n_tiles > 0) {
-      const bool is_k = lane == 0;
-      const int FULL = is_k ? K_FULL : V_FULL, EMPTY = is_k ? K_EMPTY : V_EMPTY;
-      // tile 0 of a sequence with landmarks was issued before the windows were resolved
-      int issued = n_lt > 0 ? 1 : 0;
-      for (int t = issued; t < n_tiles; ++t) {
-        const int st = t % kKV;
-        if (t >= kKV && !mbar_wait(bar[EMPTY + st], (t / kKV - 1) & 1, abort_flag, p.status)) break;
-        const bool lmk = t < n_lt;
-        mbar_expect_tx(bar[FULL + st], (lmk ? a.lmk_box : BN) * D * 2);
-        uint8_t* dst = is_k ? sm.k[st] : sm.v[st];
-        const CUtensorMap* map = lmk ? (is_k ? &a.tm_lk : &a.tm_lv) : (is_k ? &a.tm_k : &a.tm_v);
-#pragma unroll
-        for (int c = 0; c < D / 64; ++c) {
-          if (lmk) tma_load_3d(smem_u32(dst + c * (BN * 128)), map, bar[FULL + st], c * 64, BN * t, h * p.S + s);
-          else tma_load_3d(smem_u32(dst + c * (BN * 128)), map, bar[FULL + st], c * 64, h,
-                           (int)(s0 + band_lo + BN * (t - n_lt)));
-        }
-        issued = t + 1;
-      }
-      for (int t = max(0, issued - kKV); t < issued; ++t) mbar_drain(bar[FULL + t % kKV], (t / kKV) & 1);
-    }
-    if (lane == 0) mbar_drain(bar[QD_FULL], 0);
-  } else if (warp == kMmaWarp) {
-    // S = Q·Kᵀ up to two tiles ahead (a TMEM buffer is free once its row group has read it)
-    if (lane == 0 && n_tiles > 0) {
-      const uint32_t id_s = idesc_f16(kBF16, BM, BN, false, false);
-      const uint32_t q_addr = smem_u32(sm.q);
-      bool ok = mbar_wait(bar[QD_FULL], 0, abort_flag, p.status);
-      for (int t = 0; ok && t < n_tiles; ++t) {
-        const int st = t & 1, ks = t % kKV;
-        ok = mbar_wait(bar[K_FULL + ks], (t / kKV) & 1, abort_flag, p.status) &&
-             (t < 2 || mbar_wait(bar[SD_EMPTY + st], ((t >> 1) - 1) & 1, abort_flag, p.status));
-        if (!ok) break;
-        tc_fence_after();
-        const uint32_t k_addr = smem_u32(sm.k[ks]);
-#pragma unroll
-        for (int kk = 0; kk < D / 16; ++kk) {
-          const uint32_t aoff = (kk >> 2) * (BM * 128) + (kk & 3) * 32;
-          const uint32_t boff = (kk >> 2) * (BN * 128) + (kk & 3) * 32;
-          mma_f16(tS + st * BN, sdesc_sw128(q_addr + aoff, 16, 1024), sdesc_sw128(k_addr + boff, 16, 1024), id_s,
-                  kk > 0 ? 1u : 0u);
-        }
-        mma_commit(bar[SD_FULL + st]);
-        mma_commit(bar[K_EMPTY + ks]);
-      }
-      mma_commit(bar[FINAL]);
-      mbar_drain(bar[FINAL], 0);
-    }
-  } else if (warp == kMmaWarpB) {
-    // dP = dO·Vᵀ up to two tiles ahead, and dQ += dS·K once a row group has stored
-    // its tile's dS (tiles in order: the accumulation order is fixed)
-    if (lane == 0 && n_tiles > 0) {
-      const uint32_t id_s = idesc_f16(kBF16, BM, BN, false, false);
-      const uint32_t id_dq = idesc_f16(kBF16, BM, D, false, true);
-      const uint32_t do_addr = smem_u32(sm.dO);
-      bool ok = mbar_wait(bar[QD_FULL], 0, abort_flag, p.status);
-      auto issue_dp = [&](int t) -> bool {
-        const int st = t & 1, ks = t % kKV;
-        if (!mbar_wait(bar[V_FULL + ks], (t / kKV) & 1, abort_flag, p.status)) return false;
-        if (t >= 2 && !mbar_wait(bar[SD_EMPTY + st], ((t >> 1) - 1) & 1, abort_flag, p.status)) return false;
-        tc_fence_after();
-        const uint32_t v_addr = smem_u32(sm.v[ks]);
-#pragma unroll
-        for (int kk = 0; kk < D / 16; ++kk) {
-          const uint32_t aoff = (kk >> 2) * (BM * 128) + (kk & 3) * 32;
-          const uint32_t boff = (kk >> 2) * (BN * 128) + (kk & 3) * 32;
-          mma_f16(tdP + st * BN, sdesc_sw128(do_addr + aoff, 16, 1024), sdesc_sw128(v_addr + boff, 16, 1024),
-                  id_s, kk > 0 ? 1u : 0u);
-        }
-        mma_commit(bar[SD_FULL + st]);
-        mma_commit(bar[V_EMPTY + ks]);
-        return true;
-      };
-      if (ok) ok = issue_dp(0);
-      if (ok && n_tiles > 1) ok = issue_dp(1);
-      for (int t = 0; ok && t < n_tiles; ++t) {
-        const int st = t & 1, ks = t % kKV;
-        if (t + 2 < n_tiles && !(ok = issue_dp(t + 2))) break;
-        if (!(ok = mbar_wait(bar[DS_FULL + st], (t >> 1) & 1, abort_flag, p.status))) break;
-        tc_fence_after();
-        const uint32_t ds_addr = smem_u32(sm.ds[st]), k_addr = smem_u32(sm.k[ks]);
-        const int nk = tile_n(t) / 16;
-        for (int kk = 0; kk < nk; ++kk)
-          mma_f16(tdQ, sdesc_sw128(ds_addr + kk * 32, 16, 1024), sdesc_sw128(k_addr + kk * 2048, BN * 128, 1024),
-                  id_dq, (t > 0 || kk > 0) ? 1u : 0u);
-        mma_commit(bar[DS_EMPTY + st]);
-        mma_commit(bar[K_EMPTY + ks]);
-      }
-      mma_commit(bar[DQ_DONE]);
-      mma_commit(bar[FINAL + 1]);
-      mbar_drain(bar[FINAL + 1], 0);
-    }
-  } else {
-    // --------------------------------------------------------- row warps
-    // Two groups of eight warps take alternate key tiles (group = t % 2, which is
-    // also the tile's S/dP TMEM buffer and dS smem buffer), so that one group's
-    // element-wise work overlaps the other's waits; within a group, warp w reads
-    // TMEM lanes 32·(w % 4)… and owns the 32-column half (w / 4) % 2 of its tiles.
-    const uint32_t lane_addr = ((uint32_t)(32 * (warp & 3)) << 16);
-    const int grp = quarter >> 1;
-    const int ch0 = kHalfCols * (quarter & 1);  // first tile column of this thread
-    const float sl2 = p.scale * kLog2e;
-    const float inv_tau = 1.0f / p.tau_win;
-    const bool slow_edge = sm.slow_edge != 0;
-    const float nlse2 = row_live ? rh0.x : 0.f;
-    const float delta = row_live ? rh0.y : 0.f;
-    const int ne = row_live ? rec_ne : 0, ehi = rec_ehi;
-    float dw = 0.f;
-    bool ok = true;
-    for (int t = grp; t < n_tiles; t += 2) {
-      const int st = t & 1;
-      // the tile's S/dP, and its dS buffer (free once the dQ MMAs of tile t − 2 completed)
-      ok = mbar_wait(bar[SD_FULL + st], (t >> 1) & 1, abort_flag, p.status) &&
-           (t < 2 || mbar_wait(bar[DS_EMPTY + st], ((t >> 1) - 1) & 1, abort_flag, p.status));
-      if (!__all_sync(0xffffffffu, ok)) { ok = false; break; }
-      tc_fence_after();
-      const bool lmk = t < n_lt;
-      const int n0 = lmk ? 0 : band_lo + BN * (t - n_lt);
-      uint8_t* dsb = sm.ds[st];
-      bool any_in = false;
-#pragma unroll
-      for (int k = 0; k < kHalfCols / 16; ++k) {  // 16 columns at a time
-        const int c0 = ch0 + 16 * k;
-        // valid columns of this chunk: [vlo, vhi]
-        const int vlo = lmk ? 0 : lo - n0 - c0;  // lo = INT_MAX for a row without band: stays positive
-        const int vhi = lmk ? cnt - BN * t - c0 - 1 : hi - n0 - c0;
-        const bool all_in = __all_sync(0xffffffffu, vlo <= 0 && vhi >= 15);
-        const bool all_out = __all_sync(0xffffffffu, vhi < 0 || vlo > 15 || vlo > vhi);
-        uint32_t pk[8];
-        if (all_out) {
-#pragma unroll
-          for (int g = 0; g < 8; ++g) pk[g] = 0u;
-        } else {
-          any_in = true;
-          float sv[16], dpv[16];
-          tmem_ld16(tS + lane_addr + st * BN + c0, sv);
-          tmem_ld16(tdP + lane_addr + st * BN + c0, dpv);
-          tmem_wait_ld();
-          const float* lw2 = sm.lmk_lw2 + BN * t + c0;
-          // one straight-line body per (landmark tile, column mask) case: the tile
-          // kind and a warp-wide all-valid chunk are uniform, so the common case
-          // carries no per-element bias load or mask test
-          auto body = [&](auto kLmk, auto kMasked) {
-            constexpr bool kL = decltype(kLmk)::value, kM = decltype(kMasked)::value;
-            const uint32_t vmask = kM ? range_mask32(vlo, vhi) : 0xffffffffu;
-#pragma unroll
-            for (int c = 0; c < 16; c += 2) {
-              float d2[2];
-#pragma unroll
-              for (int e = 0; e < 2; ++e) {
-                const float bias = kL ? lw2[c + e] + nlse2 : nlse2;
-                const float pr = fast_exp2(fmaf(sv[c + e], sl2, bias));
-                const float dsv = pr * (dpv[c + e] - delta);
-                d2[e] = kM ? ((vmask >> (c + e)) & 1u ? dsv : 0.f) : dsv;
-              }
-              pk[c / 2] = pack2(d2[0], d2[1], kBF16);
-            }
-          };
-          using kT = std::true_type;
-          using kF = std::false_type;
-          if (lmk) {
-            if (all_in) body(kT{}, kF{}); else body(kT{}, kT{});
-          } else {
-            if (all_in) body(kF{}, kF{}); else body(kF{}, kT{});
-          }
-        }
-#pragma unroll
-        for (int g = 0; g < 2; ++g)
-          *reinterpret_cast<uint4*>(dsb + sw128_offset(r, c0 + 8 * g)) =
-              make_uint4(pk[4 * g], pk[4 * g + 1], pk[4 * g + 2], pk[4 * g + 3]);
-      }
-      // every TMEM read of the tile is done: S/dP buffer st is free for tile t + 2
-      tc_fence_before();
-      mbar_arrive(bar[SD_EMPTY + st]);
-      if (!lmk && any_in) {
-        // soft window edge on this thread's half: dS *= σ((w̃ − d)/τ); ∂loss/∂w̃ += dS·(1 − σ)/τ.
-        // The key at edge index e (distance d_e0 + e) sits in column ehi − e − n0 − ch0.
-        const int ce0 = ehi - n0 - ch0;
-        const bool has = ne > 0 && ce0 >= 0 && ce0 - (ne - 1) <= kHalfCols - 1;
-        if (!slow_edge) {
-          if (__any_sync(0xffffffffu, has)) {
-            float pv[kMaxEdge];
-#pragma unroll
-            for (int e = 0; e < kMaxEdge; ++e) {
-              const int c = ce0 - e;
-              const bool in = has && e < ne && c >= 0 && c < kHalfCols;
-              pv[e] = in ? to_f32<T>(*reinterpret_cast<const T*>(dsb + sw128_offset(r, ch0 + c))) : 0.f;
-            }
-#pragma unroll
-            for (int e = 0; e < kMaxEdge; ++e) {
-              const int c = ce0 - e;
-              if (has && e < ne && c >= 0 && c < kHalfCols) {
-                const float g = sm.eg[r][e];
-                const float v = pv[e] * g;
-                *reinterpret_cast<T*>(dsb + sw128_offset(r, ch0 + c)) = from_f32<T>(v);
-                dw = fmaf(v, (1.0f - g) * inv_tau, dw);
-              }
-            }
-          }
-        } else if (has) {
-          // edges wider than the precomputed factors: key by key
-          for (int e = max(0, ce0 - (kHalfCols - 1)); e < ne && ce0 - e >= 0; ++e) {
-            const int c = ce0 - e;
-            T* ep = reinterpret_cast<T*>(dsb + sw128_offset(r, ch0 + c));
-            const float sg = e < kMaxEdge ? sm.eg[r][e] : qrec_edge_factor(rh1.w, i - ehi + e, inv_tau);
-            const float v = to_f32<T>(*ep) * sg;
-            *ep = from_f32<T>(v);
-            dw = fmaf(v, (1.0f - sg) * inv_tau, dw);
-          }
-        }
-      }
-      fence_async_smem();
-      mbar_arrive(bar[DS_FULL + st]);
-    }
-    if (ok && n_tiles > 0) {
-      ok = mbar_wait(bar[DQ_DONE], 0, abort_flag, p.status);
-      ok = __all_sync(0xffffffffu, ok);
-      tc_fence_after();
-    }
-    // ∂loss/∂w̃ of the row: sum of the four column quarters, in quarter order
-    sm.dw_part[quarter][r] = dw;
-    mbar_arrive(bar[EPI]);
-    const bool ok2 = mbar_wait(bar[EPI], 0, abort_flag, p.status);
-    if (quarter == 0 && row_ok && p.dw_head)
-      p.dw_head[(s0 + i) * p.H + h] =
-          (ok && ok2) ? (sm.dw_part[0][r] + sm.dw_part[1][r]) + (sm.dw_part[2][r] + sm.dw_part[3][r]) : 0.f;
-    if (ok && ok2) {
-      // dQ rows staged in the (now idle) K ring, 16-byte units XOR-swizzled by
-      // row % 8, then stored row-contiguously
-      constexpr int kUnits = D * 2 / 16;
-      uint8_t* stage = sm.k[0];
-#pragma unroll
-      for (int ch = 0; ch < D / 64; ++ch) {  // 16 columns at a time
-        const int col = quarter * (D / 4) + ch * 16;
-        float o[16];
-        if (n_tiles > 0) {
-          tmem_ld16(tdQ + lane_addr + col, o);
-          tmem_wait_ld();
-        } else {
-#pragma unroll
-          for (int j = 0; j < 16; ++j) o[j] = 0.f;
-        }
-#pragma unroll
-        for (int j = 0; j < 16; j += 8) {
-          const int un = (col + j) / 8;
-          uint4 u;
-          u.x = pack2(o[j + 0] * p.scale, o[j + 1] * p.scale, kBF16);
-          u.y = pack2(o[j + 2] * p.scale, o[j + 3] * p.scale, kBF16);
-          u.z = pack2(o[j + 4] * p.scale, o[j + 5] * p.scale, kBF16);
-          u.w = pack2(o[j + 6] * p.scale, o[j + 7] * p.scale, kBF16);
-          *reinterpret_cast<uint4*>(stage + r * (kUnits * 16) + ((un ^ (r & 7)) << 4)) = u;
-        }
-      }
-      mbar_arrive(bar[EPI2]);
-      if (__all_sync(0xffffffffu, mbar_wait(bar[EPI2], 0, abort_flag, p.status))) {
-        const int rows = min(BM, L - m0);
-        const int64_t HD = (int64_t)p.H * D;
-        uint8_t* dqg = reinterpret_cast<uint8_t*>(p.dq) + ((s0 + m0) * HD + (int64_t)h * D) * 2;
-        for (int un = tid; un < rows * kUnits; un += kRowThreads) {
-          const int rr = un / kUnits, uu = un % kUnits;
-          *reinterpret_cast<uint4*>(dqg + rr * HD * 2 + uu * 16) =
-              *reinterpret_cast<const uint4*>(stage + rr * (kUnits * 16) + ((uu ^ (rr & 7)) << 4));
-        }
-      }
-    }
-  }
-  tc_fence_before();
-  __syncthreads();
-  tc_fence_after();
-  if (warp == kMmaWarp) tmem_dealloc(tmem, 512);
-}
-}  // namespace dq
 
 // ==================================================================== dK / dV
 namespace dkv {
@@ -567,6 +126,7 @@ static_assert(2 * BM * BN * 2 >= BM * 128 * 2, "the Pᵀ/dSᵀ buffers hold one 
 // Every role of the persistent CTA decodes the same items in the same order.
 struct Item {
   int h, s, key0, nkeys, q_start, n_tiles, part, L;
+  int blk, chunk, u0;  // band: block_map index; landmark: 128-slot chunk and its first query tile
   int64_t s0, lbase;
 };
 
@@ -603,17 +163,27 @@ __device__ __forceinline__ Item decode_item(const DsaltAttnParams& p, int idx) {
       nv += __popc(__ballot_sync(0xffffffffu, v));
     }
     it.nkeys = nv;
-    it.q_start = nv > 0 ? __ldg(p.pos_sorted + it.lbase + it.key0) : 0;
-    const int q_end = it.L - 1;
-    int n = (nv > 0 && q_end >= it.q_start) ? (q_end - it.q_start + BN) / BN : 0;
-    const int per = (n + DSALT_LMK_SPLIT - 1) / DSALT_LMK_SPLIT;
+    it.chunk = chunk;
+    it.blk = 0;
+    // query tiles from the 128-query block of the first slot's position to the
+    // sequence end (aligned to the dQ stage's query blocks; the columns before
+    // the first slot attend nothing), split into DSALT_LMK_SPLIT parts of whole
+    // tile pairs
+    const int first = nv > 0 ? __ldg(p.pos_sorted + it.lbase + it.key0) : 0;
+    const int qs = (first / BM) * BM;
+    const int n = nv > 0 ? (it.L - qs + BN - 1) / BN : 0;
+    const int per = ((n + DSALT_LMK_SPLIT - 1) / DSALT_LMK_SPLIT + 1) & ~1;
     const int u0 = per * it.part;
     it.n_tiles = max(0, min(n, u0 + per) - u0);
-    it.q_start += BN * u0;
+    it.u0 = u0;
+    it.q_start = qs + BN * u0;
   } else {
     const int nb = __ldg(p.num_blocks);
     const int blk = idx % nb;
     it.h = idx / nb;
+    it.blk = blk;
+    it.chunk = 0;
+    it.u0 = 0;
     it.s = __ldg(p.block_map + 2 * blk);
     it.s0 = __ldg(p.cu_seqlens + it.s);
     it.L = (int)(__ldg(p.cu_seqlens + it.s + 1) - it.s0);
@@ -625,6 +195,23 @@ __device__ __forceinline__ Item decode_item(const DsaltAttnParams& p, int idx) {
     it.n_tiles = q_end >= it.q_start ? (q_end - it.q_start + BN) / BN : 0;
   }
   return it;
+}
+
+// Index of tile u of an item in the ds_tiles scratch (the dQ stage's layout,
+// attn_tc_dq.cu): band tiles per (head, block_map index), landmark tiles per
+// (head, sequence, chunk) counted from the chunk's first query block; -1 when
+// the caller's ds_band_tiles / ds_lmk_tiles leave no room for it.
+template <bool LMK>
+__device__ __forceinline__ int64_t ds_tile_index(const DsaltAttnParams& p, const Item& it, int u) {
+  if (LMK) {
+    const int ul = it.u0 + u;
+    if (ul >= p.ds_lmk_tiles) return -1;
+    const int nch = (p.kp + BM - 1) / BM;
+    return (int64_t)p.H * p.max_blocks * p.ds_band_tiles +
+           (((int64_t)it.h * p.S + it.s) * nch + it.chunk) * p.ds_lmk_tiles + ul;
+  }
+  if (u >= p.ds_band_tiles) return -1;
+  return ((int64_t)it.h * p.max_blocks + it.blk) * p.ds_band_tiles + u;
 }
 
 template <bool LMK, typename T, int D>
@@ -659,7 +246,7 @@ __global__ void __launch_bounds__(kThreadsKV, 1) tc_bwd_dkdv_kernel(const __grid
       mbar_init(bar[SD_EMPTY + st], kRowThreads);
     }
     mbar_init(bar[PDS_FULL], kRowThreads);
-    mbar_init(bar[PDS_EMPTY], 2);
+    mbar_init(bar[PDS_EMPTY], 3);  // the dV and dK MMAs, and the store of the dSᵀ tile
     mbar_init(bar[ROWS], kRowThreads);
     mbar_init(bar[KV_DONE], 2);
     mbar_init(bar[ACC_EMPTY], kRowThreads);
@@ -881,6 +468,19 @@ __global__ void __launch_bounds__(kThreadsKV, 1) tc_bwd_dkdv_kernel(const __grid
                (u > 0 || gi == 0 || mbar_wait(bar[ACC_EMPTY], (gi - 1) & 1, abort_flag, p.status));
           if (!ok) break;
           tc_fence_after();
+          // warp B also copies the finished dSᵀ tile to the scratch for the dQ stage
+          bool stored = false;
+          if (!is_a && p.ds_tiles) {
+            const int64_t ti = ds_tile_index<LMK>(p, it, u);
+            if (ti >= 0) {
+              bulk_store(reinterpret_cast<uint8_t*>(p.ds_tiles) + ti * DSALT_DS_TILE_BYTES, smem_u32(sm.dst),
+                         DSALT_DS_TILE_BYTES);
+              bulk_commit();
+              stored = true;
+            } else {
+              flag_status(p.status, DSALT_DEV_BAD_INDEX);
+            }
+          }
           const uint32_t ba = tile_acc(qs);
 #pragma unroll
           for (int kk = 0; kk < BN / 16; ++kk)
@@ -888,6 +488,10 @@ __global__ void __launch_bounds__(kThreadsKV, 1) tc_bwd_dkdv_kernel(const __grid
                     id_kv, (u > 0 || kk > 0) ? 1u : 0u);
           mma_commit(bar[PDS_EMPTY]);
           mma_commit(bar[QDO_EMPTY + qs]);
+          if (!is_a) {
+            if (stored) bulk_wait_read0();  // the buffer is read: the rows may overwrite it
+            mbar_arrive(bar[PDS_EMPTY]);
+          }
           if (u + 2 < n) {
             ok = issue_sd(g + 2);
             if (ok && u + 2 == n - 1) mma_commit(bar[KV_EMPTY]);
@@ -900,9 +504,10 @@ __global__ void __launch_bounds__(kThreadsKV, 1) tc_bwd_dkdv_kernel(const __grid
       ++gi;
     }
     if (lane == 0) {
-      // every issued MMA completes before TMEM is released
+      // every issued MMA completes before TMEM is released, every tile store before the exit
       mma_commit(bar[FINAL + (is_a ? 0 : 1)]);
       mbar_drain(bar[FINAL + (is_a ? 0 : 1)], 0);
+      if (!is_a) bulk_wait_all();
     }
   } else {
     // ---------------------------------------------------- key-row warps (Pᵀ, dSᵀ)
@@ -1039,33 +644,44 @@ __global__ void __launch_bounds__(kThreadsKV, 1) tc_bwd_dkdv_kernel(const __grid
           ok = mbar_wait(bar[ROWS], rows_phase & 1, abort_flag, p.status);
           ++rows_phase;
           if (!__all_sync(0xffffffffu, ok)) { ok = false; break; }
-          const int col = tid & (BN - 1);
+          // eight consecutive lanes per query column: column tid / 8, edge index tid % 8
+          const int col = tid >> 3, e = tid & 7;
           const QRec& rc = sm.rec[cs][col];
           const int ne = qrec_ne(rc), ehi = rc.ehi;
+          float dwc = 0.f;  // ∂loss/∂w̃ part of this element: dS·(1 − σ)/τ
           {
-            const int e = tid >> 6;
             const int rr = ehi - e - key0;
             if (e < ne && rr >= 0 && rr < nkeys) {
               const uint32_t off = sw128_offset(rr, col);
               const float a1 = to_f32<T>(*reinterpret_cast<const T*>(sm.pt + off));
               const float a2 = to_f32<T>(*reinterpret_cast<const T*>(sm.dst + off));
               const float gf = rc.eg[e];
+              const float v = a2 * gf;
               *reinterpret_cast<T*>(sm.pt + off) = from_f32<T>(a1 * gf);
-              *reinterpret_cast<T*>(sm.dst + off) = from_f32<T>(a2 * gf);
+              *reinterpret_cast<T*>(sm.dst + off) = from_f32<T>(v);
+              dwc = v * (1.0f - gf) * inv_tau;
             }
           }
-          if (tid < BN && ne > kMaxEdge) {
+          // the column's sum over its eight lanes, in a fixed order
+          dwc += __shfl_xor_sync(0xffffffffu, dwc, 1);
+          dwc += __shfl_xor_sync(0xffffffffu, dwc, 2);
+          dwc += __shfl_xor_sync(0xffffffffu, dwc, 4);
+          if (e == 0 && ne > 0) {
             // wider soft edges than the precomputed factors: the rest one key at a time
-            for (int e = kMaxEdge; e < ne; ++e) {
-              const int rr = ehi - e - key0;
+            for (int e2 = kMaxEdge; e2 < ne; ++e2) {
+              const int rr = ehi - e2 - key0;
               if (rr < 0) break;
               if (rr >= nkeys) continue;
-              const float sg = qrec_edge_factor(rc.wt, rc.qi - (ehi - e), inv_tau);
+              const float sg = qrec_edge_factor(rc.wt, rc.qi - (ehi - e2), inv_tau);
               T* e1 = reinterpret_cast<T*>(sm.pt + sw128_offset(rr, col));
-              T* e2 = reinterpret_cast<T*>(sm.dst + sw128_offset(rr, col));
+              T* ep2 = reinterpret_cast<T*>(sm.dst + sw128_offset(rr, col));
+              const float v = to_f32<T>(*ep2) * sg;
               *e1 = from_f32<T>(to_f32<T>(*e1) * sg);
-              *e2 = from_f32<T>(to_f32<T>(*e2) * sg);
+              *ep2 = from_f32<T>(v);
+              dwc += v * (1.0f - sg) * inv_tau;
             }
+            if (p.dw_head && rc.elo <= key0 + nkeys - 1 && ehi >= key0)
+              atomicAdd(p.dw_head + (s0 + rc.qi) * p.H + h, dwc);
           }
         }
         fence_async_smem();
@@ -1245,21 +861,6 @@ static bool make_args(BwdArgs& a, const DsaltAttnParams& p, int rows_q, int rows
   return true;
 }
 
-template <typename T, int D>
-cudaError_t launch_dq(const DsaltAttnParams& p, cudaStream_t st) {
-  BwdArgs a;
-  if (!make_args<T, D>(a, p, dq::BM, dq::BN, dq::BN)) return cudaErrorInvalidValue;
-  // at least ~116 KB so that one CTA (and its 512 TMEM columns) owns the SM
-  const size_t smem = std::max(sizeof(dq::Smem<D>) + 1024, (size_t)(116 * 1024));
-  cudaError_t e = cudaFuncSetAttribute(dq::tc_bwd_dq_kernel<T, D>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-  if (e != cudaSuccess) return e;
-  dq::tc_bwd_dq_kernel<T, D><<<dim3((unsigned)p.max_blocks, (unsigned)p.H), dq::kThreadsDQ, smem, st>>>(a);
-  e = cudaGetLastError();
-  if (e != cudaSuccess) return e;
-  if (p.dw && p.dw_head) return simt_attention_stage(4, p, st);  // dw = Σ_h dw_head
-  return cudaSuccess;
-}
-
 // Non-blocking stream per device on which the landmark pass runs next to the band
 // pass (forked from and joined back into the caller's stream with events).
 static cudaError_t side_stream(cudaStream_t* out) {
@@ -1305,6 +906,13 @@ cudaError_t launch_dkdv(const DsaltAttnParams& p, float* lmk_scratch, cudaStream
   a.band_lmk = lmk_scratch ? a.dlw_lmk + DSALT_LMK_SPLIT * a.part_stride : nullptr;
   const size_t smem = std::max(sizeof(dkv::Smem<D>) + 1024, (size_t)(116 * 1024));
   cudaError_t e;
+  if (p.ds_tiles) {
+    // the all-zero tile the dQ stage reads in place of a tile that was never stored
+    const int64_t zero = DSALT_DS_TILES(p.H, p.max_blocks, p.S, p.kp, p.ds_band_tiles, p.ds_lmk_tiles) - 1;
+    e = cudaMemsetAsync(reinterpret_cast<uint8_t*>(p.ds_tiles) + zero * DSALT_DS_TILE_BYTES, 0,
+                        DSALT_DS_TILE_BYTES, st);
+    if (e != cudaSuccess) return e;
+  }
   const bool lmk = p.kp > 0 && p.S > 0;
   // the landmark pass (under-filled grid) runs on a side stream next to the band pass
   cudaEvent_t fork = nullptr, join = nullptr;
@@ -1364,10 +972,7 @@ cudaError_t launch_dkdv(const DsaltAttnParams& p, float* lmk_scratch, cudaStream
 // the band pass's fp32 rows of the keys that hold landmark slots.
 cudaError_t tc_bwd_stage(int stage, const DsaltAttnParams& p, float* lmk_scratch, cudaStream_t st) {
   const bool bf = p.dtype == DSALT_BF16;
-  if (stage == 3) {
-    if (bf) return p.D == 64 ? bwd::launch_dq<__nv_bfloat16, 64>(p, st) : bwd::launch_dq<__nv_bfloat16, 128>(p, st);
-    return p.D == 64 ? bwd::launch_dq<__half, 64>(p, st) : bwd::launch_dq<__half, 128>(p, st);
-  }
+  if (stage == 3) return tc_bwd_dq_stage(p, st);
   if (stage == 2) {
     if (p.kp > 0 && !lmk_scratch) return cudaErrorInvalidValue;
     if (bf) return p.D == 64 ? bwd::launch_dkdv<__nv_bfloat16, 64>(p, lmk_scratch, st)

@@ -99,6 +99,11 @@ static int run_attn(const DsaltAttnParams* p, int stage, void* stream) {
   } else if (p->impl == DSALT_IMPL_AUTO) {
     use_tc = p->dtype != DSALT_F32 && tc_supported(*p);
   }
+  if (use_tc && (stage == 2 || stage == 3)) {
+    // the dSᵀ tile scratch that the dK/dV stage fills and the dQ stage reads
+    if (!p->ds_tiles || p->ds_band_tiles <= 0 || (p->kp > 0 && p->ds_lmk_tiles <= 0)) return DSALT_ERR_ARG;
+    if (((uintptr_t)p->ds_tiles & 1023u) != 0) return DSALT_ERR_ALIGN;
+  }
   cudaError_t e = use_tc ? tc_attention_stage(stage, *p, s) : simt_attention_stage(stage, *p, s);
   return status_of(e);
 }

@@ -21,9 +21,15 @@ F16, BF16, F32 = 0, 1, 2
 TRAIN, INFER = 0, 1
 IMPL_AUTO, IMPL_SIMT, IMPL_TCGEN05 = 0, 1, 2
 DEV_WAIT_TIMEOUT, DEV_BAD_INDEX = 1, 2
-ABI_VERSION = 4
+ABI_VERSION = 5
 QREC_FLOATS = 16  # DSALT_QREC_FLOATS
 LMK_SPLIT = 4  # DSALT_LMK_SPLIT
+DS_TILE_BYTES = 16384  # DSALT_DS_TILE_BYTES
+
+
+def ds_tiles(H: int, max_blocks: int, S: int, kp: int, band_tiles: int, lmk_tiles: int) -> int:
+    """DSALT_DS_TILES: dSᵀ tiles of the tensor-core backward's scratch."""
+    return H * max_blocks * band_tiles + H * S * ((kp + 127) // 128) * lmk_tiles + 1
 
 _c_void_p = ctypes.c_void_p
 _i32 = ctypes.c_int32
@@ -56,9 +62,10 @@ class AttnParams(ctypes.Structure):
                 ("o", _c_void_p), ("o_f32", _c_void_p), ("lse", _c_void_p),
                 ("dout", _c_void_p), ("dout_f32", _c_void_p), ("delta", _c_void_p), ("dq", _c_void_p), ("dk", _c_void_p),
                 ("dv", _c_void_p), ("dw_head", _c_void_p), ("dw", _c_void_p), ("d_lw", _c_void_p),
-                ("lmk_grad", _c_void_p), ("qrec", _c_void_p), ("status", _c_void_p),
+                ("lmk_grad", _c_void_p), ("qrec", _c_void_p), ("ds_tiles", _c_void_p), ("status", _c_void_p),
                 ("T", _i64), ("H", _i32), ("D", _i32), ("S", _i32), ("k_lmk", _i32), ("kp", _i32),
-                ("max_blocks", _i32), ("scale", _f32), ("tau_win", _f32), ("win_edge", _f32),
+                ("max_blocks", _i32), ("ds_band_tiles", _i32), ("ds_lmk_tiles", _i32),
+                ("scale", _f32), ("tau_win", _f32), ("win_edge", _f32),
                 ("semantics", _i32), ("dtype", _i32), ("impl", _i32)]
 
 

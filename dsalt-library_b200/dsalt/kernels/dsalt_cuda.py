@@ -78,11 +78,60 @@ class Prepared:
     perm: torch.Tensor
     lmk_slot: torch.Tensor
     max_blocks: int
+    lmax: int = 0                # longest sequence (host)
+    wmax_slot: int = -1          # slot of the widest band in the pinned ring (-1: none)
+    wmax_gen: int = 0
+
+
+# The widest band of a batch (max over the sequences of seq_wmax) sizes the dSᵀ tile
+# scratch of the backward.  The forward copies it into a small ring of pinned host
+# slots right after the schedule kernel and records an event; the backward reads it
+# once that event has completed, which in practice it has (the backward is enqueued
+# long after the forward's first kernel), so the host never waits on the device.
+_WMAX_RING = 64
+_WMAX: dict = {}
+
+
+def _wmax_ring(dev: torch.device):
+    key = dev.index if dev.index is not None else torch.cuda.current_device()
+    r = _WMAX.get(key)
+    if r is None:
+        r = {"host": torch.zeros(_WMAX_RING, dtype=torch.int32).pin_memory(),
+             "events": [torch.cuda.Event() for _ in range(_WMAX_RING)], "gen": [0] * _WMAX_RING, "next": 0}
+        _WMAX[key] = r
+    return r
+
+
+def _record_wmax(prep: "Prepared", dev: torch.device) -> None:
+    if torch.cuda.is_current_stream_capturing():
+        return  # a captured graph replays without the host: the backward uses the length bound
+    r = _wmax_ring(dev)
+    slot = r["next"]
+    r["next"] = (slot + 1) % _WMAX_RING
+    r["gen"][slot] += 1
+    r["host"][slot:slot + 1].copy_(prep.seq_wmax[:max(prep.S, 1)].amax().reshape(1), non_blocking=True)
+    r["events"][slot].record()
+    prep.wmax_slot, prep.wmax_gen = slot, r["gen"][slot]
+
+
+def widest_band(prep: "Prepared", dev: torch.device) -> int:
+    """Upper bound of max_s seq_wmax[s] for sizing the backward's tile scratch."""
+    r = _WMAX.get(dev.index if dev.index is not None else torch.cuda.current_device())
+    if prep.wmax_slot >= 0 and r is not None and r["gen"][prep.wmax_slot] == prep.wmax_gen \
+            and not torch.cuda.is_current_stream_capturing():
+        r["events"][prep.wmax_slot].synchronize()
+        return max(int(r["host"][prep.wmax_slot]), 0)
+    # no recorded value (captured, or the ring moved on): a band never exceeds its sequence
+    return max(prep.lmax - 1, 0)
 
 
 def prepare(k_c: torch.Tensor, v_c: torch.Tensor, lmk_pos: torch.Tensor, lmk_w: torch.Tensor,
-            w: torch.Tensor, cu_seqlens: torch.Tensor, semantics: int) -> Prepared:
-    """Build the schedule and the sorted landmark buffers on the device."""
+            w: torch.Tensor, cu_seqlens: torch.Tensor, semantics: int, cu_host=None,
+            for_backward: bool = False) -> Prepared:
+    """Build the schedule and the sorted landmark buffers on the device.
+
+    ``cu_host``: the host copy of ``cu_seqlens`` when the caller has one;
+    ``for_backward``: record the widest band for the backward's scratch."""
     T, H, D = k_c.shape
     dev = k_c.device
     cu = cu_seqlens.to(device=dev, dtype=torch.int32).contiguous()
@@ -123,8 +172,14 @@ def prepare(k_c: torch.Tensor, v_c: torch.Tensor, lmk_pos: torch.Tensor, lmk_w: 
         _ext.call("dsalt_gather_landmarks", gp)
     else:
         lmk_slot.fill_(-1)
-    return Prepared(T, H, D, S, k_lmk, kp, semantics, cu, w32, block_map, num_blocks, seq_wmax,
-                    lmk_k, lmk_v, pos_sorted, w_sorted, perm, lmk_slot, max_blocks)
+    if cu_host is None:
+        cu_host = [int(c) for c in cu.to("cpu").tolist()]
+    lmax = max((b - a for a, b in zip(cu_host[:-1], cu_host[1:])), default=0)
+    prep = Prepared(T, H, D, S, k_lmk, kp, semantics, cu, w32, block_map, num_blocks, seq_wmax,
+                    lmk_k, lmk_v, pos_sorted, w_sorted, perm, lmk_slot, max_blocks, lmax)
+    if for_backward and T > 0:
+        _record_wmax(prep, dev)
+    return prep
 
 
 def _params(prep: Prepared, q_c, k_c, v_c, tau_win: float, win_edge: float, impl: int,
@@ -191,38 +246,18 @@ def backward(grad_out, q_c, k_c, v_c, o, lse, prep: Prepared, tau_win: float, wi
     p = _params(prep, q_c, k_c, v_c, tau_win, win_edge, impl, scale, o=o, lse=lse, dout=do_c, dout_f32=do_f32,
                 delta=delta, dq=dq, dk=dk, dv=dv, dw_head=dw_head, dw=dw, d_lw=d_lw, lmk_grad=lmk_grad,
                 qrec=qrec)
+    # the dSᵀ tiles the dK/dV stage stores for the dQ stage (tensor-core family)
+    band_tiles = (BLOCK_M + widest_band(prep, dev) + 63) // 64
+    lmk_tiles = (prep.lmax + 63) // 64 + 1
+    n_tiles = _ext.ds_tiles(H, prep.max_blocks, prep.S, prep.kp, band_tiles, lmk_tiles)
+    ds = torch.empty(n_tiles * _ext.DS_TILE_BYTES + 1024, dtype=torch.uint8, device=dev)
+    p.ds_tiles = ds.data_ptr() + (-ds.data_ptr()) % 1024
+    p.ds_band_tiles, p.ds_lmk_tiles = band_tiles, lmk_tiles
     _ext.call("dsalt_attn_bwd_preprocess", p)
-    # dK/dV and dQ are independent once Δ and the records exist: dQ runs on a side
-    # stream so that each kernel's tail waves (and the under-filled landmark pass)
-    # overlap the other's work
-    if not CONCURRENT_BACKWARD:
-        _ext.call("dsalt_attn_bwd_dkdv", p)
-        _ext.call("dsalt_attn_bwd_dq", p)
-        return dq, dk, dv, d_lw, dw
-    main = torch.cuda.current_stream(dev)
-    side = _side_stream(dev)
-    side.wait_stream(main)
-    with torch.cuda.stream(side):
-        _ext.call("dsalt_attn_bwd_dq", p)
+    # dQ multiplies the dSᵀ tiles that dK/dV stores: one after the other
     _ext.call("dsalt_attn_bwd_dkdv", p)
-    main.wait_stream(side)
+    _ext.call("dsalt_attn_bwd_dq", p)
     return dq, dk, dv, d_lw, dw
-
-
-# dK/dV and dQ on two streams (True); False runs them one after the other on the
-# caller's stream, e.g. to time each kernel alone
-CONCURRENT_BACKWARD = True
-
-
-_SIDE_STREAMS: dict = {}
-
-
-def _side_stream(dev: torch.device) -> torch.cuda.Stream:
-    key = dev.index if dev.index is not None else torch.cuda.current_device()
-    st = _SIDE_STREAMS.get(key)
-    if st is None:
-        st = _SIDE_STREAMS[key] = torch.cuda.Stream(device=dev)
-    return st
 
 
 def compute_dtype(q: torch.Tensor) -> torch.dtype:

@@ -33,14 +33,16 @@ class DSALTAttentionFunction(torch.autograd.Function):
     @staticmethod
     def forward(ctx, q, k, v, lmk_indices, lmk_bias, w_sizes, cu_seqlens):
         _cuda.check_inputs(q, k, v, cu_seqlens)
-        _validate_cu(_host_cu(cu_seqlens, None), q.shape[0])
+        cu_host = _host_cu(cu_seqlens, None)
+        _validate_cu(cu_host, q.shape[0])
         dt = _cuda.compute_dtype(q)
         q_c = q.contiguous().to(dt)
         k_c = k.contiguous().to(dt)
         v_c = v.contiguous().to(dt)
         impl = _ext.default_impl()
         with torch.no_grad():
-            prep = _cuda.prepare(k_c, v_c, lmk_indices, lmk_bias, w_sizes, cu_seqlens, _ext.INFER)
+            prep = _cuda.prepare(k_c, v_c, lmk_indices, lmk_bias, w_sizes, cu_seqlens, _ext.INFER,
+                                 cu_host=cu_host, for_backward=any(ctx.needs_input_grad))
             o, o_f32, lse = _cuda.forward(q_c, k_c, v_c, prep, 1.0, 0.0, impl)
         ctx.save_for_backward(q_c, k_c, v_c, o, lse)
         ctx.prep = prep

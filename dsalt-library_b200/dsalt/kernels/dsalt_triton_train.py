@@ -49,14 +49,16 @@ def _validate_cu(cu, T: int) -> None:
 def _train_forward(ctx, q, k, v, lmk_pos, lmk_logw, w_cont, cu_seqlens, tau_win, win_edge, cu_list, f32_out):
     _cuda.check_inputs(q, k, v, cu_seqlens)
     total_len = q.shape[0]
-    _validate_cu(_host_cu(cu_seqlens, cu_list), total_len)
+    cu_host = _host_cu(cu_seqlens, cu_list)
+    _validate_cu(cu_host, total_len)
     dt = _cuda.compute_dtype(q)
     q_c = q.contiguous().to(dt)
     k_c = k.contiguous().to(dt)
     v_c = v.contiguous().to(dt)
     impl = _ext.default_impl()
     with torch.no_grad():
-        prep = _cuda.prepare(k_c, v_c, lmk_pos, lmk_logw, w_cont, cu_seqlens, _ext.TRAIN)
+        prep = _cuda.prepare(k_c, v_c, lmk_pos, lmk_logw, w_cont, cu_seqlens, _ext.TRAIN, cu_host=cu_host,
+                             for_backward=any(ctx.needs_input_grad))
         o, o_out, lse = _cuda.forward(q_c, k_c, v_c, prep, float(tau_win), float(win_edge), impl, f32_out=f32_out)
     ctx.save_for_backward(q_c, k_c, v_c, o, lse)
     ctx.prep = prep

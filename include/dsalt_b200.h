@@ -29,7 +29,7 @@
 extern "C" {
 #endif
 
-#define DSALT_B200_ABI_VERSION 4
+#define DSALT_B200_ABI_VERSION 5
 
 /* The tensor-core dK/dV stage splits each landmark chunk's query range into
  * this many parts that run as separate CTAs; their fp32 partial sums are added
@@ -38,6 +38,13 @@ extern "C" {
 
 /* fp32 words per query record of the backward (DsaltAttnParams.qrec) */
 #define DSALT_QREC_FLOATS 16
+/* dSᵀ tiles of the tensor-core backward (ds_tiles below): 128 x 64 16-bit
+ * elements; band tiles per (head, key block), landmark tiles per (head,
+ * sequence, 128-slot chunk), and one all-zero tile at the end.              */
+#define DSALT_DS_TILE_BYTES 16384
+#define DSALT_DS_TILES(H, max_blocks, S, kp, band_tiles, lmk_tiles)                        \
+  ((int64_t)(H) * (max_blocks) * (band_tiles) +                                             \
+   (int64_t)(H) * (S) * (((kp) + 127) / 128) * (lmk_tiles) + 1)
 
 /* ---- status codes ------------------------------------------------------ */
 enum {
@@ -161,13 +168,26 @@ typedef struct DsaltAttnParams {
                                  rows of landmark keys); unused by the SIMT family */
   float* qrec;                /* [H,T,DSALT_QREC_FLOATS] fp32 scratch: per-query records
                                  (LSE, Delta, window, soft-edge factors) written by the
-                                 preprocess stage and read by the tensor-core dK/dV and dQ
-                                 stages; unused by the SIMT family */
+                                 preprocess stage and read by the tensor-core dK/dV
+                                 stage; unused by the SIMT family */
+  void* ds_tiles;             /* scratch of the tensor-core backward, 1024-byte aligned:
+                                 the dK/dV stage stores every dSᵀ tile it computes
+                                 (dtype, 128 keys x 64 queries, DSALT_DS_TILE_BYTES each,
+                                 after the soft edge) and the dQ stage multiplies them
+                                 with K, so dQ needs no recomputation of S and dP.
+                                 DSALT_DS_TILES(H, max_blocks, S, kp, ds_band_tiles,
+                                 ds_lmk_tiles) tiles; unused by the SIMT family */
   int32_t* status;            /* device status word or NULL */
   /* sizes */
   int64_t T;
   int32_t H, D, S, k_lmk, kp;
   int32_t max_blocks;
+  int32_t ds_band_tiles;      /* 64-query tiles stored per key block: at least
+                                 ceil((128 + max_s seq_wmax[s]) / 64) (the widest band
+                                 item); a key block that needs more flags
+                                 DSALT_DEV_BAD_INDEX */
+  int32_t ds_lmk_tiles;       /* 64-query tiles stored per landmark chunk: at least
+                                 ceil(longest sequence / 64) + 1 */
   float scale;                /* 1/sqrt(D) */
   float tau_win, win_edge;
   int32_t semantics;          /* DSALT_TRAIN / DSALT_INFER */

@@ -597,7 +597,7 @@ cudaError_t launch_tc_fwd(const DsaltAttnParams& p, cudaStream_t stream) {
     return cudaErrorInvalidValue;
   // at least ~116 KB so that one CTA (and its 512 TMEM columns) owns the SM
   const size_t smem = std::max(sizeof(FwdSmem<D>) + 1024, (size_t)(116 * 1024));
-  cudaError_t e = cudaFuncSetAttribute(tc_fwd_kernel<T, D>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  cudaError_t e = ensure_smem((const void*)tc_fwd_kernel<T, D>, smem);
   if (e != cudaSuccess) return e;
   dim3 grid((unsigned)p.max_blocks, (unsigned)p.H);
   tc_fwd_kernel<T, D><<<grid, kThreads, smem, stream>>>(a);

@@ -862,10 +862,13 @@ static bool make_args(BwdArgs& a, const DsaltAttnParams& p, int rows_q, int rows
 }
 
 // Non-blocking stream per device on which the landmark pass runs next to the band
-// pass (forked from and joined back into the caller's stream with events).
-static cudaError_t side_stream(cudaStream_t* out) {
+// pass, and the two events that fork it from and join it back into the caller's
+// stream; created once per device and reused (a wait uses the event's latest
+// record), so the entry point is meant for one host thread per device.
+static cudaError_t side_stream(cudaStream_t* out, cudaEvent_t* fork, cudaEvent_t* join) {
   static std::mutex mu;
   static cudaStream_t streams[64] = {};
+  static cudaEvent_t forks[64] = {}, joins[64] = {};
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return e;
@@ -873,9 +876,16 @@ static cudaError_t side_stream(cudaStream_t* out) {
   std::lock_guard<std::mutex> lock(mu);
   if (!streams[dev]) {
     e = cudaStreamCreateWithFlags(&streams[dev], cudaStreamNonBlocking);
-    if (e != cudaSuccess) return e;
+    if (e == cudaSuccess) e = cudaEventCreateWithFlags(&forks[dev], cudaEventDisableTiming);
+    if (e == cudaSuccess) e = cudaEventCreateWithFlags(&joins[dev], cudaEventDisableTiming);
+    if (e != cudaSuccess) {
+      streams[dev] = nullptr;
+      return e;
+    }
   }
   *out = streams[dev];
+  *fork = forks[dev];
+  *join = joins[dev];
   return cudaSuccess;
 }
 
@@ -918,14 +928,11 @@ cudaError_t launch_dkdv(const DsaltAttnParams& p, float* lmk_scratch, cudaStream
   cudaEvent_t fork = nullptr, join = nullptr;
   if (lmk) {
     cudaStream_t side;
-    e = side_stream(&side);
-    if (e == cudaSuccess) e = cudaEventCreateWithFlags(&fork, cudaEventDisableTiming);
-    if (e == cudaSuccess) e = cudaEventCreateWithFlags(&join, cudaEventDisableTiming);
+    e = side_stream(&side, &fork, &join);
     if (e == cudaSuccess) e = cudaEventRecord(fork, st);
     if (e == cudaSuccess) e = cudaStreamWaitEvent(side, fork, 0);
     if (e == cudaSuccess)
-      e = cudaFuncSetAttribute(dkv::tc_bwd_dkdv_kernel<true, T, D>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                               (int)smem);
+      e = ensure_smem((const void*)dkv::tc_bwd_dkdv_kernel<true, T, D>, smem);
     if (e == cudaSuccess) {
       const int nch = (p.kp + dkv::BM - 1) / dkv::BM;
       const unsigned items = (unsigned)(p.S * nch * DSALT_LMK_SPLIT * p.H);  // one item per CTA
@@ -933,13 +940,9 @@ cudaError_t launch_dkdv(const DsaltAttnParams& p, float* lmk_scratch, cudaStream
       e = cudaGetLastError();
     }
     if (e == cudaSuccess) e = cudaEventRecord(join, side);
-    if (e != cudaSuccess) {
-      if (fork) cudaEventDestroy(fork);
-      if (join) cudaEventDestroy(join);
-      return e;
-    }
+    if (e != cudaSuccess) return e;
   }
-  e = cudaFuncSetAttribute(dkv::tc_bwd_dkdv_kernel<false, T, D>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  e = ensure_smem((const void*)dkv::tc_bwd_dkdv_kernel<false, T, D>, smem);
   if (e == cudaSuccess) {
     // persistent: one CTA per SM walks the band items (block, head) round-robin
     int sms = 0;
@@ -954,8 +957,6 @@ cudaError_t launch_dkdv(const DsaltAttnParams& p, float* lmk_scratch, cudaStream
   if (lmk) {
     // join before anything can fail past this point, so the caller's stream never runs ahead of the side work
     const cudaError_t ej = cudaStreamWaitEvent(st, join, 0);
-    cudaEventDestroy(fork);
-    cudaEventDestroy(join);
     if (e == cudaSuccess) e = ej;
     if (e == cudaSuccess) {
       dkv::lmk_fixup_kernel<T, D><<<dim3((unsigned)(p.S * ((p.kp + 3) / 4)), (unsigned)p.H), 128, 0, st>>>(a);

@@ -371,8 +371,7 @@ cudaError_t launch_dq2(const DsaltAttnParams& p, cudaStream_t st) {
   if (encode_tensor_map_3d(&a.tm_lk, dt, lk, D, kp, hs, row, (uint64_t)kp * row, 64, a.lmk_box, 1) != CUDA_SUCCESS)
     return cudaErrorInvalidValue;
   const size_t smem = sizeof(dq2::Smem<D>) + 1024;
-  cudaError_t e = cudaFuncSetAttribute(dq2::tc_bwd_dq_kernel<T, D>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                       (int)smem);
+  cudaError_t e = ensure_smem((const void*)dq2::tc_bwd_dq_kernel<T, D>, smem);
   if (e != cudaSuccess) return e;
   int sms = 0;
   e = sm_count_dq(&sms);

@@ -7,10 +7,29 @@
 #include <stdint.h>
 #include <math.h>
 #include <climits>
+#include <mutex>
 
 #include "dsalt_b200.h"
 
 namespace dsalt {
+
+// cudaFuncSetAttribute(MaxDynamicSharedMemorySize) once per (kernel, device,
+// size): the attribute persists, so repeated launches skip the driver call.
+inline cudaError_t ensure_smem(const void* kernel, size_t bytes) {
+  struct Entry { const void* k; int dev; size_t bytes; };
+  static Entry done[256];
+  static int n_done = 0;
+  static std::mutex mu;
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  std::lock_guard<std::mutex> lock(mu);
+  for (int i = 0; i < n_done; ++i)
+    if (done[i].k == kernel && done[i].dev == dev && done[i].bytes >= bytes) return cudaSuccess;
+  e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes);
+  if (e == cudaSuccess && n_done < 256) done[n_done++] = Entry{kernel, dev, bytes};
+  return e;
+}
 
 // ---------------------------------------------------------------- dtypes
 template <typename T> __device__ __forceinline__ float to_f32(T x);

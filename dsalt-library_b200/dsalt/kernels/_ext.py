@@ -203,16 +203,21 @@ def status_string(code: int) -> str:
 RECORD: list | None = None
 
 
+def current_stream_handle() -> int:
+    """Raw handle of the current CUDA stream of the current device (no Stream object)."""
+    return torch._C._cuda_getCurrentRawStream(torch._C._cuda_getDevice())
+
+
 def call(name: str, params) -> None:
     """Launch ``name`` on the current CUDA stream; raise RuntimeError on a bad status."""
-    lib = load()
-    cs = torch.cuda.current_stream()
+    lib = _lib if _lib is not None else load()
     rec = RECORD
     if rec is not None:
+        cs = torch.cuda.current_stream()
         e0 = torch.cuda.Event(enable_timing=True)
         e1 = torch.cuda.Event(enable_timing=True)
         e0.record(cs)
-    rc = getattr(lib, name)(ctypes.byref(params), ctypes.c_void_p(cs.cuda_stream))
+    rc = getattr(lib, name)(ctypes.byref(params), current_stream_handle())
     if rc != OK:
         raise RuntimeError(f"{name} failed: {status_string(rc)} (status {rc})")
     if rec is not None:

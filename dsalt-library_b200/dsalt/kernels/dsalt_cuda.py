@@ -85,9 +85,11 @@ class Prepared:
 
 # The widest band of a batch (max over the sequences of seq_wmax) sizes the dSᵀ tile
 # scratch of the backward.  The forward copies it into a small ring of pinned host
-# slots right after the schedule kernel and records an event; the backward reads it
-# once that event has completed, which in practice it has (the backward is enqueued
-# long after the forward's first kernel), so the host never waits on the device.
+# slots right after the schedule kernel and records an event.  The backward uses it
+# when that event has completed; otherwise (the host runs ahead of the device) it
+# sizes the scratch for bands as long as the sequences, which needs no device
+# value, and waits for the event only when that bound would exceed
+# SCRATCH_BUDGET_BYTES.
 _WMAX_RING = 64
 _WMAX: dict = {}
 
@@ -114,15 +116,22 @@ def _record_wmax(prep: "Prepared", dev: torch.device) -> None:
     prep.wmax_slot, prep.wmax_gen = slot, r["gen"][slot]
 
 
-def widest_band(prep: "Prepared", dev: torch.device) -> int:
-    """Upper bound of max_s seq_wmax[s] for sizing the backward's tile scratch."""
+SCRATCH_BUDGET_BYTES = 8 << 30
+
+
+def widest_band(prep: "Prepared", dev: torch.device, bytes_per_band_tile: int) -> int:
+    """Upper bound of max_s seq_wmax[s] for sizing the backward's tile scratch
+    (``bytes_per_band_tile``: scratch bytes per unit of band_tiles)."""
     r = _WMAX.get(dev.index if dev.index is not None else torch.cuda.current_device())
-    if prep.wmax_slot >= 0 and r is not None and r["gen"][prep.wmax_slot] == prep.wmax_gen \
-            and not torch.cuda.is_current_stream_capturing():
-        r["events"][prep.wmax_slot].synchronize()
-        return max(int(r["host"][prep.wmax_slot]), 0)
-    # no recorded value (captured, or the ring moved on): a band never exceeds its sequence
-    return max(prep.lmax - 1, 0)
+    recorded = prep.wmax_slot >= 0 and r is not None and r["gen"][prep.wmax_slot] == prep.wmax_gen
+    length_bound = max(prep.lmax - 1, 0)   # a band never reaches past its sequence start
+    if recorded:
+        ev = r["events"][prep.wmax_slot]
+        fits = (BLOCK_M + length_bound + 63) // 64 * bytes_per_band_tile <= SCRATCH_BUDGET_BYTES
+        if ev.query() or (not fits and not torch.cuda.is_current_stream_capturing()):
+            ev.synchronize()
+            return max(int(r["host"][prep.wmax_slot]), 0)
+    return length_bound
 
 
 def prepare(k_c: torch.Tensor, v_c: torch.Tensor, lmk_pos: torch.Tensor, lmk_w: torch.Tensor,
@@ -247,7 +256,7 @@ def backward(grad_out, q_c, k_c, v_c, o, lse, prep: Prepared, tau_win: float, wi
                 delta=delta, dq=dq, dk=dk, dv=dv, dw_head=dw_head, dw=dw, d_lw=d_lw, lmk_grad=lmk_grad,
                 qrec=qrec)
     # the dSᵀ tiles the dK/dV stage stores for the dQ stage (tensor-core family)
-    band_tiles = (BLOCK_M + widest_band(prep, dev) + 63) // 64
+    band_tiles = (BLOCK_M + widest_band(prep, dev, H * prep.max_blocks * _ext.DS_TILE_BYTES) + 63) // 64
     lmk_tiles = (prep.lmax + 63) // 64 + 1
     n_tiles = _ext.ds_tiles(H, prep.max_blocks, prep.S, prep.kp, band_tiles, lmk_tiles)
     ds = torch.empty(n_tiles * _ext.DS_TILE_BYTES + 1024, dtype=torch.uint8, device=dev)

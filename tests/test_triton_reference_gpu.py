@@ -95,8 +95,9 @@ def test_selection_matches_reference_at_config2():
     assert clear.float().mean() > 0.999
     w_disc = got_w.floor().clamp(min=1)
     assert torch.equal(w_disc[clear], ref["w_disc"][clear])
-    torch.testing.assert_close(scores.cpu(), ref["scores"], rtol=1e-5, atol=1e-5)
-    torch.testing.assert_close(z_x.cpu(), ref["z_x"], rtol=1e-5, atol=1e-5)
+    # z-scores: this build accumulates the mean and the std in fp64, torch in fp32
+    torch.testing.assert_close(scores.cpu(), ref["scores"], rtol=1e-4, atol=1e-4)
+    torch.testing.assert_close(z_x.cpu(), ref["z_x"], rtol=1e-4, atol=1e-4)
     # landmark index sets: bit-exact given the reference's scores and windows
     idx = select_topk(ref["scores"].to(dev), ref["w_disc"].to(dev), cu, k, 4096).cpu()
     ri = ref["idx"]

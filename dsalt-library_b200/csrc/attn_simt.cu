@@ -104,7 +104,7 @@ simt_fwd_kernel(const DsaltAttnParams p) {
   for (int r = 0; r < R; ++r) {
     if (lane + 32 * r >= D) continue;
     const T ov = from_f32<T>(acc[r] * inv_l);
-    o[lane + 32 * r] = ov;
+    if (p.o) o[lane + 32 * r] = ov;
     if (of) of[lane + 32 * r] = to_f32<T>(ov);
   }
   if (lane == 0) p.lse[t * p.H + h] = nonempty ? m + logf(l) : -INFINITY;
@@ -122,7 +122,9 @@ bwd_preprocess_kernel(const DsaltAttnParams p) {
   const int64_t row = (int64_t)blockIdx.x * kSimtWarps + (threadIdx.x >> 5);
   if (row >= p.T * p.H) return;
   const int D = p.D;
-  const T* o = reinterpret_cast<const T*>(p.o) + row * D;
+  // the stored O: the input-dtype copy, or the fp32 copy (same values) when only that was written
+  const T* o = p.o ? reinterpret_cast<const T*>(p.o) + row * D : nullptr;
+  const float* of = p.o ? nullptr : p.o_f32 + row * D;
   const T* g = reinterpret_cast<const T*>(p.dout) + row * D;
   const float* gf = p.dout_f32 ? p.dout_f32 + row * D : nullptr;
   T* gw = const_cast<T*>(g);
@@ -139,7 +141,7 @@ bwd_preprocess_kernel(const DsaltAttnParams p) {
     } else {
       gv = to_f32<T>(g[e]);
     }
-    s = fmaf(to_f32<T>(o[e]), gv, s);
+    s = fmaf(o ? to_f32<T>(o[e]) : of[e], gv, s);
   }
   s = warp_sum(s);
   if (lane == 0) {
@@ -306,7 +308,18 @@ bwd_preprocess_vec_kernel(const DsaltAttnParams p) {
   const int64_t n_chunks = p.T * p.H * G;
   float s = 0.f;
   if (chunk < n_chunks) {
-    const uint4 ov = __ldg(reinterpret_cast<const uint4*>(p.o) + chunk);
+    // the stored O: the input-dtype copy, or the fp32 copy (same values) when only that was written
+    float of[8];
+    if (p.o) {
+      const uint4 ov = __ldg(reinterpret_cast<const uint4*>(p.o) + chunk);
+      const T* o8 = reinterpret_cast<const T*>(&ov);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) of[e] = to_f32<T>(o8[e]);
+    } else {
+      const float4 a = __ldg(reinterpret_cast<const float4*>(p.o_f32) + 2 * chunk);
+      const float4 b = __ldg(reinterpret_cast<const float4*>(p.o_f32) + 2 * chunk + 1);
+      of[0] = a.x; of[1] = a.y; of[2] = a.z; of[3] = a.w; of[4] = b.x; of[5] = b.y; of[6] = b.z; of[7] = b.w;
+    }
     uint4 gv;
     if (p.dout_f32) {
       const float4 a = __ldcs(reinterpret_cast<const float4*>(p.dout_f32) + 2 * chunk);
@@ -320,10 +333,9 @@ bwd_preprocess_vec_kernel(const DsaltAttnParams p) {
     } else {
       gv = __ldg(reinterpret_cast<const uint4*>(p.dout) + chunk);
     }
-    const T* o8 = reinterpret_cast<const T*>(&ov);
     const T* g8 = reinterpret_cast<const T*>(&gv);
 #pragma unroll
-    for (int e = 0; e < 8; ++e) s = fmaf(to_f32<T>(o8[e]), to_f32<T>(g8[e]), s);
+    for (int e = 0; e < 8; ++e) s = fmaf(of[e], to_f32<T>(g8[e]), s);
   }
 #pragma unroll
   for (int off = G / 2; off > 0; off >>= 1) s += __shfl_xor_sync(0xffffffffu, s, off);
@@ -367,7 +379,7 @@ static bool launch_preprocess_vec(const DsaltAttnParams& p, cudaStream_t st) {
     return false;
   } else {
   const auto aligned = [](const void* q) { return (reinterpret_cast<uintptr_t>(q) & 15u) == 0; };
-  if (!aligned(p.o) || !aligned(p.dout) || (p.dout_f32 && !aligned(p.dout_f32))) return false;
+  if (!aligned(p.o ? p.o : p.o_f32) || !aligned(p.dout) || (p.dout_f32 && !aligned(p.dout_f32))) return false;
   const int G = p.D / 8;
   const int64_t n_chunks = p.T * p.H * G;
   const dim3 grid((unsigned)((n_chunks + 255) / 256));

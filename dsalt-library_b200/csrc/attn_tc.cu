@@ -1,8 +1,11 @@
 // tcgen05 / TMEM / TMA forward kernel of the DSALT attention for sm_100a.
 //
-// One CTA computes 128 query rows of one (sequence, head): the rows' landmark
-// tile(s) and their band of keys [min_i(i − W_i), max_i i], in 128-key tiles.
-// 320 threads:
+// Persistent: one CTA per SM walks the work items (128 query rows of one
+// (sequence, head)) round-robin.  For each item it scans the rows' landmark
+// tile(s) and their band of keys [min_i(i − W_i), max_i i], in 128-key tiles;
+// tile stages, TMEM buffers and barrier phases run on across items, so the next
+// item's loads and first MMAs overlap the current item's last tiles and epilogue.
+// 384 threads:
 //   warps 0-7   softmax: TMEM lane r = 32·(warp % 4) + lane is query row r;
 //               warps 0-3 own key columns 0-63 of every tile, warps 4-7 columns
 //               64-127.  Each half keeps its own running max / sum and its own
@@ -12,11 +15,17 @@
 //               it grows by more than 2^8); P (bf16/fp16) goes to a 128B-swizzled
 //               K-major smem tile (chunk h = half h), where each thread applies
 //               the soft window edge to its ≤ ceil(win_edge)+1 edge keys in place.
-//   warp 8      TMA producers: lane 0 loads Q and the K tiles (a K stage frees
-//               when its S is done), lane 1 the V tiles (freed by P·V).
+//               The epilogue stages O in the P buffer and stores it row-contiguously,
+//               in the input dtype, or in fp32 when the caller asks for the op's
+//               fp32 output (o_f32: then that is the only O written).
+//   warp 8      TMA producers: lane 0 loads Q (once the previous item's last S has
+//               read it) and the K tiles, lane 1 the V tiles.
 //   warp 9      TMEM allocator + single-thread tcgen05.mma issuer:
-//               S[t%2] = Q·K_tᵀ two tiles ahead; O_h += P_t,h·V_t,h for each half
-//               h as soon as that half's P is written.
+//               S[t%2] = Q·K_tᵀ two tiles ahead.
+//   warp 10     O_h += P_t,h·V_t,h for each half h as soon as that half's P is
+//               written (an item's first one once the previous epilogue read O).
+//   warp 11     scheduler: resolves each item's row windows, landmark slots and
+//               band one or two items ahead into a double-buffered info block.
 //
 // TMEM (512 columns): S double buffer [0, 256), O_0 [256, 256 + D), O_1 after it.
 //
@@ -38,23 +47,39 @@ cudaError_t tc_bwd_stage(int stage, const DsaltAttnParams& p, float* lmk_scratch
 
 namespace {
 
-constexpr int BM = 128;              // query rows per CTA
+constexpr int BM = 128;              // query rows per item
 constexpr int BN = 128;              // keys per tile
 constexpr int HALF = BN / 2;         // key columns per softmax thread
 constexpr int kMaxLmk = 512;         // landmark slots held in shared memory
-constexpr int kThreads = 352;
+constexpr int kThreads = 384;
 constexpr int kRowThreads = 256;
 constexpr int kProducerWarp = 8;
 constexpr int kMmaWarp = 9;    // TMEM owner; issues S = Q·Kᵀ
 constexpr int kMmaWarpB = 10;  // issues O_h += P_h·V_h
+constexpr int kSchedWarp = 11; // resolves the next items' windows and landmarks
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr float kLn2 = 0.6931471805599453f;
 constexpr float kRescaleThreshold = 8.0f;  // log2 units
 constexpr int kMaxEdge = 8;                // soft-edge keys per row handled with precomputed factors
+// arrivals that release an item's info block: the eight softmax warps, the
+// producer, the two MMA warps (one elected lane each)
+constexpr int kInfoConsumers = 11;
 
 enum Bar {
-  Q_FULL = 0, K_FULL = 1, V_FULL = 3, K_EMPTY = 5, V_EMPTY = 7, S_FULL = 9, S_EMPTY = 11, P_FULL = 13,
-  O_DONE = 15, FINAL = 17, EPI = 19, EPI2 = 20, NUM_BARS = 21
+  Q_FULL = 0, Q_EMPTY = 1, K_FULL = 2, V_FULL = 4, K_EMPTY = 6, V_EMPTY = 8, S_FULL = 10, S_EMPTY = 12,
+  P_FULL = 14, O_DONE = 16, O_FREE = 18, INFO_FULL = 19, INFO_EMPTY = 21, EPI = 23, FINAL = 24, NUM_BARS = 26
+};
+
+// Everything the roles need about one item (128 query rows of one (sequence,
+// head)), resolved by the scheduler warp one or two items ahead.
+struct ItemInfo {
+  int h, s, m0, L;
+  int64_t s0;
+  int band_lo, band_hi, n_valid, n_lt, n_tiles, slow_edge;
+  int row_lo[BM], row_hi[BM], row_cnt[BM], row_de0[BM], row_ne[BM];
+  float row_wt[BM];
+  int lmk_pos[kMaxLmk];
+  float lmk_lw2[kMaxLmk];
 };
 
 template <int D>
@@ -63,14 +88,12 @@ struct alignas(1024) FwdSmem {
   uint8_t k[2][BN * D * 2];
   uint8_t v[2][BN * D * 2];
   uint8_t p[BM * BN * 2];       // chunk h (64 keys) is written by softmax half h
+  ItemInfo info[2];
+  float m_half[2][2][BM];       // epilogue [item parity][half]: running max (log2) and sum
+  float l_half[2][2][BM];
   uint64_t bars[NUM_BARS];
   uint32_t tmem_base;
   int abort_flag;
-  int band_lo, band_hi, n_valid, slow_edge;
-  float m_half[2][BM];          // epilogue: per-half running max (log2) and sum
-  float l_half[2][BM];
-  int lmk_pos[kMaxLmk];
-  float lmk_lw2[kMaxLmk];
 };
 
 struct alignas(64) FwdArgs {
@@ -81,18 +104,84 @@ struct alignas(64) FwdArgs {
 
 __device__ __forceinline__ int round16(int n) { return (n + 15) & ~15; }
 
+// MMA N extent of tile t of an item: landmark tiles first, then the band tiles
+__device__ __forceinline__ int tile_cols(const ItemInfo& in, int t) {
+  if (t < in.n_lt) return round16(min(BN, in.n_valid - BN * t));
+  return round16(min(BN, in.band_hi - (in.band_lo + BN * (t - in.n_lt)) + 1));
+}
+
+// Scheduler warp: resolve item idx into `in` (every row's window, the landmark
+// slots of its (head, sequence), the band of key tiles).  An item always has at
+// least one tile: a block whose rows attend nothing scans one masked tile.
+__device__ __forceinline__ void resolve_item(const DsaltAttnParams& p, int idx, int nb, ItemInfo& in) {
+  const int lane = threadIdx.x & 31;
+  const int blk = idx % nb, h = idx / nb;
+  const int s = __ldg(p.block_map + 2 * blk);
+  const int m0 = __ldg(p.block_map + 2 * blk + 1) * BM;
+  const int64_t s0 = __ldg(p.cu_seqlens + s);
+  const int L = (int)(__ldg(p.cu_seqlens + s + 1) - s0);
+  const int kp = p.kp;
+  const int64_t lbase = ((int64_t)h * p.S + s) * kp;
+  int nv = 0;
+  for (int c0 = 0; c0 < kp; c0 += 32) {
+    const int c = c0 + lane;
+    const int ps = c < kp ? __ldg(p.pos_sorted + lbase + c) : -1;
+    if (c < kp) {
+      in.lmk_pos[c] = ps;
+      in.lmk_lw2[c] = __ldg(p.w_sorted + lbase + c) * kLog2e;
+    }
+    nv += __popc(__ballot_sync(0xffffffffu, ps >= 0));
+  }
+  __syncwarp();
+  int blo = INT_MAX, bhi = -1, slow = 0;
+  for (int r = lane; r < BM; r += 32) {
+    const int i = m0 + r;
+    int lo = INT_MAX, hi = -1, cnt = 0, d_e0 = INT_MAX, ne = 0;
+    float wt = 0.f;
+    if (i < L) {
+      const RowWindow rw = row_window(__ldg(p.w + s0 + i), i, p.semantics, p.win_edge);
+      wt = rw.wt;
+      if (rw.W >= 0) {
+        lo = i - min(rw.W, i);
+        hi = i;
+        d_e0 = max((int)floorf(rw.core) + 1, 0);
+        ne = max(min(rw.W, i) - d_e0 + 1, 0);
+      }
+      // landmarks valid for row i form a prefix of the sorted positions
+      int a0 = 0, a1 = nv;
+      while (a0 < a1) {
+        const int mid = (a0 + a1) >> 1;
+        const int ps = in.lmk_pos[mid];
+        if (ps <= i && (float)ps < rw.win_lo) a0 = mid + 1; else a1 = mid;
+      }
+      cnt = a0;
+    }
+    in.row_lo[r] = lo; in.row_hi[r] = hi; in.row_cnt[r] = cnt;
+    in.row_de0[r] = d_e0; in.row_ne[r] = ne; in.row_wt[r] = wt;
+    if (lo <= hi) { blo = min(blo, lo); bhi = max(bhi, hi); }
+    if (ne > kMaxEdge) slow = 1;
+  }
+  blo = __reduce_min_sync(0xffffffffu, blo);
+  bhi = __reduce_max_sync(0xffffffffu, bhi);
+  slow = __reduce_or_sync(0xffffffffu, slow);
+  if (lane == 0) {
+    const int n_lt = (nv + BN - 1) / BN;
+    int n_bt = bhi >= blo ? (bhi - blo + BN) / BN : 0;
+    if (n_lt + n_bt == 0) { blo = 0; bhi = 0; n_bt = 1; }  // one fully masked tile
+    in.h = h; in.s = s; in.m0 = m0; in.L = L; in.s0 = s0;
+    in.band_lo = blo; in.band_hi = bhi; in.n_valid = nv; in.n_lt = n_lt; in.n_tiles = n_lt + n_bt;
+    in.slow_edge = slow;
+  }
+  __syncwarp();
+}
+
 template <typename T, int D>
 __global__ void __launch_bounds__(kThreads, 1) tc_fwd_kernel(const __grid_constant__ FwdArgs a) {
   using namespace sm100;
   const DsaltAttnParams& p = a.p;
-  const int blk = blockIdx.x;
-  const int h = blockIdx.y;
-  if (blk >= __ldg(p.num_blocks)) return;  // CTA-uniform, before any barrier or TMEM use
-  const int s = __ldg(p.block_map + 2 * blk);
-  const int mb = __ldg(p.block_map + 2 * blk + 1);
-  const int64_t s0 = __ldg(p.cu_seqlens + s);
-  const int L = (int)(__ldg(p.cu_seqlens + s + 1) - s0);
-  const int m0 = mb * BM;
+  const int nb = __ldg(p.num_blocks);
+  const int n_items = nb * p.H;
+  if ((int)blockIdx.x >= n_items) return;  // CTA-uniform, before any barrier or TMEM use
 
   extern __shared__ uint8_t smem_raw[];
   FwdSmem<D>& sm = *reinterpret_cast<FwdSmem<D>*>(
@@ -105,6 +194,7 @@ __global__ void __launch_bounds__(kThreads, 1) tc_fwd_kernel(const __grid_consta
 
   if (tid == 0) {
     mbar_init(bar[Q_FULL], 1);
+    mbar_init(bar[Q_EMPTY], 1);
     for (int st = 0; st < 2; ++st) {
       mbar_init(bar[K_FULL + st], 1);
       mbar_init(bar[V_FULL + st], 1);
@@ -114,17 +204,15 @@ __global__ void __launch_bounds__(kThreads, 1) tc_fwd_kernel(const __grid_consta
       mbar_init(bar[S_EMPTY + st], kRowThreads);
       mbar_init(bar[P_FULL + st], kRowThreads / 2);  // index = softmax half
       mbar_init(bar[O_DONE + st], 1);                // index = softmax half
+      mbar_init(bar[INFO_FULL + st], 32);
+      mbar_init(bar[INFO_EMPTY + st], kInfoConsumers);
     }
+    mbar_init(bar[O_FREE], kRowThreads);
+    mbar_init(bar[EPI], kRowThreads);
     mbar_init(bar[FINAL], 1);
     mbar_init(bar[FINAL + 1], 1);
-    mbar_init(bar[EPI], kRowThreads);
-    mbar_init(bar[EPI2], kRowThreads);
     fence_mbar_init();
     sm.abort_flag = 0;
-    sm.band_lo = INT_MAX;
-    sm.band_hi = -1;
-    sm.n_valid = 0;
-    sm.slow_edge = 0;
   }
   if (warp == kProducerWarp && lane == 0) {
     prefetch_tmap(&a.tm_q);
@@ -132,143 +220,115 @@ __global__ void __launch_bounds__(kThreads, 1) tc_fwd_kernel(const __grid_consta
     prefetch_tmap(&a.tm_v);
   }
   if (warp == kMmaWarp) tmem_alloc(smem_u32(&sm.tmem_base), 512);
-  // row r = 32·(warp % 4) + lane, key-column half = warp / 4; the window load is
-  // issued here so that its latency overlaps the landmark loads below
-  const int r = 32 * (warp & 3) + lane;
-  const int half = (warp >> 2) & 1;
-  const int i = m0 + r;
-  const bool row_ok = warp < 8 && i < L;
-  const float w_raw = row_ok ? __ldg(p.w + s0 + i) : 0.f;
-  const int kp = p.kp;
-  const int64_t lbase = ((int64_t)h * p.S + s) * kp;
-  for (int c = tid; c < kp; c += kThreads) {
-    const int ps = __ldg(p.pos_sorted + lbase + c);
-    sm.lmk_pos[c] = ps;
-    sm.lmk_lw2[c] = __ldg(p.w_sorted + lbase + c) * kLog2e;
-    if (ps >= 0) atomicAdd(&sm.n_valid, 1);
-  }
-  __syncthreads();
-  // The landmark tiles (every valid slot of the sequence, sorted) come first; they
-  // and Q depend only on the block, so their loads start while the windows are
-  // being resolved.
-  const int n_valid = sm.n_valid;
-  const int n_lt = (n_valid + BN - 1) / BN;
-  if (warp == kProducerWarp && lane < 2) {
-    if (lane == 0) {
-      mbar_expect_tx(bar[Q_FULL], BM * D * 2);
-#pragma unroll
-      for (int c = 0; c < D / 64; ++c)
-        tma_load_3d(smem_u32(sm.q + c * (BM * 128)), &a.tm_q, bar[Q_FULL], c * 64, h, (int)(s0 + m0));
-    }
-    if (n_lt > 0) {
-      const int FULL = lane == 0 ? K_FULL : V_FULL;
-      mbar_expect_tx(bar[FULL], a.lmk_box * D * 2);
-      uint8_t* dst = lane == 0 ? sm.k[0] : sm.v[0];
-      const CUtensorMap* map = lane == 0 ? &a.tm_lk : &a.tm_lv;
-#pragma unroll
-      for (int c = 0; c < D / 64; ++c)
-        tma_load_3d(smem_u32(dst + c * (BN * 128)), map, bar[FULL], c * 64, 0, h * p.S + s);
-    }
-  }
-
-  // ---- per-row window
-  RowWindow rw = {};
-  int lo = INT_MAX, hi = -1, cnt = 0;
-  // soft-edge keys of the row: distances d_e0 .. d_e0 + ne − 1, factors σ((w̃ − d)/τ)
-  int d_e0 = INT_MAX, ne = 0;
-  if (row_ok) {
-    rw = row_window(w_raw, i, p.semantics, p.win_edge);
-    if (rw.W >= 0) {
-      lo = i - min(rw.W, i);
-      hi = i;
-    }
-    // landmarks valid for row i form a prefix of the sorted positions
-    int a0 = 0, a1 = sm.n_valid;  // first index failing the predicate
-    while (a0 < a1) {
-      const int mid = (a0 + a1) >> 1;
-      const int ps = sm.lmk_pos[mid];
-      if (ps <= i && (float)ps < rw.win_lo) a0 = mid + 1; else a1 = mid;
-    }
-    cnt = a0;
-    if (rw.W >= 0) {
-      d_e0 = max((int)floorf(rw.core) + 1, 0);
-      ne = max(min(rw.W, i) - d_e0 + 1, 0);
-    }
-    if (half == 0) {
-      if (lo <= hi) {
-        atomicMin(&sm.band_lo, lo);
-        atomicMax(&sm.band_hi, hi);
-      }
-      if (ne > kMaxEdge) atomicOr(&sm.slow_edge, 1);
-    }
-  }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = sm.tmem_base;
-  const int band_lo = sm.band_lo, band_hi = sm.band_hi;
-  const int n_bt = band_hi >= band_lo ? (band_hi - band_lo + BN) / BN : 0;
-  const int n_tiles = n_lt + n_bt;
   volatile int* abort_flag = &sm.abort_flag;
-  // tile t: landmark tile (t < n_lt) or band tile starting at key band_lo + BN*(t - n_lt)
-  auto tile_n = [&](int t) -> int {
-    if (t < n_lt) return round16(min(BN, n_valid - BN * t));
-    return round16(min(BN, band_hi - (band_lo + BN * (t - n_lt)) + 1));
-  };
+  const int stride = gridDim.x;
   const uint32_t tS = tmem;            // S buffers: columns [0,128) and [128,256)
   const uint32_t tO = tmem + 2 * BN;   // O_h: columns [256 + h·D, 256 + (h+1)·D)
 
-  if (warp == kProducerWarp) {
-    // ------------------------------------------------------------ producers
-    if (lane < 2 && n_tiles > 0) {
-      const bool is_k = lane == 0;
-      const int FULL = is_k ? K_FULL : V_FULL, EMPTY = is_k ? K_EMPTY : V_EMPTY;
-      // tile 0 of a sequence with landmarks was issued before the windows were resolved
-      int issued = n_lt > 0 ? 1 : 0;
-      for (int t = issued; t < n_tiles; ++t) {
-        const int st = t & 1;
-        if (t >= 2 && !mbar_wait(bar[EMPTY + st], ((t >> 1) - 1) & 1, abort_flag, p.status)) break;
-        const bool lmk = t < n_lt;
-        mbar_expect_tx(bar[FULL + st], (lmk ? a.lmk_box : BN) * D * 2);
-        uint8_t* dst = is_k ? sm.k[st] : sm.v[st];
-        const CUtensorMap* map = lmk ? (is_k ? &a.tm_lk : &a.tm_lv) : (is_k ? &a.tm_k : &a.tm_v);
-#pragma unroll
-        for (int c = 0; c < D / 64; ++c) {
-          if (lmk) tma_load_3d(smem_u32(dst + c * (BN * 128)), map, bar[FULL + st], c * 64, BN * t, h * p.S + s);
-          else tma_load_3d(smem_u32(dst + c * (BN * 128)), map, bar[FULL + st], c * 64, h,
-                           (int)(s0 + band_lo + BN * (t - n_lt)));
-        }
-        issued = t + 1;
-      }
-      // drain: never leave a TMA write in flight into shared memory
-      for (int t = max(0, issued - 2); t < issued; ++t) mbar_drain(bar[FULL + (t & 1)], (t >> 1) & 1);
+  if (warp == kSchedWarp) {
+    // ------------------------------------------------------------ scheduler
+    int li = 0;
+    for (int idx = blockIdx.x; idx < n_items; idx += stride, ++li) {
+      const int ib = li & 1;
+      if (li >= 2 &&
+          !__all_sync(0xffffffffu, mbar_wait(bar[INFO_EMPTY + ib], ((li >> 1) - 1) & 1, abort_flag, p.status)))
+        break;
+      resolve_item(p, idx, nb, sm.info[ib]);
+      mbar_arrive(bar[INFO_FULL + ib]);
     }
-    if (lane == 0) mbar_drain(bar[Q_FULL], 0);
+  } else if (warp == kProducerWarp) {
+    // ------------------------------------------------------------ producers
+    // lane 0: Q (once the previous item's last S is issued) and the K tiles;
+    // lane 1: the V tiles.  Tile stages follow a tile counter that runs across items.
+    int gk = 0, li = 0, issued_k = 0, issued_q = 0;
+    bool ok = true;
+    for (int idx = blockIdx.x; ok && idx < n_items; idx += stride, ++li) {
+      const int ib = li & 1;
+      ok = mbar_wait(bar[INFO_FULL + ib], (li >> 1) & 1, abort_flag, p.status);
+      const ItemInfo& in = sm.info[ib];
+      const int n_tiles = in.n_tiles, n_lt = in.n_lt;
+      if (ok && lane < 2) {
+        const bool is_k = lane == 0;
+        if (is_k) {
+          if (li >= 1) ok = mbar_wait(bar[Q_EMPTY], (li - 1) & 1, abort_flag, p.status);
+          if (ok) {
+            mbar_expect_tx(bar[Q_FULL], BM * D * 2);
+#pragma unroll
+            for (int c = 0; c < D / 64; ++c)
+              tma_load_3d(smem_u32(sm.q + c * (BM * 128)), &a.tm_q, bar[Q_FULL], c * 64, in.h, (int)(in.s0 + in.m0));
+            issued_q = li + 1;
+          }
+        }
+        const int FULL = is_k ? K_FULL : V_FULL, EMPTY = is_k ? K_EMPTY : V_EMPTY;
+        for (int t = 0; ok && t < n_tiles; ++t) {
+          const int g = gk + t, st = g & 1;
+          if (g >= 2 && !mbar_wait(bar[EMPTY + st], ((g >> 1) - 1) & 1, abort_flag, p.status)) { ok = false; break; }
+          const bool lmk = t < n_lt;
+          mbar_expect_tx(bar[FULL + st], (lmk ? a.lmk_box : BN) * D * 2);
+          uint8_t* dst = is_k ? sm.k[st] : sm.v[st];
+          const CUtensorMap* map = lmk ? (is_k ? &a.tm_lk : &a.tm_lv) : (is_k ? &a.tm_k : &a.tm_v);
+#pragma unroll
+          for (int c = 0; c < D / 64; ++c) {
+            if (lmk) tma_load_3d(smem_u32(dst + c * (BN * 128)), map, bar[FULL + st], c * 64, BN * t, in.h * p.S + in.s);
+            else tma_load_3d(smem_u32(dst + c * (BN * 128)), map, bar[FULL + st], c * 64, in.h,
+                             (int)(in.s0 + in.band_lo + BN * (t - n_lt)));
+          }
+          issued_k = g + 1;
+        }
+      }
+      ok = __all_sync(0xffffffffu, ok);
+      gk += n_tiles;
+      if (lane == 0) mbar_arrive(bar[INFO_EMPTY + ib]);
+    }
+    // drain: never leave a TMA write in flight into shared memory
+    if (lane < 2) {
+      const int FULL = lane == 0 ? K_FULL : V_FULL;
+      for (int g = max(0, issued_k - 2); g < issued_k; ++g) mbar_drain(bar[FULL + (g & 1)], (g >> 1) & 1);
+    }
+    if (lane == 0 && issued_q > 0) mbar_drain(bar[Q_FULL], (issued_q - 1) & 1);
   } else if (warp == kMmaWarp) {
     // ------------------------------------------------------------ S issuer
     // S_t = Q·K_tᵀ as soon as K_t is in and the softmax has read S_{t−2}.  The
     // P·V products come from warp 10: one issuing thread sustains only about
     // one MMA per 110 cycles, two overlap.
-    if (lane == 0 && n_tiles > 0) {
-      const uint32_t q_addr = smem_u32(sm.q);
-      bool ok = mbar_wait(bar[Q_FULL], 0, abort_flag, p.status);
-      for (int t = 0; ok && t < n_tiles; ++t) {
-        const int st = t & 1;
-        if (!mbar_wait(bar[K_FULL + st], (t >> 1) & 1, abort_flag, p.status)) break;
-        if (t >= 2 && !mbar_wait(bar[S_EMPTY + st], ((t >> 1) - 1) & 1, abort_flag, p.status)) break;
-        tc_fence_after();
-        const uint32_t k_addr = smem_u32(sm.k[st]);
-        const uint32_t id_s = idesc_f16(kBF16, BM, tile_n(t), false, false);
+    int gs = 0, li = 0;
+    bool ok = true;
+    for (int idx = blockIdx.x; ok && idx < n_items; idx += stride, ++li) {
+      const int ib = li & 1;
+      ok = mbar_wait(bar[INFO_FULL + ib], (li >> 1) & 1, abort_flag, p.status);
+      const ItemInfo& in = sm.info[ib];
+      const int n_tiles = in.n_tiles;
+      if (ok && lane == 0) {
+        const uint32_t q_addr = smem_u32(sm.q);
+        ok = mbar_wait(bar[Q_FULL], li & 1, abort_flag, p.status);
+        for (int t = 0; ok && t < n_tiles; ++t) {
+          const int g = gs + t, st = g & 1;
+          if (!mbar_wait(bar[K_FULL + st], (g >> 1) & 1, abort_flag, p.status)) { ok = false; break; }
+          if (g >= 2 && !mbar_wait(bar[S_EMPTY + st], ((g >> 1) - 1) & 1, abort_flag, p.status)) { ok = false; break; }
+          tc_fence_after();
+          const uint32_t k_addr = smem_u32(sm.k[st]);
+          const uint32_t id_s = idesc_f16(kBF16, BM, tile_cols(in, t), false, false);
 #pragma unroll
-        for (int kk = 0; kk < D / 16; ++kk) {
-          const uint32_t off = (kk >> 2) * (BM * 128) + (kk & 3) * 32;
-          const uint64_t ad = sdesc_sw128(q_addr + off, 16, 1024);
-          const uint64_t bd = sdesc_sw128(k_addr + (kk >> 2) * (BN * 128) + (kk & 3) * 32, 16, 1024);
-          mma_f16(tS + st * BN, ad, bd, id_s, kk > 0 ? 1u : 0u);
+          for (int kk = 0; kk < D / 16; ++kk) {
+            const uint32_t off = (kk >> 2) * (BM * 128) + (kk & 3) * 32;
+            const uint64_t ad = sdesc_sw128(q_addr + off, 16, 1024);
+            const uint64_t bd = sdesc_sw128(k_addr + (kk >> 2) * (BN * 128) + (kk & 3) * 32, 16, 1024);
+            mma_f16(tS + st * BN, ad, bd, id_s, kk > 0 ? 1u : 0u);
+          }
+          mma_commit(bar[S_FULL + st]);
+          mma_commit(bar[K_EMPTY + st]);
         }
-        mma_commit(bar[S_FULL + st]);
-        mma_commit(bar[K_EMPTY + st]);
+        if (ok) mma_commit(bar[Q_EMPTY]);  // the item's last S has read Q
       }
+      ok = __shfl_sync(0xffffffffu, ok, 0);
+      gs += n_tiles;
+      if (lane == 0) mbar_arrive(bar[INFO_EMPTY + ib]);
+    }
+    if (lane == 0) {
       // drain: every issued MMA completes before TMEM is released
       mma_commit(bar[FINAL]);
       mbar_drain(bar[FINAL], 0);
@@ -277,289 +337,331 @@ __global__ void __launch_bounds__(kThreads, 1) tc_fwd_kernel(const __grid_consta
     // ------------------------------------------------------------ P·V issuer
     // O_h += P_t,h·V_t,h for each half h as soon as that half of P is written.
     // O_DONE[h] is committed once per tile and half, also when the half had no
-    // valid key (its P·V is skipped).
-    if (lane == 0 && n_tiles > 0) {
-      const uint32_t id_o = idesc_f16(kBF16, BM, D, false, true);
-      const uint32_t p_addr = smem_u32(sm.p);
-      bool ok = true;
-      bool o_written0 = false, o_written1 = false;
-      for (int t = 0; ok && t < n_tiles; ++t) {
-        const int st = t & 1;
-        const int nvalid = tile_n(t);
-        if (!mbar_wait(bar[V_FULL + st], (t >> 1) & 1, abort_flag, p.status)) break;
-        const uint32_t v_addr = smem_u32(sm.v[st]);
+    // valid key (its P·V is skipped).  An item's first P·V waits until the
+    // previous item's epilogue has read O (O_FREE).
+    int gv = 0, li = 0;
+    bool ok = true;
+    for (int idx = blockIdx.x; ok && idx < n_items; idx += stride, ++li) {
+      const int ib = li & 1;
+      ok = mbar_wait(bar[INFO_FULL + ib], (li >> 1) & 1, abort_flag, p.status);
+      const ItemInfo& in = sm.info[ib];
+      const int n_tiles = in.n_tiles;
+      if (ok && lane == 0) {
+        const uint32_t id_o = idesc_f16(kBF16, BM, D, false, true);
+        const uint32_t p_addr = smem_u32(sm.p);
+        if (li >= 1) ok = mbar_wait(bar[O_FREE], (li - 1) & 1, abort_flag, p.status);
+        bool o_written0 = false, o_written1 = false;
+        for (int t = 0; ok && t < n_tiles; ++t) {
+          const int g = gv + t, st = g & 1;
+          const int nvalid = tile_cols(in, t);
+          if (!mbar_wait(bar[V_FULL + st], (g >> 1) & 1, abort_flag, p.status)) { ok = false; break; }
+          const uint32_t v_addr = smem_u32(sm.v[st]);
 #pragma unroll
-        for (int hh = 0; hh < 2; ++hh) {
-          if (!mbar_wait(bar[P_FULL + hh], t & 1, abort_flag, p.status)) { ok = false; break; }
-          tc_fence_after();
-          const int nk = min(max(nvalid - HALF * hh, 0), HALF) / 16;  // valid 16-key steps of this half
-          bool& written = hh == 0 ? o_written0 : o_written1;
-          for (int kk = 0; kk < nk; ++kk) {
-            const uint64_t ad = sdesc_sw128(p_addr + hh * (BM * 128) + kk * 32, 16, 1024);
-            const uint64_t bd = sdesc_sw128(v_addr + (HALF / 16 * hh + kk) * 2048, BN * 128, 1024);
-            mma_f16(tO + hh * D, ad, bd, id_o, (written || kk > 0) ? 1u : 0u);
+          for (int hh = 0; hh < 2; ++hh) {
+            if (!mbar_wait(bar[P_FULL + hh], g & 1, abort_flag, p.status)) { ok = false; break; }
+            tc_fence_after();
+            const int nk = min(max(nvalid - HALF * hh, 0), HALF) / 16;  // valid 16-key steps of this half
+            bool& written = hh == 0 ? o_written0 : o_written1;
+            for (int kk = 0; kk < nk; ++kk) {
+              const uint64_t ad = sdesc_sw128(p_addr + hh * (BM * 128) + kk * 32, 16, 1024);
+              const uint64_t bd = sdesc_sw128(v_addr + (HALF / 16 * hh + kk) * 2048, BN * 128, 1024);
+              mma_f16(tO + hh * D, ad, bd, id_o, (written || kk > 0) ? 1u : 0u);
+            }
+            if (nk > 0) written = true;
+            mma_commit(bar[O_DONE + hh]);
           }
-          if (nk > 0) written = true;
-          mma_commit(bar[O_DONE + hh]);
+          if (!ok) break;
+          mma_commit(bar[V_EMPTY + st]);
         }
-        if (!ok) break;
-        mma_commit(bar[V_EMPTY + st]);
       }
+      ok = __shfl_sync(0xffffffffu, ok, 0);
+      gv += n_tiles;
+      if (lane == 0) mbar_arrive(bar[INFO_EMPTY + ib]);
+    }
+    if (lane == 0) {
       mma_commit(bar[FINAL + 1]);
       mbar_drain(bar[FINAL + 1], 0);
     }
   } else {
     // ------------------------------------------------------------ softmax (row halves)
+    // row r = 32·(warp % 4) + lane, key-column half = warp / 4
+    const int r = 32 * (warp & 3) + lane;
+    const int half = (warp >> 2) & 1;
     const uint32_t lane_addr = ((uint32_t)(32 * (warp & 3)) << 16);
     const int c0 = HALF * half;          // first tile column owned by this thread
     const uint32_t tOh = tO + half * D;  // this half's O accumulator
     const float sl2 = p.scale * kLog2e;
     const float inv_tau = 1.0f / p.tau_win;
-    const bool slow_edge = sm.slow_edge != 0;
-    // soft-edge factors of the row's edge keys (same expression as the per-key form)
-    float eg[kMaxEdge];
-#pragma unroll
-    for (int e = 0; e < kMaxEdge; ++e)
-      eg[e] = (e < ne) ? 1.0f / (1.0f + expf(-((rw.wt - (float)(d_e0 + e)) * inv_tau))) : 1.0f;
-    float m = -INFINITY, l = 0.f;  // this half's running max (log2 units) and sum
-    bool ok = true;
     uint8_t* sp = sm.p + half * (BM * 128);  // this half's P chunk: 128 rows x 64 keys
-    for (int t = 0; t < n_tiles; ++t) {
-      const int st = t & 1;
-      ok = mbar_wait(bar[S_FULL + st], (t >> 1) & 1, abort_flag, p.status);
-      if (!__all_sync(0xffffffffu, ok)) { ok = false; break; }
-      tc_fence_after();
-      // columns past the tile's valid keys hold stale values and are masked below
-      float x[HALF];
-      tmem_ld32(tS + lane_addr + st * BN + c0, x);
-      tmem_ld32(tS + lane_addr + st * BN + c0 + 32, x + 32);
-      tmem_wait_ld();
-      tc_fence_before();
-      mbar_arrive(bar[S_EMPTY + st]);
-
-      const bool lmk = t < n_lt;
-      const int n0 = lmk ? 0 : band_lo + BN * (t - n_lt);
-      // valid columns of this thread: [vlo, vhi] (band) or [0, vhi] (landmarks)
-      int vlo, vhi;
-      if (lmk) {
-        vlo = 0;
-        vhi = cnt - BN * t - c0 - 1;
-      } else {
-        vlo = lo - n0 - c0;  // lo = INT_MAX for a row without band: stays positive
-        vhi = hi - n0 - c0;
-      }
-      const bool all_in = __all_sync(0xffffffffu, vlo <= 0 && vhi >= HALF - 1);
-      const bool all_out = __all_sync(0xffffffffu, vhi < 0 || vlo > HALF - 1 || vlo > vhi);
-      float xs = lmk ? 1.0f : sl2;  // multiplier applied inside exp2
-      if (lmk) {
-        const float* lw2 = sm.lmk_lw2 + BN * t + c0;
+    int gt = 0, li = 0, epi_phase = 0;
+    bool ok = true;
+    // all softmax threads meet (bounded wait on the EPI barrier)
+    auto epi_sync = [&]() -> bool {
+      mbar_arrive(bar[EPI]);
+      const bool w = mbar_wait(bar[EPI], epi_phase & 1, abort_flag, p.status);
+      ++epi_phase;
+      return __all_sync(0xffffffffu, w);
+    };
+    for (int idx = blockIdx.x; ok && idx < n_items; idx += stride, ++li) {
+      const int ib = li & 1;
+      ok = __all_sync(0xffffffffu, mbar_wait(bar[INFO_FULL + ib], (li >> 1) & 1, abort_flag, p.status));
+      if (!ok) break;
+      const ItemInfo& in = sm.info[ib];
+      const int n_tiles = in.n_tiles, n_lt = in.n_lt, band_lo = in.band_lo;
+      const int m0 = in.m0, L = in.L, h = in.h;
+      const int64_t s0 = in.s0;
+      const int i = m0 + r;
+      const bool row_ok = i < L;
+      const int lo = in.row_lo[r], hi = in.row_hi[r], cnt = in.row_cnt[r];
+      const int d_e0 = in.row_de0[r], ne = in.row_ne[r];
+      const float wt = in.row_wt[r];
+      const bool slow_edge = in.slow_edge != 0;
+      // soft-edge factors of the row's edge keys (same expression as the per-key form)
+      float eg[kMaxEdge];
 #pragma unroll
-        for (int c = 0; c < HALF; ++c) x[c] = fmaf(x[c], sl2, lw2[c]);
-      }
-      float mt = -INFINITY;
-      if (!all_out) {
-        if (!all_in) {
-          const uint32_t m_lo = range_mask32(vlo, vhi), m_hi = range_mask32(vlo - 32, vhi - 32);
-#pragma unroll
-          for (int c = 0; c < 32; ++c) x[c] = (m_lo >> c) & 1u ? x[c] : -INFINITY;
-#pragma unroll
-          for (int c = 0; c < 32; ++c) x[32 + c] = (m_hi >> c) & 1u ? x[32 + c] : -INFINITY;
-        }
-        float mx[8];
-#pragma unroll
-        for (int g = 0; g < 8; ++g) mx[g] = max3(x[2 * g], x[2 * g + 1], x[16 + 2 * g]);
-#pragma unroll
-        for (int c = 32; c < HALF; c += 16)
-#pragma unroll
-          for (int g = 0; g < 8; ++g) mx[g] = max3(mx[g], x[c + 2 * g], x[c + 2 * g + 1]);
-#pragma unroll
-        for (int g = 0; g < 8; ++g) mx[g] = fmaxf(mx[g], x[16 + 2 * g + 1]);
-        mt = max3(max3(mx[0], mx[1], mx[2]), max3(mx[3], mx[4], mx[5]), fmaxf(mx[6], mx[7]));
-        if (!lmk) mt *= sl2;
-      }
-      const float m_new = fmaxf(m, mt);
-      bool rescale = false;
-      float factor = 1.0f;
-      if (m == -INFINITY) {
-        m = m_new;
-      } else if (m_new > m + kRescaleThreshold) {
-        factor = exp2f(m - m_new);
-        m = m_new;
-        rescale = true;
-      }
-      if (!all_out) {
-        const float ms = (m == -INFINITY) ? 0.f : m;
-        float sm8[8];
-#pragma unroll
-        for (int g = 0; g < 8; ++g) sm8[g] = 0.f;
-#pragma unroll
-        for (int c = 0; c < HALF; ++c) {
-          x[c] = fast_exp2(fmaf(x[c], xs, -ms));
-          sm8[c & 7] += x[c];
-        }
-        const float sum = ((sm8[0] + sm8[1]) + (sm8[2] + sm8[3])) + ((sm8[4] + sm8[5]) + (sm8[6] + sm8[7]));
-        l = l * factor + sum;
-      } else {
-        l = l * factor;
-      }
-
-      // this half's P chunk and O_h are free once its previous P·V has completed
-      if (t >= 1) {
-        ok = mbar_wait(bar[O_DONE + half], (t - 1) & 1, abort_flag, p.status);
+      for (int e = 0; e < kMaxEdge; ++e)
+        eg[e] = (e < ne) ? 1.0f / (1.0f + expf(-((wt - (float)(d_e0 + e)) * inv_tau))) : 1.0f;
+      float m = -INFINITY, l = 0.f;  // this half's running max (log2 units) and sum
+      for (int t = 0; t < n_tiles; ++t) {
+        const int g = gt + t, st = g & 1;
+        ok = mbar_wait(bar[S_FULL + st], (g >> 1) & 1, abort_flag, p.status);
         if (!__all_sync(0xffffffffu, ok)) { ok = false; break; }
         tc_fence_after();
-      }
-      if (all_out) {
-        const uint4 z = make_uint4(0u, 0u, 0u, 0u);
-#pragma unroll
-        for (int c8 = 0; c8 < HALF / 8; ++c8) *reinterpret_cast<uint4*>(sp + sw128_offset(r, c8 * 8)) = z;
-      } else {
-#pragma unroll
-        for (int c8 = 0; c8 < HALF / 8; ++c8) {
-          const int c = c8 * 8;
-          uint4 u;
-          u.x = pack2(x[c + 0], x[c + 1], kBF16);
-          u.y = pack2(x[c + 2], x[c + 3], kBF16);
-          u.z = pack2(x[c + 4], x[c + 5], kBF16);
-          u.w = pack2(x[c + 6], x[c + 7], kBF16);
-          *reinterpret_cast<uint4*>(sp + sw128_offset(r, c)) = u;
+        // columns past the tile's valid keys hold stale values and are masked below
+        float x[HALF];
+        tmem_ld32(tS + lane_addr + st * BN + c0, x);
+        tmem_ld32(tS + lane_addr + st * BN + c0 + 32, x + 32);
+        tmem_wait_ld();
+        tc_fence_before();
+        mbar_arrive(bar[S_EMPTY + st]);
+
+        const bool lmk = t < n_lt;
+        const int n0 = lmk ? 0 : band_lo + BN * (t - n_lt);
+        // valid columns of this thread: [vlo, vhi] (band) or [0, vhi] (landmarks)
+        int vlo, vhi;
+        if (lmk) {
+          vlo = 0;
+          vhi = cnt - BN * t - c0 - 1;
+        } else {
+          vlo = lo - n0 - c0;  // lo = INT_MAX for a row without band: stays positive
+          vhi = hi - n0 - c0;
         }
-      }
-      if (!lmk && !all_out) {
-        // soft window edge on this row's edge keys in this thread's columns:
-        // p *= σ((w̃ − d)/τ); the key at distance d_e0 + e sits in column ce0 − e
-        const int ce0 = i - d_e0 - n0 - c0;
-        const bool has = ne > 0 && ce0 >= 0 && ce0 - (ne - 1) <= HALF - 1;
-        if (!slow_edge) {
-          if (__any_sync(0xffffffffu, has)) {
-            // all loads first, then all stores: the entries are distinct
-            float pv[kMaxEdge];
+        const bool all_in = __all_sync(0xffffffffu, vlo <= 0 && vhi >= HALF - 1);
+        const bool all_out = __all_sync(0xffffffffu, vhi < 0 || vlo > HALF - 1 || vlo > vhi);
+        float xs = lmk ? 1.0f : sl2;  // multiplier applied inside exp2
+        if (lmk) {
+          const float* lw2 = in.lmk_lw2 + BN * t + c0;
 #pragma unroll
-            for (int e = 0; e < kMaxEdge; ++e) {
-              const int c = ce0 - e;
-              const bool in = has && e < ne && c >= 0 && c < HALF;
-              pv[e] = in ? to_f32<T>(*reinterpret_cast<const T*>(sp + sw128_offset(r, c))) : 0.f;
-            }
+          for (int c = 0; c < HALF; ++c) x[c] = fmaf(x[c], sl2, lw2[c]);
+        }
+        float mt = -INFINITY;
+        if (!all_out) {
+          if (!all_in) {
+            const uint32_t m_lo = range_mask32(vlo, vhi), m_hi = range_mask32(vlo - 32, vhi - 32);
 #pragma unroll
-            for (int e = 0; e < kMaxEdge; ++e) {
-              const int c = ce0 - e;
-              if (has && e < ne && c >= 0 && c < HALF) {
-                *reinterpret_cast<T*>(sp + sw128_offset(r, c)) = from_f32<T>(pv[e] * eg[e]);
-                l -= pv[e] * (1.0f - eg[e]);
+            for (int c = 0; c < 32; ++c) x[c] = (m_lo >> c) & 1u ? x[c] : -INFINITY;
+#pragma unroll
+            for (int c = 0; c < 32; ++c) x[32 + c] = (m_hi >> c) & 1u ? x[32 + c] : -INFINITY;
+          }
+          float mx[8];
+#pragma unroll
+          for (int q = 0; q < 8; ++q) mx[q] = max3(x[2 * q], x[2 * q + 1], x[16 + 2 * q]);
+#pragma unroll
+          for (int c = 32; c < HALF; c += 16)
+#pragma unroll
+            for (int q = 0; q < 8; ++q) mx[q] = max3(mx[q], x[c + 2 * q], x[c + 2 * q + 1]);
+#pragma unroll
+          for (int q = 0; q < 8; ++q) mx[q] = fmaxf(mx[q], x[16 + 2 * q + 1]);
+          mt = max3(max3(mx[0], mx[1], mx[2]), max3(mx[3], mx[4], mx[5]), fmaxf(mx[6], mx[7]));
+          if (!lmk) mt *= sl2;
+        }
+        const float m_new = fmaxf(m, mt);
+        bool rescale = false;
+        float factor = 1.0f;
+        if (m == -INFINITY) {
+          m = m_new;
+        } else if (m_new > m + kRescaleThreshold) {
+          factor = exp2f(m - m_new);
+          m = m_new;
+          rescale = true;
+        }
+        if (!all_out) {
+          const float ms = (m == -INFINITY) ? 0.f : m;
+          float sm8[8];
+#pragma unroll
+          for (int q = 0; q < 8; ++q) sm8[q] = 0.f;
+#pragma unroll
+          for (int c = 0; c < HALF; ++c) {
+            x[c] = fast_exp2(fmaf(x[c], xs, -ms));
+            sm8[c & 7] += x[c];
+          }
+          const float sum = ((sm8[0] + sm8[1]) + (sm8[2] + sm8[3])) + ((sm8[4] + sm8[5]) + (sm8[6] + sm8[7]));
+          l = l * factor + sum;
+        } else {
+          l = l * factor;
+        }
+
+        // this half's P chunk and O_h are free once its previous P·V has completed
+        if (g >= 1) {
+          ok = mbar_wait(bar[O_DONE + half], (g - 1) & 1, abort_flag, p.status);
+          if (!__all_sync(0xffffffffu, ok)) { ok = false; break; }
+          tc_fence_after();
+        }
+        if (all_out) {
+          const uint4 z = make_uint4(0u, 0u, 0u, 0u);
+#pragma unroll
+          for (int c8 = 0; c8 < HALF / 8; ++c8) *reinterpret_cast<uint4*>(sp + sw128_offset(r, c8 * 8)) = z;
+        } else {
+#pragma unroll
+          for (int c8 = 0; c8 < HALF / 8; ++c8) {
+            const int c = c8 * 8;
+            uint4 u;
+            u.x = pack2(x[c + 0], x[c + 1], kBF16);
+            u.y = pack2(x[c + 2], x[c + 3], kBF16);
+            u.z = pack2(x[c + 4], x[c + 5], kBF16);
+            u.w = pack2(x[c + 6], x[c + 7], kBF16);
+            *reinterpret_cast<uint4*>(sp + sw128_offset(r, c)) = u;
+          }
+        }
+        if (!lmk && !all_out) {
+          // soft window edge on this row's edge keys in this thread's columns:
+          // p *= σ((w̃ − d)/τ); the key at distance d_e0 + e sits in column ce0 − e
+          const int ce0 = i - d_e0 - n0 - c0;
+          const bool has = ne > 0 && ce0 >= 0 && ce0 - (ne - 1) <= HALF - 1;
+          if (!slow_edge) {
+            if (__any_sync(0xffffffffu, has)) {
+              // all loads first, then all stores: the entries are distinct
+              float pv[kMaxEdge];
+#pragma unroll
+              for (int e = 0; e < kMaxEdge; ++e) {
+                const int c = ce0 - e;
+                const bool inr = has && e < ne && c >= 0 && c < HALF;
+                pv[e] = inr ? to_f32<T>(*reinterpret_cast<const T*>(sp + sw128_offset(r, c))) : 0.f;
+              }
+#pragma unroll
+              for (int e = 0; e < kMaxEdge; ++e) {
+                const int c = ce0 - e;
+                if (has && e < ne && c >= 0 && c < HALF) {
+                  *reinterpret_cast<T*>(sp + sw128_offset(r, c)) = from_f32<T>(pv[e] * eg[e]);
+                  l -= pv[e] * (1.0f - eg[e]);
+                }
               }
             }
-          }
-        } else if (has) {
-          for (int e = max(0, ce0 - (HALF - 1)); e < ne && ce0 - e >= 0; ++e) {
-            const int c = ce0 - e;
-            T* ep = reinterpret_cast<T*>(sp + sw128_offset(r, c));
-            const float pv = to_f32<T>(*ep);
-            const float z = (rw.wt - (float)(d_e0 + e)) * inv_tau;
-            const float sg = 1.0f / (1.0f + expf(-z));
-            *ep = from_f32<T>(pv * sg);
-            l -= pv * (1.0f - sg);
+          } else if (has) {
+            for (int e = max(0, ce0 - (HALF - 1)); e < ne && ce0 - e >= 0; ++e) {
+              const int c = ce0 - e;
+              T* ep = reinterpret_cast<T*>(sp + sw128_offset(r, c));
+              const float pv = to_f32<T>(*ep);
+              const float z = (wt - (float)(d_e0 + e)) * inv_tau;
+              const float sg = 1.0f / (1.0f + expf(-z));
+              *ep = from_f32<T>(pv * sg);
+              l -= pv * (1.0f - sg);
+            }
           }
         }
-      }
-      // rescale O_h once P is out of registers; a finite running max implies an
-      // earlier tile had valid keys in this half, so O_h has been written
-      // whenever a rescale happens
-      if (__any_sync(0xffffffffu, rescale)) {
+        // rescale O_h once P is out of registers; a finite running max implies an
+        // earlier tile of this item had valid keys in this half, so O_h has been
+        // written (and holds this item's sums) whenever a rescale happens
+        if (__any_sync(0xffffffffu, rescale)) {
 #pragma unroll
-        for (int ch = 0; ch < D / 32; ++ch) {
-          float o[32];
-          tmem_ld32(tOh + lane_addr + ch * 32, o);
-          tmem_wait_ld();
-          const float f = rescale ? factor : 1.0f;
+          for (int ch = 0; ch < D / 32; ++ch) {
+            float o[32];
+            tmem_ld32(tOh + lane_addr + ch * 32, o);
+            tmem_wait_ld();
+            const float f = rescale ? factor : 1.0f;
 #pragma unroll
-          for (int j = 0; j < 32; ++j) o[j] *= f;
-          tmem_st32(tOh + lane_addr + ch * 32, o);
+            for (int j = 0; j < 32; ++j) o[j] *= f;
+            tmem_st32(tOh + lane_addr + ch * 32, o);
+          }
+          tmem_wait_st();
         }
-        tmem_wait_st();
+        fence_async_smem();
+        tc_fence_before();
+        mbar_arrive(bar[P_FULL + half]);
       }
-      fence_async_smem();
-      tc_fence_before();
-      mbar_arrive(bar[P_FULL + half]);
-    }
-    // ---- epilogue: merge the two halves of each row, O / l, LSE
-    if (ok && n_tiles > 0) {
-      ok = mbar_wait(bar[O_DONE], (n_tiles - 1) & 1, abort_flag, p.status) &&
-           mbar_wait(bar[O_DONE + 1], (n_tiles - 1) & 1, abort_flag, p.status);
+      if (!ok) break;
+      // ---- epilogue: merge the two halves of each row, O / l, LSE
+      const int gl = gt + n_tiles - 1;  // the item's last tile
+      ok = mbar_wait(bar[O_DONE], gl & 1, abort_flag, p.status) &&
+           mbar_wait(bar[O_DONE + 1], gl & 1, abort_flag, p.status);
       ok = __all_sync(0xffffffffu, ok);
+      if (!ok) break;
       tc_fence_after();
-    }
-    sm.m_half[half][r] = m;
-    sm.l_half[half][r] = l;
-    mbar_arrive(bar[EPI]);
-    ok = __all_sync(0xffffffffu, mbar_wait(bar[EPI], 0, abort_flag, p.status) && ok);
-    const float mh0 = sm.m_half[0][r], mh1 = sm.m_half[1][r];
-    const float lh0 = sm.l_half[0][r], lh1 = sm.l_half[1][r];
-    const float mm = fmaxf(mh0, mh1);
-    // a half with l = 0 never had a valid key and its O_h may be unwritten
-    const float f0 = lh0 > 0.f ? exp2f(mh0 - mm) : 0.f;
-    const float f1 = lh1 > 0.f ? exp2f(mh1 - mm) : 0.f;
-    const float lt = lh0 * f0 + lh1 * f1;
-    const bool nonempty = lt > 1e-9f && n_tiles > 0;
-    const float inv_l = nonempty ? 1.0f / lt : 0.f;
-    const bool use0 = nonempty && lh0 > 0.f, use1 = nonempty && lh1 > 0.f;
-    if (ok) {
-      // Stage the block's O rows in shared memory (all MMAs and loads are done, so
-      // the K / V buffers are free), then store them row-contiguously: bf16 rows
-      // in sm.v, fp32 rows in sm.k, 16-byte units XOR-swizzled by row % 8.
-      uint8_t* stage_h = sm.v[0];
-      uint8_t* stage_f = sm.k[0];
-      constexpr int kUnitsH = D * 2 / 16, kUnitsF = D * 4 / 16;  // 16-byte units per row
+      sm.m_half[ib][half][r] = m;
+      sm.l_half[ib][half][r] = l;
+      if (!(ok = epi_sync())) break;
+      const float mh0 = sm.m_half[ib][0][r], mh1 = sm.m_half[ib][1][r];
+      const float lh0 = sm.l_half[ib][0][r], lh1 = sm.l_half[ib][1][r];
+      const float mm = fmaxf(mh0, mh1);
+      // a half with l = 0 never had a valid key and its O_h may hold an earlier item's sums
+      const float f0 = lh0 > 0.f ? exp2f(mh0 - mm) : 0.f;
+      const float f1 = lh1 > 0.f ? exp2f(mh1 - mm) : 0.f;
+      const float lt = lh0 * f0 + lh1 * f1;
+      const bool nonempty = lt > 1e-9f;
+      const float inv_l = nonempty ? 1.0f / lt : 0.f;
+      const bool use0 = nonempty && lh0 > 0.f, use1 = nonempty && lh1 > 0.f;
+      if (row_ok && half == 0) p.lse[(s0 + i) * p.H + h] = nonempty ? (mm + log2f(lt)) * kLn2 : -INFINITY;
+      // O rows staged in the (idle) P buffer, 128 rows × 256 B with 16-byte units
+      // XOR-swizzled by row % 8, then stored row-contiguously: the input-dtype O in
+      // one round (D·2 bytes per row), or the fp32 O in D/64 rounds of 64 columns
+      // (256 bytes per row; round k: output columns [64k, 64k + 64))
+      const bool f32_out = p.o_f32 != nullptr;
+      const int rounds = f32_out ? D / 64 : 1;
+      const int units = f32_out ? 16 : D / 8;  // 16-byte units per staged row
+      const int rows = min(BM, L - m0);
+      const int64_t HD = (int64_t)p.H * D;
+      uint8_t* stage = sm.p;
+      for (int rd = 0; rd < rounds; ++rd) {
 #pragma unroll
-      for (int ch = 0; ch < D / 32; ++ch) {  // 16 columns at a time
-        const int col = half * (D / 2) + ch * 16;
-        float o0[16], o1[16];
-        if (n_tiles > 0) {
+        for (int ch = 0; ch < D / 32; ++ch) {  // this thread's D/2 output columns, 16 at a time
+          const int col = half * (D / 2) + ch * 16;
+          if (f32_out && col / 64 != rd) continue;
+          float o0[16], o1[16];
           tmem_ld16(tO + lane_addr + col, o0);
           tmem_ld16(tO + D + lane_addr + col, o1);
           tmem_wait_ld();
-        }
 #pragma unroll
-        for (int j = 0; j < 16; ++j) {
-          const float a0 = use0 ? o0[j] * f0 : 0.f;
-          const float a1 = use1 ? o1[j] * f1 : 0.f;
-          o0[j] = round_to<T>((a0 + a1) * inv_l);
-        }
+          for (int j = 0; j < 16; ++j) {
+            const float a0 = use0 ? o0[j] * f0 : 0.f;
+            const float a1 = use1 ? o1[j] * f1 : 0.f;
+            o0[j] = round_to<T>((a0 + a1) * inv_l);
+          }
+          if (f32_out) {
 #pragma unroll
-        for (int j = 0; j < 16; j += 8) {
-          const int uh = (col + j) / 8;
-          uint4 u;
-          u.x = pack2(o0[j + 0], o0[j + 1], kBF16);
-          u.y = pack2(o0[j + 2], o0[j + 3], kBF16);
-          u.z = pack2(o0[j + 4], o0[j + 5], kBF16);
-          u.w = pack2(o0[j + 6], o0[j + 7], kBF16);
-          *reinterpret_cast<uint4*>(stage_h + r * (kUnitsH * 16) + ((uh ^ (r & 7)) << 4)) = u;
-          const int uf = (col + j) / 4;
-          *reinterpret_cast<float4*>(stage_f + r * (kUnitsF * 16) + ((uf ^ (r & 7)) << 4)) =
-              make_float4(o0[j], o0[j + 1], o0[j + 2], o0[j + 3]);
-          *reinterpret_cast<float4*>(stage_f + r * (kUnitsF * 16) + (((uf + 1) ^ (r & 7)) << 4)) =
-              make_float4(o0[j + 4], o0[j + 5], o0[j + 6], o0[j + 7]);
-        }
-      }
-      if (row_ok && half == 0) p.lse[(s0 + i) * p.H + h] = nonempty ? (mm + log2f(lt)) * kLn2 : -INFINITY;
-      mbar_arrive(bar[EPI2]);
-      if (__all_sync(0xffffffffu, mbar_wait(bar[EPI2], 0, abort_flag, p.status))) {
-        const int rows = min(BM, L - m0);
-        const int64_t HD = (int64_t)p.H * D;
-        uint8_t* og = reinterpret_cast<uint8_t*>(p.o) + ((s0 + m0) * HD + (int64_t)h * D) * 2;
-        for (int u = tid; u < rows * kUnitsH; u += kRowThreads) {
-          const int rr = u / kUnitsH, uu = u % kUnitsH;
-          *reinterpret_cast<uint4*>(og + rr * HD * 2 + uu * 16) =
-              *reinterpret_cast<const uint4*>(stage_h + rr * (kUnitsH * 16) + ((uu ^ (rr & 7)) << 4));
-        }
-        if (p.o_f32) {
-          uint8_t* ofg = reinterpret_cast<uint8_t*>(p.o_f32) + ((s0 + m0) * HD + (int64_t)h * D) * 4;
-          for (int u = tid; u < rows * kUnitsF; u += kRowThreads) {
-            const int rr = u / kUnitsF, uu = u % kUnitsF;
-            *reinterpret_cast<uint4*>(ofg + rr * HD * 4 + uu * 16) =
-                *reinterpret_cast<const uint4*>(stage_f + rr * (kUnitsF * 16) + ((uu ^ (rr & 7)) << 4));
+            for (int u = 0; u < 4; ++u) {
+              const int un = (col - 64 * rd) / 4 + u;
+              *reinterpret_cast<float4*>(stage + r * 256 + ((un ^ (r & 7)) << 4)) =
+                  make_float4(o0[4 * u], o0[4 * u + 1], o0[4 * u + 2], o0[4 * u + 3]);
+            }
+          } else {
+#pragma unroll
+            for (int u = 0; u < 2; ++u) {
+              const int un = col / 8 + u;
+              *reinterpret_cast<uint4*>(stage + r * 256 + ((un ^ (r & 7)) << 4)) =
+                  make_uint4(pack2(o0[8 * u + 0], o0[8 * u + 1], kBF16), pack2(o0[8 * u + 2], o0[8 * u + 3], kBF16),
+                             pack2(o0[8 * u + 4], o0[8 * u + 5], kBF16), pack2(o0[8 * u + 6], o0[8 * u + 7], kBF16));
+            }
           }
         }
+        if (rd == rounds - 1) {
+          tc_fence_before();
+          mbar_arrive(bar[O_FREE]);  // O is read: the next item's P·V may overwrite it
+        }
+        if (!(ok = epi_sync())) break;
+        uint8_t* dst = f32_out ? reinterpret_cast<uint8_t*>(p.o_f32) + ((s0 + m0) * HD + (int64_t)h * D + rd * 64) * 4
+                               : reinterpret_cast<uint8_t*>(p.o) + ((s0 + m0) * HD + (int64_t)h * D) * 2;
+        const int64_t row_bytes = HD * (f32_out ? 4 : 2);
+        for (int un = r + BM * half; un < rows * units; un += kRowThreads) {
+          const int rr = un / units, uu = un % units;
+          *reinterpret_cast<uint4*>(dst + rr * row_bytes + uu * 16) =
+              *reinterpret_cast<const uint4*>(stage + rr * 256 + ((uu ^ (rr & 7)) << 4));
+        }
+        if (!(ok = epi_sync())) break;  // the staging area is reused (next round, or the next item's P)
       }
+      if (!ok) break;
+      gt += n_tiles;
+      __syncwarp();
+      if (lane == 0) mbar_arrive(bar[INFO_EMPTY + ib]);
     }
   }
   tc_fence_before();
@@ -599,7 +701,18 @@ cudaError_t launch_tc_fwd(const DsaltAttnParams& p, cudaStream_t stream) {
   const size_t smem = std::max(sizeof(FwdSmem<D>) + 1024, (size_t)(116 * 1024));
   cudaError_t e = ensure_smem((const void*)tc_fwd_kernel<T, D>, smem);
   if (e != cudaSuccess) return e;
-  dim3 grid((unsigned)p.max_blocks, (unsigned)p.H);
+  // persistent: one CTA per SM walks the (head, query block) items round-robin
+  static int sms[64] = {};
+  int dev = 0;
+  e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+  if (sms[dev] <= 0) {
+    e = cudaDeviceGetAttribute(&sms[dev], cudaDevAttrMultiProcessorCount, dev);
+    if (e != cudaSuccess) return e;
+  }
+  const long long items = (long long)p.max_blocks * p.H;
+  const unsigned grid = (unsigned)std::max<long long>(1, std::min<long long>(items, sms[dev]));
   tc_fwd_kernel<T, D><<<grid, kThreads, smem, stream>>>(a);
   return cudaGetLastError();
 }

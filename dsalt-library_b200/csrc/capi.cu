@@ -78,8 +78,8 @@ static int check_attn(const DsaltAttnParams* p, int stage) {
   if (p->kp > 0 && (!p->lmk_k || !p->lmk_v || !p->pos_sorted || !p->w_sorted)) return DSALT_ERR_ARG;
   if (!aligned16(p->q) || !aligned16(p->k) || !aligned16(p->v)) return DSALT_ERR_ALIGN;
   switch (stage) {
-    case 0: if (!p->o || !p->lse) return DSALT_ERR_ARG; break;
-    case 1: if (!p->o || !p->dout || !p->delta) return DSALT_ERR_ARG; break;
+    case 0: if ((!p->o && !p->o_f32) || !p->lse) return DSALT_ERR_ARG; break;
+    case 1: if ((!p->o && !p->o_f32) || !p->dout || !p->delta) return DSALT_ERR_ARG; break;
     case 2: if (!p->dout || !p->lse || !p->delta || !p->dk || !p->dv || !p->seq_wmax) return DSALT_ERR_ARG;
             if (p->kp > 0 && (!p->lmk_slot || !p->perm)) return DSALT_ERR_ARG;
             break;

@@ -211,17 +211,23 @@ def _params(prep: Prepared, q_c, k_c, v_c, tau_win: float, win_edge: float, impl
 
 
 def forward(q_c, k_c, v_c, prep: Prepared, tau_win: float, win_edge: float, impl: int, f32_out: bool = True):
-    """Run the forward; returns ``(o [T,H,D] input dtype, o_f32 [T,H,D] fp32, lse [T,H] fp32)``.
+    """Run the forward; returns ``(o, o_out, lse [T,H] fp32)``: the O the backward
+    reads and the op's output.
 
-    With ``f32_out=False`` no fp32 copy is written and the second item is ``o``.
+    16-bit inputs with ``f32_out`` write only the fp32 O (the input-dtype-rounded
+    values, the reference's ``out.float()``), which is both items; with
+    ``f32_out=False`` only the input-dtype O.  fp32 inputs write their fp32 O.
     """
-    o = torch.empty_like(q_c)
-    o_f32 = torch.empty(q_c.shape, dtype=torch.float32, device=q_c.device) \
-        if q_c.dtype != torch.float32 and f32_out else None
     lse = torch.empty(prep.T, prep.H, dtype=torch.float32, device=q_c.device)
-    p = _params(prep, q_c, k_c, v_c, tau_win, win_edge, impl, o=o, o_f32=o_f32, lse=lse)
+    if q_c.dtype != torch.float32 and f32_out:
+        o_f32 = torch.empty(q_c.shape, dtype=torch.float32, device=q_c.device)
+        p = _params(prep, q_c, k_c, v_c, tau_win, win_edge, impl, o=None, o_f32=o_f32, lse=lse)
+        _ext.call("dsalt_attn_fwd", p)
+        return o_f32, o_f32, lse
+    o = torch.empty_like(q_c)
+    p = _params(prep, q_c, k_c, v_c, tau_win, win_edge, impl, o=o, o_f32=None, lse=lse)
     _ext.call("dsalt_attn_fwd", p)
-    return o, (o_f32 if o_f32 is not None else o), lse
+    return o, o, lse
 
 
 def backward(grad_out, q_c, k_c, v_c, o, lse, prep: Prepared, tau_win: float, win_edge: float,
@@ -252,7 +258,10 @@ def backward(grad_out, q_c, k_c, v_c, o, lse, prep: Prepared, tau_win: float, wi
                            dtype=torch.float32, device=dev) if prep.kp > 0 else None
     # per-query records (LSE, Delta, window, soft-edge factors) of the tensor-core stages
     qrec = torch.empty(H, T, _ext.QREC_FLOATS, dtype=torch.float32, device=dev)
-    p = _params(prep, q_c, k_c, v_c, tau_win, win_edge, impl, scale, o=o, lse=lse, dout=do_c, dout_f32=do_f32,
+    # O as the forward wrote it: the input dtype, or only the fp32 copy of 16-bit inputs
+    o_in, o32 = (None, o) if (o.dtype == torch.float32 and q_c.dtype != torch.float32) else (o, None)
+    p = _params(prep, q_c, k_c, v_c, tau_win, win_edge, impl, scale, o=o_in, o_f32=o32, lse=lse, dout=do_c,
+                dout_f32=do_f32,
                 delta=delta, dq=dq, dk=dk, dv=dv, dw_head=dw_head, dw=dw, d_lw=d_lw, lmk_grad=lmk_grad,
                 qrec=qrec)
     # the dSᵀ tiles the dK/dV stage stores for the dQ stage (tensor-core family)

@@ -150,8 +150,11 @@ typedef struct DsaltAttnParams {
   const int32_t* pos_sorted; const float* w_sorted; const int32_t* perm;
   const int32_t* lmk_slot;
   /* forward outputs */
-  void* o;                    /* [T,H,D] dtype (saved for the backward) */
-  float* o_f32;               /* [T,H,D] fp32 copy of bf16/f16-rounded O, or NULL */
+  void* o;                    /* [T,H,D] dtype, or NULL when o_f32 is given for 16-bit
+                                 inputs (then only the fp32 O is written, and the
+                                 backward stages read that one) */
+  float* o_f32;               /* [T,H,D] fp32 O holding the bf16/f16-rounded values
+                                 (the reference op's output), or NULL */
   float* lse;                 /* [T,H] natural-log LSE, -inf for empty rows */
   /* backward */
   const void* dout;           /* [T,H,D] dtype (written by the preprocess stage when

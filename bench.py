@@ -443,6 +443,111 @@ def run_config4(args):
         dist.destroy_process_group()
 
 
+# ------------------------------------------------------ selection and gating kernels
+SEL_SHAPES = {
+    # the standalone op's shapes (d_model = H·D, as in a DSALT layer of that width)
+    "config2": dict(lens=[4096] * 4, H=16, D=128, d_model=2048, k=64, n_min=32, n_max=512),
+    "config5": dict(lens=[32768], H=32, D=128, d_model=4096, k=256, n_min=128, n_max=2048),
+}
+
+
+def run_selection(args):
+    """HBM throughput of the selection and gating kernels (window gate, hybrid score,
+    top-k, and their backward passes) at the config-2 and config-5 shapes, bf16,
+    each C-ABI entry point timed alone with CUDA events (``--steps`` launches after
+    ``--warmup``).  Bytes are algorithmic: every input read once and every output
+    written once (the hybrid score's internal norm / statistics scratch not counted).
+    The x·W_Vᵀ GEMM feeding the score is cuBLAS and not part of these kernels."""
+    import torch
+    from dsalt.kernels import _ext
+    dev = torch.device("cuda", int(os.environ.get("LOCAL_RANK", "0")))
+    torch.cuda.set_device(dev)
+    burst, sustained, hbm, src = peaks()
+    out = {}
+    shapes = [s for s in args.sel_shapes.split(",") if s]
+    for name in shapes:
+        c = SEL_SHAPES[name]
+        lens, H, D, dm, k = c["lens"], c["H"], c["D"], c["d_model"], c["k"]
+        T, S = sum(lens), len(lens)
+        g = torch.Generator(device=dev).manual_seed(3)
+        bf = torch.bfloat16
+        x = torch.randn(T, dm, generator=g, device=dev).to(bf)
+        W = (torch.randn(H * D, dm, generator=g, device=dev) / dm ** 0.5).to(bf)
+        xwv = x @ W.t()
+        gate_w = (torch.randn(dm, generator=g, device=dev) * 0.02).to(bf)
+        gate_b = torch.zeros(1, device=dev, dtype=bf)
+        alpha = torch.rand(H, generator=g, device=dev)
+        cu = torch.tensor([0] + list(__import__("itertools").accumulate(lens)), dtype=torch.int32, device=dev)
+        w_cont = torch.empty(T, dtype=bf, device=dev)
+        w_disc = torch.empty(T, device=dev)
+        logits = torch.empty(T, device=dev)
+        scores, z_v = torch.empty(T, H, device=dev), torch.empty(T, H, device=dev)
+        z_x = torch.empty(T, device=dev)
+        stats, norms = torch.empty(2 + 2 * H, device=dev), torch.empty((1 + H) * T, device=dev)
+        idx = torch.empty(H, S, k, dtype=torch.int64, device=dev)
+        g_s = torch.randn(T, H, generator=g, device=dev)
+        sums, d_alpha = torch.empty(2 * (1 + H), device=dev), torch.empty(H, device=dev)
+        sparts = torch.empty((T + _ext.SCORE_BWD_TOKENS - 1) // _ext.SCORE_BWD_TOKENS, 2 * (1 + H) + H, device=dev)
+        coef_x, coef_v = torch.empty(T, device=dev), torch.empty(T, H, device=dev)
+        dl = torch.randn(T, generator=g, device=dev)
+        dx = torch.empty_like(x)
+        parts = torch.empty((T + _ext.WIN_GATE_ROWS_PER_PART - 1) // _ext.WIN_GATE_ROWS_PER_PART, dm, device=dev)
+        sx, sv = torch.empty_like(x), torch.empty_like(xwv)
+        P = _ext
+        wg = P.WinGateParams(x=P.ptr(x), weight=P.ptr(gate_w), bias=P.ptr(gate_b), w_cont=P.ptr(w_cont), w_f32=0,
+                             w_disc=P.ptr(w_disc), logits=P.ptr(logits), T=T, d_model=dm,
+                             n_min=float(c["n_min"]), n_max=float(c["n_max"]), dtype=P.BF16)
+        sc = P.ScoreParams(x=P.ptr(x), xwv=P.ptr(xwv), alpha=P.ptr(alpha), scores=P.ptr(scores), z_x=P.ptr(z_x),
+                           z_v=P.ptr(z_v), stats=P.ptr(stats), norms=P.ptr(norms), T=T, d_model=dm, H=H, n_kv=H,
+                           dh=D, dtype=P.BF16)
+        tk = P.TopkParams(scores=P.ptr(scores), w_sizes=P.ptr(w_disc), cu_seqlens=P.ptr(cu), idx=P.ptr(idx), T=T,
+                          H=H, S=S, k=k, max_len=max(lens))
+        wgb = P.WinGateBwdParams(x=P.ptr(x), weight=P.ptr(gate_w), dl=P.ptr(dl), dx=P.ptr(dx), dw_part=P.ptr(parts),
+                                 T=T, d_model=dm, dtype=P.BF16)
+        scb = P.ScoreBwdParams(g_s=P.ptr(g_s), alpha=P.ptr(alpha), z_x=P.ptr(z_x), z_v=P.ptr(z_v),
+                               norms=P.ptr(norms), stats=P.ptr(stats), sums=P.ptr(sums), partials=P.ptr(sparts),
+                               d_alpha=P.ptr(d_alpha),
+                               coef_x=P.ptr(coef_x), coef_v=P.ptr(coef_v), T=T, H=H, n_kv=H)
+        srx = P.ScaleRowsParams(x=P.ptr(x), coef=P.ptr(coef_x), out=P.ptr(sx), T=T, groups=1, width=dm, dtype=P.BF16)
+        srv = P.ScaleRowsParams(x=P.ptr(xwv), coef=P.ptr(coef_v), out=P.ptr(sv), T=T, groups=H, width=D,
+                                dtype=P.BF16)
+        e2, e4, e8 = 2, 4, 8
+        kernels = [  # (entry point, params, algorithmic bytes)
+            ("dsalt_win_gate", wg, T * dm * e2 + dm * e2 + T * (e2 + e4 + e4)),
+            ("dsalt_hybrid_scores", sc, T * dm * e2 + T * H * D * e2 + T * H * e4 * 2 + T * e4),
+            ("dsalt_select_topk", tk, T * H * e4 + T * e4 + H * S * k * e8),
+            ("dsalt_win_gate_bwd", wgb, T * dm * e2 + dm * e2 + T * e4 + T * dm * e2 + parts.numel() * e4),
+            ("dsalt_hybrid_scores_bwd", scb, T * H * e4 * 2 + T * e4 + (1 + H) * T * e4 + T * (1 + H) * e4),
+            ("dsalt_scale_rows:x", srx, 2 * T * dm * e2 + T * e4),
+            ("dsalt_scale_rows:xwv", srv, 2 * T * H * D * e2 + T * H * e4),
+        ]
+        res = {}
+        for kname, prm, nbytes in kernels:
+            entry = kname.split(":")[0]
+            for _ in range(max(args.warmup, 1)):
+                P.call(entry, prm)
+            torch.cuda.synchronize()
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record()
+            for _ in range(args.steps):
+                P.call(entry, prm)
+            b.record()
+            torch.cuda.synchronize()
+            us = a.elapsed_time(b) / args.steps * 1e3
+            gbs = nbytes / (us * 1e-6) / 1e9
+            res[kname] = {"us": round(us, 2), "bytes": int(nbytes), "gbs": round(gbs, 1),
+                          "frac_of_hbm": round(gbs / hbm, 3)}
+        out[name] = {"shape": f"T={T} ({S} x {lens[0]}), H={H}, D={D}, d_model={dm}, k={k}, bf16", "kernels": res}
+    tot_b = sum(v["bytes"] for o in out.values() for v in o["kernels"].values())
+    tot_us = sum(v["us"] for o in out.values() for v in o["kernels"].values())
+    line = {"metric": "HBM GB/s of the selection and gating kernels", "value": tot_b / (tot_us * 1e-6) / 1e9,
+            "unit": "GB/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+            "config": {"workload": "selection/gating kernels at " + ", ".join(shapes) + " shapes"},
+            "hbm_peak_gbs": hbm, "peak_source": src, "shapes": out}
+    print(json.dumps(line), flush=True)
+
+
 # --------------------------------------------------------------------- main
 CONFIG5 = dict(N=32768, H=32, D=128, k=256, n_min=128, n_max=2048)
 METRIC5 = "attended-pair TFLOP/s inference fwd (N=32768, D=128, H=32)"
@@ -645,10 +750,11 @@ def main():
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--workload", default="config2", choices=list(WORKLOADS) + ["config4", "config5"])
+    ap.add_argument("--workload", default="config2", choices=list(WORKLOADS) + ["config4", "config5", "selection"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-triton-ref", action="store_true", help="skip timing the reference's Triton op")
+    ap.add_argument("--sel-shapes", default="config2,config5", help="selection: shapes to run")
     ap.add_argument("--bucket-mb", type=int, default=100, help="config4: DDP bucket size (MB)")
     ap.add_argument("--ddp-bf16-grads", action="store_true", help="config4: bf16 gradient all-reduce hook")
     args = ap.parse_args()
@@ -663,6 +769,13 @@ def main():
         return
     if args.workload == "config5":
         run_config5(args)
+        return
+    if args.workload == "selection":
+        if args.impl == "reference":
+            print(json.dumps({"impl": "reference", "unavailable": "the selection kernels have no CPU arm; the op "
+                              "workloads carry the CPU reference arm"}), flush=True)
+            return
+        run_selection(args)
         return
     wl = WORKLOADS[args.workload]
     if args.impl == "reference":

@@ -136,7 +136,7 @@ __device__ __forceinline__ int num_items(const DsaltAttnParams& p) {
   return __ldg(p.num_blocks) * p.H;
 }
 
-// Decode item idx; called by whole warps (the landmark slot count is a ballot).
+// Decode item idx (any single thread may call it).
 template <bool LMK>
 __device__ __forceinline__ Item decode_item(const DsaltAttnParams& p, int idx) {
   Item it;
@@ -153,15 +153,13 @@ __device__ __forceinline__ Item decode_item(const DsaltAttnParams& p, int idx) {
     it.L = (int)(__ldg(p.cu_seqlens + it.s + 1) - it.s0);
     it.lbase = ((int64_t)it.h * p.S + it.s) * p.kp;
     it.key0 = chunk * BM;
-    // valid slots are a prefix of the sorted list: count them 32 at a time
-    const int lane = threadIdx.x & 31;
-    int nv = 0;
-#pragma unroll
-    for (int k = 0; k < BM / 32; ++k) {
-      const int c = it.key0 + 32 * k + lane;
-      const bool v = c < p.kp && __ldg(p.pos_sorted + it.lbase + c) >= 0;
-      nv += __popc(__ballot_sync(0xffffffffu, v));
+    // valid slots are a prefix of the sorted list: the chunk's first invalid slot by bisection
+    int lo_c = it.key0, hi_c = min(it.key0 + BM, p.kp);
+    while (lo_c < hi_c) {
+      const int mid = (lo_c + hi_c) >> 1;
+      if (__ldg(p.pos_sorted + it.lbase + mid) >= 0) lo_c = mid + 1; else hi_c = mid;
     }
+    const int nv = lo_c - it.key0;
     it.nkeys = nv;
     it.chunk = chunk;
     it.blk = 0;
@@ -246,9 +244,9 @@ __global__ void __launch_bounds__(kThreadsKV, 1) tc_bwd_dkdv_kernel(const __grid
       mbar_init(bar[SD_EMPTY + st], kRowThreads);
     }
     mbar_init(bar[PDS_FULL], kRowThreads);
-    mbar_init(bar[PDS_EMPTY], 3);  // the dV and dK MMAs, and the store of the dSᵀ tile
+    mbar_init(bar[PDS_EMPTY], 3);  // the dV and dK MMAs, and the store warp's copy of the dSᵀ tile
     mbar_init(bar[ROWS], kRowThreads);
-    mbar_init(bar[KV_DONE], 2);
+    mbar_init(bar[KV_DONE], 3);  // both MMA warps, and the store warp (the item's last tile copied)
     mbar_init(bar[ACC_EMPTY], kRowThreads);
     mbar_init(bar[FINAL], 1);
     mbar_init(bar[FINAL + 1], 1);
@@ -266,62 +264,93 @@ __global__ void __launch_bounds__(kThreadsKV, 1) tc_bwd_dkdv_kernel(const __grid
   const float inv_tau = 1.0f / p.tau_win;
   const int stride = gridDim.x;
 
-  if (warp == kProducerWarp) {
-    // ---------------------------------------------------- TMA warp: per item K/V, then the global Q/dO ring
+  if (warp == kProducerWarp && lane == 0) {
+    // ---------------------------------------------------- TMA lane: per item K/V, then the global Q/dO ring
     int gt = 0, gi = 0, g_issued = 0, kv_issued = 0;
     bool ok = true;
     for (int idx = blockIdx.x; ok && idx < n_items; idx += stride) {
       const Item it = decode_item<LMK>(p, idx);
       if (it.n_tiles == 0) continue;
-      if (lane == 0) {
-        if (gi >= 1) ok = mbar_wait(bar[KV_EMPTY], (gi - 1) & 1, abort_flag, p.status);
-        if (ok) {
-          const uint32_t kv_bytes = (LMK ? a.lmk_box : BM) * D * 2;
-          mbar_expect_tx(bar[KV_FULL], 2 * kv_bytes);
+      if (gi >= 1) ok = mbar_wait(bar[KV_EMPTY], (gi - 1) & 1, abort_flag, p.status);
+      if (ok) {
+        const uint32_t kv_bytes = (LMK ? a.lmk_box : BM) * D * 2;
+        mbar_expect_tx(bar[KV_FULL], 2 * kv_bytes);
 #pragma unroll
-          for (int c = 0; c < D / 64; ++c) {
-            if (LMK) {
-              tma_load_3d(smem_u32(sm.k + c * (BM * 128)), &a.tm_lk, bar[KV_FULL], c * 64, it.key0, it.h * p.S + it.s);
-              tma_load_3d(smem_u32(sm.v + c * (BM * 128)), &a.tm_lv, bar[KV_FULL], c * 64, it.key0, it.h * p.S + it.s);
-            } else {
-              tma_load_3d(smem_u32(sm.k + c * (BM * 128)), &a.tm_k, bar[KV_FULL], c * 64, it.h, (int)(it.s0 + it.key0));
-              tma_load_3d(smem_u32(sm.v + c * (BM * 128)), &a.tm_v, bar[KV_FULL], c * 64, it.h, (int)(it.s0 + it.key0));
-            }
+        for (int c = 0; c < D / 64; ++c) {
+          if (LMK) {
+            tma_load_3d(smem_u32(sm.k + c * (BM * 128)), &a.tm_lk, bar[KV_FULL], c * 64, it.key0, it.h * p.S + it.s);
+            tma_load_3d(smem_u32(sm.v + c * (BM * 128)), &a.tm_lv, bar[KV_FULL], c * 64, it.key0, it.h * p.S + it.s);
+          } else {
+            tma_load_3d(smem_u32(sm.k + c * (BM * 128)), &a.tm_k, bar[KV_FULL], c * 64, it.h, (int)(it.s0 + it.key0));
+            tma_load_3d(smem_u32(sm.v + c * (BM * 128)), &a.tm_v, bar[KV_FULL], c * 64, it.h, (int)(it.s0 + it.key0));
           }
-          kv_issued = gi + 1;
         }
-        for (int u = 0; ok && u < it.n_tiles; ++u) {
-          const int g = gt + u, st = g % kQStages;
-          if (g >= kQStages && !mbar_wait(bar[QDO_EMPTY + st], (g / kQStages - 1) & 1, abort_flag, p.status)) {
-            ok = false;
-            break;
-          }
-          const int q0 = it.q_start + BN * u;
-          mbar_expect_tx(bar[Q_FULL + st], BN * D * 2);
-#pragma unroll
-          for (int c = 0; c < D / 64; ++c)
-            tma_load_3d(smem_u32(sm.q[st] + c * (BN * 128)), &a.tm_q, bar[Q_FULL + st], c * 64, it.h,
-                        (int)(it.s0 + q0));
-          mbar_expect_tx(bar[DO_FULL + st], BN * D * 2);
-#pragma unroll
-          for (int c = 0; c < D / 64; ++c)
-            tma_load_3d(smem_u32(sm.dO[st] + c * (BN * 128)), &a.tm_do, bar[DO_FULL + st], c * 64, it.h,
-                        (int)(it.s0 + q0));
-          g_issued = g + 1;
-        }
+        kv_issued = gi + 1;
       }
-      ok = __shfl_sync(0xffffffffu, ok, 0);
+      for (int u = 0; ok && u < it.n_tiles; ++u) {
+        const int g = gt + u, st = g % kQStages;
+        if (g >= kQStages && !mbar_wait(bar[QDO_EMPTY + st], (g / kQStages - 1) & 1, abort_flag, p.status)) {
+          ok = false;
+          break;
+        }
+        const int q0 = it.q_start + BN * u;
+        mbar_expect_tx(bar[Q_FULL + st], BN * D * 2);
+#pragma unroll
+        for (int c = 0; c < D / 64; ++c)
+          tma_load_3d(smem_u32(sm.q[st] + c * (BN * 128)), &a.tm_q, bar[Q_FULL + st], c * 64, it.h,
+                      (int)(it.s0 + q0));
+        mbar_expect_tx(bar[DO_FULL + st], BN * D * 2);
+#pragma unroll
+        for (int c = 0; c < D / 64; ++c)
+          tma_load_3d(smem_u32(sm.dO[st] + c * (BN * 128)), &a.tm_do, bar[DO_FULL + st], c * 64, it.h,
+                      (int)(it.s0 + q0));
+        g_issued = g + 1;
+      }
       gt += it.n_tiles;
       ++gi;
     }
-    if (lane == 0) {
-      // never leave a TMA write in flight into shared memory
-      for (int g = max(0, g_issued - kQStages); g < g_issued; ++g) {
-        mbar_drain(bar[Q_FULL + g % kQStages], (g / kQStages) & 1);
-        mbar_drain(bar[DO_FULL + g % kQStages], (g / kQStages) & 1);
-      }
-      if (kv_issued > 0) mbar_drain(bar[KV_FULL], (kv_issued - 1) & 1);
+    // never leave a TMA write in flight into shared memory
+    for (int g = max(0, g_issued - kQStages); g < g_issued; ++g) {
+      mbar_drain(bar[Q_FULL + g % kQStages], (g / kQStages) & 1);
+      mbar_drain(bar[DO_FULL + g % kQStages], (g / kQStages) & 1);
     }
+    if (kv_issued > 0) mbar_drain(bar[KV_FULL], (kv_issued - 1) & 1);
+  } else if (warp == kProducerWarp && lane == 1) {
+    // ---------------------------------------------------- store lane: dSᵀ tiles to the scratch
+    // Bulk-copies each finished dSᵀ tile (after the soft-edge fix-up) to the
+    // ds_tiles scratch that the dQ stage reads, and releases the buffer to the rows
+    // (PDS_EMPTY) once the copy has read it; after an item's last tile it also
+    // completes KV_DONE, so that the epilogue's staging never overwrites a tile
+    // that is still being copied.
+    int gt = 0;
+    bool ok = true;
+    for (int idx = blockIdx.x; ok && idx < n_items; idx += stride) {
+      const Item it = decode_item<LMK>(p, idx);
+      const int n = it.n_tiles;
+      if (n == 0) continue;
+      for (int u = 0; ok && u < n; ++u) {
+        const int g = gt + u;
+        ok = mbar_wait(bar[PDS_FULL], g & 1, abort_flag, p.status);
+        if (!ok) break;
+        bool stored = false;
+        if (p.ds_tiles) {
+          const int64_t ti = ds_tile_index<LMK>(p, it, u);
+          if (ti >= 0) {
+            bulk_store(reinterpret_cast<uint8_t*>(p.ds_tiles) + ti * DSALT_DS_TILE_BYTES, smem_u32(sm.dst),
+                       DSALT_DS_TILE_BYTES);
+            bulk_commit();
+            stored = true;
+          } else {
+            flag_status(p.status, DSALT_DEV_BAD_INDEX);
+          }
+        }
+        if (stored) bulk_wait_read0();  // the buffer is read: the rows may overwrite it
+        mbar_arrive(bar[PDS_EMPTY]);
+      }
+      if (ok) mbar_arrive(bar[KV_DONE]);
+      gt += n;
+    }
+    bulk_wait_all();  // every tile store completes before the exit
   } else if (warp == kColWarp) {
     // ---------------------------------------------------- column warp: per-tile query records
     // Lane 0 bulk-copies each tile's records (written by the preprocess stage)
@@ -468,19 +497,6 @@ __global__ void __launch_bounds__(kThreadsKV, 1) tc_bwd_dkdv_kernel(const __grid
                (u > 0 || gi == 0 || mbar_wait(bar[ACC_EMPTY], (gi - 1) & 1, abort_flag, p.status));
           if (!ok) break;
           tc_fence_after();
-          // warp B also copies the finished dSᵀ tile to the scratch for the dQ stage
-          bool stored = false;
-          if (!is_a && p.ds_tiles) {
-            const int64_t ti = ds_tile_index<LMK>(p, it, u);
-            if (ti >= 0) {
-              bulk_store(reinterpret_cast<uint8_t*>(p.ds_tiles) + ti * DSALT_DS_TILE_BYTES, smem_u32(sm.dst),
-                         DSALT_DS_TILE_BYTES);
-              bulk_commit();
-              stored = true;
-            } else {
-              flag_status(p.status, DSALT_DEV_BAD_INDEX);
-            }
-          }
           const uint32_t ba = tile_acc(qs);
 #pragma unroll
           for (int kk = 0; kk < BN / 16; ++kk)
@@ -488,10 +504,6 @@ __global__ void __launch_bounds__(kThreadsKV, 1) tc_bwd_dkdv_kernel(const __grid
                     id_kv, (u > 0 || kk > 0) ? 1u : 0u);
           mma_commit(bar[PDS_EMPTY]);
           mma_commit(bar[QDO_EMPTY + qs]);
-          if (!is_a) {
-            if (stored) bulk_wait_read0();  // the buffer is read: the rows may overwrite it
-            mbar_arrive(bar[PDS_EMPTY]);
-          }
           if (u + 2 < n) {
             ok = issue_sd(g + 2);
             if (ok && u + 2 == n - 1) mma_commit(bar[KV_EMPTY]);
@@ -504,12 +516,11 @@ __global__ void __launch_bounds__(kThreadsKV, 1) tc_bwd_dkdv_kernel(const __grid
       ++gi;
     }
     if (lane == 0) {
-      // every issued MMA completes before TMEM is released, every tile store before the exit
+      // every issued MMA completes before TMEM is released
       mma_commit(bar[FINAL + (is_a ? 0 : 1)]);
       mbar_drain(bar[FINAL + (is_a ? 0 : 1)], 0);
-      if (!is_a) bulk_wait_all();
     }
-  } else {
+  } else if (warp < kRowWarps) {
     // ---------------------------------------------------- key-row warps (Pᵀ, dSᵀ)
     const int r = 32 * (warp & 3) + lane;  // key row / TMEM lane
     const int quarter = warp >> 2;

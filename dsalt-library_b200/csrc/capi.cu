@@ -328,6 +328,9 @@ int dsalt_selftest_wait_timeout(int32_t* status, void* stream) {
 int dsalt_hybrid_scores_bwd(const DsaltScoreBwdParams* p, void* stream) {
   if (!p || p->T < 0 || p->H <= 0 || p->n_kv <= 0 || p->H % p->n_kv != 0 || p->H > 4096) return DSALT_ERR_ARG;
   if (!p->g_s || !p->alpha || !p->z_x || !p->z_v || !p->stats || !p->sums || !p->d_alpha) return DSALT_ERR_ARG;
+  if (p->T > 0 && !p->partials) return DSALT_ERR_ARG;
+  // one partial-sum block keeps 128 tokens × (2·(1+n_kv) + H) floats in shared memory
+  if (2 * (1 + p->n_kv) + p->H > DSALT_SCORE_BWD_MAX_SUMS) return DSALT_ERR_TOO_LARGE;
   if (p->T > 0 && (!p->norms || !p->coef_x || !p->coef_v)) return DSALT_ERR_ARG;
   return status_of(launch_hybrid_scores_bwd(*p, (cudaStream_t)stream));
 }

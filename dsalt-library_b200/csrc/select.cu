@@ -274,9 +274,10 @@ cudaError_t launch_hybrid_scores(const DsaltScoreParams& p, cudaStream_t st) {
 //   dn[t,c] = (dz[t,c] − mean_t dz[·,c]) / sd_c
 //             − [sd_c unclamped]·z[t,c]·Σ_t dz[·,c]·z[·,c] / ((T − 1)·sd_c),
 //   coef[t,c] = dn[t,c] / ‖·‖[t,c] (1 where the norm is 0),
-// and d α_h = Σ_t g[t,h]·(z_v[t,h] − z_x[t]).  Pass 1: one CTA per column sum
-// (Σ dz, Σ dz·z per column, d α per head), fixed-order reductions; pass 2: one
-// thread per token writes its coefficients.
+// and d α_h = Σ_t g[t,h]·(z_v[t,h] − z_x[t]).  Pass 1: the column sums (Σ dz,
+// Σ dz·z per column, d α per head) as per-128-token partials and a block-order
+// total (fixed-order reductions); pass 2: one thread per token writes its
+// coefficients.
 __device__ __forceinline__ float score_dz(const DsaltScoreBwdParams& p, int64_t t, int c) {
   const float* g = p.g_s + t * p.H;
   const int rep = p.H / p.n_kv;
@@ -294,31 +295,45 @@ __device__ __forceinline__ float score_z(const DsaltScoreBwdParams& p, int64_t t
   return c == 0 ? p.z_x[t] : p.z_v[t * p.H + (c - 1) * (p.H / p.n_kv)];
 }
 
-__global__ void __launch_bounds__(1024) score_bwd_sums_kernel(DsaltScoreBwdParams p) {
-  __shared__ float red[32];
-  const int ncol = 1 + p.n_kv;
-  const int job = blockIdx.x;  // [0, ncol): Σ dz; [ncol, 2·ncol): Σ dz·z; then d α per head
-  float acc = 0.f;
-  for (int64_t t = threadIdx.x; t < p.T; t += blockDim.x) {
-    if (job < ncol) {
-      acc += score_dz(p, t, job);
-    } else if (job < 2 * ncol) {
-      const int c = job - ncol;
-      acc += score_dz(p, t, c) * score_z(p, t, c);
-    } else {
-      const int h = job - 2 * ncol;
-      acc += p.g_s[t * p.H + h] * (p.z_v[t * p.H + h] - p.z_x[t]);
+// Pass 1a: CTA b takes tokens [128·b, 128·b + 128): each thread writes its token's
+// contributions to every sum (Σ dz, Σ dz·z per column, d α per head) into shared
+// memory, then one thread per sum adds the 128 in token order.
+constexpr int kSbTok = DSALT_SCORE_BWD_TOKENS;
+__global__ void __launch_bounds__(kSbTok) score_bwd_partial_kernel(DsaltScoreBwdParams p) {
+  extern __shared__ float contrib[];  // [kSbTok][jobs]
+  const int ncol = 1 + p.n_kv, jobs = 2 * ncol + p.H;
+  const int rep = p.H / p.n_kv;
+  const int64_t t = (int64_t)blockIdx.x * kSbTok + threadIdx.x;
+  float* row = contrib + threadIdx.x * jobs;
+  if (t < p.T) {
+    const float zx = p.z_x[t];
+    for (int c = 0; c < ncol; ++c) {
+      const float dz = score_dz(p, t, c);
+      row[c] = dz;
+      row[ncol + c] = dz * score_z(p, t, c);
     }
+    for (int h = 0; h < p.H; ++h) row[2 * ncol + h] = p.g_s[t * p.H + h] * (p.z_v[t * p.H + h] - zx);
+  } else {
+    for (int j = 0; j < jobs; ++j) row[j] = 0.f;
   }
-  acc = warp_sum(acc);
-  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = acc;
+  (void)rep;
   __syncthreads();
-  if (threadIdx.x == 0) {
-    float tot = 0.f;
-    for (int w = 0; w < (int)(blockDim.x >> 5); ++w) tot += red[w];
-    if (job < 2 * ncol) p.sums[job] = tot;
-    else p.d_alpha[job - 2 * ncol] = tot;
+  for (int j = threadIdx.x; j < jobs; j += kSbTok) {
+    float acc = 0.f;
+    for (int k = 0; k < kSbTok; ++k) acc += contrib[k * jobs + j];
+    p.partials[(int64_t)blockIdx.x * jobs + j] = acc;
   }
+}
+
+// Pass 1b: one thread per sum adds the per-block partials in block order.
+__global__ void __launch_bounds__(128) score_bwd_final_kernel(DsaltScoreBwdParams p, int nblk) {
+  const int ncol = 1 + p.n_kv, jobs = 2 * ncol + p.H;
+  const int j = blockIdx.x * blockDim.x + threadIdx.x;
+  if (j >= jobs) return;
+  float acc = 0.f;
+  for (int b = 0; b < nblk; ++b) acc += p.partials[(int64_t)b * jobs + j];
+  if (j < 2 * ncol) p.sums[j] = acc;
+  else p.d_alpha[j - 2 * ncol] = acc;
 }
 
 __global__ void __launch_bounds__(256) score_bwd_coef_kernel(DsaltScoreBwdParams p) {
@@ -339,7 +354,15 @@ __global__ void __launch_bounds__(256) score_bwd_coef_kernel(DsaltScoreBwdParams
 }
 
 cudaError_t launch_hybrid_scores_bwd(const DsaltScoreBwdParams& p, cudaStream_t st) {
-  score_bwd_sums_kernel<<<(unsigned)(2 * (1 + p.n_kv) + p.H), 1024, 0, st>>>(p);
+  const int jobs = 2 * (1 + p.n_kv) + p.H;
+  const int nblk = (int)((p.T + kSbTok - 1) / kSbTok);
+  if (nblk > 0) {
+    const size_t smem = sizeof(float) * (size_t)kSbTok * jobs;
+    cudaError_t e = ensure_smem((const void*)score_bwd_partial_kernel, smem);
+    if (e != cudaSuccess) return e;
+    score_bwd_partial_kernel<<<(unsigned)nblk, kSbTok, smem, st>>>(p);
+  }
+  score_bwd_final_kernel<<<(unsigned)((jobs + 127) / 128), 128, 0, st>>>(p, nblk);
   if (p.T > 0) score_bwd_coef_kernel<<<(unsigned)((p.T + 255) / 256), 256, 0, st>>>(p);
   return cudaGetLastError();
 }
@@ -402,6 +425,16 @@ constexpr int kTopkThreads = 1024;
 constexpr int kTopkMaxLen = 49152;  // keys held in shared memory
 constexpr int kTopkMaxK = 1024;
 
+// Warp-collective: add one count per active key to hist[bin], one shared-memory
+// atomic per distinct bin of the warp (keys of a radix round crowd into few bins).
+__device__ __forceinline__ void hist_add(uint32_t* hist, bool in, uint32_t bin) {
+  const uint32_t act = __ballot_sync(0xffffffffu, in);
+  if (in) {
+    const uint32_t peers = __match_any_sync(act, bin);
+    if ((int)(threadIdx.x & 31) == __ffs(peers) - 1) atomicAdd(&hist[bin], (uint32_t)__popc(peers));
+  }
+}
+
 // One CTA per (head, sequence): 4 rounds of 8-bit radix select find the k-th
 // largest key; the keys above it and the lowest-position ties fill the k slots.
 __global__ void __launch_bounds__(kTopkThreads) topk_kernel(DsaltTopkParams p) {
@@ -409,7 +442,7 @@ __global__ void __launch_bounds__(kTopkThreads) topk_kernel(DsaltTopkParams p) {
   uint32_t* keys = sm;                       // [max_len]
   __shared__ uint32_t hist[256];
   __shared__ uint32_t sel_prefix, sel_mask;
-  __shared__ int need, n_above, n_tie_taken;
+  __shared__ int need, n_above, n_ties, n_tie_taken;
   __shared__ uint32_t out_key[kTopkMaxK];
   __shared__ int out_pos[kTopkMaxK];
 
@@ -417,7 +450,7 @@ __global__ void __launch_bounds__(kTopkThreads) topk_kernel(DsaltTopkParams p) {
   const int s = blockIdx.x % p.S;
   const int64_t s0 = p.cu_seqlens[s];
   const int L = min((int)(p.cu_seqlens[s + 1] - s0), p.max_len);
-  const int tid = threadIdx.x;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
 
   for (int i = tid; i < L; i += kTopkThreads) {
     const float ws = p.w_sizes[s0 + i];
@@ -425,7 +458,7 @@ __global__ void __launch_bounds__(kTopkThreads) topk_kernel(DsaltTopkParams p) {
     const bool covered = (float)i < truncf(ws);
     keys[i] = covered ? 0u : order_key(p.scores[(s0 + i) * p.H + h]);
   }
-  if (tid == 0) { sel_prefix = 0; sel_mask = 0; need = p.k; }
+  if (tid == 0) { sel_prefix = 0; sel_mask = 0; need = p.k; n_above = 0; n_ties = 0; n_tie_taken = 0; }
   __syncthreads();
 
   const int k_eff = min(p.k, L);
@@ -434,39 +467,80 @@ __global__ void __launch_bounds__(kTopkThreads) topk_kernel(DsaltTopkParams p) {
       for (int b = tid; b < 256; b += kTopkThreads) hist[b] = 0;
       __syncthreads();
       const uint32_t pre = sel_prefix, msk = sel_mask;
-      for (int i = tid; i < L; i += kTopkThreads) {
-        const uint32_t kk = keys[i];
-        if ((kk & msk) == pre) atomicAdd(&hist[(kk >> shift) & 255u], 1u);
+      for (int i0 = tid & ~31; i0 < L; i0 += kTopkThreads) {  // warp-uniform trip count
+        const int i = i0 + lane;
+        const uint32_t kk = i < L ? keys[i] : 0u;
+        hist_add(hist, i < L && (kk & msk) == pre, (kk >> shift) & 255u);
       }
       __syncthreads();
-      if (tid == 0) {
-        int rem = (shift == 24) ? k_eff : need;
-        int b = 255;
-        for (; b > 0; --b) {
-          if ((int)hist[b] >= rem) break;
-          rem -= (int)hist[b];
+      if (warp == 0) {
+        // the bin holding the rem-th largest key: lane l owns bins 255 − 8l … 248 − 8l
+        const int rem0 = (shift == 24) ? k_eff : need;
+        uint32_t c[8];
+        uint32_t tot = 0;
+#pragma unroll
+        for (int q = 0; q < 8; ++q) { c[q] = hist[255 - 8 * lane - q]; tot += c[q]; }
+        uint32_t incl = tot;  // inclusive scan from the top bins down
+#pragma unroll
+        for (int off = 1; off < 32; off <<= 1) {
+          const uint32_t y = __shfl_up_sync(0xffffffffu, incl, off);
+          if (lane >= off) incl += y;
         }
-        sel_prefix = pre | ((uint32_t)b << shift);
-        sel_mask = msk | (255u << shift);
-        need = rem;  // how many keys equal to the final threshold are still needed
+        const uint32_t excl = incl - tot;
+        // the first lane whose cumulative count reaches rem0 (the last lane if none does)
+        const uint32_t hit = __ballot_sync(0xffffffffu, incl >= (uint32_t)rem0);
+        const int owner = hit ? __ffs(hit) - 1 : 31;
+        if (lane == owner) {
+          int rem = rem0 - (int)excl;
+          int b = 255 - 8 * lane;
+#pragma unroll
+          for (int q = 0; q < 8; ++q) {
+            if (b == 0 || (int)c[q] >= rem) break;
+            rem -= (int)c[q];
+            --b;
+          }
+          sel_prefix = pre | ((uint32_t)b << shift);
+          sel_mask = msk | (255u << shift);
+          need = rem;  // how many keys equal to the final threshold are still needed
+        }
       }
       __syncthreads();
     }
   }
   // threshold = sel_prefix (the k-th largest key); take all above, then `need` ties by position
   const uint32_t thr = sel_prefix;
-  if (tid == 0) { n_above = 0; n_tie_taken = 0; }
-  __syncthreads();
   if (k_eff > 0) {
-    for (int i = tid; i < L; i += kTopkThreads) {
-      if (keys[i] > thr) {
-        const int slot = atomicAdd(&n_above, 1);
-        if (slot < kTopkMaxK) { out_key[slot] = keys[i]; out_pos[slot] = i; }
+    for (int i0 = tid & ~31; i0 < L; i0 += kTopkThreads) {
+      const int i = i0 + lane;
+      const uint32_t kk = i < L ? keys[i] : 0u;
+      const bool above = i < L && kk > thr, tie = i < L && kk == thr;
+      const uint32_t ba = __ballot_sync(0xffffffffu, above), bt = __ballot_sync(0xffffffffu, tie);
+      int base_a = 0;
+      if (lane == 0 && ba) base_a = atomicAdd(&n_above, __popc(ba));
+      if (lane == 0 && bt) atomicAdd(&n_ties, __popc(bt));
+      base_a = __shfl_sync(0xffffffffu, base_a, 0);
+      if (above) {
+        const int slot = base_a + __popc(ba & ((1u << lane) - 1u));
+        if (slot < kTopkMaxK) { out_key[slot] = kk; out_pos[slot] = i; }
       }
     }
     __syncthreads();
-    // ties in position order: a single warp scans with ballots
-    if (tid < 32) {
+    if (n_ties == need) {
+      // every key equal to the threshold is taken (the usual case): any order
+      for (int i0 = tid & ~31; i0 < L; i0 += kTopkThreads) {
+        const int i = i0 + lane;
+        const bool tie = i < L && keys[i] == thr;
+        const uint32_t bt = __ballot_sync(0xffffffffu, tie);
+        int base_t = 0;
+        if (lane == 0 && bt) base_t = atomicAdd(&n_tie_taken, __popc(bt));
+        base_t = __shfl_sync(0xffffffffu, base_t, 0);
+        if (tie) {
+          const int slot = n_above + base_t + __popc(bt & ((1u << lane) - 1u));
+          if (slot < kTopkMaxK) { out_key[slot] = thr; out_pos[slot] = i; }
+        }
+      }
+    } else if (tid < 32) {
+      // more ties than slots: the lowest positions, a single warp scanning with ballots
       int taken = 0;
       const int base = n_above;
       for (int i0 = 0; i0 < L && taken < need; i0 += 32) {

@@ -21,7 +21,7 @@ F16, BF16, F32 = 0, 1, 2
 TRAIN, INFER = 0, 1
 IMPL_AUTO, IMPL_SIMT, IMPL_TCGEN05 = 0, 1, 2
 DEV_WAIT_TIMEOUT, DEV_BAD_INDEX = 1, 2
-ABI_VERSION = 5
+ABI_VERSION = 6
 QREC_FLOATS = 16  # DSALT_QREC_FLOATS
 LMK_SPLIT = 4  # DSALT_LMK_SPLIT
 DS_TILE_BYTES = 16384  # DSALT_DS_TILE_BYTES
@@ -119,8 +119,9 @@ class SwigluParams(ctypes.Structure):
 
 class ScoreBwdParams(ctypes.Structure):
     _fields_ = [("g_s", _c_void_p), ("alpha", _c_void_p), ("z_x", _c_void_p), ("z_v", _c_void_p),
-                ("norms", _c_void_p), ("stats", _c_void_p), ("sums", _c_void_p), ("d_alpha", _c_void_p),
-                ("coef_x", _c_void_p), ("coef_v", _c_void_p), ("T", _i64), ("H", _i32), ("n_kv", _i32)]
+                ("norms", _c_void_p), ("stats", _c_void_p), ("sums", _c_void_p), ("partials", _c_void_p),
+                ("d_alpha", _c_void_p), ("coef_x", _c_void_p), ("coef_v", _c_void_p), ("T", _i64), ("H", _i32),
+                ("n_kv", _i32)]
 
 
 class WinGateBwdParams(ctypes.Structure):
@@ -130,6 +131,7 @@ class WinGateBwdParams(ctypes.Structure):
 
 RMSNORM_ROWS_PER_PART = 64  # DSALT_RMSNORM_ROWS_PER_PART
 WIN_GATE_ROWS_PER_PART = 32  # DSALT_WIN_GATE_ROWS_PER_PART
+SCORE_BWD_TOKENS = 128  # DSALT_SCORE_BWD_TOKENS
 
 _STRUCTS = [ScheduleParams, GatherParams, AttnParams, ScoreParams, TopkParams, WinGateParams, RopeParams,
             RmsNormParams, ScaleRowsParams, XentParams, SwigluParams, WinGateBwdParams, ScoreBwdParams]

@@ -73,10 +73,12 @@ class _HybridScore(torch.autograd.Function):
         coef_x = torch.empty(T, dtype=torch.float32, device=dev)
         coef_v = torch.empty(T, n_kv, dtype=torch.float32, device=dev)
         sums = torch.empty(2 * (1 + n_kv), dtype=torch.float32, device=dev)
+        parts = torch.empty((T + _ext.SCORE_BWD_TOKENS - 1) // _ext.SCORE_BWD_TOKENS, 2 * (1 + n_kv) + H,
+                            dtype=torch.float32, device=dev)
         p = _ext.ScoreBwdParams(g_s=_ext.ptr(g), alpha=_ext.ptr(a), z_x=_ext.ptr(z_x), z_v=_ext.ptr(z_v),
                                 norms=_ext.ptr(norms_cm), stats=_ext.ptr(stats), sums=_ext.ptr(sums),
-                                d_alpha=_ext.ptr(d_alpha), coef_x=_ext.ptr(coef_x), coef_v=_ext.ptr(coef_v),
-                                T=T, H=H, n_kv=n_kv)
+                                partials=_ext.ptr(parts), d_alpha=_ext.ptr(d_alpha), coef_x=_ext.ptr(coef_x),
+                                coef_v=_ext.ptr(coef_v), T=T, H=H, n_kv=n_kv)
         _ext.call("dsalt_hybrid_scores_bwd", p)
         dx = dxwv = None
         # each row (group) of x / x·W_Vᵀ scaled by its coefficient, the fp32 product

@@ -29,7 +29,7 @@
 extern "C" {
 #endif
 
-#define DSALT_B200_ABI_VERSION 5
+#define DSALT_B200_ABI_VERSION 6
 
 /* The tensor-core dK/dV stage splits each landmark chunk's query range into
  * this many parts that run as separate CTAs; their fp32 partial sums are added
@@ -268,12 +268,18 @@ typedef struct DsaltScoreBwdParams {
   const float* norms;         /* [(1+n_kv), T] column-major (forward scratch) */
   const float* stats;         /* [2 + 2*n_kv] (forward scratch: mean, clamped std) */
   float* sums;                /* scratch [2*(1+n_kv)] */
+  float* partials;            /* scratch [ceil(T / DSALT_SCORE_BWD_TOKENS), 2*(1+n_kv) + H]:
+                                 per-block partial sums, added in block order */
   float* d_alpha;             /* [H] */
   float* coef_x;              /* [T] */
   float* coef_v;              /* [T, n_kv] */
   int64_t T;
   int32_t H, n_kv;
 } DsaltScoreBwdParams;
+#define DSALT_SCORE_BWD_TOKENS 128
+/* limit on 2·(1+n_kv) + H (the sums one partial block holds in shared memory);
+ * larger head counts return DSALT_ERR_TOO_LARGE                             */
+#define DSALT_SCORE_BWD_MAX_SUMS 400
 DSALT_API int dsalt_hybrid_scores_bwd(const DsaltScoreBwdParams* p, void* stream);
 
 /* Replaces the exclusion + top-k of _compute_landmark_indices

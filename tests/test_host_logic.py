@@ -114,3 +114,32 @@ def test_every_loss_fn_gives_the_chunked_loss_on_cpu(loss_fn):
     labels[0, :3] = -100
     ref = _chunked_cross_entropy(x.reshape(-1, 256), m.lm_head.weight, labels.reshape(-1), 7)
     torch.testing.assert_close(m._compute_loss(x, labels), ref)
+
+
+def test_tile_table_states_the_kernels_shapes():
+    """The fixed tile table (autotune.py, the reference tuner's replacement) gives the
+    shapes the CUDA sources compile: threads, rows, tiles and stages of each kernel."""
+    import re
+    from conftest import PKG
+    from dsalt.kernels.autotune import get_tuned_config
+
+    def const(fname, name):
+        txt = (PKG / "csrc" / fname).read_text()
+        m = re.search(rf"constexpr int {name} = (\d+);", txt)
+        assert m, (fname, name)
+        return int(m.group(1))
+    for D in (64, 128):
+        c = get_tuned_config(D)
+        assert c["fwd"]["threads"] == const("attn_tc.cu", "kThreads")
+        assert c["BLOCK_M"] == c["fwd"]["query_rows"] == const("attn_tc.cu", "BM")
+        assert c["BLOCK_N"] == c["fwd"]["key_tile"] == const("attn_tc.cu", "BN")
+        assert c["num_warps"] * 32 == c["fwd"]["threads"]
+        assert c["bwd_dkdv"]["threads"] == const("attn_tc_bwd.cu", "kThreadsKV")
+        assert c["BLOCK_N_BWD"] == c["bwd_dkdv"]["key_rows"]
+        assert c["bwd_dkdv"]["q_do_stages"] == const("attn_tc_bwd.cu", "kQStages")
+        assert c["bwd_dkdv"]["record_stages"] == const("attn_tc_bwd.cu", "kColStages")
+        assert c["bwd_dq"]["threads"] == const("attn_tc_dq.cu", "kThreads")
+        assert c["bwd_dq"]["stages"] == const("attn_tc_dq.cu", "kStages")
+        assert sum(c["fwd"]["warps"].values()) * 32 == c["fwd"]["threads"]
+        assert sum(c["bwd_dkdv"]["warps"].values()) * 32 == c["bwd_dkdv"]["threads"]
+        assert sum(c["bwd_dq"]["warps"].values()) * 32 == c["bwd_dq"]["threads"]

@@ -754,6 +754,7 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-triton-ref", action="store_true", help="skip timing the reference's Triton op")
+    ap.add_argument("--no-graph", action="store_true", help="time the eager step only (no CUDA graph)")
     ap.add_argument("--sel-shapes", default="config2,config5", help="selection: shapes to run")
     ap.add_argument("--bucket-mb", type=int, default=100, help="config4: DDP bucket size (MB)")
     ap.add_argument("--ddp-bf16-grads", action="store_true", help="config4: bf16 gradient all-reduce hook")
@@ -822,19 +823,53 @@ def run_op(args, wl):
     torch.cuda.synchronize()
     barrier()
 
-    with ClockSampler(local) as clk:
+    def timed(fn):
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         barrier()
         torch.cuda.synchronize()
         e0.record()
-        torch.cuda.nvtx.range_push("timed_steps")  # lets an ncu launch list select the timed region
         for _ in range(args.steps):
-            step()
-        torch.cuda.nvtx.range_pop()
+            fn()
         e1.record()
         torch.cuda.synchronize()
         barrier()
-    ms = e0.elapsed_time(e1)
+        return e0.elapsed_time(e1)
+
+    # the eager step: the public op called from Python every step
+    ms_eager = timed(step)
+    # the same step captured once as a CUDA graph and replayed: every kernel of the
+    # forward and backward runs each step, without the per-call host work (at N > 1
+    # the per-GPU problem is small enough for that host work to dominate)
+    graph, graph_note = None, "eager"
+    if not args.no_graph:
+        try:
+            cs = torch.cuda.Stream(device=dev)
+            cs.wait_stream(torch.cuda.current_stream(dev))
+            with torch.cuda.stream(cs):
+                for _ in range(3):
+                    step()
+            torch.cuda.current_stream(dev).wait_stream(cs)
+            torch.cuda.synchronize()
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph):
+                step()
+            for _ in range(3):
+                graph.replay()
+            torch.cuda.synchronize()
+            graph_note = "CUDA graph of the whole forward + backward step, replayed"
+        except Exception as e:  # keep the eager number
+            graph, graph_note = None, f"eager (graph capture failed: {str(e)[:200]})"
+    graph_ok = graph is not None
+    if world > 1:  # every rank takes the same path
+        flag = torch.tensor([1 if graph_ok else 0], device=dev)
+        dist.all_reduce(flag, op=dist.ReduceOp.MIN)
+        if not bool(flag.item()):
+            graph, graph_ok = None, False
+            graph_note = graph_note if graph_note.startswith("eager") else "eager (capture failed on another rank)"
+    with ClockSampler(local) as clk:
+        torch.cuda.nvtx.range_push("timed_steps")
+        ms = timed(graph.replay if graph_ok else step)
+        torch.cuda.nvtx.range_pop()
     # per-entry-point durations for the roofline and the launch count: the same steps
     # again with CUDA events recorded around each C-ABI call (the stages run one after
     # the other on the caller's stream), outside the timed region
@@ -850,6 +885,7 @@ def run_op(args, wl):
         per_kernel.setdefault(name, []).append(a.elapsed_time(b))
 
     ms_max, flops_all = job_totals(ms, 14.0 * d["D"] * pairs, world, dev)
+    ms_eager_max, _ = job_totals(ms_eager, 0.0, world, dev)
     _, scanned_all = job_totals(0.0, float(scanned), world, dev)
     _, pairs_all = job_totals(0.0, float(pairs), world, dev)
     value = flops_all * args.steps / (ms_max / 1e3) / 1e12
@@ -905,6 +941,10 @@ def run_op(args, wl):
                 "roofline": roof,
                 "kernels_ms": {n: round(v[0], 4) for n, v in kern.items()},
                 "kernels_ms_note": "CUDA events around each C-ABI call, in steps run after the timed ones",
+                "step": graph_note,
+                "eager": {"value": flops_all * args.steps / (ms_eager_max / 1e3) / 1e12,
+                          "ms_per_step": ms_eager_max / args.steps,
+                          "note": "the public op called from Python every step (host launch work included)"},
                 "attended_pairs": int(pairs_all), "scanned_pairs_fwd": int(scanned_all),
                 "attended_over_scanned": pairs_all / max(scanned_all, 1.0),
                 "gpu_launches": launches,

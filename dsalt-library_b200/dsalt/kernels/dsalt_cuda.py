@@ -268,14 +268,35 @@ def backward(grad_out, q_c, k_c, v_c, o, lse, prep: Prepared, tau_win: float, wi
     band_tiles = (BLOCK_M + widest_band(prep, dev, H * prep.max_blocks * _ext.DS_TILE_BYTES) + 63) // 64
     lmk_tiles = (prep.lmax + 63) // 64 + 1
     n_tiles = _ext.ds_tiles(H, prep.max_blocks, prep.S, prep.kp, band_tiles, lmk_tiles)
-    ds = torch.empty(n_tiles * _ext.DS_TILE_BYTES + 1024, dtype=torch.uint8, device=dev)
-    p.ds_tiles = ds.data_ptr() + (-ds.data_ptr()) % 1024
+    p.ds_tiles = _tile_scratch(dev, n_tiles * _ext.DS_TILE_BYTES)
     p.ds_band_tiles, p.ds_lmk_tiles = band_tiles, lmk_tiles
     _ext.call("dsalt_attn_bwd_preprocess", p)
     # dQ multiplies the dSᵀ tiles that dK/dV stores: one after the other
     _ext.call("dsalt_attn_bwd_dkdv", p)
     _ext.call("dsalt_attn_bwd_dq", p)
     return dq, dk, dv, d_lw, dw
+
+
+# The dSᵀ tile scratch, kept per (device, stream) and only ever grown: its size
+# changes with the band bound of each call, and a fresh multi-GB allocation per
+# backward would churn the caching allocator.  Backward calls on one stream run
+# in stream order, so they can share it.  A buffer that is outgrown stays
+# allocated, since a captured CUDA graph may still hold its address.
+_TILE_SCRATCH: dict = {}
+_RETIRED: list = []
+
+
+def _tile_scratch(dev: torch.device, nbytes: int) -> int:
+    """1024-byte-aligned device address of at least ``nbytes`` of tile scratch."""
+    idx = dev.index if dev.index is not None else torch.cuda.current_device()
+    key = (idx, _ext.current_stream_handle())
+    buf = _TILE_SCRATCH.get(key)
+    if buf is None or buf.numel() < nbytes + 1024:
+        if buf is not None:
+            _RETIRED.append(buf)
+        buf = torch.empty(nbytes + 1024, dtype=torch.uint8, device=dev)
+        _TILE_SCRATCH[key] = buf
+    return buf.data_ptr() + (-buf.data_ptr()) % 1024
 
 
 def compute_dtype(q: torch.Tensor) -> torch.dtype:

@@ -4,7 +4,7 @@
 // _train_bwd_kernel :302-333).
 //
 //   rows = 128 keys; tiles = 64 queries.  Sᵀ = K·Qᵀ, dPᵀ = V·dOᵀ (TMEM) ->
-//   Pᵀ, dSᵀ (bf16, smem; soft-edge fix-up per query column) ->
+//   Pᵀ, dSᵀ (bf16, smem; the soft-edge factor applied per element) ->
 //   dV += Pᵀ·dO, dK += dSᵀ·Q (TMEM).  Landmark items (the sorted landmark slots
 //   of one (head, sequence) as the keys, every later query as columns) write
 //   fp32 dK/dV per slot and d_lw (a row sum: no atomics); band items (128
@@ -14,11 +14,12 @@
 // Every finished dSᵀ tile is also stored (one bulk copy of the 16 KB shared
 // buffer) to the ds_tiles scratch, where the dQ stage (attn_tc_dq.cu) reads it:
 // dQ = scale·Σ dS·K without a second computation of S, dP and the exponentials.
-// The soft-edge fix-up also forms ∂loss/∂w̃ = Σ_edge dS·(1 − σ)/τ of each query
-// column (the reference's D_w, :371-383): a fixed-order sum per (key block,
-// query), added to dw_head, which the preprocess stage zeroed.  A query's edge
-// keys lie in at most two key blocks, so each dw_head entry receives at most two
-// additions onto zero, whose result does not depend on their order.
+// The row threads also form ∂loss/∂w̃ = Σ_edge dS·(1 − σ)/τ of each query column
+// (the reference's D_w, :371-383) in a fixed order: a warp reduce-scatter over
+// 32 keys, then the column warp's sum of the four row warps' partials, added to
+// dw_head, which the preprocess stage zeroed.  A query's edge keys lie in at most
+// two key blocks, so each dw_head entry receives at most two additions onto zero,
+// whose result does not depend on their order.
 //
 // All waits are bounded (sm100::mbar_wait); see attn_tc.cu.
 #include <mutex>
@@ -94,8 +95,7 @@ constexpr int kQuarter = BN / 4;  // tile columns per row thread
 enum { KV_FULL = 0, KV_EMPTY = 1, Q_FULL = 2, DO_FULL = Q_FULL + kQStages, QDO_EMPTY = DO_FULL + kQStages,
        REC_FULL = QDO_EMPTY + kQStages, COL_FULL = REC_FULL + kColStages, COL_EMPTY = COL_FULL + kColStages,
        SD_FULL = COL_EMPTY + kColStages, SD_EMPTY = SD_FULL + 2, PDS_FULL = SD_EMPTY + 2, PDS_EMPTY = PDS_FULL + 1,
-       ROWS = PDS_EMPTY + 1, KV_DONE = ROWS + 1, ACC_EMPTY = KV_DONE + 1, FINAL = ACC_EMPTY + 1, EPI = FINAL + 2,
-       NB = EPI + 1 };
+       KV_DONE = PDS_EMPTY + 1, ACC_EMPTY = KV_DONE + 1, FINAL = ACC_EMPTY + 1, EPI = FINAL + 2, NB = EPI + 1 };
 
 // per-tile summary of the query records, written by the column warp
 struct alignas(16) ColStats {
@@ -117,6 +117,7 @@ struct alignas(1024) Smem {
   int abort_flag;
   QRec rec[kColStages][BN];  // the tile's query records (bulk-copied, then fixed up)
   ColStats stats[kColStages];
+  float dwp[kColStages][4][BN];  // band items: per-row-warp partial sums of ∂loss/∂w̃ per query column
   float dlw_part[4][BM];  // landmark items: d_lw partial sums of the four column quarters
 };
 static_assert(2 * BM * BN * 2 >= BM * 128 * 2, "the Pᵀ/dSᵀ buffers hold one staged dK or dV block (D ≤ 128)");
@@ -245,7 +246,6 @@ __global__ void __launch_bounds__(kThreadsKV, 1) tc_bwd_dkdv_kernel(const __grid
     }
     mbar_init(bar[PDS_FULL], kRowThreads);
     mbar_init(bar[PDS_EMPTY], 3);  // the dV and dK MMAs, and the store warp's copy of the dSᵀ tile
-    mbar_init(bar[ROWS], kRowThreads);
     mbar_init(bar[KV_DONE], 3);  // both MMA warps, and the store warp (the item's last tile copied)
     mbar_init(bar[ACC_EMPTY], kRowThreads);
     mbar_init(bar[FINAL], 1);
@@ -381,16 +381,42 @@ __global__ void __launch_bounds__(kThreadsKV, 1) tc_bwd_dkdv_kernel(const __grid
       mbar_expect_tx(bar[REC_FULL + st], nrec * (uint32_t)sizeof(QRec));
       bulk_load(smem_u32(&sm.rec[st][0]), recg + q0, nrec * (uint32_t)sizeof(QRec), bar[REC_FULL + st]);
     };
+    // band items: ∂loss/∂w̃ of tile gd's query columns from this key block, once the
+    // rows released the tile: the four row warps' partials summed in a fixed order,
+    // one addition per column to dw_head (a column's edge keys lie in at most two
+    // key blocks, so dw_head receives at most two additions onto zero)
+    struct Prev {  // what sum_dw needs of the previous tile's item
+      int64_t s0;
+      int h, key0, nkeys;
+    };
+    auto sum_dw = [&](const Prev& c, int gd) {
+      const int sd = gd % kColStages;
+      const int klo = c.key0, khi = c.key0 + c.nkeys - 1;
+#pragma unroll
+      for (int k2 = 0; k2 < 2; ++k2) {
+        const int col = lane + 32 * k2;
+        const QRec& rc = sm.rec[sd][col];
+        if (rc.elo <= rc.ehi && rc.elo <= khi && rc.ehi >= klo) {
+          const float v = (sm.dwp[sd][0][col] + sm.dwp[sd][1][col]) + (sm.dwp[sd][2][col] + sm.dwp[sd][3][col]);
+          atomicAdd(p.dw_head + (c.s0 + rc.qi) * p.H + c.h, v);
+        }
+      }
+    };
+    const bool want_dw = !LMK && p.dw_head != nullptr;
     Cur ci{(int)blockIdx.x, 0, Item{}}, cp{(int)blockIdx.x, 0, Item{}};
     seek(ci);
     seek(cp);
-    int g_issued = 0;
+    Prev cprev{0, 0, 0, 0};
+    int g_issued = 0, g = 0;
+    bool col_ok = true;
     for (; ci.idx < n_items && g_issued < kColStages - 1; ++g_issued, advance(ci))
       if (lane == 0) issue(ci, g_issued);
-    for (int g = 0; cp.idx < n_items; ++g, advance(cp)) {
+    for (; cp.idx < n_items; ++g, advance(cp)) {
       const int st = g % kColStages;
-      if (!__all_sync(0xffffffffu, mbar_wait(bar[REC_FULL + st], (g / kColStages) & 1, abort_flag, p.status)))
+      if (!__all_sync(0xffffffffu, mbar_wait(bar[REC_FULL + st], (g / kColStages) & 1, abort_flag, p.status))) {
+        col_ok = false;
         break;
+      }
       const int q0 = cp.it.q_start + BN * cp.u;
       // per lane: columns lane (quarter lane/16) and lane + 32 (quarter 2 + lane/16)
       int st_lo_max[2], st_lo_min[2], st_qi_min[2], st_qi_max[2], st_elo_min[2], st_ehi_max[2];
@@ -431,18 +457,28 @@ __global__ void __launch_bounds__(kThreadsKV, 1) tc_bwd_dkdv_kernel(const __grid
         }
       }
       mbar_arrive(bar[COL_FULL + st]);
-      // refill the stage of tile g − 1 with the next tile once the rows released it
-      if (ci.idx < n_items) {
-        const int ng = g_issued;  // == g + kColStages − 1
-        if (ng >= kColStages &&
-            !__all_sync(0xffffffffu,
-                        mbar_wait(bar[COL_EMPTY + ng % kColStages], (ng / kColStages - 1) & 1, abort_flag, p.status)))
+      // tile g − 1: once the rows released it, its ∂loss/∂w̃ sums, then the refill
+      // of its stage with the next tile
+      if (g >= 1) {
+        if (!__all_sync(0xffffffffu, mbar_wait(bar[COL_EMPTY + (g - 1) % kColStages], ((g - 1) / kColStages) & 1,
+                                               abort_flag, p.status))) {
+          col_ok = false;
           break;
-        if (lane == 0) issue(ci, ng);
+        }
+        if (want_dw) sum_dw(cprev, g - 1);
+      }
+      if (ci.idx < n_items) {
+        if (lane == 0) issue(ci, g_issued);  // g_issued == g + kColStages − 1
         ++g_issued;
         advance(ci);
       }
+      cprev = Prev{cp.it.s0, cp.it.h, cp.it.key0, cp.it.nkeys};
     }
+    if (col_ok && g >= 1 &&
+        __all_sync(0xffffffffu, mbar_wait(bar[COL_EMPTY + (g - 1) % kColStages], ((g - 1) / kColStages) & 1,
+                                          abort_flag, p.status)) &&
+        want_dw)
+      sum_dw(cprev, g - 1);
     if (lane == 0)
       for (int g = max(0, g_issued - kColStages); g < g_issued; ++g)
         mbar_drain(bar[REC_FULL + g % kColStages], (g / kColStages) & 1);
@@ -527,7 +563,7 @@ __global__ void __launch_bounds__(kThreadsKV, 1) tc_bwd_dkdv_kernel(const __grid
     const int c0 = kQuarter * quarter;     // this thread's first column of a tile
     const uint32_t lane_addr = ((uint32_t)(32 * (warp & 3)) << 16);
     const float sl2 = p.scale * kLog2e;
-    int gt = 0, gi = 0, rows_phase = 0, epi_phase = 0;
+    int gt = 0, gi = 0, epi_phase = 0;
     bool ok = true;
     // all row threads meet (bounded wait on the EPI barrier)
     auto rows_sync = [&]() -> bool {
@@ -581,13 +617,21 @@ __global__ void __launch_bounds__(kThreadsKV, 1) tc_bwd_dkdv_kernel(const __grid
           all_in = cst.lo_max[quarter] <= jf && cst.qi_min[quarter] >= jl;
           all_out = cst.lo_min[quarter] > jl || cst.qi_max[quarter] < jf;
         }
-        // Pᵀ and dSᵀ of this thread's 16 columns, packed to the input dtype
+        // band items: this warp's keys hold soft-edge keys of some of its columns
+        // (the quarter's edge range meets the warp's key range; warp-uniform)
+        const bool warp_edge = !LMK && cst.elo_min[quarter] <= jl && cst.ehi_max[quarter] >= jf;
+        // Pᵀ and dSᵀ of this thread's 16 columns, packed to the input dtype; with
+        // warp_edge also ∂loss/∂w̃ = dS·(1 − σ)/τ of each column's entry
         uint32_t pk_p[8], pk_d[8];
+        // ∂loss/∂w̃ after the first reduce-scatter step (lane distance 16): v8[i]
+        // is the pair sum of column 8·lane[4] + i
+        float v8[8];
+        const bool u16 = lane & 16;
         if (all_out) {
           tc_fence_before();
           mbar_arrive(bar[SD_EMPTY + st]);
 #pragma unroll
-          for (int q = 0; q < 8; ++q) { pk_p[q] = 0u; pk_d[q] = 0u; }
+          for (int q = 0; q < 8; ++q) { pk_p[q] = 0u; pk_d[q] = 0u; v8[q] = 0.f; }
         } else {
           float sv[16], dpv[16];
           tmem_ld16(tS + lane_addr + st * BN + c0, sv);
@@ -595,15 +639,22 @@ __global__ void __launch_bounds__(kThreadsKV, 1) tc_bwd_dkdv_kernel(const __grid
           tmem_wait_ld();
           tc_fence_before();
           mbar_arrive(bar[SD_EMPTY + st]);
-          // the all-valid case (warp-uniform) runs without the per-element test
-          auto body = [&](auto kAllIn) {
+          // the all-valid case (warp-uniform) runs without the per-element test;
+          // the soft window edge (kEdge): Pᵀ, dSᵀ *= σ((w̃ − d)/τ) on each column's
+          // edge keys elo … ehi (factor ehi − j of the record, or computed past the
+          // stored ones)
+          auto body = [&](auto kAllIn, auto kEdgeT) {
             constexpr bool kIn = decltype(kAllIn)::value;
+            constexpr bool kEdge = decltype(kEdgeT)::value;
+            // columns 2qq, 2qq + 1, 2qq + 8, 2qq + 9 together: the first exchange of
+            // the ∂loss/∂w̃ reduce-scatter pairs column i with column i + 8
 #pragma unroll
-            for (int c = 0; c < 16; c += 2) {
-              float pr2[2], ds2[2];
+            for (int qq = 0; qq < 4; ++qq) {
+              float pr4[4], ds4[4], dw4[4];
 #pragma unroll
-              for (int e = 0; e < 2; ++e) {
-                const QRec& rq = rec[c + e];
+              for (int e4 = 0; e4 < 4; ++e4) {
+                const int cc = 2 * qq + (e4 & 1) + 8 * (e4 >> 1);
+                const QRec& rq = rec[cc];
                 // nlse2, delta (and lo, qi only where a column can be invalid)
                 float4 r0;
                 if (kIn) {
@@ -615,22 +666,69 @@ __global__ void __launch_bounds__(kThreadsKV, 1) tc_bwd_dkdv_kernel(const __grid
                 bool valid;
                 float pr;
                 if (LMK) {
-                  pr = fast_exp2(fmaf(sv[c + e], sl2, lw2 + r0.x));
+                  pr = fast_exp2(fmaf(sv[cc], sl2, lw2 + r0.x));
                   valid = kIn || (key_ok && j <= __float_as_int(r0.w) && jfl < rq.wlo);
                 } else {
-                  pr = fast_exp2(fmaf(sv[c + e], sl2, r0.x));
+                  pr = fast_exp2(fmaf(sv[cc], sl2, r0.x));
                   valid = kIn || (j >= __float_as_int(r0.z) && j <= __float_as_int(r0.w));
                 }
-                const float dsv = pr * (dpv[c + e] - r0.y);
-                pr2[e] = valid ? pr : 0.f;
-                ds2[e] = valid ? dsv : 0.f;
-                if (LMK) dlw += ds2[e];
+                float dsv = pr * (dpv[cc] - r0.y);
+                if (kEdge) {
+                  const int2 eb = *reinterpret_cast<const int2*>(&rq.ehi);  // ehi, elo
+                  float gf = 1.0f;
+                  if (j <= eb.x && j >= eb.y) {
+                    const int ei = eb.x - j;
+                    gf = ei < kMaxEdge ? rq.eg[ei] : qrec_edge_factor(rq.wt, rq.qi - j, inv_tau);
+                  }
+                  pr *= gf;
+                  dsv *= gf;
+                  dw4[e4] = valid ? dsv * (1.0f - gf) * inv_tau : 0.f;
+                }
+                pr4[e4] = valid ? pr : 0.f;
+                ds4[e4] = valid ? dsv : 0.f;
+                if (LMK) dlw += ds4[e4];
               }
-              pk_p[c / 2] = pack2(pr2[0], pr2[1], kBF16);
-              pk_d[c / 2] = pack2(ds2[0], ds2[1], kBF16);
+              pk_p[qq] = pack2(pr4[0], pr4[1], kBF16);
+              pk_d[qq] = pack2(ds4[0], ds4[1], kBF16);
+              pk_p[qq + 4] = pack2(pr4[2], pr4[3], kBF16);
+              pk_d[qq + 4] = pack2(ds4[2], ds4[3], kBF16);
+              if (kEdge) {
+#pragma unroll
+                for (int i = 0; i < 2; ++i)
+                  v8[2 * qq + i] = (u16 ? dw4[2 + i] : dw4[i]) +
+                                   __shfl_xor_sync(0xffffffffu, u16 ? dw4[i] : dw4[2 + i], 16);
+              }
             }
           };
-          if (all_in) body(std::true_type{}); else body(std::false_type{});
+          if (warp_edge) {
+            if (all_in) body(std::true_type{}, std::true_type{}); else body(std::false_type{}, std::true_type{});
+          } else {
+            if (all_in) body(std::true_type{}, std::false_type{}); else body(std::false_type{}, std::false_type{});
+          }
+        }
+        if (!LMK) {
+          // the warp's sum of each column's ∂loss/∂w̃ over its 32 keys: a fixed
+          // reduce-scatter (halves exchanged at lane distances 16, 8, 4, 2, then
+          // the pair at distance 1), after which lane l holds column
+          // 8·l[4] + 4·l[3] + 2·l[2] + l[1]; the column warp adds the four warps'
+          // partials once the tile is released
+          float part = 0.f;
+          if (warp_edge) {
+            float v4[4], v2[2];
+            const bool u8 = lane & 8, u4 = lane & 4, u2 = lane & 2;
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+              v4[i] = (u8 ? v8[i + 4] : v8[i]) + __shfl_xor_sync(0xffffffffu, u8 ? v8[i] : v8[i + 4], 8);
+#pragma unroll
+            for (int i = 0; i < 2; ++i)
+              v2[i] = (u4 ? v4[i + 2] : v4[i]) + __shfl_xor_sync(0xffffffffu, u4 ? v4[i] : v4[i + 2], 4);
+            part = (u2 ? v2[1] : v2[0]) + __shfl_xor_sync(0xffffffffu, u2 ? v2[0] : v2[1], 2);
+            part += __shfl_xor_sync(0xffffffffu, part, 1);
+          }
+          if ((lane & 1) == 0) {
+            const int colw = ((lane >> 4) & 1) * 8 + ((lane >> 3) & 1) * 4 + ((lane >> 2) & 1) * 2 + ((lane >> 1) & 1);
+            sm.dwp[cs][warp & 3][c0 + colw] = part;
+          }
         }
         // the single Pᵀ / dSᵀ buffer is free once the previous tile's dV / dK MMAs completed
         if (g >= 1) {
@@ -643,57 +741,6 @@ __global__ void __launch_bounds__(kThreadsKV, 1) tc_bwd_dkdv_kernel(const __grid
               make_uint4(pk_p[4 * q], pk_p[4 * q + 1], pk_p[4 * q + 2], pk_p[4 * q + 3]);
           *reinterpret_cast<uint4*>(sm.dst + sw128_offset(r, c0 + 8 * q)) =
               make_uint4(pk_d[4 * q], pk_d[4 * q + 1], pk_d[4 * q + 2], pk_d[4 * q + 3]);
-        }
-        // soft window edge (band items): Pᵀ, dSᵀ *= σ((w̃ − d)/τ) on each query
-        // column's edge keys, spread over the 512 row threads (column tid % 64, edge
-        // index tid / 64) once every row has stored its entries
-        const bool tile_edge =
-            !LMK && min(min(cst.elo_min[0], cst.elo_min[1]), min(cst.elo_min[2], cst.elo_min[3])) <= key0 + nkeys - 1 &&
-            max(max(cst.ehi_max[0], cst.ehi_max[1]), max(cst.ehi_max[2], cst.ehi_max[3])) >= key0;
-        if (tile_edge) {
-          mbar_arrive(bar[ROWS]);
-          ok = mbar_wait(bar[ROWS], rows_phase & 1, abort_flag, p.status);
-          ++rows_phase;
-          if (!__all_sync(0xffffffffu, ok)) { ok = false; break; }
-          // eight consecutive lanes per query column: column tid / 8, edge index tid % 8
-          const int col = tid >> 3, e = tid & 7;
-          const QRec& rc = sm.rec[cs][col];
-          const int ne = qrec_ne(rc), ehi = rc.ehi;
-          float dwc = 0.f;  // ∂loss/∂w̃ part of this element: dS·(1 − σ)/τ
-          {
-            const int rr = ehi - e - key0;
-            if (e < ne && rr >= 0 && rr < nkeys) {
-              const uint32_t off = sw128_offset(rr, col);
-              const float a1 = to_f32<T>(*reinterpret_cast<const T*>(sm.pt + off));
-              const float a2 = to_f32<T>(*reinterpret_cast<const T*>(sm.dst + off));
-              const float gf = rc.eg[e];
-              const float v = a2 * gf;
-              *reinterpret_cast<T*>(sm.pt + off) = from_f32<T>(a1 * gf);
-              *reinterpret_cast<T*>(sm.dst + off) = from_f32<T>(v);
-              dwc = v * (1.0f - gf) * inv_tau;
-            }
-          }
-          // the column's sum over its eight lanes, in a fixed order
-          dwc += __shfl_xor_sync(0xffffffffu, dwc, 1);
-          dwc += __shfl_xor_sync(0xffffffffu, dwc, 2);
-          dwc += __shfl_xor_sync(0xffffffffu, dwc, 4);
-          if (e == 0 && ne > 0) {
-            // wider soft edges than the precomputed factors: the rest one key at a time
-            for (int e2 = kMaxEdge; e2 < ne; ++e2) {
-              const int rr = ehi - e2 - key0;
-              if (rr < 0) break;
-              if (rr >= nkeys) continue;
-              const float sg = qrec_edge_factor(rc.wt, rc.qi - (ehi - e2), inv_tau);
-              T* e1 = reinterpret_cast<T*>(sm.pt + sw128_offset(rr, col));
-              T* ep2 = reinterpret_cast<T*>(sm.dst + sw128_offset(rr, col));
-              const float v = to_f32<T>(*ep2) * sg;
-              *e1 = from_f32<T>(to_f32<T>(*e1) * sg);
-              *ep2 = from_f32<T>(v);
-              dwc += v * (1.0f - sg) * inv_tau;
-            }
-            if (p.dw_head && rc.elo <= key0 + nkeys - 1 && ehi >= key0)
-              atomicAdd(p.dw_head + (s0 + rc.qi) * p.H + h, dwc);
-          }
         }
         fence_async_smem();
         mbar_arrive(bar[PDS_FULL]);

@@ -4,19 +4,23 @@
 // _train_bwd_kernel :302-333).
 //
 //   rows = 128 keys; tiles = 64 queries.  Sᵀ = K·Qᵀ, dPᵀ = V·dOᵀ (TMEM) ->
-//   Pᵀ, dSᵀ (bf16, smem; the soft-edge factor applied per element) ->
-//   dV += Pᵀ·dO, dK += dSᵀ·Q (TMEM).  Landmark items (the sorted landmark slots
+//   Pᵀ, dSᵀ (bf16, written back into the TMEM columns of Sᵀ, dPᵀ they came
+//   from, with the soft-edge factor) ->
+//   dV += Pᵀ·dO, dK += dSᵀ·Q (TMEM, A operand read from TMEM).  Landmark items (the sorted landmark slots
 //   of one (head, sequence) as the keys, every later query as columns) write
 //   fp32 dK/dV per slot and d_lw (a row sum: no atomics); band items (128
 //   consecutive keys) add those slot rows into their own before the single
 //   store.  dK/dV and d_lw are deterministic.
 //
-// Every finished dSᵀ tile is also stored (one bulk copy of the 16 KB shared
-// buffer) to the ds_tiles scratch, where the dQ stage (attn_tc_dq.cu) reads it:
-// dQ = scale·Σ dS·K without a second computation of S, dP and the exponentials.
+// Every finished dSᵀ tile is also written to one of two shared buffers (the
+// 128B-swizzled image of a 128 × 64 K-major tile) and bulk-copied from there to
+// the ds_tiles scratch (16 KB per tile), where the dQ stage (attn_tc_dq.cu) reads
+// it: dQ = scale·Σ dS·K without a second computation of S, dP and the
+// exponentials.
 // The row threads also form ∂loss/∂w̃ = Σ_edge dS·(1 − σ)/τ of each query column
-// (the reference's D_w, :371-383) in a fixed order: a warp reduce-scatter over
-// 32 keys, then the column warp's sum of the four row warps' partials, added to
+// (the reference's D_w, :371-383) in a fixed order: a warp butterfly over its 32
+// keys (only for the columns whose edge keys meet them), then the column warp's
+// sum of the four row warps' partials, added to
 // dw_head, which the preprocess stage zeroed.  A query's edge keys lie in at most
 // two key blocks, so each dw_head entry receives at most two additions onto zero,
 // whose result does not depend on their order.
@@ -35,11 +39,24 @@ cudaError_t tc_bwd_dq_stage(const DsaltAttnParams& p, cudaStream_t st);
 
 namespace bwd {
 
-constexpr int kMaxLmk = 512;
 constexpr int kMaxEdge = kQRecEdge;  // soft-edge keys per query handled with precomputed factors
 constexpr float kLog2e = 1.4426950408889634f;
 
 __device__ __forceinline__ int round16(int n) { return (n + 15) & ~15; }
+
+// the 16-bit element in the low half of b as float, and a float rounded to the
+// 16-bit type's bits
+template <typename T>
+__device__ __forceinline__ float bits_to_f32(uint32_t b) {
+  const unsigned short u = (unsigned short)(b & 0xffffu);
+  if constexpr (std::is_same<T, __half>::value) return __half2float(__ushort_as_half(u));
+  else return __bfloat162float(__ushort_as_bfloat16(u));
+}
+template <typename T>
+__device__ __forceinline__ uint32_t f32_to_bits(float v) {
+  if constexpr (std::is_same<T, __half>::value) return (uint32_t)__half_as_ushort(__float2half_rn(v));
+  else return (uint32_t)__bfloat16_as_ushort(__float2bfloat16_rn(v));
+}
 
 struct alignas(64) BwdArgs {
   CUtensorMap tm_q, tm_do, tm_k, tm_v, tm_lk, tm_lv;
@@ -82,8 +99,10 @@ constexpr int kQStages = 3;       // Q / dO tile ring
 constexpr int kColStages = 4;     // per-tile column data ring
 // 16 row warps: warp w reads TMEM lanes 32·(w % 4)… and owns the 16-column
 // quarter w / 4 of every tile (four warps per scheduler hide the latencies of
-// the element-wise work); then the TMA warp, MMA warp A (TMEM owner: Sᵀ, dV),
-// the column warp and MMA warp B (dPᵀ, dK)
+// the element-wise work); a quarter is one K = 16 step of the dV / dK MMAs, so
+// it writes its packed Pᵀ / dSᵀ over its own (already read) Sᵀ / dPᵀ columns.
+// Then the TMA warp, MMA warp A (TMEM owner: Sᵀ, dV), the column warp and MMA
+// warp B (dPᵀ, dK).
 constexpr int kRowWarps = 16;
 constexpr int kRowThreads = 32 * kRowWarps;
 constexpr int kProducerWarp = 16;
@@ -94,8 +113,9 @@ constexpr int kThreadsKV = 640;
 constexpr int kQuarter = BN / 4;  // tile columns per row thread
 enum { KV_FULL = 0, KV_EMPTY = 1, Q_FULL = 2, DO_FULL = Q_FULL + kQStages, QDO_EMPTY = DO_FULL + kQStages,
        REC_FULL = QDO_EMPTY + kQStages, COL_FULL = REC_FULL + kColStages, COL_EMPTY = COL_FULL + kColStages,
-       SD_FULL = COL_EMPTY + kColStages, SD_EMPTY = SD_FULL + 2, PDS_FULL = SD_EMPTY + 2, PDS_EMPTY = PDS_FULL + 1,
-       KV_DONE = PDS_EMPTY + 1, ACC_EMPTY = KV_DONE + 1, FINAL = ACC_EMPTY + 1, EPI = FINAL + 2, NB = EPI + 1 };
+       SD_FULL = COL_EMPTY + kColStages, PDS_FULL = SD_FULL + 2, DONE_A = PDS_FULL + 2, DONE_B = DONE_A + 2,
+       DS_EMPTY = DONE_B + 2, KV_DONE = DS_EMPTY + 2, ACC_EMPTY = KV_DONE + 1, FINAL = ACC_EMPTY + 1, EPI = FINAL + 2,
+       NB = EPI + 1 };
 
 // per-tile summary of the query records, written by the column warp
 struct alignas(16) ColStats {
@@ -110,8 +130,9 @@ struct alignas(1024) Smem {
   uint8_t v[BM * D * 2];
   uint8_t q[kQStages][BN * D * 2];
   uint8_t dO[kQStages][BN * D * 2];
-  uint8_t pt[BM * BN * 2];   // Pᵀ; with dst also the staging area of the band epilogue
-  uint8_t dst[BM * BN * 2];  // dSᵀ
+  // the two dSᵀ tile buffers of the scratch stores; in the band epilogue the
+  // staging area of one dK or dV block (D ≤ 128)
+  uint8_t stage[2 * BM * BN * 2];
   uint64_t bars[NB];
   uint32_t tmem_base;
   int abort_flag;
@@ -120,7 +141,7 @@ struct alignas(1024) Smem {
   float dwp[kColStages][4][BN];  // band items: per-row-warp partial sums of ∂loss/∂w̃ per query column
   float dlw_part[4][BM];  // landmark items: d_lw partial sums of the four column quarters
 };
-static_assert(2 * BM * BN * 2 >= BM * 128 * 2, "the Pᵀ/dSᵀ buffers hold one staged dK or dV block (D ≤ 128)");
+static_assert(2 * BM * BN * 2 >= BM * 128 * 2, "the dSᵀ buffers hold one staged dK or dV block (D ≤ 128)");
 
 // One work item: 128 keys (a band block, or a chunk of sorted landmark slots with
 // one part of its query range) of one (sequence, head), and its query tiles.
@@ -242,10 +263,11 @@ __global__ void __launch_bounds__(kThreadsKV, 1) tc_bwd_dkdv_kernel(const __grid
     }
     for (int st = 0; st < 2; ++st) {
       mbar_init(bar[SD_FULL + st], 2);
-      mbar_init(bar[SD_EMPTY + st], kRowThreads);
+      mbar_init(bar[PDS_FULL + st], kRowThreads);
+      mbar_init(bar[DONE_A + st], 1);    // dV of the buffer's tile completed (its Pᵀ is read)
+      mbar_init(bar[DONE_B + st], 1);    // dK of the buffer's tile completed (its dSᵀ is read)
+      mbar_init(bar[DS_EMPTY + st], 1);  // the store lane's copy has read the shared dSᵀ buffer
     }
-    mbar_init(bar[PDS_FULL], kRowThreads);
-    mbar_init(bar[PDS_EMPTY], 3);  // the dV and dK MMAs, and the store warp's copy of the dSᵀ tile
     mbar_init(bar[KV_DONE], 3);  // both MMA warps, and the store warp (the item's last tile copied)
     mbar_init(bar[ACC_EMPTY], kRowThreads);
     mbar_init(bar[FINAL], 1);
@@ -317,11 +339,11 @@ __global__ void __launch_bounds__(kThreadsKV, 1) tc_bwd_dkdv_kernel(const __grid
     if (kv_issued > 0) mbar_drain(bar[KV_FULL], (kv_issued - 1) & 1);
   } else if (warp == kProducerWarp && lane == 1) {
     // ---------------------------------------------------- store lane: dSᵀ tiles to the scratch
-    // Bulk-copies each finished dSᵀ tile (after the soft-edge fix-up) to the
-    // ds_tiles scratch that the dQ stage reads, and releases the buffer to the rows
-    // (PDS_EMPTY) once the copy has read it; after an item's last tile it also
-    // completes KV_DONE, so that the epilogue's staging never overwrites a tile
-    // that is still being copied.
+    // Bulk-copies each finished dSᵀ tile from its shared buffer (tile g in buffer
+    // g % 2) to the ds_tiles scratch that the dQ stage reads, and releases the
+    // buffer (DS_EMPTY) once the copy has read it; after an item's last tile it
+    // also completes KV_DONE, so that the epilogue's staging never overwrites a
+    // tile that is still being copied.
     int gt = 0;
     bool ok = true;
     for (int idx = blockIdx.x; ok && idx < n_items; idx += stride) {
@@ -329,15 +351,15 @@ __global__ void __launch_bounds__(kThreadsKV, 1) tc_bwd_dkdv_kernel(const __grid
       const int n = it.n_tiles;
       if (n == 0) continue;
       for (int u = 0; ok && u < n; ++u) {
-        const int g = gt + u;
-        ok = mbar_wait(bar[PDS_FULL], g & 1, abort_flag, p.status);
+        const int g = gt + u, st = g & 1;
+        ok = mbar_wait(bar[PDS_FULL + st], (g >> 1) & 1, abort_flag, p.status);
         if (!ok) break;
         bool stored = false;
         if (p.ds_tiles) {
           const int64_t ti = ds_tile_index<LMK>(p, it, u);
           if (ti >= 0) {
-            bulk_store(reinterpret_cast<uint8_t*>(p.ds_tiles) + ti * DSALT_DS_TILE_BYTES, smem_u32(sm.dst),
-                       DSALT_DS_TILE_BYTES);
+            bulk_store(reinterpret_cast<uint8_t*>(p.ds_tiles) + ti * DSALT_DS_TILE_BYTES,
+                       smem_u32(sm.stage + st * (BM * BN * 2)), DSALT_DS_TILE_BYTES);
             bulk_commit();
             stored = true;
           } else {
@@ -345,7 +367,7 @@ __global__ void __launch_bounds__(kThreadsKV, 1) tc_bwd_dkdv_kernel(const __grid
           }
         }
         if (stored) bulk_wait_read0();  // the buffer is read: the rows may overwrite it
-        mbar_arrive(bar[PDS_EMPTY]);
+        mbar_arrive(bar[DS_EMPTY + st]);
       }
       if (ok) mbar_arrive(bar[KV_DONE]);
       gt += n;
@@ -487,22 +509,25 @@ __global__ void __launch_bounds__(kThreadsKV, 1) tc_bwd_dkdv_kernel(const __grid
     // Two warps issue so that their MMAs overlap (one issuing thread sustains
     // only about one MMA per 110 cycles): warp A issues Sᵀ = K·Qᵀ and
     // dV += Pᵀ·dO, warp B dPᵀ = V·dOᵀ and dK += dSᵀ·Q.  Barriers they both
-    // complete count two arrivals.  An item's first two Sᵀ / dPᵀ run while the
-    // row warps still store the previous item (its accumulators are only
-    // overwritten after the epilogue released them: ACC_EMPTY).
+    // complete count two arrivals.  Pᵀ / dSᵀ of tile g sit in the TMEM buffer
+    // g % 2 of Sᵀ / dPᵀ, so a warp issues Sᵀ / dPᵀ of tile g + 2 into that buffer
+    // only after its own dV / dK MMA of tile g completed (DONE_A / DONE_B).  An
+    // item's first two Sᵀ / dPᵀ run while the row warps still store the previous
+    // item (its accumulators are only overwritten after the epilogue released
+    // them: ACC_EMPTY).
     const bool is_a = warp == kMmaWarp;
     const uint32_t id_s = idesc_f16(kBF16, BM, BN, false, false);
     const uint32_t id_kv = idesc_f16(kBF16, BM, D, false, true);
     const uint32_t kv_addr = smem_u32(is_a ? sm.k : sm.v);
-    const uint32_t pds = smem_u32(is_a ? sm.pt : sm.dst);
     const uint32_t t_sd = is_a ? tS : tdP, t_acc = is_a ? tdV : tdK;
+    const int done = is_a ? DONE_A : DONE_B;
     // operand tiles: Sᵀ reads Q, dPᵀ reads dO; dV reads dO, dK reads Q
     auto tile_sd = [&](int qs) { return smem_u32(is_a ? sm.q[qs] : sm.dO[qs]); };
     auto tile_acc = [&](int qs) { return smem_u32(is_a ? sm.dO[qs] : sm.q[qs]); };
     auto issue_sd = [&](int g) -> bool {
       const int st = g & 1, qs = g % kQStages;
       if (!mbar_wait(bar[(is_a ? Q_FULL : DO_FULL) + qs], (g / kQStages) & 1, abort_flag, p.status)) return false;
-      if (g >= 2 && !mbar_wait(bar[SD_EMPTY + st], ((g >> 1) - 1) & 1, abort_flag, p.status)) return false;
+      if (g >= 2 && !mbar_wait(bar[done + st], ((g >> 1) - 1) & 1, abort_flag, p.status)) return false;
       tc_fence_after();
       const uint32_t ba = tile_sd(qs);
 #pragma unroll
@@ -528,17 +553,19 @@ __global__ void __launch_bounds__(kThreadsKV, 1) tc_bwd_dkdv_kernel(const __grid
         if (ok && n <= 2) mma_commit(bar[KV_EMPTY]);  // every Sᵀ / dPᵀ of the item is issued
         for (int u = 0; ok && u < n; ++u) {
           const int g = gt + u, qs = g % kQStages;
-          ok = mbar_wait(bar[PDS_FULL], g & 1, abort_flag, p.status) &&
+          ok = mbar_wait(bar[PDS_FULL + (g & 1)], (g >> 1) & 1, abort_flag, p.status) &&
                mbar_wait(bar[(is_a ? DO_FULL : Q_FULL) + qs], (g / kQStages) & 1, abort_flag, p.status) &&
                (u > 0 || gi == 0 || mbar_wait(bar[ACC_EMPTY], (gi - 1) & 1, abort_flag, p.status));
           if (!ok) break;
           tc_fence_after();
           const uint32_t ba = tile_acc(qs);
+          // A = Pᵀ / dSᵀ in TMEM: K step kk (queries 16·kk …) in columns 16·kk … 16·kk + 7
+          // of the buffer, where the row warps of quarter kk wrote them
 #pragma unroll
           for (int kk = 0; kk < BN / 16; ++kk)
-            mma_f16(t_acc, sdesc_sw128(pds + kk * 32, 16, 1024), sdesc_sw128(ba + kk * 2048, BN * 128, 1024),
-                    id_kv, (u > 0 || kk > 0) ? 1u : 0u);
-          mma_commit(bar[PDS_EMPTY]);
+            mma_f16_tmem_a(t_acc, t_sd + (g & 1) * BN + kQuarter * kk, sdesc_sw128(ba + kk * 2048, BN * 128, 1024),
+                           id_kv, (u > 0 || kk > 0) ? 1u : 0u);
+          mma_commit(bar[done + (g & 1)]);
           mma_commit(bar[QDO_EMPTY + qs]);
           if (u + 2 < n) {
             ok = issue_sd(g + 2);
@@ -617,44 +644,37 @@ __global__ void __launch_bounds__(kThreadsKV, 1) tc_bwd_dkdv_kernel(const __grid
           all_in = cst.lo_max[quarter] <= jf && cst.qi_min[quarter] >= jl;
           all_out = cst.lo_min[quarter] > jl || cst.qi_max[quarter] < jf;
         }
-        // band items: this warp's keys hold soft-edge keys of some of its columns
-        // (the quarter's edge range meets the warp's key range; warp-uniform)
-        const bool warp_edge = !LMK && cst.elo_min[quarter] <= jl && cst.ehi_max[quarter] >= jf;
-        // Pᵀ and dSᵀ of this thread's 16 columns, packed to the input dtype; with
-        // warp_edge also ∂loss/∂w̃ = dS·(1 − σ)/τ of each column's entry
+        // band items: bit c of emask is set when column c0 + c has soft-edge keys
+        // among this warp's 32 keys (warp-uniform; a column's edge is a few keys,
+        // so few bits are set)
+        uint32_t emask = 0u;
+        if (!LMK) {
+          bool hit = false;
+          if (lane < kQuarter) {
+            const int2 eb = *reinterpret_cast<const int2*>(&rec[lane].ehi);  // ehi, elo
+            hit = eb.y <= eb.x && eb.y <= jl && eb.x >= jf;
+          }
+          emask = __ballot_sync(0xffffffffu, hit);
+        }
+        // Pᵀ and dSᵀ of this thread's 16 columns, packed to the input dtype
         uint32_t pk_p[8], pk_d[8];
-        // ∂loss/∂w̃ after the first reduce-scatter step (lane distance 16): v8[i]
-        // is the pair sum of column 8·lane[4] + i
-        float v8[8];
-        const bool u16 = lane & 16;
         if (all_out) {
-          tc_fence_before();
-          mbar_arrive(bar[SD_EMPTY + st]);
 #pragma unroll
-          for (int q = 0; q < 8; ++q) { pk_p[q] = 0u; pk_d[q] = 0u; v8[q] = 0.f; }
+          for (int q = 0; q < 8; ++q) { pk_p[q] = 0u; pk_d[q] = 0u; }
         } else {
           float sv[16], dpv[16];
           tmem_ld16(tS + lane_addr + st * BN + c0, sv);
           tmem_ld16(tdP + lane_addr + st * BN + c0, dpv);
           tmem_wait_ld();
-          tc_fence_before();
-          mbar_arrive(bar[SD_EMPTY + st]);
-          // the all-valid case (warp-uniform) runs without the per-element test;
-          // the soft window edge (kEdge): Pᵀ, dSᵀ *= σ((w̃ − d)/τ) on each column's
-          // edge keys elo … ehi (factor ehi − j of the record, or computed past the
-          // stored ones)
-          auto body = [&](auto kAllIn, auto kEdgeT) {
+          // the all-valid case (warp-uniform) runs without the per-element test
+          auto body = [&](auto kAllIn) {
             constexpr bool kIn = decltype(kAllIn)::value;
-            constexpr bool kEdge = decltype(kEdgeT)::value;
-            // columns 2qq, 2qq + 1, 2qq + 8, 2qq + 9 together: the first exchange of
-            // the ∂loss/∂w̃ reduce-scatter pairs column i with column i + 8
 #pragma unroll
-            for (int qq = 0; qq < 4; ++qq) {
-              float pr4[4], ds4[4], dw4[4];
+            for (int c = 0; c < 16; c += 2) {
+              float pr2[2], ds2[2];
 #pragma unroll
-              for (int e4 = 0; e4 < 4; ++e4) {
-                const int cc = 2 * qq + (e4 & 1) + 8 * (e4 >> 1);
-                const QRec& rq = rec[cc];
+              for (int e = 0; e < 2; ++e) {
+                const QRec& rq = rec[c + e];
                 // nlse2, delta (and lo, qi only where a column can be invalid)
                 float4 r0;
                 if (kIn) {
@@ -666,84 +686,79 @@ __global__ void __launch_bounds__(kThreadsKV, 1) tc_bwd_dkdv_kernel(const __grid
                 bool valid;
                 float pr;
                 if (LMK) {
-                  pr = fast_exp2(fmaf(sv[cc], sl2, lw2 + r0.x));
+                  pr = fast_exp2(fmaf(sv[c + e], sl2, lw2 + r0.x));
                   valid = kIn || (key_ok && j <= __float_as_int(r0.w) && jfl < rq.wlo);
                 } else {
-                  pr = fast_exp2(fmaf(sv[cc], sl2, r0.x));
+                  pr = fast_exp2(fmaf(sv[c + e], sl2, r0.x));
                   valid = kIn || (j >= __float_as_int(r0.z) && j <= __float_as_int(r0.w));
                 }
-                float dsv = pr * (dpv[cc] - r0.y);
-                if (kEdge) {
-                  const int2 eb = *reinterpret_cast<const int2*>(&rq.ehi);  // ehi, elo
-                  float gf = 1.0f;
-                  if (j <= eb.x && j >= eb.y) {
-                    const int ei = eb.x - j;
-                    gf = ei < kMaxEdge ? rq.eg[ei] : qrec_edge_factor(rq.wt, rq.qi - j, inv_tau);
-                  }
-                  pr *= gf;
-                  dsv *= gf;
-                  dw4[e4] = valid ? dsv * (1.0f - gf) * inv_tau : 0.f;
-                }
-                pr4[e4] = valid ? pr : 0.f;
-                ds4[e4] = valid ? dsv : 0.f;
-                if (LMK) dlw += ds4[e4];
+                const float dsv = pr * (dpv[c + e] - r0.y);
+                pr2[e] = valid ? pr : 0.f;
+                ds2[e] = valid ? dsv : 0.f;
+                if (LMK) dlw += ds2[e];
               }
-              pk_p[qq] = pack2(pr4[0], pr4[1], kBF16);
-              pk_d[qq] = pack2(ds4[0], ds4[1], kBF16);
-              pk_p[qq + 4] = pack2(pr4[2], pr4[3], kBF16);
-              pk_d[qq + 4] = pack2(ds4[2], ds4[3], kBF16);
-              if (kEdge) {
-#pragma unroll
-                for (int i = 0; i < 2; ++i)
-                  v8[2 * qq + i] = (u16 ? dw4[2 + i] : dw4[i]) +
-                                   __shfl_xor_sync(0xffffffffu, u16 ? dw4[i] : dw4[2 + i], 16);
-              }
+              pk_p[c / 2] = pack2(pr2[0], pr2[1], kBF16);
+              pk_d[c / 2] = pack2(ds2[0], ds2[1], kBF16);
             }
           };
-          if (warp_edge) {
-            if (all_in) body(std::true_type{}, std::true_type{}); else body(std::false_type{}, std::true_type{});
-          } else {
-            if (all_in) body(std::true_type{}, std::false_type{}); else body(std::false_type{}, std::false_type{});
-          }
+          if (all_in) body(std::true_type{}); else body(std::false_type{});
         }
-        if (!LMK) {
-          // the warp's sum of each column's ∂loss/∂w̃ over its 32 keys: a fixed
-          // reduce-scatter (halves exchanged at lane distances 16, 8, 4, 2, then
-          // the pair at distance 1), after which lane l holds column
-          // 8·l[4] + 4·l[3] + 2·l[2] + l[1]; the column warp adds the four warps'
-          // partials once the tile is released
-          float part = 0.f;
-          if (warp_edge) {
-            float v4[4], v2[2];
-            const bool u8 = lane & 8, u4 = lane & 4, u2 = lane & 2;
+        // soft window edge (band items, the columns of emask only, after the
+        // straight-line pass above): Pᵀ, dSᵀ *= σ((w̃ − d)/τ) on the column's edge
+        // keys elo … ehi, applied to the rounded entries (factor ehi − j of the
+        // record, or computed past the stored ones); the column's
+        // ∂loss/∂w̃ = Σ dS·(1 − σ)/τ over the warp's 32 keys by a fixed butterfly,
+        // kept by lane c
+        float dw_col = 0.f;
+        for (uint32_t m = emask; m != 0u; m &= m - 1u) {  // warp-uniform
+          const int c = __ffs(m) - 1;
+          const QRec& rq = rec[c];
+          const int2 eb = *reinterpret_cast<const int2*>(&rq.ehi);  // ehi, elo
+          float dwv = 0.f;
+          if (j >= eb.y && j <= eb.x) {
+            const int ei = eb.x - j;
+            const float gf = ei < kMaxEdge ? rq.eg[ei] : qrec_edge_factor(rq.wt, rq.qi - j, inv_tau);
+            const int w2 = c >> 1, sh = (c & 1) * 16;
+            uint32_t wp = 0u, wd = 0u;
 #pragma unroll
-            for (int i = 0; i < 4; ++i)
-              v4[i] = (u8 ? v8[i + 4] : v8[i]) + __shfl_xor_sync(0xffffffffu, u8 ? v8[i] : v8[i + 4], 8);
+            for (int i = 0; i < 8; ++i)
+              if (i == w2) { wp = pk_p[i]; wd = pk_d[i]; }
+            const float v = bits_to_f32<T>(wd >> sh) * gf;
+            wp = (wp & ~(0xffffu << sh)) | (f32_to_bits<T>(bits_to_f32<T>(wp >> sh) * gf) << sh);
+            wd = (wd & ~(0xffffu << sh)) | (f32_to_bits<T>(v) << sh);
+            dwv = v * (1.0f - gf) * inv_tau;
 #pragma unroll
-            for (int i = 0; i < 2; ++i)
-              v2[i] = (u4 ? v4[i + 2] : v4[i]) + __shfl_xor_sync(0xffffffffu, u4 ? v4[i] : v4[i + 2], 4);
-            part = (u2 ? v2[1] : v2[0]) + __shfl_xor_sync(0xffffffffu, u2 ? v2[0] : v2[1], 2);
-            part += __shfl_xor_sync(0xffffffffu, part, 1);
+            for (int i = 0; i < 8; ++i)
+              if (i == w2) { pk_p[i] = wp; pk_d[i] = wd; }
           }
-          if ((lane & 1) == 0) {
-            const int colw = ((lane >> 4) & 1) * 8 + ((lane >> 3) & 1) * 4 + ((lane >> 2) & 1) * 2 + ((lane >> 1) & 1);
-            sm.dwp[cs][warp & 3][c0 + colw] = part;
-          }
+#pragma unroll
+          for (int off = 16; off > 0; off >>= 1) dwv += __shfl_xor_sync(0xffffffffu, dwv, off);
+          if (lane == c) dw_col = dwv;
         }
-        // the single Pᵀ / dSᵀ buffer is free once the previous tile's dV / dK MMAs completed
-        if (g >= 1) {
-          ok = mbar_wait(bar[PDS_EMPTY], (g - 1) & 1, abort_flag, p.status);
+        // the shared dSᵀ buffer g % 2 is free once the store lane has read its
+        // previous tile
+        if (g >= 2) {
+          ok = mbar_wait(bar[DS_EMPTY + st], ((g >> 1) - 1) & 1, abort_flag, p.status);
           if (!__all_sync(0xffffffffu, ok)) { ok = false; break; }
         }
-#pragma unroll
-        for (int q = 0; q < 2; ++q) {
-          *reinterpret_cast<uint4*>(sm.pt + sw128_offset(r, c0 + 8 * q)) =
-              make_uint4(pk_p[4 * q], pk_p[4 * q + 1], pk_p[4 * q + 2], pk_p[4 * q + 3]);
-          *reinterpret_cast<uint4*>(sm.dst + sw128_offset(r, c0 + 8 * q)) =
-              make_uint4(pk_d[4 * q], pk_d[4 * q + 1], pk_d[4 * q + 2], pk_d[4 * q + 3]);
+        // Pᵀ, dSᵀ over this quarter's own (already read) Sᵀ, dPᵀ columns: the
+        // A operand of K step `quarter` of the dV / dK MMAs
+        tmem_st8u(tS + lane_addr + st * BN + c0, pk_p);
+        tmem_st8u(tdP + lane_addr + st * BN + c0, pk_d);
+        // the dSᵀ tile for the dQ stage: row r, columns c0 … c0 + 15 of the
+        // 128B-swizzled shared buffer
+        {
+          uint8_t* dsb = sm.stage + st * (BM * BN * 2);
+          *reinterpret_cast<uint4*>(dsb + sw128_offset(r, c0)) = make_uint4(pk_d[0], pk_d[1], pk_d[2], pk_d[3]);
+          *reinterpret_cast<uint4*>(dsb + sw128_offset(r, c0 + 8)) = make_uint4(pk_d[4], pk_d[5], pk_d[6], pk_d[7]);
         }
-        fence_async_smem();
-        mbar_arrive(bar[PDS_FULL]);
+        // the warp's ∂loss/∂w̃ sums of its 16 columns (0 without edge keys); the
+        // column warp adds the four row warps' partials once the tile is released
+        if (!LMK && lane < kQuarter) sm.dwp[cs][warp & 3][c0 + lane] = dw_col;
+        tmem_wait_st();
+        tc_fence_before();
+        fence_async_smem();  // the store lane's bulk copy reads the buffer
+        mbar_arrive(bar[PDS_FULL + st]);
         mbar_arrive(bar[COL_EMPTY + cs]);
       }
       if (!ok) break;
@@ -781,13 +796,13 @@ __global__ void __launch_bounds__(kThreadsKV, 1) tc_bwd_dkdv_kernel(const __grid
                                : 0.f;
         ok = ok && rows_sync();  // dlw_part is reused by the next item
       } else {
-        // dK, then dV: the rows are staged in the (idle) Pᵀ/dSᵀ buffers, 16-byte
-        // units XOR-swizzled by row % 8, and stored row-contiguously.  A key that
+        // dK, then dV: the rows are staged in shared memory, 16-byte units
+        // XOR-swizzled by row % 8, and stored row-contiguously.  A key that
         // holds landmark slots (first slot cl_first) also leaves its fp32 rows in
         // the band scratch: lmk_fixup_kernel adds the landmark pass's parts to them
         // and rounds once.
         constexpr int kUnits = D * 2 / 16;
-        uint8_t* stage = sm.pt;
+        uint8_t* stage = sm.stage;
         const int64_t HD = (int64_t)p.H * D;
 #pragma unroll 1
         for (int m = 0; ok && m < 2; ++m) {
@@ -829,7 +844,7 @@ __global__ void __launch_bounds__(kThreadsKV, 1) tc_bwd_dkdv_kernel(const __grid
             *reinterpret_cast<uint4*>(dst + rr * HD * 2 + uu * 16) =
                 *reinterpret_cast<const uint4*>(stage + rr * (kUnits * 16) + ((uu ^ (rr & 7)) << 4));
           }
-          ok = rows_sync();  // the staging area is reused (dV, or the next item's Pᵀ / dSᵀ)
+          ok = rows_sync();  // the staging area is reused (dV, or the next item's dSᵀ tiles)
         }
       }
       gt += n;

@@ -3,8 +3,8 @@
 //
 // The dK/dV stage (attn_tc_bwd.cu) computes every dSᵀ tile of the band and the
 // landmark pass once, applies the soft window edge and stores the tile (128 keys
-// × 64 queries, 16-bit, in the 128-byte-swizzled layout of its shared-memory
-// buffer) to the ds_tiles scratch.  Here each work item is one 128-query block of
+// × 64 queries, 16-bit, in the 128-byte-swizzled layout of a K-major shared-memory
+// operand tile) to the ds_tiles scratch.  Here each work item is one 128-query block of
 // one head: for every key block (and landmark chunk) whose dK/dV item covered
 // the block, the two stored 64-query tiles and the 128-row K tile are loaded
 // (bulk copy and TMA) and one tcgen05.mma chain accumulates dQ in TMEM:
@@ -14,7 +14,7 @@
 // No exponentials and no S/dP recomputation: this replaces the query-parallel
 // recompute of the reference's _train_bwd_kernel (dsalt/kernels/
 // dsalt_triton_train.py:240-383, dQ at :335-368; landmark part :302-333).
-// ∂loss/∂w̃ is computed by the dK/dV stage (its soft-edge fix-up).
+// ∂loss/∂w̃ is computed by the dK/dV stage (with the soft-edge factors).
 //
 // Persistent CTAs (one per SM), items (head, query block) round-robin, two TMEM
 // accumulators so that one item's epilogue overlaps the next item's MMAs.

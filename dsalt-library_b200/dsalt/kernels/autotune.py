@@ -35,7 +35,8 @@ def _tiles(head_dim: int) -> dict:
         "bwd_dkdv": {"key_rows": 128, "query_tile": 64, "q_do_stages": 3, "record_stages": 4, "threads": 640,
                      "warps": {"rows (16-column quarters)": 16, "tma + tile store": 1, "mma_s_dv": 1,
                                "records": 1, "mma_dp_dk": 1},
-                     "tmem_columns": {"S^T, dP^T (double buffer)": 256, "dK": head_dim, "dV": head_dim}},
+                     "tmem_columns": {"S^T, dP^T (double buffer; P^T, dS^T written over them)": 256,
+                                      "dK": head_dim, "dV": head_dim}},
         # attn_tc_dq.cu: persistent, dQ = dS·K over the stored dS^T tiles
         "bwd_dq": {"query_rows": 128, "key_block": 128, "stages": 3, "threads": 192,
                    "warps": {"loads": 1, "mma": 1, "epilogue": 4},

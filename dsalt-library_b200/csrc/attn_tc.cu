@@ -14,7 +14,8 @@
 //               exp2 domain with a lazy rescale (the running max only moves when
 //               it grows by more than 2^8); P (bf16/fp16) goes to a 128B-swizzled
 //               K-major smem tile (chunk h = half h), where each thread applies
-//               the soft window edge to its ≤ ceil(win_edge)+1 edge keys in place.
+//               the soft window edge to its row's ≤ ceil(win_edge)+1 edge keys in
+//               place, walking only those entries.
 //               The epilogue stages O in the P buffer and stores it row-contiguously,
 //               in the input dtype, or in fp32 when the caller asks for the op's
 //               fp32 output (o_f32: then that is the only O written).
@@ -75,7 +76,7 @@ enum Bar {
 struct ItemInfo {
   int h, s, m0, L;
   int64_t s0;
-  int band_lo, band_hi, n_valid, n_lt, n_tiles, slow_edge;
+  int band_lo, band_hi, n_valid, n_lt, n_tiles;
   int row_lo[BM], row_hi[BM], row_cnt[BM], row_de0[BM], row_ne[BM];
   float row_wt[BM];
   int lmk_pos[kMaxLmk];
@@ -133,7 +134,7 @@ __device__ __forceinline__ void resolve_item(const DsaltAttnParams& p, int idx, 
     nv += __popc(__ballot_sync(0xffffffffu, ps >= 0));
   }
   __syncwarp();
-  int blo = INT_MAX, bhi = -1, slow = 0;
+  int blo = INT_MAX, bhi = -1;
   for (int r = lane; r < BM; r += 32) {
     const int i = m0 + r;
     int lo = INT_MAX, hi = -1, cnt = 0, d_e0 = INT_MAX, ne = 0;
@@ -159,18 +160,15 @@ __device__ __forceinline__ void resolve_item(const DsaltAttnParams& p, int idx, 
     in.row_lo[r] = lo; in.row_hi[r] = hi; in.row_cnt[r] = cnt;
     in.row_de0[r] = d_e0; in.row_ne[r] = ne; in.row_wt[r] = wt;
     if (lo <= hi) { blo = min(blo, lo); bhi = max(bhi, hi); }
-    if (ne > kMaxEdge) slow = 1;
   }
   blo = __reduce_min_sync(0xffffffffu, blo);
   bhi = __reduce_max_sync(0xffffffffu, bhi);
-  slow = __reduce_or_sync(0xffffffffu, slow);
   if (lane == 0) {
     const int n_lt = (nv + BN - 1) / BN;
     int n_bt = bhi >= blo ? (bhi - blo + BN) / BN : 0;
     if (n_lt + n_bt == 0) { blo = 0; bhi = 0; n_bt = 1; }  // one fully masked tile
     in.h = h; in.s = s; in.m0 = m0; in.L = L; in.s0 = s0;
     in.band_lo = blo; in.band_hi = bhi; in.n_valid = nv; in.n_lt = n_lt; in.n_tiles = n_lt + n_bt;
-    in.slow_edge = slow;
   }
   __syncwarp();
 }
@@ -415,7 +413,6 @@ __global__ void __launch_bounds__(kThreads, 1) tc_fwd_kernel(const __grid_consta
       const int lo = in.row_lo[r], hi = in.row_hi[r], cnt = in.row_cnt[r];
       const int d_e0 = in.row_de0[r], ne = in.row_ne[r];
       const float wt = in.row_wt[r];
-      const bool slow_edge = in.slow_edge != 0;
       // soft-edge factors of the row's edge keys (same expression as the per-key form)
       float eg[kMaxEdge];
 #pragma unroll
@@ -523,40 +520,21 @@ __global__ void __launch_bounds__(kThreads, 1) tc_fwd_kernel(const __grid_consta
             *reinterpret_cast<uint4*>(sp + sw128_offset(r, c)) = u;
           }
         }
-        if (!lmk && !all_out) {
+        if (!lmk && !all_out && ne > 0) {
           // soft window edge on this row's edge keys in this thread's columns:
-          // p *= σ((w̃ − d)/τ); the key at distance d_e0 + e sits in column ce0 − e
+          // p *= σ((w̃ − d)/τ); the key at distance d_e0 + e sits in column ce0 − e.
+          // Each lane walks only its own entries (a row's edge is a few keys), the
+          // factors past the precomputed ones computed by the same expression.
           const int ce0 = i - d_e0 - n0 - c0;
-          const bool has = ne > 0 && ce0 >= 0 && ce0 - (ne - 1) <= HALF - 1;
-          if (!slow_edge) {
-            if (__any_sync(0xffffffffu, has)) {
-              // all loads first, then all stores: the entries are distinct
-              float pv[kMaxEdge];
-#pragma unroll
-              for (int e = 0; e < kMaxEdge; ++e) {
-                const int c = ce0 - e;
-                const bool inr = has && e < ne && c >= 0 && c < HALF;
-                pv[e] = inr ? to_f32<T>(*reinterpret_cast<const T*>(sp + sw128_offset(r, c))) : 0.f;
-              }
-#pragma unroll
-              for (int e = 0; e < kMaxEdge; ++e) {
-                const int c = ce0 - e;
-                if (has && e < ne && c >= 0 && c < HALF) {
-                  *reinterpret_cast<T*>(sp + sw128_offset(r, c)) = from_f32<T>(pv[e] * eg[e]);
-                  l -= pv[e] * (1.0f - eg[e]);
-                }
-              }
-            }
-          } else if (has) {
-            for (int e = max(0, ce0 - (HALF - 1)); e < ne && ce0 - e >= 0; ++e) {
-              const int c = ce0 - e;
-              T* ep = reinterpret_cast<T*>(sp + sw128_offset(r, c));
-              const float pv = to_f32<T>(*ep);
-              const float z = (wt - (float)(d_e0 + e)) * inv_tau;
-              const float sg = 1.0f / (1.0f + expf(-z));
-              *ep = from_f32<T>(pv * sg);
-              l -= pv * (1.0f - sg);
-            }
+          const int rx = r & 7;
+          uint8_t* rowp = sp + r * 128;
+          for (int e = max(0, ce0 - (HALF - 1)); e < ne && ce0 - e >= 0; ++e) {
+            const int c = ce0 - e;
+            T* ep = reinterpret_cast<T*>(rowp + ((((c >> 3) ^ rx) << 4) | ((c & 7) << 1)));
+            const float pv = to_f32<T>(*ep);
+            const float sg = e < kMaxEdge ? eg[e] : 1.0f / (1.0f + expf(-((wt - (float)(d_e0 + e)) * inv_tau)));
+            *ep = from_f32<T>(pv * sg);
+            l -= pv * (1.0f - sg);
           }
         }
         // rescale O_h once P is out of registers; a finite running max implies an

@@ -17,13 +17,8 @@
 // the ds_tiles scratch (16 KB per tile), where the dQ stage (attn_tc_dq.cu) reads
 // it: dQ = scale·Σ dS·K without a second computation of S, dP and the
 // exponentials.
-// The row threads also form ∂loss/∂w̃ = Σ_edge dS·(1 − σ)/τ of each query column
-// (the reference's D_w, :371-383) in a fixed order: a warp butterfly over its 32
-// keys (only for the columns whose edge keys meet them), then the column warp's
-// sum of the four row warps' partials, added to
-// dw_head, which the preprocess stage zeroed.  A query's edge keys lie in at most
-// two key blocks, so each dw_head entry receives at most two additions onto zero,
-// whose result does not depend on their order.
+// ∂loss/∂w̃ = Σ_edge dS·(1 − σ)/τ of each query (the reference's D_w, :371-383)
+// is formed by the dQ stage from the stored, σ-scaled dSᵀ entries.
 //
 // All waits are bounded (sm100::mbar_wait); see attn_tc.cu.
 #include <mutex>
@@ -138,7 +133,6 @@ struct alignas(1024) Smem {
   int abort_flag;
   QRec rec[kColStages][BN];  // the tile's query records (bulk-copied, then fixed up)
   ColStats stats[kColStages];
-  float dwp[kColStages][4][BN];  // band items: per-row-warp partial sums of ∂loss/∂w̃ per query column
   float dlw_part[4][BM];  // landmark items: d_lw partial sums of the four column quarters
 };
 static_assert(2 * BM * BN * 2 >= BM * 128 * 2, "the dSᵀ buffers hold one staged dK or dV block (D ≤ 128)");
@@ -403,42 +397,16 @@ __global__ void __launch_bounds__(kThreadsKV, 1) tc_bwd_dkdv_kernel(const __grid
       mbar_expect_tx(bar[REC_FULL + st], nrec * (uint32_t)sizeof(QRec));
       bulk_load(smem_u32(&sm.rec[st][0]), recg + q0, nrec * (uint32_t)sizeof(QRec), bar[REC_FULL + st]);
     };
-    // band items: ∂loss/∂w̃ of tile gd's query columns from this key block, once the
-    // rows released the tile: the four row warps' partials summed in a fixed order,
-    // one addition per column to dw_head (a column's edge keys lie in at most two
-    // key blocks, so dw_head receives at most two additions onto zero)
-    struct Prev {  // what sum_dw needs of the previous tile's item
-      int64_t s0;
-      int h, key0, nkeys;
-    };
-    auto sum_dw = [&](const Prev& c, int gd) {
-      const int sd = gd % kColStages;
-      const int klo = c.key0, khi = c.key0 + c.nkeys - 1;
-#pragma unroll
-      for (int k2 = 0; k2 < 2; ++k2) {
-        const int col = lane + 32 * k2;
-        const QRec& rc = sm.rec[sd][col];
-        if (rc.elo <= rc.ehi && rc.elo <= khi && rc.ehi >= klo) {
-          const float v = (sm.dwp[sd][0][col] + sm.dwp[sd][1][col]) + (sm.dwp[sd][2][col] + sm.dwp[sd][3][col]);
-          atomicAdd(p.dw_head + (c.s0 + rc.qi) * p.H + c.h, v);
-        }
-      }
-    };
-    const bool want_dw = !LMK && p.dw_head != nullptr;
     Cur ci{(int)blockIdx.x, 0, Item{}}, cp{(int)blockIdx.x, 0, Item{}};
     seek(ci);
     seek(cp);
-    Prev cprev{0, 0, 0, 0};
-    int g_issued = 0, g = 0;
-    bool col_ok = true;
+    int g_issued = 0;
     for (; ci.idx < n_items && g_issued < kColStages - 1; ++g_issued, advance(ci))
       if (lane == 0) issue(ci, g_issued);
-    for (; cp.idx < n_items; ++g, advance(cp)) {
+    for (int g = 0; cp.idx < n_items; ++g, advance(cp)) {
       const int st = g % kColStages;
-      if (!__all_sync(0xffffffffu, mbar_wait(bar[REC_FULL + st], (g / kColStages) & 1, abort_flag, p.status))) {
-        col_ok = false;
+      if (!__all_sync(0xffffffffu, mbar_wait(bar[REC_FULL + st], (g / kColStages) & 1, abort_flag, p.status)))
         break;
-      }
       const int q0 = cp.it.q_start + BN * cp.u;
       // per lane: columns lane (quarter lane/16) and lane + 32 (quarter 2 + lane/16)
       int st_lo_max[2], st_lo_min[2], st_qi_min[2], st_qi_max[2], st_elo_min[2], st_ehi_max[2];
@@ -479,28 +447,18 @@ __global__ void __launch_bounds__(kThreadsKV, 1) tc_bwd_dkdv_kernel(const __grid
         }
       }
       mbar_arrive(bar[COL_FULL + st]);
-      // tile g − 1: once the rows released it, its ∂loss/∂w̃ sums, then the refill
-      // of its stage with the next tile
-      if (g >= 1) {
-        if (!__all_sync(0xffffffffu, mbar_wait(bar[COL_EMPTY + (g - 1) % kColStages], ((g - 1) / kColStages) & 1,
-                                               abort_flag, p.status))) {
-          col_ok = false;
-          break;
-        }
-        if (want_dw) sum_dw(cprev, g - 1);
-      }
+      // refill the stage of tile g − 1 with the next tile once the rows released it
       if (ci.idx < n_items) {
-        if (lane == 0) issue(ci, g_issued);  // g_issued == g + kColStages − 1
+        const int ng = g_issued;  // == g + kColStages − 1
+        if (ng >= kColStages &&
+            !__all_sync(0xffffffffu,
+                        mbar_wait(bar[COL_EMPTY + ng % kColStages], (ng / kColStages - 1) & 1, abort_flag, p.status)))
+          break;
+        if (lane == 0) issue(ci, ng);
         ++g_issued;
         advance(ci);
       }
-      cprev = Prev{cp.it.s0, cp.it.h, cp.it.key0, cp.it.nkeys};
     }
-    if (col_ok && g >= 1 &&
-        __all_sync(0xffffffffu, mbar_wait(bar[COL_EMPTY + (g - 1) % kColStages], ((g - 1) / kColStages) & 1,
-                                          abort_flag, p.status)) &&
-        want_dw)
-      sum_dw(cprev, g - 1);
     if (lane == 0)
       for (int g = max(0, g_issued - kColStages); g < g_issued; ++g)
         mbar_drain(bar[REC_FULL + g % kColStages], (g / kColStages) & 1);
@@ -706,15 +664,11 @@ __global__ void __launch_bounds__(kThreadsKV, 1) tc_bwd_dkdv_kernel(const __grid
         // soft window edge (band items, the columns of emask only, after the
         // straight-line pass above): Pᵀ, dSᵀ *= σ((w̃ − d)/τ) on the column's edge
         // keys elo … ehi, applied to the rounded entries (factor ehi − j of the
-        // record, or computed past the stored ones); the column's
-        // ∂loss/∂w̃ = Σ dS·(1 − σ)/τ over the warp's 32 keys by a fixed butterfly,
-        // kept by lane c
-        float dw_col = 0.f;
+        // record, or computed past the stored ones)
         for (uint32_t m = emask; m != 0u; m &= m - 1u) {  // warp-uniform
           const int c = __ffs(m) - 1;
           const QRec& rq = rec[c];
           const int2 eb = *reinterpret_cast<const int2*>(&rq.ehi);  // ehi, elo
-          float dwv = 0.f;
           if (j >= eb.y && j <= eb.x) {
             const int ei = eb.x - j;
             const float gf = ei < kMaxEdge ? rq.eg[ei] : qrec_edge_factor(rq.wt, rq.qi - j, inv_tau);
@@ -723,17 +677,12 @@ __global__ void __launch_bounds__(kThreadsKV, 1) tc_bwd_dkdv_kernel(const __grid
 #pragma unroll
             for (int i = 0; i < 8; ++i)
               if (i == w2) { wp = pk_p[i]; wd = pk_d[i]; }
-            const float v = bits_to_f32<T>(wd >> sh) * gf;
             wp = (wp & ~(0xffffu << sh)) | (f32_to_bits<T>(bits_to_f32<T>(wp >> sh) * gf) << sh);
-            wd = (wd & ~(0xffffu << sh)) | (f32_to_bits<T>(v) << sh);
-            dwv = v * (1.0f - gf) * inv_tau;
+            wd = (wd & ~(0xffffu << sh)) | (f32_to_bits<T>(bits_to_f32<T>(wd >> sh) * gf) << sh);
 #pragma unroll
             for (int i = 0; i < 8; ++i)
               if (i == w2) { pk_p[i] = wp; pk_d[i] = wd; }
           }
-#pragma unroll
-          for (int off = 16; off > 0; off >>= 1) dwv += __shfl_xor_sync(0xffffffffu, dwv, off);
-          if (lane == c) dw_col = dwv;
         }
         // the shared dSᵀ buffer g % 2 is free once the store lane has read its
         // previous tile
@@ -752,9 +701,6 @@ __global__ void __launch_bounds__(kThreadsKV, 1) tc_bwd_dkdv_kernel(const __grid
           *reinterpret_cast<uint4*>(dsb + sw128_offset(r, c0)) = make_uint4(pk_d[0], pk_d[1], pk_d[2], pk_d[3]);
           *reinterpret_cast<uint4*>(dsb + sw128_offset(r, c0 + 8)) = make_uint4(pk_d[4], pk_d[5], pk_d[6], pk_d[7]);
         }
-        // the warp's ∂loss/∂w̃ sums of its 16 columns (0 without edge keys); the
-        // column warp adds the four row warps' partials once the tile is released
-        if (!LMK && lane < kQuarter) sm.dwp[cs][warp & 3][c0 + lane] = dw_col;
         tmem_wait_st();
         tc_fence_before();
         fence_async_smem();  // the store lane's bulk copy reads the buffer

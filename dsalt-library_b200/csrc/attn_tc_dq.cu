@@ -14,7 +14,10 @@
 // No exponentials and no S/dP recomputation: this replaces the query-parallel
 // recompute of the reference's _train_bwd_kernel (dsalt/kernels/
 // dsalt_triton_train.py:240-383, dQ at :335-368; landmark part :302-333).
-// ∂loss/∂w̃ is computed by the dK/dV stage (with the soft-edge factors).
+// ∂loss/∂w̃ of each query row is formed here too, by the epilogue thread of the
+// row: Σ over the row's soft-edge keys, in a fixed order, of dS·(1 − σ)/τ, read
+// back from the stored σ-scaled dSᵀ entries (reference :371-383), one store per
+// (token, head), no atomics.
 //
 // Persistent CTAs (one per SM), items (head, query block) round-robin, two TMEM
 // accumulators so that one item's epilogue overlaps the next item's MMAs.
@@ -273,6 +276,7 @@ __global__ void __launch_bounds__(kThreads, 1) tc_bwd_dq_kernel(const __grid_con
     const int et = tid - 32 * kEpiWarp0;      // 0..127
     const uint32_t lane_addr = (uint32_t)(32 * q4) << 16;
     constexpr int kUnits = D * 2 / 16;        // 16-byte units per dQ row
+    const float inv_tau = 1.0f / p.tau_win;
     int li = 0, epi_phase = 0;
     bool ok = true;
     auto epi_sync = [&]() -> bool {
@@ -286,6 +290,35 @@ __global__ void __launch_bounds__(kThreads, 1) tc_bwd_dq_kernel(const __grid_con
       it.nvalid = p.kp > 0 ? count_valid(p, it.lbase) : 0;
       const int n_units = for_units(p, it, [](const Unit&) {});
       const int acc = li & 1;
+      const int m0 = it.qb * BM;
+      const int rows = min(BM, it.L - m0);
+      // ∂loss/∂w̃ of query row r, its loads issued before the wait for the
+      // accumulator: edge key j = ehi − e (summed in the order of e) sits in key
+      // block kb = j / 128, query tile u = (q − 128·kb) / 64 of that block's band
+      // tiles, entry (j − 128·kb, q − 128·kb − 64·u) of the tile image
+      const bool dw_row = p.dw_head != nullptr && r < rows;
+      QRec rc;
+      rc.elo = INT_MAX;
+      rc.ehi = INT_MIN;
+      if (dw_row) {
+        const float4* rp = reinterpret_cast<const float4*>(p.qrec + ((int64_t)it.h * p.T + it.s0 + m0 + r) *
+                                                                        DSALT_QREC_FLOATS);
+        float4* rcv = reinterpret_cast<float4*>(&rc);
+#pragma unroll
+        for (int k = 0; k < DSALT_QREC_FLOATS / 4; ++k) rcv[k] = __ldg(rp + k);
+      }
+      const int ne = qrec_ne(rc);
+      auto edge_entry = [&](int e) -> float {  // the stored dS·σ of edge key ehi − e (0 past the scratch)
+        const int q = m0 + r, j = rc.ehi - e;
+        const int kb = j / KB, u = (q - kb * KB) / 64;
+        if (u >= p.ds_band_tiles) return 0.f;
+        const int64_t tile = ((int64_t)it.h * p.max_blocks + (it.blk - (it.qb - kb))) * p.ds_band_tiles + u;
+        return to_f32<T>(*reinterpret_cast<const T*>(ds_base + tile * kTile +
+                                                      sm100::sw128_offset(j - kb * KB, q - kb * KB - 64 * u)));
+      };
+      float dwv[kQRecEdge];
+#pragma unroll
+      for (int e = 0; e < kQRecEdge; ++e) dwv[e] = e < ne ? edge_entry(e) : 0.f;
       ok = __all_sync(0xffffffffu, mbar_wait(bar[ACC_FULL + acc], (li >> 1) & 1, abort_flag, p.status));
       if (!ok) break;
       tc_fence_after();
@@ -314,14 +347,20 @@ __global__ void __launch_bounds__(kThreads, 1) tc_bwd_dq_kernel(const __grid_con
       tc_fence_before();
       mbar_arrive(bar[ACC_EMPTY + acc]);  // this accumulator is read: the MMA warp may reuse it
       if (!(ok = epi_sync())) break;
-      const int m0 = it.qb * BM;
-      const int rows = min(BM, it.L - m0);
       const int64_t HD = (int64_t)p.H * D;
       uint8_t* dqg = reinterpret_cast<uint8_t*>(p.dq) + ((it.s0 + m0) * HD + (int64_t)it.h * D) * 2;
       for (int un = et; un < rows * kUnits; un += kEpiThreads) {
         const int rr = un / kUnits, uu = un % kUnits;
         *reinterpret_cast<uint4*>(dqg + rr * HD * 2 + uu * 16) =
             *reinterpret_cast<const uint4*>(sm.stage + rr * (kUnits * 16) + ((uu ^ (rr & 7)) << 4));
+      }
+      if (dw_row) {
+        float dw = 0.f;
+#pragma unroll
+        for (int e = 0; e < kQRecEdge; ++e) dw += dwv[e] * (1.0f - rc.eg[e]) * inv_tau;
+        for (int e = kQRecEdge; e < ne; ++e)
+          dw += edge_entry(e) * (1.0f - qrec_edge_factor(rc.wt, rc.qi - (rc.ehi - e), inv_tau)) * inv_tau;
+        p.dw_head[(it.s0 + m0 + r) * p.H + it.h] = dw;
       }
       if (!(ok = epi_sync())) break;  // the staging area is reused by the next item
     }

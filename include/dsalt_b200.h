@@ -210,7 +210,8 @@ DSALT_API int dsalt_attn_bwd_preprocess(const DsaltAttnParams* p, void* stream);
  * atomic-free, deterministic.                                               */
 DSALT_API int dsalt_attn_bwd_dkdv(const DsaltAttnParams* p, void* stream);
 /* Replaces the dQ / d_w̃ part of _train_bwd_kernel (dsalt_triton_train.py:
- * 335-383) and the dQ of _dsalt_bwd_kernel; writes dq, dw_head and dw.      */
+ * 335-383) and the dQ of _dsalt_bwd_kernel; writes dq, dw_head (from the
+ * σ-scaled dSᵀ entries dsalt_attn_bwd_dkdv stored) and dw.                  */
 DSALT_API int dsalt_attn_bwd_dq(const DsaltAttnParams* p, void* stream);
 
 /* ---- selection ------------------------------------------------------------

@@ -51,10 +51,11 @@ simt_fwd_kernel(const DsaltAttnParams p) {
   const float inv_tau = 1.0f / p.tau_win;
   const int D = p.D;
   const int64_t HD = (int64_t)p.H * D;
+  const int64_t KHD = (int64_t)attn_kv_heads(p) * D;  // k, v row stride (grouped kv heads)
 
   const T* q = reinterpret_cast<const T*>(p.q) + t * HD + (int64_t)h * D;
-  const T* kb = reinterpret_cast<const T*>(p.k) + (int64_t)h * D;
-  const T* vb = reinterpret_cast<const T*>(p.v) + (int64_t)h * D;
+  const T* kb = reinterpret_cast<const T*>(p.k) + (int64_t)attn_kv_head(p, h) * D;
+  const T* vb = reinterpret_cast<const T*>(p.v) + (int64_t)attn_kv_head(p, h) * D;
   RowVec<T, R> qv;
   qv.load(q, lane, D);
 
@@ -84,7 +85,7 @@ simt_fwd_kernel(const DsaltAttnParams p) {
     for (int j = jlo; j <= i; ++j) {
       const float d = (float)(i - j);
       const int64_t kt = s0 + j;
-      visit(kb + kt * HD, vb + kt * HD, edge_bias(rw, d, inv_tau));
+      visit(kb + kt * KHD, vb + kt * KHD, edge_bias(rw, d, inv_tau));
     }
   }
   const int64_t lbase = ((int64_t)h * p.S + s) * p.kp;
@@ -179,8 +180,9 @@ simt_bwd_dq_kernel(const DsaltAttnParams p) {
     RowVec<T, R> qv, gv;
     qv.load(reinterpret_cast<const T*>(p.q) + t * HD + (int64_t)h * D, lane, D);
     gv.load(reinterpret_cast<const T*>(p.dout) + t * HD + (int64_t)h * D, lane, D);
-    const T* kb = reinterpret_cast<const T*>(p.k) + (int64_t)h * D;
-    const T* vb = reinterpret_cast<const T*>(p.v) + (int64_t)h * D;
+    const int64_t KHD = (int64_t)attn_kv_heads(p) * D;  // k, v row stride (grouped kv heads)
+    const T* kb = reinterpret_cast<const T*>(p.k) + (int64_t)attn_kv_head(p, h) * D;
+    const T* vb = reinterpret_cast<const T*>(p.v) + (int64_t)attn_kv_head(p, h) * D;
     auto visit = [&](const T* kp, const T* vp, float bias, float dbias) {
       const float sc = fmaf(qv.dot(kp, lane, D), p.scale, bias);
       const float pr = expf(sc - lse);
@@ -197,7 +199,7 @@ simt_bwd_dq_kernel(const DsaltAttnParams p) {
       for (int j = jlo; j <= i; ++j) {
         const float d = (float)(i - j);
         const int64_t kt = s0 + j;
-        visit(kb + kt * HD, vb + kt * HD, edge_bias(rw, d, inv_tau), edge_dbias(rw, d, inv_tau));
+        visit(kb + kt * KHD, vb + kt * KHD, edge_bias(rw, d, inv_tau), edge_dbias(rw, d, inv_tau));
       }
     }
     const int64_t lbase = ((int64_t)h * p.S + s) * p.kp;
@@ -237,8 +239,10 @@ simt_bwd_dkdv_kernel(const DsaltAttnParams p) {
   const int64_t HD = (int64_t)p.H * D;
 
   RowVec<T, R> kv, vv;
-  kv.load(reinterpret_cast<const T*>(p.k) + t * HD + (int64_t)h * D, lane, D);
-  vv.load(reinterpret_cast<const T*>(p.v) + t * HD + (int64_t)h * D, lane, D);
+  // the kv head of query head h; dk, dv are written per query head
+  const int64_t KHD = (int64_t)attn_kv_heads(p) * D;
+  kv.load(reinterpret_cast<const T*>(p.k) + t * KHD + (int64_t)attn_kv_head(p, h) * D, lane, D);
+  vv.load(reinterpret_cast<const T*>(p.v) + t * KHD + (int64_t)attn_kv_head(p, h) * D, lane, D);
   const T* qb = reinterpret_cast<const T*>(p.q) + (int64_t)h * D;
   const T* gb = reinterpret_cast<const T*>(p.dout) + (int64_t)h * D;
   float dk[R], dv[R];

@@ -272,7 +272,7 @@ __global__ void __launch_bounds__(kThreads, 1) tc_fwd_kernel(const __grid_consta
 #pragma unroll
           for (int c = 0; c < D / 64; ++c) {
             if (lmk) tma_load_3d(smem_u32(dst + c * (BN * 128)), map, bar[FULL + st], c * 64, BN * t, in.h * p.S + in.s);
-            else tma_load_3d(smem_u32(dst + c * (BN * 128)), map, bar[FULL + st], c * 64, in.h,
+            else tma_load_3d(smem_u32(dst + c * (BN * 128)), map, bar[FULL + st], c * 64, attn_kv_head(p, in.h),
                              (int)(in.s0 + in.band_lo + BN * (t - n_lt)));
           }
           issued_k = g + 1;
@@ -664,8 +664,10 @@ cudaError_t launch_tc_fwd(const DsaltAttnParams& p, cudaStream_t stream) {
   const uint64_t row = (uint64_t)D * 2;
   const uint64_t trow = (uint64_t)p.H * D * 2;
   if (encode_3d(&a.tm_q, dt, p.q, D, p.H, p.T, row, trow, 64, 1, BM) != CUDA_SUCCESS) return cudaErrorInvalidValue;
-  if (encode_3d(&a.tm_k, dt, p.k, D, p.H, p.T, row, trow, 64, 1, BN) != CUDA_SUCCESS) return cudaErrorInvalidValue;
-  if (encode_3d(&a.tm_v, dt, p.v, D, p.H, p.T, row, trow, 64, 1, BN) != CUDA_SUCCESS) return cudaErrorInvalidValue;
+  // k, v: [T, H_kv, D] (grouped kv heads read in place)
+  const uint64_t hkv = (uint64_t)attn_kv_heads(p), kvrow = hkv * D * 2;
+  if (encode_3d(&a.tm_k, dt, p.k, D, hkv, p.T, row, kvrow, 64, 1, BN) != CUDA_SUCCESS) return cudaErrorInvalidValue;
+  if (encode_3d(&a.tm_v, dt, p.v, D, hkv, p.T, row, kvrow, 64, 1, BN) != CUDA_SUCCESS) return cudaErrorInvalidValue;
   const int kp = p.kp > 0 ? p.kp : 16;
   a.lmk_box = kp < BN ? kp : BN;
   const void* lk = p.kp > 0 ? p.lmk_k : p.k;  // any valid address when there are no landmarks

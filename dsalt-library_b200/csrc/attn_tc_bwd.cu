@@ -297,8 +297,10 @@ __global__ void __launch_bounds__(kThreadsKV, 1) tc_bwd_dkdv_kernel(const __grid
             tma_load_3d(smem_u32(sm.k + c * (BM * 128)), &a.tm_lk, bar[KV_FULL], c * 64, it.key0, it.h * p.S + it.s);
             tma_load_3d(smem_u32(sm.v + c * (BM * 128)), &a.tm_lv, bar[KV_FULL], c * 64, it.key0, it.h * p.S + it.s);
           } else {
-            tma_load_3d(smem_u32(sm.k + c * (BM * 128)), &a.tm_k, bar[KV_FULL], c * 64, it.h, (int)(it.s0 + it.key0));
-            tma_load_3d(smem_u32(sm.v + c * (BM * 128)), &a.tm_v, bar[KV_FULL], c * 64, it.h, (int)(it.s0 + it.key0));
+            tma_load_3d(smem_u32(sm.k + c * (BM * 128)), &a.tm_k, bar[KV_FULL], c * 64, attn_kv_head(p, it.h),
+                        (int)(it.s0 + it.key0));
+            tma_load_3d(smem_u32(sm.v + c * (BM * 128)), &a.tm_v, bar[KV_FULL], c * 64, attn_kv_head(p, it.h),
+                        (int)(it.s0 + it.key0));
           }
         }
         kv_issued = gi + 1;
@@ -868,8 +870,10 @@ static bool make_args(BwdArgs& a, const DsaltAttnParams& p, int rows_q, int rows
   const uint64_t row = (uint64_t)D * 2, trow = (uint64_t)p.H * D * 2;
   if (encode_3d(&a.tm_q, dt, p.q, D, p.H, p.T, row, trow, 64, 1, rows_q) != CUDA_SUCCESS) return false;
   if (encode_3d(&a.tm_do, dt, p.dout, D, p.H, p.T, row, trow, 64, 1, rows_q) != CUDA_SUCCESS) return false;
-  if (encode_3d(&a.tm_k, dt, p.k, D, p.H, p.T, row, trow, 64, 1, rows_k) != CUDA_SUCCESS) return false;
-  if (encode_3d(&a.tm_v, dt, p.v, D, p.H, p.T, row, trow, 64, 1, rows_k) != CUDA_SUCCESS) return false;
+  // k, v: [T, H_kv, D] (grouped kv heads read in place; dk, dv stay per query head)
+  const uint64_t hkv = (uint64_t)attn_kv_heads(p), kvrow = hkv * D * 2;
+  if (encode_3d(&a.tm_k, dt, p.k, D, hkv, p.T, row, kvrow, 64, 1, rows_k) != CUDA_SUCCESS) return false;
+  if (encode_3d(&a.tm_v, dt, p.v, D, hkv, p.T, row, kvrow, 64, 1, rows_k) != CUDA_SUCCESS) return false;
   const int kp = p.kp > 0 ? p.kp : 16;
   a.lmk_box = kp < rows_l ? kp : rows_l;
   const void* lk = p.kp > 0 ? p.lmk_k : p.k;

@@ -216,8 +216,8 @@ __global__ void __launch_bounds__(kThreads, 1) tc_bwd_dq_kernel(const __grid_con
               tma_load_3d(smem_u32(sm.k[st] + c * (krows * 128)), &a.tm_lk, bar[FULL + st], c * 64, un.krow,
                           it.h * p.S + it.s);
             else
-              tma_load_3d(smem_u32(sm.k[st] + c * (KB * 128)), &a.tm_k, bar[FULL + st], c * 64, it.h,
-                          (int)(it.s0 + un.krow));
+              tma_load_3d(smem_u32(sm.k[st] + c * (KB * 128)), &a.tm_k, bar[FULL + st], c * 64,
+                          attn_kv_head(p, it.h), (int)(it.s0 + un.krow));
           }
           ++g;
           g_issued = g;
@@ -401,7 +401,8 @@ cudaError_t launch_dq2(const DsaltAttnParams& p, cudaStream_t st) {
   const CUtensorMapDataType dt = std::is_same<T, __half>::value ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16
                                                                  : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
   const uint64_t row = (uint64_t)D * 2, trow = (uint64_t)p.H * D * 2;
-  if (encode_tensor_map_3d(&a.tm_k, dt, p.k, D, p.H, p.T, row, trow, 64, 1, dq2::KB) != CUDA_SUCCESS)
+  const uint64_t hkv = (uint64_t)attn_kv_heads(p);  // k: [T, H_kv, D]
+  if (encode_tensor_map_3d(&a.tm_k, dt, p.k, D, hkv, p.T, row, hkv * D * 2, 64, 1, dq2::KB) != CUDA_SUCCESS)
     return cudaErrorInvalidValue;
   const int kp = p.kp > 0 ? p.kp : 16;
   a.lmk_box = kp < 128 ? kp : 128;

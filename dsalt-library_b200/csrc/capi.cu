@@ -43,6 +43,7 @@ cudaError_t launch_xent(const DsaltXentParams& p, cudaStream_t st);
 cudaError_t launch_swiglu(const DsaltSwigluParams& p, bool bwd, cudaStream_t st);
 cudaError_t launch_win_gate_bwd(const DsaltWinGateBwdParams& p, cudaStream_t st);
 cudaError_t launch_hybrid_scores_bwd(const DsaltScoreBwdParams& p, cudaStream_t st);
+cudaError_t launch_gqa_reduce(const DsaltGqaReduceParams& p, cudaStream_t st);
 cudaError_t launch_wait_timeout_probe(int32_t* status, cudaStream_t st);
 cudaError_t launch_hybrid_scores(const DsaltScoreParams& p, cudaStream_t st);
 cudaError_t launch_topk(const DsaltTopkParams& p, cudaStream_t st);
@@ -70,6 +71,8 @@ static int check_attn(const DsaltAttnParams* p, int stage) {
   if (p->dtype != DSALT_F16 && p->dtype != DSALT_BF16 && p->dtype != DSALT_F32) return DSALT_ERR_DTYPE;
   if (p->D <= 0 || p->D > 256 || p->D % 8 != 0) return DSALT_ERR_HEAD_DIM;
   if (p->T < 0 || p->H <= 0 || p->S < 0 || p->k_lmk < 0 || p->kp < p->k_lmk) return DSALT_ERR_ARG;
+  // grouped kv heads: H a multiple of H_kv (0 = H)
+  if (p->H_kv < 0 || p->H_kv > p->H || (p->H_kv > 0 && p->H % p->H_kv != 0)) return DSALT_ERR_ARG;
   if (p->semantics != DSALT_TRAIN && p->semantics != DSALT_INFER) return DSALT_ERR_ARG;
   if (!(p->tau_win > 0.f)) return DSALT_ERR_ARG;
   if (p->impl < DSALT_IMPL_AUTO || p->impl > DSALT_IMPL_TCGEN05) return DSALT_ERR_ARG;
@@ -141,6 +144,7 @@ int dsalt_b200_params_sizeof(int which) {
     case 10: return (int)sizeof(DsaltSwigluParams);
     case 11: return (int)sizeof(DsaltWinGateBwdParams);
     case 12: return (int)sizeof(DsaltScoreBwdParams);
+    case 13: return (int)sizeof(DsaltGqaReduceParams);
   }
   return -1;
 }
@@ -156,6 +160,7 @@ int dsalt_build_schedule(const DsaltScheduleParams* p, void* stream) {
 int dsalt_gather_landmarks(const DsaltGatherParams* p, void* stream) {
   if (!p || p->H <= 0 || p->S < 0 || p->k_lmk < 0 || p->kp < p->k_lmk || p->k_lmk > 1024 || p->kp > 2048)
     return DSALT_ERR_ARG;
+  if (p->H_kv < 0 || p->H_kv > p->H || (p->H_kv > 0 && p->H % p->H_kv != 0)) return DSALT_ERR_ARG;
   if (p->dtype != DSALT_F16 && p->dtype != DSALT_BF16 && p->dtype != DSALT_F32) return DSALT_ERR_DTYPE;
   if ((p->D * (p->dtype == DSALT_F32 ? 4 : 2)) % 16 != 0) return DSALT_ERR_HEAD_DIM;
   if (p->kp == 0 || p->S == 0) return DSALT_OK;
@@ -220,6 +225,7 @@ int dsalt_win_gate(const DsaltWinGateParams* p, void* stream) {
 
 static int check_rope(const DsaltRopeParams* p, bool bwd) {
   if (!p || p->T < 0 || p->H <= 0 || p->Hkv <= 0 || p->H % p->Hkv != 0) return DSALT_ERR_ARG;
+  if (p->kv_out_heads != 0 && p->kv_out_heads != p->H && p->kv_out_heads != p->Hkv) return DSALT_ERR_ARG;
   if (p->dtype != DSALT_F16 && p->dtype != DSALT_BF16 && p->dtype != DSALT_F32) return DSALT_ERR_DTYPE;
   if (p->D <= 0 || p->D > 256 || p->D % 16 != 0) return DSALT_ERR_HEAD_DIM;
   if (p->ld != 0 && (p->ld < (int64_t)p->H * p->D || p->ld % (p->dtype == DSALT_F32 ? 4 : 8) != 0))
@@ -358,6 +364,16 @@ int dsalt_swiglu_bwd(const DsaltSwigluParams* p, void* stream) {
   const int st = check_swiglu(p, true);
   if (st != DSALT_OK || p->T == 0) return st;
   return status_of(launch_swiglu(*p, true, (cudaStream_t)stream));
+}
+
+int dsalt_gqa_reduce(const DsaltGqaReduceParams* p, void* stream) {
+  if (!p || p->T < 0 || p->H <= 0 || p->H_kv <= 0 || p->H_kv > p->H || p->H % p->H_kv != 0) return DSALT_ERR_ARG;
+  if (p->dtype != DSALT_F16 && p->dtype != DSALT_BF16 && p->dtype != DSALT_F32) return DSALT_ERR_DTYPE;
+  if (p->D <= 0 || (p->D * (p->dtype == DSALT_F32 ? 4 : 2)) % 16 != 0) return DSALT_ERR_HEAD_DIM;
+  if (p->T == 0) return DSALT_OK;
+  if (!p->x || !p->y) return DSALT_ERR_ARG;
+  if (!aligned16(p->x) || !aligned16(p->y)) return DSALT_ERR_ALIGN;
+  return status_of(launch_gqa_reduce(*p, (cudaStream_t)stream));
 }
 
 }  // extern "C"

@@ -133,6 +133,13 @@ __device__ __forceinline__ float edge_dbias(const RowWindow& r, float d, float i
   return (1.0f - sig) * inv_tau;
 }
 
+// Grouped kv heads: the kv heads of k and v (0 in the params means H) and the kv
+// head that query head h reads.
+__host__ __device__ __forceinline__ int attn_kv_heads(const DsaltAttnParams& p) { return p.H_kv > 0 ? p.H_kv : p.H; }
+__host__ __device__ __forceinline__ int attn_kv_head(const DsaltAttnParams& p, int h) {
+  return h / (p.H / attn_kv_heads(p));
+}
+
 // ------------------------------------------------------ backward query records
 // One record per (head, query token) of the backward, written by the preprocess
 // stage next to Delta and read by the tensor-core dK/dV and dQ stages, so that

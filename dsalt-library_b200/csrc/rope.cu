@@ -116,16 +116,20 @@ __global__ void __launch_bounds__(kThreads, 4) rope_gqa_fwd_kernel(const DsaltRo
   T* qo = reinterpret_cast<T*>(p.q_out) + (int64_t)row * p.D + j0;
   store8<T>(qo, a);
   store8<T>(qo + half, b);
+  // k_out expanded to the query heads, or (kv_out_heads = Hkv) once per kv head
+  const bool expand = p.kv_out_heads <= 0 || p.kv_out_heads == p.H;
+  if (!expand && h % (uint32_t)n_rep != 0) return;
+  const int64_t orow = expand ? (int64_t)row : (int64_t)t * p.Hkv + h / (uint32_t)n_rep;
   const T* k = reinterpret_cast<const T*>(p.k) + kofs;
   load8<T>(k, a);
   load8<T>(k + half, b);
   rope8<T>(a, b, c1, c2, s1, s2);
-  T* ko = reinterpret_cast<T*>(p.k_out) + (int64_t)row * p.D + j0;
+  T* ko = reinterpret_cast<T*>(p.k_out) + orow * p.D + j0;
   store8<T>(ko, a);
   store8<T>(ko + half, b);
   if (p.v_out) {
     const T* v = reinterpret_cast<const T*>(p.v) + kofs;
-    T* vo = reinterpret_cast<T*>(p.v_out) + (int64_t)row * p.D + j0;
+    T* vo = reinterpret_cast<T*>(p.v_out) + orow * p.D + j0;
     load8<T>(v, a);
     load8<T>(v + half, b);
     store8<T>(vo, a);
@@ -162,12 +166,16 @@ __global__ void __launch_bounds__(kThreads, 4) rope_gqa_bwd_kernel(const DsaltRo
   const uint32_t krow = idx >> lg;  // t·Hkv + hk
   const uint32_t t = krow / (uint32_t)p.Hkv;
   const uint32_t hk = krow - t * (uint32_t)p.Hkv;
-  const int64_t row0 = (int64_t)t * p.H + (int64_t)hk * n_rep;  // first query head of the kv head
+  // the copies of this kv head in dk_out: n_rep query-head rows (expanded), or
+  // its own row (kv_out_heads = Hkv)
+  const bool expand = p.kv_out_heads <= 0 || p.kv_out_heads == p.H;
+  const int copies = expand ? n_rep : 1;
+  const int64_t row0 = expand ? (int64_t)t * p.H + (int64_t)hk * n_rep : (int64_t)t * p.Hkv + hk;
   // the sum over the copies (fp32, rounded once), then the transposed rotation
   float x[8];
 #pragma unroll
   for (int i = 0; i < 8; ++i) { g1[i] = 0.f; g2[i] = 0.f; }
-  for (int r = 0; r < n_rep; ++r) {
+  for (int r = 0; r < copies; ++r) {
     const T* g = reinterpret_cast<const T*>(p.dk_out) + (row0 + r) * p.D + j0;
     load8<T>(g, x);
 #pragma unroll
@@ -187,7 +195,7 @@ __global__ void __launch_bounds__(kThreads, 4) rope_gqa_bwd_kernel(const DsaltRo
   if (p.dv_out && p.dv) {
 #pragma unroll
     for (int i = 0; i < 8; ++i) { g1[i] = 0.f; g2[i] = 0.f; }
-    for (int r = 0; r < n_rep; ++r) {
+    for (int r = 0; r < copies; ++r) {
       const T* g = reinterpret_cast<const T*>(p.dv_out) + (row0 + r) * p.D + j0;
       load8<T>(g, x);
 #pragma unroll

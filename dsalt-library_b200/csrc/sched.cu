@@ -160,7 +160,10 @@ __global__ void __launch_bounds__(256) gather_landmarks_kernel(DsaltGatherParams
   const int nvec = p.D / vec;
   const int per = (p.kp + gridDim.y - 1) / gridDim.y;
   const int r0 = blockIdx.y * per, r1 = min(p.kp, r0 + per);
-  const int64_t HD = (int64_t)p.H * p.D;
+  // k, v: [T, H_kv, D]; query head h reads kv head h / (H / H_kv)
+  const int hkv = p.H_kv > 0 ? p.H_kv : p.H;
+  const int64_t HD = (int64_t)hkv * p.D;
+  const int g = h / (p.H / hkv);
   const uint4* ksrc = reinterpret_cast<const uint4*>(p.k);
   const uint4* vsrc = reinterpret_cast<const uint4*>(p.v);
   uint4* kdst = reinterpret_cast<uint4*>(p.lmk_k);
@@ -170,7 +173,7 @@ __global__ void __launch_bounds__(256) gather_landmarks_kernel(DsaltGatherParams
     const int pos = spos[r];
     uint4 kv = make_uint4(0, 0, 0, 0), vv = make_uint4(0, 0, 0, 0);
     if (pos >= 0) {
-      const int64_t src = ((s0 + pos) * HD + (int64_t)h * p.D) / vec + c;
+      const int64_t src = ((s0 + pos) * HD + (int64_t)g * p.D) / vec + c;
       kv = ksrc[src];
       vv = vsrc[src];
     }

@@ -21,7 +21,7 @@ F16, BF16, F32 = 0, 1, 2
 TRAIN, INFER = 0, 1
 IMPL_AUTO, IMPL_SIMT, IMPL_TCGEN05 = 0, 1, 2
 DEV_WAIT_TIMEOUT, DEV_BAD_INDEX = 1, 2
-ABI_VERSION = 6
+ABI_VERSION = 7
 QREC_FLOATS = 16  # DSALT_QREC_FLOATS
 LMK_SPLIT = 4  # DSALT_LMK_SPLIT
 DS_TILE_BYTES = 16384  # DSALT_DS_TILE_BYTES
@@ -50,7 +50,7 @@ class GatherParams(ctypes.Structure):
                 ("pos_sorted", _c_void_p), ("w_sorted", _c_void_p), ("perm", _c_void_p),
                 ("lmk_slot", _c_void_p), ("status", _c_void_p),
                 ("T", _i64), ("H", _i32), ("D", _i32), ("S", _i32), ("k_lmk", _i32), ("kp", _i32),
-                ("dtype", _i32)]
+                ("dtype", _i32), ("H_kv", _i32)]
 
 
 class AttnParams(ctypes.Structure):
@@ -66,7 +66,7 @@ class AttnParams(ctypes.Structure):
                 ("T", _i64), ("H", _i32), ("D", _i32), ("S", _i32), ("k_lmk", _i32), ("kp", _i32),
                 ("max_blocks", _i32), ("ds_band_tiles", _i32), ("ds_lmk_tiles", _i32),
                 ("scale", _f32), ("tau_win", _f32), ("win_edge", _f32),
-                ("semantics", _i32), ("dtype", _i32), ("impl", _i32)]
+                ("semantics", _i32), ("dtype", _i32), ("impl", _i32), ("H_kv", _i32)]
 
 
 class ScoreParams(ctypes.Structure):
@@ -93,7 +93,8 @@ class RopeParams(ctypes.Structure):
                 ("q_out", _c_void_p), ("k_out", _c_void_p), ("v_out", _c_void_p),
                 ("dq_out", _c_void_p), ("dk_out", _c_void_p), ("dv_out", _c_void_p),
                 ("dq", _c_void_p), ("dk", _c_void_p), ("dv", _c_void_p),
-                ("T", _i64), ("ld", _i64), ("H", _i32), ("Hkv", _i32), ("D", _i32), ("dtype", _i32)]
+                ("T", _i64), ("ld", _i64), ("H", _i32), ("Hkv", _i32), ("D", _i32), ("dtype", _i32),
+                ("kv_out_heads", _i32)]
 
 
 class RmsNormParams(ctypes.Structure):
@@ -133,8 +134,14 @@ RMSNORM_ROWS_PER_PART = 64  # DSALT_RMSNORM_ROWS_PER_PART
 WIN_GATE_ROWS_PER_PART = 32  # DSALT_WIN_GATE_ROWS_PER_PART
 SCORE_BWD_TOKENS = 128  # DSALT_SCORE_BWD_TOKENS
 
+class GqaReduceParams(ctypes.Structure):
+    _fields_ = [("x", _c_void_p), ("y", _c_void_p), ("T", _i64), ("H", _i32), ("H_kv", _i32), ("D", _i32),
+                ("dtype", _i32)]
+
+
 _STRUCTS = [ScheduleParams, GatherParams, AttnParams, ScoreParams, TopkParams, WinGateParams, RopeParams,
-            RmsNormParams, ScaleRowsParams, XentParams, SwigluParams, WinGateBwdParams, ScoreBwdParams]
+            RmsNormParams, ScaleRowsParams, XentParams, SwigluParams, WinGateBwdParams, ScoreBwdParams,
+            GqaReduceParams]
 _ENTRY = {
     "dsalt_build_schedule": ScheduleParams,
     "dsalt_gather_landmarks": GatherParams,
@@ -156,6 +163,7 @@ _ENTRY = {
     "dsalt_hybrid_scores_bwd": ScoreBwdParams,
     "dsalt_swiglu_fwd": SwigluParams,
     "dsalt_swiglu_bwd": SwigluParams,
+    "dsalt_gqa_reduce": GqaReduceParams,
 }
 
 _lib = None

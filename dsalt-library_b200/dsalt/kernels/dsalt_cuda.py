@@ -79,6 +79,7 @@ class Prepared:
     lmk_slot: torch.Tensor
     max_blocks: int
     lmax: int = 0                # longest sequence (host)
+    H_kv: int = 0                # kv heads of k, v (grouped kv heads when < H)
     wmax_slot: int = -1          # slot of the widest band in the pinned ring (-1: none)
     wmax_gen: int = 0
 
@@ -140,13 +141,17 @@ def prepare(k_c: torch.Tensor, v_c: torch.Tensor, lmk_pos: torch.Tensor, lmk_w: 
     """Build the schedule and the sorted landmark buffers on the device.
 
     ``cu_host``: the host copy of ``cu_seqlens`` when the caller has one;
-    ``for_backward``: record the widest band for the backward's scratch."""
-    T, H, D = k_c.shape
+    ``for_backward``: record the widest band for the backward's scratch.
+    ``k_c``, ``v_c`` are ``[T, H_kv, D]``; the query heads ``H`` are those of
+    ``lmk_pos`` (``[H, S, k]``, a multiple of ``H_kv``)."""
+    T, H_kv, D = k_c.shape
     dev = k_c.device
     cu = cu_seqlens.to(device=dev, dtype=torch.int32).contiguous()
     S = cu.shape[0] - 1
-    if lmk_pos.dim() != 3 or lmk_pos.shape[0] != H or lmk_pos.shape[1] != S:
-        raise ValueError(f"lmk_pos must be [H={H}, S={S}, k], got {tuple(lmk_pos.shape)}")
+    H = int(lmk_pos.shape[0]) if lmk_pos.dim() == 3 else H_kv
+    if lmk_pos.dim() != 3 or lmk_pos.shape[1] != S or H % H_kv != 0:
+        raise ValueError(f"lmk_pos must be [H, S={S}, k] with H a multiple of H_kv={H_kv}, "
+                         f"got {tuple(lmk_pos.shape)}")
     k_lmk = int(lmk_pos.shape[2])
     kp = padded_landmarks(k_lmk)
     w32 = w.detach().to(device=dev, dtype=torch.float32).contiguous()
@@ -177,7 +182,7 @@ def prepare(k_c: torch.Tensor, v_c: torch.Tensor, lmk_pos: torch.Tensor, lmk_w: 
             cu_seqlens=_ext.ptr(cu), lmk_k=_ext.ptr(lmk_k), lmk_v=_ext.ptr(lmk_v),
             pos_sorted=_ext.ptr(pos_sorted), w_sorted=_ext.ptr(w_sorted), perm=_ext.ptr(perm),
             lmk_slot=_ext.ptr(lmk_slot), status=_ext.ptr(device_status(dev)),
-            T=T, H=H, D=D, S=S, k_lmk=k_lmk, kp=kp, dtype=_ext.dtype_code(dt))
+            T=T, H=H, D=D, S=S, k_lmk=k_lmk, kp=kp, dtype=_ext.dtype_code(dt), H_kv=H_kv)
         _ext.call("dsalt_gather_landmarks", gp)
     else:
         lmk_slot.fill_(-1)
@@ -185,7 +190,7 @@ def prepare(k_c: torch.Tensor, v_c: torch.Tensor, lmk_pos: torch.Tensor, lmk_w: 
         cu_host = [int(c) for c in cu.to("cpu").tolist()]
     lmax = max((b - a for a, b in zip(cu_host[:-1], cu_host[1:])), default=0)
     prep = Prepared(T, H, D, S, k_lmk, kp, semantics, cu, w32, block_map, num_blocks, seq_wmax,
-                    lmk_k, lmk_v, pos_sorted, w_sorted, perm, lmk_slot, max_blocks, lmax)
+                    lmk_k, lmk_v, pos_sorted, w_sorted, perm, lmk_slot, max_blocks, lmax, H_kv)
     if for_backward and T > 0:
         _record_wmax(prep, dev)
     return prep
@@ -204,7 +209,7 @@ def _params(prep: Prepared, q_c, k_c, v_c, tau_win: float, win_edge: float, impl
         max_blocks=prep.max_blocks, scale=1.0 / math.sqrt(prep.D) if scale is None else float(scale),
         tau_win=float(tau_win),
         win_edge=float(win_edge) if prep.semantics == _ext.TRAIN else 0.0,
-        semantics=prep.semantics, dtype=_ext.dtype_code(q_c.dtype), impl=impl)
+        semantics=prep.semantics, dtype=_ext.dtype_code(q_c.dtype), impl=impl, H_kv=prep.H_kv)
     for name, t in bufs.items():
         setattr(p, name, _ext.ptr(t))
     return p
@@ -248,8 +253,11 @@ def backward(grad_out, q_c, k_c, v_c, o, lse, prep: Prepared, tau_win: float, wi
     T, H = prep.T, prep.H
     delta = torch.empty(T, H, dtype=torch.float32, device=dev)
     dq = torch.empty_like(q_c)
-    dk = torch.empty_like(k_c)
-    dv = torch.empty_like(v_c)
+    # grouped kv heads: the stages write dk, dv per query head (the gradients of
+    # the expanded K/V), summed per group at the end
+    grouped = prep.H_kv != H
+    dk = torch.empty_like(q_c) if grouped else torch.empty_like(k_c)
+    dv = torch.empty_like(q_c) if grouped else torch.empty_like(v_c)
     d_lw = torch.zeros(H, prep.S, prep.k_lmk, dtype=torch.float32, device=dev)
     dw_head = torch.empty(T, H, dtype=torch.float32, device=dev) if want_dw else None
     dw = torch.empty(T, dtype=q_c.dtype, device=dev) if want_dw else None
@@ -274,7 +282,20 @@ def backward(grad_out, q_c, k_c, v_c, o, lse, prep: Prepared, tau_win: float, wi
     # dQ multiplies the dSᵀ tiles that dK/dV stores: one after the other
     _ext.call("dsalt_attn_bwd_dkdv", p)
     _ext.call("dsalt_attn_bwd_dq", p)
+    if grouped:
+        dk, dv = gqa_reduce(dk, prep.H_kv), gqa_reduce(dv, prep.H_kv)
     return dq, dk, dv, d_lw, dw
+
+
+def gqa_reduce(x: torch.Tensor, h_kv: int) -> torch.Tensor:
+    """``[T, H, D]`` per-query-head gradient -> ``[T, H_kv, D]``: each group of
+    ``H / H_kv`` heads summed in fp32 and rounded once (``dsalt_gqa_reduce``)."""
+    T, H, D = x.shape
+    y = torch.empty(T, h_kv, D, dtype=x.dtype, device=x.device)
+    p = _ext.GqaReduceParams(x=_ext.ptr(x), y=_ext.ptr(y), T=T, H=H, H_kv=h_kv, D=D,
+                             dtype=_ext.dtype_code(x.dtype))
+    _ext.call("dsalt_gqa_reduce", p)
+    return y
 
 
 # The dSᵀ tile scratch, kept per (device, stream) and only ever grown: its size
@@ -311,8 +332,11 @@ def check_inputs(q, k, v, cu_seqlens):
         _ext.require_cuda(t, name)
         if t.dim() != 3:
             raise ValueError(f"{name} must be [T, H, D], got {tuple(t.shape)}")
-    if k.shape != q.shape or v.shape != q.shape:
-        raise ValueError(f"q/k/v shapes differ: {tuple(q.shape)} {tuple(k.shape)} {tuple(v.shape)}")
+    # k, v may carry fewer (grouped) heads: H a multiple of H_kv, read in place
+    if (k.shape != v.shape or k.shape[0] != q.shape[0] or k.shape[2] != q.shape[2]
+            or k.shape[1] <= 0 or q.shape[1] % k.shape[1] != 0):
+        raise ValueError(f"q/k/v shapes differ: {tuple(q.shape)} {tuple(k.shape)} {tuple(v.shape)} "
+                         "(k and v: [T, H_kv, D] with H a multiple of H_kv)")
     if q.shape[2] % 8 != 0 or not 8 <= q.shape[2] <= 256:
         raise ValueError(f"head_dim {q.shape[2]} not supported (multiples of 8 up to 256)")
     if cu_seqlens.dim() != 1 or cu_seqlens.shape[0] < 1:

@@ -35,12 +35,16 @@ def shard_heads(t: torch.Tensor, h0: int, h1: int, dim: int) -> torch.Tensor:
 
 
 def shard_op_inputs(q, k, v, lmk_pos, lmk_logw, rank: int, world: int, extra: dict | None = None) -> dict:
-    """This rank's slice of the training op's inputs: ``q, k, v [T, H, D]`` and any
-    other ``[T, H, ...]`` tensors in ``extra`` along dim 1, ``lmk_pos, lmk_logw [H, S, k]``
-    along dim 0.  Per-token inputs (``w̃``, ``cu_seqlens``) are shared by all heads and
-    stay whole."""
-    h0, h1 = head_range(q.shape[1], world, rank)
-    out = {"q": shard_heads(q, h0, h1, 1), "k": shard_heads(k, h0, h1, 1), "v": shard_heads(v, h0, h1, 1),
+    """This rank's slice of the training op's inputs: ``q [T, H, D]`` and any other
+    ``[T, H, ...]`` tensors in ``extra`` along dim 1, ``lmk_pos, lmk_logw [H, S, k]``
+    along dim 0, and ``k, v [T, H_kv, D]``.  With grouped kv heads (``H_kv < H``)
+    whole groups stay together: the kv heads are split over the ranks and each rank
+    takes the query heads of its kv heads.  Per-token inputs (``w̃``, ``cu_seqlens``)
+    are shared by all heads and stay whole."""
+    n_rep = q.shape[1] // k.shape[1]
+    g0, g1 = head_range(k.shape[1], world, rank)
+    h0, h1 = g0 * n_rep, g1 * n_rep
+    out = {"q": shard_heads(q, h0, h1, 1), "k": shard_heads(k, g0, g1, 1), "v": shard_heads(v, g0, g1, 1),
            "lmk_pos": shard_heads(lmk_pos, h0, h1, 0), "lmk_logw": shard_heads(lmk_logw, h0, h1, 0),
            "heads": (h0, h1)}
     for name, t in (extra or {}).items():
@@ -48,8 +52,9 @@ def shard_op_inputs(q, k, v, lmk_pos, lmk_logw, rank: int, world: int, extra: di
     return out
 
 
-def gather_heads(shard: torch.Tensor, n_heads: int, group=None) -> torch.Tensor:
-    """All-gather ``[T, H_r, ...]`` shards along dim 1 into ``[T, n_heads, ...]`` on every rank.
+def gather_heads(shard: torch.Tensor, n_heads: int, group=None, n_rep: int = 1) -> torch.Tensor:
+    """All-gather ``[T, H_r, ...]`` shards along dim 1 into ``[T, n_heads, ...]`` on every rank
+    (``n_rep`` query heads per kv head: the split of ``shard_op_inputs``).
 
     One collective: each rank's shard is padded to the largest shard's head count,
     gathered rank-major with ``all_gather_into_tensor`` and reordered to head order."""
@@ -58,7 +63,7 @@ def gather_heads(shard: torch.Tensor, n_heads: int, group=None) -> torch.Tensor:
     rank = dist.get_rank(group)
     if world == 1:
         return shard
-    sizes = [head_range(n_heads, world, r) for r in range(world)]
+    sizes = [(g0 * n_rep, g1 * n_rep) for g0, g1 in (head_range(n_heads // n_rep, world, r) for r in range(world))]
     hmax = max(h1 - h0 for h0, h1 in sizes)
     T, rest = shard.shape[0], tuple(shard.shape[2:])
     h0, h1 = sizes[rank]

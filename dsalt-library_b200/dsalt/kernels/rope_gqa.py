@@ -1,4 +1,8 @@
-"""Fused attention prologue: RoPE on q and k plus the GQA expansion of k and v.
+"""Fused attention prologue: RoPE on q and k plus (optionally) the GQA expansion of k and v.
+
+With ``expand=False`` k and v keep their ``H_kv`` heads: the attention op reads
+the kv head of each query head in place (``DsaltAttnParams.H_kv``), so the
+expansion is never written.
 
 One CUDA pass (``dsalt_rope_gqa_fwd`` / ``dsalt_rope_gqa_bwd`` in ``csrc/rope.cu``)
 replaces, on the packed path of ``DSALTAttention``, the reference's
@@ -27,10 +31,11 @@ def _params(rows, kv_rows, cos, sin, **bufs) -> _ext.RopeParams:
 
 
 class RopeGqaFunction(torch.autograd.Function):
-    """``(q [T,H,D], k [T,Hkv,D], v [T,Hkv,D], cos [T,D], sin [T,D]) -> (q_rot, k_rot [T,H,D], v [T,H,D])``."""
+    """``(q [T,H,D], k [T,Hkv,D], v [T,Hkv,D], cos [T,D], sin [T,D]) -> (q_rot, k_rot [T,H,D], v [T,H,D])``,
+    or with ``expand=False`` ``(q_rot, k_rot [T,Hkv,D], v)``."""
 
     @staticmethod
-    def forward(ctx, q, k, v, cos, sin):
+    def forward(ctx, q, k, v, cos, sin, expand_kv: bool = True):
         for name, t in (("q", q), ("k", k), ("v", v), ("cos", cos), ("sin", sin)):
             _ext.require_cuda(t, name)
         if not (q.dtype == k.dtype == v.dtype == cos.dtype == sin.dtype):
@@ -43,10 +48,11 @@ class RopeGqaFunction(torch.autograd.Function):
             raise ValueError("H must be a multiple of the number of kv heads")
         q, k, v, cos, sin = (t.contiguous() for t in (q, k, v, cos, sin))
         q_out = torch.empty_like(q)
-        k_out = torch.empty(T, H, D, dtype=k.dtype, device=k.device)
-        expand = H != Hkv
+        expand = H != Hkv and expand_kv
+        k_out = torch.empty(T, H if expand else Hkv, D, dtype=k.dtype, device=k.device)
         v_out = torch.empty(T, H, D, dtype=v.dtype, device=v.device) if expand else None
         p = _params(q, k, cos, sin, q=q, k=k, v=v if expand else None, q_out=q_out, k_out=k_out, v_out=v_out)
+        p.kv_out_heads = H if expand else Hkv
         _ext.call("dsalt_rope_gqa_fwd", p)
         ctx.save_for_backward(cos, sin)
         ctx.hkv = Hkv
@@ -61,8 +67,9 @@ class RopeGqaFunction(torch.autograd.Function):
         ref = dq_out if dq_out is not None else dk_out
         H = ref.shape[1]
         dev, dt = cos.device, cos.dtype
+        hk_out = H if ctx.expand else ctx.hkv
         dq_out = torch.zeros(T, H, D, dtype=dt, device=dev) if dq_out is None else dq_out.contiguous()
-        dk_out = torch.zeros(T, H, D, dtype=dt, device=dev) if dk_out is None else dk_out.contiguous()
+        dk_out = torch.zeros(T, hk_out, D, dtype=dt, device=dev) if dk_out is None else dk_out.contiguous()
         dq = torch.empty(T, H, D, dtype=dt, device=dev)
         dk = torch.empty(T, ctx.hkv, D, dtype=dt, device=dev)
         dv = None
@@ -73,13 +80,16 @@ class RopeGqaFunction(torch.autograd.Function):
         else:
             dv = dv_out
             p = _params(dq_out, dk, cos, sin, dq_out=dq_out, dk_out=dk_out, dq=dq, dk=dk)
+        p.kv_out_heads = hk_out
         _ext.call("dsalt_rope_gqa_bwd", p)
-        return dq, dk, dv, None, None
+        return dq, dk, dv, None, None, None
 
 
-def rope_gqa(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor):
-    """RoPE on q and k and the expansion of k and v to q's heads, fused (see the module docstring)."""
-    return RopeGqaFunction.apply(q, k, v, cos, sin)
+def rope_gqa(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor,
+             expand: bool = True):
+    """RoPE on q and k and (``expand``) the expansion of k and v to q's heads, fused
+    (see the module docstring)."""
+    return RopeGqaFunction.apply(q, k, v, cos, sin, expand)
 
 
 class QkvRopeFunction(torch.autograd.Function):
@@ -97,7 +107,8 @@ class QkvRopeFunction(torch.autograd.Function):
     """
 
     @staticmethod
-    def forward(ctx, x, w_q, w_k, w_v, cos, sin, H: int, Hkv: int, D: int, dtype: torch.dtype):
+    def forward(ctx, x, w_q, w_k, w_v, cos, sin, H: int, Hkv: int, D: int, dtype: torch.dtype,
+                expand_kv: bool = True):
         _ext.require_cuda(x, "x")
         T, d = x.shape
         nq, nk = H * D, Hkv * D
@@ -110,38 +121,40 @@ class QkvRopeFunction(torch.autograd.Function):
         w[nq + nk:].copy_(w_v.detach())
         qkv = torch.mm(x2, w.t())
         cos, sin = cos.to(dtype).contiguous(), sin.to(dtype).contiguous()
+        expand = expand_kv and H != Hkv
+        hk = H if expand else Hkv  # heads of k_out and v_out
         q_out = torch.empty(T, H, D, dtype=dtype, device=dev)
-        k_out = torch.empty(T, H, D, dtype=dtype, device=dev)
-        v_out = torch.empty(T, H, D, dtype=dtype, device=dev)
+        k_out = torch.empty(T, hk, D, dtype=dtype, device=dev)
+        v_out = torch.empty(T, hk, D, dtype=dtype, device=dev)
         p = _ext.RopeParams(q=_ext.ptr(qkv), k=_ext.ptr(qkv[:, nq:]), v=_ext.ptr(qkv[:, nq + nk:]), cos=_ext.ptr(cos),
                             sin=_ext.ptr(sin), q_out=_ext.ptr(q_out), k_out=_ext.ptr(k_out), v_out=_ext.ptr(v_out),
-                            T=T, ld=W, H=H, Hkv=Hkv, D=D, dtype=_ext.dtype_code(dtype))
+                            T=T, ld=W, H=H, Hkv=Hkv, D=D, dtype=_ext.dtype_code(dtype), kv_out_heads=hk)
         if T > 0:
             _ext.call("dsalt_rope_gqa_fwd", p)
         ctx.save_for_backward(x2, w, cos, sin)
-        ctx.dims = (H, Hkv, D)
+        ctx.dims = (H, Hkv, D, hk)
         ctx.dtypes = (x.dtype, w_q.dtype, w_k.dtype, w_v.dtype)
-        if H == Hkv:
+        if not expand:
             return q_out, k_out, v_out
         return q_out, k_out, v_out, qkv[:, nq + nk:].contiguous()
 
     @staticmethod
     def backward(ctx, dq_out, dk_out, dv_out, *d_xwv):
         x2, w, cos, sin = ctx.saved_tensors
-        H, Hkv, D = ctx.dims
+        H, Hkv, D, hk = ctx.dims
         T, d = x2.shape
         nq, nk = H * D, Hkv * D
         W = nq + 2 * nk
         dt, dev = x2.dtype, x2.device
 
-        def dense(g):
-            return torch.zeros(T, H, D, dtype=dt, device=dev) if g is None else g.contiguous().to(dt)
-        dq_out, dk_out, dv_out = dense(dq_out), dense(dk_out), dense(dv_out)
+        def dense(g, heads):
+            return torch.zeros(T, heads, D, dtype=dt, device=dev) if g is None else g.contiguous().to(dt)
+        dq_out, dk_out, dv_out = dense(dq_out, H), dense(dk_out, hk), dense(dv_out, hk)
         dqkv = torch.empty(T, W, dtype=dt, device=dev)
         p = _ext.RopeParams(cos=_ext.ptr(cos), sin=_ext.ptr(sin), dq_out=_ext.ptr(dq_out), dk_out=_ext.ptr(dk_out),
                             dv_out=_ext.ptr(dv_out), dq=_ext.ptr(dqkv), dk=_ext.ptr(dqkv[:, nq:]),
                             dv=_ext.ptr(dqkv[:, nq + nk:]), T=T, ld=W, H=H, Hkv=Hkv, D=D,
-                            dtype=_ext.dtype_code(dt))
+                            dtype=_ext.dtype_code(dt), kv_out_heads=hk)
         if T > 0:
             _ext.call("dsalt_rope_gqa_bwd", p)
         if d_xwv and d_xwv[0] is not None:
@@ -152,15 +165,16 @@ class QkvRopeFunction(torch.autograd.Function):
         if any(ctx.needs_input_grad[1:4]):
             dw = torch.mm(dqkv.t(), x2, out_dtype=torch.float32)
             dw_q, dw_k, dw_v = dw[:nq].to(wq_dt), dw[nq:nq + nk].to(wk_dt), dw[nq + nk:].to(wv_dt)
-        return dx, dw_q, dw_k, dw_v, None, None, None, None, None, None
+        return dx, dw_q, dw_k, dw_v, None, None, None, None, None, None, None
 
 
-def qkv_rope(x, w_q, w_k, w_v, cos, sin, H: int, Hkv: int, D: int, dtype: torch.dtype):
+def qkv_rope(x, w_q, w_k, w_v, cos, sin, H: int, Hkv: int, D: int, dtype: torch.dtype, expand: bool = True):
     """``(q_rot, k_rot, v, xwv)``: the bias-free q/k/v projections of ``x`` [T, d] in
-    ``dtype`` with RoPE and the GQA expansion fused (see ``QkvRopeFunction``);
-    ``xwv`` [T, Hkv·D] is the unexpanded value projection (a view of ``v`` without GQA)."""
-    out = QkvRopeFunction.apply(x, w_q, w_k, w_v, cos, sin, H, Hkv, D, dtype)
-    if H == Hkv:
+    ``dtype`` with RoPE and (``expand``) the GQA expansion fused (see
+    ``QkvRopeFunction``); ``xwv`` [T, Hkv·D] is the unexpanded value projection (a
+    view of ``v`` when v is not expanded)."""
+    out = QkvRopeFunction.apply(x, w_q, w_k, w_v, cos, sin, H, Hkv, D, dtype, expand)
+    if H == Hkv or not expand:
         q, k, v = out
         return q, k, v, v.view(x.shape[0], Hkv * D)
     return out

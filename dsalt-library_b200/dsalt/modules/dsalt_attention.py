@@ -182,21 +182,23 @@ class DSALTAttention(nn.Module):
         return out.view(B, T, self.d_model), aux
 
     def _project_qkv(self, x, total_len, cos, sin):
-        """``(q, k, v, xwv)``: the projections with RoPE on q and k and k, v expanded to
-        the query heads (reference apply_rotary_emb + _repeat_kv, bitwise equal at equal
-        projections), and the value projection x·W_Vᵀ for the landmark scorer (v carries
-        no RoPE), or None with a v bias.  Bias-free in 16-bit compute on CUDA the three
-        projections run as one GEMM feeding the prologue kernel (``qkv_rope``)."""
+        """``(q, k, v, xwv)``: the projections with RoPE on q and k (reference
+        apply_rotary_emb, bitwise equal at equal projections), k and v with their
+        ``n_kv_heads`` heads: the attention ops read the kv head of each query head in
+        place instead of the reference's _repeat_kv expansion (:254-268); and the value
+        projection x·W_Vᵀ for the landmark scorer (v carries no RoPE), or None with a v
+        bias.  Bias-free in 16-bit compute on CUDA the three projections run as one GEMM
+        feeding the prologue kernel (``qkv_rope``)."""
         wq, wk, wv = self.q_proj.weight, self.k_proj.weight, self.v_proj.weight
         no_bias = self.q_proj.bias is None and self.k_proj.bias is None and self.v_proj.bias is None
         dt = _ext.half_compute_dtype(x, wq, wk, wv) if no_bias else None
         if dt is not None:
-            return qkv_rope(x, wq, wk, wv, cos, sin, self.n_heads, self.n_kv_heads, self.head_dim, dt)
+            return qkv_rope(x, wq, wk, wv, cos, sin, self.n_heads, self.n_kv_heads, self.head_dim, dt, expand=False)
         q = self.q_proj(x).view(total_len, self.n_heads, self.head_dim)
         k = self.k_proj(x).view(total_len, self.n_kv_heads, self.head_dim)
         v = self.v_proj(x).view(total_len, self.n_kv_heads, self.head_dim)
         xwv = v.view(total_len, self.kv_dim) if self.v_proj.bias is None else None
-        q, k, v = rope_gqa(q, k, v, cos.to(q.dtype), sin.to(q.dtype))
+        q, k, v = rope_gqa(q, k, v, cos.to(q.dtype), sin.to(q.dtype), expand=False)
         return q, k, v, xwv
 
     def _packed_train_triton(self, q, k, v, x, cu_seqlens, total_len, device, cu_list=None, xwv=None):
@@ -282,6 +284,7 @@ class DSALTAttention(nn.Module):
                 col[vp] = True
                 in_lmk[h] = col[None, :] & (rows[None, :] <= rows[:, None])
         mask = in_win[None] | in_lmk
+        k = self._repeat_kv(k)  # k arrives with its kv heads
         sc = torch.matmul(q[s0:e0].transpose(0, 1).float(), k[s0:e0].transpose(0, 1).float().transpose(-2, -1))
         sc = sc / math.sqrt(self.head_dim)
         return torch.softmax(sc.masked_fill(~mask, float("-inf")), dim=-1)

@@ -29,7 +29,7 @@
 extern "C" {
 #endif
 
-#define DSALT_B200_ABI_VERSION 6
+#define DSALT_B200_ABI_VERSION 7
 
 /* The tensor-core dK/dV stage splits each landmark chunk's query range into
  * this many parts that run as separate CTAs; their fp32 partial sums are added
@@ -116,8 +116,8 @@ DSALT_API int dsalt_build_schedule(const DsaltScheduleParams* p, void* stream);
  * token, else -1; the caller pre-fills it with -1).  k_lmk <= 1024,
  * kp <= 2048.                                                               */
 typedef struct DsaltGatherParams {
-  const void* k;              /* [T,H,D] dtype */
-  const void* v;              /* [T,H,D] dtype */
+  const void* k;              /* [T,H_kv,D] dtype (H_kv = H without grouped kv heads) */
+  const void* v;              /* [T,H_kv,D] dtype */
   const int64_t* lmk_pos;     /* [H,S,k_lmk] caller order, relative positions */
   const float* lmk_w;         /* [H,S,k] log-weight (train) / bias (infer), fp32 */
   const int32_t* cu_seqlens;  /* [S+1] */
@@ -131,13 +131,19 @@ typedef struct DsaltGatherParams {
   int64_t T;
   int32_t H, D, S, k_lmk, kp;
   int32_t dtype;
+  int32_t H_kv;               /* kv heads (0: H); query head h gathers from kv head
+                                 h / (H / H_kv); H must be a multiple of H_kv */
 } DsaltGatherParams;
 DSALT_API int dsalt_gather_landmarks(const DsaltGatherParams* p, void* stream);
 
 /* ---- attention ------------------------------------------------------------
  * One parameter block for the forward and the three backward stages.
- * Layouts: q,k,v,o,dout,dq,dk,dv [T,H,D] contiguous; lse, delta, dw_head
- * [T,H] fp32; landmark buffers from dsalt_gather_landmarks.                 */
+ * Layouts: q,o,dout,dq,dk,dv [T,H,D] and k,v [T,H_kv,D] contiguous; lse,
+ * delta, dw_head [T,H] fp32; landmark buffers from dsalt_gather_landmarks.
+ * Grouped kv heads (H_kv < H, the reference's n_kv_heads): query head h reads
+ * kv head h / (H / H_kv) in every kernel, so K/V are never expanded; dk and dv
+ * are then per query head ([T,H,D], the gradients of the expanded K/V), and
+ * dsalt_gqa_reduce sums each group into the [T,H_kv,D] gradient.            */
 typedef struct DsaltAttnParams {
   /* inputs */
   const void* q; const void* k; const void* v;
@@ -196,6 +202,7 @@ typedef struct DsaltAttnParams {
   int32_t semantics;          /* DSALT_TRAIN / DSALT_INFER */
   int32_t dtype;              /* DSALT_F16 / DSALT_BF16 / DSALT_F32 */
   int32_t impl;               /* DSALT_IMPL_* */
+  int32_t H_kv;               /* kv heads of k and v (0: H); H must be a multiple */
 } DsaltAttnParams;
 
 /* Replaces _train_fwd_kernel (dsalt/kernels/dsalt_triton_train.py:74-214) and
@@ -213,6 +220,20 @@ DSALT_API int dsalt_attn_bwd_dkdv(const DsaltAttnParams* p, void* stream);
  * 335-383) and the dQ of _dsalt_bwd_kernel; writes dq, dw_head (from the
  * σ-scaled dSᵀ entries dsalt_attn_bwd_dkdv stored) and dw.                  */
 DSALT_API int dsalt_attn_bwd_dq(const DsaltAttnParams* p, void* stream);
+
+/* Grouped kv heads: y[t, g, :] = Σ_{r < H/H_kv} x[t, g·(H/H_kv) + r, :], summed in
+ * fp32 and rounded once to the dtype.  Replaces the backward of the reference's
+ * K/V expansion _repeat_kv (dsalt/modules/dsalt_attention.py:254-268), whose
+ * autograd sums the expanded heads' gradients; x is dk or dv of the attention
+ * backward with H_kv < H.                                                   */
+typedef struct DsaltGqaReduceParams {
+  const void* x;              /* [T,H,D] dtype, 16-byte aligned */
+  void* y;                    /* [T,H_kv,D] dtype, 16-byte aligned */
+  int64_t T;
+  int32_t H, H_kv, D;
+  int32_t dtype;
+} DsaltGqaReduceParams;
+DSALT_API int dsalt_gqa_reduce(const DsaltGqaReduceParams* p, void* stream);
 
 /* ---- selection ------------------------------------------------------------
  * Replaces the norm / z-standardisation / mix of hybrid_scores_per_head
@@ -380,6 +401,10 @@ typedef struct DsaltRopeParams {
                                  fp32: 4, and at least H·D)                */
   int32_t H, Hkv, D;          /* D a multiple of 16 up to 256; H a multiple of Hkv */
   int32_t dtype;
+  int32_t kv_out_heads;       /* heads of k_out (and v_out, dk_out, dv_out): 0 or H
+                                 = k expanded to the query heads; Hkv = not expanded
+                                 (the attention kernels then read the kv head in
+                                 place), with v_out / dv_out NULL (v passes through) */
 } DsaltRopeParams;
 DSALT_API int dsalt_rope_gqa_fwd(const DsaltRopeParams* p, void* stream);
 DSALT_API int dsalt_rope_gqa_bwd(const DsaltRopeParams* p, void* stream);

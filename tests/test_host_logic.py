@@ -66,6 +66,45 @@ def test_model_step_entry_points_reject_bad_arguments():
     assert _rc("dsalt_xent_fwd_grad", _ext.XentParams(rows=4, vocab=10, dtype=_ext.F32)) == DT
 
 
+def test_grouped_kv_head_arguments_checked():
+    """Grouped kv heads: H must be a multiple of H_kv (0 meaning H) in the attention,
+    gather, prologue and group-sum entry points; checked before any launch."""
+    from dsalt.kernels import _ext
+    ARG, HD, OK = 1, 3, _ext.OK  # DSALT_ERR_ARG, DSALT_ERR_HEAD_DIM, DSALT_OK of include/dsalt_b200.h
+    p = _ext.AttnParams(T=4, H=6, D=64, S=1, dtype=_ext.BF16, tau_win=1.0, H_kv=4)
+    assert _rc("dsalt_attn_fwd", p) == ARG          # 6 query heads over 4 kv heads
+    p.H_kv = 8
+    assert _rc("dsalt_attn_fwd", p) == ARG          # more kv heads than query heads
+    p.H_kv = -1
+    assert _rc("dsalt_attn_fwd", p) == ARG
+    g = _ext.GatherParams(T=4, H=6, D=64, S=1, dtype=_ext.BF16, H_kv=4)
+    assert _rc("dsalt_gather_landmarks", g) == ARG
+    assert _rc("dsalt_gqa_reduce", _ext.GqaReduceParams(T=4, H=6, H_kv=4, D=64, dtype=_ext.BF16)) == ARG
+    assert _rc("dsalt_gqa_reduce", _ext.GqaReduceParams(T=4, H=8, H_kv=0, D=64, dtype=_ext.BF16)) == ARG
+    assert _rc("dsalt_gqa_reduce", _ext.GqaReduceParams(T=0, H=8, H_kv=2, D=64, dtype=_ext.BF16)) == OK
+    assert _rc("dsalt_gqa_reduce", _ext.GqaReduceParams(T=4, H=8, H_kv=2, D=12, dtype=_ext.BF16)) == HD
+    # the prologue's k output: expanded (0 or H) or per kv head (Hkv), nothing else
+    assert _rc("dsalt_rope_gqa_fwd", _ext.RopeParams(T=0, H=8, Hkv=2, D=64, dtype=_ext.BF16,
+                                                     kv_out_heads=4)) == ARG
+    assert _rc("dsalt_rope_gqa_fwd", _ext.RopeParams(T=0, H=8, Hkv=2, D=64, dtype=_ext.BF16,
+                                                     kv_out_heads=2)) == OK
+
+
+def test_gqa_head_sharding_keeps_groups():
+    """head_shard with grouped kv heads: each rank takes whole kv-head groups and the
+    query heads that read them."""
+    import torch
+    from dsalt.kernels.head_shard import shard_op_inputs
+    T, H, Hkv, D = 5, 8, 2, 4
+    q = torch.arange(T * H * D, dtype=torch.float32).view(T, H, D)
+    k = torch.arange(T * Hkv * D, dtype=torch.float32).view(T, Hkv, D)
+    pos = torch.zeros(H, 1, 3, dtype=torch.long)
+    lw = torch.zeros(H, 1, 3)
+    got = [shard_op_inputs(q, k, k, pos, lw, r, 2) for r in range(2)]
+    assert [g["heads"] for g in got] == [(0, 4), (4, 8)]
+    assert torch.equal(got[1]["k"], k[:, 1:2]) and torch.equal(got[1]["q"], q[:, 4:8])
+
+
 def test_model_step_functions_refuse_cpu_tensors():
     """The CUDA model-step functions have no CPU path: called directly on CPU tensors
     they raise (the modules route CPU tensors to the reference's torch ops instead)."""

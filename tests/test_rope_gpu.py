@@ -75,6 +75,33 @@ def test_backward_matches_autograd(shape, dtype):
             torch.testing.assert_close(ga, gb, rtol=8e-3, atol=1e-2, msg=name)
 
 
+@pytest.mark.parametrize("shape", [(300, 8, 2, 128), (129, 4, 1, 64)])
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
+def test_unexpanded_kv_heads(shape, dtype):
+    """``expand=False`` (the attention op reads the kv heads in place): k rotated per kv
+    head, v passed through; bitwise equal forward, the backward of the same
+    expression (no sum over copies)."""
+    from dsalt.kernels.rope_gqa import rope_gqa
+    T, H, Hkv, D = shape
+    q, k, v, cos, sin = _inputs(T, H, Hkv, D, dtype, seed=5 * T + H)
+    got = rope_gqa(q, k, v, cos, sin, expand=False)
+    ref = _reference(q, k, v, cos, sin, 1)
+    for name, a, b in zip(("q", "k", "v"), got, ref):
+        assert a.shape == b.shape, name
+        assert torch.equal(a, b), name
+    g = torch.Generator(device="cuda").manual_seed(4)
+    grads = [torch.randn(t.shape, generator=g, device="cuda").to(dtype) for t in ref]
+    leaves = [t.clone().requires_grad_(True) for t in (q, k, v)]
+    torch.autograd.backward(rope_gqa(*leaves, cos, sin, expand=False), grads)
+    ref_leaves = [t.clone().requires_grad_(True) for t in (q, k, v)]
+    torch.autograd.backward(_reference(*ref_leaves, cos, sin, 1), grads)
+    for name, a, b in zip(("dq", "dk", "dv"), leaves, ref_leaves):
+        if dtype == torch.float32:
+            torch.testing.assert_close(a.grad, b.grad, rtol=1e-6, atol=1e-6, msg=name)
+        else:
+            assert torch.equal(a.grad, b.grad), name
+
+
 def test_module_uses_fused_prologue_with_gqa():
     """A GQA DSALTAttention forward+backward runs through the fused prologue."""
     from dsalt.modules.dsalt_attention import DSALTAttention

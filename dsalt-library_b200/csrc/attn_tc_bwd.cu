@@ -667,24 +667,31 @@ __global__ void __launch_bounds__(kThreadsKV, 1) tc_bwd_dkdv_kernel(const __grid
         // straight-line pass above): Pᵀ, dSᵀ *= σ((w̃ − d)/τ) on the column's edge
         // keys elo … ehi, applied to the rounded entries (factor ehi − j of the
         // record, or computed past the stored ones)
+        // (branch-free per column: lanes outside the edge multiply by 1, which leaves
+        // an entry's bits unchanged)
         for (uint32_t m = emask; m != 0u; m &= m - 1u) {  // warp-uniform
           const int c = __ffs(m) - 1;
           const QRec& rq = rec[c];
           const int2 eb = *reinterpret_cast<const int2*>(&rq.ehi);  // ehi, elo
-          if (j >= eb.y && j <= eb.x) {
+          const bool ed = j >= eb.y && j <= eb.x;
+          float gf;
+          if (eb.x - eb.y < kMaxEdge) {  // warp-uniform: every factor stored
+            const float f = rq.eg[(uint32_t)(eb.x - j) & (uint32_t)(kMaxEdge - 1)];
+            gf = ed ? f : 1.0f;
+          } else {
             const int ei = eb.x - j;
-            const float gf = ei < kMaxEdge ? rq.eg[ei] : qrec_edge_factor(rq.wt, rq.qi - j, inv_tau);
-            const int w2 = c >> 1, sh = (c & 1) * 16;
-            uint32_t wp = 0u, wd = 0u;
-#pragma unroll
-            for (int i = 0; i < 8; ++i)
-              if (i == w2) { wp = pk_p[i]; wd = pk_d[i]; }
-            wp = (wp & ~(0xffffu << sh)) | (f32_to_bits<T>(bits_to_f32<T>(wp >> sh) * gf) << sh);
-            wd = (wd & ~(0xffffu << sh)) | (f32_to_bits<T>(bits_to_f32<T>(wd >> sh) * gf) << sh);
-#pragma unroll
-            for (int i = 0; i < 8; ++i)
-              if (i == w2) { pk_p[i] = wp; pk_d[i] = wd; }
+            gf = !ed ? 1.0f : ei < kMaxEdge ? rq.eg[ei] : qrec_edge_factor(rq.wt, rq.qi - j, inv_tau);
           }
+          const int w2 = c >> 1, sh = (c & 1) * 16;
+          uint32_t wp = 0u, wd = 0u;
+#pragma unroll
+          for (int i = 0; i < 8; ++i)
+            if (i == w2) { wp = pk_p[i]; wd = pk_d[i]; }
+          wp = (wp & ~(0xffffu << sh)) | (f32_to_bits<T>(bits_to_f32<T>(wp >> sh) * gf) << sh);
+          wd = (wd & ~(0xffffu << sh)) | (f32_to_bits<T>(bits_to_f32<T>(wd >> sh) * gf) << sh);
+#pragma unroll
+          for (int i = 0; i < 8; ++i)
+            if (i == w2) { pk_p[i] = wp; pk_d[i] = wd; }
         }
         // the shared dSᵀ buffer g % 2 is free once the store lane has read its
         // previous tile

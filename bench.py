@@ -56,10 +56,10 @@ KERNELS_PER_CALL = {"dsalt_build_schedule": 2, "dsalt_gather_landmarks": 1, "dsa
 # DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) per launch of each entry point's main
 # kernel, from one ncu --set full capture each of a config-2 step (profiles/*_config2.txt; for
 # dsalt_attn_bwd_dkdv the band pass, which the landmark pass and the fix-up kernel accompany)
-NCU_TRAFFIC_BYTES = {"config2": {"dsalt_attn_fwd": 304269568, "dsalt_attn_bwd_dkdv": 692519936,
-                                 "dsalt_attn_bwd_dq": 519714048}}
+NCU_TRAFFIC_BYTES = {"config2": {"dsalt_attn_fwd": 303677952, "dsalt_attn_bwd_dkdv": 691998976,
+                                 "dsalt_attn_bwd_dq": 518625536}}
 # digest of csrc/ (kernel_source_digest) when that capture was taken; other sources -> traffic null
-NCU_TRAFFIC_SRC = "5df04a3b087260dc"
+NCU_TRAFFIC_SRC = "2ae337a87675f2e5"
 CLOCK_REASONS = {0x1: "gpu_idle", 0x2: "applications_clocks_setting", 0x4: "sw_power_cap",
                  0x8: "hw_slowdown", 0x10: "sync_boost", 0x20: "sw_thermal_slowdown",
                  0x40: "hw_thermal_slowdown", 0x80: "hw_power_brake_slowdown", 0x100: "display_clock_setting"}

@@ -54,12 +54,13 @@ KERNELS_PER_CALL = {"dsalt_build_schedule": 2, "dsalt_gather_landmarks": 1, "dsa
                     "dsalt_attn_bwd_preprocess": 1, "dsalt_attn_bwd_dkdv": 3, "dsalt_attn_bwd_dq": 2}
 # (dsalt_attn_bwd_dkdv: landmark pass, band pass, landmark fix-up; dsalt_attn_bwd_dq: dQ, Σ_h d_w̃)
 # DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) per launch of each entry point's main
-# kernel, from one ncu --set full capture each of a config-2 step (profiles/*_config2.txt; for
-# dsalt_attn_bwd_dkdv the band pass, which the landmark pass and the fix-up kernel accompany)
-NCU_TRAFFIC_BYTES = {"config2": {"dsalt_attn_fwd": 303677952, "dsalt_attn_bwd_dkdv": 691998976,
-                                 "dsalt_attn_bwd_dq": 518625536}}
+# kernel: the median over the ten config-2 launches of one ncu capture of those two metrics
+# (profiles/dram_traffic_config2.txt; for dsalt_attn_bwd_dkdv the band pass, which the landmark
+# pass and the fix-up kernel accompany)
+NCU_TRAFFIC_BYTES = {"config2": {"dsalt_attn_fwd": 300558848, "dsalt_attn_bwd_dkdv": 688034560,
+                                 "dsalt_attn_bwd_dq": 515449344}}
 # digest of csrc/ (kernel_source_digest) when that capture was taken; other sources -> traffic null
-NCU_TRAFFIC_SRC = "2ae337a87675f2e5"
+NCU_TRAFFIC_SRC = "eab1b5928e7a3bd6"
 CLOCK_REASONS = {0x1: "gpu_idle", 0x2: "applications_clocks_setting", 0x4: "sw_power_cap",
                  0x8: "hw_slowdown", 0x10: "sync_boost", 0x20: "sw_thermal_slowdown",
                  0x40: "hw_thermal_slowdown", 0x80: "hw_power_brake_slowdown", 0x100: "display_clock_setting"}

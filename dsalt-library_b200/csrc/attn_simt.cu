@@ -288,7 +288,8 @@ simt_bwd_dkdv_kernel(const DsaltAttnParams p) {
       dlw += visit(s0 + i, bias);
     }
     const int slot = p.perm[lbase + c];
-    if (lane == 0 && slot >= 0 && p.d_lw) p.d_lw[((int64_t)h * p.S + s) * p.k_lmk + slot] = dlw;
+    if (lane == 0 && slot >= 0 && p.d_lw)
+      p.d_lw[((int64_t)h * p.S + s) * p.k_lmk + slot] = p.grad_round ? round_to<T>(dlw) : dlw;
   }
   T* dko = reinterpret_cast<T*>(p.dk) + t * HD + (int64_t)h * D;
   T* dvo = reinterpret_cast<T*>(p.dv) + t * HD + (int64_t)h * D;
@@ -397,14 +398,16 @@ static bool launch_preprocess_vec(const DsaltAttnParams& p, cudaStream_t st) {
   }
 }
 
-// d_w̃[t] = Σ_h dw_head[t,h], cast to the input dtype (dsalt_triton_train.py:748,756)
+// d_w̃[t] = Σ_h dw_head[t,h] in fp32; with round set, the value after the cast to
+// the input dtype (dsalt_triton_train.py:748,756), kept in fp32
 template <typename T>
-__global__ void dw_reduce_kernel(const float* __restrict__ dw_head, T* __restrict__ dw, int64_t T_, int H) {
+__global__ void dw_reduce_kernel(const float* __restrict__ dw_head, float* __restrict__ dw, int64_t T_, int H,
+                                 int round) {
   const int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (t >= T_) return;
   float s = 0.f;
   for (int h = 0; h < H; ++h) s += dw_head[t * H + h];
-  dw[t] = from_f32<T>(s);
+  dw[t] = round ? round_to<T>(s) : s;
 }
 
 // ------------------------------------------------------------------ launchers
@@ -419,14 +422,23 @@ static cudaError_t launch_simt(int stage, const DsaltAttnParams& p, cudaStream_t
     case 1:
       if (!launch_preprocess_vec<T>(p, st)) bwd_preprocess_kernel<T, R><<<grid, block, 0, st>>>(p);
       break;
-    case 2: simt_bwd_dkdv_kernel<T, R><<<grid, block, 0, st>>>(p); break;
+    case 2: {
+      // the kernel visits keys that hold a landmark: empty slots get their zero here
+      const size_t n_lw = (size_t)p.H * p.S * p.k_lmk;
+      if (p.d_lw && n_lw) {
+        const cudaError_t e = cudaMemsetAsync(p.d_lw, 0, n_lw * sizeof(float), st);
+        if (e != cudaSuccess) return e;
+      }
+      simt_bwd_dkdv_kernel<T, R><<<grid, block, 0, st>>>(p);
+      break;
+    }
     case 3:
       simt_bwd_dq_kernel<T, R><<<grid, block, 0, st>>>(p);
       if (p.dw && p.dw_head)
-        dw_reduce_kernel<T><<<(unsigned)((p.T + 255) / 256), 256, 0, st>>>(p.dw_head, reinterpret_cast<T*>(p.dw), p.T, p.H);
+        dw_reduce_kernel<T><<<(unsigned)((p.T + 255) / 256), 256, 0, st>>>(p.dw_head, p.dw, p.T, p.H, p.grad_round);
       break;
     case 4:  // d_w̃ head reduction only (after the tensor-core dQ kernel)
-      dw_reduce_kernel<T><<<(unsigned)((p.T + 255) / 256), 256, 0, st>>>(p.dw_head, reinterpret_cast<T*>(p.dw), p.T, p.H);
+      dw_reduce_kernel<T><<<(unsigned)((p.T + 255) / 256), 256, 0, st>>>(p.dw_head, p.dw, p.T, p.H, p.grad_round);
       break;
   }
   return cudaGetLastError();

@@ -814,7 +814,7 @@ __global__ void __launch_bounds__(kThreadsKV, 1) tc_bwd_dkdv_kernel(const __grid
 
 // Keys holding landmark slots: dK / dV = round(band rows + Σ over the key's slots
 // (duplicates are adjacent) and over the landmark pass's query-range parts, in
-// that fixed order); d_lw of every slot = Σ over its parts.  One warp per
+// that fixed order); d_lw of every slot = Σ over its parts (0 for an empty slot).  One warp per
 // (slot, sequence, head): blockIdx.x = s·ceil(kp/4) + slot/4; D/32 columns per lane.
 template <typename T, int D>
 __global__ void __launch_bounds__(128) lmk_fixup_kernel(const BwdArgs a) {
@@ -830,13 +830,18 @@ __global__ void __launch_bounds__(128) lmk_fixup_kernel(const BwdArgs a) {
   const float* band_v = a.band_lmk + a.part_stride * D;
   {
     const int pos = __ldg(p.pos_sorted + lbase + c);
-    if (pos < 0) return;  // an invalid slot
+    // every caller slot sits at one sorted position (empty ones last): its d_lw,
+    // 0 for an empty slot, is written here
     if (lane == 0 && p.d_lw) {
-      float g = 0.f;
-      for (int pp = 0; pp < DSALT_LMK_SPLIT; ++pp) g += __ldg(a.dlw_lmk + pp * a.part_stride + lbase + c);
       const int slot_c = __ldg(p.perm + lbase + c);
-      if (slot_c >= 0) p.d_lw[((int64_t)h * p.S + s) * p.k_lmk + slot_c] = g;
+      if (slot_c >= 0) {
+        float g = 0.f;
+        if (pos >= 0)
+          for (int pp = 0; pp < DSALT_LMK_SPLIT; ++pp) g += __ldg(a.dlw_lmk + pp * a.part_stride + lbase + c);
+        p.d_lw[((int64_t)h * p.S + s) * p.k_lmk + slot_c] = p.grad_round ? round_to<T>(g) : g;
+      }
     }
+    if (pos < 0) return;  // an invalid slot
     if (c > 0 && __ldg(p.pos_sorted + lbase + c - 1) == pos) return;  // not the first slot of its key
     float kk[kCols], vv[kCols];
     const int col0 = lane * kCols;

@@ -76,6 +76,7 @@ static int check_attn(const DsaltAttnParams* p, int stage) {
   if (p->semantics != DSALT_TRAIN && p->semantics != DSALT_INFER) return DSALT_ERR_ARG;
   if (!(p->tau_win > 0.f)) return DSALT_ERR_ARG;
   if (p->impl < DSALT_IMPL_AUTO || p->impl > DSALT_IMPL_TCGEN05) return DSALT_ERR_ARG;
+  if (p->grad_round != 0 && p->grad_round != 1) return DSALT_ERR_ARG;
   if (p->T == 0) return DSALT_OK;
   if (!p->q || !p->k || !p->v || !p->w || !p->cu_seqlens) return DSALT_ERR_ARG;
   if (p->kp > 0 && (!p->lmk_k || !p->lmk_v || !p->pos_sorted || !p->w_sorted)) return DSALT_ERR_ARG;
@@ -93,7 +94,14 @@ static int check_attn(const DsaltAttnParams* p, int stage) {
 
 static int run_attn(const DsaltAttnParams* p, int stage, void* stream) {
   int st = check_attn(p, stage);
-  if (st != DSALT_OK || p->T == 0) return st;
+  if (st != DSALT_OK) return st;
+  if (p->T == 0) {
+    // no tokens: every landmark slot is empty and its gradient is 0
+    const size_t n_lw = (size_t)p->H * p->S * p->k_lmk;
+    if (stage == 2 && p->d_lw && n_lw)
+      return status_of(cudaMemsetAsync(p->d_lw, 0, n_lw * sizeof(float), (cudaStream_t)stream));
+    return DSALT_OK;
+  }
   cudaStream_t s = (cudaStream_t)stream;
   bool use_tc = false;
   if (p->impl == DSALT_IMPL_TCGEN05) {
@@ -153,7 +161,13 @@ int dsalt_build_schedule(const DsaltScheduleParams* p, void* stream) {
   if (!p || p->S < 0 || p->T < 0 || p->block <= 0 || p->max_blocks < 0) return DSALT_ERR_ARG;
   if (!p->cu_seqlens || !p->block_map || !p->num_blocks) return DSALT_ERR_ARG;
   if ((p->seq_wmax || p->seq_id) && p->T > 0 && !p->w) return DSALT_ERR_ARG;
-  if (p->S == 0) return status_of(cudaMemsetAsync(p->num_blocks, 0, sizeof(int32_t), (cudaStream_t)stream));
+  if (p->seq_wmax_batch && !p->seq_wmax) return DSALT_ERR_ARG;
+  if (p->S == 0) {
+    cudaError_t e = cudaMemsetAsync(p->num_blocks, 0, sizeof(int32_t), (cudaStream_t)stream);
+    if (e == cudaSuccess && p->seq_wmax_batch)
+      e = cudaMemsetAsync(p->seq_wmax_batch, 0, sizeof(int32_t), (cudaStream_t)stream);
+    return status_of(e);
+  }
   return status_of(launch_schedule(*p, (cudaStream_t)stream));
 }
 

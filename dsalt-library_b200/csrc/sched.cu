@@ -14,12 +14,17 @@
 
 namespace dsalt {
 
-// One CTA: per-sequence block counts, exclusive scan, table fill.
+// One CTA: per-sequence block counts, exclusive scan, table fill; also clears
+// the band maxima that seq_meta_kernel (launched after it) raises.
 __global__ void __launch_bounds__(1024) build_block_map_kernel(DsaltScheduleParams p) {
   __shared__ int32_t warp_tot[32];
   __shared__ int32_t carry;
   const int tid = threadIdx.x;
   if (tid == 0) carry = 0;
+  if (p.seq_wmax) {
+    for (int b = tid; b < p.S; b += 1024) p.seq_wmax[b] = 0;
+    if (tid == 0 && p.seq_wmax_batch) *p.seq_wmax_batch = 0;
+  }
   __syncthreads();
   for (int base = 0; base < p.S; base += 1024) {
     const int b = base + tid;
@@ -67,6 +72,8 @@ __global__ void __launch_bounds__(1024) build_block_map_kernel(DsaltSchedulePara
 // Per token: its sequence id and the running per-sequence max band length.  A
 // warp whose 32 tokens lie in one sequence (the common case) reduces its maximum
 // first and issues one atomic; a warp across a boundary issues one per token.
+// The batch maximum is raised only by a value that raised its sequence's: every
+// final seq_wmax[s] reaches it, with a few atomics per sequence on one word.
 __global__ void seq_meta_kernel(DsaltScheduleParams p) {
   const int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   const bool valid = t < p.T;
@@ -82,17 +89,14 @@ __global__ void seq_meta_kernel(DsaltScheduleParams p) {
   const int s0 = __shfl_sync(0xffffffffu, s, 0);
   if (__all_sync(0xffffffffu, s == s0)) {
     const int m = __reduce_max_sync(0xffffffffu, W);
-    if ((threadIdx.x & 31) == 0 && s0 >= 0 && m > 0) atomicMax(p.seq_wmax + s0, m);
+    if ((threadIdx.x & 31) == 0 && s0 >= 0 && m > 0 && atomicMax(p.seq_wmax + s0, m) < m && p.seq_wmax_batch)
+      atomicMax(p.seq_wmax_batch, m);
   } else if (valid && W > 0) {
-    atomicMax(p.seq_wmax + s, W);
+    if (atomicMax(p.seq_wmax + s, W) < W && p.seq_wmax_batch) atomicMax(p.seq_wmax_batch, W);
   }
 }
 
 cudaError_t launch_schedule(const DsaltScheduleParams& p, cudaStream_t st) {
-  if (p.seq_wmax) {
-    cudaError_t e = cudaMemsetAsync(p.seq_wmax, 0, sizeof(int32_t) * (size_t)p.S, st);
-    if (e != cudaSuccess) return e;
-  }
   build_block_map_kernel<<<1, 1024, 0, st>>>(p);
   if (p.T > 0 && (p.seq_wmax || p.seq_id))
     seq_meta_kernel<<<(unsigned)((p.T + 255) / 256), 256, 0, st>>>(p);

@@ -21,7 +21,7 @@ F16, BF16, F32 = 0, 1, 2
 TRAIN, INFER = 0, 1
 IMPL_AUTO, IMPL_SIMT, IMPL_TCGEN05 = 0, 1, 2
 DEV_WAIT_TIMEOUT, DEV_BAD_INDEX = 1, 2
-ABI_VERSION = 7
+ABI_VERSION = 8
 QREC_FLOATS = 16  # DSALT_QREC_FLOATS
 LMK_SPLIT = 4  # DSALT_LMK_SPLIT
 DS_TILE_BYTES = 16384  # DSALT_DS_TILE_BYTES
@@ -41,7 +41,7 @@ class ScheduleParams(ctypes.Structure):
     _fields_ = [("cu_seqlens", _c_void_p), ("w", _c_void_p), ("block_map", _c_void_p),
                 ("num_blocks", _c_void_p), ("seq_wmax", _c_void_p), ("seq_id", _c_void_p),
                 ("T", _i64), ("S", _i32), ("block", _i32), ("max_blocks", _i32),
-                ("semantics", _i32)]
+                ("semantics", _i32), ("seq_wmax_batch", _c_void_p)]
 
 
 class GatherParams(ctypes.Structure):
@@ -66,7 +66,8 @@ class AttnParams(ctypes.Structure):
                 ("T", _i64), ("H", _i32), ("D", _i32), ("S", _i32), ("k_lmk", _i32), ("kp", _i32),
                 ("max_blocks", _i32), ("ds_band_tiles", _i32), ("ds_lmk_tiles", _i32),
                 ("scale", _f32), ("tau_win", _f32), ("win_edge", _f32),
-                ("semantics", _i32), ("dtype", _i32), ("impl", _i32), ("H_kv", _i32)]
+                ("semantics", _i32), ("dtype", _i32), ("impl", _i32), ("H_kv", _i32),
+                ("grad_round", _i32)]
 
 
 class ScoreParams(ctypes.Structure):

@@ -82,6 +82,7 @@ class Prepared:
     H_kv: int = 0                # kv heads of k, v (grouped kv heads when < H)
     wmax_slot: int = -1          # slot of the widest band in the pinned ring (-1: none)
     wmax_gen: int = 0
+    seq_wmax_batch: torch.Tensor | None = None   # [1] int32: max over s of seq_wmax
 
 
 # The widest band of a batch (max over the sequences of seq_wmax) sizes the dSᵀ tile
@@ -112,7 +113,7 @@ def _record_wmax(prep: "Prepared", dev: torch.device) -> None:
     slot = r["next"]
     r["next"] = (slot + 1) % _WMAX_RING
     r["gen"][slot] += 1
-    r["host"][slot:slot + 1].copy_(prep.seq_wmax[:max(prep.S, 1)].amax().reshape(1), non_blocking=True)
+    r["host"][slot:slot + 1].copy_(prep.seq_wmax_batch, non_blocking=True)
     r["events"][slot].record()
     prep.wmax_slot, prep.wmax_gen = slot, r["gen"][slot]
 
@@ -160,11 +161,14 @@ def prepare(k_c: torch.Tensor, v_c: torch.Tensor, lmk_pos: torch.Tensor, lmk_w: 
     max_blocks = (T + BLOCK_M - 1) // BLOCK_M + S
     block_map = torch.empty(max(max_blocks, 1), 2, dtype=torch.int32, device=dev)
     num_blocks = torch.empty(1, dtype=torch.int32, device=dev)
-    seq_wmax = torch.empty(max(S, 1), dtype=torch.int32, device=dev)
+    # per-sequence band maxima, then the batch maximum (written by the schedule kernels)
+    wmax_buf = torch.empty(max(S, 1) + 1, dtype=torch.int32, device=dev)
+    seq_wmax, seq_wmax_batch = wmax_buf[:max(S, 1)], wmax_buf[max(S, 1):]
     sp = _ext.ScheduleParams(
         cu_seqlens=_ext.ptr(cu), w=_ext.ptr(w32), block_map=_ext.ptr(block_map),
         num_blocks=_ext.ptr(num_blocks), seq_wmax=_ext.ptr(seq_wmax), seq_id=0,
-        T=T, S=S, block=BLOCK_M, max_blocks=max_blocks, semantics=semantics)
+        T=T, S=S, block=BLOCK_M, max_blocks=max_blocks, semantics=semantics,
+        seq_wmax_batch=_ext.ptr(seq_wmax_batch))
     _ext.call("dsalt_build_schedule", sp)
 
     dt = k_c.dtype
@@ -190,7 +194,8 @@ def prepare(k_c: torch.Tensor, v_c: torch.Tensor, lmk_pos: torch.Tensor, lmk_w: 
         cu_host = [int(c) for c in cu.to("cpu").tolist()]
     lmax = max((b - a for a, b in zip(cu_host[:-1], cu_host[1:])), default=0)
     prep = Prepared(T, H, D, S, k_lmk, kp, semantics, cu, w32, block_map, num_blocks, seq_wmax,
-                    lmk_k, lmk_v, pos_sorted, w_sorted, perm, lmk_slot, max_blocks, lmax, H_kv)
+                    lmk_k, lmk_v, pos_sorted, w_sorted, perm, lmk_slot, max_blocks, lmax, H_kv,
+                    seq_wmax_batch=seq_wmax_batch)
     if for_backward and T > 0:
         _record_wmax(prep, dev)
     return prep
@@ -236,8 +241,12 @@ def forward(q_c, k_c, v_c, prep: Prepared, tau_win: float, win_edge: float, impl
 
 
 def backward(grad_out, q_c, k_c, v_c, o, lse, prep: Prepared, tau_win: float, win_edge: float,
-             impl: int, want_dw: bool, scale: float | None = None):
-    """Run the backward stages; returns ``(dq, dk, dv, d_lw [H,S,k] fp32, dw [T] or None)``.
+             impl: int, want_dw: bool, scale: float | None = None, grad_round: bool = True):
+    """Run the backward stages; returns ``(dq, dk, dv, d_lw [H,S,k] fp32, dw [T] fp32 or None)``.
+
+    ``grad_round``: ``d_lw`` and ``dw`` hold their sums rounded to the input dtype,
+    in fp32 (the values the reference's autograd functions return after their
+    ``.to(out_dtype)``, which autograd widens back for the fp32 parameters).
 
     ``grad_out`` may be fp32 (the op's output dtype) or the input dtype; an fp32
     gradient is rounded to the input dtype by the preprocess kernel itself.
@@ -258,9 +267,9 @@ def backward(grad_out, q_c, k_c, v_c, o, lse, prep: Prepared, tau_win: float, wi
     grouped = prep.H_kv != H
     dk = torch.empty_like(q_c) if grouped else torch.empty_like(k_c)
     dv = torch.empty_like(q_c) if grouped else torch.empty_like(v_c)
-    d_lw = torch.zeros(H, prep.S, prep.k_lmk, dtype=torch.float32, device=dev)
+    d_lw = torch.empty(H, prep.S, prep.k_lmk, dtype=torch.float32, device=dev)  # every slot written
     dw_head = torch.empty(T, H, dtype=torch.float32, device=dev) if want_dw else None
-    dw = torch.empty(T, dtype=q_c.dtype, device=dev) if want_dw else None
+    dw = torch.empty(T, dtype=torch.float32, device=dev) if want_dw else None
     # partial landmark-slot dK, dV, d_lw of the tensor-core dK/dV stage
     lmk_grad = torch.empty(((2 * prep.D + 1) * _ext.LMK_SPLIT + 2 * prep.D) * H * prep.S * prep.kp,
                            dtype=torch.float32, device=dev) if prep.kp > 0 else None
@@ -272,6 +281,7 @@ def backward(grad_out, q_c, k_c, v_c, o, lse, prep: Prepared, tau_win: float, wi
                 dout_f32=do_f32,
                 delta=delta, dq=dq, dk=dk, dv=dv, dw_head=dw_head, dw=dw, d_lw=d_lw, lmk_grad=lmk_grad,
                 qrec=qrec)
+    p.grad_round = 1 if grad_round else 0
     # the dSᵀ tiles the dK/dV stage stores for the dQ stage (tensor-core family)
     band_tiles = (BLOCK_M + widest_band(prep, dev, H * prep.max_blocks * _ext.DS_TILE_BYTES) + 63) // 64
     lmk_tiles = (prep.lmax + 63) // 64 + 1

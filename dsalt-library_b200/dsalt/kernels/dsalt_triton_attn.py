@@ -56,7 +56,8 @@ class DSALTAttentionFunction(torch.autograd.Function):
         dq, dk, dv, d_bias, _ = _cuda.backward(grad_out, q_c, k_c, v_c, o, lse, ctx.prep, 1.0, 0.0,
                                                ctx.impl, want_dw=False)
         od = ctx.out_dtype
-        return dq.to(od), dk.to(od), dv.to(od), None, d_bias.to(od), None, None
+        # d_bias: fp32 holding the values of the reference's d_bias.to(out_dtype)
+        return dq.to(od), dk.to(od), dv.to(od), None, d_bias, None, None
 
 
 def _dynamo_opaque(fn):

@@ -46,5 +46,6 @@ def dsalt_triton_backward(grad_out, q, k, v, out, lse, lmk_K, lmk_V, lmk_pos, lm
     lse_c = lse.contiguous().to(torch.float32)
     prep = _cuda.prepare(k_c, v_c, lmk_pos, lmk_bias, w_sizes, cu_seqlens, _ext.INFER, for_backward=True)
     dq, dk, dv, d_bias, _ = _cuda.backward(grad_out, q_c, k_c, v_c, o_c, lse_c, prep, 1.0, 0.0,
-                                           _ext.default_impl(), want_dw=False, scale=float(scale))
+                                           _ext.default_impl(), want_dw=False, scale=float(scale),
+                                           grad_round=False)
     return dq.float(), dk.float(), dv.float(), d_bias

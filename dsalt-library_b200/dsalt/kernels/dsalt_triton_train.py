@@ -74,7 +74,9 @@ def _train_backward(ctx, grad_out):
     dq, dk, dv, d_lw, dw = _cuda.backward(grad_out, q_c, k_c, v_c, o, lse, ctx.prep, ctx.tau_win,
                                           ctx.win_edge, ctx.impl, want_dw=True)
     od = ctx.out_dtype
-    return dq.to(od), dk.to(od), dv.to(od), d_lw.to(od), dw.to(od)
+    # d_lw, dw: fp32 holding the values of the reference's .to(out_dtype) casts
+    # (:750-757), so autograd hands them to the fp32 parameters without a cast
+    return dq.to(od), dk.to(od), dv.to(od), d_lw, dw
 
 
 class DSALTTrainFunction(torch.autograd.Function):

@@ -29,7 +29,7 @@
 extern "C" {
 #endif
 
-#define DSALT_B200_ABI_VERSION 7
+#define DSALT_B200_ABI_VERSION 8
 
 /* The tensor-core dK/dV stage splits each landmark chunk's query range into
  * this many parts that run as separate CTAs; their fp32 partial sums are added
@@ -88,6 +88,9 @@ enum {
  *     blocks of `block` query rows; rows past num_blocks are untouched;
  *   num_blocks [1] int32; seq_wmax [S] int32 = max over the sequence's rows of
  *     the number of band keys before the diagonal (floor(w̃) train, w-1 infer);
+ *   seq_wmax_batch [1] int32 = max over s of seq_wmax[s] (optional, may be
+ *     NULL; needs seq_wmax) — the widest band of the batch, ready to copy to
+ *     the host without a reduction launch;
  *   seq_id [T] int32 = sequence of every packed token (optional, may be NULL).
  * max_blocks must be >= ceil(T/block) + S.                                    */
 typedef struct DsaltScheduleParams {
@@ -102,6 +105,7 @@ typedef struct DsaltScheduleParams {
   int32_t block;
   int32_t max_blocks;
   int32_t semantics;
+  int32_t* seq_wmax_batch;    /* [1] or NULL */
 } DsaltScheduleParams;
 DSALT_API int dsalt_build_schedule(const DsaltScheduleParams* p, void* stream);
 
@@ -169,8 +173,9 @@ typedef struct DsaltAttnParams {
   float* delta;               /* [T,H] scratch */
   void* dq; void* dk; void* dv;       /* [T,H,D] dtype */
   float* dw_head;             /* [T,H] scratch (train) */
-  void* dw;                   /* [T] dtype: Σ_h ∂loss/∂w̃ (train) or NULL */
-  float* d_lw;                /* [H,S,k_lmk] fp32, caller slot order: ∂loss/∂lmk_w */
+  float* dw;                  /* [T] fp32: Σ_h ∂loss/∂w̃ (train) or NULL */
+  float* d_lw;                /* [H,S,k_lmk] fp32, caller slot order: ∂loss/∂lmk_w;
+                                 every slot is written (0 for an empty slot) */
   float* lmk_grad;            /* fp32 scratch of the tensor-core dK/dV stage:
                                  ((2·D + 1)·DSALT_LMK_SPLIT + 2·D)·H·S·kp floats
                                  (partial landmark-slot dK, dV, d_lw and the band
@@ -203,6 +208,10 @@ typedef struct DsaltAttnParams {
   int32_t dtype;              /* DSALT_F16 / DSALT_BF16 / DSALT_F32 */
   int32_t impl;               /* DSALT_IMPL_* */
   int32_t H_kv;               /* kv heads of k and v (0: H); H must be a multiple */
+  int32_t grad_round;         /* 1: dw and d_lw hold their fp32 sums rounded to the
+                                 input dtype (the values the reference's autograd
+                                 functions return, .to(out_dtype), widened back to
+                                 fp32 exactly); 0: the fp32 sums */
 } DsaltAttnParams;
 
 /* Replaces _train_fwd_kernel (dsalt/kernels/dsalt_triton_train.py:74-214) and

@@ -16,17 +16,22 @@
 //               K-major smem tile (chunk h = half h), where each thread applies
 //               the soft window edge to its row's ≤ ceil(win_edge)+1 edge keys in
 //               place, walking only those entries.
-//               The epilogue stages O in the P buffer and stores it row-contiguously,
-//               in the input dtype, or in fp32 when the caller asks for the op's
-//               fp32 output (o_f32: then that is the only O written).
+//               The epilogue stages O in the P buffer: the input-dtype O is stored
+//               row-contiguously by the threads; the op's fp32 output (o_f32: then
+//               the only O written) in rounds of 64 columns, both halves merging 32
+//               columns each into two 32-column boxes that thread 0 stores with
+//               TMA without waiting (plain stores for a block cut by its sequence
+//               end); the next round's columns come out of TMEM meanwhile, and the
+//               next item's first P waits for the last round's read (STAGE_FREE).
 //   warp 8      TMA producers: lane 0 loads Q (once the previous item's last S has
 //               read it) and the K tiles, lane 1 the V tiles.
 //   warp 9      TMEM allocator + single-thread tcgen05.mma issuer:
 //               S[t%2] = Q·K_tᵀ two tiles ahead.
 //   warp 10     O_h += P_t,h·V_t,h for each half h as soon as that half's P is
 //               written (an item's first one once the previous epilogue read O).
-//   warp 11     scheduler: resolves each item's row windows, landmark slots and
-//               band one or two items ahead into a double-buffered info block.
+//   warp 11     scheduler: resolves each item's row windows, landmark slots,
+//               band and soft-edge factors one or two items ahead into a
+//               double-buffered info block.
 //
 // TMEM (512 columns): S double buffer [0, 256), O_0 [256, 256 + D), O_1 after it.
 //
@@ -68,7 +73,8 @@ constexpr int kInfoConsumers = 11;
 
 enum Bar {
   Q_FULL = 0, Q_EMPTY = 1, K_FULL = 2, V_FULL = 4, K_EMPTY = 6, V_EMPTY = 8, S_FULL = 10, S_EMPTY = 12,
-  P_FULL = 14, O_DONE = 16, O_FREE = 18, INFO_FULL = 19, INFO_EMPTY = 21, EPI = 23, FINAL = 24, NUM_BARS = 26
+  P_FULL = 14, O_DONE = 16, O_FREE = 18, INFO_FULL = 19, INFO_EMPTY = 21, EPI = 23, FINAL = 24, STAGE_FREE = 26,
+  NUM_BARS = 27
 };
 
 // Everything the roles need about one item (128 query rows of one (sequence,
@@ -79,6 +85,7 @@ struct ItemInfo {
   int band_lo, band_hi, n_valid, n_lt, n_tiles;
   int row_lo[BM], row_hi[BM], row_cnt[BM], row_de0[BM], row_ne[BM];
   float row_wt[BM];
+  float row_eg[kMaxEdge][BM];  // σ((w̃ − d)/τ) of each row's first kMaxEdge edge keys (1 past ne)
   int lmk_pos[kMaxLmk];
   float lmk_lw2[kMaxLmk];
 };
@@ -99,8 +106,10 @@ struct alignas(1024) FwdSmem {
 
 struct alignas(64) FwdArgs {
   CUtensorMap tm_q, tm_k, tm_v, tm_lk, tm_lv;
+  CUtensorMap tm_o;  // fp32 O [T, H, D], 32-column x 128-row boxes (valid when o_tma)
   DsaltAttnParams p;
   int lmk_box;  // rows of one landmark TMA box
+  int o_tma;    // 1: full blocks of the fp32 O are stored with TMA
 };
 
 __device__ __forceinline__ int round16(int n) { return (n + 15) & ~15; }
@@ -123,6 +132,7 @@ __device__ __forceinline__ void resolve_item(const DsaltAttnParams& p, int idx, 
   const int L = (int)(__ldg(p.cu_seqlens + s + 1) - s0);
   const int kp = p.kp;
   const int64_t lbase = ((int64_t)h * p.S + s) * kp;
+  const float inv_tau = 1.0f / p.tau_win;
   int nv = 0;
   for (int c0 = 0; c0 < kp; c0 += 32) {
     const int c = c0 + lane;
@@ -159,6 +169,14 @@ __device__ __forceinline__ void resolve_item(const DsaltAttnParams& p, int idx, 
     }
     in.row_lo[r] = lo; in.row_hi[r] = hi; in.row_cnt[r] = cnt;
     in.row_de0[r] = d_e0; in.row_ne[r] = ne; in.row_wt[r] = wt;
+    // soft-edge factors σ((w̃ − d)/τ) of the row's first edge keys (d ≤ w̃: the
+    // exponent is ≤ 0), with the fast intrinsics: they scale 16-bit P values
+#pragma unroll
+    for (int e = 0; e < kMaxEdge; ++e) {
+      float f = 1.0f;
+      if (e < ne) f = __fdividef(1.0f, 1.0f + __expf(-((wt - (float)(d_e0 + e)) * inv_tau)));
+      in.row_eg[e][r] = f;
+    }
     if (lo <= hi) { blo = min(blo, lo); bhi = max(bhi, hi); }
   }
   blo = __reduce_min_sync(0xffffffffu, blo);
@@ -207,6 +225,7 @@ __global__ void __launch_bounds__(kThreads, 1) tc_fwd_kernel(const __grid_consta
     }
     mbar_init(bar[O_FREE], kRowThreads);
     mbar_init(bar[EPI], kRowThreads);
+    mbar_init(bar[STAGE_FREE], 1);
     mbar_init(bar[FINAL], 1);
     mbar_init(bar[FINAL + 1], 1);
     fence_mbar_init();
@@ -413,11 +432,6 @@ __global__ void __launch_bounds__(kThreads, 1) tc_fwd_kernel(const __grid_consta
       const int lo = in.row_lo[r], hi = in.row_hi[r], cnt = in.row_cnt[r];
       const int d_e0 = in.row_de0[r], ne = in.row_ne[r];
       const float wt = in.row_wt[r];
-      // soft-edge factors of the row's edge keys (same expression as the per-key form)
-      float eg[kMaxEdge];
-#pragma unroll
-      for (int e = 0; e < kMaxEdge; ++e)
-        eg[e] = (e < ne) ? 1.0f / (1.0f + expf(-((wt - (float)(d_e0 + e)) * inv_tau))) : 1.0f;
       float m = -INFINITY, l = 0.f;  // this half's running max (log2 units) and sum
       for (int t = 0; t < n_tiles; ++t) {
         const int g = gt + t, st = g & 1;
@@ -504,6 +518,16 @@ __global__ void __launch_bounds__(kThreads, 1) tc_fwd_kernel(const __grid_consta
           if (!__all_sync(0xffffffffu, ok)) { ok = false; break; }
           tc_fence_after();
         }
+        if (t == 0) {
+          // the P buffer also stages the previous item's fp32 O: free once the TMA
+          // stores that thread 0 issued have read it (thread 0 releases it here)
+          if (tid == 0) {
+            bulk_wait_read0();
+            mbar_arrive(bar[STAGE_FREE]);
+          }
+          ok = mbar_wait(bar[STAGE_FREE], li & 1, abort_flag, p.status);
+          if (!__all_sync(0xffffffffu, ok)) { ok = false; break; }
+        }
         if (all_out) {
           const uint4 z = make_uint4(0u, 0u, 0u, 0u);
 #pragma unroll
@@ -532,7 +556,8 @@ __global__ void __launch_bounds__(kThreads, 1) tc_fwd_kernel(const __grid_consta
             const int c = ce0 - e;
             T* ep = reinterpret_cast<T*>(rowp + ((((c >> 3) ^ rx) << 4) | ((c & 7) << 1)));
             const float pv = to_f32<T>(*ep);
-            const float sg = e < kMaxEdge ? eg[e] : 1.0f / (1.0f + expf(-((wt - (float)(d_e0 + e)) * inv_tau)));
+            const float sg = e < kMaxEdge ? in.row_eg[e][r]
+                                          : 1.0f / (1.0f + expf(-((wt - (float)(d_e0 + e)) * inv_tau)));
             *ep = from_f32<T>(pv * sg);
             l -= pv * (1.0f - sg);
           }
@@ -559,12 +584,6 @@ __global__ void __launch_bounds__(kThreads, 1) tc_fwd_kernel(const __grid_consta
       }
       if (!ok) break;
       // ---- epilogue: merge the two halves of each row, O / l, LSE
-      const int gl = gt + n_tiles - 1;  // the item's last tile
-      ok = mbar_wait(bar[O_DONE], gl & 1, abort_flag, p.status) &&
-           mbar_wait(bar[O_DONE + 1], gl & 1, abort_flag, p.status);
-      ok = __all_sync(0xffffffffu, ok);
-      if (!ok) break;
-      tc_fence_after();
       sm.m_half[ib][half][r] = m;
       sm.l_half[ib][half][r] = l;
       if (!(ok = epi_sync())) break;
@@ -579,21 +598,80 @@ __global__ void __launch_bounds__(kThreads, 1) tc_fwd_kernel(const __grid_consta
       const float inv_l = nonempty ? 1.0f / lt : 0.f;
       const bool use0 = nonempty && lh0 > 0.f, use1 = nonempty && lh1 > 0.f;
       if (row_ok && half == 0) p.lse[(s0 + i) * p.H + h] = nonempty ? (mm + log2f(lt)) * kLn2 : -INFINITY;
-      // O rows staged in the (idle) P buffer, 128 rows × 256 B with 16-byte units
-      // XOR-swizzled by row % 8, then stored row-contiguously: the input-dtype O in
-      // one round (D·2 bytes per row), or the fp32 O in D/64 rounds of 64 columns
-      // (256 bytes per row; round k: output columns [64k, 64k + 64))
-      const bool f32_out = p.o_f32 != nullptr;
-      const int rounds = f32_out ? D / 64 : 1;
-      const int units = f32_out ? 16 : D / 8;  // 16-byte units per staged row
+      // both halves' last P·V have completed: O_0 and O_1 are final
+      const int gl = gt + n_tiles - 1;  // the item's last tile
+      ok = mbar_wait(bar[O_DONE], gl & 1, abort_flag, p.status) &&
+           mbar_wait(bar[O_DONE + 1], gl & 1, abort_flag, p.status);
+      ok = __all_sync(0xffffffffu, ok);
+      if (!ok) break;
+      tc_fence_after();
       const int rows = min(BM, L - m0);
       const int64_t HD = (int64_t)p.H * D;
       uint8_t* stage = sm.p;
-      for (int rd = 0; rd < rounds; ++rd) {
+      if (p.o_f32 != nullptr) {
+        // fp32 O in rounds of 64 output columns: half h merges columns 64·rd + 32·h + [0, 32)
+        // of its row into box h of the staging area (128 rows x 128 B, 16-byte units
+        // XOR-swizzled by row % 8: the SWIZZLE_128B image of one 32-column box of tm_o)
+        const bool tma = a.o_tma != 0 && rows == BM;
+        uint8_t* box = stage + half * (BM * 128);
+        for (int rd = 0; rd < D / 64; ++rd) {
+          float v[32];
+#pragma unroll
+          for (int c16 = 0; c16 < 2; ++c16) {
+            const int col = 64 * rd + 32 * half + 16 * c16;
+            float o1[16];
+            tmem_ld16(tO + lane_addr + col, v + 16 * c16);
+            tmem_ld16(tO + D + lane_addr + col, o1);
+            tmem_wait_ld();
+#pragma unroll
+            for (int j = 0; j < 16; ++j) {
+              const float a0 = use0 ? v[16 * c16 + j] * f0 : 0.f;
+              const float a1 = use1 ? o1[j] * f1 : 0.f;
+              v[16 * c16 + j] = round_to<T>((a0 + a1) * inv_l);
+            }
+          }
+          if (rd == D / 64 - 1) {
+            tc_fence_before();
+            mbar_arrive(bar[O_FREE]);  // O is read: the next item's P·V may overwrite it
+          }
+          if (rd > 0) {
+            // the previous round's boxes have been read by its TMA stores (while this
+            // round's columns came out of TMEM) or copied by the threads
+            if (tma && tid == 0) bulk_wait_read0();
+            if (!(ok = epi_sync())) break;
+          }
+#pragma unroll
+          for (int u = 0; u < 8; ++u)
+            *reinterpret_cast<float4*>(box + r * 128 + ((u ^ (r & 7)) << 4)) =
+                make_float4(v[4 * u], v[4 * u + 1], v[4 * u + 2], v[4 * u + 3]);
+          if (tma) fence_async_smem();  // the staged rows, visible to the TMA stores
+          if (!(ok = epi_sync())) break;
+          if (tma) {
+            if (tid == 0) {
+              tma_store_3d(&a.tm_o, smem_u32(stage), 64 * rd, h, (int)(s0 + m0));
+              tma_store_3d(&a.tm_o, smem_u32(stage + BM * 128), 64 * rd + 32, h, (int)(s0 + m0));
+              bulk_commit();
+            }
+          } else {
+            // a block cut by its sequence end: the rows that exist, row-contiguously
+            uint8_t* dst = reinterpret_cast<uint8_t*>(p.o_f32) + ((s0 + m0) * HD + (int64_t)h * D + rd * 64) * 4;
+            const int64_t row_bytes = HD * 4;
+            for (int un = r + BM * half; un < rows * 16; un += kRowThreads) {
+              const int rr = un >> 4, uu = un & 15;
+              const uint8_t* src = stage + (uu >> 3) * (BM * 128) + rr * 128 + (((uu & 7) ^ (rr & 7)) << 4);
+              *reinterpret_cast<uint4*>(dst + rr * row_bytes + uu * 16) = *reinterpret_cast<const uint4*>(src);
+            }
+          }
+        }
+        // the threads' copies are done before the next item writes P (TMA stores:
+        // released through STAGE_FREE at the next item's first P)
+        if (ok && !tma) ok = epi_sync();
+      } else {
+        // input-dtype O: 128 rows x D·2 bytes staged with 16-byte units XOR-swizzled
+        // by row % 8, then stored row-contiguously
 #pragma unroll
         for (int ch = 0; ch < D / 32; ++ch) {  // this thread's D/2 output columns, 16 at a time
           const int col = half * (D / 2) + ch * 16;
-          if (f32_out && col / 64 != rd) continue;
           float o0[16], o1[16];
           tmem_ld16(tO + lane_addr + col, o0);
           tmem_ld16(tO + D + lane_addr + col, o1);
@@ -602,39 +680,28 @@ __global__ void __launch_bounds__(kThreads, 1) tc_fwd_kernel(const __grid_consta
           for (int j = 0; j < 16; ++j) {
             const float a0 = use0 ? o0[j] * f0 : 0.f;
             const float a1 = use1 ? o1[j] * f1 : 0.f;
-            o0[j] = round_to<T>((a0 + a1) * inv_l);
+            o0[j] = (a0 + a1) * inv_l;
           }
-          if (f32_out) {
 #pragma unroll
-            for (int u = 0; u < 4; ++u) {
-              const int un = (col - 64 * rd) / 4 + u;
-              *reinterpret_cast<float4*>(stage + r * 256 + ((un ^ (r & 7)) << 4)) =
-                  make_float4(o0[4 * u], o0[4 * u + 1], o0[4 * u + 2], o0[4 * u + 3]);
-            }
-          } else {
-#pragma unroll
-            for (int u = 0; u < 2; ++u) {
-              const int un = col / 8 + u;
-              *reinterpret_cast<uint4*>(stage + r * 256 + ((un ^ (r & 7)) << 4)) =
-                  make_uint4(pack2(o0[8 * u + 0], o0[8 * u + 1], kBF16), pack2(o0[8 * u + 2], o0[8 * u + 3], kBF16),
-                             pack2(o0[8 * u + 4], o0[8 * u + 5], kBF16), pack2(o0[8 * u + 6], o0[8 * u + 7], kBF16));
-            }
+          for (int u = 0; u < 2; ++u) {
+            const int un = col / 8 + u;
+            *reinterpret_cast<uint4*>(stage + r * 256 + ((un ^ (r & 7)) << 4)) =
+                make_uint4(pack2(o0[8 * u + 0], o0[8 * u + 1], kBF16), pack2(o0[8 * u + 2], o0[8 * u + 3], kBF16),
+                           pack2(o0[8 * u + 4], o0[8 * u + 5], kBF16), pack2(o0[8 * u + 6], o0[8 * u + 7], kBF16));
           }
         }
-        if (rd == rounds - 1) {
-          tc_fence_before();
-          mbar_arrive(bar[O_FREE]);  // O is read: the next item's P·V may overwrite it
-        }
+        tc_fence_before();
+        mbar_arrive(bar[O_FREE]);  // O is read: the next item's P·V may overwrite it
         if (!(ok = epi_sync())) break;
-        uint8_t* dst = f32_out ? reinterpret_cast<uint8_t*>(p.o_f32) + ((s0 + m0) * HD + (int64_t)h * D + rd * 64) * 4
-                               : reinterpret_cast<uint8_t*>(p.o) + ((s0 + m0) * HD + (int64_t)h * D) * 2;
-        const int64_t row_bytes = HD * (f32_out ? 4 : 2);
+        uint8_t* dst = reinterpret_cast<uint8_t*>(p.o) + ((s0 + m0) * HD + (int64_t)h * D) * 2;
+        const int64_t row_bytes = HD * 2;
+        constexpr int units = D / 8;  // 16-byte units per staged row
         for (int un = r + BM * half; un < rows * units; un += kRowThreads) {
           const int rr = un / units, uu = un % units;
           *reinterpret_cast<uint4*>(dst + rr * row_bytes + uu * 16) =
               *reinterpret_cast<const uint4*>(stage + rr * 256 + ((uu ^ (rr & 7)) << 4));
         }
-        if (!(ok = epi_sync())) break;  // the staging area is reused (next round, or the next item's P)
+        if (!(ok = epi_sync())) break;  // the staging area is reused by the next item's P
       }
       if (!ok) break;
       gt += n_tiles;
@@ -642,6 +709,7 @@ __global__ void __launch_bounds__(kThreads, 1) tc_fwd_kernel(const __grid_consta
       if (lane == 0) mbar_arrive(bar[INFO_EMPTY + ib]);
     }
   }
+  if (tid == 0) bulk_wait_all();  // the fp32 O stores this thread issued have completed
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
@@ -677,6 +745,10 @@ cudaError_t launch_tc_fwd(const DsaltAttnParams& p, cudaStream_t stream) {
     return cudaErrorInvalidValue;
   if (encode_3d(&a.tm_lv, dt, lv, D, kp, hs, row, (uint64_t)kp * row, 64, a.lmk_box, 1) != CUDA_SUCCESS)
     return cudaErrorInvalidValue;
+  // fp32 O: [T, H, D] in boxes of 32 columns (128 B, the swizzle span) x 128 rows
+  a.o_tma = p.o_f32 != nullptr && ((uintptr_t)p.o_f32 & 15u) == 0 &&
+            encode_3d(&a.tm_o, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, p.o_f32, D, p.H, p.T, (uint64_t)D * 4,
+                      (uint64_t)p.H * D * 4, 32, 1, BM) == CUDA_SUCCESS;
   // at least ~116 KB so that one CTA (and its 512 TMEM columns) owns the SM
   const size_t smem = std::max(sizeof(FwdSmem<D>) + 1024, (size_t)(116 * 1024));
   cudaError_t e = ensure_smem((const void*)tc_fwd_kernel<T, D>, smem);

@@ -400,7 +400,7 @@ cudaError_t launch_dq2(const DsaltAttnParams& p, cudaStream_t st) {
   a.p = p;
   const CUtensorMapDataType dt = std::is_same<T, __half>::value ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16
                                                                  : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
-  const uint64_t row = (uint64_t)D * 2, trow = (uint64_t)p.H * D * 2;
+  const uint64_t row = (uint64_t)D * 2;
   const uint64_t hkv = (uint64_t)attn_kv_heads(p);  // k: [T, H_kv, D]
   if (encode_tensor_map_3d(&a.tm_k, dt, p.k, D, hkv, p.T, row, hkv * D * 2, 64, 1, dq2::KB) != CUDA_SUCCESS)
     return cudaErrorInvalidValue;

@@ -577,6 +577,7 @@ __global__ void __launch_bounds__(kTopkThreads) topk_kernel(DsaltTopkParams p) {
 
 cudaError_t launch_topk(const DsaltTopkParams& p, cudaStream_t st) {
   if (p.H * p.S == 0) return cudaSuccess;
+  if (p.max_len > kTopkMaxLen || p.k > kTopkMaxK) return cudaErrorInvalidValue;  // checked by the entry point
   const size_t smem = sizeof(uint32_t) * (size_t)max(p.max_len, 1);
   cudaError_t e = ensure_smem((const void*)topk_kernel, smem);
   if (e != cudaSuccess) return e;

@@ -57,10 +57,10 @@ KERNELS_PER_CALL = {"dsalt_build_schedule": 2, "dsalt_gather_landmarks": 1, "dsa
 # kernel: the median over the ten config-2 launches of one ncu capture of those two metrics
 # (profiles/dram_traffic_config2.txt; for dsalt_attn_bwd_dkdv the band pass, which the landmark
 # pass and the fix-up kernel accompany)
-NCU_TRAFFIC_BYTES = {"config2": {"dsalt_attn_fwd": 300558848, "dsalt_attn_bwd_dkdv": 688034560,
-                                 "dsalt_attn_bwd_dq": 515449344}}
+NCU_TRAFFIC_BYTES = {"config2": {"dsalt_attn_fwd": 301239808, "dsalt_attn_bwd_dkdv": 687554688,
+                                 "dsalt_attn_bwd_dq": 515452800}}
 # digest of csrc/ (kernel_source_digest) when that capture was taken; other sources -> traffic null
-NCU_TRAFFIC_SRC = "eab1b5928e7a3bd6"
+NCU_TRAFFIC_SRC = "232497833c0a8d95"
 CLOCK_REASONS = {0x1: "gpu_idle", 0x2: "applications_clocks_setting", 0x4: "sw_power_cap",
                  0x8: "hw_slowdown", 0x10: "sync_boost", 0x20: "sw_thermal_slowdown",
                  0x40: "hw_thermal_slowdown", 0x80: "hw_power_brake_slowdown", 0x100: "display_clock_setting"}

@@ -182,3 +182,19 @@ def test_tile_table_states_the_kernels_shapes():
         assert sum(c["fwd"]["warps"].values()) * 32 == c["fwd"]["threads"]
         assert sum(c["bwd_dkdv"]["warps"].values()) * 32 == c["bwd_dkdv"]["threads"]
         assert sum(c["bwd_dq"]["warps"].values()) * 32 == c["bwd_dq"]["threads"]
+
+
+def test_gradient_rounding_and_batch_band_arguments():
+    """grad_round is 0 or 1; the batch's widest band needs the per-sequence maxima
+    (both checked before any launch)."""
+    from dsalt.kernels import _ext
+    ARG = 1  # DSALT_ERR_ARG
+    base = dict(T=0, H=2, D=64, S=1, k_lmk=0, kp=0, scale=0.125, tau_win=1.0, win_edge=4.0,
+                semantics=_ext.TRAIN, dtype=_ext.BF16, impl=0)
+    assert _rc("dsalt_attn_bwd_dkdv", _ext.AttnParams(**base, grad_round=2)) == ARG
+    assert _rc("dsalt_attn_bwd_dq", _ext.AttnParams(**base, grad_round=-1)) == ARG
+    assert _rc("dsalt_attn_bwd_dkdv", _ext.AttnParams(**base, grad_round=1)) == _ext.OK  # no tokens, no slots
+    cu = ctypes.c_int32(0)
+    sp = _ext.ScheduleParams(cu_seqlens=ctypes.addressof(cu), block_map=1, num_blocks=1, seq_wmax=0,
+                             seq_wmax_batch=1, T=0, S=1, block=128, max_blocks=1, semantics=_ext.TRAIN)
+    assert _rc("dsalt_build_schedule", sp) == ARG

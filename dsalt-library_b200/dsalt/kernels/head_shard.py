@@ -78,3 +78,23 @@ def gather_heads(shard: torch.Tensor, n_heads: int, group=None, n_rep: int = 1) 
     recv = recv.view((world, T, hmax) + rest)
     parts = [recv[r, :, :h1 - h0] for r, (h0, h1) in enumerate(sizes)]
     return torch.cat(parts, dim=1)
+
+
+def reduce_window_grad(partial: torch.Tensor, out_dtype: torch.dtype | None = None, group=None) -> torch.Tensor:
+    """∂loss/∂w̃ of the whole op from the head shards.
+
+    ``w̃ [T]`` is shared by every head, so its gradient is a sum over heads
+    (``dsalt_triton_train.py:748``): with the heads split over the ranks, each rank
+    holds the sum over its own heads.  One ``all_reduce`` (SUM, fp32) adds the
+    shards; with ``out_dtype`` the total is then rounded once to that dtype and kept
+    in fp32, as the reference's ``d_w_tok.to(out_dtype)`` (``:756``) reaches an fp32
+    ``w̃``.  The training op rounds each rank's own sum already (``grad_round``),
+    so the total differs from the unsharded op's by at most those per-rank
+    roundings.  Outside the timed op: a ``[T]`` fp32 exchange."""
+    import torch.distributed as dist
+    total = partial.detach().to(torch.float32).clone()
+    if dist.is_initialized() and dist.get_world_size(group) > 1:
+        dist.all_reduce(total, op=dist.ReduceOp.SUM, group=group)
+    if out_dtype is not None and out_dtype != torch.float32:
+        total = total.to(out_dtype).to(torch.float32)
+    return total

@@ -68,16 +68,21 @@ def _shard_worker(rank: int, world: int, port: int, out_dir: str) -> None:
     import numpy as np
     import torch
     import torch.distributed as dist
-    from dsalt.kernels.head_shard import gather_heads, shard_op_inputs
+    from dsalt.kernels.head_shard import gather_heads, reduce_window_grad, shard_op_inputs
     from oracle import dsalt_oracle as O
     dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60))
     try:
         inp = _global_batch()
-        sh = shard_op_inputs(inp["q"], inp["k"], inp["v"], inp["pos"], inp["logw"], rank, world)
+        sh = shard_op_inputs(inp["q"], inp["k"], inp["v"], inp["pos"], inp["logw"], rank, world,
+                             extra={"do": inp["do"]})
         o, _ = O.attention_fwd(sh["q"].numpy(), sh["k"].numpy(), sh["v"].numpy(), sh["lmk_pos"].numpy(),
                                sh["lmk_logw"].numpy(), inp["w"].numpy(), inp["cu"].numpy())
         full = gather_heads(torch.from_numpy(np.ascontiguousarray(o)), inp["q"].shape[1])
-        torch.save({"heads": sh["heads"], "o": full}, os.path.join(out_dir, f"shard{rank}.pt"))
+        g = O.attention_bwd(sh["q"].numpy(), sh["k"].numpy(), sh["v"].numpy(), sh["do"].numpy(),
+                            sh["lmk_pos"].numpy(), sh["lmk_logw"].numpy(), inp["w"].numpy(), inp["cu"].numpy(),
+                            1.0, 4.0, "train")
+        d_w = reduce_window_grad(torch.from_numpy(np.ascontiguousarray(g["d_w"])))
+        torch.save({"heads": sh["heads"], "o": full, "d_w": d_w}, os.path.join(out_dir, f"shard{rank}.pt"))
     finally:
         dist.destroy_process_group()
 
@@ -92,13 +97,15 @@ def _global_batch():
     pos = torch.stack([torch.stack([torch.randperm(L, generator=g)[:k] for L in lens]) for _ in range(H)])
     logw = torch.log(torch.sigmoid(torch.randn(H, len(lens), k, generator=g, dtype=torch.float64)))
     cu = torch.tensor([0, 70, 115, 205], dtype=torch.int32)
-    return dict(q=q, k=kk, v=v, w=w, pos=pos, logw=logw, cu=cu)
+    do = torch.randn(T, H, D, generator=g, dtype=torch.float64)
+    return dict(q=q, k=kk, v=v, w=w, pos=pos, logw=logw, cu=cu, do=do)
 
 
 @pytest.mark.parametrize("world", [2, 3])
 def test_head_shards_reassemble_to_the_whole_op(tmp_path, world):
     """5 heads over 2 or 3 ranks (uneven shards): every rank's all-gathered O equals
-    the oracle's forward over all heads at once."""
+    the oracle's forward over all heads at once, and the all-reduced shard sums of
+    ∂loss/∂w̃ equal the oracle's gradient over all heads."""
     import numpy as np
     import torch
     from oracle import dsalt_oracle as O
@@ -106,11 +113,14 @@ def test_head_shards_reassemble_to_the_whole_op(tmp_path, world):
     inp = _global_batch()
     ref, _ = O.attention_fwd(inp["q"].numpy(), inp["k"].numpy(), inp["v"].numpy(), inp["pos"].numpy(),
                              inp["logw"].numpy(), inp["w"].numpy(), inp["cu"].numpy())
+    g = O.attention_bwd(inp["q"].numpy(), inp["k"].numpy(), inp["v"].numpy(), inp["do"].numpy(), inp["pos"].numpy(),
+                        inp["logw"].numpy(), inp["w"].numpy(), inp["cu"].numpy(), 1.0, 4.0, "train")
     covered = []
     for r in range(world):
         got = torch.load(tmp_path / f"shard{r}.pt")
         covered.append(tuple(got["heads"]))
         assert np.array_equal(got["o"].numpy(), ref)
+        assert np.allclose(got["d_w"].numpy(), g["d_w"], rtol=1e-5, atol=1e-6)
     assert covered[0][0] == 0 and covered[-1][1] == 5
     assert all(a[1] == b[0] for a, b in zip(covered, covered[1:]))
 

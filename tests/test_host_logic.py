@@ -198,3 +198,14 @@ def test_gradient_rounding_and_batch_band_arguments():
     sp = _ext.ScheduleParams(cu_seqlens=ctypes.addressof(cu), block_map=1, num_blocks=1, seq_wmax=0,
                              seq_wmax_batch=1, T=0, S=1, block=128, max_blocks=1, semantics=_ext.TRAIN)
     assert _rc("dsalt_build_schedule", sp) == ARG
+
+
+def test_reduce_window_grad_single_process_rounds_once():
+    """Without a process group the shard sum is the local one; with out_dtype it is
+    rounded once to that dtype and kept in fp32."""
+    from dsalt.kernels.head_shard import reduce_window_grad
+    g = torch.Generator().manual_seed(5)
+    x = torch.randn(1000, generator=g, dtype=torch.float64)
+    assert torch.equal(reduce_window_grad(x), x.float())
+    r = reduce_window_grad(x, torch.bfloat16)
+    assert r.dtype == torch.float32 and torch.equal(r, x.float().bfloat16().float())
